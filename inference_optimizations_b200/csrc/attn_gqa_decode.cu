@@ -1,0 +1,505 @@
+// GQA-packed split-K decode / speculative-verify attention over a paged NVFP4 / FP8 / bf16 KV pool, sm_100a.
+//
+// Capability of the reference's split-K verify and NVFP4 decode kernels (`attention/verify-splitk/gemma31_verify.py`
+// K29, `kv-cache-4bit/kv4tri-triton-backend/kv4tri_nvfp4_attention.py:257` nvfp4_decode_fwd): one CTA per
+// (request, kv head, split); its rows are the request's n_q query tokens x the G query heads sharing the kv head, so
+// every KV byte is read once per kv head.  Designed here for tcgen05 instead of a transliteration:
+//
+//  * swap-AB: tokens are the MMA M dimension (128 per tile), query rows the N dimension (16), so a decode step with
+//    2..16 rows still issues full-height UMMAs.  S^T = K Q^T lands in TMEM with lane = token, column = row.
+//  * O^T = V^T P^T with V read MN-major straight from the same token-row tiles K uses (no transpose pass).
+//  * the pool is read by one bulk async copy per (page, kv head, K|V) into a raw ring; 8 dequant warps expand
+//    E2M1 x E4M3 (or E4M3, or bf16) to f16 128-byte-swizzled tiles; the pool rows are stored with the same 16-byte
+//    chunk XOR swizzle so both the raw reads and the tile writes are bank-conflict free.
+//  * warp roles: 0-3 softmax + O accumulation (registers), 4-11 dequant, 12 bulk-copy producer, 13 UMMA issuer.
+//  * split-K partials (o normalised, lse in log2 units) are merged by a second kernel.
+//  * every mbarrier wait is bounded; a timeout records a status code and the CTA unwinds.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace iob {
+namespace {
+
+constexpr int kTileTok = 128;
+constexpr int kN = 16;           // UMMA N (query rows, padded)
+constexpr int kRing = 4;         // f16 slab buffers (128 tokens x 64 dims each)
+constexpr int kSlabBytes = kTileTok * 128;
+constexpr int kThreads = 448;
+constexpr int kSoftmaxWarps = 4;
+constexpr int kDequantWarps = 8;
+constexpr int kProducerWarp = 12;
+constexpr int kMmaWarp = 13;
+
+struct Smem {
+  uint64_t raw_full[8], raw_empty[8];
+  uint64_t chunk_full[kRing], chunk_empty[kRing];
+  uint64_t s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2];
+  uint32_t tmem_base;
+  int abort;
+  float red[kSoftmaxWarps][kN];
+  float row_m[kN];
+  float row_alpha[kN];
+};
+
+// must match kv_swizzle_byte() (kernels.h), which the pool writers use
+__device__ __forceinline__ int pool_chunk_pos(int j, int r, int nch) {
+  return (j & ~(nch - 1)) | ((j ^ r) & (nch - 1));
+}
+
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t addr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(lbo_bytes >> 4) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t v) {
+  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
+  float2 f = __bfloat1622float2(b);
+  __half2 h = __float22half2_rn(f);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Expand 32 values (one token row, dims [32*half, 32*half+32) of slab c) to 4 f16 16-byte chunks.
+template <int FMT, int D>
+__device__ __forceinline__ void dequant_32(const uint8_t* part, int r, int c, int half, uint4 (&o)[4]) {
+  if constexpr (FMT == kKvNvfp4) {
+    constexpr int RB = D / 2, NCH = (RB / 16) < 8 ? (RB / 16) : 8;
+    const uint8_t* row = part + r * RB;
+    const uint4 in = *reinterpret_cast<const uint4*>(row + pool_chunk_pos(2 * c + half, r, NCH) * 16);
+    const uint16_t sc = *reinterpret_cast<const uint16_t*>(part + 64 * RB + r * (D / 16) + c * 4 + half * 2);
+    const uint32_t s0 = half2_bcast(__ushort_as_half(static_cast<unsigned short>(e4m3x2_to_f16x2(sc) & 0xFFFF)));
+    const uint32_t s1 = half2_bcast(__ushort_as_half(static_cast<unsigned short>(e4m3x2_to_f16x2(sc) >> 16)));
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&in);
+    uint32_t* ow = reinterpret_cast<uint32_t*>(o);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ow[i] = hmul2_u32(e2m1x2_to_f16x2(b[i]), i < 8 ? s0 : s1);
+  } else if constexpr (FMT == kKvFp8) {
+    constexpr int RB = D, NCH = 8;
+    const uint8_t* row = part + r * RB;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const uint4 in = *reinterpret_cast<const uint4*>(row + pool_chunk_pos(4 * c + 2 * half + k, r, NCH) * 16);
+      const uint16_t* h = reinterpret_cast<const uint16_t*>(&in);
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o[2 * k]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ow[i] = e4m3x2_to_f16x2(h[i]);
+    }
+  } else {
+    constexpr int RB = 2 * D, NCH = 8;
+    const uint8_t* row = part + r * RB;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint4 in = *reinterpret_cast<const uint4*>(row + pool_chunk_pos(8 * c + 4 * half + k, r, NCH) * 16);
+      const uint32_t* iw = reinterpret_cast<const uint32_t*>(&in);
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o[k]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ow[i] = bf16x2_to_f16x2(iw[i]);
+    }
+  }
+}
+
+template <int FMT, int D>
+__device__ __forceinline__ constexpr int part_bytes() {
+  return FMT == kKvNvfp4 ? 64 * (D / 2 + D / 16) : (FMT == kKvFp8 ? 64 * D : 64 * D * 2);
+}
+
+template <int FMT, int D, int RMAX>
+__global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecodeArgs a) {
+  constexpr int NS = D / 64;                       // 64-dim slabs per head vector
+  constexpr int PB = part_bytes<FMT, D>();         // bytes of K (or V) of one (page, head)
+  constexpr int NST = (PB <= 20 * 1024) ? 6 : ((PB <= 32 * 1024) ? 4 : 2);
+  constexpr int MB = D / 128;                      // 128-dim M blocks of O^T
+  constexpr int kOCols = MB * kN;
+  static_assert(RMAX <= kN, "rows");
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = base;                                   // kRing x 16 KB
+  uint8_t* sq = ring + kRing * kSlabBytes;                // NS x 2 KB
+  uint8_t* sp = sq + NS * kN * 128;                       // 2 x (2 x 2 KB)
+  uint8_t* raw = sp + 2 * 2 * kN * 128;                   // NST x PB
+  Smem& sm = *reinterpret_cast<Smem*>(raw + NST * PB);
+
+  const int G = a.Hq / a.Hk;
+  const int R = a.n_q * G;
+  const int work = blockIdx.x;
+  const int split = work % a.num_splits;
+  const int bh = work / a.num_splits;
+  const int h = bh % a.Hk;
+  const int b = bh / a.Hk;
+  const int kv_len = a.kv_len[b];
+  const int q_first = kv_len - a.n_q;                     // position of query token 0
+  const int kv_begin = a.window > 0 ? max(0, q_first - a.window + 1) : 0;
+  const int tile0 = kv_begin / kTileTok + split * a.tiles_per_split;
+  const int tile_end = min((kv_len + kTileTok - 1) / kTileTok, kv_begin / kTileTok + (split + 1) * a.tiles_per_split);
+  const int ntiles = tile_end - tile0;
+  const size_t part_out = (static_cast<size_t>(bh) * a.num_splits + split);
+  if (ntiles <= 0) {  // empty split: publish an empty partial
+    if (a.num_splits > 1 && threadIdx.x < RMAX) a.lse_part[part_out * RMAX + threadIdx.x] = -INFINITY;
+    return;
+  }
+  const int first_page = kv_begin / a.page;
+  const int n_pages = (kv_len + a.page - 1) / a.page;
+  const int* pt = a.page_table + static_cast<size_t>(b) * a.pt_stride;
+  const int warp = warp_id(), lane = lane_id();
+
+  // ---- Q -> f16 slabs (rows >= R zero), barriers, TMEM
+  {
+    const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(a.q);
+    for (int idx = threadIdx.x; idx < kN * NS * 8; idx += kThreads) {
+      const int row = idx / (NS * 8), rem = idx % (NS * 8), c = rem / 8, ch = rem % 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (row < R) {
+        const int t = row / G, g = row % G;
+        const uint4 in = *reinterpret_cast<const uint4*>(
+            q + ((static_cast<size_t>(b) * a.n_q + t) * a.Hq + h * G + g) * D + c * 64 + ch * 8);
+        const uint32_t* iw = reinterpret_cast<const uint32_t*>(&in);
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ow[i] = bf16x2_to_f16x2(iw[i]);
+      }
+      *reinterpret_cast<uint4*>(sq + c * (kN * 128) + sw128_chunk(row, ch)) = v;
+    }
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NST; ++i) { mbar_init(&sm.raw_full[i], 1); mbar_init(&sm.raw_empty[i], kDequantWarps); }
+    for (int i = 0; i < kRing; ++i) { mbar_init(&sm.chunk_full[i], kDequantWarps); mbar_init(&sm.chunk_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.s_full[i], 1); mbar_init(&sm.s_empty[i], kSoftmaxWarps);
+      mbar_init(&sm.p_full[i], kSoftmaxWarps); mbar_init(&sm.o_full[i], 1); mbar_init(&sm.o_empty[i], kSoftmaxWarps);
+    }
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) { tmem_alloc(&sm.tmem_base, 256); tmem_relinquish(); }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const uint32_t tS = tmem;            // 2 x 16 columns
+  const uint32_t tO = tmem + 32;       // 2 x kOCols columns
+  volatile int* abort = &sm.abort;
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      const uint8_t* pool = a.pool;
+      int issued = 0;
+      for (int j = 0; j < ntiles && !*abort; ++j) {
+        for (int part = 0; part < 2; ++part) {
+          for (int pg = 0; pg < 2; ++pg) {
+            const int seq = 4 * j + 2 * part + pg, st = seq % NST;
+            if (*abort) break;
+            if (!mbar_wait(&sm.raw_empty[st], ((seq / NST) & 1) ^ 1, abort, a.status, kTimeoutProducer)) break;
+            issued = seq + 1;
+            const int pidx = (tile0 + j) * 2 + pg;
+            const int phys = (pidx >= first_page && pidx < n_pages) ? pt[pidx] : -1;
+            if (phys >= 0) {
+              const uint8_t* src = pool + (static_cast<size_t>(phys) * a.Hk + h) * (2 * PB) + part * PB;
+              mbar_expect_tx(&sm.raw_full[st], PB);
+              bulk_g2s(raw + st * PB, src, PB, &sm.raw_full[st]);
+            } else {
+              mbar_arrive(&sm.raw_full[st]);
+            }
+          }
+        }
+      }
+      // drain: the last copies must land before the CTA may exit
+      for (int seq = max(0, issued - NST); seq < issued; ++seq)
+        mbar_wait(&sm.raw_full[seq % NST], (seq / NST) & 1, nullptr, a.status, kTimeoutProducer);
+    }
+  } else if (warp >= kSoftmaxWarps && warp < kSoftmaxWarps + kDequantWarps) {
+    // ---------------------------------------------------------------- dequant warps
+    const int dw = warp - kSoftmaxWarps;
+    const int tok = 16 * dw + (lane & 7) + 8 * (lane >> 4);   // 0..127 within the tile
+    const int half = (lane >> 3) & 1;
+    const int pg = tok / 64, r = tok % 64;
+    for (int j = 0; j < ntiles; ++j) {
+      const int pidx = (tile0 + j) * 2 + pg;
+      const bool valid = pidx >= first_page && pidx < n_pages && pt[pidx] >= 0;
+      for (int part = 0; part < 2; ++part) {
+        const int seq_raw = 4 * j + 2 * part + pg, st = seq_raw % NST;
+        // both pages of this part must be resident (each warp only reads its own page, but arrives on both)
+        const int seq0 = 4 * j + 2 * part, st0 = seq0 % NST, st1 = (seq0 + 1) % NST;
+        if (!mbar_wait(&sm.raw_full[st0], (seq0 / NST) & 1, abort, a.status, kTimeoutConsumer)) goto done;
+        if (!mbar_wait(&sm.raw_full[st1], ((seq0 + 1) / NST) & 1, abort, a.status, kTimeoutConsumer)) goto done;
+        for (int c = 0; c < NS; ++c) {
+          const int seq = j * 2 * NS + part * NS + c, buf = seq % kRing;
+          if (!mbar_wait(&sm.chunk_empty[buf], ((seq / kRing) & 1) ^ 1, abort, a.status, kTimeoutConsumer)) goto done;
+          uint4 o[4];
+          if (valid) dequant_32<FMT, D>(raw + st * PB, r, c, half, o);
+          else { o[0] = o[1] = o[2] = o[3] = make_uint4(0, 0, 0, 0); }
+          uint8_t* slab = ring + buf * kSlabBytes;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(slab + sw128_chunk(tok, half * 4 + q)) = o[q];
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.chunk_full[buf]);
+        }
+        __syncwarp();
+        if (lane == 0) { mbar_arrive(&sm.raw_empty[st0]); mbar_arrive(&sm.raw_empty[st1]); }
+      }
+    }
+  done:;
+  } else if (warp == kMmaWarp) {
+    // ---------------------------------------------------------------- UMMA issuer
+    const uint32_t id_qk = idesc_dense(0, 0, 128, kN);
+    const uint32_t id_pv = idesc_dense(0, 0, 128, kN) | (1u << 15);   // A (V^T) MN-major
+    const uint32_t ring_addr = smem_u32(ring), q_addr = smem_u32(sq), p_addr = smem_u32(sp);
+    for (int j = 0; j < ntiles; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
+      bool ok = true;
+      for (int c = 0; c < NS && ok; ++c) {
+        const int seq = j * 2 * NS + c, buf = seq % kRing;
+        ok = mbar_wait(&sm.chunk_full[buf], (seq / kRing) & 1, abort, a.status, kTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16_ss(tS + sb * kN, desc_sw128(ring_addr + buf * kSlabBytes + kk * 32),
+                        desc_sw128(q_addr + c * (kN * 128) + kk * 32), id_qk, (c > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&sm.chunk_empty[buf]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&sm.s_full[sb]);
+      __syncwarp();
+      if (!mbar_wait(&sm.p_full[sb], (j >> 1) & 1, abort, a.status, kTimeoutMma)) break;
+      if (!mbar_wait(&sm.o_empty[sb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
+      for (int mb = 0; mb < MB && ok; ++mb) {
+        const int seq0 = j * 2 * NS + NS + 2 * mb, buf0 = seq0 % kRing;
+        ok = mbar_wait(&sm.chunk_full[buf0], (seq0 / kRing) & 1, abort, a.status, kTimeoutMma) &&
+             mbar_wait(&sm.chunk_full[buf0 + 1], ((seq0 + 1) / kRing) & 1, abort, a.status, kTimeoutMma);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_f16_ss(tO + sb * kOCols + mb * kN,
+                        desc_mn_sw128(ring_addr + buf0 * kSlabBytes + kk * 2048, kSlabBytes),
+                        desc_sw128(p_addr + sb * (2 * kN * 128) + (kk >> 2) * (kN * 128) + (kk & 3) * 32), id_pv,
+                        kk > 0 ? 1u : 0u);
+          umma_commit(&sm.chunk_empty[buf0]);
+          umma_commit(&sm.chunk_empty[buf0 + 1]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&sm.o_full[sb]);
+      __syncwarp();
+    }
+  } else if (warp < kSoftmaxWarps) {
+    // ---------------------------------------------------------------- softmax + O accumulation
+    const float scale_log2 = a.sm_scale * a.k_scale * 1.4426950408889634f;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+    float acc[MB][RMAX];
+    float lpart[RMAX];
+    float alpha_prev[RMAX];
+#pragma unroll
+    for (int n = 0; n < RMAX; ++n) {
+      lpart[n] = 0.f;
+      alpha_prev[n] = 1.f;
+#pragma unroll
+      for (int mb = 0; mb < MB; ++mb) acc[mb][n] = 0.f;
+    }
+    if (threadIdx.x < kN) sm.row_m[threadIdx.x] = -INFINITY;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    bool ok = true;
+    auto consume_o = [&](int i) -> bool {
+      const int sb = i & 1;
+      if (!mbar_wait(&sm.o_full[sb], (i >> 1) & 1, abort, a.status, kTimeoutConsumer)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int mb = 0; mb < MB; ++mb) {
+        uint32_t r[16];
+        tmem_ld16(tO + lane_base + sb * kOCols + mb * kN, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int n = 0; n < RMAX; ++n) acc[mb][n] = acc[mb][n] * alpha_prev[n] + __uint_as_float(r[n]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.o_empty[sb]);
+      return true;
+    };
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&sm.s_full[sb], (j >> 1) & 1, abort, a.status, kTimeoutConsumer)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sr[16];
+      tmem_ld16(tS + lane_base + sb * kN, sr);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.s_empty[sb]);
+      const int tokpos = (tile0 + j) * kTileTok + 32 * warp + lane;
+      float s[RMAX];
+      float tmax[RMAX];
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n) {
+        const int t = n / G;
+        const int qpos = q_first + t;
+        const bool vis = n < R && tokpos <= qpos && tokpos >= kv_begin &&
+                         (a.window <= 0 || qpos - tokpos < a.window);
+        s[n] = vis ? __uint_as_float(sr[n]) * scale_log2 : -INFINITY;
+        tmax[n] = warp_max(s[n]);
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int n = 0; n < RMAX; ++n) sm.red[warp][n] = tmax[n];
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      float mnew[RMAX], alpha[RMAX];
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n) {
+        const float mt = fmaxf(fmaxf(sm.red[0][n], sm.red[1][n]), fmaxf(sm.red[2][n], sm.red[3][n]));
+        const float mo = sm.row_m[n];
+        mnew[n] = fmaxf(mo, mt);
+        alpha[n] = (mnew[n] == -INFINITY) ? 1.f : exp2f(mo - mnew[n]);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n)
+        if (threadIdx.x == n) sm.row_m[n] = mnew[n];
+      // P (f16) into the B operand: row n, token k -> slab k / 64, SW128 K-major
+      uint8_t* pbuf = sp + sb * (2 * kN * 128);
+      const int k = 32 * warp + lane;
+#pragma unroll
+      for (int n = 0; n < kN; ++n) {
+        float p = 0.f;
+        if (n < RMAX) {
+          p = (s[n] == -INFINITY) ? 0.f : exp2f(s[n] - mnew[n]);
+          lpart[n] = lpart[n] * alpha[n] + p;
+        }
+        *reinterpret_cast<__half*>(pbuf + (k >> 6) * (kN * 128) + sw128_off16(n, k & 63)) = __float2half_rn(p);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.p_full[sb]);
+      if (j > 0) ok = consume_o(j - 1);
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n) alpha_prev[n] = alpha[n];
+    }
+    if (ok) ok = consume_o(ntiles - 1);
+    // ---- epilogue: row sums, normalise, store
+    float l[RMAX];
+#pragma unroll
+    for (int n = 0; n < RMAX; ++n) l[n] = warp_sum(lpart[n]);
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (lane == 0) {
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n) sm.red[warp][n] = l[n];
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+    for (int n = 0; n < RMAX; ++n) l[n] = sm.red[0][n] + sm.red[1][n] + sm.red[2][n] + sm.red[3][n];
+    if (ok) {
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n) {
+        if (n >= R) break;
+        const int t = n / G, g = n % G;
+        const float inv = l[n] > 0.f ? a.v_scale / l[n] : 0.f;
+        if (a.num_splits == 1) {
+          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) +
+                             ((static_cast<size_t>(b) * a.n_q + t) * a.Hq + h * G + g) * D;
+#pragma unroll
+          for (int mb = 0; mb < MB; ++mb) o[mb * 128 + 32 * warp + lane] = __float2bfloat16(acc[mb][n] * inv);
+        } else {
+          float* o = a.o_part + (part_out * RMAX + n) * D;
+#pragma unroll
+          for (int mb = 0; mb < MB; ++mb) o[mb * 128 + 32 * warp + lane] = acc[mb][n] * inv;
+          if (warp == 0 && lane == 0)
+            a.lse_part[part_out * RMAX + n] = l[n] > 0.f ? sm.row_m[n] + log2f(l[n]) : -INFINITY;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// Merge split partials: out = sum_s 2^(lse_s - lse_max) o_s / sum_s 2^(lse_s - lse_max).  One CTA per (b, kvh, row).
+template <int RMAX>
+__global__ void gqa_combine_kernel(const GqaDecodeArgs a) {
+  const int G = a.Hq / a.Hk;
+  const int n = blockIdx.x % RMAX;
+  const int bh = blockIdx.x / RMAX;
+  if (n >= a.n_q * G) return;
+  const int h = bh % a.Hk, b = bh / a.Hk;
+  const int t = n / G, g = n % G;
+  const float* lse = a.lse_part + static_cast<size_t>(bh) * a.num_splits * RMAX;
+  float m = -INFINITY;
+  for (int s = 0; s < a.num_splits; ++s) m = fmaxf(m, lse[s * RMAX + n]);
+  __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + ((static_cast<size_t>(b) * a.n_q + t) * a.Hq + h * G + g) * a.D;
+  for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < a.num_splits; ++s) {
+      const float ls = lse[s * RMAX + n];
+      if (ls == -INFINITY) continue;
+      const float w = exp2f(ls - m);
+      num += w * a.o_part[((static_cast<size_t>(bh) * a.num_splits + s) * RMAX + n) * a.D + d];
+      den += w;
+    }
+    o[d] = __float2bfloat16(den > 0.f ? num / den : 0.f);
+  }
+}
+
+template <int FMT, int D, int RMAX>
+cudaError_t launch_t(const GqaDecodeArgs& a, cudaStream_t s) {
+  constexpr int PB = part_bytes<FMT, D>();
+  constexpr int NST = (PB <= 20 * 1024) ? 6 : ((PB <= 32 * 1024) ? 4 : 2);
+  const int smem = 1024 + kRing * kSlabBytes + (D / 64) * kN * 128 + 4 * kN * 128 + NST * PB + sizeof(Smem);
+  auto kern = gqa_decode_kernel<FMT, D, RMAX>;
+  IOB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  kern<<<a.B * a.Hk * a.num_splits, kThreads, smem, s>>>(a);
+  IOB_CUDA_CHECK(cudaGetLastError());
+  if (a.num_splits > 1) {
+    gqa_combine_kernel<RMAX><<<a.B * a.Hk * RMAX, 128, 0, s>>>(a);
+    IOB_CUDA_CHECK(cudaGetLastError());
+  }
+  return cudaSuccess;
+}
+
+template <int FMT, int D>
+cudaError_t launch_r(const GqaDecodeArgs& a, cudaStream_t s) {
+  const int R = a.n_q * (a.Hq / a.Hk);
+  if (R <= 8) return launch_t<FMT, D, 8>(a, s);
+  if (R <= 16) return launch_t<FMT, D, 16>(a, s);
+  return cudaErrorInvalidValue;
+}
+
+template <int FMT>
+cudaError_t launch_d(const GqaDecodeArgs& a, cudaStream_t s) {
+  switch (a.D) {
+    case 128: return launch_r<FMT, 128>(a, s);
+    case 256: return launch_r<FMT, 256>(a, s);
+    case 512: return launch_r<FMT, 512>(a, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+cudaError_t gqa_decode(const GqaDecodeArgs& a, cudaStream_t s) {
+  if (a.B == 0) return cudaSuccess;
+  if (a.page != 64 || a.Hq % a.Hk != 0 || a.num_splits < 1 || a.tiles_per_split < 1) return cudaErrorInvalidValue;
+  switch (a.fmt) {
+    case kKvNvfp4: return launch_d<kKvNvfp4>(a, s);
+    case kKvFp8: return launch_d<kKvFp8>(a, s);
+    case kKvBf16: return launch_d<kKvBf16>(a, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace iob

@@ -1,0 +1,203 @@
+// Torch bindings for the sm_100a kernels.  Each binding validates shapes/dtypes, then calls the plain-pointer launcher
+// on the current CUDA stream (so CUDA-graph capture and stream ordering follow torch's).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "kernels.h"
+
+namespace {
+
+#define CHECK_CUDA_OK(expr)                                                         \
+  do {                                                                              \
+    cudaError_t _e = (expr);                                                        \
+    TORCH_CHECK(_e == cudaSuccess, #expr, " failed: ", cudaGetErrorString(_e));     \
+  } while (0)
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void req(const at::Tensor& t, at::ScalarType dt, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == dt, name, " has dtype ", t.scalar_type(), ", expected ", dt);
+}
+
+void rmsnorm(const at::Tensor& x, c10::optional<at::Tensor> residual, at::Tensor out, const at::Tensor& w, double eps,
+             bool plus_one) {
+  req(x, at::kBFloat16, "x");
+  req(out, at::kBFloat16, "out");
+  req(w, at::kBFloat16, "weight");
+  const int hidden = x.size(-1);
+  const int rows = x.numel() / hidden;
+  TORCH_CHECK(x.stride(-1) == 1 && out.is_contiguous() && w.is_contiguous(), "layout");
+  const int stride = x.dim() > 1 ? x.stride(-2) : hidden;
+  void* res = nullptr;
+  if (residual.has_value()) {
+    req(*residual, at::kBFloat16, "residual");
+    TORCH_CHECK(residual->is_contiguous(), "residual layout");
+    res = residual->data_ptr();
+  }
+  const at::cuda::CUDAGuard g(x.device());
+  CHECK_CUDA_OK(iob::rmsnorm(x.data_ptr(), res, out.data_ptr(), w.data_ptr(), rows, hidden, stride, eps, plus_one,
+                             res != nullptr, stream()));
+}
+
+void act_mul(const at::Tensor& gu, at::Tensor out, bool gelu) {
+  req(gu, at::kBFloat16, "gate_up");
+  req(out, at::kBFloat16, "out");
+  TORCH_CHECK(gu.is_contiguous() && out.is_contiguous(), "layout");
+  const int ffn = out.size(-1);
+  const int rows = out.numel() / ffn;
+  TORCH_CHECK(gu.size(-1) == 2 * ffn && ffn % 8 == 0, "shape");
+  const at::cuda::CUDAGuard g(gu.device());
+  if (gelu) CHECK_CUDA_OK(iob::gelu_tanh_mul(gu.data_ptr(), out.data_ptr(), rows, ffn, stream()));
+  else CHECK_CUDA_OK(iob::silu_mul(gu.data_ptr(), out.data_ptr(), rows, ffn, stream()));
+}
+
+void embed(const at::Tensor& ids, const at::Tensor& table, at::Tensor out, double scale) {
+  req(ids, at::kInt, "ids");
+  req(table, at::kBFloat16, "table");
+  req(out, at::kBFloat16, "out");
+  const at::cuda::CUDAGuard g(ids.device());
+  CHECK_CUDA_OK(iob::embed(ids.data_ptr<int>(), table.data_ptr(), out.data_ptr(), ids.numel(), table.size(1),
+                           scale, stream()));
+}
+
+void argmax(const at::Tensor& logits, at::Tensor idx, c10::optional<at::Tensor> val) {
+  TORCH_CHECK(logits.is_cuda() && logits.stride(-1) == 1, "logits");
+  req(idx, at::kInt, "idx");
+  const bool f32 = logits.scalar_type() == at::kFloat;
+  TORCH_CHECK(f32 || logits.scalar_type() == at::kBFloat16, "logits dtype");
+  const int vocab = logits.size(-1);
+  TORCH_CHECK(vocab % 8 == 0, "vocab % 8");
+  float* v = nullptr;
+  if (val.has_value()) { req(*val, at::kFloat, "val"); v = val->data_ptr<float>(); }
+  const at::cuda::CUDAGuard g(logits.device());
+  CHECK_CUDA_OK(iob::argmax_rows(logits.data_ptr(), idx.data_ptr<int>(), v, logits.numel() / vocab, vocab,
+                                 logits.dim() > 1 ? logits.stride(-2) : vocab, f32, stream()));
+}
+
+void gqa_prep(const at::Tensor& qkv, c10::optional<at::Tensor> q_norm, c10::optional<at::Tensor> k_norm,
+              const at::Tensor& cos_sin, const at::Tensor& pos, const at::Tensor& slot, at::Tensor q_out,
+              at::Tensor pool, int64_t fmt, double k_scale, double v_scale, int64_t Hq, int64_t Hk, int64_t D,
+              int64_t page, double eps, bool plus_one) {
+  req(qkv, at::kBFloat16, "qkv");
+  req(cos_sin, at::kFloat, "cos_sin");
+  req(pos, at::kInt, "pos");
+  req(slot, at::kInt, "slot");
+  req(q_out, at::kBFloat16, "q_out");
+  req(pool, at::kByte, "pool");
+  TORCH_CHECK(qkv.stride(-1) == 1 && qkv.size(-1) >= (Hq + 2 * Hk) * D, "qkv shape");
+  TORCH_CHECK(cos_sin.size(-1) == D, "cos_sin width");
+  iob::GqaPrepArgs a{};
+  a.qkv = qkv.data_ptr();
+  a.qkv_stride = qkv.stride(0);
+  a.q_norm = q_norm.has_value() ? q_norm->data_ptr() : nullptr;
+  a.k_norm = k_norm.has_value() ? k_norm->data_ptr() : nullptr;
+  a.cos_sin = cos_sin.data_ptr<float>();
+  a.pos = pos.data_ptr<int>();
+  a.slot = slot.data_ptr<int>();
+  a.q_out = q_out.data_ptr();
+  a.pool = pool.data_ptr<uint8_t>();
+  a.fmt = fmt;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  a.T = qkv.size(0);
+  a.Hq = Hq; a.Hk = Hk; a.D = D; a.page = page;
+  a.eps = eps;
+  a.plus_one = plus_one;
+  const at::cuda::CUDAGuard g(qkv.device());
+  CHECK_CUDA_OK(iob::gqa_prep(a, stream()));
+}
+
+void mla_quant_write(const at::Tensor& nope, const at::Tensor& rope, const at::Tensor& slot, at::Tensor pool,
+                     int64_t fmt) {
+  req(nope, at::kBFloat16, "nope");
+  req(rope, at::kBFloat16, "rope");
+  req(slot, at::kInt, "slot");
+  req(pool, at::kByte, "pool");
+  TORCH_CHECK(nope.size(-1) == 512 && rope.size(-1) == 64 && nope.stride(-1) == 1 && rope.stride(-1) == 1, "shape");
+  TORCH_CHECK(pool.size(-1) == (fmt == iob::kKvNvfp4 ? 352 : 576), "pool row bytes");
+  const at::cuda::CUDAGuard g(nope.device());
+  CHECK_CUDA_OK(iob::mla_quant_write(nope.data_ptr(), nope.stride(0), rope.data_ptr(), rope.stride(0),
+                                     slot.data_ptr<int>(), pool.data_ptr<uint8_t>(), nope.size(0), fmt, stream()));
+}
+
+void index_key_write(const at::Tensor& k, const at::Tensor& slot, at::Tensor pool) {
+  req(k, at::kBFloat16, "k");
+  req(slot, at::kInt, "slot");
+  req(pool, at::kByte, "pool");
+  TORCH_CHECK(k.size(-1) == 128 && k.stride(-1) == 1 && pool.size(-1) == 132, "shape");
+  const at::cuda::CUDAGuard g(k.device());
+  CHECK_CUDA_OK(iob::index_key_write(k.data_ptr(), k.stride(0), slot.data_ptr<int>(), pool.data_ptr<uint8_t>(),
+                                     k.size(0), stream()));
+}
+
+void gqa_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& page_table, const at::Tensor& kv_len,
+                at::Tensor out, at::Tensor o_part, at::Tensor lse_part, at::Tensor status, int64_t n_q, int64_t Hk,
+                int64_t page, int64_t window, int64_t fmt, int64_t tiles_per_split, int64_t num_splits,
+                double sm_scale, double k_scale, double v_scale) {
+  req(q, at::kBFloat16, "q");
+  req(pool, at::kByte, "pool");
+  req(page_table, at::kInt, "page_table");
+  req(kv_len, at::kInt, "kv_len");
+  req(out, at::kBFloat16, "out");
+  req(o_part, at::kFloat, "o_part");
+  req(lse_part, at::kFloat, "lse_part");
+  req(status, at::kInt, "status");
+  TORCH_CHECK(q.is_contiguous() && out.is_contiguous() && page_table.is_contiguous(), "layout");
+  TORCH_CHECK(q.dim() == 3, "q [B*n_q, Hq, D]");
+  iob::GqaDecodeArgs a{};
+  a.q = q.data_ptr();
+  a.pool = pool.data_ptr<uint8_t>();
+  a.page_table = page_table.data_ptr<int>();
+  a.kv_len = kv_len.data_ptr<int>();
+  a.out = out.data_ptr();
+  a.o_part = o_part.data_ptr<float>();
+  a.lse_part = lse_part.data_ptr<float>();
+  a.status = status.data_ptr<int>();
+  a.B = kv_len.size(0);
+  a.n_q = n_q;
+  a.Hq = q.size(1);
+  a.Hk = Hk;
+  a.D = q.size(2);
+  a.pt_stride = page_table.size(1);
+  a.page = page;
+  a.window = window;
+  a.fmt = fmt;
+  a.tiles_per_split = tiles_per_split;
+  a.num_splits = num_splits;
+  a.sm_scale = sm_scale;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
+  TORCH_CHECK(q.size(0) == a.B * n_q, "q rows");
+  const int rmax = a.n_q * (a.Hq / a.Hk) <= 8 ? 8 : 16;
+  if (num_splits > 1)
+    TORCH_CHECK(o_part.numel() >= (int64_t)a.B * Hk * num_splits * rmax * a.D &&
+                    lse_part.numel() >= (int64_t)a.B * Hk * num_splits * rmax,
+                "split workspace too small");
+  const at::cuda::CUDAGuard g(q.device());
+  CHECK_CUDA_OK(iob::gqa_decode(a, stream()));
+}
+
+void umma_gemm_test(const at::Tensor& A, const at::Tensor& B, at::Tensor C) {
+  req(A, at::kBFloat16, "A");
+  req(B, at::kBFloat16, "B");
+  req(C, at::kFloat, "C");
+  const at::cuda::CUDAGuard g(A.device());
+  CHECK_CUDA_OK(iob::umma_gemm_test(A.data_ptr(), B.data_ptr(), C.data_ptr<float>(), A.size(0), B.size(0),
+                                    A.size(1), stream()));
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("rmsnorm", &rmsnorm);
+  m.def("act_mul", &act_mul);
+  m.def("embed", &embed);
+  m.def("argmax", &argmax);
+  m.def("gqa_prep", &gqa_prep);
+  m.def("mla_quant_write", &mla_quant_write);
+  m.def("index_key_write", &index_key_write);
+  m.def("gqa_decode", &gqa_decode);
+  m.def("umma_gemm_test", &umma_gemm_test);
+}

@@ -1,0 +1,270 @@
+// Device-side building blocks for the sm_100a kernels of this package: mbarriers, bulk async copies, tcgen05
+// (TMEM allocation, UMMA issue/commit, TMEM loads), shared-memory / instruction descriptors, FP4/FP8 conversions
+// and bounded waits.  Written against the PTX ISA; descriptor bit positions cross-checked with CUTLASS's
+// cute/arch/mma_sm100_desc.hpp (SmemDescriptor / InstrDescriptor).  No multicast variants exist here on purpose:
+// nothing in this package issues a cluster-multicast load.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+
+namespace iob {
+
+// ----------------------------------------------------------------------------------------------- status words
+// Kernels that wait on anything (mbarrier, peer flag) take an `int* status` in global memory.  A wait that runs
+// past its limit records one of these codes (first writer wins) and the kernel unwinds instead of hanging.
+enum StatusCode : int {
+  kOk = 0,
+  kTimeoutProducer = 1,
+  kTimeoutMma = 2,
+  kTimeoutConsumer = 3,
+  kTimeoutPeer = 4,
+  kBadIndex = 5,
+};
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitimate wait
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void record_status(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+// ----------------------------------------------------------------------------------------------- small helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+__device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_max(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ----------------------------------------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait.  `abort` is a shared-memory flag: once any role of the CTA gave up, every later wait returns false
+// at once so the whole CTA unwinds within one limit.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                          int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (abort && *abort) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      if (abort) *abort = 1;
+      record_status(status, code);
+      return false;
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------------------------- async copies
+// Plain (non-tensor, non-multicast) bulk copy global -> this CTA's shared memory, completing on an mbarrier.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ----------------------------------------------------------------------------------------------- tcgen05 / TMEM
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D(tmem) (+)= A(smem desc) * B(smem desc)^T, kind::f16 (f16 or bf16 inputs, fp32 accumulate); one thread issues.
+__device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D(tmem) (+)= A(smem desc) * B(smem desc)^T, kind::f8f6f4 (E4M3/E5M2/... inputs, fp32 accumulate).
+__device__ __forceinline__ void umma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on `bar` once every previously issued tcgen05.mma of this thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Warp w (w = warp index % 4) reads TMEM lanes 32w..32w+31; thread t gets lane 32w+t, columns [col, col+16).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+// Shared-memory matrix descriptor, K-major operand in the 128-byte-swizzle canonical layout: rows of 128 bytes,
+// the 16-byte chunk c of row r stored at chunk c ^ (r & 7), 8-row groups 1024 bytes apart (SBO).  Tiles whose K
+// extent exceeds one 128-byte row are stored as separate [rows x 128 B] slabs; a K step inside a slab advances the
+// start address by its byte offset.  Bits: [0,14) addr>>4, [16,30) LBO>>4, [32,46) SBO>>4, [46,48) version = 1,
+// [49,52) base offset, [61,64) layout (2 = SWIZZLE_128B).  Slab bases must be 1024-byte aligned.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 / kind::f8f6f4 dense MMA, both operands K-major, fp32 accumulator.
+// fmt: kind::f16 -> 0 = f16, 1 = bf16;  kind::f8f6f4 -> 0 = E4M3, 1 = E5M2.
+__host__ __device__ constexpr uint32_t idesc_dense(uint32_t a_fmt, uint32_t b_fmt, uint32_t m, uint32_t n) {
+  return (1u << 4) | (a_fmt << 7) | (b_fmt << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// Byte offset of element (row, k) of 2-byte elements inside a [rows x 64] SW128 K-major slab.
+__device__ __forceinline__ uint32_t sw128_off16(uint32_t row, uint32_t k) {
+  const uint32_t chunk = (k >> 3) ^ (row & 7);
+  return row * 128u + chunk * 16u + (k & 7) * 2u;
+}
+// Byte offset of the 16-byte chunk `c` (0..7) of row `row` inside a SW128 slab.
+__device__ __forceinline__ uint32_t sw128_chunk(uint32_t row, uint32_t c) {
+  return row * 128u + ((c ^ (row & 7)) * 16u);
+}
+
+// ----------------------------------------------------------------------------------------------- FP4 / FP8
+// Two E2M1 codes (one byte, element 2i in the low nibble) -> f16x2, exact.
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint8_t b) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .b8 t;\n\t"
+      "mov.b16 {t, _}, %1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, t;\n\t}\n"
+      : "=r"(out)
+      : "h"(static_cast<uint16_t>(b)));
+  return out;
+}
+// Two E4M3 bytes (low byte = first element) -> f16x2, exact.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
+  uint32_t out;
+  asm volatile("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(out) : "h"(v));
+  return out;
+}
+__device__ __forceinline__ float e4m3_to_float(uint8_t v) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(v), __NV_E4M3);
+  return __half2float(__half(h));
+}
+__device__ __forceinline__ uint8_t float_to_e4m3(float x) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));
+}
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t half2_bcast(__half h) {
+  __half2 r = __halves2half2(h, h);
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// E2M1 magnitude code of y >= 0: number of midpoints strictly below y (ties round down), saturating at 7 (= 6.0).
+__device__ __forceinline__ uint32_t e2m1_code_mag(float y) {
+  return (y > 0.25f) + (y > 0.75f) + (y > 1.25f) + (y > 1.75f) + (y > 2.5f) + (y > 3.5f) + (y > 5.0f);
+}
+__device__ __forceinline__ uint32_t e2m1_code(float y) {  // signed, no negative zero
+  const uint32_t m = e2m1_code_mag(fabsf(y));
+  return m | ((y < 0.f && m > 0) ? 8u : 0u);
+}
+// Block scale rule shared by every NVFP4 writer: e4m3(clamp(amax / 6, 2^-9, 448)).
+__device__ __forceinline__ uint8_t nvfp4_block_scale(float amax) {
+  const float s = fminf(fmaxf(amax / 6.0f, 0.001953125f), 448.0f);
+  return float_to_e4m3(s);
+}
+
+}  // namespace iob
+
+#define IOB_CUDA_CHECK(expr)                                                                   \
+  do {                                                                                         \
+    cudaError_t _e = (expr);                                                                   \
+    if (_e != cudaSuccess) return _e;                                                          \
+  } while (0)

@@ -1,0 +1,91 @@
+// Host-side launch API of the CUDA kernels.  Plain pointers and a stream: no torch types, so the .cu files compile
+// without torch headers and the same launchers serve the torch bindings (bindings.cpp) and C callers.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace iob {
+
+enum KvFormat : int { kKvBf16 = 0, kKvFp8 = 1, kKvNvfp4 = 2 };
+
+// Bytes of one (page, kv_head) block of a GQA pool page: K then V, each page_size tokens of head_dim values.
+//   bf16 : [K 64 x D x 2][V 64 x D x 2]
+//   fp8  : [K 64 x D][V 64 x D]                      (E4M3, per-layer k/v scale)
+//   nvfp4: [Kcodes 64 x D/2][Kscales 64 x D/16][Vcodes 64 x D/2][Vscales 64 x D/16]   (+ per-layer global scale)
+#if defined(__CUDACC__)
+__host__ __device__
+#endif
+inline int gqa_block_bytes(int fmt, int head_dim, int page) {
+  if (fmt == kKvBf16) return 2 * page * head_dim * 2;
+  if (fmt == kKvFp8) return 2 * page * head_dim;
+  return 2 * page * (head_dim / 2 + head_dim / 16);
+}
+
+// ---- elementwise / normalisation (elementwise.cu)
+cudaError_t rmsnorm(const void* x, void* residual, void* out, const void* weight, int rows, int hidden,
+                    int x_stride, float eps, bool plus_one, bool add_residual, cudaStream_t s);
+cudaError_t gelu_tanh_mul(const void* gate_up, void* out, int rows, int ffn, cudaStream_t s);
+cudaError_t silu_mul(const void* gate_up, void* out, int rows, int ffn, cudaStream_t s);
+cudaError_t embed(const int* ids, const void* table, void* out, int rows, int hidden, float scale, cudaStream_t s);
+cudaError_t argmax_rows(const void* logits, int* out_idx, float* out_val, int rows, int vocab, int stride,
+                        bool logits_fp32, cudaStream_t s);
+
+// Fused GQA QKV epilogue: per-head RMSNorm of q and k, NeoX RoPE (cos/sin table [max_pos, D]: D/2 cos then D/2
+// sin), q written as bf16 [T, Hq, D], k/v quantized into the paged pool at slot[t] (page = slot / 64).
+struct GqaPrepArgs {
+  const void* qkv;      // bf16 [T, (Hq + 2 Hk) * D], row stride qkv_stride elements
+  int qkv_stride;
+  const void* q_norm;   // bf16 [D] or null (no norm)
+  const void* k_norm;
+  const float* cos_sin; // fp32 [max_pos, D]
+  const int* pos;       // [T]
+  const int* slot;      // [T], -1 = do not write
+  void* q_out;          // bf16 [T, Hq, D]
+  uint8_t* pool;        // layer pool base: [num_pages, Hk, block_bytes]
+  int fmt;
+  float k_scale, v_scale;  // fp8: e4m3(x / scale); nvfp4: global scale
+  int T, Hq, Hk, D, page;
+  float eps;
+  bool plus_one;
+};
+cudaError_t gqa_prep(const GqaPrepArgs& a, cudaStream_t s);
+
+// MLA latent rows: nope [T, 512] + rope [T, 64] (bf16) -> pool row slot[t]; fmt kKvNvfp4 (352 B) or kKvFp8 (576 B).
+cudaError_t mla_quant_write(const void* nope, int nope_stride, const void* rope, int rope_stride, const int* slot,
+                            uint8_t* pool, int T, int fmt, cudaStream_t s);
+// Indexer keys [T, 128] bf16 -> 132-byte rows (E4M3 * per-token fp32 scale).
+cudaError_t index_key_write(const void* k, int k_stride, const int* slot, uint8_t* pool, int T, cudaStream_t s);
+
+// Pool rows (one token's K or V codes of one head) are stored with their 16-byte chunks XOR-swizzled by the token's
+// row in the page: chunk j of row r lives at chunk (j & ~(n-1)) | ((j ^ r) & (n-1)), n = min(8, row_bytes / 16).
+// Readers that fetch the same chunk of 8 consecutive rows then hit 8 different shared-memory bank groups.
+#if defined(__CUDACC__)
+__host__ __device__
+#endif
+inline int kv_swizzle_byte(int byte_in_row, int row, int row_bytes) {
+  const int nch = (row_bytes / 16) < 8 ? (row_bytes / 16) : 8;
+  const int j = byte_in_row >> 4;
+  const int pos = (j & ~(nch - 1)) | ((j ^ row) & (nch - 1));
+  return (pos << 4) | (byte_in_row & 15);
+}
+
+// ---- GQA split-K decode / verify attention (attn_gqa_decode.cu)
+struct GqaDecodeArgs {
+  const void* q;           // bf16 [B * n_q, Hq, D] (normed + roped)
+  const uint8_t* pool;     // layer pool [num_pages, Hk, 2 parts (K, V), part_bytes]
+  const int* page_table;   // [B, pt_stride] physical page per logical page
+  const int* kv_len;       // [B] tokens in the pool (query tokens included, they are the last n_q)
+  void* out;               // bf16 [B * n_q, Hq, D]
+  float* o_part;           // [B * Hk * num_splits, RMAX, D]  (num_splits > 1)
+  float* lse_part;         // [B * Hk * num_splits, RMAX]     (log2 units)
+  int* status;             // device status word (bounded-wait timeouts)
+  int B, n_q, Hq, Hk, D, pt_stride, page, window, fmt;
+  int tiles_per_split, num_splits;
+  float sm_scale, k_scale, v_scale;
+};
+cudaError_t gqa_decode(const GqaDecodeArgs& a, cudaStream_t s);
+
+// ---- primitive check (umma_test.cu): C[M, N] fp32 = A[M, K] * B[N, K]^T, bf16 inputs, one CTA per 128 rows.
+cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, cudaStream_t s);
+
+}  // namespace iob

@@ -1,0 +1,88 @@
+// Minimal tcgen05 GEMM used by the GPU tests to validate the primitives every tensor-core kernel here is built on:
+// SW128 K-major shared-memory descriptors, the kind::f16 instruction descriptor, single-thread UMMA issue with
+// commit-to-mbarrier, and the TMEM accumulator layout read back with tcgen05.ld (lane = row, column = n).
+// C[M, N] fp32 = A[M, K] * B[N, K]^T; A, B bf16 row-major; M % 128 == 0, N % 16 == 0, N <= 256, K % 64 == 0.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace iob {
+namespace {
+
+__global__ void __launch_bounds__(128) umma_gemm_kernel(const __nv_bfloat16* __restrict__ A,
+                                                        const __nv_bfloat16* __restrict__ B, float* __restrict__ C,
+                                                        int N, int K) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;                 // 128 x 128 B
+  uint8_t* sB = smem + 128 * 128;     // N x 128 B
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_base;
+  const int m0 = blockIdx.x * 128;
+  uint32_t ncols = 32;
+  while (ncols < (uint32_t)N) ncols <<= 1;
+  if (warp_id() == 0) {
+    tmem_alloc(&tmem_base, ncols);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base;
+  const uint32_t idesc = idesc_dense(1, 1, 128, N);
+  uint32_t phase = 0;
+  for (int k0 = 0; k0 < K; k0 += 64) {
+    for (int c = threadIdx.x; c < 128 * 8; c += blockDim.x) {
+      const int r = c >> 3, ch = c & 7;
+      *reinterpret_cast<uint4*>(sA + sw128_chunk(r, ch)) =
+          *reinterpret_cast<const uint4*>(A + (size_t)(m0 + r) * K + k0 + ch * 8);
+    }
+    for (int c = threadIdx.x; c < N * 8; c += blockDim.x) {
+      const int r = c >> 3, ch = c & 7;
+      *reinterpret_cast<uint4*>(sB + sw128_chunk(r, ch)) =
+          *reinterpret_cast<const uint4*>(B + (size_t)r * K + k0 + ch * 8);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        umma_f16_ss(tbase, desc_sw128(smem_u32(sA) + kk * 32), desc_sw128(smem_u32(sB) + kk * 32), idesc,
+                    (k0 > 0 || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(&bar);
+    }
+    mbar_wait(&bar, phase, nullptr, nullptr, 0);
+    phase ^= 1;
+    tc_fence_after();
+  }
+  const int w = warp_id();
+  for (int col = 0; col < N; col += 16) {
+    uint32_t r[16];
+    tmem_ld16(tbase + (static_cast<uint32_t>(32 * w) << 16) + col, r);
+    tmem_ld_wait();
+    float* dst = C + (size_t)(m0 + 32 * w + lane_id()) * N + col;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) dst[j] = __uint_as_float(r[j]);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp_id() == 0) tmem_dealloc(tbase, ncols);
+}
+
+}  // namespace
+
+cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, cudaStream_t s) {
+  if (M % 128 || N % 16 || N > 256 || K % 64) return cudaErrorInvalidValue;
+  const int smem = 1024 + 128 * 128 + N * 128;
+  IOB_CUDA_CHECK(cudaFuncSetAttribute(umma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  umma_gemm_kernel<<<M / 128, 128, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(A),
+                                             reinterpret_cast<const __nv_bfloat16*>(B), C, N, K);
+  return cudaGetLastError();
+}
+
+}  // namespace iob

@@ -1,0 +1,115 @@
+"""GQA attention over the paged pool: split-K decode / speculative verify (csrc/attn_gqa_decode.cu) and the fp32
+oracle.  Semantics of the reference's grouped decode and split-K verify (`attention/verify-splitk/gemma31_verify.py:1-24`,
+`kv-cache-4bit/kv4tri-triton-backend/kv4tri_nvfp4_attention.py:257`): request b has kv_len[b] tokens in the pool, the
+last n_q of which are its query tokens; query token t sees key positions p <= q_pos(t) and, with a sliding window W,
+only q_pos(t) - p < W (W = 1024 on Gemma sliding layers: each query sees 1024 keys including itself)."""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from .._ext import ext
+from .kvcache import gqa_pool_read_ref
+
+NUM_SMS = 148
+TILE = 128
+
+
+def split_policy(batch_heads: int, max_ctx: int, window: int = 0, target_ctas: int = 2 * NUM_SMS,
+                 min_tiles: int = 4) -> tuple[int, int]:
+    """(num_splits, tiles_per_split): enough CTAs to fill the 148 SMs twice, at least `min_tiles` 128-token tiles
+    per split.  Fixed per (batch, context bound) so a captured CUDA graph keeps a valid schedule."""
+    span = min(max_ctx, window + TILE) if window > 0 else max_ctx
+    tiles = max(1, (span + TILE - 1) // TILE + (1 if window > 0 else 0))
+    splits = max(1, min((target_ctas + batch_heads - 1) // batch_heads, tiles // min_tiles))
+    tps = (tiles + splits - 1) // splits
+    splits = (tiles + tps - 1) // tps
+    return splits, tps
+
+
+@dataclass
+class DecodeWorkspace:
+    o_part: torch.Tensor
+    lse_part: torch.Tensor
+    status: torch.Tensor
+
+    @staticmethod
+    def allocate(max_b: int, hk: int, max_splits: int, d: int, rmax: int = 16, device="cuda") -> "DecodeWorkspace":
+        n = max_b * hk * max_splits * rmax
+        return DecodeWorkspace(torch.empty(n * d, dtype=torch.float32, device=device),
+                               torch.empty(n, dtype=torch.float32, device=device),
+                               torch.zeros(1, dtype=torch.int32, device=device))
+
+
+def gqa_decode(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor, kv_len: torch.Tensor, n_q: int,
+               hk: int, fmt: int, sm_scale: float, window: int = 0, k_scale: float = 1.0, v_scale: float = 1.0,
+               splits: Optional[tuple[int, int]] = None, ws: Optional[DecodeWorkspace] = None,
+               max_ctx: Optional[int] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q bf16 [B * n_q, Hq, D] -> out bf16 [B * n_q, Hq, D]."""
+    b = kv_len.shape[0]
+    d = q.shape[-1]
+    if out is None:
+        out = torch.empty_like(q)
+    if not q.is_cuda:
+        out.copy_(gqa_decode_ref(q, pool, page_table, kv_len, n_q, hk, fmt, sm_scale, window, k_scale, v_scale)
+                  .to(out.dtype))
+        return out
+    if splits is None:
+        if max_ctx is None:
+            max_ctx = int(kv_len.max().item())
+        splits = split_policy(b * hk, max_ctx, window)
+    ns, tps = splits
+    if ws is None:
+        ws = DecodeWorkspace.allocate(b, hk, ns, d, device=q.device)
+    ext().gqa_decode(q, pool, page_table, kv_len, out, ws.o_part, ws.lse_part, ws.status, n_q, hk, 64, window, fmt,
+                     tps, ns, sm_scale, k_scale, v_scale)
+    return out
+
+
+def gqa_decode_ref(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor, kv_len: torch.Tensor, n_q: int,
+                   hk: int, fmt: int, sm_scale: float, window: int = 0, k_scale: float = 1.0,
+                   v_scale: float = 1.0) -> torch.Tensor:
+    b = kv_len.shape[0]
+    hq, d = q.shape[1], q.shape[2]
+    g = hq // hk
+    out = torch.zeros(b * n_q, hq, d, dtype=torch.float32)
+    for i in range(b):
+        n = int(kv_len[i])
+        k, v = gqa_pool_read_ref(pool, page_table[i].cpu(), n, fmt, d, k_scale, v_scale)   # [n, Hk, D]
+        kk = k.repeat_interleave(g, dim=1)
+        vv = v.repeat_interleave(g, dim=1)
+        for t in range(n_q):
+            qpos = n - n_q + t
+            p = torch.arange(n)
+            vis = p <= qpos
+            if window > 0:
+                vis &= (qpos - p) < window
+            qi = q[i * n_q + t].float().cpu()                                  # [Hq, D]
+            s = torch.einsum("hd,nhd->hn", qi, kk[vis]) * sm_scale
+            pr = torch.softmax(s, dim=-1)
+            out[i * n_q + t] = torch.einsum("hn,nhd->hd", pr, vv[vis])
+    return out.to(q.device)
+
+
+def dense_attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float, q_pos: torch.Tensor,
+                        k_pos: torch.Tensor, window: int = 0) -> torch.Tensor:
+    """fp32 GQA attention on contiguous tensors: q [Tq, Hq, D], k/v [Tk, Hk, D], causal by positions (+ window)."""
+    hq, hk = q.shape[1], k.shape[1]
+    g = hq // hk
+    kk = k.float().repeat_interleave(g, dim=1)
+    vv = v.float().repeat_interleave(g, dim=1)
+    s = torch.einsum("qhd,khd->hqk", q.float(), kk) * sm_scale
+    vis = k_pos[None, :] <= q_pos[:, None]
+    if window > 0:
+        vis &= (q_pos[:, None] - k_pos[None, :]) < window
+    s = s.masked_fill(~vis[None], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    p = torch.nan_to_num(p, nan=0.0)
+    return torch.einsum("hqk,khd->qhd", p, vv)
+
+
+def sm_scale_for(d: int) -> float:
+    return 1.0 / math.sqrt(d)

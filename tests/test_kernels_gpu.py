@@ -1,0 +1,149 @@
+"""sm_100a kernels against the fp32 torch oracles (bit-exact for quantized writes, toleranced for math)."""
+import math
+
+import pytest
+import torch
+
+from inference_optimizations_b200.ops import attention as A
+from inference_optimizations_b200.ops import basic as B
+from inference_optimizations_b200.ops import formats as F
+from inference_optimizations_b200.ops import kvcache as K
+
+pytestmark = pytest.mark.gpu
+
+
+def test_umma_primitives(cuda):
+    from inference_optimizations_b200._ext import ext
+    torch.manual_seed(0)
+    for (m, n, k) in [(128, 16, 64), (256, 64, 256), (128, 256, 512)]:
+        a = torch.randn(m, k, device=cuda).to(torch.bfloat16)
+        b = torch.randn(n, k, device=cuda).to(torch.bfloat16)
+        c = torch.empty(m, n, device=cuda)
+        ext().umma_gemm_test(a, b, c)
+        torch.cuda.synchronize()
+        ref = a.float() @ b.float().T
+        assert torch.allclose(c, ref, rtol=1e-3, atol=1e-2), (m, n, k, (c - ref).abs().max().item())
+
+
+@pytest.mark.parametrize("hidden,residual", [(5376, True), (7168, False), (256, True)])
+def test_rmsnorm(cuda, hidden, residual):
+    torch.manual_seed(1)
+    x = torch.randn(7, hidden, device=cuda).to(torch.bfloat16)
+    w = (torch.randn(hidden, device=cuda) * 0.1).to(torch.bfloat16)
+    r = torch.randn(7, hidden, device=cuda).to(torch.bfloat16) if residual else None
+    r_ref = r.cpu().clone() if residual else None
+    y = B.rmsnorm(x, w, 1e-6, True, r)
+    y_ref = B.rmsnorm(x.cpu(), w.cpu(), 1e-6, True, r_ref)
+    assert torch.allclose(y.cpu().float(), y_ref.float(), rtol=2e-2, atol=2e-2)
+    if residual:
+        assert torch.equal(r.cpu(), r_ref)
+
+
+def test_act_embed_argmax(cuda):
+    torch.manual_seed(2)
+    gu = torch.randn(5, 2 * 1024, device=cuda).to(torch.bfloat16)
+    for gelu in (True, False):
+        assert torch.allclose(B.act_mul(gu, gelu).cpu().float(), B.act_mul(gu.cpu(), gelu).float(),
+                              rtol=2e-2, atol=2e-2)
+    table = torch.randn(100, 256, device=cuda).to(torch.bfloat16)
+    ids = torch.tensor([3, 99, 0, 3], device=cuda, dtype=torch.int32)
+    assert torch.allclose(B.embed(ids, table, 16.0).cpu().float(), B.embed(ids.cpu(), table.cpu(), 16.0).float())
+    logits = torch.randn(6, 262144, device=cuda).to(torch.bfloat16)
+    logits[2, 777] = 100.0
+    logits[2, 5] = 100.0  # tie: smallest index wins
+    idx = B.argmax(logits)
+    assert idx.cpu().tolist() == B.argmax(logits.cpu()).tolist()
+    assert idx[2].item() == 5
+
+
+@pytest.mark.parametrize("fmt", [K.FMT_NVFP4, K.FMT_FP8, K.FMT_BF16])
+@pytest.mark.parametrize("d", [256, 512])
+def test_gqa_prep_bitexact(cuda, fmt, d):
+    torch.manual_seed(3)
+    hq, hk, t = 4, 2, 70
+    qkv = (torch.randn(t, (hq + 2 * hk) * d, device=cuda) * 2).to(torch.bfloat16)
+    qn = (torch.randn(d, device=cuda) * 0.1).to(torch.bfloat16)
+    kn = (torch.randn(d, device=cuda) * 0.1).to(torch.bfloat16)
+    cs = B.rope_table(4096, d, 10000.0, cuda)
+    pos = torch.randint(0, 4000, (t,), device=cuda, dtype=torch.int32)
+    slot = torch.randperm(3 * 64, device=cuda)[:t].int()
+    slot[5] = -1
+    pool = torch.zeros(3, hk, 2, K.part_bytes(fmt, d), dtype=torch.uint8, device=cuda)
+    pool_ref = pool.cpu().clone()
+    ks, vs = (0.5, 0.25) if fmt == K.FMT_FP8 else (1.0, 1.0)
+    q = K.gqa_prep(qkv, qn, kn, cs, pos, slot, pool, fmt, hq, hk, d, 1e-6, True, ks, vs)
+    q_ref = K.gqa_prep(qkv.cpu(), qn.cpu(), kn.cpu(), cs.cpu(), pos.cpu(), slot.cpu(), pool_ref, fmt, hq, hk, d,
+                       1e-6, True, ks, vs)
+    assert torch.allclose(q.cpu().float(), q_ref.float(), rtol=1e-2, atol=1e-2)
+    mism = (pool.cpu() != pool_ref).sum().item()
+    # rope in fp32 may differ by one bf16 ulp -> rare single-code differences; require near bit-exactness
+    assert mism <= max(4, pool.numel() // 20000), mism
+
+
+def test_mla_and_index_writers_bitexact(cuda):
+    torch.manual_seed(4)
+    t = 33
+    nope = (torch.randn(t, 512, device=cuda) * 3).to(torch.bfloat16)
+    rope = torch.randn(t, 64, device=cuda).to(torch.bfloat16)
+    slot = torch.randperm(100, device=cuda)[:t].int()
+    for width in (352, 576):
+        pool = torch.zeros(100, width, dtype=torch.uint8, device=cuda)
+        ref = pool.cpu().clone()
+        K.mla_write(nope, rope, slot, pool)
+        K.mla_write(nope.cpu(), rope.cpu(), slot.cpu(), ref)
+        assert torch.equal(pool.cpu(), ref), width
+    k = torch.randn(t, 128, device=cuda).to(torch.bfloat16)
+    pool = torch.zeros(100, 132, dtype=torch.uint8, device=cuda)
+    ref = pool.cpu().clone()
+    K.index_key_write(k, slot, pool)
+    K.index_key_write(k.cpu(), slot.cpu(), ref)
+    assert torch.equal(pool.cpu(), ref)
+
+
+def _build_pool(cuda, fmt, d, hk, lens, scale=(1.0, 1.0), seed=0):
+    torch.manual_seed(seed)
+    b = len(lens)
+    max_pages = max((n + 63) // 64 for n in lens)
+    n_pages = b * max_pages + 3
+    perm = torch.randperm(n_pages)
+    pt = perm[: b * max_pages].reshape(b, max_pages).int()
+    pool = torch.zeros(n_pages, hk, 2, K.part_bytes(fmt, d), dtype=torch.uint8)
+    for i, n in enumerate(lens):
+        k = torch.randn(n, hk, d).to(torch.bfloat16).float()
+        v = torch.randn(n, hk, d).to(torch.bfloat16).float()
+        pos = torch.arange(n)
+        slot = pt[i][pos // 64].long() * 64 + pos % 64
+        K.gqa_pool_write_ref(pool, slot, k, v, fmt, *scale)
+    return pool.to(cuda), pt.to(cuda), torch.tensor(lens, dtype=torch.int32, device=cuda)
+
+
+@pytest.mark.parametrize("fmt", [K.FMT_NVFP4, K.FMT_FP8, K.FMT_BF16])
+@pytest.mark.parametrize("d,window,n_q", [(512, 0, 1), (256, 96, 1), (512, 0, 4), (256, 0, 4), (128, 0, 1)])
+def test_gqa_decode(cuda, fmt, d, window, n_q):
+    hq, hk = 4, 2
+    lens = [300, 1, 129, 700][: 4] if n_q == 1 else [300, 4, 129, 700]
+    scale = (0.5, 0.25) if fmt == K.FMT_FP8 else (1.0, 1.0)
+    pool, pt, kv_len = _build_pool(cuda, fmt, d, hk, lens, scale)
+    q = torch.randn(len(lens) * n_q, hq, d, device=cuda).to(torch.bfloat16)
+    sm = 1.0 / math.sqrt(d)
+    ref = A.gqa_decode_ref(q.cpu(), pool.cpu(), pt.cpu(), kv_len.cpu(), n_q, hk, fmt, sm, window, *scale)
+    for splits in (None, (1, 64)):
+        out = A.gqa_decode(q, pool, pt, kv_len, n_q, hk, fmt, sm, window, *scale, splits=splits)
+        torch.cuda.synchronize()
+        err = (out.cpu().float() - ref).abs().max().item()
+        assert err < 2e-2, (splits, err)
+
+
+def test_gqa_decode_long_context_splits(cuda):
+    hq, hk, d = 4, 2, 512
+    lens = [5000, 3333]
+    pool, pt, kv_len = _build_pool(cuda, K.FMT_NVFP4, d, hk, lens, seed=7)
+    q = torch.randn(2, hq, d, device=cuda).to(torch.bfloat16)
+    sm = 1.0 / math.sqrt(d)
+    ref = A.gqa_decode_ref(q.cpu(), pool.cpu(), pt.cpu(), kv_len.cpu(), 1, hk, K.FMT_NVFP4, sm)
+    out = A.gqa_decode(q, pool, pt, kv_len, 1, hk, K.FMT_NVFP4, sm)
+    torch.cuda.synchronize()
+    assert (out.cpu().float() - ref).abs().max().item() < 2e-2
+    # deterministic
+    out2 = A.gqa_decode(q, pool, pt, kv_len, 1, hk, K.FMT_NVFP4, sm)
+    assert torch.equal(out, out2)

@@ -1,0 +1,74 @@
+"""CPU oracle consistency: pool write/read round trip, paged decode oracle vs dense attention, op references."""
+import math
+
+import torch
+
+from inference_optimizations_b200.ops import attention as A
+from inference_optimizations_b200.ops import basic as B
+from inference_optimizations_b200.ops import kvcache as K
+
+
+def test_swizzle_perm_is_permutation():
+    for rb in (64, 128, 256, 512, 1024):
+        p = K.kv_swizzle_perm(rb)
+        for r in range(64):
+            assert sorted(p[r].tolist()) == list(range(rb))
+
+
+def test_pool_roundtrip_all_formats():
+    torch.manual_seed(0)
+    hk, d, n = 2, 256, 150
+    for fmt in (K.FMT_BF16, K.FMT_FP8, K.FMT_NVFP4):
+        pool = torch.zeros(4, hk, 2, K.part_bytes(fmt, d), dtype=torch.uint8)
+        pages = torch.tensor([2, 0, 3])
+        k = torch.randn(n, hk, d).to(torch.bfloat16).float()
+        v = torch.randn(n, hk, d).to(torch.bfloat16).float()
+        pos = torch.arange(n)
+        K.gqa_pool_write_ref(pool, pages[pos // 64] * 64 + pos % 64, k, v, fmt, 0.5, 0.5)
+        k2, v2 = K.gqa_pool_read_ref(pool, pages, n, fmt, d, 0.5, 0.5)
+        tol = {K.FMT_BF16: 0.0, K.FMT_FP8: 0.3, K.FMT_NVFP4: 0.7}[fmt]
+        assert (k2 - k).abs().max() <= tol + 1e-6 and (v2 - v).abs().max() <= tol + 1e-6
+
+
+def test_decode_ref_matches_dense():
+    torch.manual_seed(1)
+    hq, hk, d, n_q = 4, 2, 128, 3
+    lens = [70, 5]
+    fmt = K.FMT_BF16
+    pool = torch.zeros(6, hk, 2, K.part_bytes(fmt, d), dtype=torch.uint8)
+    pt = torch.tensor([[1, 4], [0, 5]], dtype=torch.int32)
+    ks, vs = [], []
+    for i, n in enumerate(lens):
+        k = torch.randn(n, hk, d).to(torch.bfloat16).float()
+        v = torch.randn(n, hk, d).to(torch.bfloat16).float()
+        pos = torch.arange(n)
+        K.gqa_pool_write_ref(pool, pt[i][pos // 64].long() * 64 + pos % 64, k, v, fmt)
+        ks.append(k)
+        vs.append(v)
+    q = torch.randn(len(lens) * n_q, hq, d).to(torch.bfloat16)
+    sm = 1 / math.sqrt(d)
+    for window in (0, 4):
+        out = A.gqa_decode_ref(q, pool, pt, torch.tensor(lens), n_q, hk, fmt, sm, window)
+        for i, n in enumerate(lens):
+            qp = torch.arange(n - n_q, n)
+            ref = A.dense_attention_ref(q[i * n_q:(i + 1) * n_q], ks[i], vs[i], sm, qp, torch.arange(n), window)
+            assert torch.allclose(out[i * n_q:(i + 1) * n_q], ref, atol=1e-5)
+
+
+def test_split_policy():
+    ns, tps = A.split_policy(32 * 16, 33000)
+    assert ns * tps * 128 >= 33000 and ns >= 1
+    ns, tps = A.split_policy(4, 200000)
+    assert ns > 1 and tps >= 4
+    ns, tps = A.split_policy(512, 1030, window=1024)
+    assert ns * tps * 128 >= 1024 + 128
+
+
+def test_rmsnorm_and_argmax_ref():
+    x = torch.randn(3, 64).to(torch.bfloat16)
+    w = torch.zeros(64).to(torch.bfloat16)
+    y = B.rmsnorm(x, w, 1e-6, plus_one=True)
+    ref = x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)
+    assert torch.allclose(y.float(), ref, atol=2e-2)
+    lg = torch.tensor([[1.0, 3.0, 3.0, 0.0]])
+    assert B.argmax(lg).tolist() == [1]
