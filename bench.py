@@ -1,0 +1,154 @@
+"""Flagship serving benchmark: decode throughput of the Gemma-class 31B dense GQA model.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W]            (N > 1: launched by torch.distributed.run)
+    python bench.py --impl reference ...                            (the reference arm)
+
+Workload: 32 sessions, each holding a 32768-token random prompt in the paged KV pool, generating greedily (up to 512
+output tokens).  One timed step = one engine iteration over all sessions (one decode step, or one speculative step
+with --spec).  Tensor parallel over the N GPUs (strong scaling: the total work is fixed).  Prints one JSON line on rank
+0: `value` = output tokens / device time of the step computation (max over ranks); `e2e` = the same through
+`Engine.step()` including each step's pinned host->device input copy and device->host result read, timed on the device
+from the first input copy to the last result (max over ranks).  Weights and KV (~170 GB read per step at N=1) are far
+larger than L2, so no flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+METRIC = "output tok/s per 8×B200 box at 1/2/4/8 GPUs; per-user decode tok/s, 64×200k ctx"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=40)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--model", default="gemma31b")
+    p.add_argument("--sessions", type=int, default=32)
+    p.add_argument("--ctx", type=int, default=32768)
+    p.add_argument("--max-new", type=int, default=512)
+    p.add_argument("--kv", default="nvfp4", choices=["nvfp4", "fp8", "bf16"])
+    p.add_argument("--spec", type=int, default=0, help="1 = speculative decoding (1-layer draft, 3 tokens)")
+    p.add_argument("--no-graphs", action="store_true")
+    return p.parse_args()
+
+
+def reference_arm(args) -> None:
+    # The reference is a collection of SGLang v0.5.20 patches and kernels; it has no installable package and SGLang
+    # is not present on this image, so its serving stack cannot run here (install attempt recorded in DESIGN.md).
+    print(json.dumps({"impl": "reference", "unavailable": "reference is an SGLang patch set with no setup.py/"
+                      "pyproject (pip: 'not installable') and SGLang is not installed offline"}))
+
+
+def main() -> int:
+    args = parse()
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            reference_arm(args)
+        return 0
+    import torch
+    from inference_optimizations_b200.config import EngineConfig, model_config
+    from inference_optimizations_b200.engine.engine import Engine
+    from inference_optimizations_b200.engine.synthetic import synth_decode_sessions
+    from inference_optimizations_b200.parallel import dist as D
+    from inference_optimizations_b200.utils.clocks import ClockSampler, rejected
+
+    info = D.init("nccl")
+    tp, rank = info.world, info.rank
+    dev = torch.device("cuda", info.local_rank)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    cfg = model_config(args.model)
+    steps, warm = args.steps, max(3, args.warmup)
+    max_new = max(args.max_new, steps + warm + 8)
+    ecfg = EngineConfig(model=args.model, device=str(dev), kv_dtype=args.kv, max_running=args.sessions,
+                        chunked_prefill=2048, spec=bool(args.spec), cuda_graphs=not args.no_graphs,
+                        graph_batch_sizes=str(args.sessions), tp=tp)
+    max_seq = args.ctx + max_new + 64
+    eng = Engine(ecfg, cfg, max_seq=max_seq, tp_rank=rank, tp=tp,
+                 all_reduce=D.nccl_all_reduce if tp > 1 else None,
+                 argmax_merge=D.argmax_merge if tp > 1 else None)
+    synth_decode_sessions(eng, args.sessions, args.ctx, max_new, seed=1)
+    torch.cuda.synchronize()
+    for _ in range(warm):
+        eng.step()
+    launches = eng.runner.count_step_launches(eng.runner._bucket(args.sessions))
+    torch.cuda.synchronize()
+    if tp > 1:
+        torch.distributed.barrier()
+    clocks = ClockSampler(info.local_rank).start()
+    time.sleep(0.3)
+    eng.runner.event_log = []
+    table0 = sum(t.bytes_synced for t in eng.runner.kv.tables.values())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record()
+    toks = 0
+    for _ in range(steps):
+        out = eng.step()
+        toks += sum(len(v) for v in out.values())
+    ev1.record()
+    torch.cuda.synchronize()
+    if tp > 1:
+        torch.distributed.barrier()
+    ck = clocks.stop()
+    dev_ms = sum(a.elapsed_time(b) for a, b in eng.runner.event_log)
+    e2e_ms = ev0.elapsed_time(ev1)
+    dev_ms = D.max_over_ranks(dev_ms)
+    e2e_ms = D.max_over_ranks(e2e_ms)
+    stage = eng.runner.stage
+    h2d = stage.h2d_bytes() + (sum(t.bytes_synced for t in eng.runner.kv.tables.values()) - table0) // steps
+    d2h = 4 * args.sessions * (1 + (ecfg.draft_tokens if ecfg.spec else 0))
+    value = toks / (dev_ms / 1e3)
+    accept = None
+    if ecfg.spec:
+        acc = [r.accepted / max(1, r.spec_steps) for r in eng.sched.running]
+        accept = sum(acc) / max(1, len(acc))
+    res = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": tp,
+        "steps": steps,
+        "warmup": warm,
+        "ms_per_step": round(dev_ms / steps, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": ("synthetic: random token ids and random-init weights of the named architecture; each session's "
+                 f"{args.ctx}-token prompt is in the paged KV pool as random well-formed {args.kv} rows "
+                 "(the prefill compute is not part of the timed decode steps)"),
+        "config": {"model": "Dense GQA hd512 (Gemma-class 31B): 60 layers, hidden 5376, 32 q / 16 kv heads, "
+                            "head_dim 256 on SWA-1024 layers and 512 on every 6th (global) layer, GeGLU 21504, "
+                            "vocab 262144",
+                   "global_batch": args.sessions, "seq_len": args.ctx, "parallelism": f"tp{tp}",
+                   "kv_cache": args.kv, "speculative": bool(ecfg.spec), "draft_tokens": ecfg.draft_tokens if ecfg.spec else 0,
+                   "accept_per_step": accept,
+                   "l2": "no flush: every step reads weights + KV (~170 GB at N=1), far larger than the 126 MB L2"},
+        "per_user_tok_s": round(value / args.sessions, 3),
+        "clocks": {"sm_mhz": ck.get("sm_mhz"), "sm_max_mhz": ck.get("sm_max_mhz"), "reasons": ck.get("reasons"),
+                   "samples": ck.get("samples")},
+        "e2e": {"value": round(toks / (e2e_ms / 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "api": "Engine.step()"},
+        "gpu_launches": launches * steps,
+        "impl": "ours",
+    }
+    bad = rejected(ck)
+    if bad:
+        res["clocks"]["rejected"] = bad
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if tp > 1:
+        eng.runner.graphs.clear()
+        D.shutdown()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

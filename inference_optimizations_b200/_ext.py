@@ -10,6 +10,49 @@ import torch
 
 _mod = None
 _err: Exception | None = None
+_counter: list | None = None     # when set, [launches] is incremented per kernel launched through ext()
+
+
+def _kernels_of(name: str, args: tuple) -> int:
+    if name == "gqa_decode":
+        return 2 if args[15] > 1 else 1          # main kernel (+ split combine)
+    if name == "mla_decode":
+        return 2 if args[-1] > 1 else 1
+    return 1
+
+
+class _Counting:
+    def __init__(self, mod):
+        self._m = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._m, name)
+
+        def call(*args, **kw):
+            if _counter is not None:
+                _counter[0] += _kernels_of(name, args)
+            return fn(*args, **kw)
+        return call
+
+
+class count_launches:
+    """Context manager counting this package's kernel launches (eager execution; a CUDA graph captured from the
+    same code replays exactly the counted sequence)."""
+
+    def __enter__(self):
+        global _counter
+        _counter = [0]
+        self.box = _counter
+        return self
+
+    @property
+    def n(self) -> int:
+        return self.box[0]
+
+    def __exit__(self, *exc):
+        global _counter
+        _counter = None
+        return False
 
 
 def ext():
@@ -23,7 +66,7 @@ def ext():
         raise RuntimeError(
             "inference_optimizations_b200._C is not built or failed to load "
             "(run `python setup.py build_ext --inplace`): " + repr(_err))
-    return _mod
+    return _Counting(_mod) if _counter is not None else _mod
 
 
 def available() -> bool:

@@ -141,7 +141,7 @@ PRESETS: dict[str, Any] = {
                                  weight_dtype="fp8", expert_dtype="nvfp4", vocab=154880),
     # small shapes for tests (same code paths, tiny dims)
     "tiny_gqa": lambda: GQAConfig(name="tiny_gqa", num_layers=6, hidden=256, num_q_heads=4, num_kv_heads=2,
-                                  num_kv_heads_global=2, head_dim=64, head_dim_global=128, global_every=3,
+                                  num_kv_heads_global=2, head_dim=128, head_dim_global=256, global_every=3,
                                   sliding_window=48, ffn=512, vocab=512),
     "tiny_mla": lambda: MLAMoEConfig(name="tiny_mla", num_layers=3, hidden=256, num_heads=4, q_lora=128, kv_lora=512,
                                      qk_nope=32, qk_rope=64, v_head=32, index_heads=4, index_dim=128, index_topk=64,

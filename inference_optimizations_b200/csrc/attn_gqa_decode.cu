@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
   }
   const int first_page = kv_begin / a.page;
   const int n_pages = (kv_len + a.page - 1) / a.page;
-  const int* pt = a.page_table + static_cast<size_t>(b) * a.pt_stride;
+  const int* pt = a.page_table + static_cast<size_t>(a.req_idx ? a.req_idx[b] : b) * a.pt_stride;
   const int warp = warp_id(), lane = lane_id();
 
   // ---- Q -> f16 slabs (rows >= R zero), barriers, TMEM

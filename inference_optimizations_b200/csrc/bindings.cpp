@@ -132,8 +132,8 @@ void index_key_write(const at::Tensor& k, const at::Tensor& slot, at::Tensor poo
                                      k.size(0), stream()));
 }
 
-void gqa_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& page_table, const at::Tensor& kv_len,
-                at::Tensor out, at::Tensor o_part, at::Tensor lse_part, at::Tensor status, int64_t n_q, int64_t Hk,
+void gqa_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& page_table,
+                c10::optional<at::Tensor> req_idx, const at::Tensor& kv_len, at::Tensor out, at::Tensor o_part, at::Tensor lse_part, at::Tensor status, int64_t n_q, int64_t Hk,
                 int64_t page, int64_t window, int64_t fmt, int64_t tiles_per_split, int64_t num_splits,
                 double sm_scale, double k_scale, double v_scale) {
   req(q, at::kBFloat16, "q");
@@ -150,6 +150,7 @@ void gqa_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& p
   a.q = q.data_ptr();
   a.pool = pool.data_ptr<uint8_t>();
   a.page_table = page_table.data_ptr<int>();
+  if (req_idx.has_value()) { req(*req_idx, at::kInt, "req_idx"); a.req_idx = req_idx->data_ptr<int>(); }
   a.kv_len = kv_len.data_ptr<int>();
   a.out = out.data_ptr();
   a.o_part = o_part.data_ptr<float>();

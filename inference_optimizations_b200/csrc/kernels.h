@@ -73,7 +73,8 @@ inline int kv_swizzle_byte(int byte_in_row, int row, int row_bytes) {
 struct GqaDecodeArgs {
   const void* q;           // bf16 [B * n_q, Hq, D] (normed + roped)
   const uint8_t* pool;     // layer pool [num_pages, Hk, 2 parts (K, V), part_bytes]
-  const int* page_table;   // [B, pt_stride] physical page per logical page
+  const int* page_table;   // [rows, pt_stride] physical page per logical page
+  const int* req_idx;      // [B] page-table row of batch entry b (null: row b)
   const int* kv_len;       // [B] tokens in the pool (query tokens included, they are the last n_q)
   void* out;               // bf16 [B * n_q, Hq, D]
   float* o_part;           // [B * Hk * num_splits, RMAX, D]  (num_splits > 1)

@@ -1,0 +1,74 @@
+"""Public serving API: `Engine(EngineConfig).generate(prompts)` or `add_request` + `step()` in a loop.
+
+One Engine per process / GPU.  With tensor parallelism every rank runs the same Engine; rank 0's scheduler decides and
+the decision (the packed step inputs) is identical on every rank because every rank receives the same requests in the
+same order (the HTTP front end broadcasts them, `server/http.py`), so the per-step host traffic needs no collective.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+
+from ..config import EngineConfig, GQAConfig, MLAMoEConfig, model_config
+from .runner import GQARunner
+from .scheduler import Request, SamplingParams, Scheduler
+
+
+@dataclass
+class StepStats:
+    kind: str
+    tokens_out: int
+    seconds: float
+
+
+class Engine:
+    def __init__(self, ecfg: EngineConfig, model_cfg=None, max_seq: int = 4096, tp_rank: int = 0, tp: int = 1,
+                 all_reduce=None, argmax_merge=None, global_pages: Optional[int] = None):
+        self.ecfg = ecfg
+        self.cfg = model_cfg if model_cfg is not None else model_config(ecfg.model)
+        self.device = torch.device(ecfg.device)
+        if isinstance(self.cfg, GQAConfig):
+            self.runner = GQARunner(self.cfg, ecfg, self.device, max_seq, tp_rank, tp, all_reduce, argmax_merge,
+                                    global_pages)
+        else:
+            from .mla_runner import MLARunner
+            self.runner = MLARunner(self.cfg, ecfg, self.device, max_seq, tp_rank, tp)
+        self.sched = Scheduler(ecfg.max_running, ecfg.chunked_prefill, ecfg.decode_burst,
+                               can_admit=self.runner.can_admit)
+        self.stats: list[StepStats] = []
+        self.finished: list[Request] = []
+
+    def add_request(self, prompt: list, params: Optional[SamplingParams] = None) -> Request:
+        return self.sched.new_request(prompt, params or SamplingParams())
+
+    def step(self) -> dict:
+        """One engine iteration.  Returns rid -> tokens produced this step."""
+        t0 = time.perf_counter()
+        batch = self.sched.schedule()
+        if batch is None:
+            return {}
+        if batch.kind == "prefill":
+            nxt = self.runner.prefill(batch)
+            self.sched.commit_prefill(batch, nxt)
+            out = {rid: [t] for rid, t in nxt.items()}
+        else:
+            reqs = [s.req for s in batch.segments]
+            out = self.runner.spec_decode(reqs) if self.runner.spec else self.runner.decode(reqs)
+            self.sched.commit_decode(out)
+        for r in [s.req for s in batch.segments]:
+            if r.finished and r not in self.finished:
+                self.finished.append(r)
+                self.runner.detach(r)
+        self.stats.append(StepStats(batch.kind, sum(len(v) for v in out.values()), time.perf_counter() - t0))
+        return out
+
+    def generate(self, prompts: list, params: Optional[SamplingParams] = None, max_steps: int = 1 << 30) -> list:
+        reqs = [self.add_request(p, params) for p in prompts]
+        steps = 0
+        while self.sched.has_work() and steps < max_steps:
+            self.step()
+            steps += 1
+        return [r.output for r in reqs]

@@ -1,0 +1,348 @@
+"""Model runner for the GQA family: turns scheduled segments into device step tensors, runs prefill (eager) and
+decode / speculative steps (CUDA graphs per batch bucket), and samples greedily.
+
+Step inputs travel as ONE pinned int32 staging buffer copied host->device per step (ids, positions, pool slots per
+layer kind, per-group kv lengths and page-table rows); the page tables are synced the same way.  Results come back as
+one device->host copy of the sampled ids.  This is the engine's whole per-step host traffic, which is what bench.py's
+end-to-end number accounts for.
+
+Attention runs every mode (prefill chunks, decode, verify, draft extend) through the same split-K kernel: a segment
+of L tokens is cut into groups of n_q consecutive tokens (n_q * G <= 16 query rows per kv head); a group's last
+rows may be padding (slot -1, output discarded), which is safe because a query only sees keys at or before its own
+position.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+
+from ..config import EngineConfig, GQAConfig
+from ..kv.allocator import DUMMY_PAGE, OutOfPages, RequestPages
+from ..models.gqa import GQAKVCache, GQAModel, StepTensors
+from ..ops import attention as A
+from ..ops import basic as B
+from .scheduler import Batch, Request, Segment
+
+KINDS = ("global", "swa", "draft")
+
+
+@dataclass
+class Packed:
+    ids: list
+    pos: list
+    slot: dict
+    kv_len: list
+    req_idx: list
+    n_q: int
+    logit_rows: list            # row index per segment that wants logits
+    seg_rows: list              # (segment, first row) for each segment
+
+
+class StagingBuffers:
+    """One device int32 buffer holding every per-step input, plus its pinned host twin."""
+
+    def __init__(self, max_tokens: int, max_groups: int, kinds: tuple, device):
+        self.kinds = kinds
+        self.T, self.G = max_tokens, max_groups
+        n = max_tokens * (2 + len(kinds)) + 2 * max_groups
+        pin = torch.device(device).type == "cuda"
+        self.host = torch.zeros(n, dtype=torch.int32, pin_memory=pin)
+        self.dev = torch.zeros(n, dtype=torch.int32, device=device)
+
+    def views(self, buf: torch.Tensor, t: int, g: int):
+        T, G = self.T, self.G
+        ids, pos = buf[:t], buf[T:T + t]
+        slots = {k: buf[(2 + i) * T:(2 + i) * T + t] for i, k in enumerate(self.kinds)}
+        base = (2 + len(self.kinds)) * T
+        return ids, pos, slots, buf[base:base + g], buf[base + G:base + G + g]
+
+    def fill(self, p: Packed) -> None:
+        t, g = len(p.ids), len(p.kv_len)
+        ids, pos, slots, kvl, rix = self.views(self.host, t, g)
+        ids.copy_(torch.tensor(p.ids, dtype=torch.int32))
+        pos.copy_(torch.tensor(p.pos, dtype=torch.int32))
+        for k in self.kinds:
+            slots[k].copy_(torch.tensor(p.slot.get(k, [-1] * t), dtype=torch.int32))
+        kvl.copy_(torch.tensor(p.kv_len, dtype=torch.int32))
+        rix.copy_(torch.tensor(p.req_idx, dtype=torch.int32))
+
+    def upload(self) -> None:
+        self.dev.copy_(self.host, non_blocking=True)
+
+    def step_tensors(self, t: int, g: int, n_q: int, splits: dict) -> StepTensors:
+        ids, pos, slots, kvl, rix = self.views(self.dev, t, g)
+        return StepTensors(ids, pos, slots, kvl, rix, n_q, splits)
+
+    def h2d_bytes(self) -> int:
+        return self.host.numel() * 4
+
+
+class GQARunner:
+    def __init__(self, cfg: GQAConfig, ecfg: EngineConfig, device, max_seq: int, tp_rank: int = 0, tp: int = 1,
+                 all_reduce: Optional[Callable] = None, argmax_merge: Optional[Callable] = None,
+                 global_pages: Optional[int] = None):
+        self.cfg, self.ecfg, self.device = cfg, ecfg, torch.device(device)
+        self.tp, self.tp_rank = tp, tp_rank
+        self.max_seq = max_seq
+        self.argmax_merge = argmax_merge
+        self.model = GQAModel(cfg, device, tp_rank, tp, ecfg.seed, all_reduce)
+        self.spec = ecfg.spec
+        self.n_draft = ecfg.draft_tokens if ecfg.spec else 0
+        self.draft = GQAModel(cfg, device, tp_rank, tp, ecfg.seed, all_reduce, draft=True) if self.spec else None
+        G = cfg.num_q_heads // cfg.num_kv_heads
+        self.n_q_prefill = max(1, 16 // G)
+        self.max_running = ecfg.max_running
+        w = cfg.sliding_window
+        per_req_swa = (w + self.ecfg.chunked_prefill) // 64 + 3
+        if global_pages is None:
+            global_pages = self.max_running * ((max_seq + 64 + 63) // 64) + 2
+        swa_pages = self.max_running * (w // 64 + 4) + per_req_swa + 2
+        self.kv = GQAKVCache(cfg, tp, device, ecfg.kv_dtype, self.max_running + 1, max_seq + 64, global_pages,
+                             swa_pages, draft_pages=swa_pages if self.spec else 0)
+        self.dummy_row = self.max_running
+        self.pages: dict[int, dict[str, RequestPages]] = {}
+        max_tok = max(ecfg.chunked_prefill + 16 * self.n_q_prefill, self.max_running * (self.n_draft + 1))
+        self.max_tok = max_tok
+        self.max_groups = max_tok
+        self.stage = StagingBuffers(max_tok, self.max_groups, KINDS, device)
+        self.kv.reserve_workspace(self.max_running, self._max_splits())
+        self.graphs: dict = {}
+        self.graph_pool = None
+        self.out_ids = torch.zeros(max_tok, dtype=torch.int32, device=device)
+        pin = self.device.type == "cuda"
+        self.out_host = torch.zeros(max_tok, dtype=torch.int32, pin_memory=pin)
+        self.hidden_buf = None            # target pre-norm hidden of the last verify/decode (draft input)
+
+    # ------------------------------------------------------------------------------------------ memory
+    def _max_splits(self) -> int:
+        best = 1
+        for kind, hk in (("global", self.cfg.num_kv_heads_global // self.tp), ("swa", self.cfg.num_kv_heads // self.tp)):
+            for b in range(1, self.max_running + 1):
+                best = max(best, A.split_policy(b * hk, self.max_seq, self.cfg.sliding_window if kind == "swa" else 0)[0])
+        return best
+
+    def can_admit(self, r: Request) -> bool:
+        need = (r.prompt_len + r.params.max_new_tokens + self.n_draft + 64) // 64 + 1
+        return self.kv.alloc["global"].free >= need + self._reserved_growth()
+
+    def _reserved_growth(self) -> int:
+        tot = 0
+        for rid, pg in self.pages.items():
+            tot += max(0, pg["_max_pages"] - len(pg["global"].pages))
+        return tot
+
+    def attach(self, r: Request) -> None:
+        w = self.cfg.sliding_window
+        pg = {"global": RequestPages(self.kv.alloc["global"], self.kv.tables["global"], r.slot),
+              "swa": RequestPages(self.kv.alloc["swa"], self.kv.tables["swa"], r.slot, window=w)}
+        if self.spec:
+            pg["draft"] = RequestPages(self.kv.alloc["draft"], self.kv.tables["draft"], r.slot, window=w)
+        pg["_max_pages"] = (r.prompt_len + r.params.max_new_tokens + self.n_draft + 64) // 64 + 1
+        self.pages[r.rid] = pg
+
+    def detach(self, r: Request) -> None:
+        pg = self.pages.pop(r.rid, None)
+        if pg:
+            for k in KINDS:
+                if k in pg:
+                    pg[k].free()
+
+    # ------------------------------------------------------------------------------------------ packing
+    def _pack(self, segs: list, n_q: int, kinds: tuple, pad_groups_to: int = 0, draft_offset: int = 0) -> Packed:
+        ids, pos, kvl, rix, logit_rows, seg_rows = [], [], [], [], [], []
+        slot = {k: [] for k in kinds}
+        for s in segs:
+            L = len(s.tokens)
+            ngroups = (L + n_q - 1) // n_q
+            pg = self.pages[s.req.rid]
+            for k in kinds:
+                pg[k].ensure(s.start + L + draft_offset)
+            seg_rows.append((s, len(ids)))
+            for gi in range(ngroups):
+                for t in range(n_q):
+                    j = gi * n_q + t
+                    p = s.start + j
+                    if j < L:
+                        ids.append(int(s.tokens[j]))
+                        pos.append(p)
+                        for k in kinds:
+                            slot[k].append(pg[k].slot_of(p))
+                    else:
+                        ids.append(0)
+                        pos.append(p)
+                        for k in kinds:
+                            slot[k].append(-1)
+                kvl.append(s.start + (gi + 1) * n_q)
+                rix.append(s.req.slot)
+            if s.logits:
+                logit_rows.append(seg_rows[-1][1] + L - 1)
+        while len(kvl) < pad_groups_to:
+            for t in range(n_q):
+                ids.append(0)
+                pos.append(t)
+                for k in kinds:
+                    slot[k].append(-1)
+            kvl.append(n_q)
+            rix.append(self.dummy_row)
+        return Packed(ids, pos, slot, kvl, rix, n_q, logit_rows, seg_rows)
+
+    # ------------------------------------------------------------------------------------------ forward pieces
+    def _target(self, st: StepTensors):
+        return self.model.forward(st, self.kv)
+
+    def _greedy(self, x_sel: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        logits = self.model.logits_local(x_sel, self.model.embed)
+        if self.tp == 1:
+            return B.argmax(logits, out=out[: x_sel.shape[0]])
+        val = torch.empty(x_sel.shape[0], dtype=torch.float32, device=self.device)
+        loc = B.argmax(logits, val=val)
+        return self.argmax_merge(loc, val, self.model.vocab_local, out[: x_sel.shape[0]])
+
+    # ------------------------------------------------------------------------------------------ prefill
+    def prefill(self, batch: Batch) -> dict:
+        for s in batch.segments:
+            if s.req.rid not in self.pages:
+                self.attach(s.req)
+        kinds = ("global", "swa")
+        p = self._pack(batch.segments, self.n_q_prefill, kinds)
+        self.kv.sync_tables()
+        self.stage.fill(p)
+        self.stage.upload()
+        st = self.stage.step_tensors(len(p.ids), len(p.kv_len), p.n_q, {"global": (1, 1 << 20), "swa": (1, 1 << 20)})
+        x, resid = self._target(st)
+        rows = torch.tensor(p.logit_rows, dtype=torch.long, device=self.device)
+        res = {}
+        if len(p.logit_rows):
+            self._greedy(x[rows], self.out_ids)
+            self.out_host[: len(p.logit_rows)].copy_(self.out_ids[: len(p.logit_rows)], non_blocking=True)
+        if self.spec:
+            self._draft_prefill(batch, p, resid)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream().synchronize()
+        k = 0
+        for s in batch.segments:
+            if s.logits:
+                res[s.req.rid] = int(self.out_host[k])
+                k += 1
+        self._trim(batch.segments)
+        return res
+
+    def _trim(self, segs) -> None:
+        for s in segs:
+            pg = self.pages.get(s.req.rid)
+            if pg is None:
+                continue
+            nxt = s.start + len(s.tokens)
+            pg["swa"].trim(nxt)
+            if "draft" in pg:
+                pg["draft"].trim(nxt)
+
+    # ------------------------------------------------------------------------------------------ decode
+    def _bucket(self, n: int) -> int:
+        for b in self.ecfg.graph_sizes():
+            if b >= n:
+                return b
+        return n
+
+    def decode(self, reqs: list) -> dict:
+        """One greedy decode step (n_q = 1) for every running request."""
+        segs = [Segment(r, r.kv_len, [r.pending], True) for r in reqs]
+        bucket = self._bucket(len(segs))
+        p = self._pack(segs, 1, ("global", "swa"), pad_groups_to=bucket)
+        self.kv.sync_tables()
+        self.stage.fill(p)
+        self.stage.upload()
+        fn = self._decode_fn(bucket)
+        self._timed(fn)
+        n = len(segs)
+        self.out_host[:n].copy_(self.out_ids[:n], non_blocking=True)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream().synchronize()
+        res = {r.rid: [int(self.out_host[i])] for i, r in enumerate(reqs)}
+        self._trim([Segment(r, r.kv_len, [0], False) for r in reqs])
+        return res
+
+    def _timed(self, fn: Callable) -> None:
+        """Run a step body; when `self.event_log` is a list, bracket it with CUDA events (device time of the step
+        computation without host staging) and append the pair."""
+        if getattr(self, "event_log", None) is not None and self.device.type == "cuda":
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            self.event_log.append((e0, e1))
+        else:
+            fn()
+
+    def count_step_launches(self, bucket: int) -> int:
+        """Kernel launches of one decode step body (run eagerly under the counter)."""
+        from .._ext import count_launches
+        body = self._spec_body(bucket) if self.spec else self._decode_body(bucket)
+        with count_launches() as c:
+            body()
+        return c.n
+
+    def _splits(self, groups: int) -> dict:
+        cfg = self.cfg
+        return {"global": A.split_policy(groups * cfg.num_kv_heads_global // self.tp, self.max_seq),
+                "swa": A.split_policy(groups * cfg.num_kv_heads // self.tp, self.max_seq, cfg.sliding_window),
+                "draft": A.split_policy(groups * cfg.num_kv_heads // self.tp, self.max_seq, cfg.sliding_window)}
+
+    def _decode_body(self, bucket: int) -> Callable:
+        st = self.stage.step_tensors(bucket, bucket, 1, self._splits(bucket))
+
+        def body():
+            x, resid = self._target(st)
+            self._greedy(x, self.out_ids)
+        return body
+
+    def _decode_fn(self, bucket: int) -> Callable:
+        key = ("decode", bucket)
+        if key in self.graphs:
+            return self.graphs[key]
+        body = self._decode_body(bucket)
+        if not (self.ecfg.cuda_graphs and self.device.type == "cuda"):
+            self.graphs[key] = body
+            return body
+        fn = self._capture(body)
+        self.graphs[key] = fn
+        return fn
+
+    def _capture(self, body: Callable) -> Callable:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            body()                       # warm-up outside capture (lazy library init)
+        torch.cuda.current_stream().wait_stream(s)
+        if self.graph_pool is None:
+            self.graph_pool = torch.cuda.graph_pool_handle()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self.graph_pool):
+            body()
+        return g.replay
+
+    # ------------------------------------------------------------------------------------------ speculative
+    def _draft_prefill(self, batch: Batch, p: Packed, resid: torch.Tensor) -> None:
+        """Fill the draft layer's KV over each prefill segment: draft input at position q is (token q, target hidden
+        at q - 1); the first position of a segment reuses its own hidden (no earlier hidden in this batch)."""
+        shift = torch.arange(len(p.ids), device=self.device) - 1
+        shift.clamp_(min=0)
+        for s, r0 in p.seg_rows:
+            shift[r0] = r0
+        hprev = resid[shift]
+        self._draft_forward(p, hprev)
+
+    def _draft_forward(self, p: Packed, hprev: torch.Tensor, st: Optional[StepTensors] = None) -> tuple:
+        if st is None:
+            st = self.stage.step_tensors(len(p.ids), len(p.kv_len), p.n_q, {"draft": (1, 1 << 20)})
+        d = self.draft
+        emb = B.embed(st.ids, self.model.embed, self.model.embed_scale)
+        x0 = torch.nn.functional.linear(torch.cat([emb, hprev], dim=-1), d.fc)
+        layer_off = self.cfg.num_layers
+        st_d = StepTensors(st.ids, st.pos, {"draft": st.slot["draft"], "swa": st.slot["draft"]}, st.kv_len,
+                           st.req_idx, st.n_q, {"draft": st.splits.get("draft")})
+        x, resid = d.forward(st_d, self.kv, layer_offset=layer_off, inputs_embeds=x0)
+        return x, resid

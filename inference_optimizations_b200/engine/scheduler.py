@@ -1,0 +1,162 @@
+"""Continuous-batching scheduler: waiting queue, chunked prefill, running decode set, decode-burst admission.
+
+Policy (one decision per engine step, the SGLang event-loop shape the reference patches, `tooling/diagnostics/
+numinous_step_trace.py:1-12`):
+  * if a request is part-way through a chunked prefill, its next chunk runs (a chunk is never held, reference
+    `scheduler/decode-burst/0002-*.patch`);
+  * else, if requests are waiting and memory allows, a prefill batch is formed from the head of the queue up to
+    `chunked_prefill` tokens - unless the decode-burst rule holds prefill admission
+    (`scheduler/decode-burst/decode_burst.py:7-37`, re-implemented in `burst.py`);
+  * else all running requests decode one step (or one speculative step).
+Admission reserves KV pages for the whole prompt plus the generation budget, so a running request never stalls on
+memory (no retraction path is needed; the reference's retraction-abort fix covers a case that cannot arise here).
+"""
+from __future__ import annotations
+
+import itertools
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Optional
+
+from .burst import hold_prefill, next_streak
+
+
+@dataclass
+class SamplingParams:
+    max_new_tokens: int = 128
+    temperature: float = 0.0       # greedy only in this version
+    stop_token_ids: tuple = ()
+    ignore_eos: bool = True
+
+
+@dataclass
+class Request:
+    rid: int
+    prompt: list
+    params: SamplingParams
+    output: list = field(default_factory=list)
+    slot: int = -1                 # row in the page tables
+    prefilled: int = 0             # prompt tokens already in the KV pool
+    kv_len: int = 0                # tokens in the KV pool
+    pending: Optional[int] = None  # sampled token not yet in the pool (the next decode input)
+    finished: bool = False
+    draft_state: dict = field(default_factory=dict)
+    accepted: int = 0              # speculative: drafts accepted in total
+    spec_steps: int = 0
+
+    @property
+    def prompt_len(self) -> int:
+        return len(self.prompt)
+
+    def total_len(self) -> int:
+        return self.prompt_len + len(self.output)
+
+
+@dataclass
+class Segment:
+    req: Request
+    start: int
+    tokens: list
+    logits: bool
+
+
+@dataclass
+class Batch:
+    kind: str                      # "prefill" | "decode"
+    segments: list
+
+
+class Scheduler:
+    def __init__(self, max_running: int, chunked_prefill: int, decode_burst: int = 1, can_admit=None):
+        self.max_running = max_running
+        self.chunk = chunked_prefill
+        self.burst = decode_burst
+        self.waiting: deque[Request] = deque()
+        self.running: list[Request] = []
+        self.prefilling: Optional[Request] = None
+        self.streak = 0
+        self.last_was_extend: Optional[bool] = None
+        self._ids = itertools.count()
+        self.can_admit = can_admit or (lambda req: True)
+        self.free_slots = list(range(max_running - 1, -1, -1))
+
+    def new_request(self, prompt: list, params: SamplingParams) -> Request:
+        r = Request(next(self._ids), list(prompt), params)
+        self.waiting.append(r)
+        return r
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running or self.prefilling)
+
+    def _admit(self) -> Optional[Request]:
+        if not self.waiting or not self.free_slots or len(self.running) >= self.max_running:
+            return None
+        r = self.waiting[0]
+        if not self.can_admit(r):
+            return None
+        self.waiting.popleft()
+        r.slot = self.free_slots.pop()
+        return r
+
+    def schedule(self) -> Optional[Batch]:
+        # an unfinished chunked prefill always continues; otherwise admission follows the decode-burst rule
+        if self.prefilling is None:
+            hold = hold_prefill(self.burst, self.streak, self.last_was_extend, bool(self.running))
+            if not hold:
+                self.prefilling = self._admit()
+        if self.prefilling is not None:
+            segs, budget = [], self.chunk
+            while self.prefilling is not None and budget > 0:
+                r = self.prefilling
+                n = min(budget, r.prompt_len - r.prefilled)
+                last = r.prefilled + n == r.prompt_len
+                segs.append(Segment(r, r.prefilled, r.prompt[r.prefilled:r.prefilled + n], last))
+                r.prefilled += n
+                budget -= n
+                if not last:
+                    break
+                self.prefilling = self._admit() if budget > 0 else None
+            self.streak = next_streak(self.burst, self.streak, True)
+            self.last_was_extend = True
+            return Batch("prefill", segs)
+        if self.running:
+            self.streak = next_streak(self.burst, self.streak, False)
+            self.last_was_extend = False
+            return Batch("decode", [Segment(r, r.kv_len, [r.pending], True) for r in self.running])
+        return None
+
+    def commit_prefill(self, batch: Batch, next_tokens: dict) -> None:
+        for s in batch.segments:
+            r = s.req
+            r.kv_len = s.start + len(s.tokens)
+            if s.logits:
+                r.pending = next_tokens[r.rid]
+                r.output.append(r.pending)
+                self.running.append(r)
+                self._check_done(r)
+
+    def commit_decode(self, new_tokens: dict) -> None:
+        """new_tokens: rid -> list of tokens appended this step (1, or 1 + accepted drafts)."""
+        for r in list(self.running):
+            toks = new_tokens.get(r.rid)
+            if not toks:
+                continue
+            r.kv_len += len(toks)        # the previous pending token and the accepted drafts are now in the pool
+            for t in toks:
+                if len(r.output) >= r.params.max_new_tokens:
+                    break
+                r.output.append(t)
+            r.pending = toks[-1]
+            self._check_done(r)
+
+    def _check_done(self, r: Request) -> None:
+        done = len(r.output) >= r.params.max_new_tokens or (
+            not r.params.ignore_eos and r.output and r.output[-1] in r.params.stop_token_ids)
+        if done:
+            r.finished = True
+            if r in self.running:
+                self.running.remove(r)
+            self.free_slots.append(r.slot)
+
+    def finished_requests(self) -> list:
+        return []

@@ -1,0 +1,290 @@
+"""Dense GQA decoder with interleaved sliding-window / global layers (Gemma class), tensor parallel.
+
+Per layer (Gemma-3 block): x = norm_in(h); qkv = x W_qkv; q, k = qk-norm + RoPE; k, v -> paged pool (fused kernel);
+a = attention(q, pool); o = a W_o (TP all-reduce); h += norm_post_attn(o); x = norm_pre_ffn(h);
+f = (gelu_tanh(x W_g) * x W_u) W_d (TP all-reduce); h += norm_post_ffn(f).  Norms use the (1 + w) convention,
+embeddings are scaled by sqrt(hidden) and tied to the LM head.  Sliding layers see 1024 keys (q - kv < 1024), the
+rule of `attention/extend-gqa/extend_attention_gqa.py:18-24`; head_dim 256 on sliding layers, 512 on global layers.
+
+Tensor parallel (tp ranks): q/k/v heads and FFN columns are split across ranks (column-parallel W_qkv, W_gu;
+row-parallel W_o, W_d followed by an all-reduce), the vocabulary of the LM head is split and the greedy token is the
+max over ranks of the local argmax.  Weights are random-init (seeded) or loaded from HF safetensors (`loader.py`).
+
+The draft head for speculative decoding (EAGLE-style, one sliding-window layer, `speculative/` in the reference)
+shares the embedding / LM head: x = W_fc [emb(token); h_prev] -> layer -> norm -> logits.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Callable, Optional
+
+import torch
+import torch.nn.functional as Fn
+
+from ..config import GQAConfig
+from ..ops import attention as A
+from ..ops import basic as B
+from ..ops import kvcache as K
+
+
+def _randn(shape, std, gen, device, dtype=torch.bfloat16):
+    t = torch.empty(shape, dtype=dtype, device=device)
+    # fill in slices so a 30 GB model never needs a second fp32 copy
+    flat = t.view(-1)
+    step = 1 << 26
+    for i in range(0, flat.numel(), step):
+        n = min(step, flat.numel() - i)
+        flat[i:i + n] = (torch.randn(n, generator=gen, device=device, dtype=torch.float32) * std).to(dtype)
+    return t
+
+
+@dataclass
+class LayerWeights:
+    qkv: torch.Tensor
+    o: torch.Tensor
+    gu: torch.Tensor
+    down: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    n_in: torch.Tensor
+    n_post_attn: torch.Tensor
+    n_pre_ffn: torch.Tensor
+    n_post_ffn: torch.Tensor
+
+
+@dataclass
+class LayerGeom:
+    head_dim: int
+    kv_heads: int        # local
+    q_heads: int         # local
+    window: int          # 0 = global
+    kind: str            # "global" | "swa"
+
+
+class GQAModel:
+    def __init__(self, cfg: GQAConfig, device, tp_rank: int = 0, tp: int = 1, seed: int = 0,
+                 all_reduce: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
+                 weights: Optional[dict] = None, draft: bool = False):
+        self.cfg, self.device, self.tp_rank, self.tp = cfg, torch.device(device), tp_rank, tp
+        self.all_reduce = all_reduce
+        if cfg.num_q_heads % tp or cfg.num_kv_heads % tp or cfg.num_kv_heads_global % tp or cfg.ffn % tp:
+            raise ValueError(f"tp={tp} does not divide the head / ffn counts")
+        self.hidden = cfg.hidden
+        self.ffn_local = cfg.ffn // tp
+        self.vocab_local = cfg.vocab // tp
+        n_layers = cfg.draft_layers if draft else cfg.num_layers
+        self.geoms = []
+        for i in range(n_layers):
+            glob = (not draft) and cfg.is_global(i)
+            d = cfg.head_dim_global if glob else cfg.head_dim
+            hk = (cfg.num_kv_heads_global if glob else cfg.num_kv_heads) // tp
+            self.geoms.append(LayerGeom(d, hk, cfg.num_q_heads // tp, 0 if glob else cfg.sliding_window,
+                                        "global" if glob else ("draft" if draft else "swa")))
+        gen = torch.Generator(device=self.device)
+        gen.manual_seed(seed * 1000 + (7 if draft else 0))
+        std = cfg.init_std
+        h = cfg.hidden
+        if weights is None:
+            self.embed = None if draft else _randn((cfg.vocab, h), std, gen, self.device)
+            self.layers = []
+            for g in self.geoms:
+                zeros = lambda n: torch.zeros(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
+                self.layers.append(LayerWeights(
+                    qkv=_randn(((g.q_heads + 2 * g.kv_heads) * g.head_dim, h), std, gen, self.device),
+                    o=_randn((h, g.q_heads * g.head_dim), std, gen, self.device),
+                    gu=_randn((2 * self.ffn_local, h), std, gen, self.device),
+                    down=_randn((h, self.ffn_local), std, gen, self.device),
+                    q_norm=zeros(g.head_dim), k_norm=zeros(g.head_dim),
+                    n_in=zeros(h), n_post_attn=zeros(h), n_pre_ffn=zeros(h), n_post_ffn=zeros(h)))
+            self.final_norm = torch.zeros(h, dtype=torch.bfloat16, device=self.device)
+            self.fc = _randn((h, 2 * h), std, gen, self.device) if draft else None
+        else:
+            self._adopt(weights, draft)
+        self.rope = {}
+        self.embed_scale = math.sqrt(h) if cfg.embed_scale else 1.0
+
+    # ------------------------------------------------------------------------------------------------ weights
+    def _adopt(self, w: dict, draft: bool) -> None:
+        """Take already-sharded tensors (see loader.py) keyed by HF names."""
+        h = self.cfg.hidden
+        self.embed = None if draft else w["model.embed_tokens.weight"]
+        self.final_norm = w["model.norm.weight"]
+        self.fc = w.get("fc.weight")
+        self.layers = []
+        for i, g in enumerate(self.geoms):
+            p = f"model.layers.{i}."
+            self.layers.append(LayerWeights(
+                qkv=torch.cat([w[p + "self_attn.q_proj.weight"], w[p + "self_attn.k_proj.weight"],
+                               w[p + "self_attn.v_proj.weight"]], 0),
+                o=w[p + "self_attn.o_proj.weight"],
+                gu=torch.cat([w[p + "mlp.gate_proj.weight"], w[p + "mlp.up_proj.weight"]], 0),
+                down=w[p + "mlp.down_proj.weight"],
+                q_norm=w[p + "self_attn.q_norm.weight"], k_norm=w[p + "self_attn.k_norm.weight"],
+                n_in=w[p + "input_layernorm.weight"], n_post_attn=w[p + "post_attention_layernorm.weight"],
+                n_pre_ffn=w[p + "pre_feedforward_layernorm.weight"],
+                n_post_ffn=w[p + "post_feedforward_layernorm.weight"]))
+        assert all(l.qkv.shape[1] == h for l in self.layers)
+
+    def rope_table(self, d: int, theta: float, max_pos: int) -> torch.Tensor:
+        key = (d, theta)
+        t = self.rope.get(key)
+        if t is None or t.shape[0] < max_pos:
+            t = B.rope_table(max_pos, d, theta, self.device)
+            self.rope[key] = t
+        return t
+
+    def num_bytes(self) -> int:
+        n = sum(t.numel() * t.element_size() for l in self.layers for t in vars(l).values())
+        if self.embed is not None:
+            n += self.embed.numel() * 2
+        return n
+
+    # ------------------------------------------------------------------------------------------------ forward
+    def _reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.tp > 1:
+            return self.all_reduce(x)
+        return x
+
+    def layer_forward(self, i: int, x_norm: torch.Tensor, resid: torch.Tensor, st: "StepTensors",
+                      kv: "GQAKVCache", layer_id: int, next_norm: Optional[torch.Tensor]) -> torch.Tensor:
+        """x_norm = norm_in(h) [T, H]; resid = h (updated in place).  Returns the next layer's normed input."""
+        cfg, w, g = self.cfg, self.layers[i], self.geoms[i]
+        eps = cfg.rms_eps
+        qkv = Fn.linear(x_norm, w.qkv)
+        theta = cfg.rope_theta_global if g.kind == "global" else cfg.rope_theta
+        cs = self.rope_table(g.head_dim, theta, kv.max_pos)
+        pool = kv.pools[layer_id]
+        slot = st.slot[g.kind]
+        q = K.gqa_prep(qkv, w.q_norm if cfg.qk_norm else None, w.k_norm if cfg.qk_norm else None, cs, st.pos, slot,
+                       pool, kv.fmt, g.q_heads, g.kv_heads, g.head_dim, eps, True, kv.k_scale, kv.v_scale)
+        attn = A.gqa_decode(q, pool, kv.tables[g.kind].dev, st.kv_len, st.n_q, g.kv_heads, kv.fmt,
+                            1.0 / math.sqrt(g.head_dim), g.window, kv.k_scale, kv.v_scale,
+                            splits=st.splits.get(g.kind), ws=kv.workspace(g.head_dim, g.kv_heads), req_idx=st.req_idx)
+        o = self._reduce(Fn.linear(attn.view(attn.shape[0], -1), w.o))
+        o = B.rmsnorm(o, w.n_post_attn, eps, True)
+        x = B.rmsnorm(o, w.n_pre_ffn, eps, True, residual=resid)          # resid += o; x = norm(resid)
+        f = self._reduce(Fn.linear(B.act_mul(Fn.linear(x, w.gu), gelu=True), w.down))
+        f = B.rmsnorm(f, w.n_post_ffn, eps, True)
+        return B.rmsnorm(f, next_norm, eps, True, residual=resid)       # resid += f; x = norm_next(resid)
+
+    def forward(self, st: "StepTensors", kv: "GQAKVCache", layer_offset: int = 0,
+                inputs_embeds: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Returns (final-normed hidden [T, H], pre-norm residual stream [T, H])."""
+        cfg = self.cfg
+        if inputs_embeds is None:
+            resid = B.embed(st.ids, self.embed, self.embed_scale)
+        else:
+            resid = inputs_embeds
+        x = B.rmsnorm(resid, self.layers[0].n_in, cfg.rms_eps, True)
+        for i in range(len(self.layers)):
+            nxt = self.layers[i + 1].n_in if i + 1 < len(self.layers) else self.final_norm
+            x = self.layer_forward(i, x, resid, st, kv, layer_offset + i, nxt)
+        return x, resid
+
+    def logits_local(self, x_final: torch.Tensor, embed: torch.Tensor) -> torch.Tensor:
+        lo = self.tp_rank * self.vocab_local
+        return Fn.linear(x_final, embed[lo:lo + self.vocab_local])
+
+    @torch.no_grad()
+    def reference_logits(self, tokens: list) -> torch.Tensor:
+        """Cache-free fp32-attention forward of one sequence (tp = 1): logits [T, V].  The oracle for engine tests:
+        same op sequence and bf16 rounding points, dense causal attention instead of the paged kernel."""
+        from ..ops.attention import dense_attention_ref
+        from ..ops.kvcache import _head_rmsnorm
+        cfg, eps = self.cfg, self.cfg.rms_eps
+        t = len(tokens)
+        ids = torch.tensor(tokens, dtype=torch.int32, device=self.device)
+        pos = torch.arange(t, device=self.device)
+        resid = B.embed(ids, self.embed, self.embed_scale)
+        x = B.rmsnorm(resid, self.layers[0].n_in, eps, True)
+        for i, (w, g) in enumerate(zip(self.layers, self.geoms)):
+            qkv = Fn.linear(x, w.qkv).float().reshape(t, -1, g.head_dim)
+            theta = cfg.rope_theta_global if g.kind == "global" else cfg.rope_theta
+            cs = self.rope_table(g.head_dim, theta, t + 64)
+            q = B.apply_rope_ref(_head_rmsnorm(qkv[:, :g.q_heads], w.q_norm, eps, True), pos, cs)
+            k = B.apply_rope_ref(_head_rmsnorm(qkv[:, g.q_heads:g.q_heads + g.kv_heads], w.k_norm, eps, True), pos, cs)
+            v = qkv[:, g.q_heads + g.kv_heads:]
+            q, k, v = (z.to(torch.bfloat16).float() for z in (q, k, v))
+            a = dense_attention_ref(q, k, v, 1.0 / math.sqrt(g.head_dim), pos, pos, g.window)
+            o = Fn.linear(a.to(torch.bfloat16).reshape(t, -1), w.o)
+            o = B.rmsnorm(o, w.n_post_attn, eps, True)
+            x = B.rmsnorm(o, w.n_pre_ffn, eps, True, residual=resid)
+            f = Fn.linear(B.act_mul(Fn.linear(x, w.gu), gelu=True), w.down)
+            f = B.rmsnorm(f, w.n_post_ffn, eps, True)
+            nxt = self.layers[i + 1].n_in if i + 1 < len(self.layers) else self.final_norm
+            x = B.rmsnorm(f, nxt, eps, True, residual=resid)
+        return Fn.linear(x, self.embed).float()
+
+
+@dataclass
+class StepTensors:
+    """Device inputs of one forward step (fixed addresses when captured in a CUDA graph)."""
+    ids: torch.Tensor                 # int32 [T]
+    pos: torch.Tensor                 # int32 [T]
+    slot: dict                        # kind -> int32 [T] pool slot (-1 = no write)
+    kv_len: torch.Tensor              # int32 [B] per group
+    req_idx: torch.Tensor             # int32 [B] page-table row per group
+    n_q: int
+    splits: dict = field(default_factory=dict)   # kind -> (num_splits, tiles_per_split) or None
+
+
+class GQAKVCache:
+    """Paged KV pools of all layers + page tables.  Kinds: "global" (full-context layers), "swa" (sliding-window
+    layers, pages released behind the window) and "draft" (the draft head's sliding-window layer)."""
+
+    def __init__(self, cfg: GQAConfig, tp: int, device, fmt: str, max_requests: int, max_seq: int,
+                 global_pages: int, swa_pages: int, draft_pages: int = 0, k_scale: float = 1.0,
+                 v_scale: float = 1.0):
+        from ..kv.allocator import PageAllocator, PageTable
+        self.cfg, self.fmt_name, self.fmt = cfg, fmt, K.FMT_IDS[fmt]
+        self.device = torch.device(device)
+        self.max_pos = max_seq + 64
+        self.k_scale, self.v_scale = k_scale, v_scale
+        max_pages = (max_seq + 63) // 64 + 1
+        self.pools = []
+        self.kinds = []
+        for i in range(cfg.num_layers):
+            glob = cfg.is_global(i)
+            d = cfg.head_dim_global if glob else cfg.head_dim
+            hk = (cfg.num_kv_heads_global if glob else cfg.num_kv_heads) // tp
+            n = global_pages if glob else swa_pages
+            self.pools.append(torch.zeros(n, hk, 2, K.part_bytes(self.fmt, d), dtype=torch.uint8, device=device))
+            self.kinds.append("global" if glob else "swa")
+        if draft_pages:
+            for _ in range(cfg.draft_layers):
+                self.pools.append(torch.zeros(draft_pages, cfg.num_kv_heads // tp, 2, K.part_bytes(self.fmt, cfg.head_dim),
+                                              dtype=torch.uint8, device=device))
+                self.kinds.append("draft")
+        self.alloc = {"global": PageAllocator(global_pages), "swa": PageAllocator(swa_pages)}
+        self.tables = {"global": PageTable(max_requests, max_pages, device), "swa": PageTable(max_requests, max_pages, device)}
+        if draft_pages:
+            self.alloc["draft"] = PageAllocator(draft_pages)
+            self.tables["draft"] = PageTable(max_requests, max_pages, device)
+        self._ws = {}
+
+    def workspace(self, d: int, hk: int) -> Optional[A.DecodeWorkspace]:
+        return self._ws.get((d, hk))
+
+    def reserve_workspace(self, max_groups: int, max_splits: int) -> None:
+        if self.device.type != "cuda":
+            return
+        for i, p in enumerate(self.pools):
+            hk = p.shape[1]
+            d = {K.FMT_NVFP4: p.shape[3] * 16 // (64 * 9), K.FMT_FP8: p.shape[3] // 64,
+                 K.FMT_BF16: p.shape[3] // 128}[self.fmt]
+            key = (d, hk)
+            need = max_groups * hk * max_splits * 16
+            if key not in self._ws or self._ws[key].lse_part.numel() < need:
+                self._ws[key] = A.DecodeWorkspace.allocate(max_groups, hk, max_splits, d, device=self.device)
+
+    def sync_tables(self) -> None:
+        for t in self.tables.values():
+            t.sync()
+
+    def bytes_per_token(self) -> float:
+        tot = 0.0
+        for p, kind in zip(self.pools, self.kinds):
+            if kind == "global":
+                tot += p[0].numel() / 64
+        return tot

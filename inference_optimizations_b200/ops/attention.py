@@ -47,14 +47,17 @@ class DecodeWorkspace:
 def gqa_decode(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor, kv_len: torch.Tensor, n_q: int,
                hk: int, fmt: int, sm_scale: float, window: int = 0, k_scale: float = 1.0, v_scale: float = 1.0,
                splits: Optional[tuple[int, int]] = None, ws: Optional[DecodeWorkspace] = None,
-               max_ctx: Optional[int] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """q bf16 [B * n_q, Hq, D] -> out bf16 [B * n_q, Hq, D]."""
+               max_ctx: Optional[int] = None, out: Optional[torch.Tensor] = None,
+               req_idx: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q bf16 [B * n_q, Hq, D] -> out bf16 [B * n_q, Hq, D].  Batch entry b uses page-table row req_idx[b]
+    (default b)."""
     b = kv_len.shape[0]
     d = q.shape[-1]
     if out is None:
         out = torch.empty_like(q)
     if not q.is_cuda:
-        out.copy_(gqa_decode_ref(q, pool, page_table, kv_len, n_q, hk, fmt, sm_scale, window, k_scale, v_scale)
+        pt = page_table if req_idx is None else page_table[req_idx.long()]
+        out.copy_(gqa_decode_ref(q, pool, pt, kv_len, n_q, hk, fmt, sm_scale, window, k_scale, v_scale)
                   .to(out.dtype))
         return out
     if splits is None:
@@ -64,7 +67,7 @@ def gqa_decode(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor, kv
     ns, tps = splits
     if ws is None:
         ws = DecodeWorkspace.allocate(b, hk, ns, d, device=q.device)
-    ext().gqa_decode(q, pool, page_table, kv_len, out, ws.o_part, ws.lse_part, ws.status, n_q, hk, 64, window, fmt,
+    ext().gqa_decode(q, pool, page_table, req_idx, kv_len, out, ws.o_part, ws.lse_part, ws.status, n_q, hk, 64, window, fmt,
                      tps, ns, sm_scale, k_scale, v_scale)
     return out
 
