@@ -3,14 +3,17 @@
 // Capability of the reference's split-K verify and NVFP4 decode kernels (`attention/verify-splitk/gemma31_verify.py`
 // K29, `kv-cache-4bit/kv4tri-triton-backend/kv4tri_nvfp4_attention.py:257` nvfp4_decode_fwd): one CTA per
 // (request, kv head, split); its rows are the request's n_q query tokens x the G query heads sharing the kv head, so
-// every KV byte is read once per kv head.  Designed here for tcgen05 instead of a transliteration:
+// every KV byte is read once per kv head.  Designed for tcgen05 rather than transliterated:
 //
 //  * swap-AB: tokens are the MMA M dimension (128 per tile), query rows the N dimension (16), so a decode step with
 //    2..16 rows still issues full-height UMMAs.  S^T = K Q^T lands in TMEM with lane = token, column = row.
-//  * O^T = V^T P^T with V read MN-major straight from the same token-row tiles K uses (no transpose pass).
-//  * the pool is read by one bulk async copy per (page, kv head, K|V) into a raw ring; 8 dequant warps expand
-//    E2M1 x E4M3 (or E4M3, or bf16) to f16 128-byte-swizzled tiles; the pool rows are stored with the same 16-byte
-//    chunk XOR swizzle so both the raw reads and the tile writes are bank-conflict free.
+//  * K never touches shared memory after its raw bytes: the dequant warp that owns a token (TMEM lane) expands it
+//    to f16 and writes it straight into TMEM with tcgen05.st; QK is the A-from-TMEM UMMA form.  One handoff per tile.
+//  * O^T = V^T P^T with V (MN-major) read from f16 128-byte-swizzled slabs in a 6-deep shared-memory ring.
+//  * the pool is read by one bulk async copy per (page, kv head, K|V) into a raw ring; pool rows are stored with a
+//    16-byte chunk XOR swizzle so the dequant reads and slab writes are bank-conflict free.
+//  * skewed schedule: iteration j handles K of tile j, then V of tile j-1, so the softmax of tile j-1 overlaps the
+//    next tile's loads, dequant and QK instead of sitting between QK and PV.
 //  * warp roles: 0-3 softmax + O accumulation (registers), 4-11 dequant, 12 bulk-copy producer, 13 UMMA issuer.
 //  * split-K partials (o normalised, lse in log2 units) are merged by a second kernel.
 //  * every mbarrier wait is bounded; a timeout records a status code and the CTA unwinds.
@@ -22,23 +25,25 @@ namespace {
 
 constexpr int kTileTok = 128;
 constexpr int kN = 16;           // UMMA N (query rows, padded)
-constexpr int kRing = 4;         // f16 slab buffers (128 tokens x 64 dims each)
 constexpr int kSlabBytes = kTileTok * 128;
 constexpr int kThreads = 448;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kDequantWarps = 8;
 constexpr int kProducerWarp = 12;
 constexpr int kMmaWarp = 13;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemK = 256;  // K tile: D/2 columns (two f16 per column)
 
 struct Smem {
   uint64_t raw_full[8], raw_empty[8];
-  uint64_t chunk_full[kRing], chunk_empty[kRing];
+  uint64_t ring_full[8], ring_empty[8];
+  uint64_t k_full, k_empty;
   uint64_t s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2];
   uint32_t tmem_base;
   int abort;
+  int raw_valid[8];       // stage holds a real page (else the dequant writes zeros); published by the producer
   float red[kSoftmaxWarps][kN];
   float row_m[kN];
-  float row_alpha[kN];
 };
 
 // must match kv_swizzle_byte() (kernels.h), which the pool writers use
@@ -63,20 +68,43 @@ __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t v) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Expand 32 values (one token row, dims [32*half, 32*half+32) of slab c) to 4 f16 16-byte chunks.
 template <int FMT, int D>
-__device__ __forceinline__ void dequant_32(const uint8_t* part, int r, int c, int half, uint4 (&o)[4]) {
+__device__ __forceinline__ constexpr int part_bytes() {
+  return FMT == kKvNvfp4 ? 64 * (D / 2 + D / 16) : (FMT == kKvFp8 ? 64 * D : 64 * D * 2);
+}
+template <int FMT, int D>
+__device__ __host__ __forceinline__ constexpr int raw_stages() {
+  return part_bytes<FMT, D>() <= 10 * 1024 ? 6 : (part_bytes<FMT, D>() <= 32 * 1024 ? 4 : 2);
+}
+template <int FMT, int D>
+__device__ __host__ __forceinline__ constexpr int ring_slabs() {
+  return raw_stages<FMT, D>() * part_bytes<FMT, D>() <= 100 * 1024 ? 6 : 4;
+}
+
+// 16 code bytes (32 values) of an NVFP4 row at 16-byte chunk j -> 16 f16x2, scaled by the two block scales.
+__device__ __forceinline__ void nvfp4_chunk(const uint8_t* row, int pos, uint32_t s0, uint32_t s1, uint32_t* ow) {
+  const uint4 in = *reinterpret_cast<const uint4*>(row + pos * 16);
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(&in);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t f[4];
+    e2m1x8_to_f16x2x4(w[i], f);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) ow[4 * i + k] = hmul2_u32(f[k], i < 2 ? s0 : s1);
+  }
+}
+__device__ __forceinline__ uint32_t scale_h2(uint16_t two, int which) {
+  const uint32_t f = e4m3x2_to_f16x2(two);
+  return half2_bcast(__ushort_as_half(static_cast<unsigned short>(which ? (f >> 16) : (f & 0xFFFF))));
+}
+
+// Expand 32 values (one token row, dims [64c + 32 half, +32)) to 16 f16x2 words.
+template <int FMT, int D>
+__device__ __forceinline__ void dequant_32(const uint8_t* part, int r, int c, int half, uint32_t* ow) {
   if constexpr (FMT == kKvNvfp4) {
     constexpr int RB = D / 2, NCH = (RB / 16) < 8 ? (RB / 16) : 8;
-    const uint8_t* row = part + r * RB;
-    const uint4 in = *reinterpret_cast<const uint4*>(row + pool_chunk_pos(2 * c + half, r, NCH) * 16);
     const uint16_t sc = *reinterpret_cast<const uint16_t*>(part + 64 * RB + r * (D / 16) + c * 4 + half * 2);
-    const uint32_t s0 = half2_bcast(__ushort_as_half(static_cast<unsigned short>(e4m3x2_to_f16x2(sc) & 0xFFFF)));
-    const uint32_t s1 = half2_bcast(__ushort_as_half(static_cast<unsigned short>(e4m3x2_to_f16x2(sc) >> 16)));
-    const uint8_t* b = reinterpret_cast<const uint8_t*>(&in);
-    uint32_t* ow = reinterpret_cast<uint32_t*>(o);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) ow[i] = hmul2_u32(e2m1x2_to_f16x2(b[i]), i < 8 ? s0 : s1);
+    nvfp4_chunk(part + r * RB, pool_chunk_pos(2 * c + half, r, NCH), scale_h2(sc, 0), scale_h2(sc, 1), ow);
   } else if constexpr (FMT == kKvFp8) {
     constexpr int RB = D, NCH = 8;
     const uint8_t* row = part + r * RB;
@@ -84,9 +112,8 @@ __device__ __forceinline__ void dequant_32(const uint8_t* part, int r, int c, in
     for (int k = 0; k < 2; ++k) {
       const uint4 in = *reinterpret_cast<const uint4*>(row + pool_chunk_pos(4 * c + 2 * half + k, r, NCH) * 16);
       const uint16_t* h = reinterpret_cast<const uint16_t*>(&in);
-      uint32_t* ow = reinterpret_cast<uint32_t*>(&o[2 * k]);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ow[i] = e4m3x2_to_f16x2(h[i]);
+      for (int i = 0; i < 8; ++i) ow[8 * k + i] = e4m3x2_to_f16x2(h[i]);
     }
   } else {
     constexpr int RB = 2 * D, NCH = 8;
@@ -95,31 +122,27 @@ __device__ __forceinline__ void dequant_32(const uint8_t* part, int r, int c, in
     for (int k = 0; k < 4; ++k) {
       const uint4 in = *reinterpret_cast<const uint4*>(row + pool_chunk_pos(8 * c + 4 * half + k, r, NCH) * 16);
       const uint32_t* iw = reinterpret_cast<const uint32_t*>(&in);
-      uint32_t* ow = reinterpret_cast<uint32_t*>(&o[k]);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) ow[i] = bf16x2_to_f16x2(iw[i]);
+      for (int i = 0; i < 4; ++i) ow[4 * k + i] = bf16x2_to_f16x2(iw[i]);
     }
   }
-}
-
-template <int FMT, int D>
-__device__ __forceinline__ constexpr int part_bytes() {
-  return FMT == kKvNvfp4 ? 64 * (D / 2 + D / 16) : (FMT == kKvFp8 ? 64 * D : 64 * D * 2);
 }
 
 template <int FMT, int D, int RMAX>
 __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecodeArgs a) {
   constexpr int NS = D / 64;                       // 64-dim slabs per head vector
   constexpr int PB = part_bytes<FMT, D>();         // bytes of K (or V) of one (page, head)
-  constexpr int NST = (PB <= 20 * 1024) ? 6 : ((PB <= 32 * 1024) ? 4 : 2);
+  constexpr int NST = raw_stages<FMT, D>();
+  constexpr int RING = ring_slabs<FMT, D>();
   constexpr int MB = D / 128;                      // 128-dim M blocks of O^T
   constexpr int kOCols = MB * kN;
   static_assert(RMAX <= kN, "rows");
+  static_assert(RING % 2 == 0, "V slab pairs need an even ring");
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = base;                                   // kRing x 16 KB
-  uint8_t* sq = ring + kRing * kSlabBytes;                // NS x 2 KB
+  uint8_t* ring = base;                                   // RING x 16 KB (V slabs)
+  uint8_t* sq = ring + RING * kSlabBytes;                 // NS x 2 KB
   uint8_t* sp = sq + NS * kN * 128;                       // 2 x (2 x 2 KB)
   uint8_t* raw = sp + 2 * 2 * kN * 128;                   // NST x PB
   Smem& sm = *reinterpret_cast<Smem*>(raw + NST * PB);
@@ -167,7 +190,9 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
   }
   if (threadIdx.x == 0) {
     for (int i = 0; i < NST; ++i) { mbar_init(&sm.raw_full[i], 1); mbar_init(&sm.raw_empty[i], kDequantWarps); }
-    for (int i = 0; i < kRing; ++i) { mbar_init(&sm.chunk_full[i], kDequantWarps); mbar_init(&sm.chunk_empty[i], 1); }
+    for (int i = 0; i < RING; ++i) { mbar_init(&sm.ring_full[i], kDequantWarps); mbar_init(&sm.ring_empty[i], 1); }
+    mbar_init(&sm.k_full, kDequantWarps);
+    mbar_init(&sm.k_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.s_full[i], 1); mbar_init(&sm.s_empty[i], kSoftmaxWarps);
       mbar_init(&sm.p_full[i], kSoftmaxWarps); mbar_init(&sm.o_full[i], 1); mbar_init(&sm.o_empty[i], kSoftmaxWarps);
@@ -175,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
     sm.abort = 0;
     fence_mbar_init();
   }
-  if (warp == kMmaWarp) { tmem_alloc(&sm.tmem_base, 256); tmem_relinquish(); }
+  if (warp == kMmaWarp) { tmem_alloc(&sm.tmem_base, kTmemCols); tmem_relinquish(); }
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -183,26 +208,38 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
   const uint32_t tmem = sm.tmem_base;
   const uint32_t tS = tmem;            // 2 x 16 columns
   const uint32_t tO = tmem + 32;       // 2 x kOCols columns
+  const uint32_t tK = tmem + kTmemK;   // D/2 columns
   volatile int* abort = &sm.abort;
+
+  // Work order (every role walks it identically): iteration j = 0..ntiles handles the K part of tile j (when
+  // j < ntiles), then the V part of tile j - 1 (when j >= 1).  A "part" is one (K | V, tile): 2 raw pages
+  // (raw seq 2p, 2p+1).  V parts also own NS ring slabs (ring seq NS v .. NS v + NS - 1, v = tile index).
+  auto parts_before = [&](int j) { return min(j, ntiles) + max(0, j - 1); };
+  auto part_index = [&](int j, int which) { return parts_before(j) + ((which == 1 && j < ntiles) ? 1 : 0); };
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
       const uint8_t* pool = a.pool;
       int issued = 0;
-      for (int j = 0; j < ntiles && !*abort; ++j) {
-        for (int part = 0; part < 2; ++part) {
+      for (int j = 0; j <= ntiles && !*abort; ++j) {
+        for (int which = 0; which < 2; ++which) {
+          const int tile = which == 0 ? j : j - 1;
+          if (tile < 0 || tile >= ntiles) continue;
+          const int pidx0 = part_index(j, which);
           for (int pg = 0; pg < 2; ++pg) {
-            const int seq = 4 * j + 2 * part + pg, st = seq % NST;
+            const int seq = 2 * pidx0 + pg, st = seq % NST;
             if (*abort) break;
             if (!mbar_wait(&sm.raw_empty[st], ((seq / NST) & 1) ^ 1, abort, a.status, kTimeoutProducer)) break;
             issued = seq + 1;
-            const int pidx = (tile0 + j) * 2 + pg;
+            const int pidx = (tile0 + tile) * 2 + pg;
             const int phys = (pidx >= first_page && pidx < n_pages) ? pt[pidx] : -1;
             if (phys >= 0) {
-              const uint8_t* src = pool + (static_cast<size_t>(phys) * a.Hk + h) * (2 * PB) + part * PB;
+              const uint8_t* src = pool + (static_cast<size_t>(phys) * a.Hk + h) * (2 * PB) + which * PB;
+              sm.raw_valid[st] = 1;
               mbar_expect_tx(&sm.raw_full[st], PB);
               bulk_g2s(raw + st * PB, src, PB, &sm.raw_full[st]);
             } else {
+              sm.raw_valid[st] = 0;
               mbar_arrive(&sm.raw_full[st]);
             }
           }
@@ -215,85 +252,123 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
   } else if (warp >= kSoftmaxWarps && warp < kSoftmaxWarps + kDequantWarps) {
     // ---------------------------------------------------------------- dequant warps
     const int dw = warp - kSoftmaxWarps;
-    const int tok = 16 * dw + (lane & 7) + 8 * (lane >> 4);   // 0..127 within the tile
-    const int half = (lane >> 3) & 1;
-    const int pg = tok / 64, r = tok % 64;
-    for (int j = 0; j < ntiles; ++j) {
-      const int pidx = (tile0 + j) * 2 + pg;
-      const bool valid = pidx >= first_page && pidx < n_pages && pt[pidx] >= 0;
-      for (int part = 0; part < 2; ++part) {
-        const int seq_raw = 4 * j + 2 * part + pg, st = seq_raw % NST;
-        // both pages of this part must be resident (each warp only reads its own page, but arrives on both)
-        const int seq0 = 4 * j + 2 * part, st0 = seq0 % NST, st1 = (seq0 + 1) % NST;
-        if (!mbar_wait(&sm.raw_full[st0], (seq0 / NST) & 1, abort, a.status, kTimeoutConsumer)) goto done;
-        if (!mbar_wait(&sm.raw_full[st1], ((seq0 + 1) / NST) & 1, abort, a.status, kTimeoutConsumer)) goto done;
+    // K role: thread = TMEM lane = token; warps dw and dw + 4 split the head dims in halves
+    const int kq = warp & 3, ktok = 32 * kq + lane, kpg = ktok / 64, kr = ktok % 64;
+    const int kdim0 = (dw >> 2) * (D / 2);
+    const uint32_t k_lane = static_cast<uint32_t>(32 * kq) << 16;
+    // V role: warp dw covers tokens 16 dw .. 16 dw + 15 x two 32-dim halves of a slab
+    const int vtok = 16 * dw + (lane & 7) + 8 * (lane >> 4);
+    const int vhalf = (lane >> 3) & 1;
+    const int vpg = vtok / 64, vr = vtok % 64;
+    for (int j = 0; j <= ntiles; ++j) {
+      if (j < ntiles) {  // ---- K(j) -> TMEM
+        const int p = part_index(j, 0);
+        const int seq0 = 2 * p, st0 = seq0 % NST, st1 = (seq0 + 1) % NST;
+        if (!mbar_wait(&sm.raw_full[st0], (seq0 / NST) & 1, abort, a.status, kTimeoutConsumer)) break;
+        if (!mbar_wait(&sm.raw_full[st1], ((seq0 + 1) / NST) & 1, abort, a.status, kTimeoutConsumer)) break;
+        if (!mbar_wait(&sm.k_empty, (j & 1) ^ 1, abort, a.status, kTimeoutConsumer)) break;
+        tc_fence_after();
+        const int st = kpg ? st1 : st0;
+        const bool valid = sm.raw_valid[st] != 0;
+        const uint8_t* part = raw + st * PB;
+#pragma unroll 1
+        for (int d0 = kdim0; d0 < kdim0 + D / 2; d0 += 64) {
+          uint32_t v[32];
+          if (valid) {
+            dequant_32<FMT, D>(part, kr, d0 / 64, 0, v);
+            dequant_32<FMT, D>(part, kr, d0 / 64, 1, v + 16);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0;
+          }
+          tmem_st32(tK + k_lane + d0 / 2, v);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sm.k_full);
+          mbar_arrive(&sm.raw_empty[st0]);
+          mbar_arrive(&sm.raw_empty[st1]);
+        }
+      }
+      if (j == 0) continue;
+      {  // ---- V(j-1) -> shared-memory ring
+        const int i = j - 1;
+        const int p = part_index(j, 1);
+        const int seq0 = 2 * p, st0 = seq0 % NST, st1 = (seq0 + 1) % NST;
+        if (!mbar_wait(&sm.raw_full[st0], (seq0 / NST) & 1, abort, a.status, kTimeoutConsumer)) break;
+        if (!mbar_wait(&sm.raw_full[st1], ((seq0 + 1) / NST) & 1, abort, a.status, kTimeoutConsumer)) break;
+        const int st = vpg ? st1 : st0;
+        const bool valid = sm.raw_valid[st] != 0;
+        bool ok = true;
         for (int c = 0; c < NS; ++c) {
-          const int seq = j * 2 * NS + part * NS + c, buf = seq % kRing;
-          if (!mbar_wait(&sm.chunk_empty[buf], ((seq / kRing) & 1) ^ 1, abort, a.status, kTimeoutConsumer)) goto done;
-          uint4 o[4];
-          if (valid) dequant_32<FMT, D>(raw + st * PB, r, c, half, o);
-          else { o[0] = o[1] = o[2] = o[3] = make_uint4(0, 0, 0, 0); }
+          const int seq = NS * i + c, buf = seq % RING;
+          if (!(ok = mbar_wait(&sm.ring_empty[buf], ((seq / RING) & 1) ^ 1, abort, a.status, kTimeoutConsumer)))
+            break;
+          uint32_t o[16];
+          if (valid) dequant_32<FMT, D>(raw + st * PB, vr, c, vhalf, o);
+          else {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) o[k] = 0;
+          }
           uint8_t* slab = ring + buf * kSlabBytes;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(slab + sw128_chunk(tok, half * 4 + q)) = o[q];
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(slab + sw128_chunk(vtok, vhalf * 4 + q)) =
+                make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&sm.chunk_full[buf]);
+          if (lane == 0) mbar_arrive(&sm.ring_full[buf]);
         }
+        if (!ok) break;
         __syncwarp();
         if (lane == 0) { mbar_arrive(&sm.raw_empty[st0]); mbar_arrive(&sm.raw_empty[st1]); }
       }
     }
-  done:;
   } else if (warp == kMmaWarp) {
-    // ---------------------------------------------------------------- UMMA issuer
-    const uint32_t id_qk = idesc_dense(0, 0, 128, kN);
-    const uint32_t id_pv = idesc_dense(0, 0, 128, kN) | (1u << 15);   // A (V^T) MN-major
-    const uint32_t ring_addr = smem_u32(ring), q_addr = smem_u32(sq), p_addr = smem_u32(sp);
-    for (int j = 0; j < ntiles; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
-      bool ok = true;
-      for (int c = 0; c < NS && ok; ++c) {
-        const int seq = j * 2 * NS + c, buf = seq % kRing;
-        ok = mbar_wait(&sm.chunk_full[buf], (seq / kRing) & 1, abort, a.status, kTimeoutMma);
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) {
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_f16_ss(tS + sb * kN, desc_sw128(ring_addr + buf * kSlabBytes + kk * 32),
-                        desc_sw128(q_addr + c * (kN * 128) + kk * 32), id_qk, (c > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&sm.chunk_empty[buf]);
+    // ---------------------------------------------------------------- UMMA issuer (one thread)
+    if (lane == 0) {
+      const uint32_t id_qk = idesc_dense(0, 0, 128, kN);
+      const uint32_t id_pv = idesc_dense(0, 0, 128, kN) | (1u << 15);   // A (V^T) MN-major
+      const uint32_t ring_addr = smem_u32(ring), q_addr = smem_u32(sq), p_addr = smem_u32(sp);
+      for (int j = 0; j <= ntiles; ++j) {
+        if (j < ntiles) {  // QK(j): A = K tile in TMEM, B = Q slabs
+          const int sb = j & 1;
+          if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
+          if (!mbar_wait(&sm.k_full, j & 1, abort, a.status, kTimeoutMma)) break;
+          tc_fence_after();
+#pragma unroll 4
+          for (int s = 0; s < D / 16; ++s)
+            umma_f16_ts(tS + sb * kN, tK + 8 * s, desc_sw128(q_addr + (s >> 2) * (kN * 128) + (s & 3) * 32), id_qk,
+                        s > 0 ? 1u : 0u);
+          umma_commit(&sm.s_full[sb]);
+          umma_commit(&sm.k_empty);
         }
-        __syncwarp();
-      }
-      if (!ok) break;
-      if (lane == 0) umma_commit(&sm.s_full[sb]);
-      __syncwarp();
-      if (!mbar_wait(&sm.p_full[sb], (j >> 1) & 1, abort, a.status, kTimeoutMma)) break;
-      if (!mbar_wait(&sm.o_empty[sb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
-      for (int mb = 0; mb < MB && ok; ++mb) {
-        const int seq0 = j * 2 * NS + NS + 2 * mb, buf0 = seq0 % kRing;
-        ok = mbar_wait(&sm.chunk_full[buf0], (seq0 / kRing) & 1, abort, a.status, kTimeoutMma) &&
-             mbar_wait(&sm.chunk_full[buf0 + 1], ((seq0 + 1) / kRing) & 1, abort, a.status, kTimeoutMma);
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) {
+        if (j == 0) continue;
+        // PV(j - 1)
+        const int i = j - 1, sb = i & 1;
+        if (!mbar_wait(&sm.p_full[sb], (i >> 1) & 1, abort, a.status, kTimeoutMma)) break;
+        if (!mbar_wait(&sm.o_empty[sb], ((i >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
+        bool ok = true;
+        for (int mb = 0; mb < MB; ++mb) {
+          const int seq0 = NS * i + 2 * mb, buf0 = seq0 % RING;
+          ok = mbar_wait(&sm.ring_full[buf0], (seq0 / RING) & 1, abort, a.status, kTimeoutMma) &&
+               mbar_wait(&sm.ring_full[buf0 + 1], ((seq0 + 1) / RING) & 1, abort, a.status, kTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             umma_f16_ss(tO + sb * kOCols + mb * kN,
                         desc_mn_sw128(ring_addr + buf0 * kSlabBytes + kk * 2048, kSlabBytes),
                         desc_sw128(p_addr + sb * (2 * kN * 128) + (kk >> 2) * (kN * 128) + (kk & 3) * 32), id_pv,
                         kk > 0 ? 1u : 0u);
-          umma_commit(&sm.chunk_empty[buf0]);
-          umma_commit(&sm.chunk_empty[buf0 + 1]);
+          umma_commit(&sm.ring_empty[buf0]);
+          umma_commit(&sm.ring_empty[buf0 + 1]);
         }
-        __syncwarp();
+        if (!ok) break;
+        umma_commit(&sm.o_full[sb]);
       }
-      if (!ok) break;
-      if (lane == 0) umma_commit(&sm.o_full[sb]);
-      __syncwarp();
     }
   } else if (warp < kSoftmaxWarps) {
     // ---------------------------------------------------------------- softmax + O accumulation
@@ -316,13 +391,17 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
       const int sb = i & 1;
       if (!mbar_wait(&sm.o_full[sb], (i >> 1) & 1, abort, a.status, kTimeoutConsumer)) return false;
       tc_fence_after();
+      uint32_t r[MB][RMAX];
 #pragma unroll
       for (int mb = 0; mb < MB; ++mb) {
-        uint32_t r[16];
-        tmem_ld16(tO + lane_base + sb * kOCols + mb * kN, r);
-        tmem_ld_wait();
+        if constexpr (RMAX == 8) tmem_ld8(tO + lane_base + sb * kOCols + mb * kN, r[mb]);
+        else tmem_ld16(tO + lane_base + sb * kOCols + mb * kN, r[mb]);
+      }
+      tmem_ld_wait();
 #pragma unroll
-        for (int n = 0; n < RMAX; ++n) acc[mb][n] = acc[mb][n] * alpha_prev[n] + __uint_as_float(r[n]);
+      for (int mb = 0; mb < MB; ++mb) {
+#pragma unroll
+        for (int n = 0; n < RMAX; ++n) acc[mb][n] = acc[mb][n] * alpha_prev[n] + __uint_as_float(r[mb][n]);
       }
       tc_fence_before();
       __syncwarp();
@@ -425,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -458,8 +537,11 @@ __global__ void gqa_combine_kernel(const GqaDecodeArgs a) {
 template <int FMT, int D, int RMAX>
 cudaError_t launch_t(const GqaDecodeArgs& a, cudaStream_t s) {
   constexpr int PB = part_bytes<FMT, D>();
-  constexpr int NST = (PB <= 20 * 1024) ? 6 : ((PB <= 32 * 1024) ? 4 : 2);
-  const int smem = 1024 + kRing * kSlabBytes + (D / 64) * kN * 128 + 4 * kN * 128 + NST * PB + sizeof(Smem);
+  constexpr int NST = raw_stages<FMT, D>();
+  constexpr int RING = ring_slabs<FMT, D>();
+  const int smem = 1024 + RING * kSlabBytes + (D / 64) * kN * 128 + 4 * kN * 128 + NST * PB + sizeof(Smem);
+  static_assert(1024 + RING * kSlabBytes + (D / 64) * kN * 128 + 4 * kN * 128 + NST * PB + sizeof(Smem) <= 232448,
+                "shared memory budget");
   auto kern = gqa_decode_kernel<FMT, D, RMAX>;
   IOB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   kern<<<a.B * a.Hk * a.num_splits, kThreads, smem, s>>>(a);

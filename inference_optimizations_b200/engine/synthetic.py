@@ -48,6 +48,8 @@ def synth_decode_sessions(engine, n: int, ctx: int, max_new: int, seed: int = 0)
         for k, rp in pg.items():
             if k.startswith("_"):
                 continue
+            if rp.window > 0:        # sliding-window kinds only ever hold the live window
+                rp.high = max(0, (ctx - rp.window) // rp.page)
             rp.ensure(ctx)
             rp.trim(ctx)
         r.prefilled = r.kv_len = ctx

@@ -24,8 +24,19 @@ def split_policy(batch_heads: int, max_ctx: int, window: int = 0, target_ctas: i
     per split.  Fixed per (batch, context bound) so a captured CUDA graph keeps a valid schedule."""
     span = min(max_ctx, window + TILE) if window > 0 else max_ctx
     tiles = max(1, (span + TILE - 1) // TILE + (1 if window > 0 else 0))
-    splits = max(1, min((target_ctas + batch_heads - 1) // batch_heads, tiles // min_tiles))
-    tps = (tiles + splits - 1) // splits
+    best, best_cost = 1, None
+    for s in range(1, 17):
+        if s > 1 and tiles // s < min_tiles:
+            break
+        ctas = batch_heads * s
+        waves = -(-ctas // NUM_SMS)
+        # relative time: whole waves over useful CTAs, plus a small per-split combine / setup cost
+        cost = waves * NUM_SMS / ctas * (1.0 + 0.03 * (s - 1)) * (1.0 + 4.0 * s / max(tiles, 1) * 0.05)
+        if ctas < target_ctas // 2:
+            cost *= 1.0 + (target_ctas // 2 - ctas) / target_ctas
+        if best_cost is None or cost < best_cost - 1e-9:
+            best, best_cost = s, cost
+    tps = (tiles + best - 1) // best
     splits = (tiles + tps - 1) // tps
     return splits, tps
 
