@@ -9,7 +9,7 @@
 //    2..16 rows still issues full-height UMMAs.  S^T = K Q^T lands in TMEM with lane = token, column = row.
 //  * K never touches shared memory after its raw bytes: the dequant warp that owns a token (TMEM lane) expands it
 //    to f16 and writes it straight into TMEM with tcgen05.st; QK is the A-from-TMEM UMMA form.  One handoff per tile.
-//  * O^T = V^T P^T with V (MN-major) read from f16 128-byte-swizzled slabs in a 6-deep shared-memory ring.
+//  * O^T = V^T P^T with V (MN-major) read from f16 128-byte-swizzled slabs in a shared-memory ring.
 //  * the pool is read by one bulk async copy per (page, kv head, K|V) into a raw ring; pool rows are stored with a
 //    16-byte chunk XOR swizzle so the dequant reads and slab writes are bank-conflict free.
 //  * skewed schedule: iteration j handles K of tile j, then V of tile j-1, so the softmax of tile j-1 overlaps the
@@ -33,6 +33,7 @@ constexpr int kProducerWarp = 12;
 constexpr int kMmaWarp = 13;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemK = 256;  // K tile: D/2 columns (two f16 per column)
+constexpr int kSParts = 4;        // independent partial S accumulators (QK k-steps interleaved across them)
 
 struct Smem {
   uint64_t raw_full[8], raw_empty[8];
@@ -44,6 +45,7 @@ struct Smem {
   int raw_valid[8];       // stage holds a real page (else the dequant writes zeros); published by the producer
   float red[kSoftmaxWarps][kN];
   float row_m[kN];
+  float q_scale[kN];      // E4M3 path: per-row Q scale (q = e4m3 * q_scale)
 };
 
 // must match kv_swizzle_byte() (kernels.h), which the pool writers use
@@ -72,14 +74,25 @@ template <int FMT, int D>
 __device__ __forceinline__ constexpr int part_bytes() {
   return FMT == kKvNvfp4 ? 64 * (D / 2 + D / 16) : (FMT == kKvFp8 ? 64 * D : 64 * D * 2);
 }
+// Shared memory split: V slab ring (4 x 16 KB) + Q + P, the rest is raw staging (bytes in flight are what bounds
+// a latency-limited stream; the L2 prefetch below covers the remaining distance).
+template <int FMT, int D>
+__device__ __host__ __forceinline__ constexpr int ring_slabs() { return part_bytes<FMT, D>() <= 20 * 1024 ? 6 : 4; }
+
+// Diagnostic timeline (CTA 0 only, when a.trace is set): event e of tile j at trace[e * 512 + j].
+enum TraceEv { kEvKDeqStart, kEvKDeqEnd, kEvVDeqStart, kEvVDeqEnd, kEvQkStart, kEvQkEnd, kEvPvStart, kEvPvEnd,
+               kEvSReady, kEvPReady, kEvODone, kEvProdK, kEvProdV, kEvKRaw, kEvStart, kEvEnd };
+__device__ __forceinline__ void trace_ev(long long* tr, int ev, int j) {
+  if (tr != nullptr && blockIdx.x == 0 && j < 512) tr[ev * 512 + j] = clock64();
+}
 template <int FMT, int D>
 __device__ __host__ __forceinline__ constexpr int raw_stages() {
-  return part_bytes<FMT, D>() <= 10 * 1024 ? 6 : (part_bytes<FMT, D>() <= 32 * 1024 ? 4 : 2);
+  // 224 KB minus ring, Q and P, in whole parts; at least 2 (a part is two pages resident together), at most 8
+  return (229376 - ring_slabs<FMT, D>() * 16384 - (D / 64) * 2048 - 8192) / part_bytes<FMT, D>() > 8   ? 8
+         : (229376 - ring_slabs<FMT, D>() * 16384 - (D / 64) * 2048 - 8192) / part_bytes<FMT, D>() < 2 ? 2
+         : (229376 - ring_slabs<FMT, D>() * 16384 - (D / 64) * 2048 - 8192) / part_bytes<FMT, D>();
 }
-template <int FMT, int D>
-__device__ __host__ __forceinline__ constexpr int ring_slabs() {
-  return raw_stages<FMT, D>() * part_bytes<FMT, D>() <= 100 * 1024 ? 6 : 4;
-}
+constexpr int kPrefetchParts = 4;   // L2 prefetch distance, in parts (2 tiles)
 
 // 16 code bytes (32 values) of an NVFP4 row at 16-byte chunk j -> 16 f16x2, scaled by the two block scales.
 __device__ __forceinline__ void nvfp4_chunk(const uint8_t* row, int pos, uint32_t s0, uint32_t s1, uint32_t* ow) {
@@ -206,10 +219,11 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t tS = tmem;            // 2 x 16 columns
-  const uint32_t tO = tmem + 32;       // 2 x kOCols columns
+  const uint32_t tS = tmem;            // 2 buffers x kSParts partial S accumulators x 16 columns
+  const uint32_t tO = tmem + 128;      // 2 x kOCols columns
   const uint32_t tK = tmem + kTmemK;   // D/2 columns
   volatile int* abort = &sm.abort;
+  if (threadIdx.x == 0) trace_ev(a.trace, kEvStart, 0);
 
   // Work order (every role walks it identically): iteration j = 0..ntiles handles the K part of tile j (when
   // j < ntiles), then the V part of tile j - 1 (when j >= 1).  A "part" is one (K | V, tile): 2 raw pages
@@ -220,17 +234,33 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
   if (warp == kProducerWarp) {
     if (lane == 0) {
       const uint8_t* pool = a.pool;
+      // part index -> (tile, which): 0 = K0; 2j-1 = K(j) (j < ntiles) or V(ntiles-1) (last); 2j = V(j-1)
+      auto prefetch_part = [&](int p) {
+        if (p >= 2 * ntiles) return;
+        int tile, which;
+        if (p == 0) { tile = 0; which = 0; }
+        else if (p & 1) { const int j = (p + 1) / 2; if (j < ntiles) { tile = j; which = 0; } else { tile = ntiles - 1; which = 1; } }
+        else { tile = p / 2 - 1; which = 1; }
+        for (int pg = 0; pg < 2; ++pg) {
+          const int pidx = (tile0 + tile) * 2 + pg;
+          const int phys = (pidx >= first_page && pidx < n_pages) ? pt[pidx] : -1;
+          if (phys >= 0) prefetch_l2(pool + (static_cast<size_t>(phys) * a.Hk + h) * (2 * PB) + which * PB, PB);
+        }
+      };
+      for (int p = 0; p < kPrefetchParts; ++p) prefetch_part(p);
       int issued = 0;
       for (int j = 0; j <= ntiles && !*abort; ++j) {
         for (int which = 0; which < 2; ++which) {
           const int tile = which == 0 ? j : j - 1;
           if (tile < 0 || tile >= ntiles) continue;
           const int pidx0 = part_index(j, which);
+          prefetch_part(pidx0 + kPrefetchParts);
           for (int pg = 0; pg < 2; ++pg) {
             const int seq = 2 * pidx0 + pg, st = seq % NST;
             if (*abort) break;
             if (!mbar_wait(&sm.raw_empty[st], ((seq / NST) & 1) ^ 1, abort, a.status, kTimeoutProducer)) break;
             issued = seq + 1;
+            if (pg == 0) trace_ev(a.trace, which == 0 ? kEvProdK : kEvProdV, tile);
             const int pidx = (tile0 + tile) * 2 + pg;
             const int phys = (pidx >= first_page && pidx < n_pages) ? pt[pidx] : -1;
             if (phys >= 0) {
@@ -266,8 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
         const int seq0 = 2 * p, st0 = seq0 % NST, st1 = (seq0 + 1) % NST;
         if (!mbar_wait(&sm.raw_full[st0], (seq0 / NST) & 1, abort, a.status, kTimeoutConsumer)) break;
         if (!mbar_wait(&sm.raw_full[st1], ((seq0 + 1) / NST) & 1, abort, a.status, kTimeoutConsumer)) break;
+        if (dw == 0 && lane == 0) trace_ev(a.trace, kEvKRaw, j);
         if (!mbar_wait(&sm.k_empty, (j & 1) ^ 1, abort, a.status, kTimeoutConsumer)) break;
         tc_fence_after();
+        if (dw == 0 && lane == 0) trace_ev(a.trace, kEvKDeqStart, j);
         const int st = kpg ? st1 : st0;
         const bool valid = sm.raw_valid[st] != 0;
         const uint8_t* part = raw + st * PB;
@@ -290,6 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
           mbar_arrive(&sm.k_full);
           mbar_arrive(&sm.raw_empty[st0]);
           mbar_arrive(&sm.raw_empty[st1]);
+          if (dw == 0) trace_ev(a.trace, kEvKDeqEnd, j);
         }
       }
       if (j == 0) continue;
@@ -301,6 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
         if (!mbar_wait(&sm.raw_full[st1], ((seq0 + 1) / NST) & 1, abort, a.status, kTimeoutConsumer)) break;
         const int st = vpg ? st1 : st0;
         const bool valid = sm.raw_valid[st] != 0;
+        if (dw == 0 && lane == 0) trace_ev(a.trace, kEvVDeqStart, i);
         bool ok = true;
         for (int c = 0; c < NS; ++c) {
           const int seq = NS * i + c, buf = seq % RING;
@@ -324,6 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
         if (!ok) break;
         __syncwarp();
         if (lane == 0) { mbar_arrive(&sm.raw_empty[st0]); mbar_arrive(&sm.raw_empty[st1]); }
+        if (dw == 0 && lane == 0) trace_ev(a.trace, kEvVDeqEnd, i);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -338,36 +373,48 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
           if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
           if (!mbar_wait(&sm.k_full, j & 1, abort, a.status, kTimeoutMma)) break;
           tc_fence_after();
+          trace_ev(a.trace, kEvQkStart, j);
+          // k-step s accumulates into partial s % kSParts: consecutive MMAs are independent (no accumulator chain)
 #pragma unroll 4
           for (int s = 0; s < D / 16; ++s)
-            umma_f16_ts(tS + sb * kN, tK + 8 * s, desc_sw128(q_addr + (s >> 2) * (kN * 128) + (s & 3) * 32), id_qk,
-                        s > 0 ? 1u : 0u);
+            umma_f16_ts(tS + sb * (kSParts * kN) + (s % kSParts) * kN, tK + 8 * s,
+                        desc_sw128(q_addr + (s >> 2) * (kN * 128) + (s & 3) * 32), id_qk, s >= kSParts ? 1u : 0u);
           umma_commit(&sm.s_full[sb]);
           umma_commit(&sm.k_empty);
+          trace_ev(a.trace, kEvQkEnd, j);
         }
         if (j == 0) continue;
         // PV(j - 1)
         const int i = j - 1, sb = i & 1;
         if (!mbar_wait(&sm.p_full[sb], (i >> 1) & 1, abort, a.status, kTimeoutMma)) break;
         if (!mbar_wait(&sm.o_empty[sb], ((i >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
+        trace_ev(a.trace, kEvPvStart, i);
         bool ok = true;
-        for (int mb = 0; mb < MB; ++mb) {
-          const int seq0 = NS * i + 2 * mb, buf0 = seq0 % RING;
-          ok = mbar_wait(&sm.ring_full[buf0], (seq0 / RING) & 1, abort, a.status, kTimeoutMma) &&
-               mbar_wait(&sm.ring_full[buf0 + 1], ((seq0 + 1) / RING) & 1, abort, a.status, kTimeoutMma);
+        // M blocks in groups of two (4 ring slabs), their MMAs interleaved so consecutive MMAs are independent
+        constexpr int GS = MB < 2 ? MB : 2;
+        for (int mg = 0; mg < MB; mg += GS) {
+          for (int q = 0; q < 2 * GS && ok; ++q) {
+            const int seq = NS * i + 2 * mg + q;
+            ok = mbar_wait(&sm.ring_full[seq % RING], (seq / RING) & 1, abort, a.status, kTimeoutMma);
+          }
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_f16_ss(tO + sb * kOCols + mb * kN,
-                        desc_mn_sw128(ring_addr + buf0 * kSlabBytes + kk * 2048, kSlabBytes),
-                        desc_sw128(p_addr + sb * (2 * kN * 128) + (kk >> 2) * (kN * 128) + (kk & 3) * 32), id_pv,
-                        kk > 0 ? 1u : 0u);
-          umma_commit(&sm.ring_empty[buf0]);
-          umma_commit(&sm.ring_empty[buf0 + 1]);
+          for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+            for (int g = 0; g < GS; ++g) {
+              const int buf0 = (NS * i + 2 * (mg + g)) % RING;
+              umma_f16_ss(tO + sb * kOCols + (mg + g) * kN,
+                          desc_mn_sw128(ring_addr + buf0 * kSlabBytes + kk * 2048, kSlabBytes),
+                          desc_sw128(p_addr + sb * (2 * kN * 128) + (kk >> 2) * (kN * 128) + (kk & 3) * 32), id_pv,
+                          kk > 0 ? 1u : 0u);
+            }
+          }
+          for (int q = 0; q < 2 * GS; ++q) umma_commit(&sm.ring_empty[(NS * i + 2 * mg + q) % RING]);
         }
         if (!ok) break;
         umma_commit(&sm.o_full[sb]);
+        trace_ev(a.trace, kEvPvEnd, i);
       }
     }
   } else if (warp < kSoftmaxWarps) {
@@ -406,15 +453,31 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.o_empty[sb]);
+      if (threadIdx.x == 0) trace_ev(a.trace, kEvODone, i);
       return true;
     };
     for (int j = 0; j < ntiles && ok; ++j) {
       const int sb = j & 1;
       if (!mbar_wait(&sm.s_full[sb], (j >> 1) & 1, abort, a.status, kTimeoutConsumer)) { ok = false; break; }
       tc_fence_after();
-      uint32_t sr[16];
-      tmem_ld16(tS + lane_base + sb * kN, sr);
-      tmem_ld_wait();
+      if (threadIdx.x == 0) trace_ev(a.trace, kEvSReady, j);
+      float sacc[RMAX];
+      {
+        uint32_t sr[kSParts][RMAX];
+#pragma unroll
+        for (int q = 0; q < kSParts; ++q) {
+          if constexpr (RMAX == 8) tmem_ld8(tS + lane_base + sb * (kSParts * kN) + q * kN, sr[q]);
+          else tmem_ld16(tS + lane_base + sb * (kSParts * kN) + q * kN, sr[q]);
+        }
+        tmem_ld_wait();
+#pragma unroll
+        for (int n = 0; n < RMAX; ++n) {
+          float v = 0.f;
+#pragma unroll
+          for (int q = 0; q < kSParts; ++q) v += __uint_as_float(sr[q][n]);
+          sacc[n] = v;
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.s_empty[sb]);
@@ -427,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
         const int qpos = q_first + t;
         const bool vis = n < R && tokpos <= qpos && tokpos >= kv_begin &&
                          (a.window <= 0 || qpos - tokpos < a.window);
-        s[n] = vis ? __uint_as_float(sr[n]) * scale_log2 : -INFINITY;
+        s[n] = vis ? sacc[n] * scale_log2 : -INFINITY;
         tmax[n] = warp_max(s[n]);
       }
       if (lane == 0) {
@@ -462,6 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.p_full[sb]);
+      if (threadIdx.x == 0) trace_ev(a.trace, kEvPReady, j);
       if (j > 0) ok = consume_o(j - 1);
 #pragma unroll
       for (int n = 0; n < RMAX; ++n) alpha_prev[n] = alpha[n];
@@ -502,7 +566,507 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace_ev(a.trace, kEvEnd, 0);
   if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+
+// =====================================================================================================================
+// E4M3-operand variant (kind::f8f6f4, K = 32 per UMMA).  A UMMA instruction costs about the same whatever its N, so a
+// decode tile with 2..16 query rows is bound by the instruction count: K = 32 halves it for both QK and PV.  K/V are
+// dequantized to E4M3 (E2M1 x block scale rounded once, the kv4mla "fp8" mode), Q gets a per-row scale, P is stored
+// as E4M3 x 256.  V slabs are one full 128-dim M block (128 B of E4M3 per token row).
+template <int FMT, int D>
+__device__ __host__ __forceinline__ constexpr int ring_f8() { return part_bytes<FMT, D>() <= 20 * 1024 ? 6 : 4; }
+template <int FMT, int D>
+__device__ __host__ __forceinline__ constexpr int raw_stages_f8() {
+  return (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096) / part_bytes<FMT, D>() > 8   ? 8
+         : (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096) / part_bytes<FMT, D>() < 2 ? 2
+         : (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096) / part_bytes<FMT, D>();
+}
+
+__device__ __forceinline__ uint32_t pack_e4m3x4(uint32_t h01, uint32_t h23) {
+  return static_cast<uint32_t>(f16x2_to_e4m3x2(h01)) | (static_cast<uint32_t>(f16x2_to_e4m3x2(h23)) << 16);
+}
+
+// 64 values of one token row (dims [d0, d0 + 64)) as E4M3 bytes packed four per word: 16 words.
+template <int FMT, int D>
+__device__ __forceinline__ void dequant_e4m3_64(const uint8_t* part, int r, int d0, uint32_t* out) {
+  if constexpr (FMT == kKvFp8) {
+    constexpr int RB = D, NCH = 8;
+    const uint8_t* row = part + r * RB;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint4 in = *reinterpret_cast<const uint4*>(row + pool_chunk_pos(d0 / 16 + k, r, NCH) * 16);
+      out[4 * k] = in.x; out[4 * k + 1] = in.y; out[4 * k + 2] = in.z; out[4 * k + 3] = in.w;
+    }
+  } else {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t h[16];
+      dequant_32<FMT, D>(part, r, d0 / 64, half, h);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) out[8 * half + i] = pack_e4m3x4(h[2 * i], h[2 * i + 1]);
+    }
+  }
+}
+
+// E4M3 kernel roles: warps 0-3 softmax, 4-11 K dequant, 12-19 V dequant, 20 producer, 21 UMMA issuer, 22-23 idle
+// (six full warpgroups so setmaxnreg can move registers: softmax 160, dequant 72, producer/issuer 32 per thread;
+// 128 x 160 + 512 x 72 + 128 x 32 = 61440 = 768 threads x 80 at launch).
+constexpr int kThreadsF8 = 768;
+constexpr int kProducerWarpF8 = 20;
+constexpr int kMmaWarpF8 = 21;
+
+// TMEM rows (columns) [0, RMAX) of this thread's lane.
+template <int RMAX>
+__device__ __forceinline__ void tmem_ld_rows(uint32_t taddr, uint32_t* r) {
+  if constexpr (RMAX == 2) tmem_ld2(taddr, r);
+  else if constexpr (RMAX == 4) tmem_ld4(taddr, r);
+  else if constexpr (RMAX == 8) tmem_ld8(taddr, r);
+  else tmem_ld16(taddr, r);
+}
+
+template <int FMT, int D, int RMAX>
+__global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaDecodeArgs a) {
+  constexpr int NQS = D / 128;                     // 128-dim slabs (Q rows, V M blocks)
+  constexpr int PB = part_bytes<FMT, D>();
+  constexpr int NST = raw_stages_f8<FMT, D>();
+  // K and V parts go through separate raw rings (page slots [0, NSTK) and [NSTK, NST)): each ring is consumed in
+  // order by one warp group, so no mbarrier is ever waited on more than one phase ahead.
+  constexpr int NSTK = NST / 2, NSTV = NST - NSTK;
+  static_assert(NSTK >= 2 && NSTV >= 2, "each raw ring holds at least one part (two pages)");
+  constexpr int RING = ring_f8<FMT, D>();
+  constexpr int MB = D / 128;
+  constexpr int kOCols = MB * kN;
+  constexpr float kPScale = 256.f;
+  static_assert(RMAX <= kN, "rows");
+  static_assert(RING >= MB, "all V blocks of a tile are multiplied together");
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = base;                                   // RING x 16 KB (V slabs, E4M3)
+  uint8_t* sq = ring + RING * kSlabBytes;                 // NQS x 2 KB (Q, E4M3)
+  uint8_t* sp = sq + NQS * kN * 128;                      // 2 x 2 KB (P, E4M3)
+  uint8_t* raw = sp + 2 * kN * 128;                       // NST x PB
+  Smem& sm = *reinterpret_cast<Smem*>(raw + NST * PB);
+
+  const int G = a.Hq / a.Hk;
+  const int R = a.n_q * G;
+  const int work = blockIdx.x;
+  const int split = work % a.num_splits;
+  const int bh = work / a.num_splits;
+  const int h = bh % a.Hk;
+  const int b = bh / a.Hk;
+  const int kv_len = a.kv_len[b];
+  const int q_first = kv_len - a.n_q;
+  const int kv_begin = a.window > 0 ? max(0, q_first - a.window + 1) : 0;
+  const int tile0 = kv_begin / kTileTok + split * a.tiles_per_split;
+  const int tile_end = min((kv_len + kTileTok - 1) / kTileTok, kv_begin / kTileTok + (split + 1) * a.tiles_per_split);
+  const int ntiles = tile_end - tile0;
+  const size_t part_out = (static_cast<size_t>(bh) * a.num_splits + split);
+  if (ntiles <= 0) {
+    if (a.num_splits > 1 && threadIdx.x < RMAX) a.lse_part[part_out * RMAX + threadIdx.x] = -INFINITY;
+    return;
+  }
+  const int first_page = kv_begin / a.page;
+  const int n_pages = (kv_len + a.page - 1) / a.page;
+  const int* pt = a.page_table + static_cast<size_t>(a.req_idx ? a.req_idx[b] : b) * a.pt_stride;
+  const int warp = warp_id(), lane = lane_id();
+  const __nv_bfloat16* qg = reinterpret_cast<const __nv_bfloat16*>(a.q);
+  auto qrow = [&](int row) {
+    const int t = row / G, g = row % G;
+    return qg + ((static_cast<size_t>(b) * a.n_q + t) * a.Hq + h * G + g) * D;
+  };
+
+  // ---- Q -> per-row scale, E4M3 slabs (rows >= R zero)
+  for (int row = warp; row < kN; row += kThreadsF8 / 32) {
+    float amax = 0.f;
+    if (row < R) {
+      const __nv_bfloat16* qr = qrow(row);
+      for (int d = lane; d < D; d += 32) amax = fmaxf(amax, fabsf(__bfloat162float(qr[d])));
+    }
+    amax = warp_max(amax);
+    if (lane == 0) sm.q_scale[row] = fmaxf(amax, 1e-20f) / 448.f;
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NST; ++i) { mbar_init(&sm.raw_full[i], 1); mbar_init(&sm.raw_empty[i], kDequantWarps); }
+    for (int i = 0; i < RING; ++i) { mbar_init(&sm.ring_full[i], kDequantWarps); mbar_init(&sm.ring_empty[i], 1); }
+    mbar_init(&sm.k_full, kDequantWarps);
+    mbar_init(&sm.k_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.s_full[i], 1); mbar_init(&sm.s_empty[i], kSoftmaxWarps);
+      mbar_init(&sm.p_full[i], kSoftmaxWarps); mbar_init(&sm.o_full[i], 1); mbar_init(&sm.o_empty[i], kSoftmaxWarps);
+    }
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarpF8) { tmem_alloc(&sm.tmem_base, kTmemCols); tmem_relinquish(); }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < kN * NQS * 8; idx += kThreadsF8) {
+    const int row = idx / (NQS * 8), rem = idx % (NQS * 8), c = rem / 8, ch = rem % 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < R) {
+      const float inv = 1.f / sm.q_scale[row];
+      const uint4* src = reinterpret_cast<const uint4*>(qrow(row) + c * 128 + ch * 16);
+      const uint4 i0 = src[0], i1 = src[1];
+      const __nv_bfloat16* e0 = reinterpret_cast<const __nv_bfloat16*>(&i0);
+      const __nv_bfloat16* e1 = reinterpret_cast<const __nv_bfloat16*>(&i1);
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const __nv_bfloat16* e = k < 2 ? e0 : e1;
+        const int o = (k & 1) * 4;
+        w[k] = static_cast<uint32_t>(f32x2_to_e4m3x2(__bfloat162float(e[o]) * inv, __bfloat162float(e[o + 1]) * inv)) |
+               (static_cast<uint32_t>(f32x2_to_e4m3x2(__bfloat162float(e[o + 2]) * inv,
+                                                       __bfloat162float(e[o + 3]) * inv)) << 16);
+      }
+      v = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    *reinterpret_cast<uint4*>(sq + c * (kN * 128) + sw128_chunk(row, ch)) = v;
+  }
+  for (int idx = threadIdx.x; idx < 2 * kN * 128 / 16; idx += kThreadsF8)
+    reinterpret_cast<uint4*>(sp)[idx] = make_uint4(0, 0, 0, 0);
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  const uint32_t tS = tmem;
+  const uint32_t tO = tmem + 128;
+  const uint32_t tK = tmem + kTmemK;   // D/4 columns (four E4M3 per column)
+  volatile int* abort = &sm.abort;
+  if (threadIdx.x == 0) trace_ev(a.trace, kEvStart, 0);
+
+  auto parts_before = [&](int j) { return min(j, ntiles) + max(0, j - 1); };
+  auto part_index = [&](int j, int which) { return parts_before(j) + ((which == 1 && j < ntiles) ? 1 : 0); };
+
+  if (warp < kSoftmaxWarps) {
+    regs_inc<160>();
+    const float base_scale = a.sm_scale * a.k_scale * 1.4426950408889634f;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+    float acc[MB][RMAX];
+    float lpart[RMAX];
+    float alpha_prev[RMAX];
+    float rs[RMAX];
+#pragma unroll
+    for (int n = 0; n < RMAX; ++n) {
+      lpart[n] = 0.f;
+      alpha_prev[n] = 1.f;
+      rs[n] = base_scale * sm.q_scale[n];
+#pragma unroll
+      for (int mb = 0; mb < MB; ++mb) acc[mb][n] = 0.f;
+    }
+    if (threadIdx.x < kN) sm.row_m[threadIdx.x] = -INFINITY;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    bool ok = true;
+    auto consume_o = [&](int i) -> bool {
+      const int sb = i & 1;
+      if (!mbar_wait(&sm.o_full[sb], (i >> 1) & 1, abort, a.status, kTimeoutConsumer)) return false;
+      tc_fence_after();
+      uint32_t r[MB][RMAX];
+#pragma unroll
+      for (int mb = 0; mb < MB; ++mb) tmem_ld_rows<RMAX>(tO + lane_base + sb * kOCols + mb * kN, r[mb]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int mb = 0; mb < MB; ++mb) {
+#pragma unroll
+        for (int n = 0; n < RMAX; ++n) acc[mb][n] = acc[mb][n] * alpha_prev[n] + __uint_as_float(r[mb][n]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.o_empty[sb]);
+      if (threadIdx.x == 0) trace_ev(a.trace, kEvODone, i);
+      return true;
+    };
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&sm.s_full[sb], (j >> 1) & 1, abort, a.status, kTimeoutConsumer)) { ok = false; break; }
+      tc_fence_after();
+      if (threadIdx.x == 0) trace_ev(a.trace, kEvSReady, j);
+      float sacc[RMAX];
+      {
+        uint32_t sr[kSParts][RMAX];
+#pragma unroll
+        for (int q = 0; q < kSParts; ++q) tmem_ld_rows<RMAX>(tS + lane_base + sb * (kSParts * kN) + q * kN, sr[q]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int n = 0; n < RMAX; ++n) {
+          float v = 0.f;
+#pragma unroll
+          for (int q = 0; q < kSParts; ++q) v += __uint_as_float(sr[q][n]);
+          sacc[n] = v;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.s_empty[sb]);
+      const int tokpos = (tile0 + j) * kTileTok + 32 * warp + lane;
+      float s[RMAX];
+      float tmax[RMAX];
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n) {
+        const int t = n / G;
+        const int qpos = q_first + t;
+        const bool vis = n < R && tokpos <= qpos && tokpos >= kv_begin && (a.window <= 0 || qpos - tokpos < a.window);
+        s[n] = vis ? sacc[n] * rs[n] : -INFINITY;
+        tmax[n] = warp_max(s[n]);
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int n = 0; n < RMAX; ++n) sm.red[warp][n] = tmax[n];
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      float mnew[RMAX], alpha[RMAX];
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n) {
+        const float mt = fmaxf(fmaxf(sm.red[0][n], sm.red[1][n]), fmaxf(sm.red[2][n], sm.red[3][n]));
+        const float mo = sm.row_m[n];
+        mnew[n] = fmaxf(mo, mt);
+        alpha[n] = (mnew[n] == -INFINITY) ? 1.f : exp2f(mo - mnew[n]);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n)
+        if (threadIdx.x == n) sm.row_m[n] = mnew[n];
+      // P (E4M3 x 256) into the B operand: row n, token k, SW128 K-major (one 128-token slab)
+      uint8_t* pbuf = sp + sb * (kN * 128);
+      const int k = 32 * warp + lane;
+#pragma unroll
+      for (int n = 0; n < RMAX; n += 2) {
+        float p0 = 0.f, p1 = 0.f;
+        p0 = (s[n] == -INFINITY) ? 0.f : exp2f(s[n] - mnew[n]);
+        lpart[n] = lpart[n] * alpha[n] + p0;
+        if (n + 1 < RMAX) {
+          p1 = (s[n + 1] == -INFINITY) ? 0.f : exp2f(s[n + 1] - mnew[n + 1]);
+          lpart[n + 1] = lpart[n + 1] * alpha[n + 1] + p1;
+        }
+        const uint16_t e = f32x2_to_e4m3x2(p0 * kPScale, p1 * kPScale);
+        pbuf[n * 128 + (((k >> 4) ^ (n & 7)) << 4) + (k & 15)] = static_cast<uint8_t>(e & 0xFF);
+        pbuf[(n + 1) * 128 + (((k >> 4) ^ ((n + 1) & 7)) << 4) + (k & 15)] = static_cast<uint8_t>(e >> 8);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.p_full[sb]);
+      if (threadIdx.x == 0) trace_ev(a.trace, kEvPReady, j);
+      if (j > 0) ok = consume_o(j - 1);
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n) alpha_prev[n] = alpha[n];
+    }
+    if (ok) ok = consume_o(ntiles - 1);
+    float l[RMAX];
+#pragma unroll
+    for (int n = 0; n < RMAX; ++n) l[n] = warp_sum(lpart[n]);
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (lane == 0) {
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n) sm.red[warp][n] = l[n];
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+#pragma unroll
+    for (int n = 0; n < RMAX; ++n) l[n] = sm.red[0][n] + sm.red[1][n] + sm.red[2][n] + sm.red[3][n];
+    if (ok) {
+#pragma unroll
+      for (int n = 0; n < RMAX; ++n) {
+        if (n >= R) break;
+        const int t = n / G, g = n % G;
+        const float inv = l[n] > 0.f ? a.v_scale / (l[n] * kPScale) : 0.f;
+        if (a.num_splits == 1) {
+          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) +
+                             ((static_cast<size_t>(b) * a.n_q + t) * a.Hq + h * G + g) * D;
+#pragma unroll
+          for (int mb = 0; mb < MB; ++mb) o[mb * 128 + 32 * warp + lane] = __float2bfloat16(acc[mb][n] * inv);
+        } else {
+          float* o = a.o_part + (part_out * RMAX + n) * D;
+#pragma unroll
+          for (int mb = 0; mb < MB; ++mb) o[mb * 128 + 32 * warp + lane] = acc[mb][n] * inv;
+          if (warp == 0 && lane == 0)
+            a.lse_part[part_out * RMAX + n] = l[n] > 0.f ? sm.row_m[n] + log2f(l[n]) : -INFINITY;
+        }
+      }
+    }
+    } else if (warp < kSoftmaxWarps + kDequantWarps) {
+    regs_dec<72>();
+    // ---- K warps: K(j) -> TMEM (E4M3); thread = TMEM lane = token, warps dw and dw + 4 split the dims
+    const int dw = warp - kSoftmaxWarps;
+    const int kq = warp & 3, ktok = 32 * kq + lane, kpg = ktok / 64, kr = ktok % 64;
+    const int kdim0 = (dw >> 2) * (D / 2);
+    const uint32_t k_lane = static_cast<uint32_t>(32 * kq) << 16;
+    for (int j = 0; j < ntiles; ++j) {
+      const int seq0 = 2 * j, st0 = seq0 % NSTK, st1 = (seq0 + 1) % NSTK;
+      if (!mbar_wait(&sm.raw_full[st0], (seq0 / NSTK) & 1, abort, a.status, kTimeoutConsumer)) break;
+      if (!mbar_wait(&sm.raw_full[st1], ((seq0 + 1) / NSTK) & 1, abort, a.status, kTimeoutConsumer)) break;
+      if (!mbar_wait(&sm.k_empty, (j & 1) ^ 1, abort, a.status, kTimeoutConsumer)) break;
+      tc_fence_after();
+      if (dw == 0 && lane == 0) trace_ev(a.trace, kEvKDeqStart, j);
+      const int st = kpg ? st1 : st0;
+      const bool valid = sm.raw_valid[st] != 0;
+      const uint8_t* part = raw + st * PB;
+#pragma unroll 1
+      for (int d0 = kdim0; d0 < kdim0 + D / 2; d0 += 64) {
+        uint32_t v[16];
+        if (valid) dequant_e4m3_64<FMT, D>(part, kr, d0, v);
+        else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0;
+        }
+        tmem_st16(tK + k_lane + d0 / 4, v);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.k_full);
+        mbar_arrive(&sm.raw_empty[st0]);
+        mbar_arrive(&sm.raw_empty[st1]);
+        if (dw == 0) trace_ev(a.trace, kEvKDeqEnd, j);
+      }
+    }
+  } else if (warp < kSoftmaxWarps + 2 * kDequantWarps) {
+    regs_dec<72>();
+    // ---- V warps: V(i) -> ring, one 128-dim E4M3 slab per M block; warp covers 16 tokens x two 64-dim halves
+    const int dw = warp - kSoftmaxWarps - kDequantWarps;
+    const int vtok = 16 * dw + (lane & 7) + 8 * (lane >> 4);
+    const int vhalf = (lane >> 3) & 1;
+    const int vpg = vtok / 64, vr = vtok % 64;
+    for (int i = 0; i < ntiles; ++i) {
+      const int seq0 = 2 * i, st0 = NSTK + seq0 % NSTV, st1 = NSTK + (seq0 + 1) % NSTV;
+      if (!mbar_wait(&sm.raw_full[st0], (seq0 / NSTV) & 1, abort, a.status, kTimeoutConsumer)) break;
+      if (!mbar_wait(&sm.raw_full[st1], ((seq0 + 1) / NSTV) & 1, abort, a.status, kTimeoutConsumer)) break;
+      const int st = vpg ? st1 : st0;
+      const bool valid = sm.raw_valid[st] != 0;
+      if (dw == 0 && lane == 0) trace_ev(a.trace, kEvVDeqStart, i);
+      bool ok = true;
+      for (int mb = 0; mb < MB; ++mb) {
+        const int seq = MB * i + mb, buf = seq % RING;
+        if (!(ok = mbar_wait(&sm.ring_empty[buf], ((seq / RING) & 1) ^ 1, abort, a.status, kTimeoutConsumer)))
+          break;
+        uint32_t o[16];
+        if (valid) dequant_e4m3_64<FMT, D>(raw + st * PB, vr, 128 * mb + 64 * vhalf, o);
+        else {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) o[k] = 0;
+        }
+        uint8_t* slab = ring + buf * kSlabBytes;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(slab + sw128_chunk(vtok, vhalf * 4 + q)) =
+              make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.ring_full[buf]);
+      }
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) { mbar_arrive(&sm.raw_empty[st0]); mbar_arrive(&sm.raw_empty[st1]); }
+      if (dw == 0 && lane == 0) trace_ev(a.trace, kEvVDeqEnd, i);
+    }
+  } else {
+    regs_dec<32>();
+    if (warp == kProducerWarpF8) {
+    if (lane == 0) {
+      const uint8_t* pool = a.pool;
+      auto prefetch_part = [&](int p) {
+        if (p >= 2 * ntiles) return;
+        int tile, which;
+        if (p == 0) { tile = 0; which = 0; }
+        else if (p & 1) { const int j = (p + 1) / 2; if (j < ntiles) { tile = j; which = 0; } else { tile = ntiles - 1; which = 1; } }
+        else { tile = p / 2 - 1; which = 1; }
+        for (int pg = 0; pg < 2; ++pg) {
+          const int pidx = (tile0 + tile) * 2 + pg;
+          const int phys = (pidx >= first_page && pidx < n_pages) ? pt[pidx] : -1;
+          if (phys >= 0) prefetch_l2(pool + (static_cast<size_t>(phys) * a.Hk + h) * (2 * PB) + which * PB, PB);
+        }
+      };
+      for (int p = 0; p < kPrefetchParts; ++p) prefetch_part(p);
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j <= ntiles && !*abort; ++j) {
+        for (int which = 0; which < 2; ++which) {
+          const int tile = which == 0 ? j : j - 1;
+          if (tile < 0 || tile >= ntiles) continue;
+          const int pidx0 = part_index(j, which);
+          prefetch_part(pidx0 + kPrefetchParts);
+          for (int pg = 0; pg < 2; ++pg) {
+            const int rs = 2 * tile + pg;                       // sequence within this part's ring
+            const int nst = which == 0 ? NSTK : NSTV;
+            const int st = (which == 0 ? 0 : NSTK) + rs % nst;
+            if (*abort) break;
+            if (!mbar_wait(&sm.raw_empty[st], ((rs / nst) & 1) ^ 1, abort, a.status, kTimeoutProducer)) break;
+            (which == 0 ? issued_k : issued_v) = rs + 1;
+            const int pidx = (tile0 + tile) * 2 + pg;
+            const int phys = (pidx >= first_page && pidx < n_pages) ? pt[pidx] : -1;
+            if (phys >= 0) {
+              sm.raw_valid[st] = 1;
+              mbar_expect_tx(&sm.raw_full[st], PB);
+              bulk_g2s(raw + st * PB, pool + (static_cast<size_t>(phys) * a.Hk + h) * (2 * PB) + which * PB, PB,
+                       &sm.raw_full[st]);
+            } else {
+              sm.raw_valid[st] = 0;
+              mbar_arrive(&sm.raw_full[st]);
+            }
+          }
+        }
+      }
+      for (int rs = max(0, issued_k - NSTK); rs < issued_k; ++rs)
+        mbar_wait(&sm.raw_full[rs % NSTK], (rs / NSTK) & 1, nullptr, a.status, kTimeoutProducer);
+      for (int rs = max(0, issued_v - NSTV); rs < issued_v; ++rs)
+        mbar_wait(&sm.raw_full[NSTK + rs % NSTV], (rs / NSTV) & 1, nullptr, a.status, kTimeoutProducer);
+    }
+    } else if (warp == kMmaWarpF8) {
+    if (lane == 0) {
+      const uint32_t id_qk = idesc_dense(0, 0, 128, kN);                 // E4M3 x E4M3, K-major both
+      const uint32_t id_pv = idesc_dense(0, 0, 128, kN) | (1u << 15);   // A (V^T) MN-major
+      const uint32_t ring_addr = smem_u32(ring), q_addr = smem_u32(sq), p_addr = smem_u32(sp);
+      for (int j = 0; j <= ntiles; ++j) {
+        if (j < ntiles) {
+          const int sb = j & 1;
+          if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
+          if (!mbar_wait(&sm.k_full, j & 1, abort, a.status, kTimeoutMma)) break;
+          tc_fence_after();
+          trace_ev(a.trace, kEvQkStart, j);
+#pragma unroll 4
+          for (int s = 0; s < D / 32; ++s)
+            umma_f8_ts(tS + sb * (kSParts * kN) + (s % kSParts) * kN, tK + 8 * s,
+                       desc_sw128(q_addr + (s >> 2) * (kN * 128) + (s & 3) * 32), id_qk, s >= kSParts ? 1u : 0u);
+          umma_commit(&sm.s_full[sb]);
+          umma_commit(&sm.k_empty);
+          trace_ev(a.trace, kEvQkEnd, j);
+        }
+        if (j == 0) continue;
+        const int i = j - 1, sb = i & 1;
+        if (!mbar_wait(&sm.p_full[sb], (i >> 1) & 1, abort, a.status, kTimeoutMma)) break;
+        if (!mbar_wait(&sm.o_empty[sb], ((i >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
+        trace_ev(a.trace, kEvPvStart, i);
+        bool ok = true;
+        for (int mb = 0; mb < MB && ok; ++mb) {
+          const int seq = MB * i + mb;
+          ok = mbar_wait(&sm.ring_full[seq % RING], (seq / RING) & 1, abort, a.status, kTimeoutMma);
+        }
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+          for (int mb = 0; mb < MB; ++mb) {
+            const int buf = (MB * i + mb) % RING;
+            umma_f8_ss(tO + sb * kOCols + mb * kN, desc_mn_sw128(ring_addr + buf * kSlabBytes + kk * 4096, kSlabBytes),
+                       desc_sw128(p_addr + sb * (kN * 128) + kk * 32), id_pv, kk > 0 ? 1u : 0u);
+          }
+        }
+        for (int mb = 0; mb < MB; ++mb) umma_commit(&sm.ring_empty[(MB * i + mb) % RING]);
+        umma_commit(&sm.o_full[sb]);
+        trace_ev(a.trace, kEvPvEnd, i);
+      }
+    }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) trace_ev(a.trace, kEvEnd, 0);
+  if (warp == kMmaWarpF8) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -542,9 +1106,24 @@ cudaError_t launch_t(const GqaDecodeArgs& a, cudaStream_t s) {
   const int smem = 1024 + RING * kSlabBytes + (D / 64) * kN * 128 + 4 * kN * 128 + NST * PB + sizeof(Smem);
   static_assert(1024 + RING * kSlabBytes + (D / 64) * kN * 128 + 4 * kN * 128 + NST * PB + sizeof(Smem) <= 232448,
                 "shared memory budget");
-  auto kern = gqa_decode_kernel<FMT, D, RMAX>;
-  IOB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  kern<<<a.B * a.Hk * a.num_splits, kThreads, smem, s>>>(a);
+  bool launched = false;
+  if constexpr (FMT != kKvBf16) {
+    if (!a.exact) {
+    constexpr int NST8 = raw_stages_f8<FMT, D>();
+    constexpr int RING8 = ring_f8<FMT, D>();
+    constexpr int smem8 = 1024 + RING8 * kSlabBytes + (D / 128) * kN * 128 + 2 * kN * 128 + NST8 * PB + sizeof(Smem);
+    static_assert(smem8 <= 232448, "shared memory budget (E4M3 path)");
+    auto kern8 = gqa_decode_f8_kernel<FMT, D, RMAX>;
+    IOB_CUDA_CHECK(cudaFuncSetAttribute(kern8, cudaFuncAttributeMaxDynamicSharedMemorySize, smem8));
+    kern8<<<a.B * a.Hk * a.num_splits, kThreadsF8, smem8, s>>>(a);
+    launched = true;
+    }
+  }
+  if (!launched) {
+    auto kern = gqa_decode_kernel<FMT, D, RMAX>;
+    IOB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<a.B * a.Hk * a.num_splits, kThreads, smem, s>>>(a);
+  }
   IOB_CUDA_CHECK(cudaGetLastError());
   if (a.num_splits > 1) {
     gqa_combine_kernel<RMAX><<<a.B * a.Hk * RMAX, 128, 0, s>>>(a);
@@ -556,6 +1135,7 @@ cudaError_t launch_t(const GqaDecodeArgs& a, cudaStream_t s) {
 template <int FMT, int D>
 cudaError_t launch_r(const GqaDecodeArgs& a, cudaStream_t s) {
   const int R = a.n_q * (a.Hq / a.Hk);
+  if (R <= 2 && FMT != kKvBf16 && !a.exact) return launch_t<FMT, D, 2>(a, s);
   if (R <= 8) return launch_t<FMT, D, 8>(a, s);
   if (R <= 16) return launch_t<FMT, D, 16>(a, s);
   return cudaErrorInvalidValue;

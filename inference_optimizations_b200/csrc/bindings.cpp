@@ -135,7 +135,8 @@ void index_key_write(const at::Tensor& k, const at::Tensor& slot, at::Tensor poo
 void gqa_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& page_table,
                 c10::optional<at::Tensor> req_idx, const at::Tensor& kv_len, at::Tensor out, at::Tensor o_part, at::Tensor lse_part, at::Tensor status, int64_t n_q, int64_t Hk,
                 int64_t page, int64_t window, int64_t fmt, int64_t tiles_per_split, int64_t num_splits,
-                double sm_scale, double k_scale, double v_scale) {
+                double sm_scale, double k_scale, double v_scale, c10::optional<at::Tensor> trace,
+                int64_t exact) {
   req(q, at::kBFloat16, "q");
   req(pool, at::kByte, "pool");
   req(page_table, at::kInt, "page_table");
@@ -170,6 +171,8 @@ void gqa_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& p
   a.sm_scale = sm_scale;
   a.k_scale = k_scale;
   a.v_scale = v_scale;
+  if (trace.has_value()) { req(*trace, at::kLong, "trace"); a.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>()); }
+  a.exact = static_cast<int>(exact);
   TORCH_CHECK(q.size(0) == a.B * n_q, "q rows");
   const int rmax = a.n_q * (a.Hq / a.Hk) <= 8 ? 8 : 16;
   if (num_splits > 1)
@@ -189,6 +192,13 @@ void umma_gemm_test(const at::Tensor& A, const at::Tensor& B, at::Tensor C) {
                                     A.size(1), stream()));
 }
 
+void umma_rate_test(int64_t n, int64_t count, int64_t nacc, int64_t ts, at::Tensor out) {
+  req(out, at::kLong, "out");
+  const at::cuda::CUDAGuard g(out.device());
+  CHECK_CUDA_OK(iob::umma_rate_test(n, count, nacc, ts, reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
+                                    stream()));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -201,4 +211,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("index_key_write", &index_key_write);
   m.def("gqa_decode", &gqa_decode);
   m.def("umma_gemm_test", &umma_gemm_test);
+  m.def("umma_rate_test", &umma_rate_test);
 }

@@ -83,10 +83,13 @@ struct GqaDecodeArgs {
   int B, n_q, Hq, Hk, D, pt_stride, page, window, fmt;
   int tiles_per_split, num_splits;
   float sm_scale, k_scale, v_scale;
+  long long* trace;        // optional [16 events x 512 tiles] clock64 timeline of CTA 0 (diagnostics), else null
+  int exact;               // 1: f16 operands (exact dequant); 0: E4M3 operands (K = 32 UMMAs) for NVFP4 / FP8 pools
 };
 cudaError_t gqa_decode(const GqaDecodeArgs& a, cudaStream_t s);
 
 // ---- primitive check (umma_test.cu): C[M, N] fp32 = A[M, K] * B[N, K]^T, bf16 inputs, one CTA per 128 rows.
 cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, cudaStream_t s);
+cudaError_t umma_rate_test(int n, int count, int nacc, int ts, long long* out, cudaStream_t s);
 
 }  // namespace iob

@@ -86,3 +86,73 @@ cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N,
 }
 
 }  // namespace iob
+
+// ---------------------------------------------------------------------------------------------------------------
+// Issue-rate probe (diagnostic): one thread per issuing warp issues `count` UMMAs back to back.
+// variant: 0 kind::f16 SS M128; 1 kind::f16 TS M128; 2 SS without a memory clobber; 3 kind::f8f6f4 SS M128 (K=32);
+//          4 kind::f16 .ws SS M128 (N >= 64); 5 kind::f16 SS M64; 6 as 0 with two issuing warps (own accumulators).
+// out[0] = cycles issuing, out[1] = cycles to completion of all.  Operands are zero-filled.
+namespace iob {
+namespace {
+__device__ __forceinline__ void umma_f16_ss_nc(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+               "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+               ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_f16_ws_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+               "tcgen05.mma.ws.cta_group::1.kind::f16 [%0], %1, %2, %3, p, 0;\n\t}\n"
+               ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__global__ void __launch_bounds__(128) umma_rate_kernel(int n, int count, int nacc, int variant, long long* out) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar[2];
+  __shared__ uint32_t tmem_base;
+  for (int i = threadIdx.x; i < (16384 + 32768) / 16; i += blockDim.x) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  if (warp_id() == 0) { tmem_alloc(&tmem_base, 512); tmem_relinquish(); }
+  if (threadIdx.x == 0) { mbar_init(&bar[0], 1); mbar_init(&bar[1], 1); fence_mbar_init(); }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t t = tmem_base;
+  const int issuers = variant == 6 ? 2 : 1;
+  if (lane_id() == 0 && warp_id() < issuers) {
+    const int m = variant == 5 ? 64 : 128;
+    const uint32_t idesc = variant == 3 ? idesc_dense(0, 0, m, n) : idesc_dense(1, 1, m, n);
+    const uint64_t a = desc_sw128(smem_u32(smem)), b = desc_sw128(smem_u32(smem + 16384));
+    const uint32_t dbase = t + warp_id() * 128;
+    const long long c0 = clock64();
+    for (int i = 0; i < count; ++i) {
+      const uint32_t d = dbase + (i % nacc) * n;
+      switch (variant) {
+        case 1: umma_f16_ts(d, t + 256, b, idesc, 1u); break;
+        case 2: umma_f16_ss_nc(d, a, b, idesc, 1u); break;
+        case 3: umma_f8_ss(d, a, b, idesc, 1u); break;
+        case 4: umma_f16_ws_ss(d, a, b, idesc, 1u); break;
+        default: umma_f16_ss(d, a, b, idesc, 1u); break;
+      }
+    }
+    const long long c1 = clock64();
+    umma_commit(&bar[warp_id()]);
+    mbar_wait(&bar[warp_id()], 0, nullptr, nullptr, 0);
+    const long long c2 = clock64();
+    if (threadIdx.x == 0) {
+      out[0] = c1 - c0;
+      out[1] = c2 - c0;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp_id() == 0) { tc_fence_after(); tmem_dealloc(t, 512); }
+}
+}  // namespace
+
+cudaError_t umma_rate_test(int n, int count, int nacc, int variant, long long* out, cudaStream_t s) {
+  const int smem = 1024 + 16384 + 256 * 128;
+  IOB_CUDA_CHECK(cudaFuncSetAttribute(umma_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  umma_rate_kernel<<<1, 128, smem, s>>>(n, count, nacc, variant, out);
+  return cudaGetLastError();
+}
+}  // namespace iob

@@ -25,15 +25,14 @@ def split_policy(batch_heads: int, max_ctx: int, window: int = 0, target_ctas: i
     span = min(max_ctx, window + TILE) if window > 0 else max_ctx
     tiles = max(1, (span + TILE - 1) // TILE + (1 if window > 0 else 0))
     best, best_cost = 1, None
+    overhead_tiles = 3.0          # per-CTA prologue / pipeline fill / epilogue, in tile units (measured timeline)
     for s in range(1, 17):
         if s > 1 and tiles // s < min_tiles:
             break
         ctas = batch_heads * s
-        waves = -(-ctas // NUM_SMS)
-        # relative time: whole waves over useful CTAs, plus a small per-split combine / setup cost
-        cost = waves * NUM_SMS / ctas * (1.0 + 0.03 * (s - 1)) * (1.0 + 4.0 * s / max(tiles, 1) * 0.05)
-        if ctas < target_ctas // 2:
-            cost *= 1.0 + (target_ctas // 2 - ctas) / target_ctas
+        waves = -(-ctas // NUM_SMS)            # one CTA per SM at a time
+        tps = -(-tiles // s)
+        cost = waves * (tps + overhead_tiles) + (0.5 if s > 1 else 0.0)   # + split combine
         if best_cost is None or cost < best_cost - 1e-9:
             best, best_cost = s, cost
     tps = (tiles + best - 1) // best
@@ -59,9 +58,11 @@ def gqa_decode(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor, kv
                hk: int, fmt: int, sm_scale: float, window: int = 0, k_scale: float = 1.0, v_scale: float = 1.0,
                splits: Optional[tuple[int, int]] = None, ws: Optional[DecodeWorkspace] = None,
                max_ctx: Optional[int] = None, out: Optional[torch.Tensor] = None,
-               req_idx: Optional[torch.Tensor] = None) -> torch.Tensor:
+               req_idx: Optional[torch.Tensor] = None, trace: Optional[torch.Tensor] = None,
+               exact: bool = False) -> torch.Tensor:
     """q bf16 [B * n_q, Hq, D] -> out bf16 [B * n_q, Hq, D].  Batch entry b uses page-table row req_idx[b]
-    (default b)."""
+    (default b).  NVFP4 / FP8 pools run E4M3 tensor-core operands unless `exact` (f16 operands, exact dequant);
+    bf16 pools always run f16."""
     b = kv_len.shape[0]
     d = q.shape[-1]
     if out is None:
@@ -79,7 +80,7 @@ def gqa_decode(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor, kv
     if ws is None:
         ws = DecodeWorkspace.allocate(b, hk, ns, d, device=q.device)
     ext().gqa_decode(q, pool, page_table, req_idx, kv_len, out, ws.o_part, ws.lse_part, ws.status, n_q, hk, 64, window, fmt,
-                     tps, ns, sm_scale, k_scale, v_scale)
+                     tps, ns, sm_scale, k_scale, v_scale, trace, int(exact))
     return out
 
 

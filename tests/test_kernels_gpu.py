@@ -117,9 +117,10 @@ def _build_pool(cuda, fmt, d, hk, lens, scale=(1.0, 1.0), seed=0):
     return pool.to(cuda), pt.to(cuda), torch.tensor(lens, dtype=torch.int32, device=cuda)
 
 
+@pytest.mark.parametrize("exact", [True, False])
 @pytest.mark.parametrize("fmt", [K.FMT_NVFP4, K.FMT_FP8, K.FMT_BF16])
 @pytest.mark.parametrize("d,window,n_q", [(512, 0, 1), (256, 96, 1), (512, 0, 4), (256, 0, 4), (128, 0, 1)])
-def test_gqa_decode(cuda, fmt, d, window, n_q):
+def test_gqa_decode(cuda, fmt, d, window, n_q, exact):
     hq, hk = 4, 2
     lens = [300, 1, 129, 700][: 4] if n_q == 1 else [300, 4, 129, 700]
     scale = (0.5, 0.25) if fmt == K.FMT_FP8 else (1.0, 1.0)
@@ -127,11 +128,13 @@ def test_gqa_decode(cuda, fmt, d, window, n_q):
     q = torch.randn(len(lens) * n_q, hq, d, device=cuda).to(torch.bfloat16)
     sm = 1.0 / math.sqrt(d)
     ref = A.gqa_decode_ref(q.cpu(), pool.cpu(), pt.cpu(), kv_len.cpu(), n_q, hk, fmt, sm, window, *scale)
+    # E4M3 operands round K/V/Q/P once each (relative 2^-4): compare against the output's scale
+    tol = 2e-2 if (exact or fmt == K.FMT_BF16) else 0.06 * max(1.0, ref.abs().max().item())
     for splits in (None, (1, 64)):
-        out = A.gqa_decode(q, pool, pt, kv_len, n_q, hk, fmt, sm, window, *scale, splits=splits)
+        out = A.gqa_decode(q, pool, pt, kv_len, n_q, hk, fmt, sm, window, *scale, splits=splits, exact=exact)
         torch.cuda.synchronize()
         err = (out.cpu().float() - ref).abs().max().item()
-        assert err < 2e-2, (splits, err)
+        assert err < tol, (splits, err)
 
 
 def test_gqa_decode_long_context_splits(cuda):
@@ -141,9 +144,12 @@ def test_gqa_decode_long_context_splits(cuda):
     q = torch.randn(2, hq, d, device=cuda).to(torch.bfloat16)
     sm = 1.0 / math.sqrt(d)
     ref = A.gqa_decode_ref(q.cpu(), pool.cpu(), pt.cpu(), kv_len.cpu(), 1, hk, K.FMT_NVFP4, sm)
-    out = A.gqa_decode(q, pool, pt, kv_len, 1, hk, K.FMT_NVFP4, sm)
+    out = A.gqa_decode(q, pool, pt, kv_len, 1, hk, K.FMT_NVFP4, sm, exact=True)
     torch.cuda.synchronize()
     assert (out.cpu().float() - ref).abs().max().item() < 2e-2
+    fast = A.gqa_decode(q, pool, pt, kv_len, 1, hk, K.FMT_NVFP4, sm)
+    torch.cuda.synchronize()
+    assert (fast.cpu().float() - ref).abs().max().item() < 0.06 * max(1.0, ref.abs().max().item())
     # deterministic
     out2 = A.gqa_decode(q, pool, pt, kv_len, 1, hk, K.FMT_NVFP4, sm)
-    assert torch.equal(out, out2)
+    assert torch.equal(fast, out2)
