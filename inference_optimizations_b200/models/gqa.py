@@ -16,6 +16,7 @@ shares the embedding / LM head: x = W_fc [emb(token); h_prev] -> layer -> norm -
 from __future__ import annotations
 
 import math
+import zlib
 from dataclasses import dataclass, field
 from typing import Callable, Optional
 
@@ -81,24 +82,42 @@ class GQAModel:
             hk = (cfg.num_kv_heads_global if glob else cfg.num_kv_heads) // tp
             self.geoms.append(LayerGeom(d, hk, cfg.num_q_heads // tp, 0 if glob else cfg.sliding_window,
                                         "global" if glob else ("draft" if draft else "swa")))
-        gen = torch.Generator(device=self.device)
-        gen.manual_seed(seed * 1000 + (7 if draft else 0))
         std = cfg.init_std
         h = cfg.hidden
         if weights is None:
-            self.embed = None if draft else _randn((cfg.vocab, h), std, gen, self.device)
+            # TP-invariant random init: every weight is generated as `nb` canonical blocks along its sharded
+            # dimension, each from its own seed, and a rank generates only the blocks it owns.  Any tp dividing nb
+            # therefore assembles exactly the same full model.
+            nb = next(n for n in (8, 4, 2, 1) if cfg.num_q_heads % n == 0 and cfg.num_kv_heads % n == 0
+                      and cfg.num_kv_heads_global % n == 0 and cfg.ffn % n == 0 and cfg.vocab % n == 0)
+            if nb % tp:
+                raise ValueError(f"tp={tp} does not divide the {nb} canonical weight blocks")
+            own = range(tp_rank * nb // tp, (tp_rank + 1) * nb // tp)
+            tag = f"{seed}/{'draft' if draft else 'main'}"
+
+            def blocks(name, shape, blk_ids, dim):
+                parts = []
+                for b in blk_ids:
+                    g = torch.Generator(device=self.device)
+                    g.manual_seed(zlib.crc32(f"{tag}/{name}/{b}".encode()))
+                    parts.append(_randn(shape, std, g, self.device))
+                return parts[0] if len(parts) == 1 else torch.cat(parts, dim=dim)
+
+            zeros = lambda n: torch.zeros(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
+            self.embed = None if draft else blocks("embed", (cfg.vocab // nb, h), range(nb), 0)
             self.layers = []
-            for g in self.geoms:
-                zeros = lambda n: torch.zeros(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
+            for i, g in enumerate(self.geoms):
+                d, hq_b, hk_b, f_b = g.head_dim, cfg.num_q_heads // nb, g.kv_heads * tp // nb, cfg.ffn // nb
+                qkv = torch.cat([blocks(f"{i}.q", (hq_b * d, h), own, 0), blocks(f"{i}.k", (hk_b * d, h), own, 0),
+                                 blocks(f"{i}.v", (hk_b * d, h), own, 0)], 0)
+                gu = torch.cat([blocks(f"{i}.gate", (f_b, h), own, 0), blocks(f"{i}.up", (f_b, h), own, 0)], 0)
                 self.layers.append(LayerWeights(
-                    qkv=_randn(((g.q_heads + 2 * g.kv_heads) * g.head_dim, h), std, gen, self.device),
-                    o=_randn((h, g.q_heads * g.head_dim), std, gen, self.device),
-                    gu=_randn((2 * self.ffn_local, h), std, gen, self.device),
-                    down=_randn((h, self.ffn_local), std, gen, self.device),
-                    q_norm=zeros(g.head_dim), k_norm=zeros(g.head_dim),
+                    qkv=qkv, o=blocks(f"{i}.o", (h, hq_b * d), own, 1), gu=gu,
+                    down=blocks(f"{i}.down", (h, f_b), own, 1),
+                    q_norm=zeros(d), k_norm=zeros(d),
                     n_in=zeros(h), n_post_attn=zeros(h), n_pre_ffn=zeros(h), n_post_ffn=zeros(h)))
             self.final_norm = torch.zeros(h, dtype=torch.bfloat16, device=self.device)
-            self.fc = _randn((h, 2 * h), std, gen, self.device) if draft else None
+            self.fc = blocks("fc", (h, 2 * h), [0], 0) if draft else None
         else:
             self._adopt(weights, draft)
         self.rope = {}

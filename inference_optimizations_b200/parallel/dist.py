@@ -66,14 +66,29 @@ def nccl_all_reduce(x: torch.Tensor) -> torch.Tensor:
     return x
 
 
+def host_all_reduce(x: torch.Tensor) -> torch.Tensor:
+    """All-reduce for CPU tensors over gloo (fp32 accumulation, result cast back in place)."""
+    xf = x.float()
+    dist.all_reduce(xf)
+    x.copy_(xf.to(x.dtype))
+    return x
+
+
 def argmax_merge(local_idx: torch.Tensor, local_val: torch.Tensor, vocab_local: int,
                  out: torch.Tensor) -> torch.Tensor:
     """Global greedy token from per-rank vocab-shard argmaxes: the max value, smallest global index on ties."""
     world = dist.get_world_size()
-    vals = torch.empty(world, local_val.numel(), dtype=local_val.dtype, device=local_val.device)
-    idxs = torch.empty(world, local_idx.numel(), dtype=local_idx.dtype, device=local_idx.device)
-    dist.all_gather_into_tensor(vals, local_val.contiguous())
-    dist.all_gather_into_tensor(idxs, local_idx.contiguous())
+    if local_val.is_cuda:
+        vals = torch.empty(world, local_val.numel(), dtype=local_val.dtype, device=local_val.device)
+        idxs = torch.empty(world, local_idx.numel(), dtype=local_idx.dtype, device=local_idx.device)
+        dist.all_gather_into_tensor(vals, local_val.contiguous())
+        dist.all_gather_into_tensor(idxs, local_idx.contiguous())
+    else:
+        vl = [torch.empty_like(local_val) for _ in range(world)]
+        il = [torch.empty_like(local_idx) for _ in range(world)]
+        dist.all_gather(vl, local_val.contiguous())
+        dist.all_gather(il, local_idx.contiguous())
+        vals, idxs = torch.stack(vl), torch.stack(il)
     best = vals.argmax(dim=0)                       # first max = lowest rank = smallest global index
     g = torch.gather(idxs, 0, best[None]).squeeze(0) + best.to(idxs.dtype) * vocab_local
     out.copy_(g.to(out.dtype))
