@@ -114,7 +114,8 @@ class GQARunner:
         self.out_ids = torch.zeros(max_tok, dtype=torch.int32, device=device)
         pin = self.device.type == "cuda"
         self.out_host = torch.zeros(max_tok, dtype=torch.int32, pin_memory=pin)
-        self.hidden_buf = None            # target pre-norm hidden of the last verify/decode (draft input)
+        if self.spec:
+            self._init_spec()
 
     # ------------------------------------------------------------------------------------------ memory
     def _max_splits(self) -> int:
@@ -206,12 +207,13 @@ class GQARunner:
         for s in batch.segments:
             if s.req.rid not in self.pages:
                 self.attach(s.req)
-        kinds = ("global", "swa")
+        kinds = ("global", "swa", "draft") if self.spec else ("global", "swa")
         p = self._pack(batch.segments, self.n_q_prefill, kinds)
         self.kv.sync_tables()
         self.stage.fill(p)
         self.stage.upload()
-        st = self.stage.step_tensors(len(p.ids), len(p.kv_len), p.n_q, {"global": (1, 1 << 20), "swa": (1, 1 << 20)})
+        st = self.stage.step_tensors(len(p.ids), len(p.kv_len), p.n_q,
+                                     {"global": (1, 1 << 20), "swa": (1, 1 << 20), "draft": (1, 1 << 20)})
         x, resid = self._target(st)
         rows = torch.tensor(p.logit_rows, dtype=torch.long, device=self.device)
         res = {}
@@ -219,13 +221,17 @@ class GQARunner:
             self._greedy(x[rows], self.out_ids)
             self.out_host[: len(p.logit_rows)].copy_(self.out_ids[: len(p.logit_rows)], non_blocking=True)
         if self.spec:
-            self._draft_prefill(batch, p, resid)
+            self._draft_prefill(batch, p, resid, st)
+            for s, r0 in p.seg_rows:
+                if s.logits:   # target hidden of the last prompt position: the first draft step's input
+                    self.hbuf[s.req.slot, 0].copy_(resid[r0 + len(s.tokens) - 1])
         if self.device.type == "cuda":
             torch.cuda.current_stream().synchronize()
         k = 0
         for s in batch.segments:
             if s.logits:
                 res[s.req.rid] = int(self.out_host[k])
+                s.req.draft_state["ld"] = s.start + len(s.tokens)   # draft KV exact below this position
                 k += 1
         self._trim(batch.segments)
         return res
@@ -325,24 +331,139 @@ class GQARunner:
         return g.replay
 
     # ------------------------------------------------------------------------------------------ speculative
-    def _draft_prefill(self, batch: Batch, p: Packed, resid: torch.Tensor) -> None:
+    # EAGLE-style greedy speculation with a one-layer draft head (`speculative/` in the reference; semantics of a
+    # top-1 chain, where the tree mask equals the causal mask, `attention/verify-splitk/gemma31_verify.py:19-24`).
+    # Per request, with L tokens in the target KV and pending token x_L:
+    #   1. draft extend over positions [ld, L] (tokens x_ld..x_L, inputs = target hiddens h_{ld-1}..h_{L-1}): makes the
+    #      draft KV exact up to L and proposes d1;
+    #   2. two draft decodes (inputs = the draft's own hidden) propose d2, d3;
+    #   3. target verify of [x_L, d1, d2, d3] at positions L..L+3 through the split-K verify kernel (n_q = 4);
+    #   4. accept the longest prefix with d_{i+1} == argmax_i, plus the target's next token.
+    # The whole device part is one CUDA graph per batch bucket; the host sends positions / slots / ids and reads back
+    # 7 ints per request.
+
+    def _init_spec(self) -> None:
+        h = self.cfg.hidden
+        nmax = self.max_running + 1
+        self.hbuf = torch.zeros(nmax, 4, h, dtype=torch.bfloat16, device=self.device)
+        kinds_d = ("draft",)
+        self.st_ext = StagingBuffers(self.max_running * 4, self.max_running, kinds_d, self.device)
+        self.st_d2 = StagingBuffers(self.max_running, self.max_running, kinds_d, self.device)
+        self.st_d3 = StagingBuffers(self.max_running, self.max_running, kinds_d, self.device)
+        self.st_ver = StagingBuffers(self.max_running * 4, self.max_running, ("global", "swa"), self.device)
+        self.spec_out = torch.zeros(self.max_running, 7, dtype=torch.int32, device=self.device)
+        pin = self.device.type == "cuda"
+        self.spec_out_host = torch.zeros(self.max_running, 7, dtype=torch.int32, pin_memory=pin)
+
+    def _draft_prefill(self, batch: Batch, p: Packed, resid: torch.Tensor, st: StepTensors) -> None:
         """Fill the draft layer's KV over each prefill segment: draft input at position q is (token q, target hidden
         at q - 1); the first position of a segment reuses its own hidden (no earlier hidden in this batch)."""
         shift = torch.arange(len(p.ids), device=self.device) - 1
         shift.clamp_(min=0)
         for s, r0 in p.seg_rows:
             shift[r0] = r0
-        hprev = resid[shift]
-        self._draft_forward(p, hprev)
+        self._draft_forward(st, resid[shift])
 
-    def _draft_forward(self, p: Packed, hprev: torch.Tensor, st: Optional[StepTensors] = None) -> tuple:
-        if st is None:
-            st = self.stage.step_tensors(len(p.ids), len(p.kv_len), p.n_q, {"draft": (1, 1 << 20)})
+    def _draft_forward(self, st: StepTensors, hprev: torch.Tensor) -> tuple:
         d = self.draft
         emb = B.embed(st.ids, self.model.embed, self.model.embed_scale)
         x0 = torch.nn.functional.linear(torch.cat([emb, hprev], dim=-1), d.fc)
-        layer_off = self.cfg.num_layers
-        st_d = StepTensors(st.ids, st.pos, {"draft": st.slot["draft"], "swa": st.slot["draft"]}, st.kv_len,
-                           st.req_idx, st.n_q, {"draft": st.splits.get("draft")})
-        x, resid = d.forward(st_d, self.kv, layer_offset=layer_off, inputs_embeds=x0)
-        return x, resid
+        st_d = StepTensors(st.ids, st.pos, {"draft": st.slot["draft"]}, st.kv_len, st.req_idx, st.n_q,
+                           {"draft": st.splits.get("draft")})
+        return d.forward(st_d, self.kv, layer_offset=self.cfg.num_layers, inputs_embeds=x0)
+
+    def _draft_logits_argmax(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        return self._greedy(x, out)
+
+    def _spec_body(self, bucket: int) -> Callable:
+        sp = self._splits(bucket)
+        st_ext = self.st_ext.step_tensors(bucket * 4, bucket, 4, sp)
+        st_d2 = self.st_d2.step_tensors(bucket, bucket, 1, sp)
+        st_d3 = self.st_d3.step_tensors(bucket, bucket, 1, sp)
+        st_ver = self.st_ver.step_tensors(bucket * 4, bucket, 4, sp)
+        h = self.cfg.hidden
+        rows = torch.arange(bucket, device=self.device) * 4
+        d_tok = torch.zeros(3, bucket, dtype=torch.int32, device=self.device)
+        t_tok = torch.zeros(bucket * 4, dtype=torch.int32, device=self.device)
+
+        def body():
+            rix = st_ver.req_idx.long()
+            # 1. draft extend: hidden inputs are the stored target hiddens of the request
+            hin = self.hbuf[rix].reshape(bucket * 4, h)
+            x, resid = self._draft_forward(st_ext, hin)
+            sel = rows + (st_ver.pos.view(bucket, 4)[:, 0] - st_ext.pos.view(bucket, 4)[:, 0]).long()
+            self._greedy(x[sel], d_tok[0])
+            g = resid[sel]
+            # 2-3. draft decodes
+            for k, stk in ((1, st_d2), (2, st_d3)):
+                stk.ids.copy_(d_tok[k - 1])
+                x, g = self._draft_forward(stk, g)
+                self._greedy(x, d_tok[k])
+            # 4. verify [x_L, d1, d2, d3]
+            ids4 = st_ver.ids.view(bucket, 4)
+            ids4[:, 1:].copy_(d_tok.t())
+            xv, rv = self._target(st_ver)
+            self._greedy(xv, t_tok)
+            self.hbuf.index_copy_(0, rix, rv.view(bucket, 4, h))
+            self.spec_out[:bucket, :4].copy_(t_tok.view(bucket, 4))
+            self.spec_out[:bucket, 4:].copy_(d_tok.t())
+        return body
+
+    def _spec_fn(self, bucket: int) -> Callable:
+        key = ("spec", bucket)
+        if key not in self.graphs:
+            body = self._spec_body(bucket)
+            self.graphs[key] = self._capture(body) if (self.ecfg.cuda_graphs and self.device.type == "cuda") else body
+        return self.graphs[key]
+
+    def spec_decode(self, reqs: list) -> dict:
+        if not hasattr(self, "hbuf"):
+            self._init_spec()
+        bucket = self._bucket(len(reqs))
+        ext, d2, d3, ver = [], [], [], []
+        for r in reqs:
+            L = r.kv_len
+            ld = r.draft_state.get("ld", L)
+            hist = (r.prompt + r.output)
+            toks = [hist[p] for p in range(ld, L)] + [r.pending]        # x_ld .. x_L
+            ext.append(Segment(r, ld, toks, False))
+            d2.append(Segment(r, L + 1, [0], False))
+            d3.append(Segment(r, L + 2, [0], False))
+            ver.append(Segment(r, L, [r.pending, 0, 0, 0], False))
+        for st, segs, nq, kinds in ((self.st_ext, ext, 4, ("draft",)), (self.st_d2, d2, 1, ("draft",)),
+                                    (self.st_d3, d3, 1, ("draft",)), (self.st_ver, ver, 4, ("global", "swa"))):
+            st.fill(self._pack(segs, nq, kinds, pad_groups_to=bucket))
+        self.kv.sync_tables()
+        for st in (self.st_ext, self.st_d2, self.st_d3, self.st_ver):
+            st.upload()
+        self._timed(self._spec_fn(bucket))
+        n = len(reqs)
+        self.spec_out_host[:n].copy_(self.spec_out[:n], non_blocking=True)
+        if self.device.type == "cuda":
+            torch.cuda.current_stream().synchronize()
+        res = {}
+        for i, r in enumerate(reqs):
+            o = self.spec_out_host[i].tolist()
+            t, d = o[:4], o[4:]
+            a = 0
+            while a < 3 and d[a] == t[a]:
+                a += 1
+            res[r.rid] = d[:a] + [t[a]]
+            r.accepted += a
+            r.spec_steps += 1
+            r.draft_state["ld"] = r.kv_len + 1                  # draft KV exact up to L after this step's extend
+            # hidden rows 0..a of this verify are the next extend's inputs (stored by the graph)
+            pg = self.pages.get(r.rid)
+            if pg is not None:
+                pg["swa"].trim(r.kv_len + a + 1)                  # next target query position L'
+                pg["draft"].trim(r.kv_len + 1)                    # next draft extend starts at L + 1
+        return res
+
+    def after_synthetic(self, reqs: list) -> None:
+        """Synthetic sessions: the draft KV counts as exact up to the prompt end; random target hiddens."""
+        if self.spec:
+            if not hasattr(self, "hbuf"):
+                self._init_spec()
+            for r in reqs:
+                r.draft_state["ld"] = r.kv_len
+            self.hbuf.normal_()

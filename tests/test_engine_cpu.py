@@ -42,3 +42,23 @@ def test_continuous_batching_many_requests():
     prompts = [[5 + i] * (10 + 7 * i) for i in range(7)]       # more requests than max_running
     outs = eng.generate(prompts, SamplingParams(max_new_tokens=4))
     assert all(len(o) == 4 for o in outs)
+
+
+def test_speculative_decoding_preserves_greedy_output():
+    torch.manual_seed(5)
+    prompts = [torch.randint(1, 500, (n,)).tolist() for n in (70, 33)]
+    base = _engine().generate(prompts, SamplingParams(max_new_tokens=9))
+    eng = _engine(spec=True, draft_tokens=3)
+    spec = eng.generate(prompts, SamplingParams(max_new_tokens=9))
+    ref_model = eng.runner.model
+    for p, a, b in zip(prompts, base, spec):
+        seq = list(p)
+        for ta, tb in zip(a, b):
+            ref = ref_model.reference_logits(seq)[-1]
+            top2 = torch.topk(ref, 2).values
+            if (top2[0] - top2[1]).item() <= 1e-2:
+                break                      # numerically tied step: continuations may legitimately diverge
+            assert ta == tb == int(ref.argmax())
+            seq.append(ta)
+    steps = [r for r in eng.finished]
+    assert all(r.spec_steps > 0 for r in steps)

@@ -39,3 +39,25 @@ def test_engine_quantized_kv_runs(cuda, kv):
     outs = eng.generate(prompts, SamplingParams(max_new_tokens=5))
     assert all(len(o) == 5 for o in outs)
     assert eng.runner.kv.alloc["global"].used == 0
+
+
+def test_speculative_decoding_gpu_matches_reference(cuda):
+    torch.manual_seed(3)
+    ecfg = EngineConfig(model="tiny_gqa", device="cuda:0", kv_dtype="bf16", max_running=4, chunked_prefill=64,
+                        graph_batch_sizes="1,2,4", spec=True, draft_tokens=3)
+    eng = Engine(ecfg, max_seq=512)
+    prompts = [torch.randint(1, 500, (n,)).tolist() for n in (90, 41, 150)]
+    outs = eng.generate(prompts, SamplingParams(max_new_tokens=10))
+    checked = 0
+    for p, o in zip(prompts, outs):
+        seq = list(p)
+        for tok in o:
+            ref = eng.runner.model.reference_logits(seq)[-1]
+            top2 = torch.topk(ref, 2).values
+            if (top2[0] - top2[1]).item() <= 0.05:
+                break
+            assert tok == int(ref.argmax())
+            checked += 1
+            seq.append(tok)
+    assert checked >= 6
+    assert all(r.spec_steps > 0 for r in eng.finished)
