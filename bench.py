@@ -33,7 +33,8 @@ def parse():
     p.add_argument("--ctx", type=int, default=32768)
     p.add_argument("--max-new", type=int, default=512)
     p.add_argument("--kv", default="nvfp4", choices=["nvfp4", "fp8", "bf16"])
-    p.add_argument("--spec", type=int, default=0, help="1 = speculative decoding (1-layer draft, 3 tokens)")
+    p.add_argument("--spec", type=int, default=1,
+                   help="1 = speculative decoding, the config's 1-layer draft proposing 3 tokens (default); 0 = plain")
     p.add_argument("--no-graphs", action="store_true")
     return p.parse_args()
 
@@ -65,7 +66,9 @@ def main() -> int:
     torch.backends.cuda.matmul.allow_tf32 = False
     cfg = model_config(args.model)
     steps, warm = args.steps, max(3, args.warmup)
-    max_new = max(args.max_new, steps + warm + 8)
+    # generation budget: no session may finish inside the timed steps (up to 4 tokens per speculative step, then
+    # the decode-only pass)
+    max_new = max(args.max_new, 4 * (steps + warm) + 2 * steps + 16)
     ecfg = EngineConfig(model=args.model, device=str(dev), kv_dtype=args.kv, max_running=args.sessions,
                         chunked_prefill=2048, spec=bool(args.spec), cuda_graphs=not args.no_graphs,
                         graph_batch_sizes=str(args.sessions), tp=tp)
@@ -97,6 +100,23 @@ def main() -> int:
     if tp > 1:
         torch.distributed.barrier()
     ck = clocks.stop()
+    decode_only = None
+    if ecfg.spec:
+        # secondary figure: the same sessions advanced by plain greedy decode steps (device time of the step bodies)
+        runner = eng.runner
+        for _ in range(2):
+            out = runner.decode(list(eng.sched.running))
+            eng.sched.commit_decode(out)
+        runner.event_log = []
+        dtoks = 0
+        for _ in range(steps):
+            out = runner.decode(list(eng.sched.running))
+            eng.sched.commit_decode(out)
+            dtoks += sum(len(v) for v in out.values())
+        torch.cuda.synchronize()
+        d_ms = D.max_over_ranks(sum(a.elapsed_time(b) for a, b in runner.event_log))
+        decode_only = {"value": round(dtoks / (d_ms / 1e3), 2), "ms_per_step": round(d_ms / steps, 4),
+                       "note": "plain greedy decode of the same sessions (no draft/verify)"}
     dev_ms = sum(a.elapsed_time(b) for a, b in eng.runner.event_log)
     e2e_ms = ev0.elapsed_time(ev1)
     dev_ms = D.max_over_ranks(dev_ms)
@@ -139,6 +159,10 @@ def main() -> int:
         "gpu_launches": launches * steps,
         "impl": "ours",
     }
+    if decode_only is not None:
+        res["decode_only"] = decode_only
+        res["config"]["spec_note"] = ("random-init draft head: acceptance is whatever the untrained draft achieves "
+                                      "against the random-init target (measured above)")
     bad = rejected(ck)
     if bad:
         res["clocks"]["rejected"] = bad
