@@ -183,13 +183,66 @@ void gqa_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& p
   CHECK_CUDA_OK(iob::gqa_decode(a, stream()));
 }
 
-void umma_gemm_test(const at::Tensor& A, const at::Tensor& B, at::Tensor C) {
+void mla_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& idx, at::Tensor out,
+                c10::optional<at::Tensor> lse, at::Tensor o_part, at::Tensor lse_part, at::Tensor status, int64_t fmt,
+                int64_t tiles_per_split, int64_t num_splits, double sm_scale) {
+  req(q, at::kBFloat16, "q");
+  req(pool, at::kByte, "pool");
+  req(idx, at::kInt, "idx");
+  req(out, at::kBFloat16, "out");
+  req(o_part, at::kFloat, "o_part");
+  req(lse_part, at::kFloat, "lse_part");
+  req(status, at::kInt, "status");
+  TORCH_CHECK(q.is_contiguous() && out.is_contiguous() && pool.is_contiguous(), "layout");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 576, "q [T, H, 576]");
+  TORCH_CHECK(idx.dim() == 2 && idx.stride(1) == 1 && idx.size(0) == q.size(0), "idx [T, topk]");
+  TORCH_CHECK(out.size(0) == q.size(0) && out.size(1) == q.size(1) && out.size(2) == 512, "out [T, H, 512]");
+  const int64_t rb = fmt == iob::kKvNvfp4 ? 352 : 576;
+  TORCH_CHECK(pool.dim() == 2 && pool.size(1) == rb, "pool row bytes");
+  iob::MlaDecodeArgs a{};
+  a.q = q.data_ptr();
+  a.pool = pool.data_ptr<uint8_t>();
+  a.idx = idx.data_ptr<int>();
+  a.out = out.data_ptr();
+  if (lse.has_value()) {
+    req(*lse, at::kFloat, "lse");
+    TORCH_CHECK(lse->numel() >= q.size(0) * q.size(1), "lse size");
+    a.lse = lse->data_ptr<float>();
+  }
+  a.o_part = o_part.data_ptr<float>();
+  a.lse_part = lse_part.data_ptr<float>();
+  a.status = status.data_ptr<int>();
+  a.T = q.size(0);
+  a.H = q.size(1);
+  a.topk = idx.size(1);
+  a.idx_stride = idx.stride(0);
+  a.fmt = fmt;
+  a.tiles_per_split = tiles_per_split;
+  a.num_splits = num_splits;
+  a.sm_scale = sm_scale;
+  if (num_splits > 1)
+    TORCH_CHECK(o_part.numel() >= num_splits * a.T * a.H * 512 && lse_part.numel() >= num_splits * a.T * a.H,
+                "split workspace too small");
+  const at::cuda::CUDAGuard g(q.device());
+  CHECK_CUDA_OK(iob::mla_decode(a, stream()));
+}
+
+void umma_gemm_test(const at::Tensor& A, const at::Tensor& B, at::Tensor C, int64_t sw64) {
   req(A, at::kBFloat16, "A");
   req(B, at::kBFloat16, "B");
   req(C, at::kFloat, "C");
   const at::cuda::CUDAGuard g(A.device());
   CHECK_CUDA_OK(iob::umma_gemm_test(A.data_ptr(), B.data_ptr(), C.data_ptr<float>(), A.size(0), B.size(0),
-                                    A.size(1), stream()));
+                                    A.size(1), static_cast<int>(sw64), stream()));
+}
+
+void umma_f8_mn_test(const at::Tensor& A, const at::Tensor& B, at::Tensor C) {
+  req(A, at::kByte, "A");
+  req(B, at::kByte, "B");
+  req(C, at::kFloat, "C");
+  TORCH_CHECK(A.size(0) == 128 && B.size(0) == A.size(1) && C.size(0) == 128 && C.size(1) == B.size(1), "shapes");
+  const at::cuda::CUDAGuard g(A.device());
+  CHECK_CUDA_OK(iob::umma_f8_mn_test(A.data_ptr(), B.data_ptr(), C.data_ptr<float>(), B.size(1), A.size(1), stream()));
 }
 
 void umma_rate_test(int64_t n, int64_t count, int64_t nacc, int64_t ts, at::Tensor out) {
@@ -210,6 +263,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_quant_write", &mla_quant_write);
   m.def("index_key_write", &index_key_write);
   m.def("gqa_decode", &gqa_decode);
+  m.def("mla_decode", &mla_decode);
   m.def("umma_gemm_test", &umma_gemm_test);
+  m.def("umma_f8_mn_test", &umma_f8_mn_test);
   m.def("umma_rate_test", &umma_rate_test);
 }

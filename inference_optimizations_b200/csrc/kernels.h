@@ -88,8 +88,25 @@ struct GqaDecodeArgs {
 };
 cudaError_t gqa_decode(const GqaDecodeArgs& a, cudaStream_t s);
 
+// ---- sparse MLA decode (attn_mla_decode.cu): DSA attention over gathered latent rows, H <= 128 heads.
+struct MlaDecodeArgs {
+  const void* q;           // bf16 [T, H, 576]: 512 latent dims then 64 rope dims
+  const uint8_t* pool;     // [rows, 352] NVFP4 latent rows (fmt = kKvNvfp4) or [rows, 576] E4M3 rows (kKvFp8)
+  const int* idx;          // [T, idx_stride] pool rows attended by each token; -1 = masked
+  void* out;               // bf16 [T, H, 512]
+  float* lse;              // [T, H] natural-log logsumexp, or null
+  float* o_part;           // [num_splits, T, H, 512] (num_splits > 1)
+  float* lse_part;         // [num_splits, T, H] log2 units (num_splits > 1)
+  int* status;             // device status word (bounded-wait timeouts)
+  int T, H, topk, idx_stride, fmt;
+  int tiles_per_split, num_splits;  // 128-row tiles of the top-k list per split
+  float sm_scale;
+};
+cudaError_t mla_decode(const MlaDecodeArgs& a, cudaStream_t s);
+
 // ---- primitive check (umma_test.cu): C[M, N] fp32 = A[M, K] * B[N, K]^T, bf16 inputs, one CTA per 128 rows.
-cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, cudaStream_t s);
+cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, int sw64, cudaStream_t s);
+cudaError_t umma_f8_mn_test(const void* A, const void* B, float* C, int N, int K, cudaStream_t s);
 cudaError_t umma_rate_test(int n, int count, int nacc, int ts, long long* out, cudaStream_t s);
 
 }  // namespace iob

@@ -72,6 +72,80 @@ def gqa_decode_case(b: int, hk: int, hq: int, d: int, ctx: int, fmt_name: str, n
             "gbs": round(nbytes / us / 1e3, 1), "frac_hbm": round(nbytes / us / 1e3 / PEAKS["hbm_gbs"], 3)}
 
 
+def _time_flushed(fn, iters: int = 10) -> float:
+    """Mean device time of fn over `iters` launches, L2 flushed (a 256 MB write) before each, flush not timed."""
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for _ in range(3):
+        fn()
+    total = 0.0
+    for _ in range(iters):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        total += e0.elapsed_time(e1)
+    return total / iters * 1e3
+
+
+def mla_pool_random(rows: int, fmt: int, dev, distinct: int = 1 << 16, seed: int = 0) -> torch.Tensor:
+    """A pool of `rows` well-formed latent rows (quantized N(0,1) latents), `distinct` unique rows tiled."""
+    from ..ops import formats as F
+    from ..ops import kvcache as K
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    n = min(rows, distinct)
+    nope = torch.randn(n, F.MLA_NOPE, generator=g)
+    rope = torch.randn(n, F.MLA_ROPE, generator=g)
+    base = (F.mla_row_quantize(nope, rope) if fmt == K.FMT_NVFP4 else F.mla_fp8_row_quantize(nope, rope)).to(dev)
+    reps = -(-rows // n)
+    return base.repeat(reps, 1)[:rows].contiguous()
+
+
+def mla_decode_case(b: int, heads: int, ctx: int, topk: int, fmt_name: str, n_q: int = 1, launches: int = 0) -> dict:
+    """BASELINE config 2 shape: b sequences x n_q query tokens, `heads` heads x 576, `ctx` cached tokens each in a
+    page-64 pool, top-`topk` positions per token from a random-normal indexer score, mapped through a random page
+    table to pool rows."""
+    from ..ops import kvcache as K
+    from ..ops import mla as M
+    dev = torch.device("cuda:0")
+    fmt = K.FMT_IDS[fmt_name]
+    per = -(-ctx // 64)
+    pages = b * per + 1
+    pool = mla_pool_random(pages * 64, fmt, dev)
+    pt = (torch.randperm(pages - 1, device=dev)[: b * per] + 1).view(b, per)
+    t = b * n_q
+    gen = torch.Generator(device=dev).manual_seed(1)
+    scores = torch.randn(t, ctx, device=dev, generator=gen)
+    pos = scores.topk(topk, dim=-1).indices                                  # [T, topk]
+    seq = torch.arange(t, device=dev) // n_q
+    idx = (pt[seq[:, None], pos // 64] * 64 + pos % 64).int().contiguous()
+    del scores
+    q = torch.randn(t, heads, 576, device=dev, generator=gen).to(torch.bfloat16)
+    splits = M.mla_split_policy(t, topk)
+    ws = M.MlaWorkspace.allocate(t, heads, splits[0], device=dev)
+    out = torch.empty(t, heads, 512, dtype=torch.bfloat16, device=dev)
+    sm = M.mla_sm_scale()
+
+    def fn():
+        M.mla_decode(q, pool, idx, sm, fmt, splits=splits, ws=ws, out=out)
+    if launches:
+        for _ in range(launches):
+            fn()
+        torch.cuda.synchronize()
+        return {}
+    us = _time_flushed(fn)
+    assert int(ws.status.item()) == 0, "kernel status"
+    row_b = M.ROW_BYTES[fmt]
+    nbytes = t * topk * row_b + q.numel() * 2 + out.numel() * 2
+    flops = 2 * t * heads * topk * (576 + 512)
+    return {"kernel": "mla_decode", "tokens": t, "heads": heads, "ctx": ctx, "topk": topk, "fmt": fmt_name,
+            "splits": list(splits), "us": round(us, 2), "bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1),
+            "tflops": round(flops / us / 1e6, 1),
+            "frac_fp8_peak": round(flops / us / 1e6 / (2 * PEAKS["bf16_tflops"]), 3),
+            "l2": "flushed before each launch (256 MB write)"}
+
+
 def main() -> None:
     _load_peaks()
     p = argparse.ArgumentParser()
@@ -91,8 +165,7 @@ def main() -> None:
     if a.kernel == "gqa_decode":
         r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches)
     elif a.kernel == "mla_decode":
-        from ..ops.mla import mla_decode_case
-        r = mla_decode_case(a.b, a.heads, a.ctx, a.topk, a.fmt, a.nq, a.launches, PEAKS)
+        r = mla_decode_case(a.b, a.heads, a.ctx, a.topk, a.fmt, a.nq, a.launches)
     else:
         raise SystemExit(f"unknown kernel {a.kernel}")
     if r:

@@ -18,11 +18,25 @@ def test_umma_primitives(cuda):
     for (m, n, k) in [(128, 16, 64), (256, 64, 256), (128, 256, 512)]:
         a = torch.randn(m, k, device=cuda).to(torch.bfloat16)
         b = torch.randn(n, k, device=cuda).to(torch.bfloat16)
-        c = torch.empty(m, n, device=cuda)
-        ext().umma_gemm_test(a, b, c)
-        torch.cuda.synchronize()
         ref = a.float() @ b.float().T
-        assert torch.allclose(c, ref, rtol=1e-3, atol=1e-2), (m, n, k, (c - ref).abs().max().item())
+        for sw64 in (0, 1):
+            c = torch.empty(m, n, device=cuda)
+            ext().umma_gemm_test(a, b, c, sw64)
+            torch.cuda.synchronize()
+            assert torch.allclose(c, ref, rtol=1e-3, atol=1e-2), (m, n, k, sw64, (c - ref).abs().max().item())
+
+
+def test_umma_f8_mn_major(cuda):
+    from inference_optimizations_b200._ext import ext
+    torch.manual_seed(0)
+    for (n, k) in [(128, 128), (256, 256)]:
+        a = torch.randn(128, k, device=cuda).to(torch.float8_e4m3fn)
+        b = torch.randn(k, n, device=cuda).to(torch.float8_e4m3fn)
+        c = torch.empty(128, n, device=cuda)
+        ext().umma_f8_mn_test(a.view(torch.uint8), b.view(torch.uint8), c)
+        torch.cuda.synchronize()
+        ref = a.float() @ b.float()
+        assert torch.allclose(c, ref, rtol=1e-4, atol=1e-3), (n, k, (c - ref).abs().max().item())
 
 
 @pytest.mark.parametrize("hidden,residual", [(5376, True), (7168, False), (256, True)])
@@ -153,3 +167,45 @@ def test_gqa_decode_long_context_splits(cuda):
     # deterministic
     out2 = A.gqa_decode(q, pool, pt, kv_len, 1, hk, K.FMT_NVFP4, sm)
     assert torch.equal(fast, out2)
+
+
+def _mla_case(cuda, t, h, topk, fmt, rows=3000, mask_frac=0.1, seed=5):
+    from inference_optimizations_b200.ops import mla as M
+    torch.manual_seed(seed)
+    nope = torch.randn(rows, 512) * 1.5
+    rope = torch.randn(rows, 64)
+    pool = (F.mla_row_quantize(nope, rope) if fmt == K.FMT_NVFP4 else F.mla_fp8_row_quantize(nope, rope)).to(cuda)
+    idx = torch.stack([torch.randperm(rows)[:topk] for _ in range(t)]).int()
+    idx[torch.rand(t, topk) < mask_frac] = -1
+    q = (torch.randn(t, h, 576) * 2).to(torch.bfloat16).to(cuda)
+    return M, pool, idx.to(cuda), q
+
+
+@pytest.mark.parametrize("fmt", [K.FMT_NVFP4, K.FMT_FP8])
+@pytest.mark.parametrize("t,h,topk", [(3, 128, 2048), (5, 64, 200), (2, 16, 64), (1, 128, 640)])
+def test_mla_decode(cuda, fmt, t, h, topk):
+    M, pool, idx, q = _mla_case(cuda, t, h, topk, fmt)
+    sm = 1.0 / math.sqrt(192)
+    ref, ref_lse = M.mla_decode_ref(q, pool, idx, sm, fmt)
+    tol = 0.06 * max(1.0, ref.abs().max().item())
+    for splits in (None, (1, 64), (-(-topk // 128), 1)):
+        out, lse = M.mla_decode(q, pool, idx, sm, fmt, splits=splits, return_lse=True)
+        torch.cuda.synchronize()
+        err = (out.float() - ref).abs().max().item()
+        assert err < tol, (splits, err, tol)
+        assert (lse - ref_lse).abs().max().item() < 0.05, splits
+
+
+def test_mla_decode_masked_and_deterministic(cuda):
+    M, pool, idx, q = _mla_case(cuda, 4, 128, 512, K.FMT_NVFP4, seed=9)
+    idx[1] = -1                      # every row masked: zero output, -inf lse
+    idx[2, 128:] = -1                # only the first tile visible
+    sm = 1.0 / math.sqrt(192)
+    ref, ref_lse = M.mla_decode_ref(q, pool, idx, sm, K.FMT_NVFP4)
+    out, lse = M.mla_decode(q, pool, idx, sm, K.FMT_NVFP4, return_lse=True)
+    out2 = M.mla_decode(q, pool, idx, sm, K.FMT_NVFP4)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
+    assert out[1].abs().max().item() == 0 and torch.isinf(lse[1]).all()
+    assert (out.float() - ref).abs().max().item() < 0.06 * max(1.0, ref.abs().max().item())
+    assert (lse[[0, 2, 3]] - ref_lse[[0, 2, 3]]).abs().max().item() < 0.05

@@ -1,0 +1,62 @@
+"""Sparse MLA (DSA) decode on CPU: the fp32 oracle and BASELINE config 1 (NVFP4 KV quantize + dequant-gather +
+sparse MLA decode against unquantized attention), plus the split planner."""
+import math
+
+import torch
+
+from inference_optimizations_b200.ops import formats as F
+from inference_optimizations_b200.ops import mla as M
+from inference_optimizations_b200.ops.kvcache import FMT_FP8, FMT_NVFP4
+
+
+def test_config1_nvfp4_sparse_decode_vs_unquantized():
+    torch.manual_seed(0)
+    b, h, n, topk = 4, 16, 4096, 2048
+    nope = torch.randn(b * n, 512)
+    rope = torch.randn(b * n, 64)
+    pool = F.mla_row_quantize(nope, rope)                           # [b*n, 352]
+    assert pool.shape == (b * n, 352)
+    scores = torch.randn(b, n)                                      # random-normal indexer
+    pos = scores.topk(topk, dim=-1).indices
+    idx = (pos + torch.arange(b)[:, None] * n).int()
+    q = torch.randn(b, h, 576)
+    sm = 1.0 / math.sqrt(576)
+    out, lse = M.mla_decode(q, pool, idx, sm, FMT_NVFP4, return_lse=True)
+    kv = torch.cat([nope, rope], dim=-1)
+    exact, exact_lse = F.sparse_mla_reference(q, kv, idx, sm)
+    # 4-bit latents: per-element relative error <= 1/4 of the block's step; the attention output is an average of
+    # ~2048 rows, so its error shrinks well below that
+    rel = (out.float() - exact).norm() / exact.norm()
+    assert rel < 0.12, rel
+    assert (lse - exact_lse).abs().max() < 0.1
+    # FP8 rows on the same indices are closer still
+    pool8 = F.mla_fp8_row_quantize(nope, rope)
+    out8 = M.mla_decode(q, pool8, idx, sm, FMT_FP8)
+    rel8 = (out8.float() - exact).norm() / exact.norm()
+    assert rel8 < rel and rel8 < 0.05, rel8
+
+
+def test_reference_masks_and_matches_dense():
+    torch.manual_seed(1)
+    rows, t, h, topk = 300, 3, 4, 40
+    pool = F.mla_row_quantize(torch.randn(rows, 512), torch.randn(rows, 64))
+    idx = torch.stack([torch.randperm(rows)[:topk] for _ in range(t)]).int()
+    idx[0, ::3] = -1
+    idx[2] = -1
+    q = torch.randn(t, h, 576)
+    out, lse = M.mla_decode_ref(q, pool, idx, 0.1)
+    kv = F.mla_row_dequantize(pool)
+    for i in range(2):
+        sel = idx[i][idx[i] >= 0].long()
+        s = q[i] @ kv[sel].T * 0.1
+        assert torch.allclose(out[i], torch.softmax(s, -1) @ kv[sel, :512], atol=1e-5)
+        assert torch.allclose(lse[i], torch.logsumexp(s, -1), atol=1e-5)
+    assert out[2].abs().max() == 0 and torch.isinf(lse[2]).all()
+
+
+def test_split_policy_fills_sms():
+    assert M.mla_split_policy(64, 2048) == (1, 16)          # 128 CTAs: one wave already
+    ns, tps = M.mla_split_policy(1, 2048)
+    assert ns * tps >= 16 and 2 * ns <= 148 and ns > 4
+    ns, tps = M.mla_split_policy(8, 200)
+    assert ns * tps * 128 >= 200
