@@ -100,6 +100,8 @@ def main() -> int:
     if tp > 1:
         torch.distributed.barrier()
     ck = clocks.stop()
+    dev_ms = D.max_over_ranks(sum(a.elapsed_time(b) for a, b in eng.runner.event_log))
+    e2e_ms = D.max_over_ranks(ev0.elapsed_time(ev1))
     decode_only = None
     if ecfg.spec:
         # secondary figure: the same sessions advanced by plain greedy decode steps (device time of the step bodies)
@@ -117,10 +119,6 @@ def main() -> int:
         d_ms = D.max_over_ranks(sum(a.elapsed_time(b) for a, b in runner.event_log))
         decode_only = {"value": round(dtoks / (d_ms / 1e3), 2), "ms_per_step": round(d_ms / steps, 4),
                        "note": "plain greedy decode of the same sessions (no draft/verify)"}
-    dev_ms = sum(a.elapsed_time(b) for a, b in eng.runner.event_log)
-    e2e_ms = ev0.elapsed_time(ev1)
-    dev_ms = D.max_over_ranks(dev_ms)
-    e2e_ms = D.max_over_ranks(e2e_ms)
     stage = eng.runner.stage
     h2d = stage.h2d_bytes() + (sum(t.bytes_synced for t in eng.runner.kv.tables.values()) - table0) // steps
     d2h = 4 * args.sessions * (1 + (ecfg.draft_tokens if ecfg.spec else 0))

@@ -183,47 +183,65 @@ void gqa_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& p
   CHECK_CUDA_OK(iob::gqa_decode(a, stream()));
 }
 
-void mla_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& idx, at::Tensor out,
-                c10::optional<at::Tensor> lse, at::Tensor o_part, at::Tensor lse_part, at::Tensor status, int64_t fmt,
-                int64_t tiles_per_split, int64_t num_splits, double sm_scale) {
-  req(q, at::kBFloat16, "q");
+void mla_decode(c10::optional<at::Tensor> q, at::Tensor q8, at::Tensor q_scale, const at::Tensor& pool,
+                const at::Tensor& idx, at::Tensor out, c10::optional<at::Tensor> lse, at::Tensor o_part,
+                at::Tensor lse_part, at::Tensor status, int64_t fmt, int64_t tiles_per_split, int64_t num_splits,
+                double sm_scale, c10::optional<at::Tensor> trace) {
+  req(q8, at::kByte, "q8");
+  req(q_scale, at::kFloat, "q_scale");
   req(pool, at::kByte, "pool");
   req(idx, at::kInt, "idx");
   req(out, at::kBFloat16, "out");
   req(o_part, at::kFloat, "o_part");
   req(lse_part, at::kFloat, "lse_part");
   req(status, at::kInt, "status");
-  TORCH_CHECK(q.is_contiguous() && out.is_contiguous() && pool.is_contiguous(), "layout");
-  TORCH_CHECK(q.dim() == 3 && q.size(2) == 576, "q [T, H, 576]");
-  TORCH_CHECK(idx.dim() == 2 && idx.stride(1) == 1 && idx.size(0) == q.size(0), "idx [T, topk]");
-  TORCH_CHECK(out.size(0) == q.size(0) && out.size(1) == q.size(1) && out.size(2) == 512, "out [T, H, 512]");
+  TORCH_CHECK(q8.is_contiguous() && out.is_contiguous() && pool.is_contiguous() && q_scale.is_contiguous(), "layout");
+  TORCH_CHECK(q8.dim() == 3 && q8.size(2) == 576, "q8 [T, H, 576]");
+  const int64_t T = q8.size(0), H = q8.size(1);
+  TORCH_CHECK(q_scale.numel() >= T * H, "q_scale [T, H]");
+  TORCH_CHECK(idx.dim() == 2 && idx.stride(1) == 1 && idx.size(0) == T, "idx [T, topk]");
+  TORCH_CHECK(out.size(0) == T && out.size(1) == H && out.size(2) == 512, "out [T, H, 512]");
   const int64_t rb = fmt == iob::kKvNvfp4 ? 352 : 576;
   TORCH_CHECK(pool.dim() == 2 && pool.size(1) == rb, "pool row bytes");
   iob::MlaDecodeArgs a{};
-  a.q = q.data_ptr();
+  if (q.has_value()) {
+    req(*q, at::kBFloat16, "q");
+    TORCH_CHECK(q->is_contiguous() && q->sizes() == q8.sizes(), "q [T, H, 576] bf16");
+    a.q = q->data_ptr();
+    a.q8_out = q8.data_ptr<uint8_t>();
+    a.q_scale_out = q_scale.data_ptr<float>();
+  }
+  a.q8 = q8.data_ptr<uint8_t>();
+  a.q_scale = q_scale.data_ptr<float>();
   a.pool = pool.data_ptr<uint8_t>();
   a.idx = idx.data_ptr<int>();
   a.out = out.data_ptr();
   if (lse.has_value()) {
     req(*lse, at::kFloat, "lse");
-    TORCH_CHECK(lse->numel() >= q.size(0) * q.size(1), "lse size");
+    TORCH_CHECK(lse->numel() >= T * H, "lse size");
     a.lse = lse->data_ptr<float>();
   }
   a.o_part = o_part.data_ptr<float>();
   a.lse_part = lse_part.data_ptr<float>();
   a.status = status.data_ptr<int>();
-  a.T = q.size(0);
-  a.H = q.size(1);
+  a.T = T;
+  a.H = H;
   a.topk = idx.size(1);
   a.idx_stride = idx.stride(0);
   a.fmt = fmt;
+  a.pool_rows = static_cast<int>(std::min<int64_t>(pool.size(0), INT32_MAX));
   a.tiles_per_split = tiles_per_split;
   a.num_splits = num_splits;
   a.sm_scale = sm_scale;
+  if (trace.has_value()) {
+    req(*trace, at::kLong, "trace");
+    TORCH_CHECK(trace->numel() >= 40 * 64, "trace size");
+    a.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
+  }
   if (num_splits > 1)
-    TORCH_CHECK(o_part.numel() >= num_splits * a.T * a.H * 512 && lse_part.numel() >= num_splits * a.T * a.H,
+    TORCH_CHECK(o_part.numel() >= num_splits * T * H * 512 && lse_part.numel() >= num_splits * T * H,
                 "split workspace too small");
-  const at::cuda::CUDAGuard g(q.device());
+  const at::cuda::CUDAGuard g(q8.device());
   CHECK_CUDA_OK(iob::mla_decode(a, stream()));
 }
 
@@ -243,6 +261,14 @@ void umma_f8_mn_test(const at::Tensor& A, const at::Tensor& B, at::Tensor C) {
   TORCH_CHECK(A.size(0) == 128 && B.size(0) == A.size(1) && C.size(0) == 128 && C.size(1) == B.size(1), "shapes");
   const at::cuda::CUDAGuard g(A.device());
   CHECK_CUDA_OK(iob::umma_f8_mn_test(A.data_ptr(), B.data_ptr(), C.data_ptr<float>(), B.size(1), A.size(1), stream()));
+}
+
+void nvfp4_lut_test(const at::Tensor& words, at::Tensor out) {
+  req(words, at::kInt, "words");
+  req(out, at::kInt, "out");
+  const at::cuda::CUDAGuard g(words.device());
+  CHECK_CUDA_OK(iob::nvfp4_lut_test(reinterpret_cast<const uint32_t*>(words.data_ptr<int>()), words.numel(),
+                                    out.data_ptr<int>(), stream()));
 }
 
 void umma_rate_test(int64_t n, int64_t count, int64_t nacc, int64_t ts, at::Tensor out) {
@@ -266,5 +292,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_decode", &mla_decode);
   m.def("umma_gemm_test", &umma_gemm_test);
   m.def("umma_f8_mn_test", &umma_f8_mn_test);
+  m.def("nvfp4_lut_test", &nvfp4_lut_test);
   m.def("umma_rate_test", &umma_rate_test);
 }

@@ -125,6 +125,105 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// ----------------------------------------------------------------------------------------------- clusters
+// Distributed shared memory between the CTAs of a thread-block cluster: plain stores and mbarrier arrivals into a
+// peer CTA's shared memory (no multicast anywhere).
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of this CTA's shared-memory location `addr` in the shared window of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// Arrive (release, cluster scope) on an mbarrier in a peer CTA (address from mapa_shared).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from this CTA's shared memory into a peer
+// CTA's shared memory (dst and the peer's mbarrier as mapa_shared addresses), completing as tx bytes on that mbarrier.
+__device__ __forceinline__ void bulk_s2peer(uint32_t dst_cluster, const void* src, uint32_t bytes,
+                                            uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_cluster),
+      "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's committed bulk-copy groups still have source reads pending.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_cluster() {
+  asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
+}
+// Whole-cluster barrier (every thread of every CTA of the cluster).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Wait on a local mbarrier whose arrivals may come from peer CTAs (acquire at cluster scope); bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_try_wait_cl(uint64_t* bar, uint32_t parity, uint32_t hint_ns = 20000) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+// Non-blocking test (acquire at cluster scope): for issue loops that poll several barriers.
+__device__ __forceinline__ bool mbar_test_cl(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Non-blocking test of a CTA-local phase.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                             int code) {
+  const unsigned long long t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cl(bar, parity)) return true;
+    if ((it & 63) == 0) {
+      if (abort && *abort) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        if (abort) *abort = 1;
+        record_status(status, code);
+        return false;
+      }
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------------------------- async copies
 // Plain (non-tensor, non-multicast) bulk copy global -> this CTA's shared memory, completing on an mbarrier.
 // Both addresses 16-byte aligned, bytes a multiple of 16.
@@ -381,6 +480,43 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
 __device__ __forceinline__ uint32_t half2_bcast(__half h) {
   __half2 r = __halves2half2(h, h);
   return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// E2M1 x E4M3 -> f16 (exact) -> E4M3 (round to nearest even): 8 values of one code word, one scale.
+__device__ __forceinline__ uint2 f4_word_to_e4m3(uint32_t w, uint32_t scale_h2) {
+  uint32_t h[4];
+  e2m1x8_to_f16x2x4(w, h);
+  const uint32_t e0 = f16x2_to_e4m3x2(hmul2_u32(h[0], scale_h2));
+  const uint32_t e1 = f16x2_to_e4m3x2(hmul2_u32(h[1], scale_h2));
+  const uint32_t e2 = f16x2_to_e4m3x2(hmul2_u32(h[2], scale_h2));
+  const uint32_t e3 = f16x2_to_e4m3x2(hmul2_u32(h[3], scale_h2));
+  return make_uint2(e0 | (e1 << 16), e2 | (e3 << 16));
+}
+
+// NVFP4 -> E4M3 without per-value conversions (conversions share the 16/clk/SM XU pipe with the softmax's exp).
+// For each 16-value block the eight possible products {0, .5, 1, 1.5, 2, 3, 4, 6} x scale are formed once in f16
+// (exact) and rounded to E4M3 (round to nearest even): an 8-byte table in two registers, byte k = code k.  A byte
+// permute with the codes' magnitude nibbles as selector then decodes four values at a time; the sign bits are
+// moved to bit 7 of each byte with a second permute.  Bit-identical to converting each value separately for every
+// non-negative scale (block scales are amax / 6 >= 0 by construction).
+__device__ __forceinline__ uint2 f4_scale_table(uint32_t sb) {
+  const uint32_t s2 = e4m3x2_to_f16x2(static_cast<uint16_t>(sb | (sb << 8)));
+  const uint32_t e01 = f16x2_to_e4m3x2(hmul2_u32(s2, 0x38000000u));   // (0, 0.5)
+  const uint32_t e23 = f16x2_to_e4m3x2(hmul2_u32(s2, 0x3E003C00u));   // (1, 1.5)
+  const uint32_t e45 = f16x2_to_e4m3x2(hmul2_u32(s2, 0x42004000u));   // (2, 3)
+  const uint32_t e67 = f16x2_to_e4m3x2(hmul2_u32(s2, 0x46004400u));   // (4, 6)
+  return make_uint2(e01 | (e23 << 16), e45 | (e67 << 16));
+}
+// Eight E2M1 codes (nibble i = value i) -> eight E4M3 bytes through the block's table.
+__device__ __forceinline__ uint2 f4_decode8(uint32_t w, uint2 tab) {
+  const uint32_t mag = w & 0x77777777u;
+  const uint32_t lo = __byte_perm(tab.x, tab.y, mag);
+  const uint32_t hi = __byte_perm(tab.x, tab.y, mag >> 16);
+  const uint32_t x = w & 0x88888888u;   // sign of value 2k + 1 at bit 7 of byte k
+  const uint32_t y = x << 4;            // sign of value 2k at bit 7 of byte k
+  const uint32_t slo = __byte_perm(y, x, 0x5140);
+  const uint32_t shi = __byte_perm(y, x, 0x7362);
+  return make_uint2(lo | (slo & 0x80808080u), hi | (shi & 0x80808080u));
 }
 
 // E2M1 magnitude code of y >= 0: number of midpoints strictly below y (ties round down), saturating at 7 (= 6.0).

@@ -90,7 +90,11 @@ cudaError_t gqa_decode(const GqaDecodeArgs& a, cudaStream_t s);
 
 // ---- sparse MLA decode (attn_mla_decode.cu): DSA attention over gathered latent rows, H <= 128 heads.
 struct MlaDecodeArgs {
-  const void* q;           // bf16 [T, H, 576]: 512 latent dims then 64 rope dims
+  const void* q;           // bf16 [T, H, 576] (512 latent dims then 64 rope dims), quantized first into q8_out, or null
+  uint8_t* q8_out;         // with q: E4M3 destination (== q8) and q_scale_out (== q_scale)
+  float* q_scale_out;
+  const uint8_t* q8;       // E4M3 [T, H, 576]: q / q_scale
+  const float* q_scale;    // [T, H] per-head scale (amax / 448)
   const uint8_t* pool;     // [rows, 352] NVFP4 latent rows (fmt = kKvNvfp4) or [rows, 576] E4M3 rows (kKvFp8)
   const int* idx;          // [T, idx_stride] pool rows attended by each token; -1 = masked
   void* out;               // bf16 [T, H, 512]
@@ -99,8 +103,10 @@ struct MlaDecodeArgs {
   float* lse_part;         // [num_splits, T, H] log2 units (num_splits > 1)
   int* status;             // device status word (bounded-wait timeouts)
   int T, H, topk, idx_stride, fmt;
+  int pool_rows;           // rows in the pool: an index outside [0, pool_rows) is treated as masked (status kBadIndex)
   int tiles_per_split, num_splits;  // 128-row tiles of the top-k list per split
   float sm_scale;
+  long long* trace;        // optional [40 events x 64 tiles] clock64 timeline of CTA (0, 0, 0), else null
 };
 cudaError_t mla_decode(const MlaDecodeArgs& a, cudaStream_t s);
 
@@ -108,5 +114,6 @@ cudaError_t mla_decode(const MlaDecodeArgs& a, cudaStream_t s);
 cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, int sw64, cudaStream_t s);
 cudaError_t umma_f8_mn_test(const void* A, const void* B, float* C, int N, int K, cudaStream_t s);
 cudaError_t umma_rate_test(int n, int count, int nacc, int ts, long long* out, cudaStream_t s);
+cudaError_t nvfp4_lut_test(const uint32_t* words, int nwords, int* out, cudaStream_t s);
 
 }  // namespace iob

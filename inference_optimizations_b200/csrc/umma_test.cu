@@ -250,3 +250,30 @@ cudaError_t umma_f8_mn_test(const void* A, const void* B, float* C, int N, int K
   return cudaGetLastError();
 }
 }  // namespace iob
+
+// ---------------------------------------------------------------------------------------------------------------
+// NVFP4 -> E4M3 lookup-table decode (f4_scale_table + f4_decode8) against per-value conversion (f4_word_to_e4m3):
+// every non-negative finite E4M3 scale (block scales are amax / 6 >= 0 by construction) x `nwords` code words.
+// out[0] = mismatching words.
+namespace iob {
+namespace {
+__global__ void nvfp4_lut_kernel(const uint32_t* __restrict__ words, int nwords, int* out) {
+  const int scale = blockIdx.x;                              // 0..126
+  if (scale >= 0x7F) return;
+  const uint2 tab = f4_scale_table(static_cast<uint32_t>(scale));
+  const uint32_t s2 = e4m3x2_to_f16x2(static_cast<uint16_t>(scale | (scale << 8)));
+  int bad = 0;
+  for (int i = threadIdx.x; i < nwords; i += blockDim.x) {
+    const uint2 a = f4_decode8(words[i], tab);
+    const uint2 b = f4_word_to_e4m3(words[i], s2);
+    bad += (a.x != b.x) || (a.y != b.y);
+  }
+  if (bad) atomicAdd(out, bad);
+}
+}  // namespace
+
+cudaError_t nvfp4_lut_test(const uint32_t* words, int nwords, int* out, cudaStream_t s) {
+  nvfp4_lut_kernel<<<127, 256, 0, s>>>(words, nwords, out);
+  return cudaGetLastError();
+}
+}  // namespace iob

@@ -17,7 +17,7 @@ from . import formats as F
 from .kvcache import FMT_FP8, FMT_NVFP4
 
 NUM_SMS = 148
-TILE = 128
+TILE = 128                # rows per kernel tile (split granularity and lazy-rescale step)
 ROW_BYTES = {FMT_NVFP4: F.MLA_ROW_BYTES, FMT_FP8: F.MLA_FP8_ROW_BYTES}
 
 
@@ -43,19 +43,27 @@ class MlaWorkspace:
     o_part: torch.Tensor
     lse_part: torch.Tensor
     status: torch.Tensor
+    q8: torch.Tensor           # E4M3 query, quantized per (token, head) by the kernel's first pass
+    q_scale: torch.Tensor
 
     @staticmethod
     def allocate(tokens: int, heads: int, max_splits: int, device="cuda") -> "MlaWorkspace":
         n = max(1, tokens * heads * max_splits)
         return MlaWorkspace(torch.empty(n * 512, dtype=torch.float32, device=device),
                             torch.empty(n, dtype=torch.float32, device=device),
-                            torch.zeros(1, dtype=torch.int32, device=device))
+                            torch.zeros(1, dtype=torch.int32, device=device),
+                            torch.empty(tokens, heads, 576, dtype=torch.uint8, device=device),
+                            torch.empty(tokens, heads, dtype=torch.float32, device=device))
+
+    def fits(self, tokens: int, heads: int, splits: int) -> bool:
+        return (self.q8.shape[0] >= tokens and self.q8.shape[1] == heads
+                and self.lse_part.numel() >= tokens * heads * splits)
 
 
 def mla_decode(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_scale: float, fmt: int = FMT_NVFP4,
                splits: Optional[tuple[int, int]] = None, ws: Optional[MlaWorkspace] = None,
                out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
-               return_lse: bool = False):
+               return_lse: bool = False, trace: Optional[torch.Tensor] = None):
     """q bf16 [T, H, 576], pool uint8 [rows, 352 | 576], idx int32 [T, topk] -> out bf16 [T, H, 512]
     (and lse fp32 [T, H], natural log, with return_lse)."""
     t, h, _ = q.shape
@@ -74,7 +82,9 @@ def mla_decode(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_scale:
     ns, tps = splits
     if ws is None:
         ws = MlaWorkspace.allocate(t, h, ns, device=q.device)
-    ext().mla_decode(q, pool, idx, out, lse, ws.o_part, ws.lse_part, ws.status, fmt, tps, ns, sm_scale)
+    assert ws.fits(t, h, ns), "workspace too small"
+    ext().mla_decode(q.contiguous(), ws.q8[:t], ws.q_scale[:t], pool, idx, out, lse, ws.o_part, ws.lse_part, ws.status,
+                     fmt, tps, ns, sm_scale, trace)
     return (out, lse) if return_lse else out
 
 
@@ -105,3 +115,67 @@ def mla_decode_ref(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_sc
 def mla_sm_scale(qk_head_dim: int = 192) -> float:
     """DeepSeek-style softmax scale: 1 / sqrt(qk_nope_head_dim + qk_rope_head_dim) of the un-absorbed heads."""
     return 1.0 / math.sqrt(qk_head_dim)
+
+
+def _e4m3(x: torch.Tensor) -> torch.Tensor:
+    return x.clamp(-448.0, 448.0).to(torch.float8_e4m3fn).float()
+
+
+def mla_decode_emul_e4m3(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_scale: float,
+                         fmt: int = FMT_NVFP4, tiles_per_split: Optional[int] = None, tau: float = 8.0):
+    """CPU emulation of the kernel's arithmetic: per-(token, head) E4M3 query, rows rounded to E4M3, 128-row tiles
+    with the lazy running max (rescale only when a tile's max exceeds the reference by more than 2^tau),
+    P = 2^(s - m) rounded to E4M3, the row sum over unrounded P; with `tiles_per_split`, each split runs that
+    schedule on its own tiles and the partials merge by their base-2 LSE.  Agrees with the kernel up to fp32
+    accumulation order; used to test the kernel tightly where the fp32 oracle can only bound the E4M3 error."""
+    log2e = 1.4426950408889634
+    qf = q.float().cpu()
+    t, h, _ = qf.shape
+    amax = qf.abs().amax(-1, keepdim=True)
+    qs = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    q8 = _e4m3(qf * (1.0 / qs))
+    ic = idx.cpu().long()
+    ntiles = -(-ic.shape[1] // TILE)
+    tps = tiles_per_split or ntiles
+    ninf = float("-inf")
+    out = torch.zeros(t, h, F.MLA_NOPE)
+    lse = torch.full((t, h), ninf)
+    for i in range(t):
+        parts = []
+        for s0 in range(0, ntiles, tps):
+            m = torch.full((h,), ninf)
+            l = torch.zeros(h)
+            o = torch.zeros(h, F.MLA_NOPE)
+            for j in range(s0, min(ntiles, s0 + tps)):
+                ids = ic[i, j * TILE:(j + 1) * TILE]
+                valid = ids >= 0
+                rows = torch.zeros(ids.numel(), F.MLA_QK)
+                if valid.any():
+                    rows[valid] = dequant_rows(pool[ids[valid].to(pool.device)].cpu(), fmt)
+                k8 = _e4m3(rows)
+                sc = (q8[i] @ k8.T) * (qs[i] * sm_scale * log2e)
+                sc[:, ~valid] = ninf
+                mt = sc.max(-1).values
+                first = (m == ninf) & (mt > ninf)
+                grow = (m > ninf) & (mt > m + tau)
+                alpha = torch.where(grow, torch.exp2(m - mt), torch.ones_like(m))
+                m = torch.where(first | grow, mt, m)
+                l = l * alpha
+                o = o * alpha[:, None]
+                p = torch.where(sc == ninf, torch.zeros_like(sc), torch.exp2(sc - m[:, None]))
+                l = l + p.sum(-1)
+                o = o + _e4m3(p) @ k8[:, :F.MLA_NOPE]
+            ok = l > 0
+            on = torch.where(ok[:, None], o / l.clamp(min=1e-30)[:, None], torch.zeros_like(o))
+            parts.append((on, torch.where(ok, m + torch.log2(l.clamp(min=1e-30)), torch.full_like(m, ninf))))
+        lmax = torch.stack([p[1] for p in parts]).max(0).values
+        num = torch.zeros(h, F.MLA_NOPE)
+        den = torch.zeros(h)
+        for on, l2 in parts:
+            w = torch.where(l2 == ninf, torch.zeros_like(l2), torch.exp2(l2 - lmax))
+            num += w[:, None] * on
+            den += w
+        ok = den > 0
+        out[i] = torch.where(ok[:, None], num / den.clamp(min=1e-30)[:, None], torch.zeros_like(num))
+        lse[i] = torch.where(ok, (lmax + torch.log2(den.clamp(min=1e-30))) / log2e, torch.full_like(den, ninf))
+    return out.to(q.device), lse.to(q.device)

@@ -26,7 +26,7 @@ setup(
             name="inference_optimizations_b200._C",
             sources=sources,
             include_dirs=[os.path.join(HERE, CSRC)],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS + os.environ.get("IOB_EXTRA_NVCC", "").split()},
             libraries=["cuda"],
         )
     ],

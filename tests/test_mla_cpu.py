@@ -55,8 +55,8 @@ def test_reference_masks_and_matches_dense():
 
 
 def test_split_policy_fills_sms():
-    assert M.mla_split_policy(64, 2048) == (1, 16)          # 128 CTAs: one wave already
+    assert M.mla_split_policy(64, 2048) == (1, 2048 // M.TILE)     # 128 CTAs: one wave already
     ns, tps = M.mla_split_policy(1, 2048)
-    assert ns * tps >= 16 and 2 * ns <= 148 and ns > 4
+    assert ns * tps * M.TILE >= 2048 and 2 * ns <= 148 and ns > 4
     ns, tps = M.mla_split_policy(8, 200)
-    assert ns * tps * 128 >= 200
+    assert ns * tps * M.TILE >= 200
