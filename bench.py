@@ -77,10 +77,19 @@ def main() -> int:
                  all_reduce=D.nccl_all_reduce if tp > 1 else None,
                  argmax_merge=D.argmax_merge if tp > 1 else None)
     synth_decode_sessions(eng, args.sessions, args.ctx, max_new, seed=1)
+    eng.runner.warm_graphs(args.sessions)
     torch.cuda.synchronize()
     for _ in range(warm):
         eng.step()
-    launches = eng.runner.count_step_launches(eng.runner._bucket(args.sessions))
+    # the adaptive speculation policy probes, prices and decides before the timed steps (all ranks alike)
+    extra = 0
+    while ecfg.spec and eng.spec_policy.decided is None and extra < 64:
+        eng.step()
+        extra += 1
+    bucket = eng.runner._bucket(args.sessions)
+    launches_by_kind = {k: eng.runner.count_step_launches(bucket, k) for k in (("spec", "decode") if ecfg.spec
+                                                                                else ("decode",))}
+    n_stats = len(eng.stats)
     torch.cuda.synchronize()
     if tp > 1:
         torch.distributed.barrier()
@@ -96,6 +105,8 @@ def main() -> int:
         out = eng.step()
         toks += sum(len(v) for v in out.values())
     ev1.record()
+    kinds = [st.kind for st in eng.stats[n_stats:]]
+    launches = sum(launches_by_kind.get(k, 0) for k in kinds)
     torch.cuda.synchronize()
     if tp > 1:
         torch.distributed.barrier()
@@ -154,13 +165,19 @@ def main() -> int:
                    "samples": ck.get("samples")},
         "e2e": {"value": round(toks / (e2e_ms / 1e3), 2), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "api": "Engine.step()"},
-        "gpu_launches": launches * steps,
+        "gpu_launches": launches,
         "impl": "ours",
     }
     if decode_only is not None:
         res["decode_only"] = decode_only
+        hist = eng.spec_policy.history[-1] if eng.spec_policy.history else {}
+        res["config"]["spec_policy"] = {
+            "mode": ecfg.spec_policy, "timed_steps": {k: kinds.count(k) for k in set(kinds)},
+            "probe": {k: (round(v, 5) if isinstance(v, float) else v) for k, v in hist.items()}}
         res["config"]["spec_note"] = ("random-init draft head: acceptance is whatever the untrained draft achieves "
-                                      "against the random-init target (measured above)")
+                                      "against the random-init target; the adaptive policy (speculate only while "
+                                      "n * E[tokens] / t(step) beats plain decode) priced both modes before the "
+                                      "timed steps")
     bad = rejected(ck)
     if bad:
         res["clocks"]["rejected"] = bad

@@ -185,6 +185,7 @@ class EngineConfig:
     # speculative decoding
     spec: bool = False
     draft_tokens: int = 3
+    spec_policy: str = "adaptive"        # "adaptive": speculate only while it beats plain decode; "always"
     # runtime
     cuda_graphs: bool = True
     graph_batch_sizes: str = "1,2,4,8,16,32,64"

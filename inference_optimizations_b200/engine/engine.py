@@ -15,11 +15,12 @@ import torch
 from ..config import EngineConfig, GQAConfig, MLAMoEConfig, model_config
 from .runner import GQARunner
 from .scheduler import Request, SamplingParams, Scheduler
+from .spec_policy import SpecPolicy
 
 
 @dataclass
 class StepStats:
-    kind: str
+    kind: str                     # "prefill" | "decode" | "spec"
     tokens_out: int
     seconds: float
 
@@ -40,6 +41,7 @@ class Engine:
                                can_admit=self.runner.can_admit)
         self.stats: list[StepStats] = []
         self.finished: list[Request] = []
+        self.spec_policy = SpecPolicy(ecfg.draft_tokens, ecfg.spec_policy)
 
     def add_request(self, prompt: list, params: Optional[SamplingParams] = None) -> Request:
         return self.sched.new_request(prompt, params or SamplingParams())
@@ -56,13 +58,29 @@ class Engine:
             out = {rid: [t] for rid, t in nxt.items()}
         else:
             reqs = [s.req for s in batch.segments]
-            out = self.runner.spec_decode(reqs) if self.runner.spec else self.runner.decode(reqs)
+            spec_on = getattr(self.runner, "spec", False)
+            kind = "decode"
+            if spec_on and self.spec_policy.use_spec(
+                    [r.rid for r in reqs], can_spec=not any(r.draft_state.get("stale") for r in reqs),
+                    can_price=all(self.runner.draft_row(r) <= 3 for r in reqs)):
+                before = sum(r.accepted for r in reqs)
+                t1 = time.perf_counter()
+                kind = "spec"
+                out = self.runner.spec_decode(reqs)
+                self.spec_policy.observe_spec((sum(r.accepted for r in reqs) - before) / len(reqs),
+                                              time.perf_counter() - t1)
+            else:
+                t1 = time.perf_counter()
+                out = self.runner.decode(reqs)
+                if spec_on:
+                    self.spec_policy.observe_plain(time.perf_counter() - t1)
             self.sched.commit_decode(out)
         for r in [s.req for s in batch.segments]:
             if r.finished and r not in self.finished:
                 self.finished.append(r)
                 self.runner.detach(r)
-        self.stats.append(StepStats(batch.kind, sum(len(v) for v in out.values()), time.perf_counter() - t0))
+        self.stats.append(StepStats(batch.kind if batch.kind == "prefill" else kind,
+                                    sum(len(v) for v in out.values()), time.perf_counter() - t0))
         return out
 
     def generate(self, prompts: list, params: Optional[SamplingParams] = None, max_steps: int = 1 << 30) -> list:

@@ -268,8 +268,35 @@ class GQARunner:
         if self.device.type == "cuda":
             torch.cuda.current_stream().synchronize()
         res = {r.rid: [int(self.out_host[i])] for i, r in enumerate(reqs)}
+        if self.spec:
+            self._keep_draft_inputs(reqs)
         self._trim([Segment(r, r.kv_len, [0], False) for r in reqs])
         return res
+
+    def draft_row(self, r) -> int:
+        """Row of the stored target hiddens that a plain decode step of `r` fills: the next draft extend covers
+        positions [ld, L] with inputs h_{ld-1} .. h_{L-1} in rows 0 .. L - ld."""
+        return r.kv_len - r.draft_state.get("ld", r.kv_len) + 1
+
+    def _keep_draft_inputs(self, reqs: list) -> None:
+        """After a plain decode step on a speculative engine: store each request's new target hidden where the next
+        draft extend reads it, or mark the request's draft stale when the extend window (4 positions) is full."""
+        if not hasattr(self, "hbuf"):
+            self._init_spec()
+        h = self.cfg.hidden
+        if all(r.draft_state.get("stale") for r in reqs):
+            return
+        dummy = self.hbuf.shape[0] - 1
+        idx = []
+        for r in reqs:
+            row = self.draft_row(r)
+            if 0 <= row <= 3 and not r.draft_state.get("stale"):
+                idx.append(r.slot * 4 + row)
+            else:
+                r.draft_state["stale"] = True
+                idx.append(dummy * 4)
+        dev = torch.tensor(idx, dtype=torch.long).to(self.device, non_blocking=True)
+        self.hbuf.view(-1, h).index_copy_(0, dev, self.dec_resid[:len(reqs)])
 
     def _timed(self, fn: Callable) -> None:
         """Run a step body; when `self.event_log` is a list, bracket it with CUDA events (device time of the step
@@ -283,10 +310,12 @@ class GQARunner:
         else:
             fn()
 
-    def count_step_launches(self, bucket: int) -> int:
-        """Kernel launches of one decode step body (run eagerly under the counter)."""
+    def count_step_launches(self, bucket: int, kind: Optional[str] = None) -> int:
+        """Kernel launches (of this package's extension) in one decode step body, run eagerly under the counter;
+        kind "spec" | "decode" (default: the engine's configured mode)."""
         from .._ext import count_launches
-        body = self._spec_body(bucket) if self.spec else self._decode_body(bucket)
+        spec = self.spec if kind is None else kind == "spec"
+        body = self._spec_body(bucket) if spec else self._decode_body(bucket)
         with count_launches() as c:
             body()
         return c.n
@@ -303,6 +332,8 @@ class GQARunner:
         def body():
             x, resid = self._target(st)
             self._greedy(x, self.out_ids)
+            if self.spec:
+                self.dec_resid[:bucket].copy_(resid[:bucket])
         return body
 
     def _decode_fn(self, bucket: int) -> Callable:
@@ -316,6 +347,24 @@ class GQARunner:
         fn = self._capture(body)
         self.graphs[key] = fn
         return fn
+
+    def warm_graphs(self, n: int) -> None:
+        """Capture the decode (and speculative) graphs of n's batch bucket on padding-only inputs (no KV writes, the
+        dummy request row), so that capture never lands inside a timed or policy-priced step."""
+        bucket = self._bucket(n)
+        self.stage.fill(self._pack([], 1, ("global", "swa"), pad_groups_to=bucket))
+        self.stage.upload()
+        self._decode_fn(bucket)
+        if self.spec:
+            if not hasattr(self, "hbuf"):
+                self._init_spec()
+            for st, nq, kinds in ((self.st_ext, 4, ("draft",)), (self.st_d2, 1, ("draft",)),
+                                  (self.st_d3, 1, ("draft",)), (self.st_ver, 4, ("global", "swa"))):
+                st.fill(self._pack([], nq, kinds, pad_groups_to=bucket))
+                st.upload()
+            self._spec_fn(bucket)
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
 
     def _capture(self, body: Callable) -> Callable:
         s = torch.cuda.Stream()
@@ -354,6 +403,8 @@ class GQARunner:
         self.spec_out = torch.zeros(self.max_running, 7, dtype=torch.int32, device=self.device)
         pin = self.device.type == "cuda"
         self.spec_out_host = torch.zeros(self.max_running, 7, dtype=torch.int32, pin_memory=pin)
+        self.dec_resid = torch.zeros(max(self.ecfg.graph_sizes() + [self.max_running]), h, dtype=torch.bfloat16,
+                                     device=self.device)
 
     def _draft_prefill(self, batch: Batch, p: Packed, resid: torch.Tensor, st: StepTensors) -> None:
         """Fill the draft layer's KV over each prefill segment: draft input at position q is (token q, target hidden

@@ -62,3 +62,34 @@ def test_speculative_decoding_preserves_greedy_output():
             seq.append(ta)
     steps = [r for r in eng.finished]
     assert all(r.spec_steps > 0 for r in steps)
+
+
+def test_spec_policy_math_and_switching():
+    from inference_optimizations_b200.engine.spec_policy import SpecPolicy, expected_tokens, geometric_p
+    assert geometric_p(0.0, 3) == 0.0 and geometric_p(3.0, 3) == 1.0
+    p = geometric_p(1.5, 3)
+    assert abs(p + p * p + p ** 3 - 1.5) < 1e-9
+    assert expected_tokens(0.0, 4) == 1.0 and abs(expected_tokens(p, 4) - 2.5) < 1e-9
+    # no acceptance: speculation (1.3x slower per step) loses -> plain decode until the running set changes
+    pol = SpecPolicy(3, probe_steps=3)
+    rids = [1, 2]
+    modes = []
+    for _ in range(8):
+        spec = pol.use_spec(rids)
+        modes.append(spec)
+        if spec:
+            pol.observe_spec(0.0, 1.3)
+        else:
+            pol.observe_plain(1.0)
+    assert modes[:3] == [True] * 3 and not any(modes[3:])
+    assert pol.history[-1]["spec"] is False
+    assert pol.use_spec([1, 2, 3]) is True             # new running set: probe again
+    # high acceptance: 2.5 tokens per 1.3x step beats plain
+    pol = SpecPolicy(3, probe_steps=3)
+    for _ in range(6):
+        if pol.use_spec(rids):
+            pol.observe_spec(1.5, 1.3)
+        else:
+            pol.observe_plain(1.0)
+    assert pol.use_spec(rids) is True and pol.history[-1]["gain"] > 1.5
+    assert SpecPolicy(3, "always").use_spec(rids) is True
