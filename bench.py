@@ -132,7 +132,8 @@ def main() -> int:
                        "note": "plain greedy decode of the same sessions (no draft/verify)"}
     stage = eng.runner.stage
     h2d = stage.h2d_bytes() + (sum(t.bytes_synced for t in eng.runner.kv.tables.values()) - table0) // steps
-    d2h = 4 * args.sessions * (1 + (ecfg.draft_tokens if ecfg.spec else 0))
+    # per-step result reads: 4 B per session for a plain step, 7 int32 per session for a speculative step
+    d2h = sum(4 * args.sessions * (7 if k == "spec" else 1) for k in kinds) // max(1, len(kinds))
     value = toks / (dev_ms / 1e3)
     accept = None
     if ecfg.spec:
