@@ -126,7 +126,8 @@ void index_key_write(const at::Tensor& k, const at::Tensor& slot, at::Tensor poo
   req(k, at::kBFloat16, "k");
   req(slot, at::kInt, "slot");
   req(pool, at::kByte, "pool");
-  TORCH_CHECK(k.size(-1) == 128 && k.stride(-1) == 1 && pool.size(-1) == 132, "shape");
+  TORCH_CHECK(k.size(-1) == 128 && k.stride(-1) == 1 && pool.size(-1) == 64 * 132 && pool.is_contiguous(),
+              "k [T, 128], pool [pages, 64 x 132]");
   const at::cuda::CUDAGuard g(k.device());
   CHECK_CUDA_OK(iob::index_key_write(k.data_ptr(), k.stride(0), slot.data_ptr<int>(), pool.data_ptr<uint8_t>(),
                                      k.size(0), stream()));
@@ -245,6 +246,44 @@ void mla_decode(c10::optional<at::Tensor> q, at::Tensor q8, at::Tensor q_scale, 
   CHECK_CUDA_OK(iob::mla_decode(a, stream()));
 }
 
+void indexer(const at::Tensor& q8, const at::Tensor& w, const at::Tensor& pool, const at::Tensor& page_table,
+             c10::optional<at::Tensor> req_idx, const at::Tensor& limit, at::Tensor scores, at::Tensor out_slots,
+             c10::optional<at::Tensor> out_pos, at::Tensor status, int64_t tiles_per_cta, int64_t max_tiles,
+             int64_t do_logits, int64_t do_topk) {
+  req(q8, at::kByte, "q8");
+  req(w, at::kFloat, "w");
+  req(pool, at::kByte, "pool");
+  req(page_table, at::kInt, "page_table");
+  req(limit, at::kInt, "limit");
+  req(scores, at::kFloat, "scores");
+  req(out_slots, at::kInt, "out_slots");
+  req(status, at::kInt, "status");
+  TORCH_CHECK(q8.dim() == 3 && q8.size(2) == 128 && q8.is_contiguous(), "q8 [T, Hi, 128]");
+  TORCH_CHECK(pool.size(-1) == 64 * 132 || (pool.dim() == 1 && pool.numel() % (64 * 132) == 0), "index pool pages");
+  iob::IndexerArgs a{};
+  a.q8 = q8.data_ptr<uint8_t>();
+  a.w = w.data_ptr<float>();
+  a.pool = pool.data_ptr<uint8_t>();
+  a.page_table = page_table.data_ptr<int>();
+  if (req_idx.has_value()) { req(*req_idx, at::kInt, "req_idx"); a.req_idx = req_idx->data_ptr<int>(); }
+  a.limit = limit.data_ptr<int>();
+  a.scores = scores.data_ptr<float>();
+  a.out_slots = out_slots.data_ptr<int>();
+  if (out_pos.has_value()) { req(*out_pos, at::kInt, "out_pos"); a.out_pos = out_pos->data_ptr<int>(); }
+  a.status = status.data_ptr<int>();
+  a.T = q8.size(0);
+  a.Hi = q8.size(1);
+  a.pt_stride = page_table.size(1);
+  a.score_stride = scores.size(1);
+  a.tiles_per_cta = tiles_per_cta;
+  a.max_tiles = max_tiles;
+  a.topk = out_slots.size(1);
+  TORCH_CHECK(scores.size(0) >= a.T && out_slots.size(0) >= a.T && w.numel() >= a.T * a.Hi, "shapes");
+  const at::cuda::CUDAGuard g(q8.device());
+  if (do_logits) CHECK_CUDA_OK(iob::indexer_logits(a, stream()));
+  if (do_topk) CHECK_CUDA_OK(iob::indexer_topk(a, stream()));
+}
+
 void umma_gemm_test(const at::Tensor& A, const at::Tensor& B, at::Tensor C, int64_t sw64) {
   req(A, at::kBFloat16, "A");
   req(B, at::kBFloat16, "B");
@@ -290,6 +329,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("index_key_write", &index_key_write);
   m.def("gqa_decode", &gqa_decode);
   m.def("mla_decode", &mla_decode);
+  m.def("indexer", &indexer);
   m.def("umma_gemm_test", &umma_gemm_test);
   m.def("umma_f8_mn_test", &umma_f8_mn_test);
   m.def("nvfp4_lut_test", &nvfp4_lut_test);

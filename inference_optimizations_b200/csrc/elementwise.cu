@@ -344,12 +344,15 @@ __global__ void index_key_kernel(const __nv_bfloat16* __restrict__ k, int k_stri
   }
   amax = fmaxf(warp_max(amax), 1e-10f);
   const float sc = amax / 448.f;
-  uint8_t* row = pool + (size_t)s * 132;
+  // page-blocked layout: [64 x 128 B values, 16-byte chunk c of row r at c ^ (r & 7)][64 x fp32 scales]
+  uint8_t* page = pool + (size_t)(s >> 6) * (64 * 132);
+  const int r = s & 63;
   uint32_t w = 0;
 #pragma unroll
   for (int j = 0; j < 4; ++j) w |= static_cast<uint32_t>(float_to_e4m3(v[j] / sc)) << (8 * j);
-  *reinterpret_cast<uint32_t*>(row + lane * 4) = w;
-  if (lane == 0) *reinterpret_cast<float*>(row + 128) = sc;
+  const int byte = lane * 4;
+  *reinterpret_cast<uint32_t*>(page + r * 128 + (((byte >> 4) ^ (r & 7)) << 4) + (byte & 15)) = w;
+  if (lane == 0) *reinterpret_cast<float*>(page + 64 * 128 + 4 * r) = sc;
 }
 
 }  // namespace

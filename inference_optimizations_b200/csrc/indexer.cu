@@ -1,0 +1,302 @@
+// DSA lightning indexer: per-token relevance scores over the cached positions, then the top-k positions as pool slots.
+//
+// Semantics (the reference's indexer, `negative-results/code/idx_epilogue/triton_mla_logits.py:1-12` and the
+// DeepGEMM paged MQA-logits interface it patches): for query token t with Hi <= 64 indexer heads,
+//     score[t, j] = k_scale[j] * sum_h w[t, h] * relu(q[t, h] . k[j])          for positions j < limit[t]
+// with E4M3 queries (the per-(token, head) query scale folded into w by the caller) and the 132-byte E4M3 keys
+// (128 values + fp32 scale) of the index pool.  Then the `topk` highest-scoring positions per token (ties: lower
+// position first; fewer positions than topk -> all of them, padded with -1), emitted as pool slots through the page
+// table, in ascending position order.
+//
+// indexer_logits_kernel: the index pool stores each 64-token page as [64 x 128 B values in the 128-byte-swizzle
+// order][64 x fp32 scales] (ops/kvcache.py), so one plain bulk copy per page lands a ready K-major UMMA operand.
+// Swap-AB kind::f8f6f4 UMMA: D[128 positions x 64 heads] = K[128 x 128] Q^T (4 MMAs of K = 32), double-buffered
+// in TMEM; four epilogue warps (thread = position = TMEM lane) apply relu, the head weights and the key scale.
+// One producer thread streams pages through a 4-stage ring.  Memory-bound by design: 132 B per position.
+//
+// indexer_topk_kernel: one CTA per token, radix select on the order-preserving integer image of the fp32 scores
+// (12 + 12 + 8 bits, shared-memory histograms), then a position-ordered compaction.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace iob {
+namespace {
+
+constexpr int kITile = 128;                 // positions per tile (two pages)
+constexpr int kIStages = 4;
+constexpr int kIStageBytes = 2 * 64 * 128;  // values of two pages
+constexpr int kIThreads = 192;              // warp 0 producer, warp 1 MMA, warps 2..5 epilogue
+constexpr int kIPageBytes = 64 * 132;
+
+struct IdxSmem {
+  uint64_t full[kIStages], empty[kIStages];
+  uint64_t d_full[2], d_empty[2];
+  uint64_t q_ready, fin;
+  float scales[kIStages][kITile];
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int DUMMY = 0>
+__global__ void __launch_bounds__(kIThreads, 1) indexer_logits_kernel(const IndexerArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = base;                                   // kIStages x 16 KB
+  uint8_t* sq = ring + kIStages * kIStageBytes;           // Q: 64 heads x 128 B, SW128
+  IdxSmem& sm = *reinterpret_cast<IdxSmem*>(sq + 64 * 128);
+
+  const int t = blockIdx.y;
+  const int limit = a.limit[t];
+  const int ntile_all = (limit + kITile - 1) / kITile;
+  const int tile0 = blockIdx.x * a.tiles_per_cta;
+  const int ntiles = min(ntile_all, tile0 + a.tiles_per_cta) - tile0;
+  if (ntiles <= 0) return;
+  const int warp = warp_id(), lane = lane_id();
+  const int* pt = a.page_table + static_cast<size_t>(a.req_idx ? a.req_idx[t] : t) * a.pt_stride;
+  const int n_pages = (limit + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kIStages; ++i) { mbar_init(&sm.full[i], 1); mbar_init(&sm.empty[i], 1 + 4); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&sm.d_full[i], 1); mbar_init(&sm.d_empty[i], 4); }
+    mbar_init(&sm.q_ready, 4);
+    mbar_init(&sm.fin, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) { tmem_alloc(&sm.tmem_base, 128); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* abort = &sm.abort;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer: two pages per tile
+    if (lane == 0) {
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % kIStages;
+        if (j >= kIStages && !mbar_wait(&sm.empty[st], ((j / kIStages) - 1) & 1, abort, a.status, kTimeoutProducer))
+          break;
+        uint32_t bytes = 0;
+        int phys[2];
+        for (int pg = 0; pg < 2; ++pg) {
+          const int lp = 2 * (tile0 + j) + pg;
+          phys[pg] = lp < n_pages ? pt[lp] : -1;
+          if (phys[pg] >= 0) bytes += 64 * 128 + 64 * 4;
+        }
+        if (bytes) mbar_expect_tx(&sm.full[st], bytes);
+        for (int pg = 0; pg < 2; ++pg) {
+          if (phys[pg] < 0) continue;
+          const uint8_t* page = a.pool + static_cast<size_t>(phys[pg]) * kIPageBytes;
+          bulk_g2s(ring + st * kIStageBytes + pg * 64 * 128, page, 64 * 128, &sm.full[st]);
+          bulk_g2s(&sm.scales[st][64 * pg], page + 64 * 128, 64 * 4, &sm.full[st]);
+        }
+        if (!bytes) mbar_arrive(&sm.full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      const uint32_t idesc = idesc_dense(0, 0, 128, 64);
+      const uint32_t ring_a = smem_u32(ring), q_a = smem_u32(sq);
+      bool ok = mbar_wait(&sm.q_ready, 0, abort, a.status, kTimeoutMma);
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int st = j % kIStages, db = j & 1;
+        if (!(ok = mbar_wait(&sm.full[st], (j / kIStages) & 1, abort, a.status, kTimeoutMma))) break;
+        if (j >= 2 && !(ok = mbar_wait(&sm.d_empty[db], ((j >> 1) - 1) & 1, abort, a.status, kTimeoutMma))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f8_ss(tmem + 64 * db, desc_sw128(ring_a + st * kIStageBytes + 32 * kk), desc_sw128(q_a + 32 * kk), idesc,
+                     kk > 0 ? 1u : 0u);
+        umma_commit(&sm.d_full[db]);
+        umma_commit(&sm.empty[st]);
+      }
+      umma_commit(&sm.fin);            // every issued MMA has completed before TMEM is released
+      mbar_wait(&sm.fin, 0, nullptr, a.status, kTimeoutMma);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue: thread = position in tile
+    const int quad = warp & 3;                    // TMEM lane quadrant this warp may access
+    const int row = 32 * quad + lane;             // position within the tile
+    const uint32_t lane_base = static_cast<uint32_t>(32 * quad) << 16;
+    // Q [64 heads x 128 B] (head h = row of the B operand) -> SW128 shared memory, zero beyond Hi
+    for (int i = threadIdx.x - 64; i < 64 * 8; i += 128) {
+      const int h = i >> 3, c = i & 7;
+      const uint4 v = h < a.Hi ? *reinterpret_cast<const uint4*>(a.q8 + (static_cast<size_t>(t) * a.Hi + h) * 128 + 16 * c)
+                               : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(sq + sw128_chunk(h, c)) = v;
+    }
+    float w[64];
+#pragma unroll
+    for (int h = 0; h < 64; ++h) w[h] = h < a.Hi ? a.w[static_cast<size_t>(t) * a.Hi + h] : 0.f;
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.q_ready);
+    float* out = a.scores + static_cast<size_t>(t) * a.score_stride;
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j % kIStages, db = j & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.d_full[db], (j >> 1) & 1, abort, a.status, kTimeoutConsumer))) break;
+      tc_fence_after();
+      uint32_t d[64];
+      tmem_ld32(tmem + lane_base + 64 * db, d);
+      tmem_ld32(tmem + lane_base + 64 * db + 32, d + 32);
+      tmem_ld_wait();
+      // the key scales came in with the stage's bulk copies: acquire that phase here too before reading them
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.full[st], (j / kIStages) & 1, abort, a.status, kTimeoutConsumer))) break;
+      const float ks = sm.scales[st][row];
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) { mbar_arrive(&sm.d_empty[db]); mbar_arrive(&sm.empty[st]); }
+      float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+#pragma unroll
+      for (int h = 0; h < 64; h += 4) {
+        acc0 = fmaf(w[h], fmaxf(__uint_as_float(d[h]), 0.f), acc0);
+        acc1 = fmaf(w[h + 1], fmaxf(__uint_as_float(d[h + 1]), 0.f), acc1);
+        acc2 = fmaf(w[h + 2], fmaxf(__uint_as_float(d[h + 2]), 0.f), acc2);
+        acc3 = fmaf(w[h + 3], fmaxf(__uint_as_float(d[h + 3]), 0.f), acc3);
+      }
+      const int pos = (tile0 + j) * kITile + row;
+      if (pos < a.score_stride) out[pos] = pos < limit ? ks * ((acc0 + acc1) + (acc2 + acc3)) : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr int kKThreads = 1024;
+
+// Block-wide exclusive prefix sum of one int per thread (1024 threads); returns the total through `total`.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int& total) {
+  const int lane = lane_id(), warp = warp_id();
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int ws = warp_sums[lane];
+    int wincl = ws;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, wincl, o);
+      if (lane >= o) wincl += n;
+    }
+    warp_sums[lane] = wincl - ws;
+    if (lane == 31) warp_sums[32] = wincl;
+  }
+  __syncthreads();
+  const int res = warp_sums[warp] + incl - v;
+  total = warp_sums[32];
+  __syncthreads();
+  return res;
+}
+
+__global__ void __launch_bounds__(kKThreads) indexer_topk_kernel(const IndexerArgs a) {
+  __shared__ int hist[4096];
+  __shared__ int warp_sums[33];
+  __shared__ int sel_bin, sel_above;
+  const int t = blockIdx.x;
+  const int L = min(a.limit[t], a.score_stride);
+  const int K = a.topk;
+  const float* sc = a.scores + static_cast<size_t>(t) * a.score_stride;
+  const int* pt = a.page_table + static_cast<size_t>(a.req_idx ? a.req_idx[t] : t) * a.pt_stride;
+  int* out = a.out_slots + static_cast<size_t>(t) * K;
+  int* out_pos = a.out_pos ? a.out_pos + static_cast<size_t>(t) * K : nullptr;
+  auto emit = [&](int i, int p) {
+    out[i] = p >= 0 ? pt[p >> 6] * 64 + (p & 63) : -1;
+    if (out_pos) out_pos[i] = p;
+  };
+  if (L <= K) {
+    for (int i = threadIdx.x; i < K; i += kKThreads) emit(i, i < L ? i : -1);
+    return;
+  }
+  // ---- radix select of the K-th largest order key: 12 + 12 + 8 bits
+  uint32_t prefix = 0, mask = 0;
+  int remaining = K;
+  const int shifts[3] = {20, 8, 0};
+  const int widths[3] = {12, 12, 8};
+#pragma unroll 1
+  for (int pass = 0; pass < 3; ++pass) {
+    const int sh = shifts[pass], nb = 1 << widths[pass];
+    for (int b = threadIdx.x; b < 4096; b += kKThreads) hist[b] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < L; i += kKThreads) {
+      const uint32_t u = order_key(sc[i]);
+      if ((u & mask) == prefix) atomicAdd(&hist[(u >> sh) & (nb - 1)], 1);
+    }
+    __syncthreads();
+    // suffix sums from the top bin: each thread owns 4 consecutive bins (nb / 1024 <= 4)
+    const int per = nb / kKThreads > 0 ? nb / kKThreads : 1;
+    const int b0 = nb - (threadIdx.x + 1) * per;       // thread 0 owns the highest bins
+    int mine = 0;
+    if (b0 >= 0)
+      for (int k = 0; k < per; ++k) mine += hist[b0 + k];
+    int total;
+    const int above = block_exclusive_scan(mine, warp_sums, total);   // count in bins higher than this thread's
+    if (b0 >= 0 && above < remaining && above + mine >= remaining) {
+      int acc = above;
+      for (int k = per - 1; k >= 0; --k) {
+        const int c = hist[b0 + k];
+        if (acc + c >= remaining) { sel_bin = b0 + k; sel_above = acc; break; }
+        acc += c;
+      }
+    }
+    __syncthreads();
+    remaining -= sel_above;
+    prefix |= static_cast<uint32_t>(sel_bin) << sh;
+    mask |= static_cast<uint32_t>(nb - 1) << sh;
+    __syncthreads();
+  }
+  // ---- compaction in position order: keys above the threshold, then the first `remaining` equal ones
+  const int chunk = (L + kKThreads - 1) / kKThreads;
+  const int i0 = threadIdx.x * chunk, i1 = min(L, i0 + chunk);
+  int gt = 0, eq = 0;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t u = order_key(sc[i]);
+    gt += u > prefix;
+    eq += u == prefix;
+  }
+  int tot;
+  const int eq_before = block_exclusive_scan(eq, warp_sums, tot);
+  const int take_eq = max(0, min(eq, remaining - eq_before));
+  const int off = block_exclusive_scan(gt + take_eq, warp_sums, tot);
+  int w = off, eq_seen = 0;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t u = order_key(sc[i]);
+    if (u > prefix || (u == prefix && eq_seen++ < take_eq)) emit(w++, i);
+  }
+}
+
+}  // namespace
+
+cudaError_t indexer_logits(const IndexerArgs& a, cudaStream_t s) {
+  if (a.T == 0) return cudaSuccess;
+  if (a.Hi < 1 || a.Hi > 64 || a.tiles_per_cta < 1 || a.max_tiles < 1 || a.T > 65535) return cudaErrorInvalidValue;
+  const int smem = 1024 + kIStages * kIStageBytes + 64 * 128 + static_cast<int>(sizeof(IdxSmem));
+  auto kern = indexer_logits_kernel<0>;
+  IOB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  kern<<<dim3((a.max_tiles + a.tiles_per_cta - 1) / a.tiles_per_cta, a.T), kIThreads, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t indexer_topk(const IndexerArgs& a, cudaStream_t s) {
+  if (a.T == 0) return cudaSuccess;
+  if (a.topk < 1) return cudaErrorInvalidValue;
+  indexer_topk_kernel<<<a.T, kKThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace iob

@@ -110,6 +110,25 @@ struct MlaDecodeArgs {
 };
 cudaError_t mla_decode(const MlaDecodeArgs& a, cudaStream_t s);
 
+// ---- DSA lightning indexer (indexer.cu): scores over the cached positions, then top-k positions as pool slots.
+struct IndexerArgs {
+  const uint8_t* q8;       // E4M3 [T, Hi, 128] indexer queries
+  const float* w;          // [T, Hi] head weights (the query scale folded in)
+  const uint8_t* pool;     // index pool [pages, 64 x 132 B] (values swizzled per page, then scales)
+  const int* page_table;   // [rows, pt_stride]
+  const int* req_idx;      // [T] page-table row of each token (null: row t)
+  const int* limit;        // [T] visible positions 0 .. limit - 1
+  float* scores;           // [T, score_stride] fp32 (logits output / top-k input)
+  int* out_slots;          // [T, topk] pool slots, -1 padded
+  int* out_pos;            // [T, topk] positions (optional)
+  int* status;
+  int T, Hi, pt_stride, score_stride;
+  int tiles_per_cta, max_tiles;   // 128-position tiles per CTA; tiles of the longest token
+  int topk;
+};
+cudaError_t indexer_logits(const IndexerArgs& a, cudaStream_t s);
+cudaError_t indexer_topk(const IndexerArgs& a, cudaStream_t s);
+
 // ---- primitive check (umma_test.cu): C[M, N] fp32 = A[M, K] * B[N, K]^T, bf16 inputs, one CTA per 128 rows.
 cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, int sw64, cudaStream_t s);
 cudaError_t umma_f8_mn_test(const void* A, const void* B, float* C, int N, int K, cudaStream_t s);

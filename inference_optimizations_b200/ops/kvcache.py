@@ -150,9 +150,40 @@ def mla_write(nope: torch.Tensor, rope: torch.Tensor, slot: torch.Tensor, pool: 
     pool[slot[keep].long()] = rows[keep]
 
 
+# DSA indexer key pool: 132 bytes per token (128 E4M3 values + fp32 scale, `F.index_key_quantize`), stored per
+# 64-token page as [64 x 128 B values][64 x fp32 scales] = 8448 B, the values of row r in the 128-byte-swizzle order
+# (16-byte chunk c at c ^ (r & 7)).  A page is then a ready K-major tensor-core operand for one plain bulk copy.
+INDEX_PAGE_BYTES = 64 * F.INDEX_ROW_BYTES
+
+
+def index_pool_offsets(slot: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Byte offsets (values [n, 128], scale [n]) of the tokens in `slot` inside a flat index pool."""
+    s = slot.long()
+    page, r = s // 64, s % 64
+    b = torch.arange(128, device=s.device)
+    chunk = (b // 16)[None, :] ^ (r % 8)[:, None]
+    vals = page[:, None] * INDEX_PAGE_BYTES + r[:, None] * 128 + chunk * 16 + (b % 16)[None, :]
+    scale = page * INDEX_PAGE_BYTES + 64 * 128 + 4 * r
+    return vals, scale
+
+
 def index_key_write(k: torch.Tensor, slot: torch.Tensor, pool: torch.Tensor) -> None:
+    """k [T, 128] -> pool [pages, 8448] uint8 at token slots (-1 = skip)."""
     if k.is_cuda:
         ext().index_key_write(k, slot.int(), pool)
         return
     keep = slot >= 0
-    pool[slot[keep].long()] = F.index_key_quantize(k)[keep]
+    rows = F.index_key_quantize(k)[keep]
+    vals, sc = index_pool_offsets(slot[keep])
+    flat = pool.view(-1)
+    flat[vals.reshape(-1)] = rows[:, :128].reshape(-1)
+    sidx = sc[:, None] + torch.arange(4)[None, :]
+    flat[sidx.reshape(-1)] = rows[:, 128:].reshape(-1)
+
+
+def index_key_read(pool: torch.Tensor, slot: torch.Tensor) -> torch.Tensor:
+    """Logical 132-byte rows [n, 132] of the tokens in `slot` (the inverse of index_key_write's layout)."""
+    vals, sc = index_pool_offsets(slot)
+    flat = pool.reshape(-1)
+    sidx = sc[:, None] + torch.arange(4, device=pool.device)[None, :]
+    return torch.cat([flat[vals], flat[sidx]], dim=1)

@@ -146,6 +146,37 @@ def mla_decode_case(b: int, heads: int, ctx: int, topk: int, fmt_name: str, n_q:
             "l2": "flushed before each launch (256 MB write)"}
 
 
+def indexer_case(b: int, ctx: int, topk: int, heads: int = 64, launches: int = 0) -> dict:
+    """DSA indexer at decode: b tokens, each scoring `ctx` cached positions (132 B each) and keeping the top-k."""
+    from ..ops import indexer as I
+    from ..ops import kvcache as K
+    dev = torch.device("cuda:0")
+    per = -(-ctx // 64)
+    pages = b * per + 1
+    pool = torch.randint(0, 256, (pages, K.INDEX_PAGE_BYTES), dtype=torch.uint8, device=dev)
+    sc = pool[:, 64 * 128:].view(pages, 64 * 4).view(torch.float32)
+    sc.copy_(torch.rand_like(sc) + 0.5)                                  # finite positive key scales
+    vals = pool[:, :64 * 128]
+    vals[(vals & 0x7F) == 0x7F] = 0                                      # no E4M3 NaN codes
+    pt = (torch.randperm(pages - 1, device=dev)[: b * per] + 1).view(b, per).int()
+    q8, w = I.indexer_q_quant(torch.randn(b, heads, 128, device=dev), torch.rand(b, heads, device=dev))
+    limit = torch.full((b,), ctx, dtype=torch.int32, device=dev)
+    ws = I.IndexerWorkspace.allocate(b, ctx, dev)
+
+    def fn():
+        I.indexer_select(q8, w, pool, pt, limit, topk, ctx, ws=ws)
+    if launches:
+        for _ in range(launches):
+            fn()
+        torch.cuda.synchronize()
+        return {}
+    us = _time_flushed(fn)
+    nbytes = b * ctx * 132
+    return {"kernel": "indexer_logits+topk", "tokens": b, "ctx": ctx, "topk": topk, "heads": heads,
+            "us": round(us, 2), "bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1),
+            "frac_hbm": round(nbytes / us / 1e3 / PEAKS["hbm_gbs"], 3), "l2": "flushed before each launch"}
+
+
 def main() -> None:
     _load_peaks()
     p = argparse.ArgumentParser()
@@ -164,6 +195,8 @@ def main() -> None:
     a = p.parse_args()
     if a.kernel == "gqa_decode":
         r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches)
+    elif a.kernel == "indexer":
+        r = indexer_case(a.b, a.ctx, a.topk, launches=a.launches)
     elif a.kernel == "mla_decode":
         r = mla_decode_case(a.b, a.heads, a.ctx, a.topk, a.fmt, a.nq, a.launches)
     else:

@@ -124,11 +124,12 @@ def test_mla_and_index_writers_bitexact(cuda):
         K.mla_write(nope.cpu(), rope.cpu(), slot.cpu(), ref)
         assert torch.equal(pool.cpu(), ref), width
     k = torch.randn(t, 128, device=cuda).to(torch.bfloat16)
-    pool = torch.zeros(100, 132, dtype=torch.uint8, device=cuda)
+    pool = torch.zeros(2, K.INDEX_PAGE_BYTES, dtype=torch.uint8, device=cuda)
     ref = pool.cpu().clone()
     K.index_key_write(k, slot, pool)
     K.index_key_write(k.cpu(), slot.cpu(), ref)
     assert torch.equal(pool.cpu(), ref)
+    assert torch.equal(K.index_key_read(ref, slot.cpu()), F.index_key_quantize(k.cpu()))
 
 
 def _build_pool(cuda, fmt, d, hk, lens, scale=(1.0, 1.0), seed=0):
@@ -233,3 +234,36 @@ def test_mla_decode_masked_and_deterministic(cuda):
     assert out[1].abs().max().item() == 0 and torch.isinf(lse[1]).all()
     assert (out.float() - ref).abs().max().item() < 2e-2 * max(1.0, ref.abs().max().item())
     assert (lse[[0, 2, 3]] - ref_lse[[0, 2, 3]]).abs().max().item() < 2e-3
+
+
+@pytest.mark.parametrize("hi,topk", [(64, 2048), (32, 256)])
+def test_indexer_scores_and_topk(cuda, hi, topk):
+    from inference_optimizations_b200._ext import ext
+    from inference_optimizations_b200.ops import indexer as I
+    torch.manual_seed(11)
+    lens = [300, 5000, 64, 2100, 1, 0]
+    t = len(lens)
+    per = max(-(-n // 64) for n in lens)
+    pages = t * per + 2
+    pt = torch.randperm(pages)[: t * per].view(t, per).int()
+    pool = torch.zeros(pages, K.INDEX_PAGE_BYTES, dtype=torch.uint8)
+    for i, n in enumerate(lens):
+        if n:
+            pos = torch.arange(n)
+            K.index_key_write(torch.randn(n, 128).to(torch.bfloat16), (pt[i][pos // 64] * 64 + pos % 64).int(), pool)
+    q8, w = I.indexer_q_quant(torch.randn(t, hi, 128), torch.rand(t, hi))
+    limit = torch.tensor(lens, dtype=torch.int32)
+    max_ctx = max(lens)
+    ref = I.indexer_scores_ref(q8, w, pool, pt, limit, -(-max_ctx // 128) * 128)
+    ws = I.IndexerWorkspace.allocate(t, max_ctx, cuda)
+    slots, pos = I.indexer_select(q8.to(cuda), w.to(cuda), pool.to(cuda), pt.to(cuda), limit.to(cuda), topk,
+                                  max_ctx, ws=ws, tiles_per_cta=8, with_pos=True)
+    torch.cuda.synchronize()
+    assert ws.status.item() == 0
+    got = ws.scores.cpu()
+    for i, n in enumerate(lens):
+        if n:
+            assert torch.allclose(got[i, :n], ref[i, :n], rtol=1e-4, atol=1e-4), i
+    # selection is exact against the oracle run on the kernel's own scores
+    rs, rp = I.topk_ref(got, limit, topk, pt)
+    assert torch.equal(pos.cpu(), rp) and torch.equal(slots.cpu(), rs)

@@ -72,3 +72,24 @@ def test_rmsnorm_and_argmax_ref():
     assert torch.allclose(y.float(), ref, atol=2e-2)
     lg = torch.tensor([[1.0, 3.0, 3.0, 0.0]])
     assert B.argmax(lg).tolist() == [1]
+
+
+def test_index_pool_layout_roundtrip():
+    from inference_optimizations_b200.ops import formats as F
+    from inference_optimizations_b200.ops import kvcache as K
+    torch.manual_seed(0)
+    k = torch.randn(150, 128).to(torch.bfloat16)
+    slot = torch.randperm(3 * 64)[:150].int()
+    slot[7] = -1
+    pool = torch.zeros(3, K.INDEX_PAGE_BYTES, dtype=torch.uint8)
+    K.index_key_write(k, slot, pool)
+    keep = slot >= 0
+    assert torch.equal(K.index_key_read(pool, slot[keep]), F.index_key_quantize(k[keep].float()))
+    # values of one page form a 128-byte-swizzled [64 x 128] tile: chunk c of row r at c ^ (r & 7)
+    r, c = 13, 3
+    page = pool[0]
+    rows = F.index_key_quantize(k.float())
+    pos = (slot == r).nonzero()
+    if len(pos):
+        i = int(pos[0])
+        assert torch.equal(page[r * 128 + ((c ^ (r & 7)) * 16): r * 128 + ((c ^ (r & 7)) * 16) + 16], rows[i, 16 * c:16 * c + 16])
