@@ -284,6 +284,36 @@ void indexer(const at::Tensor& q8, const at::Tensor& w, const at::Tensor& pool, 
   if (do_topk) CHECK_CUDA_OK(iob::indexer_topk(a, stream()));
 }
 
+void ar_norm2(const at::Tensor& peers, int64_t flag_offset, int64_t rows_cap, int64_t half, int64_t rank,
+              at::Tensor epoch, at::Tensor resid, at::Tensor out, c10::optional<at::Tensor> w1,
+              c10::optional<at::Tensor> w2, double eps, double plus_one, at::Tensor status) {
+  req(peers, at::kLong, "peers");
+  req(epoch, at::kInt, "epoch");
+  req(resid, at::kBFloat16, "resid");
+  req(out, at::kBFloat16, "out");
+  req(status, at::kInt, "status");
+  TORCH_CHECK(resid.is_contiguous() && out.is_contiguous() && resid.dim() == 2, "resid [T, H]");
+  iob::ArNormArgs a{};
+  a.peers = reinterpret_cast<void* const*>(peers.data_ptr<int64_t>());
+  a.flag_offset = flag_offset;
+  a.rows_cap = rows_cap;
+  a.H = resid.size(1);
+  a.T = resid.size(0);
+  a.half = half;
+  a.rank = rank;
+  a.nranks = peers.numel();
+  a.epoch = epoch.data_ptr<int>();
+  a.resid = resid.data_ptr();
+  a.out = out.data_ptr();
+  if (w1.has_value()) { req(*w1, at::kBFloat16, "w1"); a.w1 = w1->data_ptr(); }
+  if (w2.has_value()) { req(*w2, at::kBFloat16, "w2"); a.w2 = w2->data_ptr(); }
+  a.eps = eps;
+  a.plus_one = plus_one;
+  a.status = status.data_ptr<int>();
+  const at::cuda::CUDAGuard g(resid.device());
+  CHECK_CUDA_OK(iob::ar_norm2(a, stream()));
+}
+
 void umma_gemm_test(const at::Tensor& A, const at::Tensor& B, at::Tensor C, int64_t sw64) {
   req(A, at::kBFloat16, "A");
   req(B, at::kBFloat16, "B");
@@ -330,6 +360,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gqa_decode", &gqa_decode);
   m.def("mla_decode", &mla_decode);
   m.def("indexer", &indexer);
+  m.def("ar_norm2", &ar_norm2);
   m.def("umma_gemm_test", &umma_gemm_test);
   m.def("umma_f8_mn_test", &umma_f8_mn_test);
   m.def("nvfp4_lut_test", &nvfp4_lut_test);

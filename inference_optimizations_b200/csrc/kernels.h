@@ -129,6 +129,21 @@ struct IndexerArgs {
 cudaError_t indexer_logits(const IndexerArgs& a, cudaStream_t s);
 cudaError_t indexer_topk(const IndexerArgs& a, cudaStream_t s);
 
+// ---- tensor-parallel all-reduce fused with the following norm chain (comm.cu), over symmetric peer memory.
+struct ArNormArgs {
+  void* const* peers;      // [nranks] device pointers to every rank's symmetric buffer (peers[rank] = own)
+  long long flag_offset;   // byte offset of the [2][nranks] int flags inside each buffer
+  int rows_cap, H, T, half, rank, nranks;
+  int* epoch;              // [2] this rank's flag values for the two halves (initialised {1, 0})
+  void* resid;             // bf16 [T, H], updated in place: resid += o
+  void* out;               // bf16 [T, H]: rmsnorm(resid, w2)
+  const void* w1;          // bf16 [H] norm applied to the reduced sum first (null: none)
+  const void* w2;          // bf16 [H] norm of the new residual (null: out is not written)
+  float eps, plus_one;
+  int* status;
+};
+cudaError_t ar_norm2(const ArNormArgs& a, cudaStream_t s);
+
 // ---- primitive check (umma_test.cu): C[M, N] fp32 = A[M, K] * B[N, K]^T, bf16 inputs, one CTA per 128 rows.
 cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, int sw64, cudaStream_t s);
 cudaError_t umma_f8_mn_test(const void* A, const void* B, float* C, int N, int K, cudaStream_t s);

@@ -92,6 +92,14 @@ class GQARunner:
         self.spec = ecfg.spec
         self.n_draft = ecfg.draft_tokens if ecfg.spec else 0
         self.draft = GQAModel(cfg, device, tp_rank, tp, ecfg.seed, all_reduce, draft=True) if self.spec else None
+        self.tp_comm = None
+        if tp > 1 and ecfg.fused_comm and self.device.type == "cuda":
+            from ..parallel.symm import TPComm
+            rows = max(ecfg.chunked_prefill, 4 * max(ecfg.graph_sizes() + [ecfg.max_running]))
+            self.tp_comm = TPComm(tp_rank, tp, rows, cfg.hidden, self.device)
+            self.model.tp_comm = self.tp_comm
+            if self.draft is not None:
+                self.draft.tp_comm = self.tp_comm
         G = cfg.num_q_heads // cfg.num_kv_heads
         self.n_q_prefill = max(1, 16 // G)
         self.max_running = ecfg.max_running

@@ -69,6 +69,7 @@ class GQAModel:
                  weights: Optional[dict] = None, draft: bool = False):
         self.cfg, self.device, self.tp_rank, self.tp = cfg, torch.device(device), tp_rank, tp
         self.all_reduce = all_reduce
+        self.tp_comm = None          # parallel.symm.TPComm: fused peer-memory all-reduce + norms (tp > 1)
         if cfg.num_q_heads % tp or cfg.num_kv_heads % tp or cfg.num_kv_heads_global % tp or cfg.ffn % tp:
             raise ValueError(f"tp={tp} does not divide the head / ffn counts")
         self.hidden = cfg.hidden
@@ -180,6 +181,14 @@ class GQAModel:
         attn = A.gqa_decode(q, pool, kv.tables[g.kind].dev, st.kv_len, st.n_q, g.kv_heads, kv.fmt,
                             1.0 / math.sqrt(g.head_dim), g.window, kv.k_scale, kv.v_scale,
                             splits=st.splits.get(g.kind), ws=kv.workspace(g.head_dim, g.kv_heads), req_idx=st.req_idx)
+        if self.tp > 1 and self.tp_comm is not None and attn.shape[0] <= self.tp_comm.rows_cap:
+            # row-parallel GEMMs write their partials into the symmetric buffer; one kernel reduces over NVLink and
+            # applies post-norm, residual add and the next pre-norm
+            comm, t = self.tp_comm, attn.shape[0]
+            torch.matmul(attn.view(t, -1), w.o.t(), out=comm.out_buffer(t))
+            x = comm.reduce_norm2(t, resid, w.n_post_attn, w.n_pre_ffn, eps)
+            torch.matmul(B.act_mul(Fn.linear(x, w.gu), gelu=True), w.down.t(), out=comm.out_buffer(t))
+            return comm.reduce_norm2(t, resid, w.n_post_ffn, next_norm, eps)
         o = self._reduce(Fn.linear(attn.view(attn.shape[0], -1), w.o))
         o = B.rmsnorm(o, w.n_post_attn, eps, True)
         x = B.rmsnorm(o, w.n_pre_ffn, eps, True, residual=resid)          # resid += o; x = norm(resid)
