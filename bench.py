@@ -36,6 +36,8 @@ def parse():
     p.add_argument("--spec", type=int, default=1,
                    help="1 = speculative decoding, the config's 1-layer draft proposing 3 tokens (default); 0 = plain")
     p.add_argument("--no-graphs", action="store_true")
+    p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
+                   help="tensor-parallel all-reduce: own peer-memory kernel fused with the norms (default) or NCCL")
     return p.parse_args()
 
 
@@ -71,7 +73,7 @@ def main() -> int:
     max_new = max(args.max_new, 4 * (steps + warm) + 2 * steps + 16)
     ecfg = EngineConfig(model=args.model, device=str(dev), kv_dtype=args.kv, max_running=args.sessions,
                         chunked_prefill=2048, spec=bool(args.spec), cuda_graphs=not args.no_graphs,
-                        graph_batch_sizes=str(args.sessions), tp=tp)
+                        graph_batch_sizes=str(args.sessions), tp=tp, fused_comm=args.comm == "fused")
     max_seq = args.ctx + max_new + 64
     eng = Engine(ecfg, cfg, max_seq=max_seq, tp_rank=rank, tp=tp,
                  all_reduce=D.nccl_all_reduce if tp > 1 else None,
@@ -158,7 +160,7 @@ def main() -> int:
                             "head_dim 256 on SWA-1024 layers and 512 on every 6th (global) layer, GeGLU 21504, "
                             "vocab 262144",
                    "global_batch": args.sessions, "seq_len": args.ctx, "parallelism": f"tp{tp}",
-                   "kv_cache": args.kv, "speculative": bool(ecfg.spec), "draft_tokens": ecfg.draft_tokens if ecfg.spec else 0,
+                   "kv_cache": args.kv, "tp_comm": args.comm if tp > 1 else None, "speculative": bool(ecfg.spec), "draft_tokens": ecfg.draft_tokens if ecfg.spec else 0,
                    "accept_per_step": accept,
                    "l2": "no flush: every step reads weights + KV (~170 GB at N=1), far larger than the 126 MB L2"},
         "per_user_tok_s": round(value / args.sessions, 3),
