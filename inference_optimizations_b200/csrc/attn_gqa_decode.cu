@@ -47,6 +47,7 @@ struct Smem {
   float row_m[kN];
   float q_scale[kN];      // E4M3 path: per-row Q scale (q = e4m3 * q_scale)
 };
+constexpr int kF4TabBytes = 256 * 8;   // E4M3 path, NVFP4 pools: scale byte -> E4M3 products, after Smem
 
 // must match kv_swizzle_byte() (kernels.h), which the pool writers use
 __device__ __forceinline__ int pool_chunk_pos(int j, int r, int nch) {
@@ -583,9 +584,9 @@ template <int FMT, int D>
 __device__ __host__ __forceinline__ constexpr int ring_f8() { return part_bytes<FMT, D>() <= 20 * 1024 ? 6 : 4; }
 template <int FMT, int D>
 __device__ __host__ __forceinline__ constexpr int raw_stages_f8() {
-  return (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096) / part_bytes<FMT, D>() > 8   ? 8
-         : (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096) / part_bytes<FMT, D>() < 2 ? 2
-         : (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096) / part_bytes<FMT, D>();
+  return (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096 - kF4TabBytes) / part_bytes<FMT, D>() > 8   ? 8
+         : (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096 - kF4TabBytes) / part_bytes<FMT, D>() < 2 ? 2
+         : (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096 - kF4TabBytes) / part_bytes<FMT, D>();
 }
 
 __device__ __forceinline__ uint32_t pack_e4m3x4(uint32_t h01, uint32_t h23) {
@@ -594,8 +595,26 @@ __device__ __forceinline__ uint32_t pack_e4m3x4(uint32_t h01, uint32_t h23) {
 
 // 64 values of one token row (dims [d0, d0 + 64)) as E4M3 bytes packed four per word: 16 words.
 template <int FMT, int D>
-__device__ __forceinline__ void dequant_e4m3_64(const uint8_t* part, int r, int d0, uint32_t* out) {
-  if constexpr (FMT == kKvFp8) {
+__device__ __forceinline__ void dequant_e4m3_64(const uint8_t* part, int r, int d0, uint32_t* out,
+                                                const uint2* f4tab) {
+  if constexpr (FMT == kKvNvfp4) {
+    // one 8-byte shared-memory table per 16-value block (scale byte -> the eight E4M3 products), then byte permutes
+    constexpr int RB = D / 2, NCH = (RB / 16) < 8 ? (RB / 16) : 8;
+    const int c = d0 / 64;
+    const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(part + 64 * RB + r * (D / 16) + c * 4);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint4 in = *reinterpret_cast<const uint4*>(part + r * RB + pool_chunk_pos(2 * c + half, r, NCH) * 16);
+      const uint32_t w[4] = {in.x, in.y, in.z, in.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint2 tab = f4tab[(sc4 >> (8 * (2 * half + (q >> 1)))) & 0xFFu];
+        const uint2 e = f4_decode8(w[q], tab);
+        out[8 * half + 2 * q] = e.x;
+        out[8 * half + 2 * q + 1] = e.y;
+      }
+    }
+  } else if constexpr (FMT == kKvFp8) {
     constexpr int RB = D, NCH = 8;
     const uint8_t* row = part + r * RB;
 #pragma unroll
@@ -704,6 +723,8 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
     sm.abort = 0;
     fence_mbar_init();
   }
+  uint2* f4tab = reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(&sm) + ((sizeof(Smem) + 15) & ~size_t(15)));
+  if constexpr (FMT == kKvNvfp4) f4_table_fill(f4tab);
   if (warp == kMmaWarpF8) { tmem_alloc(&sm.tmem_base, kTmemCols); tmem_relinquish(); }
   __syncthreads();
   for (int idx = threadIdx.x; idx < kN * NQS * 8; idx += kThreadsF8) {
@@ -908,7 +929,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
 #pragma unroll 1
       for (int d0 = kdim0; d0 < kdim0 + D / 2; d0 += 64) {
         uint32_t v[16];
-        if (valid) dequant_e4m3_64<FMT, D>(part, kr, d0, v);
+        if (valid) dequant_e4m3_64<FMT, D>(part, kr, d0, v, f4tab);
         else {
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] = 0;
@@ -945,7 +966,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
         if (!(ok = mbar_wait(&sm.ring_empty[buf], ((seq / RING) & 1) ^ 1, abort, a.status, kTimeoutConsumer)))
           break;
         uint32_t o[16];
-        if (valid) dequant_e4m3_64<FMT, D>(raw + st * PB, vr, 128 * mb + 64 * vhalf, o);
+        if (valid) dequant_e4m3_64<FMT, D>(raw + st * PB, vr, 128 * mb + 64 * vhalf, o, f4tab);
         else {
 #pragma unroll
           for (int k = 0; k < 16; ++k) o[k] = 0;
@@ -1111,7 +1132,8 @@ cudaError_t launch_t(const GqaDecodeArgs& a, cudaStream_t s) {
     if (!a.exact) {
     constexpr int NST8 = raw_stages_f8<FMT, D>();
     constexpr int RING8 = ring_f8<FMT, D>();
-    constexpr int smem8 = 1024 + RING8 * kSlabBytes + (D / 128) * kN * 128 + 2 * kN * 128 + NST8 * PB + sizeof(Smem);
+    constexpr int smem8 = 1024 + RING8 * kSlabBytes + (D / 128) * kN * 128 + 2 * kN * 128 + NST8 * PB +
+                          ((sizeof(Smem) + 15) & ~size_t(15)) + kF4TabBytes;
     static_assert(smem8 <= 232448, "shared memory budget (E4M3 path)");
     auto kern8 = gqa_decode_f8_kernel<FMT, D, RMAX>;
     IOB_CUDA_CHECK(cudaFuncSetAttribute(kern8, cudaFuncAttributeMaxDynamicSharedMemorySize, smem8));

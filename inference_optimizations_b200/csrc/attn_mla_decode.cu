@@ -50,6 +50,7 @@ struct MlaSmem {
   uint64_t s_free;              // S loaded into registers                (8 softmax-warp arrivals)
   uint64_t q_ready, fin;
   alignas(16) float bias[kMRing][kMTile];   // 0 live row, -inf masked (read as float4)
+  uint2 f4tab[256];             // scale byte -> E4M3 products {0, .5, 1, 1.5, 2, 3, 4, 6} x scale
   uint32_t tmem_base;
   int abort;
 };
@@ -129,13 +130,14 @@ __device__ __forceinline__ void load_row(const uint8_t* row, int q, RawRow<FMT>&
   }
 }
 
-// The 16-byte E4M3 chunk c (0..15: values 16 c .. 16 c + 15 of the thread's 256) of a raw row share.
+// The 16-byte E4M3 chunk c (0..15: values 16 c .. 16 c + 15 of the thread's 256) of a raw row share; `tabs` is the
+// CTA's scale-byte -> E4M3 product table (f4_table_fill).
 template <int FMT>
-__device__ __forceinline__ uint4 row_chunk(const RawRow<FMT>& x, int c) {
+__device__ __forceinline__ uint4 row_chunk(const RawRow<FMT>& x, int c, const uint2* tabs) {
   if constexpr (FMT == kKvNvfp4) {
     const uint4& cw = x.v[c >> 1];                    // 32 values per code chunk
     const uint32_t sb = (u4_get(x.sc, c >> 2) >> (8 * (c & 3))) & 0xFFu;   // scale of these 16 values
-    const uint2 tab = f4_scale_table(sb);
+    const uint2 tab = tabs[sb];
     const uint2 lo = f4_decode8(u4_get(cw, 2 * (c & 1)), tab);
     const uint2 hi = f4_decode8(u4_get(cw, 2 * (c & 1) + 1), tab);
     return make_uint4(lo.x, lo.y, hi.x, hi.y);
@@ -180,6 +182,7 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
     sm.abort = 0;
     fence_mbar_init();
   }
+  if constexpr (FMT == kKvNvfp4) f4_table_fill(sm.f4tab);
   if (warp == kMMmaWarp) { tmem_alloc(&sm.tmem_base, 512); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
@@ -390,7 +393,7 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
         uint8_t* tb = tiles + rb * kMTileBytes;
 #pragma unroll
         for (int c = 0; c < 16; ++c)
-          *reinterpret_cast<uint4*>(tb + (2 * q + (c >> 3)) * kMBlk + sw128_chunk(trow, c & 7)) = row_chunk<FMT>(cur, c);
+          *reinterpret_cast<uint4*>(tb + (2 * q + (c >> 3)) * kMBlk + sw128_chunk(trow, c & 7)) = row_chunk<FMT>(cur, c, sm.f4tab);
 #pragma unroll
         for (int c = 0; c < 2; ++c)
           *reinterpret_cast<uint4*>(tb + kMRopeOff + sw64_chunk(trow, 2 * q + c)) = cur.rope[c];

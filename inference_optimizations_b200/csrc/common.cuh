@@ -507,16 +507,27 @@ __device__ __forceinline__ uint2 f4_scale_table(uint32_t sb) {
   const uint32_t e67 = f16x2_to_e4m3x2(hmul2_u32(s2, 0x46004400u));   // (4, 6)
   return make_uint2(e01 | (e23 << 16), e45 | (e67 << 16));
 }
-// Eight E2M1 codes (nibble i = value i) -> eight E4M3 bytes through the block's table.
+// Eight E2M1 codes (nibble i = value i) -> eight E4M3 bytes through the block's table.  The sign masks come from a
+// byte permute in sign-replicate mode (selector nibble bit 3): value 2k + 1's sign is the msb of code byte k, value
+// 2k's sign is the msb of byte k of (codes << 4).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
 __device__ __forceinline__ uint2 f4_decode8(uint32_t w, uint2 tab) {
   const uint32_t mag = w & 0x77777777u;
-  const uint32_t lo = __byte_perm(tab.x, tab.y, mag);
-  const uint32_t hi = __byte_perm(tab.x, tab.y, mag >> 16);
-  const uint32_t x = w & 0x88888888u;   // sign of value 2k + 1 at bit 7 of byte k
-  const uint32_t y = x << 4;            // sign of value 2k at bit 7 of byte k
-  const uint32_t slo = __byte_perm(y, x, 0x5140);
-  const uint32_t shi = __byte_perm(y, x, 0x7362);
+  const uint32_t lo = prmt(tab.x, tab.y, mag);
+  const uint32_t hi = prmt(tab.x, tab.y, mag >> 16);
+  const uint32_t y = w << 4;
+  const uint32_t slo = prmt(y, w, 0xD9C8u);
+  const uint32_t shi = prmt(y, w, 0xFBEAu);
   return make_uint2(lo | (slo & 0x80808080u), hi | (shi & 0x80808080u));
+}
+// Shared-memory table of f4_scale_table for every scale byte (256 x 8 B), filled cooperatively by the CTA; a 16-value
+// block then costs one 8-byte shared load instead of building its table.
+__device__ __forceinline__ void f4_table_fill(uint2* tab) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) tab[i] = f4_scale_table(static_cast<uint32_t>(i));
 }
 
 // E2M1 magnitude code of y >= 0: number of midpoints strictly below y (ties round down), saturating at 7 (= 6.0).
