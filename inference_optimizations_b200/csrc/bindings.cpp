@@ -314,6 +314,19 @@ void ar_norm2(const at::Tensor& peers, int64_t flag_offset, int64_t rows_cap, in
   CHECK_CUDA_OK(iob::ar_norm2(a, stream()));
 }
 
+void moe_route(const at::Tensor& logits, const at::Tensor& bias, at::Tensor ids, at::Tensor wts, int64_t n_group,
+               int64_t topk_group, double scale) {
+  req(logits, at::kFloat, "logits");
+  req(bias, at::kFloat, "bias");
+  req(ids, at::kInt, "ids");
+  req(wts, at::kFloat, "wts");
+  TORCH_CHECK(logits.dim() == 2 && logits.is_contiguous() && bias.numel() == logits.size(1), "logits [T, E]");
+  const at::cuda::CUDAGuard g(logits.device());
+  CHECK_CUDA_OK(iob::moe_route(logits.data_ptr<float>(), bias.data_ptr<float>(), ids.data_ptr<int>(),
+                               wts.data_ptr<float>(), logits.size(0), logits.size(1), ids.size(1), n_group, topk_group,
+                               scale, stream()));
+}
+
 void umma_gemm_test(const at::Tensor& A, const at::Tensor& B, at::Tensor C, int64_t sw64) {
   req(A, at::kBFloat16, "A");
   req(B, at::kBFloat16, "B");
@@ -361,6 +374,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_decode", &mla_decode);
   m.def("indexer", &indexer);
   m.def("ar_norm2", &ar_norm2);
+  m.def("moe_route", &moe_route);
   m.def("umma_gemm_test", &umma_gemm_test);
   m.def("umma_f8_mn_test", &umma_f8_mn_test);
   m.def("nvfp4_lut_test", &nvfp4_lut_test);

@@ -144,6 +144,10 @@ struct ArNormArgs {
 };
 cudaError_t ar_norm2(const ArNormArgs& a, cudaStream_t s);
 
+// ---- MoE router (moe.cu): sigmoid, bias-corrected group-limited top-k, renormalised * scale.
+cudaError_t moe_route(const float* logits, const float* bias, int* ids, float* wts, int T, int E, int K, int G,
+                      int KG, float scale, cudaStream_t s);
+
 // ---- primitive check (umma_test.cu): C[M, N] fp32 = A[M, K] * B[N, K]^T, bf16 inputs, one CTA per 128 rows.
 cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, int sw64, cudaStream_t s);
 cudaError_t umma_f8_mn_test(const void* A, const void* B, float* C, int N, int K, cudaStream_t s);

@@ -1,0 +1,115 @@
+"""Model runner for the MLA + DSA + MoE family (`models/mla.py`): paged latent + index pools sharing one page table,
+chunked prefill and decode through the same forward (sparse attention makes every prompt token an independent
+query over its causal prefix), greedy sampling.  Runs eagerly: the MoE's per-step expert grouping has
+data-dependent shapes.  Same runner contract as `engine/runner.py GQARunner` (prefill / decode / attach / detach /
+can_admit)."""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from ..config import EngineConfig, MLAMoEConfig
+from ..kv.allocator import RequestPages
+from ..models.mla import MLAKVCache, MLAModel, MLAStep
+from ..ops import basic as B
+from ..ops.kvcache import FMT_FP8, FMT_NVFP4
+from .scheduler import Batch, Request, Segment
+
+
+class MLARunner:
+    def __init__(self, cfg: MLAMoEConfig, ecfg: EngineConfig, device, max_seq: int, tp_rank: int = 0, tp: int = 1):
+        if tp != 1:
+            raise NotImplementedError("the MLA family runs on one GPU per engine here (tp = 1)")
+        self.cfg, self.ecfg, self.device = cfg, ecfg, torch.device(device)
+        self.tp, self.tp_rank = tp, tp_rank
+        self.max_seq = max_seq
+        self.spec = False
+        self.model = MLAModel(cfg, self.device, ecfg.seed)
+        fmt = FMT_NVFP4 if ecfg.kv_dtype == "nvfp4" else FMT_FP8
+        self.max_running = ecfg.max_running
+        per_req = (max_seq + 64 + 63) // 64 + 1
+        pages = self.max_running * per_req + 2
+        self.kv = MLAKVCache(cfg, self.device, fmt, self.max_running + 1, per_req, pages)
+        self.dummy_row = self.max_running
+        self.pages: dict[int, RequestPages] = {}
+        self.graphs: dict = {}
+        self.event_log = None
+
+    # ------------------------------------------------------------------------------------------ memory
+    def can_admit(self, r: Request) -> bool:
+        need = (r.prompt_len + r.params.max_new_tokens + 64) // 64 + 1
+        reserved = sum(max(0, rp.high_pages - len(rp.pages)) for rp in self.pages.values())
+        return self.kv.alloc.free >= need + reserved
+
+    def attach(self, r: Request) -> None:
+        rp = RequestPages(self.kv.alloc, self.kv.table, r.slot)
+        rp.high_pages = (r.prompt_len + r.params.max_new_tokens + 64) // 64 + 1
+        self.pages[r.rid] = rp
+
+    def detach(self, r: Request) -> None:
+        rp = self.pages.pop(r.rid, None)
+        if rp is not None:
+            rp.free()
+
+    # ------------------------------------------------------------------------------------------ steps
+    def _step(self, segs: list) -> tuple[MLAStep, list]:
+        ids, pos, slot, limit, rix, logit_rows = [], [], [], [], [], []
+        for s in segs:
+            rp = self.pages[s.req.rid]
+            rp.ensure(s.start + len(s.tokens))
+            for j, tok in enumerate(s.tokens):
+                p = s.start + j
+                ids.append(int(tok))
+                pos.append(p)
+                slot.append(rp.slot_of(p))
+                limit.append(p + 1)
+                rix.append(s.req.slot)
+            if s.logits:
+                logit_rows.append(len(ids) - 1)
+        self.kv.table.sync()
+        dev = self.device
+        mk = lambda v: torch.tensor(v, dtype=torch.int32).to(dev, non_blocking=True)  # noqa: E731
+        st = MLAStep(mk(ids), mk(pos), mk(slot), mk(limit), mk(rix), self.max_seq + 1)
+        return st, logit_rows
+
+    def _run(self, segs: list) -> list:
+        st, rows = self._step(segs)
+
+        def body():
+            x = self.model.forward(st, self.kv)
+            if rows:
+                sel = x[torch.tensor(rows, dtype=torch.long, device=self.device)]
+                self._out = B.argmax(self.model.logits(sel))
+        if self.event_log is not None and self.device.type == "cuda":
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            body()
+            e1.record()
+            self.event_log.append((e0, e1))
+        else:
+            body()
+        return self._out.cpu().tolist() if rows else []
+
+    def prefill(self, batch: Batch) -> dict:
+        for s in batch.segments:
+            if s.req.rid not in self.pages:
+                self.attach(s.req)
+        out = self._run(batch.segments)
+        res, k = {}, 0
+        for s in batch.segments:
+            if s.logits:
+                res[s.req.rid] = int(out[k])
+                k += 1
+        return res
+
+    def decode(self, reqs: list) -> dict:
+        segs = [Segment(r, r.kv_len, [r.pending], True) for r in reqs]
+        out = self._run(segs)
+        return {r.rid: [int(out[i])] for i, r in enumerate(reqs)}
+
+    def warm_graphs(self, n: int) -> None:
+        """Eager runner: nothing to capture."""
+
+    def count_step_launches(self, bucket: int, kind: Optional[str] = None) -> int:
+        return 0

@@ -1,0 +1,87 @@
+"""Routed mixture of experts (DeepSeek-V3 class): sigmoid router with bias-corrected, group-limited top-k selection,
+SwiGLU experts, shared expert.
+
+Router semantics (the `noaux_tc` router the reference serves; `moe-gemm/router-piggyback/dp_router_piggyback.py:1-25`
+carries its top-k ids / weights): scores = sigmoid(x W_gate^T); selection uses scores + e_bias; with n_group > 1 the
+experts are split into groups, a group's score is the sum of its two best biased scores, only the topk_group best
+groups stay eligible; the top-k experts' *unbiased* scores are renormalised to sum 1 and scaled by routed_scale.
+`router="softmax"`: softmax over experts, top-k, renormalised (Qwen / Mixtral style).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as Fn
+
+from .._ext import ext
+
+
+def route(logits: torch.Tensor, e_bias: torch.Tensor, topk: int, n_group: int, topk_group: int,
+          routed_scale: float, kind: str = "sigmoid") -> tuple[torch.Tensor, torch.Tensor]:
+    """logits fp32 [T, E] -> (expert ids int32 [T, topk], weights fp32 [T, topk]).  Ties: lower expert id."""
+    if logits.is_cuda and kind == "sigmoid":
+        t, e = logits.shape
+        ids = torch.empty(t, topk, dtype=torch.int32, device=logits.device)
+        w = torch.empty(t, topk, dtype=torch.float32, device=logits.device)
+        ext().moe_route(logits.float().contiguous(), e_bias.float().contiguous(), ids, w, n_group, topk_group,
+                        routed_scale)
+        return ids, w
+    return route_ref(logits, e_bias, topk, n_group, topk_group, routed_scale, kind)
+
+
+def _topk_stable(x: torch.Tensor, k: int) -> torch.Tensor:
+    """Indices of the k largest per row; ties go to the lower index (stable descending sort)."""
+    return torch.sort(x, dim=-1, descending=True, stable=True).indices[..., :k]
+
+
+def route_ref(logits: torch.Tensor, e_bias: torch.Tensor, topk: int, n_group: int, topk_group: int,
+              routed_scale: float, kind: str = "sigmoid") -> tuple[torch.Tensor, torch.Tensor]:
+    logits = logits.float()
+    t, e = logits.shape
+    if kind == "softmax":
+        p = torch.softmax(logits, dim=-1)
+        ids = _topk_stable(p, topk)
+        w = p.gather(1, ids)
+        return ids.int(), w / w.sum(-1, keepdim=True)
+    scores = torch.sigmoid(logits)
+    sel = scores + e_bias.float()[None, :]
+    if n_group > 1:
+        g = sel.view(t, n_group, e // n_group)
+        gscore = g.sort(dim=-1, descending=True).values[..., :2].sum(-1)
+        keep = _topk_stable(gscore, topk_group)
+        mask = torch.zeros(t, n_group, dtype=torch.bool, device=logits.device)
+        mask.scatter_(1, keep, True)
+        sel = sel.masked_fill(~mask.repeat_interleave(e // n_group, dim=1), float("-inf"))
+    ids = _topk_stable(sel, topk)
+    w = scores.gather(1, ids)
+    w = w / w.sum(-1, keepdim=True).clamp(min=1e-20) * routed_scale
+    return ids.int(), w
+
+
+def swiglu(x: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    from .basic import act_mul
+    return Fn.linear(act_mul(Fn.linear(x, w_gu), gelu=False), w_down)
+
+
+def moe_forward(x: torch.Tensor, gate: torch.Tensor, e_bias: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor,
+                shared_gu: torch.Tensor, shared_down: torch.Tensor, topk: int, n_group: int, topk_group: int,
+                routed_scale: float, kind: str = "sigmoid") -> torch.Tensor:
+    """x bf16 [T, H]; w_gu [E, 2F, H]; w_down [E, H, F]; shared_* one shared expert (or None).  Dropless: every
+    (token, expert) pair is computed; contributions are summed in fp32 in expert order then added to the shared
+    expert's output."""
+    t = x.shape[0]
+    logits = Fn.linear(x.float(), gate.float())
+    ids, w = route(logits, e_bias, topk, n_group, topk_group, routed_scale, kind)
+    out = torch.zeros(t, x.shape[1], dtype=torch.float32, device=x.device)
+    flat = ids.long().view(-1)
+    order = torch.argsort(flat, stable=True)
+    experts, counts = torch.unique_consecutive(flat[order], return_counts=True)
+    start = 0
+    for e, c in zip(experts.tolist(), counts.tolist()):
+        sel = order[start:start + c]
+        start += c
+        rows = sel // topk
+        y = swiglu(x[rows], w_gu[e], w_down[e])
+        out.index_add_(0, rows, y.float() * w.view(-1)[sel, None])
+    if shared_gu is not None:
+        out += swiglu(x, shared_gu, shared_down).float()
+    return out.to(torch.bfloat16)
