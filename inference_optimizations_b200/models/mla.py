@@ -132,6 +132,20 @@ class MLAModel:
         self.rope = {}
         self.sm_scale = 1.0 / math.sqrt(c.qk_nope + c.qk_rope)
 
+    def copy_from(self, other: "MLAModel") -> None:
+        """Take another instance's weights (any device): device RNG streams differ, so tests that compare devices
+        copy one model's weights into the other."""
+        dev = self.device
+        for name in ("embed", "lm_head", "final_norm"):
+            setattr(self, name, getattr(other, name).to(dev))
+        for mine, theirs in zip(self.layers, other.layers):
+            for f in vars(theirs):
+                v = getattr(theirs, f)
+                if isinstance(v, dict):
+                    setattr(mine, f, {k: (t.to(dev) if t is not None else None) for k, t in v.items()})
+                else:
+                    setattr(mine, f, v.to(dev))
+
     def rope_table(self, max_pos: int) -> torch.Tensor:
         key = max_pos
         if key not in self.rope:
