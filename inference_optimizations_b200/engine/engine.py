@@ -42,6 +42,10 @@ class Engine:
         self.stats: list[StepStats] = []
         self.finished: list[Request] = []
         self.spec_policy = SpecPolicy(ecfg.draft_tokens, ecfg.spec_policy)
+        self.trace = None
+        if ecfg.trace:
+            from ..tooling.trace import StepTrace
+            self.trace = StepTrace(ecfg.trace, tp_rank)
 
     def add_request(self, prompt: list, params: Optional[SamplingParams] = None) -> Request:
         return self.sched.new_request(prompt, params or SamplingParams())
@@ -49,9 +53,17 @@ class Engine:
     def step(self) -> dict:
         """One engine iteration.  Returns rid -> tokens produced this step."""
         t0 = time.perf_counter()
+        rec = self.trace.begin() if self.trace else None
         batch = self.sched.schedule()
         if batch is None:
             return {}
+        if rec is not None:
+            t_s = self.trace.phase(rec, "schedule", t0)
+            log = getattr(self.runner, "event_log", None)
+            n_ev = len(log) if log is not None else None
+            if log is None and self.device.type == "cuda":
+                self.runner.event_log = []
+                n_ev = 0
         if batch.kind == "prefill":
             nxt = self.runner.prefill(batch)
             self.sched.commit_prefill(batch, nxt)
@@ -81,6 +93,17 @@ class Engine:
                 self.runner.detach(r)
         self.stats.append(StepStats(batch.kind if batch.kind == "prefill" else kind,
                                     sum(len(v) for v in out.values()), time.perf_counter() - t0))
+        if rec is not None:
+            self.trace.phase(rec, "run+commit", t_s)
+            rec.update(kind=self.stats[-1].kind, tokens=self.stats[-1].tokens_out, running=len(self.sched.running),
+                       waiting=len(self.sched.waiting), batch=len(batch.segments))
+            ev = None
+            log = getattr(self.runner, "event_log", None)
+            if n_ev is not None and log is not None and len(log) > n_ev:
+                ev = log[-1]
+                if len(log) > 4096:          # the trace keeps its own reference; bound the runner's list
+                    del log[:-1]
+            self.trace.end(rec, ev)
         return out
 
     def generate(self, prompts: list, params: Optional[SamplingParams] = None, max_steps: int = 1 << 30) -> list:

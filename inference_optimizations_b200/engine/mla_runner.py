@@ -14,7 +14,7 @@ from ..kv.allocator import RequestPages
 from ..models.mla import MLAKVCache, MLAModel, MLAStep
 from ..ops import basic as B
 from ..ops.kvcache import FMT_FP8, FMT_NVFP4
-from .scheduler import Batch, Request, Segment
+from .scheduler import Batch, Request, SamplingParams, Segment
 
 
 class MLARunner:
@@ -107,6 +107,18 @@ class MLARunner:
         segs = [Segment(r, r.kv_len, [r.pending], True) for r in reqs]
         out = self._run(segs)
         return {r.rid: [int(out[i])] for i, r in enumerate(reqs)}
+
+    @torch.no_grad()
+    def score(self, tokens: list) -> torch.Tensor:
+        """Teacher-forced full logits [T, V] (fp32, CPU) of one sequence; a scratch request row, freed after."""
+        r = Request(rid=-1, prompt=list(tokens), params=SamplingParams(max_new_tokens=1))
+        r.slot = next(i for i in range(self.max_running) if all(p.slot != i for p in self.pages.values()))
+        self.attach(r)
+        try:
+            st, _ = self._step([Segment(r, 0, list(tokens), False)])
+            return self.model.logits(self.model.forward(st, self.kv)).float().cpu()
+        finally:
+            self.detach(r)
 
     def warm_graphs(self, n: int) -> None:
         """Eager runner: nothing to capture."""

@@ -24,7 +24,7 @@ from ..kv.allocator import DUMMY_PAGE, OutOfPages, RequestPages
 from ..models.gqa import GQAKVCache, GQAModel, StepTensors
 from ..ops import attention as A
 from ..ops import basic as B
-from .scheduler import Batch, Request, Segment
+from .scheduler import SamplingParams, Batch, Request, Segment
 
 KINDS = ("global", "swa", "draft")
 
@@ -243,6 +243,29 @@ class GQARunner:
                 k += 1
         self._trim(batch.segments)
         return res
+
+    @torch.no_grad()
+    def score(self, tokens: list) -> torch.Tensor:
+        """Teacher-forced full logits [T, V] (fp32, CPU) of one sequence through the paged pool (tp = 1): the
+        accuracy gate's input.  Uses a scratch request row; nothing stays allocated."""
+        if self.tp != 1:
+            raise NotImplementedError("score() gathers logits on one rank")
+        r = Request(rid=-1, prompt=list(tokens), params=SamplingParams(max_new_tokens=1))
+        r.slot = next(i for i in range(self.max_running) if all(p["global"].slot != i for p in self.pages.values()))
+        self.attach(r)
+        try:
+            kinds = ("global", "swa", "draft") if self.spec else ("global", "swa")
+            p = self._pack([Segment(r, 0, list(tokens), True)], self.n_q_prefill, kinds)
+            self.kv.sync_tables()
+            self.stage.fill(p)
+            self.stage.upload()
+            st = self.stage.step_tensors(len(p.ids), len(p.kv_len), p.n_q,
+                                         {"global": (1, 1 << 20), "swa": (1, 1 << 20), "draft": (1, 1 << 20)})
+            x, _ = self._target(st)
+            rows = torch.arange(len(tokens), device=self.device)
+            return self.model.logits_local(x[rows], self.model.embed).float().cpu()
+        finally:
+            self.detach(r)
 
     def _trim(self, segs) -> None:
         for s in segs:

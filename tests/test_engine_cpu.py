@@ -93,3 +93,19 @@ def test_spec_policy_math_and_switching():
             pol.observe_plain(1.0)
     assert pol.use_spec(rids) is True and pol.history[-1]["gain"] > 1.5
     assert SpecPolicy(3, "always").use_spec(rids) is True
+
+
+def test_step_trace_records(tmp_path):
+    from inference_optimizations_b200.config import EngineConfig, model_config
+    from inference_optimizations_b200.engine.engine import Engine
+    from inference_optimizations_b200.engine.scheduler import SamplingParams
+    from inference_optimizations_b200.tooling.trace import read
+    ecfg = EngineConfig(model="tiny_gqa", device="cpu", kv_dtype="bf16", max_running=2, chunked_prefill=16,
+                        cuda_graphs=False, trace=str(tmp_path))
+    eng = Engine(ecfg, model_config("tiny_gqa"), max_seq=128)
+    eng.generate([[1, 2, 3] * 10, [4, 5] * 7], SamplingParams(max_new_tokens=3))
+    eng.trace.flush()
+    recs = read(str(tmp_path / "trace.rank0.jsonl"))
+    assert len(recs) == len(eng.stats)
+    assert {r["kind"] for r in recs} >= {"prefill", "decode"}
+    assert all("schedule" in r["phases"] for r in recs) and recs[0]["step"] == 0
