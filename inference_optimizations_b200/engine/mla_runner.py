@@ -68,6 +68,9 @@ class MLARunner:
             if s.logits:
                 logit_rows.append(len(ids) - 1)
         self.kv.table.sync()
+        if self.ecfg.bounds_check:
+            from ..tooling.bounds import check_mla_step
+            check_mla_step(ids, pos, slot, limit, rix, self.kv, self.max_running + 1, self.cfg.vocab)
         dev = self.device
         mk = lambda v: torch.tensor(v, dtype=torch.int32).to(dev, non_blocking=True)  # noqa: E731
         st = MLAStep(mk(ids), mk(pos), mk(slot), mk(limit), mk(rix), self.max_seq + 1)

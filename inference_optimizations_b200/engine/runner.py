@@ -196,7 +196,12 @@ class GQARunner:
                     slot[k].append(-1)
             kvl.append(n_q)
             rix.append(self.dummy_row)
-        return Packed(ids, pos, slot, kvl, rix, n_q, logit_rows, seg_rows)
+        p = Packed(ids, pos, slot, kvl, rix, n_q, logit_rows, seg_rows)
+        if self.ecfg.bounds_check:
+            from ..tooling.bounds import check_gqa_pack
+            self.kv.sync_tables()
+            check_gqa_pack(p, self.kv, self.max_running + 1)
+        return p
 
     # ------------------------------------------------------------------------------------------ forward pieces
     def _target(self, st: StepTensors):

@@ -48,3 +48,21 @@ def test_safetensors_roundtrip_and_tp_sharding(tmp_path):
         mr = GQAModel(cfg, "cpu", r, 2, seed=3)
         assert torch.equal(sh["model.layers.0.self_attn.o_proj.weight"], mr.layers[0].o)
         assert torch.equal(sh["model.embed_tokens.weight"], mr.embed)
+
+
+def test_bounds_check_catches_bad_page_table():
+    import pytest
+    from inference_optimizations_b200.engine.scheduler import SamplingParams
+    from inference_optimizations_b200.tooling.bounds import BoundsError
+    for model in ("tiny_gqa", "tiny_mla"):
+        ecfg = EngineConfig(model=model, device="cpu", kv_dtype="nvfp4", max_running=2, chunked_prefill=32,
+                            cuda_graphs=False, bounds_check=True)
+        eng = Engine(ecfg, model_config(model), max_seq=128)
+        eng.generate([[1, 2, 3] * 5], SamplingParams(max_new_tokens=2))          # clean run passes the checks
+        r = eng.add_request([4, 5, 6] * 5, SamplingParams(max_new_tokens=4))
+        eng.step()                                                               # prefill
+        table = eng.runner.kv.tables["global"] if model == "tiny_gqa" else eng.runner.kv.table
+        table.host[r.slot, 0] = 10 ** 6                                           # corrupt: not a page
+        table._dirty.add(r.slot)
+        with pytest.raises(BoundsError):
+            eng.step()
