@@ -186,6 +186,7 @@ class EngineConfig:
     spec: bool = False
     draft_tokens: int = 3
     spec_policy: str = "adaptive"        # "adaptive": speculate only while it beats plain decode; "always"
+    prefix_cache: bool = True            # radix prefix reuse (MLA family; sliding-window GQA models do not reuse)
     # runtime
     cuda_graphs: bool = True
     graph_batch_sizes: str = "1,2,4,8,16,32,64"

@@ -38,7 +38,7 @@ class Engine:
             from .mla_runner import MLARunner
             self.runner = MLARunner(self.cfg, ecfg, self.device, max_seq, tp_rank, tp)
         self.sched = Scheduler(ecfg.max_running, ecfg.chunked_prefill, ecfg.decode_burst,
-                               can_admit=self.runner.can_admit)
+                               can_admit=self.runner.can_admit, on_admit=getattr(self.runner, "on_admit", None))
         self.stats: list[StepStats] = []
         self.finished: list[Request] = []
         self.spec_policy = SpecPolicy(ecfg.draft_tokens, ecfg.spec_policy)

@@ -35,22 +35,59 @@ class MLARunner:
         self.pages: dict[int, RequestPages] = {}
         self.graphs: dict = {}
         self.event_log = None
+        self.prefix_cache = None
+        if ecfg.prefix_cache:
+            from ..kv.radix import RadixCache
+            self.prefix_cache = RadixCache(self.kv.alloc)
 
     # ------------------------------------------------------------------------------------------ memory
     def can_admit(self, r: Request) -> bool:
         need = (r.prompt_len + r.params.max_new_tokens + 64) // 64 + 1
         reserved = sum(max(0, rp.high_pages - len(rp.pages)) for rp in self.pages.values())
-        return self.kv.alloc.free >= need + reserved
+        short = need + reserved - self.kv.alloc.free
+        if short > 0 and self.prefix_cache is not None:
+            self.prefix_cache.evict(short)
+            short = need + reserved - self.kv.alloc.free
+        return short <= 0
 
     def attach(self, r: Request) -> None:
         rp = RequestPages(self.kv.alloc, self.kv.table, r.slot)
         rp.high_pages = (r.prompt_len + r.params.max_new_tokens + 64) // 64 + 1
+        rp.cached = []
         self.pages[r.rid] = rp
+
+    def on_admit(self, r: Request) -> None:
+        """Reuse the longest cached page-aligned prefix of the prompt (at least one prompt token stays to prefill,
+        it produces the first output's logits)."""
+        self.attach(r)
+        if self.prefix_cache is None:
+            return
+        path = self.prefix_cache.match(r.prompt[: ((r.prompt_len - 1) // 64) * 64])
+        rp = self.pages[r.rid]
+        for lp, node in enumerate(path):
+            rp.pages[lp] = node.page
+            self.kv.table.set(r.slot, lp, node.page)
+        rp.high = len(path)
+        rp.cached = path
+        r.prefilled = r.kv_len = 64 * len(path)
 
     def detach(self, r: Request) -> None:
         rp = self.pages.pop(r.rid, None)
-        if rp is not None:
+        if rp is None:
+            return
+        if self.prefix_cache is None:
             rp.free()
+            return
+        hist = (r.prompt + r.output)[: r.kv_len]
+        full = len(hist) // 64
+        cached = {n.page for n in rp.cached}
+        donate = [rp.pages[lp] for lp in range(full)]
+        rejected = set(self.prefix_cache.insert(hist[: 64 * full], donate))
+        self.prefix_cache.release(rp.cached)
+        keep = set(donate) - rejected
+        self.kv.alloc.release([pg for pg in rp.pages.values() if pg not in keep and pg not in cached])
+        rp.pages.clear()
+        self.kv.table.clear(r.slot)
 
     # ------------------------------------------------------------------------------------------ steps
     def _step(self, segs: list) -> tuple[MLAStep, list]:

@@ -67,7 +67,7 @@ class Batch:
 
 
 class Scheduler:
-    def __init__(self, max_running: int, chunked_prefill: int, decode_burst: int = 1, can_admit=None):
+    def __init__(self, max_running: int, chunked_prefill: int, decode_burst: int = 1, can_admit=None, on_admit=None):
         self.max_running = max_running
         self.chunk = chunked_prefill
         self.burst = decode_burst
@@ -78,6 +78,7 @@ class Scheduler:
         self.last_was_extend: Optional[bool] = None
         self._ids = itertools.count()
         self.can_admit = can_admit or (lambda req: True)
+        self.on_admit = on_admit          # runner hook: may reuse cached KV (sets prefilled / kv_len)
         self.free_slots = list(range(max_running - 1, -1, -1))
 
     def new_request(self, prompt: list, params: SamplingParams) -> Request:
@@ -96,6 +97,8 @@ class Scheduler:
             return None
         self.waiting.popleft()
         r.slot = self.free_slots.pop()
+        if self.on_admit is not None:
+            self.on_admit(r)
         return r
 
     def schedule(self) -> Optional[Batch]:

@@ -44,3 +44,27 @@ def test_router_oracle_group_limits_and_weights():
     assert torch.allclose(w.sum(-1), torch.full((t,), 2.5))
     scores = torch.sigmoid(logits)
     assert torch.allclose(w / 2.5, scores.gather(1, ids.long()) / scores.gather(1, ids.long()).sum(-1, keepdim=True))
+
+
+def test_radix_prefix_cache_reuse_is_exact():
+    torch.manual_seed(5)
+    cfg = model_config("tiny_mla")
+    shared = torch.randint(0, cfg.vocab, (150,)).tolist()
+    a = shared + torch.randint(0, cfg.vocab, (20,)).tolist()
+    b = shared + torch.randint(0, cfg.vocab, (33,)).tolist()
+    eng = _engine()
+    out_a = eng.generate([a], SamplingParams(max_new_tokens=4))[0]
+    held = eng.runner.prefix_cache.held
+    assert held == (150 + 20 + 3) // 64                     # full pages of a's KV (prompt + 3 decoded tokens)
+    r = eng.add_request(b, SamplingParams(max_new_tokens=4))
+    while not r.finished:
+        eng.step()
+    assert eng.runner.prefix_cache.hits == 1
+    # b reused 2 pages (128 tokens) of a's prefix; its tokens equal a cold engine's
+    cold = _engine()
+    cold.runner.prefix_cache = None
+    assert r.output == cold.generate([b], SamplingParams(max_new_tokens=4))[0]
+    # eviction frees unreferenced pages
+    held, free0 = eng.runner.prefix_cache.held, eng.runner.kv.alloc.free
+    assert eng.runner.prefix_cache.clear() == held and eng.runner.prefix_cache.held == 0
+    assert eng.runner.kv.alloc.free == free0 + held
