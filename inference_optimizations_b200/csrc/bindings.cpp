@@ -327,6 +327,99 @@ void moe_route(const at::Tensor& logits, const at::Tensor& bias, at::Tensor ids,
                                scale, stream()));
 }
 
+void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_scale, const at::Tensor& off,
+              const at::Tensor& pairs, const c10::optional<at::Tensor>& pair_w, at::Tensor out,
+              const c10::optional<at::Tensor>& out_scale, at::Tensor status, int64_t n_tiles, int64_t kc, int64_t G,
+              int64_t NT, int64_t mode, int64_t src_div, int64_t src_limit, double out_mul, int64_t num_ctas) {
+  req(wpack, at::kByte, "wpack");
+  req(x, at::kByte, "x");
+  req(x_scale, at::kInt, "x_scale");
+  req(off, at::kInt, "off");
+  req(pairs, at::kInt, "pairs");
+  req(status, at::kInt, "status");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) == kc * 128, "x [rows, KC*128]");
+  TORCH_CHECK(x_scale.dim() == 2 && x_scale.is_contiguous() && x_scale.size(1) == kc && x_scale.size(0) == x.size(0),
+              "x_scale [rows, KC]");
+  const int64_t E = off.numel() - 1;
+  TORCH_CHECK(wpack.numel() == E * n_tiles * kc * G * (16384 + 512), "wpack size");
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "out [pairs, N]");
+  if (mode == iob::kMoeOutSwigluFp8) {
+    req(out, at::kByte, "out");
+    TORCH_CHECK(out_scale.has_value() && out_scale->scalar_type() == at::kInt && out_scale->dim() == 2 &&
+                    out_scale->is_contiguous() && out_scale->size(1) >= n_tiles && out.size(1) >= n_tiles * 128,
+                "out_scale [pairs, n_tiles]");
+  } else {
+    req(out, at::kBFloat16, "out");
+    TORCH_CHECK(out.size(1) >= n_tiles * 128, "out width");
+  }
+  if (mode == iob::kMoeOutBf16Weighted)
+    TORCH_CHECK(pair_w.has_value() && pair_w->scalar_type() == at::kFloat, "pair_w fp32");
+  iob::MoeGemmArgs a{};
+  a.wpack = wpack.data_ptr<uint8_t>();
+  a.x = x.data_ptr<uint8_t>();
+  a.x_scale = reinterpret_cast<const uint32_t*>(x_scale.data_ptr<int>());
+  a.expert_off = off.data_ptr<int>();
+  a.pairs = pairs.data_ptr<int>();
+  a.pair_w = pair_w.has_value() ? pair_w->data_ptr<float>() : nullptr;
+  a.out = out.data_ptr();
+  a.out_scale = out_scale.has_value() ? reinterpret_cast<uint32_t*>(out_scale->data_ptr<int>()) : nullptr;
+  a.status = status.data_ptr<int>();
+  a.E = static_cast<int>(E);
+  a.n_tiles = static_cast<int>(n_tiles);
+  a.KC = static_cast<int>(kc);
+  a.G = static_cast<int>(G);
+  a.NT = static_cast<int>(NT);
+  a.mode = static_cast<int>(mode);
+  a.src_div = static_cast<int>(src_div);
+  a.src_limit = static_cast<int>(src_limit);
+  a.x_stride = static_cast<int>(x.stride(0));
+  a.out_stride = static_cast<int>(out.stride(0));
+  a.out_scale_stride = out_scale.has_value() ? static_cast<int>(out_scale->stride(0)) : 0;
+  a.num_ctas = static_cast<int>(num_ctas);
+  a.out_mul = static_cast<float>(out_mul);
+  const at::cuda::CUDAGuard g(x.device());
+  CHECK_CUDA_OK(iob::moe_gemm(a, stream()));
+}
+
+void moe_align(const at::Tensor& ids, int64_t e0, int64_t E, int64_t extra, at::Tensor off, at::Tensor pairs) {
+  req(ids, at::kInt, "ids");
+  req(off, at::kInt, "off");
+  req(pairs, at::kInt, "pairs");
+  TORCH_CHECK(ids.is_contiguous() && off.numel() == E + (extra > 0 ? 2 : 1) && pairs.numel() >= ids.numel() + extra,
+              "moe_align shapes");
+  const at::cuda::CUDAGuard g(ids.device());
+  CHECK_CUDA_OK(iob::moe_align(ids.data_ptr<int>(), static_cast<int>(ids.numel()), static_cast<int>(e0),
+                               static_cast<int>(E), static_cast<int>(extra), off.data_ptr<int>(), pairs.data_ptr<int>(),
+                               stream()));
+}
+
+void moe_combine(const at::Tensor& rows, int64_t T, int64_t topk, int64_t shared, at::Tensor y) {
+  req(rows, at::kBFloat16, "rows");
+  req(y, at::kBFloat16, "y");
+  TORCH_CHECK(rows.is_contiguous() && y.is_contiguous() && rows.size(1) == y.size(1) &&
+                  rows.size(0) >= T * topk + (shared ? T : 0) && y.size(0) >= T,
+              "moe_combine shapes");
+  const at::cuda::CUDAGuard g(y.device());
+  CHECK_CUDA_OK(iob::moe_combine(rows.data_ptr(), static_cast<int>(T), static_cast<int>(topk),
+                                 static_cast<int>(y.size(1)), static_cast<int>(shared), y.data_ptr(), stream()));
+}
+
+void rmsnorm_quant(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps, double plus_one, at::Tensor q,
+                   at::Tensor sc) {
+  req(x, at::kBFloat16, "x");
+  req(q, at::kByte, "q");
+  req(sc, at::kInt, "sc");
+  TORCH_CHECK(x.is_contiguous() && q.is_contiguous() && sc.is_contiguous() && q.sizes() == x.sizes() &&
+                  sc.size(0) == x.size(0) && sc.size(1) * 128 == x.size(1),
+              "rmsnorm_quant shapes");
+  if (w.has_value()) TORCH_CHECK(w->scalar_type() == at::kBFloat16 && w->numel() == x.size(1), "w");
+  const at::cuda::CUDAGuard g(x.device());
+  CHECK_CUDA_OK(iob::rmsnorm_quant(x.data_ptr(), w.has_value() ? w->data_ptr() : nullptr, static_cast<float>(eps),
+                                   static_cast<float>(plus_one), static_cast<int>(x.size(0)),
+                                   static_cast<int>(x.size(1)), q.data_ptr<uint8_t>(),
+                                   reinterpret_cast<uint32_t*>(sc.data_ptr<int>()), stream()));
+}
+
 void umma_gemm_test(const at::Tensor& A, const at::Tensor& B, at::Tensor C, int64_t sw64) {
   req(A, at::kBFloat16, "A");
   req(B, at::kBFloat16, "B");
@@ -375,6 +468,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("indexer", &indexer);
   m.def("ar_norm2", &ar_norm2);
   m.def("moe_route", &moe_route);
+  m.def("moe_gemm", &moe_gemm);
+  m.def("moe_align", &moe_align);
+  m.def("moe_combine", &moe_combine);
+  m.def("rmsnorm_quant", &rmsnorm_quant);
   m.def("umma_gemm_test", &umma_gemm_test);
   m.def("umma_f8_mn_test", &umma_f8_mn_test);
   m.def("nvfp4_lut_test", &nvfp4_lut_test);

@@ -149,6 +149,27 @@ cudaError_t moe_route(const float* logits, const float* bias, int* ids, float* w
                       int KG, float scale, cudaStream_t s);
 
 // ---- primitive check (umma_test.cu): C[M, N] fp32 = A[M, K] * B[N, K]^T, bf16 inputs, one CTA per 128 rows.
+// ---- grouped block-scaled expert GEMM + routing prep (moe_gemm.cu)
+enum MoeOutMode { kMoeOutBf16 = 0, kMoeOutSwigluFp8 = 1, kMoeOutBf16Weighted = 2 };
+struct MoeGemmArgs {
+  const uint8_t* wpack;       // [E][n_tiles][KC] blocks: G SW128 tiles (128 x 128 B) then G scale atoms (512 B)
+  const uint8_t* x;           // FP8 E4M3 activation rows, row stride x_stride bytes
+  const uint32_t* x_scale;    // UE8M0 x4 words [rows][KC]
+  const int* expert_off;      // [E + 1]
+  const int* pairs;           // pair ids bucketed by expert
+  const float* pair_w;        // per-pair weight (kMoeOutBf16Weighted)
+  void* out;                  // bf16 [pairs][out_stride] or FP8 [pairs][out_stride] (SwiGLU mode)
+  uint32_t* out_scale;        // SwiGLU mode: UE8M0 x4 words [pairs][out_scale_stride]
+  int* status;
+  int E, n_tiles, KC, G, NT, mode, src_div, src_limit, x_stride, out_stride, out_scale_stride, num_ctas;
+  float out_mul;
+};
+cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s);
+cudaError_t moe_align(const int* ids, int P, int e0, int E, int extra, int* off, int* pairs, cudaStream_t s);
+cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared, void* y, cudaStream_t s);
+cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_one, int T, int H, uint8_t* q,
+                          uint32_t* sc, cudaStream_t s);
+
 cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, int sw64, cudaStream_t s);
 cudaError_t umma_f8_mn_test(const void* A, const void* B, float* C, int N, int K, cudaStream_t s);
 cudaError_t umma_rate_test(int n, int count, int nacc, int ts, long long* out, cudaStream_t s);

@@ -1,0 +1,568 @@
+// Grouped, block-scaled expert GEMM on the 5th-generation tensor cores, plus the routing prep it reads.
+//
+//   out[p, n] = sum_k  x[src(p), k] * W_e[n, k]      for every (token, expert) pair p routed to expert e
+//
+// Weights are FP8 E4M3 with one UE8M0 scale per 128 x 128 block, activations FP8 E4M3 with one UE8M0 scale per
+// 1 x 128 block (the DeepSeek-V3 FP8 recipe in its power-of-two-scale form, `moe-gemm/norm-quant-fused/
+// pro_norm_quant.py:1-17`).  The scales are applied INSIDE the MMA: `tcgen05.mma ... kind::mxf8f6f4.block_scale`
+// with one scale per 32 K-values, fed the 128-block scale replicated four times.
+//
+// Swap-AB: the weight tile is the 128-row M operand and the expert's tokens are the N operand (N = 16..128), so a
+// decode step with a handful of tokens per expert streams every touched weight exactly once at full tensor-core
+// width -- the weight-streaming regime the reference's grouped MoE decode GEMMs target
+// (`moe-gemm/w4a4-moe-decode-gemm/moe_decode_gemm.py:1-25`, `moe-gemm/cutedsl-grouped-nvfp4/grouped_gemm.py`).
+//
+// Weights are pre-packed once at load time into UMMA-ready blocks: for (expert, 128-row tile, 128-wide K chunk)
+// G tiles of 128 rows x 128 bytes in the SW128 K-major layout, then their G scale-factor atoms (512 bytes each:
+// row r = r0 + 32 r1 at byte r0 * 16 + r1 * 4 + j, j = the four 32-wide K sub-blocks).  One plain bulk copy per
+// pipeline stage fetches a whole block.  G = 2 packs the gate and up projections of the same 128 FFN columns, so
+// one CTA holds both accumulators and the epilogue applies SwiGLU and re-quantizes to FP8 (per-128 UE8M0 scale)
+// for the down projection without another pass over memory.
+//
+// Activation rows are gathered by pair id with cp.async (16-byte chunks, landing in SW128 order) -- the token
+// permutation never materializes.  Persistent CTAs (one per SM) walk the list of non-empty (expert, token tile,
+// weight tile) items; TMEM holds two accumulator sets when they fit, so the epilogue of one item overlaps the
+// mainloop of the next.
+//
+// Roles (256 threads): warp 0 weight producer (bulk copies), warp 1 MMA issuer + TMEM owner, warps 2-3 activation
+// gather (cp.async), warps 4-7 epilogue (TMEM lanes 32 (w - 4) ..).  Every wait is bounded (status + unwind).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace iob {
+namespace {
+
+constexpr int kMgThreads = 256;
+constexpr uint32_t kTile = 16384;      // 128 rows x 128 bytes
+constexpr uint32_t kSfAtom = 512;      // 128 rows x 4 scale bytes
+constexpr int kMaxExperts = 1024;
+constexpr uint32_t kSmemBudget = 227 * 1024;
+
+template <int NT, int G>
+struct Cfg {
+  static constexpr uint32_t kX = NT * 128;
+  static constexpr uint32_t kSfb = kSfAtom;                       // NT <= 128: one atom
+  static constexpr uint32_t kRaw = G * kTile + kX + G * kSfAtom + kSfb;
+  static constexpr uint32_t kStage = (kRaw + 1023) / 1024 * 1024;
+  static constexpr uint32_t kCtrl = 2048;                         // barriers, work prefix, reduction scratch
+  static constexpr int kStagesFit = (kSmemBudget - kCtrl - 1024) / kStage;
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr int kAccCols = G * NT;
+  static constexpr int kSfCols = 4 * G + 4;
+  static constexpr int kAccBufs = (2 * kAccCols + kSfCols <= 512) ? 2 : 1;
+  static constexpr int kUsed = kAccBufs * kAccCols + kSfCols;
+  static constexpr uint32_t kTmemCols = kUsed <= 32 ? 32 : kUsed <= 64 ? 64 : kUsed <= 128 ? 128 : kUsed <= 256 ? 256 : 512;
+  static constexpr uint32_t kSmem = kCtrl + 1024 + kStages * kStage;
+  static_assert(kStages >= 2, "pipeline too shallow");
+  static_assert(kUsed <= 512, "TMEM overflow");
+  static_assert(kSmem <= kSmemBudget, "smem overflow");
+};
+
+struct MgCtrl {
+  uint64_t w_full[8], x_full[8], empty[8];
+  uint64_t acc_full[2], acc_empty[2], fin;
+  uint32_t tmem_base;
+  int abort;
+  int n_items;
+};
+
+// Shared-memory matrix descriptor for a 32-row x 16-byte no-swizzle source (tcgen05.cp 32x128b): 8-row core
+// matrices 128 bytes apart.
+__device__ __forceinline__ uint64_t desc_sf(uint32_t addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;
+  d |= static_cast<uint64_t>(128 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  return d;
+}
+// smem (32 rows x 128 bits) -> TMEM lanes 0..31, broadcast to all four lane quarters.
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+// Block-scaled E4M3 x E4M3 MMA with UE8M0 scales per 32 K-values (scale TMEM addresses carry the byte index in
+// their top two bits, mirrored in the descriptor's scale-factor id fields).
+__device__ __forceinline__ void umma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+// kind::mxf8f6f4 block-scaled descriptor: E4M3 x E4M3, both K-major, UE8M0 scales, M = 128.
+__host__ __device__ constexpr uint32_t idesc_mxf8(uint32_t n, uint32_t sf_id) {
+  return (sf_id << 4) | (0u << 7) | (0u << 10) | ((n >> 3) << 17) | (1u << 23) | ((128u >> 4) << 24) |
+         (sf_id << 29);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n)); }
+
+// Item i of this launch -> (expert, token tile, weight tile), via the per-expert prefix of item counts.
+__device__ __forceinline__ void item_coords(const int* prefix, int E, int n_tiles, int i, int& e, int& tt, int& nt) {
+  int lo = 0, hi = E;                 // find e with prefix[e] <= i < prefix[e + 1]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (prefix[mid] <= i) lo = mid; else hi = mid;
+  }
+  e = lo;
+  const int local = i - prefix[e];
+  tt = local / n_tiles;
+  nt = local - tt * n_tiles;
+}
+
+// Activation row of pair p: p / src_div for routed pairs, p - src_limit for the shared-expert rows after them.
+__device__ __forceinline__ int src_row(const MoeGemmArgs& a, int p) {
+  return p < a.src_limit ? p / a.src_div : p - a.src_limit;
+}
+
+// UE8M0 exponent of the smallest power of two s with amax / s <= 448 (biased byte, clamped to [1, 253]).
+__device__ __forceinline__ uint32_t ue8m0_for(float amax) {
+  const float x = amax * (1.0f / 448.0f);
+  const uint32_t b = __float_as_uint(x);
+  int e = static_cast<int>((b >> 23) & 0xFF) - 127 + ((b & 0x7FFFFF) ? 1 : 0);
+  if (x == 0.f) e = -126;
+  e = max(-126, min(126, e));
+  return static_cast<uint32_t>(e + 127);
+}
+
+template <int NT, int G>
+__global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmArgs a) {
+  using C = Cfg<NT, G>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  MgCtrl& ctl = *reinterpret_cast<MgCtrl*>(base);
+  int* prefix = reinterpret_cast<int*>(base + 256);                // [E + 1] (E <= 255 here, checked on the host)
+  float* red = reinterpret_cast<float*>(base + 1280);              // [4][NT<=128 chunk of 32]
+  uint8_t* stages = base + C::kCtrl;
+  const int warp = warp_id(), lane = lane_id();
+  volatile int* abort = &ctl.abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&ctl.w_full[s], 1);
+      mbar_init(&ctl.x_full[s], 64);
+      mbar_init(&ctl.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl.acc_full[b], 1);
+      mbar_init(&ctl.acc_empty[b], 128);
+    }
+    mbar_init(&ctl.fin, 1);
+    ctl.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctl.tmem_base, C::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 2) {                    // per-expert prefix of item counts (warp scan over chunks of experts)
+    const int per = (a.E + 31) / 32;
+    int local = 0;
+    for (int j = 0; j < per; ++j) {
+      const int e = lane * per + j;
+      if (e < a.E) {
+        const int cnt = a.expert_off[e + 1] - a.expert_off[e];
+        local += (cnt + NT - 1) / NT * a.n_tiles;
+      }
+    }
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int run = incl - local;
+    for (int j = 0; j < per; ++j) {
+      const int e = lane * per + j;
+      if (e < a.E) {
+        prefix[e] = run;
+        const int cnt = a.expert_off[e + 1] - a.expert_off[e];
+        run += (cnt + NT - 1) / NT * a.n_tiles;
+      }
+    }
+    if (lane == 31) {
+      prefix[a.E] = incl;
+      ctl.n_items = incl;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const int n_items = ctl.n_items;
+  const uint32_t tmem = ctl.tmem_base;
+  const uint32_t sfa_col = C::kAccBufs * C::kAccCols;
+  const uint32_t sfb_col = sfa_col + 4 * G;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- weight producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+        int e, tt, nt;
+        item_coords(prefix, a.E, a.n_tiles, i, e, tt, nt);
+        const uint8_t* src = a.wpack + ((static_cast<size_t>(e) * a.n_tiles + nt) * a.KC) * (G * (kTile + kSfAtom));
+        for (int kc = 0; kc < a.KC; ++kc, ++it) {
+          const uint32_t s = it % C::kStages;
+          if (it >= static_cast<uint32_t>(C::kStages) &&
+              !mbar_wait(&ctl.empty[s], ((it / C::kStages) - 1) & 1, abort, a.status, kTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = stages + s * C::kStage;
+          mbar_expect_tx(&ctl.w_full[s], G * (kTile + kSfAtom));
+          const uint8_t* blk = src + static_cast<size_t>(kc) * (G * (kTile + kSfAtom));
+          bulk_g2s(st, blk, G * kTile, &ctl.w_full[s]);
+          bulk_g2s(st + G * kTile + C::kX, blk + G * kTile, G * kSfAtom, &ctl.w_full[s]);
+        }
+      }
+      // drain: every issued copy has landed before the CTA can exit (bounded, regardless of abort)
+      const uint32_t first = it > static_cast<uint32_t>(C::kStages) ? it - C::kStages : 0;
+      for (uint32_t j = first; j < it; ++j) mbar_wait(&ctl.w_full[j % C::kStages], (j / C::kStages) & 1, nullptr,
+                                                      a.status, kTimeoutProducer);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0;
+      int li = 0;
+      bool ok = true;
+      for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++li) {
+        const int buf = li % C::kAccBufs, use = li / C::kAccBufs;
+        if (use > 0 && !mbar_wait(&ctl.acc_empty[buf], (use - 1) & 1, abort, a.status, kTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * C::kAccCols;
+        for (int kc = 0; kc < a.KC; ++kc, ++it) {
+          const uint32_t s = it % C::kStages, ph = (it / C::kStages) & 1;
+          if (!mbar_wait(&ctl.w_full[s], ph, abort, a.status, kTimeoutMma) ||
+              !mbar_wait(&ctl.x_full[s], ph, abort, a.status, kTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          fence_proxy_async_smem();
+          const uint32_t st = smem_u32(stages + s * C::kStage);
+          const uint32_t x_s = st + G * kTile;
+          const uint32_t sfa_s = x_s + C::kX;
+          const uint32_t sfb_s = sfa_s + G * kSfAtom;
+#pragma unroll
+          for (int g = 0; g < G; ++g) tmem_cp_sf(tmem + sfa_col + 4 * g, desc_sf(sfa_s + g * kSfAtom));
+          tmem_cp_sf(tmem + sfb_col, desc_sf(sfb_s));
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint64_t bd = desc_sw128(x_s + 32 * j);
+            const uint32_t id = idesc_mxf8(NT, j);
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              umma_mxf8(acc + g * NT, desc_sw128(st + g * kTile + 32 * j), bd, id,
+                        (tmem + sfa_col + 4 * g) | (static_cast<uint32_t>(j) << 30),
+                        (tmem + sfb_col) | (static_cast<uint32_t>(j) << 30), (kc | j) ? 1u : 0u);
+            }
+          }
+          umma_commit(&ctl.empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&ctl.acc_full[buf]);
+      }
+      umma_commit(&ctl.fin);          // every MMA issued above has completed before TMEM is freed
+      mbar_wait(&ctl.fin, 0, nullptr, a.status, kTimeoutMma);
+    }
+  } else if (warp < 4) {
+    // ---------------------------------------------------------------- activation gather (64 threads)
+    const int t64 = threadIdx.x - 64;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+      int e, tt, nt;
+      item_coords(prefix, a.E, a.n_tiles, i, e, tt, nt);
+      const int row0 = a.expert_off[e] + tt * NT;
+      const int rows = min(NT, a.expert_off[e + 1] - row0);
+      // rows handled by this thread: r = t64 / 8 + 8 m (chunk t64 % 8); scale rows t64, t64 + 64
+      constexpr int kRpt = NT / 8;
+      const uint8_t* xrow[kRpt];
+#pragma unroll
+      for (int m = 0; m < kRpt; ++m) {
+        const int r = t64 / 8 + 8 * m;
+        xrow[m] = r < rows ? a.x + static_cast<size_t>(src_row(a, a.pairs[row0 + r])) * a.x_stride : nullptr;
+      }
+      const uint32_t* srow[2];
+#pragma unroll
+      for (int m = 0; m < 2; ++m) {
+        const int r = t64 + 64 * m;
+        srow[m] = (r < rows && r < NT) ? a.x_scale + static_cast<size_t>(src_row(a, a.pairs[row0 + r])) * a.KC
+                                       : nullptr;
+      }
+      for (int kc = 0; kc < a.KC; ++kc, ++it) {
+        const uint32_t s = it % C::kStages;
+        if (it >= static_cast<uint32_t>(C::kStages) &&
+            !mbar_wait(&ctl.empty[s], ((it / C::kStages) - 1) & 1, abort, a.status, kTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        const uint32_t x_s = smem_u32(stages + s * C::kStage) + G * kTile;
+        const uint32_t sfb_s = x_s + C::kX + G * kSfAtom;
+        const int c = t64 & 7;
+#pragma unroll
+        for (int m = 0; m < kRpt; ++m) {
+          const int r = t64 / 8 + 8 * m;
+          if (xrow[m]) cp_async16(x_s + sw128_chunk(r, c), xrow[m] + kc * 128 + c * 16);
+        }
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+          const int r = t64 + 64 * m;
+          if (srow[m]) cp_async4(sfb_s + (r & 31) * 16 + (r >> 5) * 4, srow[m] + kc);
+        }
+        cp_async_arrive_noinc(&ctl.x_full[s]);
+      }
+    }
+    cp_async_wait_all();
+  } else {
+    // ---------------------------------------------------------------- epilogue (128 threads)
+    const int q = warp - 4;                       // TMEM lane quarter
+    const int n_local = q * 32 + lane;            // weight row within the 128-row tile
+    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    int li = 0;
+    for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++li) {
+      int e, tt, nt;
+      item_coords(prefix, a.E, a.n_tiles, i, e, tt, nt);
+      const int row0 = a.expert_off[e] + tt * NT;
+      const int rows = min(NT, a.expert_off[e + 1] - row0);
+      const int buf = li % C::kAccBufs, use = li / C::kAccBufs;
+      if (!mbar_wait(&ctl.acc_full[buf], use & 1, abort, a.status, kTimeoutConsumer)) break;
+      tc_fence_after();
+      const uint32_t acc = tmem + lane_addr + buf * C::kAccCols;
+      constexpr int kChunk = NT < 32 ? NT : 32;
+      for (int c0 = 0; c0 < NT; c0 += kChunk) {
+        uint32_t v0[kChunk], v1[kChunk];
+        if constexpr (kChunk == 16) tmem_ld16(acc + c0, v0); else tmem_ld32(acc + c0, v0);
+        if constexpr (G == 2) {
+          if constexpr (kChunk == 16) tmem_ld16(acc + NT + c0, v1); else tmem_ld32(acc + NT + c0, v1);
+        }
+        tmem_ld_wait();
+        if (a.mode == kMoeOutSwigluFp8) {
+          float h[kChunk];
+#pragma unroll
+          for (int t = 0; t < kChunk; ++t) {
+            const float g = __uint_as_float(v0[t]);
+            const float u = G == 2 ? __uint_as_float(v1[t]) : 1.f;
+            h[t] = g / (1.f + __expf(-g)) * u;
+            const float m = warp_max(fabsf(h[t]));
+            if (lane == 0) red[q * 32 + t] = m;
+          }
+          named_bar(1, 128);
+#pragma unroll
+          for (int t = 0; t < kChunk; ++t) {
+            const int r = c0 + t;
+            const float amax = fmaxf(fmaxf(red[t], red[32 + t]), fmaxf(red[64 + t], red[96 + t]));
+            const uint32_t eb = ue8m0_for(amax);
+            if (r < rows) {
+              const int p = a.pairs[row0 + r];
+              const float inv = __uint_as_float((254u - eb) << 23);          // 2^-(eb - 127)
+              reinterpret_cast<uint8_t*>(a.out)[static_cast<size_t>(p) * a.out_stride + nt * 128 + n_local] =
+                  float_to_e4m3(h[t] * inv);
+              if (n_local == 0) a.out_scale[static_cast<size_t>(p) * a.out_scale_stride + nt] = eb * 0x01010101u;
+            }
+          }
+          named_bar(1, 128);
+        } else {
+#pragma unroll
+          for (int t = 0; t < kChunk; ++t) {
+            const int r = c0 + t;
+            if (r < rows) {
+              const int p = a.pairs[row0 + r];
+              float v = __uint_as_float(v0[t]) * a.out_mul;
+              if (a.mode == kMoeOutBf16Weighted) v *= a.pair_w[p];
+              reinterpret_cast<__nv_bfloat16*>(a.out)[static_cast<size_t>(p) * a.out_stride + nt * 128 + n_local] =
+                  __float2bfloat16(v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&ctl.acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+template <int NT, int G>
+cudaError_t launch_mg(const MoeGemmArgs& a, cudaStream_t s) {
+  using C = Cfg<NT, G>;
+  static bool attr = false;
+  if (!attr) {
+    IOB_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(C::kSmem)));
+    attr = true;
+  }
+  moe_gemm_kernel<NT, G><<<a.num_ctas, kMgThreads, C::kSmem, s>>>(a);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------------ routing prep
+// Pairs p (token p / topk, slot p % topk) whose expert lies in [e0, e0 + E) are bucketed by expert: off[E + 1] and
+// pairs sorted by expert (order inside an expert is irrelevant: each pair is its own MMA column).  `extra` rows
+// P .. P + extra - 1 all go to bucket E (a shared expert run as one more group of the same launch).
+__global__ void __launch_bounds__(1024) moe_align_kernel(const int* ids, int P, int e0, int E, int extra, int* off,
+                                                         int* pairs) {
+  __shared__ int cnt[kMaxExperts + 2];
+  __shared__ int pos[kMaxExperts + 2];
+  const int nb = E + (extra > 0 ? 1 : 0);
+  for (int e = threadIdx.x; e < nb; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    const int e = ids[p] - e0;
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  if (threadIdx.x == 0 && extra > 0) cnt[E] = extra;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int e = 0; e < nb; ++e) {
+      off[e] = run;
+      pos[e] = run;
+      run += cnt[e];
+    }
+    off[nb] = run;
+  }
+  __syncthreads();
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    const int e = ids[p] - e0;
+    if (e >= 0 && e < E) pairs[atomicAdd(&pos[e], 1)] = p;
+  }
+  for (int t = threadIdx.x; t < extra; t += blockDim.x) pairs[pos[E] + t] = P + t;
+}
+
+// y[t] = sum_k rows[t * topk + k] (+ rows[P + t] when shared), fp32 in slot order, bf16 out.
+__global__ void moe_combine_kernel(const __nv_bfloat16* rows, int T, int topk, int H, int shared,
+                                   __nv_bfloat16* y) {
+  const int t = blockIdx.x;
+  const int P = T * topk;
+  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int k = 0; k <= topk; ++k) {
+      if (k == topk && !shared) break;
+      const size_t r = k < topk ? static_cast<size_t>(t) * topk + k : static_cast<size_t>(P) + t;
+      const uint4 u = *reinterpret_cast<const uint4*>(rows + r * H + c * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        acc[2 * i] += f.x;
+        acc[2 * i + 1] += f.y;
+      }
+    }
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+      ow[i] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    *reinterpret_cast<uint4*>(y + static_cast<size_t>(t) * H + c * 8) = o;
+  }
+}
+
+// RMSNorm (optional) + FP8 E4M3 quantization with one UE8M0 scale per 128 columns (scale words replicate the
+// exponent byte four times: the layout the block-scaled GEMM gathers).  `w` null: quantize x as is.
+__global__ void rmsnorm_quant_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, float plus_one,
+                                     int H, uint8_t* q, uint32_t* sc) {
+  const int row = blockIdx.x;
+  const __nv_bfloat16* xr = x + static_cast<size_t>(row) * H;
+  __shared__ float red[32];
+  float inv = 1.f;
+  if (w) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      const float v = __bfloat162float(xr[i]);
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if (lane_id() == 0) red[warp_id()] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+      v = warp_sum(v);
+      if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    inv = rsqrtf(red[0] / H + eps);
+  }
+  // one warp per 128-column group: 4 values per lane
+  for (int g = warp_id(); g < H / 128; g += blockDim.x / 32) {
+    float v[4];
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = g * 128 + lane_id() * 4 + j;
+      float f = __bfloat162float(xr[c]);
+      if (w) f = __bfloat162float(__float2bfloat16(f * inv * (__bfloat162float(w[c]) + plus_one)));
+      v[j] = f;
+      m = fmaxf(m, fabsf(f));
+    }
+    m = warp_max(m);
+    const uint32_t eb = ue8m0_for(m);
+    const float s = __uint_as_float((254u - eb) << 23);
+    uint32_t packed = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) packed |= static_cast<uint32_t>(float_to_e4m3(v[j] * s)) << (8 * j);
+    reinterpret_cast<uint32_t*>(q + static_cast<size_t>(row) * H + g * 128)[lane_id()] = packed;
+    if (lane_id() == 0) sc[static_cast<size_t>(row) * (H / 128) + g] = eb * 0x01010101u;
+  }
+}
+
+}  // namespace
+
+cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
+  if (a.E <= 0 || a.E > 255 || a.KC <= 0 || a.n_tiles <= 0 || a.num_ctas <= 0 || a.src_div <= 0 ||
+      (a.x_stride % 16) || (reinterpret_cast<uintptr_t>(a.x) % 16) || (reinterpret_cast<uintptr_t>(a.wpack) % 16) ||
+      (a.mode == kMoeOutSwigluFp8 && a.G != 2))
+    return cudaErrorInvalidValue;
+#define IOB_MG(NT_, G_) \
+  if (a.NT == NT_ && a.G == G_) return launch_mg<NT_, G_>(a, s);
+  IOB_MG(16, 1) IOB_MG(32, 1) IOB_MG(64, 1) IOB_MG(128, 1)
+  IOB_MG(16, 2) IOB_MG(32, 2) IOB_MG(64, 2) IOB_MG(128, 2)
+#undef IOB_MG
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t moe_align(const int* ids, int P, int e0, int E, int extra, int* off, int* pairs, cudaStream_t s) {
+  if (E <= 0 || E > kMaxExperts) return cudaErrorInvalidValue;
+  moe_align_kernel<<<1, 1024, 0, s>>>(ids, P, e0, E, extra, off, pairs);
+  return cudaGetLastError();
+}
+
+cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared, void* y, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (H % 8) return cudaErrorInvalidValue;
+  moe_combine_kernel<<<T, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(rows), T, topk, H, shared,
+                                       static_cast<__nv_bfloat16*>(y));
+  return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_one, int T, int H, uint8_t* q,
+                          uint32_t* sc, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (H % 128) return cudaErrorInvalidValue;
+  rmsnorm_quant_kernel<<<T, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                         static_cast<const __nv_bfloat16*>(w), eps, plus_one, H, q, sc);
+  return cudaGetLastError();
+}
+
+}  // namespace iob

@@ -1,0 +1,181 @@
+"""FP8 block-scaled expert GEMMs (DeepSeek-V3 recipe: E4M3 weights with one power-of-two scale per 128 x 128 block,
+E4M3 activations with one per 1 x 128 block) and the fused MoE feed-forward built on them.
+
+Layouts (the kernel contract of `csrc/moe_gemm.cu`):
+  * activation rows: uint8 E4M3 [rows, K] + int32 scale words [rows, K / 128], each word the UE8M0 exponent byte
+    replicated four times (one byte per 32-wide MMA sub-block);
+  * packed weights: per (expert, 128-row tile, 128-wide K chunk) G tiles of 128 x 128 bytes in the SW128 K-major
+    layout (16-byte chunk c of row r stored at chunk c ^ (r % 8)), then G scale atoms of 512 bytes (row r = r0 +
+    32 r1 at byte 16 r0 + 4 r1 + j).  G = 2 interleaves gate and up rows of the same 128 FFN columns.
+
+Scale rule (`moe-gemm/norm-quant-fused/pro_norm_quant.py:1-17`, UE8M0 form): s = 2^ceil(log2(amax / 448)), q =
+e4m3(x / s); computed exactly from the float bits so kernel and oracle agree.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as Fn
+
+from .._ext import ext
+
+TILE = 128
+INV448 = torch.tensor(1.0 / 448.0, dtype=torch.float32)
+
+
+def ue8m0_exponent(amax: torch.Tensor) -> torch.Tensor:
+    """Biased UE8M0 byte (int32) of the smallest power of two s with amax / s <= 448, clamped to [1, 253]."""
+    x = amax.float() * INV448.to(amax.device)
+    bits = x.view(torch.int32)
+    e = ((bits >> 23) & 0xFF) - 127 + ((bits & 0x7FFFFF) != 0).int()
+    e = torch.where(x == 0, torch.full_like(e, -126), e)
+    return e.clamp(-126, 126) + 127
+
+
+def _pow2(eb: torch.Tensor) -> torch.Tensor:
+    return torch.exp2(eb.float() - 127.0)
+
+
+def quant_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """x [R, K] (K % 128 == 0) -> (q uint8 [R, K], scale words int32 [R, K / 128])."""
+    r, k = x.shape
+    g = x.float().view(r, k // TILE, TILE)
+    eb = ue8m0_exponent(g.abs().amax(-1))
+    q = (g / _pow2(eb)[..., None]).to(torch.float8_e4m3fn).view(torch.uint8).view(r, k)
+    return q, (eb * 0x01010101).to(torch.int32)
+
+
+def dequant_rows(q: torch.Tensor, sc: torch.Tensor) -> torch.Tensor:
+    r, k = q.shape
+    v = q.view(torch.float8_e4m3fn).float().view(r, k // TILE, TILE)
+    return (v * _pow2(sc & 0xFF)[..., None]).view(r, k)
+
+
+def quant_blocks(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """w [..., N, K] -> (q uint8 [..., N, K], exponent bytes uint8 [..., N / 128, K / 128])."""
+    *lead, n, k = w.shape
+    b = w.float().reshape(*lead, n // TILE, TILE, k // TILE, TILE)
+    eb = ue8m0_exponent(b.abs().amax(dim=(-3, -1)))
+    q = (b / _pow2(eb)[..., :, None, :, None]).to(torch.float8_e4m3fn).view(torch.uint8)
+    return q.reshape(*lead, n, k), eb.to(torch.uint8)
+
+
+def dequant_blocks(q: torch.Tensor, eb: torch.Tensor) -> torch.Tensor:
+    *lead, n, k = q.shape
+    v = q.view(torch.float8_e4m3fn).float().reshape(*lead, n // TILE, TILE, k // TILE, TILE)
+    return (v * _pow2(eb.int())[..., :, None, :, None]).reshape(*lead, n, k)
+
+
+def _sw128(tiles: torch.Tensor) -> torch.Tensor:
+    """[..., 128, 128] bytes -> SW128 order (16-byte chunk c of row r at chunk c ^ (r % 8))."""
+    r = torch.arange(TILE, device=tiles.device)
+    idx = (torch.arange(8, device=tiles.device)[None, :] ^ (r[:, None] % 8))          # out[r, j] = in[r, j ^ r%8]
+    t = tiles.reshape(*tiles.shape[:-1], 8, 16)
+    idx = idx.view(*([1] * (t.dim() - 3)), TILE, 8, 1).expand(*t.shape[:-3], TILE, 8, 16)
+    return torch.gather(t, -2, idx).reshape(tiles.shape)
+
+
+def sf_atom(eb_rows: torch.Tensor) -> torch.Tensor:
+    """Per-row exponent bytes [..., 128] -> the 512-byte scale atom (row r0 + 32 r1 at 16 r0 + 4 r1 + j, j < 4)."""
+    v = eb_rows.reshape(*eb_rows.shape[:-1], 4, 32)                 # [.., r1, r0]
+    return v.transpose(-1, -2)[..., None].expand(*eb_rows.shape[:-1], 32, 4, 4).reshape(*eb_rows.shape[:-1], 512)
+
+
+def pack_weights(qs: list, ebs: list) -> torch.Tensor:
+    """Pack G quantized weights that feed the same CTA (each q [E, N, K] uint8 with exponent bytes eb either per
+    128 x 128 block [E, N/128, K/128] or per row and 128-chunk [E, N, K/128]) into
+    [E, N/128, K/128, G * (16384 + 512)] uint8."""
+    E, N, K = qs[0].shape
+    nt, kc = N // TILE, K // TILE
+    tiles, atoms = [], []
+    for q, eb in zip(qs, ebs):
+        t = q.view(E, nt, TILE, kc, TILE).permute(0, 1, 3, 2, 4).contiguous()             # [E, nt, kc, 128, 128]
+        tiles.append(_sw128(t).reshape(E, nt, kc, TILE * TILE))
+        if eb.shape[1] == nt:                                                              # block scale: all rows
+            atoms.append(eb.view(E, nt, kc, 1).expand(E, nt, kc, 512))
+        else:
+            rows = eb.view(E, nt, TILE, kc).permute(0, 1, 3, 2)                            # [E, nt, kc, 128]
+            atoms.append(sf_atom(rows))
+    return torch.cat(tiles + atoms, dim=-1).contiguous()
+
+
+def pick_nt(rows_per_expert: int) -> int:
+    for nt in (16, 32, 64):
+        if rows_per_expert <= nt:
+            return nt
+    return 128
+
+
+class Fp8Experts:
+    """Routed (+ one shared) SwiGLU experts with FP8 block-scaled weights, executed by two grouped GEMM launches:
+    gate/up with fused SwiGLU + FP8 re-quantization, then down with the routing weight folded into the epilogue;
+    a combine kernel sums each token's top-k rows (+ shared) in slot order."""
+
+    def __init__(self, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor,
+                 shared: tuple | None = None, num_ctas: int | None = None):
+        """w_gate / w_up [E, F, H], w_down [E, H, F] (any float dtype, quantized here); shared = (g, u, d) of one
+        expert with the same shapes minus E."""
+        if shared is not None:
+            w_gate = torch.cat([w_gate, shared[0][None]])
+            w_up = torch.cat([w_up, shared[1][None]])
+            w_down = torch.cat([w_down, shared[2][None]])
+        self.has_shared = shared is not None
+        self.E = w_gate.shape[0] - int(self.has_shared)
+        self.F, self.H = w_gate.shape[1], w_gate.shape[2]
+        qg, eg = quant_blocks(w_gate)
+        qu, eu = quant_blocks(w_up)
+        qd, ed = quant_blocks(w_down)
+        self.q = (qg, eg, qu, eu, qd, ed)                        # kept for the oracle
+        self.w1 = pack_weights([qg, qu], [eg, eu])
+        self.w2 = pack_weights([qd], [ed])
+        dev = w_gate.device
+        self.num_ctas = num_ctas or (torch.cuda.get_device_properties(dev).multi_processor_count
+                                     if dev.type == "cuda" else 1)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def dequant(self):
+        qg, eg, qu, eu, qd, ed = self.q
+        return dequant_blocks(qg, eg), dequant_blocks(qu, eu), dequant_blocks(qd, ed)
+
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, nt: int | None = None) -> torch.Tensor:
+        """x bf16 [T, H] (already normalized), ids int32 [T, k] (expert ids in [0, E)), w fp32 [T, k] -> bf16 [T, H]."""
+        t, k = ids.shape
+        dev = x.device
+        P = t * k
+        extra = t if self.has_shared else 0
+        E = self.E + int(self.has_shared)
+        xq = torch.empty(t, self.H, dtype=torch.uint8, device=dev)
+        xs = torch.empty(t, self.H // TILE, dtype=torch.int32, device=dev)
+        ext().rmsnorm_quant(x.contiguous(), None, 0.0, 0.0, xq, xs)
+        off = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        pairs = torch.empty(P + extra, dtype=torch.int32, device=dev)
+        ext().moe_align(ids.contiguous().view(-1), 0, self.E, extra, off, pairs)
+        nt = nt or pick_nt(max(1, -(-2 * P // self.E)))
+        h = torch.empty(P + extra, self.F, dtype=torch.uint8, device=dev)
+        hs = torch.empty(P + extra, self.F // TILE, dtype=torch.int32, device=dev)
+        ext().moe_gemm(self.w1, xq, xs, off, pairs, None, h, hs, self.status, self.F // TILE, self.H // TILE, 2, nt,
+                       1, k, P, 1.0, self.num_ctas)
+        pw = torch.cat([w.float().reshape(-1), torch.ones(extra, device=dev)])
+        rows = torch.empty(P + extra, self.H, dtype=torch.bfloat16, device=dev)
+        ext().moe_gemm(self.w2, h, hs, off, pairs, pw, rows, None, self.status, self.H // TILE, self.F // TILE, 1,
+                       nt, 2, 1, 1 << 30, 1.0, self.num_ctas)
+        y = torch.empty(t, self.H, dtype=torch.bfloat16, device=dev)
+        ext().moe_combine(rows, t, k, int(self.has_shared), y)
+        return y
+
+    def forward_ref(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """fp32 oracle of the same arithmetic: FP8 activations, FP8 SwiGLU output, bf16 rows, fp32 slot-order sum."""
+        wg, wu, wd = (m.to(x.device) for m in self.dequant())
+        t, k = ids.shape
+        xq, xs = quant_rows(x.float())
+        xd = dequant_rows(xq, xs)
+        pairs = [(tt, kk, int(ids[tt, kk])) for tt in range(t) for kk in range(k)]
+        if self.has_shared:
+            pairs += [(tt, -1, self.E) for tt in range(t)]
+        out = torch.zeros(t, self.H, dtype=torch.float32, device=x.device)
+        for tt, kk, e in pairs:
+            hh = Fn.silu(xd[tt] @ wg[e].T) * (xd[tt] @ wu[e].T)
+            hq, hs = quant_rows(hh[None])
+            hd = dequant_rows(hq, hs)[0]
+            r = (hd @ wd[e].T) * (float(w[tt, kk]) if kk >= 0 else 1.0)
+            out[tt] += r.to(torch.bfloat16).float()
+        return out.to(torch.bfloat16)

@@ -1,0 +1,129 @@
+"""Block-scaled grouped expert GEMM (tcgen05 kind::mxf8f6f4) and the FP8 MoE feed-forward against fp32 oracles."""
+import pytest
+import torch
+import torch.nn.functional as Fn
+
+from inference_optimizations_b200.ops import moe_gemm as MG
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(cuda, E, N, K, T, topk, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(E, N, K, generator=g)
+    # per-row weight scales spread over 2^-6 .. 2^6 exercise the A scale-factor layout row by row
+    w = w * torch.exp2(torch.randint(-6, 7, (E, N, 1), generator=g).float())
+    x = torch.randn(T, K, generator=g) * torch.exp2(torch.randint(-8, 9, (T, 1), generator=g).float())
+    ids = torch.randint(0, E, (T, topk), generator=g, dtype=torch.int32)
+    return w, x, ids
+
+
+def _quant_rowwise_weights(w):
+    E, N, K = w.shape
+    q, sc = MG.quant_rows(w.reshape(E * N, K))
+    return q.view(E, N, K), (sc & 0xFF).to(torch.uint8).view(E, N, K // 128), MG.dequant_rows(q, sc).view(E, N, K)
+
+
+@pytest.mark.parametrize("nt", [16, 32, 64, 128])
+@pytest.mark.parametrize("ctas", [148, 3])
+def test_moe_gemm_plain(cuda, nt, ctas):
+    from inference_optimizations_b200._ext import ext
+    E, N, K, T, topk = 3, 256, 384, 37, 2
+    w, x, ids = _case(cuda, E, N, K, T, topk, seed=nt + ctas)
+    wq, web, wd = _quant_rowwise_weights(w)
+    xq, xs = MG.quant_rows(x)
+    xd = MG.dequant_rows(xq, xs)
+    pack = MG.pack_weights([wq], [web]).to(cuda)
+    P = T * topk
+    off = torch.empty(E + 1, dtype=torch.int32, device=cuda)
+    pairs = torch.empty(P, dtype=torch.int32, device=cuda)
+    ext().moe_align(ids.view(-1).to(cuda), 0, E, 0, off, pairs)
+    cnt = torch.bincount(ids.view(-1).long(), minlength=E)
+    assert off.cpu().tolist() == [0] + torch.cumsum(cnt, 0).tolist()
+    out = torch.zeros(P, N, dtype=torch.bfloat16, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    ext().moe_gemm(pack, xq.to(cuda), xs.to(cuda), off, pairs, None, out, None, status, N // 128, K // 128, 1, nt,
+                   0, topk, P, 1.0, ctas)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    ref = torch.stack([xd[p // topk] @ wd[int(ids.view(-1)[p])].T for p in range(P)])
+    got = out.float().cpu()
+    err = (got - ref).abs() / (ref.abs() + 1e-3 * ref.abs().amax(1, keepdim=True))
+    assert err.max().item() < 1e-2, err.max().item()
+
+
+@pytest.mark.parametrize("nt", [16, 64])
+def test_moe_gemm_swiglu_quant(cuda, nt):
+    from inference_optimizations_b200._ext import ext
+    E, F, K, T, topk = 2, 256, 256, 20, 2
+    g = torch.Generator().manual_seed(7)
+    wg = torch.randn(E, F, K, generator=g) * 0.05
+    wu = torch.randn(E, F, K, generator=g) * 0.05
+    x = torch.randn(T, K, generator=g)
+    ids = torch.randint(0, E, (T, topk), generator=g, dtype=torch.int32)
+    qg, eg = MG.quant_blocks(wg)
+    qu, eu = MG.quant_blocks(wu)
+    pack = MG.pack_weights([qg, qu], [eg, eu]).to(cuda)
+    xq, xs = MG.quant_rows(x)
+    xd = MG.dequant_rows(xq, xs)
+    P = T * topk
+    off = torch.empty(E + 1, dtype=torch.int32, device=cuda)
+    pairs = torch.empty(P, dtype=torch.int32, device=cuda)
+    ext().moe_align(ids.view(-1).to(cuda), 0, E, 0, off, pairs)
+    h = torch.zeros(P, F, dtype=torch.uint8, device=cuda)
+    hs = torch.zeros(P, F // 128, dtype=torch.int32, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    ext().moe_gemm(pack, xq.to(cuda), xs.to(cuda), off, pairs, None, h, hs, status, F // 128, K // 128, 2, nt, 1,
+                   topk, P, 1.0, 148)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    dg, du = MG.dequant_blocks(qg, eg), MG.dequant_blocks(qu, eu)
+    e_of = ids.view(-1).long()
+    hh = torch.stack([Fn.silu(xd[p // topk] @ dg[e_of[p]].T) * (xd[p // topk] @ du[e_of[p]].T) for p in range(P)])
+    rq, rs = MG.quant_rows(hh)
+    # scales: the same power of two except where amax sits within float rounding of a boundary
+    assert ((hs.cpu() & 0xFF) == (rs & 0xFF)).float().mean().item() > 0.97
+    got = MG.dequant_rows(h.cpu(), hs.cpu())
+    cos = Fn.cosine_similarity(got.flatten(), hh.flatten(), dim=0).item()
+    assert cos > 0.998, cos
+    assert (h.cpu() == rq).float().mean().item() > 0.95
+
+
+def test_rmsnorm_quant_matches_oracle(cuda):
+    from inference_optimizations_b200._ext import ext
+    torch.manual_seed(3)
+    x = (torch.randn(6, 512) * torch.exp2(torch.randint(-5, 6, (6, 1)).float())).to(torch.bfloat16)
+    q = torch.empty(6, 512, dtype=torch.uint8, device=cuda)
+    sc = torch.empty(6, 4, dtype=torch.int32, device=cuda)
+    ext().rmsnorm_quant(x.to(cuda), None, 0.0, 0.0, q, sc)
+    rq, rs = MG.quant_rows(x.float())
+    assert torch.equal(sc.cpu(), rs) and torch.equal(q.cpu(), rq)
+    w = (torch.randn(512) * 0.1).to(torch.bfloat16)
+    ext().rmsnorm_quant(x.to(cuda), w.to(cuda), 1e-6, 1.0, q, sc)
+    xf = x.float()
+    n = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * (w.float() + 1.0)).to(torch.bfloat16).float()
+    rq, rs = MG.quant_rows(n)
+    assert (q.cpu() == rq).float().mean().item() > 0.99
+    assert torch.equal(sc.cpu(), rs)
+
+
+@pytest.mark.parametrize("shared", [False, True])
+def test_fp8_experts_forward(cuda, shared):
+    torch.manual_seed(11)
+    E, F, H, T, topk = 6, 256, 512, 13, 3
+    wg = torch.randn(E, F, H, device=cuda) * 0.04
+    wu = torch.randn(E, F, H, device=cuda) * 0.04
+    wd = torch.randn(E, H, F, device=cuda) * 0.04
+    sh = tuple(torch.randn(*s, device=cuda) * 0.04 for s in ((F, H), (F, H), (H, F))) if shared else None
+    ex = MG.Fp8Experts(wg, wu, wd, shared=sh)
+    x = torch.randn(T, H, device=cuda).to(torch.bfloat16)
+    ids = torch.stack([torch.randperm(E, device=cuda)[:topk] for _ in range(T)]).int()
+    w = torch.softmax(torch.randn(T, topk, device=cuda), -1)
+    y = ex.forward(x, ids, w)
+    torch.cuda.synchronize()
+    assert ex.status.item() == 0
+    ref = ex.forward_ref(x, ids, w)
+    cos = Fn.cosine_similarity(y.float().flatten(), ref.float().flatten(), dim=0).item()
+    assert cos > 0.999, cos
+    rel = ((y.float() - ref.float()).norm() / ref.float().norm()).item()
+    assert rel < 0.03, rel
