@@ -330,27 +330,34 @@ void moe_route(const at::Tensor& logits, const at::Tensor& bias, at::Tensor ids,
 void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_scale, const at::Tensor& off,
               const at::Tensor& pairs, const c10::optional<at::Tensor>& pair_w, at::Tensor out,
               const c10::optional<at::Tensor>& out_scale, at::Tensor status, int64_t n_tiles, int64_t kc, int64_t G,
-              int64_t NT, int64_t mode, int64_t src_div, int64_t src_limit, double out_mul, int64_t num_ctas) {
+              int64_t NT, int64_t mode, int64_t src_div, int64_t src_limit, double out_mul, int64_t num_ctas,
+              int64_t kind, const c10::optional<at::Tensor>& expert_mul) {
   req(wpack, at::kByte, "wpack");
   req(x, at::kByte, "x");
   req(x_scale, at::kInt, "x_scale");
   req(off, at::kInt, "off");
   req(pairs, at::kInt, "pairs");
   req(status, at::kInt, "status");
-  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) == kc * 128, "x [rows, KC*128]");
-  TORCH_CHECK(x_scale.dim() == 2 && x_scale.is_contiguous() && x_scale.size(1) == kc && x_scale.size(0) == x.size(0),
-              "x_scale [rows, KC]");
+  TORCH_CHECK(kind == 0 || kind == 1, "kind");
+  const int64_t sfw = kind == 0 ? 1 : 4;
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) == kc * 128, "x [rows, KC*128 bytes]");
+  TORCH_CHECK(x_scale.dim() == 2 && x_scale.is_contiguous() && x_scale.size(1) == kc * sfw &&
+                  x_scale.size(0) == x.size(0),
+              "x_scale [rows, KC * words]");
   const int64_t E = off.numel() - 1;
-  TORCH_CHECK(wpack.numel() == E * n_tiles * kc * G * (16384 + 512), "wpack size");
+  TORCH_CHECK(wpack.numel() == E * n_tiles * kc * G * (16384 + 512 * sfw), "wpack size");
+  if (expert_mul.has_value())
+    TORCH_CHECK(expert_mul->scalar_type() == at::kFloat && expert_mul->numel() >= E, "expert_mul fp32 [E]");
   TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "out [pairs, N]");
-  if (mode == iob::kMoeOutSwigluFp8) {
+  if (mode == iob::kMoeOutSwigluQuant) {
     req(out, at::kByte, "out");
     TORCH_CHECK(out_scale.has_value() && out_scale->scalar_type() == at::kInt && out_scale->dim() == 2 &&
-                    out_scale->is_contiguous() && out_scale->size(1) >= n_tiles && out.size(1) >= n_tiles * 128,
-                "out_scale [pairs, n_tiles]");
+                    out_scale->is_contiguous() && out_scale->size(1) >= n_tiles * (kind == 0 ? 1 : 2) &&
+                    out.size(1) >= n_tiles * (kind == 0 ? 128 : 64),
+                "out_scale [pairs, n_tiles words] / out [pairs, F bytes]");
   } else {
     req(out, at::kBFloat16, "out");
-    TORCH_CHECK(out.size(1) >= n_tiles * 128, "out width");
+    TORCH_CHECK(out.size(1) >= n_tiles * G * 128, "out width");
   }
   if (mode == iob::kMoeOutBf16Weighted)
     TORCH_CHECK(pair_w.has_value() && pair_w->scalar_type() == at::kFloat, "pair_w fp32");
@@ -377,6 +384,8 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
   a.out_scale_stride = out_scale.has_value() ? static_cast<int>(out_scale->stride(0)) : 0;
   a.num_ctas = static_cast<int>(num_ctas);
   a.out_mul = static_cast<float>(out_mul);
+  a.kind = static_cast<int>(kind);
+  a.expert_mul = expert_mul.has_value() ? expert_mul->data_ptr<float>() : nullptr;
   const at::cuda::CUDAGuard g(x.device());
   CHECK_CUDA_OK(iob::moe_gemm(a, stream()));
 }
@@ -405,18 +414,20 @@ void moe_combine(const at::Tensor& rows, int64_t T, int64_t topk, int64_t shared
 }
 
 void rmsnorm_quant(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps, double plus_one, at::Tensor q,
-                   at::Tensor sc) {
+                   at::Tensor sc, int64_t fmt) {
   req(x, at::kBFloat16, "x");
   req(q, at::kByte, "q");
   req(sc, at::kInt, "sc");
-  TORCH_CHECK(x.is_contiguous() && q.is_contiguous() && sc.is_contiguous() && q.sizes() == x.sizes() &&
-                  sc.size(0) == x.size(0) && sc.size(1) * 128 == x.size(1),
+  TORCH_CHECK(fmt == 0 || fmt == 1, "fmt");
+  TORCH_CHECK(x.is_contiguous() && q.is_contiguous() && sc.is_contiguous() && q.size(0) == x.size(0) &&
+                  q.size(1) * (fmt == 0 ? 1 : 2) == x.size(1) && sc.size(0) == x.size(0) &&
+                  sc.size(1) * (fmt == 0 ? 128 : 64) == x.size(1),
               "rmsnorm_quant shapes");
   if (w.has_value()) TORCH_CHECK(w->scalar_type() == at::kBFloat16 && w->numel() == x.size(1), "w");
   const at::cuda::CUDAGuard g(x.device());
   CHECK_CUDA_OK(iob::rmsnorm_quant(x.data_ptr(), w.has_value() ? w->data_ptr() : nullptr, static_cast<float>(eps),
                                    static_cast<float>(plus_one), static_cast<int>(x.size(0)),
-                                   static_cast<int>(x.size(1)), q.data_ptr<uint8_t>(),
+                                   static_cast<int>(x.size(1)), static_cast<int>(fmt), q.data_ptr<uint8_t>(),
                                    reinterpret_cast<uint32_t*>(sc.data_ptr<int>()), stream()));
 }
 

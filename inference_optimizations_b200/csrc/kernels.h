@@ -150,24 +150,27 @@ cudaError_t moe_route(const float* logits, const float* bias, int* ids, float* w
 
 // ---- primitive check (umma_test.cu): C[M, N] fp32 = A[M, K] * B[N, K]^T, bf16 inputs, one CTA per 128 rows.
 // ---- grouped block-scaled expert GEMM + routing prep (moe_gemm.cu)
-enum MoeOutMode { kMoeOutBf16 = 0, kMoeOutSwigluFp8 = 1, kMoeOutBf16Weighted = 2 };
+enum MoeOutMode { kMoeOutBf16 = 0, kMoeOutSwigluQuant = 1, kMoeOutBf16Weighted = 2 };
 struct MoeGemmArgs {
-  const uint8_t* wpack;       // [E][n_tiles][KC] blocks: G SW128 tiles (128 x 128 B) then G scale atoms (512 B)
+  const uint8_t* wpack;       // [E][n_tiles][KC] blocks: G SW128 tiles (128 x 128 B) then G scale atoms (512 B);
+                              // plain modes: the G tiles are output columns (nt G + g) 128 ..; SwiGLU: gate, up
   const uint8_t* x;           // FP8 E4M3 activation rows, row stride x_stride bytes
-  const uint32_t* x_scale;    // UE8M0 x4 words [rows][KC]
+  const uint32_t* x_scale;    // kind 0: UE8M0 x4 words [rows][KC]; kind 1: E4M3 bytes [rows][K / 16]
   const int* expert_off;      // [E + 1]
   const int* pairs;           // pair ids bucketed by expert
   const float* pair_w;        // per-pair weight (kMoeOutBf16Weighted)
   void* out;                  // bf16 [pairs][out_stride] or FP8 [pairs][out_stride] (SwiGLU mode)
   uint32_t* out_scale;        // SwiGLU mode: UE8M0 x4 words [pairs][out_scale_stride]
+  const float* expert_mul;    // optional per-expert output multiplier (NVFP4 weight global scales)
   int* status;
   int E, n_tiles, KC, G, NT, mode, src_div, src_limit, x_stride, out_stride, out_scale_stride, num_ctas;
+  int kind;                   // 0: FP8 E4M3 + UE8M0 per 32 (128-blocks replicated); 1: NVFP4 (E2M1 + E4M3 per 16)
   float out_mul;
 };
 cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s);
 cudaError_t moe_align(const int* ids, int P, int e0, int E, int extra, int* off, int* pairs, cudaStream_t s);
 cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared, void* y, cudaStream_t s);
-cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_one, int T, int H, uint8_t* q,
+cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_one, int T, int H, int fmt, uint8_t* q,
                           uint32_t* sc, cudaStream_t s);
 
 cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, int sw64, cudaStream_t s);

@@ -36,19 +36,24 @@ constexpr int kMgThreads = 256;
 constexpr uint32_t kTile = 16384;      // 128 rows x 128 bytes
 constexpr uint32_t kSfAtom = 512;      // 128 rows x 4 scale bytes
 constexpr int kMaxExperts = 1024;
+constexpr int kMaxGemmExperts = 1023;  // buckets per GEMM launch (the work prefix lives in shared memory)
 constexpr uint32_t kSmemBudget = 227 * 1024;
 
-template <int NT, int G>
+// KIND 0: E4M3 operands, UE8M0 scale per 32 K (one scale word per row per 128-byte chunk, 4 MMAs of K = 32 read
+// its four bytes).  KIND 1: packed E2M1 operands (256 values per 128-byte chunk), E4M3 scale per 16 K (four words
+// per row per chunk: MMA j of K = 64 reads word j's four bytes).
+template <int NT, int G, int KIND>
 struct Cfg {
+  static constexpr int kSfw = KIND == 0 ? 1 : 4;                  // scale words (atoms) per row per chunk
   static constexpr uint32_t kX = NT * 128;
-  static constexpr uint32_t kSfb = kSfAtom;                       // NT <= 128: one atom
-  static constexpr uint32_t kRaw = G * kTile + kX + G * kSfAtom + kSfb;
+  static constexpr uint32_t kWBlk = G * (kTile + kSfw * kSfAtom);  // packed weight bytes per stage
+  static constexpr uint32_t kRaw = kWBlk + kX + kSfw * kSfAtom;
   static constexpr uint32_t kStage = (kRaw + 1023) / 1024 * 1024;
-  static constexpr uint32_t kCtrl = 2048;                         // barriers, work prefix, reduction scratch
+  static constexpr uint32_t kCtrl = 5120;                         // barriers, work prefix, reduction scratch
   static constexpr int kStagesFit = (kSmemBudget - kCtrl - 1024) / kStage;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr int kAccCols = G * NT;
-  static constexpr int kSfCols = 4 * G + 4;
+  static constexpr int kSfCols = 4 * kSfw * (G + 1);
   static constexpr int kAccBufs = (2 * kAccCols + kSfCols <= 512) ? 2 : 1;
   static constexpr int kUsed = kAccBufs * kAccCols + kSfCols;
   static constexpr uint32_t kTmemCols = kUsed <= 32 ? 32 : kUsed <= 64 ? 64 : kUsed <= 128 ? 128 : kUsed <= 256 ? 256 : 512;
@@ -90,6 +95,21 @@ __device__ __forceinline__ void umma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint
       "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
       : "memory");
+}
+// Block-scaled packed-E2M1 MMA with E4M3 scales per 16 K-values (NVFP4), K = 64 per instruction.
+__device__ __forceinline__ void umma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+// kind::mxf4nvf4 descriptor: E2M1 x E2M1 (format code 1), both K-major, E4M3 scales, M = 128, K = 64.
+__host__ __device__ constexpr uint32_t idesc_nvf4(uint32_t n) {
+  return (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (0u << 23) | ((128u >> 4) << 24);
 }
 // kind::mxf8f6f4 block-scaled descriptor: E4M3 x E4M3, both K-major, UE8M0 scales, M = 128.
 __host__ __device__ constexpr uint32_t idesc_mxf8(uint32_t n, uint32_t sf_id) {
@@ -137,14 +157,15 @@ __device__ __forceinline__ uint32_t ue8m0_for(float amax) {
   return static_cast<uint32_t>(e + 127);
 }
 
-template <int NT, int G>
+template <int NT, int G, int KIND>
 __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmArgs a) {
-  using C = Cfg<NT, G>;
+  using C = Cfg<NT, G, KIND>;
+  constexpr int kSfw = C::kSfw;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   MgCtrl& ctl = *reinterpret_cast<MgCtrl*>(base);
-  int* prefix = reinterpret_cast<int*>(base + 256);                // [E + 1] (E <= 255 here, checked on the host)
-  float* red = reinterpret_cast<float*>(base + 1280);              // [4][NT<=128 chunk of 32]
+  int* prefix = reinterpret_cast<int*>(base + 256);                // [E + 1], E <= kMaxGemmExperts
+  float* red = reinterpret_cast<float*>(base + 4608);              // [4 warps][32 tokens]
   uint8_t* stages = base + C::kCtrl;
   const int warp = warp_id(), lane = lane_id();
   volatile int* abort = &ctl.abort;
@@ -203,7 +224,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
   const int n_items = ctl.n_items;
   const uint32_t tmem = ctl.tmem_base;
   const uint32_t sfa_col = C::kAccBufs * C::kAccCols;
-  const uint32_t sfb_col = sfa_col + 4 * G;
+  const uint32_t sfb_col = sfa_col + 4 * G * kSfw;
 
   if (warp == 0) {
     // ---------------------------------------------------------------- weight producer
@@ -213,7 +234,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
       for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
         int e, tt, nt;
         item_coords(prefix, a.E, a.n_tiles, i, e, tt, nt);
-        const uint8_t* src = a.wpack + ((static_cast<size_t>(e) * a.n_tiles + nt) * a.KC) * (G * (kTile + kSfAtom));
+        const uint8_t* src = a.wpack + ((static_cast<size_t>(e) * a.n_tiles + nt) * a.KC) * C::kWBlk;
         for (int kc = 0; kc < a.KC; ++kc, ++it) {
           const uint32_t s = it % C::kStages;
           if (it >= static_cast<uint32_t>(C::kStages) &&
@@ -222,10 +243,10 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
             break;
           }
           uint8_t* st = stages + s * C::kStage;
-          mbar_expect_tx(&ctl.w_full[s], G * (kTile + kSfAtom));
-          const uint8_t* blk = src + static_cast<size_t>(kc) * (G * (kTile + kSfAtom));
+          mbar_expect_tx(&ctl.w_full[s], C::kWBlk);
+          const uint8_t* blk = src + static_cast<size_t>(kc) * C::kWBlk;
           bulk_g2s(st, blk, G * kTile, &ctl.w_full[s]);
-          bulk_g2s(st + G * kTile + C::kX, blk + G * kTile, G * kSfAtom, &ctl.w_full[s]);
+          bulk_g2s(st + G * kTile + C::kX, blk + G * kTile, G * kSfw * kSfAtom, &ctl.w_full[s]);
         }
       }
       // drain: every issued copy has landed before the CTA can exit (bounded, regardless of abort)
@@ -256,19 +277,24 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
           const uint32_t st = smem_u32(stages + s * C::kStage);
           const uint32_t x_s = st + G * kTile;
           const uint32_t sfa_s = x_s + C::kX;
-          const uint32_t sfb_s = sfa_s + G * kSfAtom;
+          const uint32_t sfb_s = sfa_s + G * kSfw * kSfAtom;
 #pragma unroll
-          for (int g = 0; g < G; ++g) tmem_cp_sf(tmem + sfa_col + 4 * g, desc_sf(sfa_s + g * kSfAtom));
-          tmem_cp_sf(tmem + sfb_col, desc_sf(sfb_s));
+          for (int w = 0; w < G * kSfw; ++w) tmem_cp_sf(tmem + sfa_col + 4 * w, desc_sf(sfa_s + w * kSfAtom));
+#pragma unroll
+          for (int w = 0; w < kSfw; ++w) tmem_cp_sf(tmem + sfb_col + 4 * w, desc_sf(sfb_s + w * kSfAtom));
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint64_t bd = desc_sw128(x_s + 32 * j);
-            const uint32_t id = idesc_mxf8(NT, j);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-              umma_mxf8(acc + g * NT, desc_sw128(st + g * kTile + 32 * j), bd, id,
-                        (tmem + sfa_col + 4 * g) | (static_cast<uint32_t>(j) << 30),
-                        (tmem + sfb_col) | (static_cast<uint32_t>(j) << 30), (kc | j) ? 1u : 0u);
+              if constexpr (KIND == 0) {
+                umma_mxf8(acc + g * NT, desc_sw128(st + g * kTile + 32 * j), bd, idesc_mxf8(NT, j),
+                          (tmem + sfa_col + 4 * g) | (static_cast<uint32_t>(j) << 30),
+                          (tmem + sfb_col) | (static_cast<uint32_t>(j) << 30), (kc | j) ? 1u : 0u);
+              } else {
+                umma_nvf4(acc + g * NT, desc_sw128(st + g * kTile + 32 * j), bd, idesc_nvf4(NT),
+                          tmem + sfa_col + 4 * (g * 4 + j), tmem + sfb_col + 4 * j, (kc | j) ? 1u : 0u);
+              }
             }
           }
           umma_commit(&ctl.empty[s]);
@@ -301,8 +327,9 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
 #pragma unroll
       for (int m = 0; m < 2; ++m) {
         const int r = t64 + 64 * m;
-        srow[m] = (r < rows && r < NT) ? a.x_scale + static_cast<size_t>(src_row(a, a.pairs[row0 + r])) * a.KC
-                                       : nullptr;
+        srow[m] = (r < rows && r < NT)
+                      ? a.x_scale + static_cast<size_t>(src_row(a, a.pairs[row0 + r])) * (a.KC * kSfw)
+                      : nullptr;
       }
       for (int kc = 0; kc < a.KC; ++kc, ++it) {
         const uint32_t s = it % C::kStages;
@@ -312,7 +339,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
           break;
         }
         const uint32_t x_s = smem_u32(stages + s * C::kStage) + G * kTile;
-        const uint32_t sfb_s = x_s + C::kX + G * kSfAtom;
+        const uint32_t sfb_s = x_s + C::kX + G * kSfw * kSfAtom;
         const int c = t64 & 7;
 #pragma unroll
         for (int m = 0; m < kRpt; ++m) {
@@ -322,7 +349,11 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
 #pragma unroll
         for (int m = 0; m < 2; ++m) {
           const int r = t64 + 64 * m;
-          if (srow[m]) cp_async4(sfb_s + (r & 31) * 16 + (r >> 5) * 4, srow[m] + kc);
+          if (srow[m]) {
+#pragma unroll
+            for (int w = 0; w < kSfw; ++w)
+              cp_async4(sfb_s + w * kSfAtom + (r & 31) * 16 + (r >> 5) * 4, srow[m] + kc * kSfw + w);
+          }
         }
         cp_async_arrive_noinc(&ctl.x_full[s]);
       }
@@ -343,6 +374,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
       if (!mbar_wait(&ctl.acc_full[buf], use & 1, abort, a.status, kTimeoutConsumer)) break;
       tc_fence_after();
       const uint32_t acc = tmem + lane_addr + buf * C::kAccCols;
+      const float emul = a.out_mul * (a.expert_mul ? a.expert_mul[e] : 1.f);
       constexpr int kChunk = NT < 32 ? NT : 32;
       for (int c0 = 0; c0 < NT; c0 += kChunk) {
         uint32_t v0[kChunk], v1[kChunk];
@@ -351,12 +383,12 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
           if constexpr (kChunk == 16) tmem_ld16(acc + NT + c0, v1); else tmem_ld32(acc + NT + c0, v1);
         }
         tmem_ld_wait();
-        if (a.mode == kMoeOutSwigluFp8) {
+        if (a.mode == kMoeOutSwigluQuant && KIND == 0) {
           float h[kChunk];
 #pragma unroll
           for (int t = 0; t < kChunk; ++t) {
-            const float g = __uint_as_float(v0[t]);
-            const float u = G == 2 ? __uint_as_float(v1[t]) : 1.f;
+            const float g = __uint_as_float(v0[t]) * emul;
+            const float u = G == 2 ? __uint_as_float(v1[t]) * emul : 1.f;
             h[t] = g / (1.f + __expf(-g)) * u;
             const float m = warp_max(fabsf(h[t]));
             if (lane == 0) red[q * 32 + t] = m;
@@ -376,16 +408,44 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
             }
           }
           named_bar(1, 128);
-        } else {
+        } else if (a.mode == kMoeOutSwigluQuant) {
+          // NVFP4 output: 16 consecutive columns (16 lanes) share one E4M3 scale; element 2i in the low nibble
 #pragma unroll
           for (int t = 0; t < kChunk; ++t) {
+            const float g = __uint_as_float(v0[t]) * emul;
+            const float u = G == 2 ? __uint_as_float(v1[t]) * emul : 1.f;
+            const float h = g / (1.f + __expf(-g)) * u;
+            float m = fabsf(h);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const uint8_t sb = nvfp4_block_scale(m);
+            const uint32_t code = e2m1_code(h / e4m3_to_float(sb));
+            const uint32_t hi = __shfl_down_sync(0xffffffffu, code, 1);
             const int r = c0 + t;
             if (r < rows) {
               const int p = a.pairs[row0 + r];
-              float v = __uint_as_float(v0[t]) * a.out_mul;
-              if (a.mode == kMoeOutBf16Weighted) v *= a.pair_w[p];
-              reinterpret_cast<__nv_bfloat16*>(a.out)[static_cast<size_t>(p) * a.out_stride + nt * 128 + n_local] =
-                  __float2bfloat16(v);
+              const int col = nt * 128 + n_local;
+              if ((lane & 1) == 0)
+                reinterpret_cast<uint8_t*>(a.out)[static_cast<size_t>(p) * a.out_stride + col / 2] =
+                    static_cast<uint8_t>(code | (hi << 4));
+              if ((lane & 15) == 0)
+                reinterpret_cast<uint8_t*>(a.out_scale)[static_cast<size_t>(p) * a.out_scale_stride * 4 + col / 16] =
+                    sb;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+#pragma unroll
+            for (int t = 0; t < kChunk; ++t) {
+              const int r = c0 + t;
+              if (r < rows) {
+                const int p = a.pairs[row0 + r];
+                float v = __uint_as_float(g == 0 ? v0[t] : v1[t]) * emul;
+                if (a.mode == kMoeOutBf16Weighted) v *= a.pair_w[p];
+                reinterpret_cast<__nv_bfloat16*>(a.out)[static_cast<size_t>(p) * a.out_stride +
+                                                        (nt * G + g) * 128 + n_local] = __float2bfloat16(v);
+              }
             }
           }
         }
@@ -402,16 +462,16 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
   }
 }
 
-template <int NT, int G>
+template <int NT, int G, int KIND>
 cudaError_t launch_mg(const MoeGemmArgs& a, cudaStream_t s) {
-  using C = Cfg<NT, G>;
+  using C = Cfg<NT, G, KIND>;
   static bool attr = false;
   if (!attr) {
-    IOB_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    IOB_CUDA_CHECK(cudaFuncSetAttribute(moe_gemm_kernel<NT, G, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(C::kSmem)));
     attr = true;
   }
-  moe_gemm_kernel<NT, G><<<a.num_ctas, kMgThreads, C::kSmem, s>>>(a);
+  moe_gemm_kernel<NT, G, KIND><<<a.num_ctas, kMgThreads, C::kSmem, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -479,10 +539,12 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* rows, int T, int topk, i
   }
 }
 
-// RMSNorm (optional) + FP8 E4M3 quantization with one UE8M0 scale per 128 columns (scale words replicate the
-// exponent byte four times: the layout the block-scaled GEMM gathers).  `w` null: quantize x as is.
+// RMSNorm (optional) + quantization of a row for the block-scaled GEMM.  fmt 0: FP8 E4M3 with one UE8M0 scale per
+// 128 columns (scale words replicate the exponent byte four times: the layout the GEMM gathers).  fmt 1: NVFP4 --
+// E2M1 pairs (element 2i in the low nibble) with one E4M3 scale e4m3(clamp(amax / 6, 2^-9, 448)) per 16 columns.
+// `w` null: quantize x as is.
 __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, float plus_one,
-                                     int H, uint8_t* q, uint32_t* sc) {
+                                     int H, int fmt, uint8_t* q, uint32_t* sc) {
   const int row = blockIdx.x;
   const __nv_bfloat16* xr = x + static_cast<size_t>(row) * H;
   __shared__ float red[32];
@@ -504,40 +566,67 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* x, const __nv_bfloat16
     __syncthreads();
     inv = rsqrtf(red[0] / H + eps);
   }
-  // one warp per 128-column group: 4 values per lane
-  for (int g = warp_id(); g < H / 128; g += blockDim.x / 32) {
-    float v[4];
-    float m = 0.f;
+  auto val = [&](int c) {
+    float f = __bfloat162float(xr[c]);
+    if (w) f = __bfloat162float(__float2bfloat16(f * inv * (__bfloat162float(w[c]) + plus_one)));
+    return f;
+  };
+  if (fmt == 0) {
+    // one warp per 128-column group: 4 values per lane
+    for (int g = warp_id(); g < H / 128; g += blockDim.x / 32) {
+      float v[4];
+      float m = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = g * 128 + lane_id() * 4 + j;
-      float f = __bfloat162float(xr[c]);
-      if (w) f = __bfloat162float(__float2bfloat16(f * inv * (__bfloat162float(w[c]) + plus_one)));
-      v[j] = f;
-      m = fmaxf(m, fabsf(f));
+      for (int j = 0; j < 4; ++j) {
+        v[j] = val(g * 128 + lane_id() * 4 + j);
+        m = fmaxf(m, fabsf(v[j]));
+      }
+      m = warp_max(m);
+      const uint32_t eb = ue8m0_for(m);
+      const float s = __uint_as_float((254u - eb) << 23);
+      uint32_t packed = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) packed |= static_cast<uint32_t>(float_to_e4m3(v[j] * s)) << (8 * j);
+      reinterpret_cast<uint32_t*>(q + static_cast<size_t>(row) * H + g * 128)[lane_id()] = packed;
+      if (lane_id() == 0) sc[static_cast<size_t>(row) * (H / 128) + g] = eb * 0x01010101u;
     }
-    m = warp_max(m);
-    const uint32_t eb = ue8m0_for(m);
-    const float s = __uint_as_float((254u - eb) << 23);
-    uint32_t packed = 0;
+  } else {
+    // one thread per 16-column block
+    uint8_t* sb_row = reinterpret_cast<uint8_t*>(sc) + static_cast<size_t>(row) * (H / 16);
+    for (int b = threadIdx.x; b < H / 16; b += blockDim.x) {
+      float v[16];
+      float m = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) packed |= static_cast<uint32_t>(float_to_e4m3(v[j] * s)) << (8 * j);
-    reinterpret_cast<uint32_t*>(q + static_cast<size_t>(row) * H + g * 128)[lane_id()] = packed;
-    if (lane_id() == 0) sc[static_cast<size_t>(row) * (H / 128) + g] = eb * 0x01010101u;
+      for (int j = 0; j < 16; ++j) {
+        v[j] = val(b * 16 + j);
+        m = fmaxf(m, fabsf(v[j]));
+      }
+      const uint8_t sb = nvfp4_block_scale(m);
+      const float sf = e4m3_to_float(sb);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) lo |= e2m1_code(v[j] / sf) << (4 * j);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) hi |= e2m1_code(v[8 + j] / sf) << (4 * j);
+      *reinterpret_cast<uint2*>(q + static_cast<size_t>(row) * (H / 2) + b * 8) = make_uint2(lo, hi);
+      sb_row[b] = sb;
+    }
   }
 }
 
 }  // namespace
 
 cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
-  if (a.E <= 0 || a.E > 255 || a.KC <= 0 || a.n_tiles <= 0 || a.num_ctas <= 0 || a.src_div <= 0 ||
+  if (a.E <= 0 || a.E > kMaxGemmExperts || a.KC <= 0 || a.n_tiles <= 0 || a.num_ctas <= 0 || a.src_div <= 0 ||
       (a.x_stride % 16) || (reinterpret_cast<uintptr_t>(a.x) % 16) || (reinterpret_cast<uintptr_t>(a.wpack) % 16) ||
-      (a.mode == kMoeOutSwigluFp8 && a.G != 2))
+      (a.mode == kMoeOutSwigluQuant && a.G != 2) || a.kind < 0 || a.kind > 1)
     return cudaErrorInvalidValue;
-#define IOB_MG(NT_, G_) \
-  if (a.NT == NT_ && a.G == G_) return launch_mg<NT_, G_>(a, s);
-  IOB_MG(16, 1) IOB_MG(32, 1) IOB_MG(64, 1) IOB_MG(128, 1)
-  IOB_MG(16, 2) IOB_MG(32, 2) IOB_MG(64, 2) IOB_MG(128, 2)
+#define IOB_MG(NT_, G_, K_) \
+  if (a.NT == NT_ && a.G == G_ && a.kind == K_) return launch_mg<NT_, G_, K_>(a, s);
+  IOB_MG(16, 1, 0) IOB_MG(32, 1, 0) IOB_MG(64, 1, 0) IOB_MG(128, 1, 0)
+  IOB_MG(16, 2, 0) IOB_MG(32, 2, 0) IOB_MG(64, 2, 0) IOB_MG(128, 2, 0)
+  IOB_MG(16, 1, 1) IOB_MG(32, 1, 1) IOB_MG(64, 1, 1) IOB_MG(128, 1, 1)
+  IOB_MG(16, 2, 1) IOB_MG(32, 2, 1) IOB_MG(64, 2, 1) IOB_MG(128, 2, 1)
 #undef IOB_MG
   return cudaErrorInvalidValue;
 }
@@ -556,12 +645,12 @@ cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared, vo
   return cudaGetLastError();
 }
 
-cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_one, int T, int H, uint8_t* q,
+cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_one, int T, int H, int fmt, uint8_t* q,
                           uint32_t* sc, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  if (H % 128) return cudaErrorInvalidValue;
+  if ((fmt == 0 && H % 128) || (fmt == 1 && H % 64) || fmt < 0 || fmt > 1) return cudaErrorInvalidValue;
   rmsnorm_quant_kernel<<<T, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
-                                         static_cast<const __nv_bfloat16*>(w), eps, plus_one, H, q, sc);
+                                         static_cast<const __nv_bfloat16*>(w), eps, plus_one, H, fmt, q, sc);
   return cudaGetLastError();
 }
 

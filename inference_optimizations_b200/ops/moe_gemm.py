@@ -10,6 +10,11 @@ Layouts (the kernel contract of `csrc/moe_gemm.cu`):
 
 Scale rule (`moe-gemm/norm-quant-fused/pro_norm_quant.py:1-17`, UE8M0 form): s = 2^ceil(log2(amax / 448)), q =
 e4m3(x / s); computed exactly from the float bits so kernel and oracle agree.
+
+NVFP4 experts (W4A4, the GLM-5 / Kimi serving format; `moe-gemm/w4a4-moe-decode-gemm/moe_decode_gemm.py:1-25`,
+`moe-gemm/cutedsl-grouped-nvfp4/nvfp4_layout.py:1-20`): weights E2M1 with one E4M3 scale per 16 values and one fp32
+global scale per expert (gate and up share it), activations E2M1 + E4M3 per 16 (global 1).  Same 128-byte K chunks
+(256 values), four scale atoms per tile per chunk (MMA j of K = 64 reads atom j).
 """
 from __future__ import annotations
 
@@ -17,6 +22,7 @@ import torch
 import torch.nn.functional as Fn
 
 from .._ext import ext
+from . import formats as FM
 
 TILE = 128
 INV448 = torch.tensor(1.0 / 448.0, dtype=torch.float32)
@@ -75,9 +81,13 @@ def _sw128(tiles: torch.Tensor) -> torch.Tensor:
 
 
 def sf_atom(eb_rows: torch.Tensor) -> torch.Tensor:
-    """Per-row exponent bytes [..., 128] -> the 512-byte scale atom (row r0 + 32 r1 at 16 r0 + 4 r1 + j, j < 4)."""
-    v = eb_rows.reshape(*eb_rows.shape[:-1], 4, 32)                 # [.., r1, r0]
-    return v.transpose(-1, -2)[..., None].expand(*eb_rows.shape[:-1], 32, 4, 4).reshape(*eb_rows.shape[:-1], 512)
+    """Scale bytes of 128 rows -> the 512-byte scale atom (row r0 + 32 r1 at 16 r0 + 4 r1 + j, j < 4).  eb_rows is
+    [..., 128] (one byte per row, replicated over j) or [..., 128, 4] (byte j of each row)."""
+    if eb_rows.shape[-1] != 4 or eb_rows.dim() == 1:
+        eb_rows = eb_rows[..., None].expand(*eb_rows.shape, 4)
+    lead = eb_rows.shape[:-2]
+    v = eb_rows.reshape(*lead, 4, 32, 4)                            # [.., r1, r0, j]
+    return v.transpose(-2, -3).reshape(*lead, 512)
 
 
 def pack_weights(qs: list, ebs: list) -> torch.Tensor:
@@ -98,6 +108,65 @@ def pack_weights(qs: list, ebs: list) -> torch.Tensor:
     return torch.cat(tiles + atoms, dim=-1).contiguous()
 
 
+def pack_weights_paired(q: torch.Tensor, eb: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """Plain-output weights: when N % 256 == 0 pack output tiles 2j and 2j + 1 into one block (one CTA computes
+    256 output columns per item: half the items and weight-tile issue overhead).  Returns (packed, G)."""
+    E, N, K = q.shape
+    if N % 256:
+        return pack_weights([q], [eb]), 1
+    qv = q.view(E, N // 256, 2, TILE, K)
+    per_row = eb.shape[1] == N
+    ev = eb.view(E, N // 256, 2, TILE, -1) if per_row else eb.view(E, N // 256, 2, -1)
+    qs = [qv[:, :, g].reshape(E, N // 2, K) for g in range(2)]
+    es = [ev[:, :, g].reshape(E, N // 2, -1) if per_row else ev[:, :, g] for g in range(2)]
+    return pack_weights(qs, es), 2
+
+
+def quant_nvfp4_weights(w: torch.Tensor, groups: int = 1) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """w [E, N, K] -> (E2M1 pairs uint8 [E, N, K/2], E4M3 scale bytes uint8 [E, N, K/16], global fp32 [E]); the
+    global scale is amax / (448 * 6) over each expert (over `groups` consecutive N-blocks jointly when gate and up
+    are stacked: pass them concatenated along N with groups = 1)."""
+    E, N, K = w.shape
+    qs, ss, gs = [], [], []
+    for e in range(E):
+        g = max(float(w[e].abs().amax()) / (448.0 * 6.0), 1e-30)
+        q, s8 = FM.nvfp4_quantize(w[e].float(), g)
+        qs.append(q)
+        ss.append(s8.view(torch.uint8))
+        gs.append(g)
+    return torch.stack(qs), torch.stack(ss), torch.tensor(gs, dtype=torch.float32, device=w.device)
+
+
+def dequant_nvfp4_weights(q: torch.Tensor, s8: torch.Tensor, gs: torch.Tensor) -> torch.Tensor:
+    return torch.stack([FM.nvfp4_dequantize(q[e], s8[e].view(torch.float8_e4m3fn), float(gs[e]))
+                        for e in range(q.shape[0])])
+
+
+def quant_nvfp4_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """x [R, K] -> (E2M1 pairs uint8 [R, K/2], E4M3 scale bytes as int32 words [R, K/64]) with global scale 1."""
+    q, s8 = FM.nvfp4_quantize(x.float(), 1.0)
+    return q, s8.view(torch.uint8).contiguous().view(torch.int32)
+
+
+def dequant_nvfp4_rows(q: torch.Tensor, sc: torch.Tensor) -> torch.Tensor:
+    return FM.nvfp4_dequantize(q, sc.contiguous().view(torch.uint8).view(torch.float8_e4m3fn), 1.0)
+
+
+def pack_weights_nvfp4(qs: list, scs: list) -> torch.Tensor:
+    """Pack G NVFP4 weights (each E2M1 pairs [E, N, K/2], scale bytes [E, N, K/16]) into
+    [E, N/128, K/256, G * (16384 + 4 * 512)] uint8: G SW128 tiles, then atoms [g][j] (MMA j of the chunk)."""
+    E, N, Kh = qs[0].shape
+    nt, kc = N // TILE, Kh // TILE
+    tiles, atoms = [], []
+    for q in qs:
+        t = q.reshape(E, nt, TILE, kc, TILE).permute(0, 1, 3, 2, 4).contiguous()
+        tiles.append(_sw128(t).reshape(E, nt, kc, TILE * TILE))
+    for sc in scs:
+        v = sc.reshape(E, nt, TILE, kc, 4, 4).permute(0, 1, 3, 4, 2, 5)                  # [E, nt, kc, j, 128, 4]
+        atoms.append(sf_atom(v).reshape(E, nt, kc, 4 * 512))
+    return torch.cat(tiles + atoms, dim=-1).contiguous()
+
+
 def pick_nt(rows_per_expert: int) -> int:
     for nt in (16, 32, 64):
         if rows_per_expert <= nt:
@@ -105,36 +174,64 @@ def pick_nt(rows_per_expert: int) -> int:
     return 128
 
 
-class Fp8Experts:
-    """Routed (+ one shared) SwiGLU experts with FP8 block-scaled weights, executed by two grouped GEMM launches:
-    gate/up with fused SwiGLU + FP8 re-quantization, then down with the routing weight folded into the epilogue;
-    a combine kernel sums each token's top-k rows (+ shared) in slot order."""
+class BlockScaledExperts:
+    """Routed (+ one shared) SwiGLU experts with block-scaled weights (fmt "fp8": E4M3 + UE8M0 per 128 x 128;
+    "nvfp4": E2M1 + E4M3 per 16 + fp32 per expert), executed by two grouped GEMM launches: gate/up with fused
+    SwiGLU + re-quantization (to the same format), then down with the routing weight folded into the epilogue; a
+    combine kernel sums each token's top-k rows (+ shared) in slot order."""
 
     def __init__(self, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor,
-                 shared: tuple | None = None, num_ctas: int | None = None):
-        """w_gate / w_up [E, F, H], w_down [E, H, F] (any float dtype, quantized here); shared = (g, u, d) of one
-        expert with the same shapes minus E."""
+                 shared: tuple | None = None, fmt: str = "fp8", num_ctas: int | None = None):
+        """w_gate / w_up [E, F, H], w_down [E, H, F] (any float dtype, quantized here one expert at a time);
+        shared = (g, u, d) of one expert with the same shapes minus E."""
         if shared is not None:
             w_gate = torch.cat([w_gate, shared[0][None]])
             w_up = torch.cat([w_up, shared[1][None]])
             w_down = torch.cat([w_down, shared[2][None]])
+        self.fmt, self.kind = fmt, {"fp8": 0, "nvfp4": 1}[fmt]
         self.has_shared = shared is not None
         self.E = w_gate.shape[0] - int(self.has_shared)
         self.F, self.H = w_gate.shape[1], w_gate.shape[2]
-        qg, eg = quant_blocks(w_gate)
-        qu, eu = quant_blocks(w_up)
-        qd, ed = quant_blocks(w_down)
-        self.q = (qg, eg, qu, eu, qd, ed)                        # kept for the oracle
-        self.w1 = pack_weights([qg, qu], [eg, eu])
-        self.w2 = pack_weights([qd], [ed])
         dev = w_gate.device
+        if fmt == "fp8":
+            qg, eg = quant_blocks(w_gate)
+            qu, eu = quant_blocks(w_up)
+            qd, ed = quant_blocks(w_down)
+            self.q = (qg, eg, qu, eu, qd, ed)
+            self.w1 = pack_weights([qg, qu], [eg, eu])
+            self.w2, self.g2 = pack_weights_paired(qd, ed)
+            self.mul1 = self.mul2 = None
+        else:
+            qgu, sgu, ggu = quant_nvfp4_weights(torch.cat([w_gate, w_up], dim=1))   # gate and up share a global
+            qd, sd, gd = quant_nvfp4_weights(w_down)
+            F = self.F
+            self.q = (qgu, sgu, ggu, qd, sd, gd)
+            self.w1 = pack_weights_nvfp4([qgu[:, :F], qgu[:, F:]], [sgu[:, :F], sgu[:, F:]])
+            self.w2 = pack_weights_nvfp4([qd], [sd])
+            self.g2 = 1
+            self.mul1, self.mul2 = ggu, gd
         self.num_ctas = num_ctas or (torch.cuda.get_device_properties(dev).multi_processor_count
                                      if dev.type == "cuda" else 1)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def dequant(self):
-        qg, eg, qu, eu, qd, ed = self.q
-        return dequant_blocks(qg, eg), dequant_blocks(qu, eu), dequant_blocks(qd, ed)
+        if self.fmt == "fp8":
+            qg, eg, qu, eu, qd, ed = self.q
+            return dequant_blocks(qg, eg), dequant_blocks(qu, eu), dequant_blocks(qd, ed)
+        qgu, sgu, ggu, qd, sd, gd = self.q
+        gu = dequant_nvfp4_weights(qgu, sgu, ggu)
+        return gu[:, :self.F], gu[:, self.F:], dequant_nvfp4_weights(qd, sd, gd)
+
+    def _quant_x(self, x: torch.Tensor):
+        t, dev = x.shape[0], x.device
+        if self.kind == 0:
+            xq = torch.empty(t, self.H, dtype=torch.uint8, device=dev)
+            xs = torch.empty(t, self.H // TILE, dtype=torch.int32, device=dev)
+        else:
+            xq = torch.empty(t, self.H // 2, dtype=torch.uint8, device=dev)
+            xs = torch.empty(t, self.H // 64, dtype=torch.int32, device=dev)
+        ext().rmsnorm_quant(x.contiguous(), None, 0.0, 0.0, xq, xs, self.kind)
+        return xq, xs
 
     def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, nt: int | None = None) -> torch.Tensor:
         """x bf16 [T, H] (already normalized), ids int32 [T, k] (expert ids in [0, E)), w fp32 [T, k] -> bf16 [T, H]."""
@@ -143,39 +240,46 @@ class Fp8Experts:
         P = t * k
         extra = t if self.has_shared else 0
         E = self.E + int(self.has_shared)
-        xq = torch.empty(t, self.H, dtype=torch.uint8, device=dev)
-        xs = torch.empty(t, self.H // TILE, dtype=torch.int32, device=dev)
-        ext().rmsnorm_quant(x.contiguous(), None, 0.0, 0.0, xq, xs)
+        xq, xs = self._quant_x(x)
         off = torch.empty(E + 1, dtype=torch.int32, device=dev)
         pairs = torch.empty(P + extra, dtype=torch.int32, device=dev)
         ext().moe_align(ids.contiguous().view(-1), 0, self.E, extra, off, pairs)
         nt = nt or pick_nt(max(1, -(-2 * P // self.E)))
-        h = torch.empty(P + extra, self.F, dtype=torch.uint8, device=dev)
-        hs = torch.empty(P + extra, self.F // TILE, dtype=torch.int32, device=dev)
-        ext().moe_gemm(self.w1, xq, xs, off, pairs, None, h, hs, self.status, self.F // TILE, self.H // TILE, 2, nt,
-                       1, k, P, 1.0, self.num_ctas)
+        kc1 = self.H // (TILE if self.kind == 0 else 2 * TILE)
+        kc2 = self.F // (TILE if self.kind == 0 else 2 * TILE)
+        if self.kind == 0:
+            h = torch.empty(P + extra, self.F, dtype=torch.uint8, device=dev)
+            hs = torch.empty(P + extra, self.F // TILE, dtype=torch.int32, device=dev)
+        else:
+            h = torch.empty(P + extra, self.F // 2, dtype=torch.uint8, device=dev)
+            hs = torch.empty(P + extra, self.F // 64, dtype=torch.int32, device=dev)
+        ext().moe_gemm(self.w1, xq, xs, off, pairs, None, h, hs, self.status, self.F // TILE, kc1, 2, nt,
+                       1, k, P, 1.0, self.num_ctas, self.kind, self.mul1)
         pw = torch.cat([w.float().reshape(-1), torch.ones(extra, device=dev)])
         rows = torch.empty(P + extra, self.H, dtype=torch.bfloat16, device=dev)
-        ext().moe_gemm(self.w2, h, hs, off, pairs, pw, rows, None, self.status, self.H // TILE, self.F // TILE, 1,
-                       nt, 2, 1, 1 << 30, 1.0, self.num_ctas)
+        ext().moe_gemm(self.w2, h, hs, off, pairs, pw, rows, None, self.status, self.H // (TILE * self.g2),
+                       kc2, self.g2, nt, 2, 1, 1 << 30, 1.0, self.num_ctas, self.kind, self.mul2)
         y = torch.empty(t, self.H, dtype=torch.bfloat16, device=dev)
         ext().moe_combine(rows, t, k, int(self.has_shared), y)
         return y
 
     def forward_ref(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        """fp32 oracle of the same arithmetic: FP8 activations, FP8 SwiGLU output, bf16 rows, fp32 slot-order sum."""
+        """fp32 oracle of the same arithmetic: quantized activations, quantized SwiGLU output, bf16 rows, fp32
+        slot-order sum."""
         wg, wu, wd = (m.to(x.device) for m in self.dequant())
         t, k = ids.shape
-        xq, xs = quant_rows(x.float())
-        xd = dequant_rows(xq, xs)
+        qr, dr = (quant_rows, dequant_rows) if self.kind == 0 else (quant_nvfp4_rows, dequant_nvfp4_rows)
+        xd = dr(*qr(x.float()))
         pairs = [(tt, kk, int(ids[tt, kk])) for tt in range(t) for kk in range(k)]
         if self.has_shared:
             pairs += [(tt, -1, self.E) for tt in range(t)]
         out = torch.zeros(t, self.H, dtype=torch.float32, device=x.device)
         for tt, kk, e in pairs:
             hh = Fn.silu(xd[tt] @ wg[e].T) * (xd[tt] @ wu[e].T)
-            hq, hs = quant_rows(hh[None])
-            hd = dequant_rows(hq, hs)[0]
+            hd = dr(*qr(hh[None]))[0]
             r = (hd @ wd[e].T) * (float(w[tt, kk]) if kk >= 0 else 1.0)
             out[tt] += r.to(torch.bfloat16).float()
         return out.to(torch.bfloat16)
+
+
+Fp8Experts = BlockScaledExperts

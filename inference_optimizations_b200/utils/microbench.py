@@ -3,6 +3,7 @@ profiles/.  Usage:
 
     python -m inference_optimizations_b200.utils.microbench gqa_decode --b 8 --ctx 8192 --d 512 --fmt nvfp4
     python -m inference_optimizations_b200.utils.microbench mla_decode --b 64 --heads 128 --ctx 131072 --fmt nvfp4
+    python -m inference_optimizations_b200.utils.microbench moe_gemm --b 64 --topk 8 --experts 32 --total-experts 256
 
 `--launches N` runs exactly N launches and no timing loop (the form used under ncu: `-s N-1 -c 1`).
 Each timed case prints one JSON line with microseconds, bytes moved and GB/s against the measured HBM peak.
@@ -177,6 +178,73 @@ def indexer_case(b: int, ctx: int, topk: int, heads: int = 64, launches: int = 0
             "frac_hbm": round(nbytes / us / 1e3 / PEAKS["hbm_gbs"], 3), "l2": "flushed before each launch"}
 
 
+def moe_gemm_case(b: int, experts: int, total_experts: int, topk: int, hidden: int, ffn: int, wfmt: str = "fp8",
+                  launches: int = 0) -> dict:
+    """Grouped block-scaled expert GEMMs at decode: b tokens routed top-k over `total_experts`; this GPU owns
+    experts [0, experts) (the expert-parallel slice).  Weights are random packed blocks (no NaN codes); gate/up
+    (fused SwiGLU + requant) and down (routing-weighted bf16 rows) are timed separately.  wfmt: fp8 | nvfp4."""
+    from .._ext import ext
+    from ..ops import moe_gemm as MG
+    dev = torch.device("cuda:0")
+    E, H, F = experts, hidden, ffn
+    kind = 0 if wfmt == "fp8" else 1
+    sfw = 1 if kind == 0 else 4
+    vals = 128 if kind == 0 else 256                                      # K values per 128-byte chunk
+
+    def rand_pack(n_tiles, kc, g):
+        blk = g * (16384 + 512 * sfw)
+        w = torch.randint(0, 256, (E, n_tiles, kc, blk), dtype=torch.uint8, device=dev)
+        if kind == 0:
+            w[(w & 0x7F) == 0x7F] = 0
+        w[..., g * 16384:] = 120 if kind == 0 else 0x30                   # 2^-7 (UE8M0) / 0.5 (E4M3)
+        return w
+    gd = 2 if (H % 256 == 0 and kind == 0) else 1
+    w1, w2 = rand_pack(F // 128, H // vals, 2), rand_pack(H // (128 * gd), F // vals, gd)
+    ids = torch.rand(b, total_experts, device=dev).topk(topk, dim=-1).indices.int()
+    wts = torch.softmax(torch.randn(b, topk, device=dev), -1)
+    x = torch.randn(b, H, device=dev)
+    xq, xs = MG.quant_rows(x) if kind == 0 else MG.quant_nvfp4_rows(x)
+    P = b * topk
+    off = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    pairs = torch.empty(P, dtype=torch.int32, device=dev)
+    ext().moe_align(ids.view(-1), 0, E, 0, off, pairs)
+    local = ids[ids < E]
+    n_pairs, touched = int(local.numel()), int(torch.unique(local).numel())
+    nt = MG.pick_nt(max(1, -(-2 * n_pairs // E)))
+    h = torch.empty(P, F if kind == 0 else F // 2, dtype=torch.uint8, device=dev)
+    hs = torch.empty(P, F // 128 if kind == 0 else F // 64, dtype=torch.int32, device=dev)
+    rows = torch.empty(P, H, dtype=torch.bfloat16, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+
+    def gemm1():
+        ext().moe_gemm(w1, xq, xs, off, pairs, None, h, hs, status, F // 128, H // vals, 2, nt, 1, topk, P, 1.0,
+                       sms, kind, None)
+
+    def gemm2():
+        ext().moe_gemm(w2, h, hs, off, pairs, wts.view(-1), rows, None, status, H // (128 * gd), F // vals, gd, nt,
+                       2, 1, 1 << 30, 1.0, sms, kind, None)
+    if launches:
+        for _ in range(launches):
+            gemm1()
+            gemm2()
+        torch.cuda.synchronize()
+        return {}
+    us1, us2 = _time(gemm1), _time(gemm2)
+    torch.cuda.synchronize()
+    assert status.item() == 0, status.item()
+    wb = 1.0 if kind == 0 else 0.5                                        # weight bytes per value
+    sb = (1 / 32) if kind == 0 else (1 / 8)                               # scale-atom bytes per weight byte
+    b1 = touched * 2 * F * H * wb * (1 + sb) + n_pairs * (H + F) * wb
+    b2 = touched * H * F * wb * (1 + sb) + n_pairs * (F * wb + 2 * H)
+    frac = lambda nb, us: round(nb / us / 1e3 / PEAKS["hbm_gbs"], 3)  # noqa: E731
+    return {"kernel": f"moe_gemm_{wfmt}_blockscaled", "tokens": b, "topk": topk, "experts_local": E,
+            "experts_total": total_experts, "pairs_local": n_pairs, "experts_touched": touched, "nt": nt,
+            "hidden": H, "ffn": F, "gate_up_us": round(us1, 2), "gate_up_frac_hbm": frac(b1, us1),
+            "down_us": round(us2, 2), "down_frac_hbm": frac(b2, us2), "bytes": int(b1 + b2),
+            "l2": "weights per launch exceed L2 (each touched expert read once)"}
+
+
 def main() -> None:
     _load_peaks()
     p = argparse.ArgumentParser()
@@ -192,11 +260,18 @@ def main() -> None:
     p.add_argument("--window", type=int, default=0)
     p.add_argument("--topk", type=int, default=2048)
     p.add_argument("--launches", type=int, default=0)
+    p.add_argument("--experts", type=int, default=32)
+    p.add_argument("--total-experts", type=int, default=256)
+    p.add_argument("--hidden", type=int, default=7168)
+    p.add_argument("--ffn", type=int, default=2048)
+    p.add_argument("--wfmt", default="fp8", choices=["fp8", "nvfp4"])
     a = p.parse_args()
     if a.kernel == "gqa_decode":
         r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches)
     elif a.kernel == "indexer":
         r = indexer_case(a.b, a.ctx, a.topk, launches=a.launches)
+    elif a.kernel == "moe_gemm":
+        r = moe_gemm_case(a.b, a.experts, a.total_experts, a.topk, a.hidden, a.ffn, a.wfmt, a.launches)
     elif a.kernel == "mla_decode":
         r = mla_decode_case(a.b, a.heads, a.ctx, a.topk, a.fmt, a.nq, a.launches)
     else:

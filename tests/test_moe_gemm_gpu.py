@@ -43,7 +43,7 @@ def test_moe_gemm_plain(cuda, nt, ctas):
     out = torch.zeros(P, N, dtype=torch.bfloat16, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
     ext().moe_gemm(pack, xq.to(cuda), xs.to(cuda), off, pairs, None, out, None, status, N // 128, K // 128, 1, nt,
-                   0, topk, P, 1.0, ctas)
+                   0, topk, P, 1.0, ctas, 0, None)
     torch.cuda.synchronize()
     assert status.item() == 0
     ref = torch.stack([xd[p // topk] @ wd[int(ids.view(-1)[p])].T for p in range(P)])
@@ -74,7 +74,7 @@ def test_moe_gemm_swiglu_quant(cuda, nt):
     hs = torch.zeros(P, F // 128, dtype=torch.int32, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
     ext().moe_gemm(pack, xq.to(cuda), xs.to(cuda), off, pairs, None, h, hs, status, F // 128, K // 128, 2, nt, 1,
-                   topk, P, 1.0, 148)
+                   topk, P, 1.0, 148, 0, None)
     torch.cuda.synchronize()
     assert status.item() == 0
     dg, du = MG.dequant_blocks(qg, eg), MG.dequant_blocks(qu, eu)
@@ -95,11 +95,11 @@ def test_rmsnorm_quant_matches_oracle(cuda):
     x = (torch.randn(6, 512) * torch.exp2(torch.randint(-5, 6, (6, 1)).float())).to(torch.bfloat16)
     q = torch.empty(6, 512, dtype=torch.uint8, device=cuda)
     sc = torch.empty(6, 4, dtype=torch.int32, device=cuda)
-    ext().rmsnorm_quant(x.to(cuda), None, 0.0, 0.0, q, sc)
+    ext().rmsnorm_quant(x.to(cuda), None, 0.0, 0.0, q, sc, 0)
     rq, rs = MG.quant_rows(x.float())
     assert torch.equal(sc.cpu(), rs) and torch.equal(q.cpu(), rq)
     w = (torch.randn(512) * 0.1).to(torch.bfloat16)
-    ext().rmsnorm_quant(x.to(cuda), w.to(cuda), 1e-6, 1.0, q, sc)
+    ext().rmsnorm_quant(x.to(cuda), w.to(cuda), 1e-6, 1.0, q, sc, 0)
     xf = x.float()
     n = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * (w.float() + 1.0)).to(torch.bfloat16).float()
     rq, rs = MG.quant_rows(n)
@@ -127,3 +127,85 @@ def test_fp8_experts_forward(cuda, shared):
     assert cos > 0.999, cos
     rel = ((y.float() - ref.float()).norm() / ref.float().norm()).item()
     assert rel < 0.03, rel
+
+
+def test_moe_gemm_paired_tiles(cuda):
+    """Plain output with two adjacent 128-column tiles per CTA (G = 2) equals the single-tile launch."""
+    from inference_optimizations_b200._ext import ext
+    E, N, K, T, topk = 2, 512, 256, 19, 2
+    w, x, ids = _case(cuda, E, N, K, T, topk, seed=5)
+    wq, web, wd = _quant_rowwise_weights(w)
+    xq, xs = MG.quant_rows(x)
+    P = T * topk
+    off = torch.empty(E + 1, dtype=torch.int32, device=cuda)
+    pairs = torch.empty(P, dtype=torch.int32, device=cuda)
+    ext().moe_align(ids.view(-1).to(cuda), 0, E, 0, off, pairs)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    outs = []
+    for pack, g in (MG.pack_weights_paired(wq, web), (MG.pack_weights([wq], [web]), 1)):
+        out = torch.zeros(P, N, dtype=torch.bfloat16, device=cuda)
+        ext().moe_gemm(pack.to(cuda), xq.to(cuda), xs.to(cuda), off, pairs, None, out, None, status, N // (128 * g),
+                       K // 128, g, 32, 0, topk, P, 1.0, 148, 0, None)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("nt", [16, 128])
+def test_moe_gemm_nvfp4_plain(cuda, nt):
+    """kind::mxf4nvf4 (E2M1 x E2M1, E4M3 scale per 16): every scale byte differs, so the four scale atoms per
+    chunk and their row layout are all exercised; the per-expert global scale comes in through expert_mul."""
+    from inference_optimizations_b200._ext import ext
+    E, N, K, T, topk = 3, 256, 512, 29, 2
+    w, x, ids = _case(cuda, E, N, K, T, topk, seed=40 + nt)
+    wq, ws, wg = MG.quant_nvfp4_weights(w)
+    wd = MG.dequant_nvfp4_weights(wq, ws, wg)
+    xq, xs = MG.quant_nvfp4_rows(x)
+    xd = MG.dequant_nvfp4_rows(xq, xs)
+    pack = MG.pack_weights_nvfp4([wq], [ws]).to(cuda)
+    P = T * topk
+    off = torch.empty(E + 1, dtype=torch.int32, device=cuda)
+    pairs = torch.empty(P, dtype=torch.int32, device=cuda)
+    ext().moe_align(ids.view(-1).to(cuda), 0, E, 0, off, pairs)
+    out = torch.zeros(P, N, dtype=torch.bfloat16, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    ext().moe_gemm(pack, xq.to(cuda), xs.to(cuda), off, pairs, None, out, None, status, N // 128, K // 256, 1, nt,
+                   0, topk, P, 1.0, 148, 1, wg.to(cuda))
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    ref = torch.stack([xd[p // topk] @ wd[int(ids.view(-1)[p])].T for p in range(P)])
+    got = out.float().cpu()
+    err = (got - ref).abs() / (ref.abs() + 1e-3 * ref.abs().amax(1, keepdim=True))
+    assert err.max().item() < 1e-2, err.max().item()
+
+
+def test_quant_nvfp4_rows_matches_oracle(cuda):
+    from inference_optimizations_b200._ext import ext
+    torch.manual_seed(9)
+    x = (torch.randn(5, 512) * torch.exp2(torch.randint(-5, 6, (5, 1)).float())).to(torch.bfloat16)
+    q = torch.empty(5, 256, dtype=torch.uint8, device=cuda)
+    sc = torch.empty(5, 8, dtype=torch.int32, device=cuda)
+    ext().rmsnorm_quant(x.to(cuda), None, 0.0, 0.0, q, sc, 1)
+    rq, rs = MG.quant_nvfp4_rows(x.float())
+    assert torch.equal(q.cpu(), rq) and torch.equal(sc.cpu(), rs)
+
+
+@pytest.mark.parametrize("shared", [False, True])
+def test_nvfp4_experts_forward(cuda, shared):
+    torch.manual_seed(12)
+    E, F, H, T, topk = 5, 256, 512, 11, 2
+    wg = torch.randn(E, F, H, device=cuda) * 0.04
+    wu = torch.randn(E, F, H, device=cuda) * 0.04
+    wd = torch.randn(E, H, F, device=cuda) * 0.04
+    sh = tuple(torch.randn(*s, device=cuda) * 0.04 for s in ((F, H), (F, H), (H, F))) if shared else None
+    ex = MG.BlockScaledExperts(wg, wu, wd, shared=sh, fmt="nvfp4")
+    x = torch.randn(T, H, device=cuda).to(torch.bfloat16)
+    ids = torch.stack([torch.randperm(E, device=cuda)[:topk] for _ in range(T)]).int()
+    w = torch.softmax(torch.randn(T, topk, device=cuda), -1)
+    y = ex.forward(x, ids, w)
+    torch.cuda.synchronize()
+    assert ex.status.item() == 0
+    ref = ex.forward_ref(x, ids, w)
+    cos = Fn.cosine_similarity(y.float().flatten(), ref.float().flatten(), dim=0).item()
+    assert cos > 0.995, cos
