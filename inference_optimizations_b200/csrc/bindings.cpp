@@ -330,8 +330,11 @@ void moe_route(const at::Tensor& logits, const at::Tensor& bias, at::Tensor ids,
 void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_scale, const at::Tensor& off,
               const at::Tensor& pairs, const c10::optional<at::Tensor>& pair_w, at::Tensor out,
               const c10::optional<at::Tensor>& out_scale, at::Tensor status, int64_t n_tiles, int64_t kc, int64_t G,
-              int64_t NT, int64_t mode, int64_t src_div, int64_t src_limit, double out_mul, int64_t num_ctas,
-              int64_t kind, const c10::optional<at::Tensor>& expert_mul) {
+              int64_t NT, int64_t mode, int64_t src_div, int64_t src_limit, int64_t src_shared_base, double out_mul,
+              int64_t num_ctas,
+              int64_t kind, const c10::optional<at::Tensor>& expert_mul,
+              const c10::optional<at::Tensor>& out_peers, int64_t out_offset, int64_t out_div, int64_t out_rank,
+              int64_t out_shared_base, int64_t pairs_total) {
   req(wpack, at::kByte, "wpack");
   req(x, at::kByte, "x");
   req(x_scale, at::kInt, "x_scale");
@@ -379,6 +382,7 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
   a.mode = static_cast<int>(mode);
   a.src_div = static_cast<int>(src_div);
   a.src_limit = static_cast<int>(src_limit);
+  a.src_shared_base = static_cast<int>(src_shared_base);
   a.x_stride = static_cast<int>(x.stride(0));
   a.out_stride = static_cast<int>(out.stride(0));
   a.out_scale_stride = out_scale.has_value() ? static_cast<int>(out_scale->stride(0)) : 0;
@@ -386,6 +390,16 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
   a.out_mul = static_cast<float>(out_mul);
   a.kind = static_cast<int>(kind);
   a.expert_mul = expert_mul.has_value() ? expert_mul->data_ptr<float>() : nullptr;
+  if (out_peers.has_value()) {
+    TORCH_CHECK(out_peers->scalar_type() == at::kLong && mode != iob::kMoeOutSwigluQuant && out_div > 0,
+                "out_peers: int64 table, plain bf16 mode");
+    a.out_peers = reinterpret_cast<const long long*>(out_peers->data_ptr<int64_t>());
+  }
+  a.out_offset = out_offset;
+  a.out_div = static_cast<int>(out_div);
+  a.out_rank = static_cast<int>(out_rank);
+  a.out_shared_base = static_cast<int>(out_shared_base);
+  a.pairs_total = static_cast<int>(pairs_total);
   const at::cuda::CUDAGuard g(x.device());
   CHECK_CUDA_OK(iob::moe_gemm(a, stream()));
 }
@@ -394,23 +408,70 @@ void moe_align(const at::Tensor& ids, int64_t e0, int64_t E, int64_t extra, at::
   req(ids, at::kInt, "ids");
   req(off, at::kInt, "off");
   req(pairs, at::kInt, "pairs");
-  TORCH_CHECK(ids.is_contiguous() && off.numel() == E + (extra > 0 ? 2 : 1) && pairs.numel() >= ids.numel() + extra,
+  // off has E + 1 entries (routed only) or E + 2 (one shared bucket after the routed ones, `extra` rows)
+  const bool shared = off.numel() == E + 2;
+  TORCH_CHECK(ids.is_contiguous() && (shared || (off.numel() == E + 1 && extra == 0)) &&
+                  pairs.numel() >= ids.numel() + extra,
               "moe_align shapes");
   const at::cuda::CUDAGuard g(ids.device());
   CHECK_CUDA_OK(iob::moe_align(ids.data_ptr<int>(), static_cast<int>(ids.numel()), static_cast<int>(e0),
-                               static_cast<int>(E), static_cast<int>(extra), off.data_ptr<int>(), pairs.data_ptr<int>(),
-                               stream()));
+                               static_cast<int>(E), shared ? 1 : 0, static_cast<int>(extra), off.data_ptr<int>(),
+                               pairs.data_ptr<int>(), stream()));
 }
 
-void moe_combine(const at::Tensor& rows, int64_t T, int64_t topk, int64_t shared, at::Tensor y) {
+void moe_combine(const at::Tensor& rows, int64_t T, int64_t topk, int64_t shared_base,
+                 const c10::optional<at::Tensor>& w, at::Tensor y) {
   req(rows, at::kBFloat16, "rows");
   req(y, at::kBFloat16, "y");
   TORCH_CHECK(rows.is_contiguous() && y.is_contiguous() && rows.size(1) == y.size(1) &&
-                  rows.size(0) >= T * topk + (shared ? T : 0) && y.size(0) >= T,
+                  rows.size(0) >= T * topk && (shared_base < 0 || rows.size(0) >= shared_base + T) && y.size(0) >= T,
               "moe_combine shapes");
+  if (w.has_value()) TORCH_CHECK(w->scalar_type() == at::kFloat && w->is_contiguous() && w->numel() >= T * topk, "w");
   const at::cuda::CUDAGuard g(y.device());
   CHECK_CUDA_OK(iob::moe_combine(rows.data_ptr(), static_cast<int>(T), static_cast<int>(topk),
-                                 static_cast<int>(y.size(1)), static_cast<int>(shared), y.data_ptr(), stream()));
+                                 static_cast<int>(y.size(1)), static_cast<int>(shared_base),
+                                 w.has_value() ? w->data_ptr<float>() : nullptr, y.data_ptr(), stream()));
+}
+
+void ep_dispatch(const at::Tensor& peers, const at::Tensor& xq, const at::Tensor& xs, const at::Tensor& ids,
+                 int64_t off_x, int64_t off_s, int64_t off_ids, int64_t T_max, int64_t rank, int64_t world,
+                 int64_t E_loc) {
+  req(peers, at::kLong, "peers");
+  req(xq, at::kByte, "xq");
+  req(xs, at::kInt, "xs");
+  req(ids, at::kInt, "ids");
+  TORCH_CHECK(xq.is_contiguous() && xs.is_contiguous() && ids.is_contiguous() && ids.dim() == 2 &&
+                  xq.size(0) >= ids.size(0) && xs.size(0) >= ids.size(0) && peers.numel() == world,
+              "ep_dispatch shapes");
+  iob::EpDispatchArgs a{};
+  a.peers = reinterpret_cast<const long long*>(peers.data_ptr<int64_t>());
+  a.xq = xq.data_ptr<uint8_t>();
+  a.xs = reinterpret_cast<const uint8_t*>(xs.data_ptr<int>());
+  a.ids = ids.data_ptr<int>();
+  a.off_x = off_x;
+  a.off_s = off_s;
+  a.off_ids = off_ids;
+  a.T = static_cast<int>(ids.size(0));
+  a.T_max = static_cast<int>(T_max);
+  a.topk = static_cast<int>(ids.size(1));
+  a.rank = static_cast<int>(rank);
+  a.world = static_cast<int>(world);
+  a.E_loc = static_cast<int>(E_loc);
+  a.row_bytes = static_cast<int>(xq.size(1));
+  a.scale_bytes = static_cast<int>(xs.size(1) * 4);
+  const at::cuda::CUDAGuard g(xq.device());
+  CHECK_CUDA_OK(iob::ep_dispatch(a, stream()));
+}
+
+void ep_barrier(const at::Tensor& peers, int64_t off_flags, int64_t rank, int64_t world, at::Tensor epoch,
+                at::Tensor status) {
+  req(peers, at::kLong, "peers");
+  req(epoch, at::kInt, "epoch");
+  req(status, at::kInt, "status");
+  const at::cuda::CUDAGuard g(epoch.device());
+  CHECK_CUDA_OK(iob::ep_barrier(reinterpret_cast<const long long*>(peers.data_ptr<int64_t>()), off_flags,
+                                static_cast<int>(rank), static_cast<int>(world), epoch.data_ptr<int>(),
+                                status.data_ptr<int>(), stream()));
 }
 
 void rmsnorm_quant(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps, double plus_one, at::Tensor q,
@@ -483,6 +544,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_align", &moe_align);
   m.def("moe_combine", &moe_combine);
   m.def("rmsnorm_quant", &rmsnorm_quant);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_barrier", &ep_barrier);
   m.def("umma_gemm_test", &umma_gemm_test);
   m.def("umma_f8_mn_test", &umma_f8_mn_test);
   m.def("nvfp4_lut_test", &nvfp4_lut_test);

@@ -162,14 +162,36 @@ struct MoeGemmArgs {
   void* out;                  // bf16 [pairs][out_stride] or FP8 [pairs][out_stride] (SwiGLU mode)
   uint32_t* out_scale;        // SwiGLU mode: UE8M0 x4 words [pairs][out_scale_stride]
   const float* expert_mul;    // optional per-expert output multiplier (NVFP4 weight global scales)
+  // Optional peer-memory output (expert parallelism): row p < pairs_total goes to rank p / out_div, row p % out_div
+  // of the region at byte offset out_offset of that rank's symmetric buffer; shared-expert rows p >= pairs_total
+  // go to this rank (out_rank), row out_shared_base + p - pairs_total.  Plain bf16 modes only.
+  const long long* out_peers;
+  long long out_offset;
+  int out_div, out_rank, out_shared_base, pairs_total;
   int* status;
-  int E, n_tiles, KC, G, NT, mode, src_div, src_limit, x_stride, out_stride, out_scale_stride, num_ctas;
+  int E, n_tiles, KC, G, NT, mode, src_div, src_limit, src_shared_base, x_stride, out_stride, out_scale_stride;
+  int num_ctas;
   int kind;                   // 0: FP8 E4M3 + UE8M0 per 32 (128-blocks replicated); 1: NVFP4 (E2M1 + E4M3 per 16)
   float out_mul;
 };
 cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s);
-cudaError_t moe_align(const int* ids, int P, int e0, int E, int extra, int* off, int* pairs, cudaStream_t s);
-cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared, void* y, cudaStream_t s);
+cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, int extra, int* off, int* pairs,
+                      cudaStream_t s);
+cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_base, const float* w, void* y,
+                        cudaStream_t s);
+
+// ---- expert-parallel exchange over peer memory (ep.cu)
+struct EpDispatchArgs {
+  const long long* peers;     // [world] base address of every rank's symmetric buffer (device)
+  const uint8_t* xq;          // this rank's quantized rows [T, row_bytes]
+  const uint8_t* xs;          // their scale bytes [T, scale_bytes]
+  const int* ids;             // [T, topk] global expert ids
+  long long off_x, off_s, off_ids;   // byte offsets of the receive regions inside the symmetric buffer
+  int T, T_max, topk, rank, world, E_loc, row_bytes, scale_bytes;
+};
+cudaError_t ep_dispatch(const EpDispatchArgs& a, cudaStream_t s);
+cudaError_t ep_barrier(const long long* peers, long long off_flags, int rank, int world, int* epoch, int* status,
+                       cudaStream_t s);
 cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_one, int T, int H, int fmt, uint8_t* q,
                           uint32_t* sc, cudaStream_t s);
 

@@ -142,9 +142,10 @@ __device__ __forceinline__ void item_coords(const int* prefix, int E, int n_tile
   nt = local - tt * n_tiles;
 }
 
-// Activation row of pair p: p / src_div for routed pairs, p - src_limit for the shared-expert rows after them.
+// Activation row of pair p: p / src_div for routed pairs, src_shared_base + p - src_limit for the shared-expert
+// rows after them.
 __device__ __forceinline__ int src_row(const MoeGemmArgs& a, int p) {
-  return p < a.src_limit ? p / a.src_div : p - a.src_limit;
+  return p < a.src_limit ? p / a.src_div : a.src_shared_base + p - a.src_limit;
 }
 
 // UE8M0 exponent of the smallest power of two s with amax / s <= 448 (biased byte, clamped to [1, 253]).
@@ -443,8 +444,17 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
                 const int p = a.pairs[row0 + r];
                 float v = __uint_as_float(g == 0 ? v0[t] : v1[t]) * emul;
                 if (a.mode == kMoeOutBf16Weighted) v *= a.pair_w[p];
-                reinterpret_cast<__nv_bfloat16*>(a.out)[static_cast<size_t>(p) * a.out_stride +
-                                                        (nt * G + g) * 128 + n_local] = __float2bfloat16(v);
+                __nv_bfloat16* dst;
+                if (a.out_peers) {                      // expert parallelism: the row goes to its token's owner
+                  const bool sh = p >= a.pairs_total;
+                  const int rr = sh ? a.out_rank : p / a.out_div;
+                  const long long row = sh ? a.out_shared_base + (p - a.pairs_total) : p % a.out_div;
+                  dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(a.out_peers[rr]) + a.out_offset) +
+                        row * a.out_stride;
+                } else {
+                  dst = reinterpret_cast<__nv_bfloat16*>(a.out) + static_cast<size_t>(p) * a.out_stride;
+                }
+                dst[(nt * G + g) * 128 + n_local] = __float2bfloat16(v);
               }
             }
           }
@@ -476,21 +486,21 @@ cudaError_t launch_mg(const MoeGemmArgs& a, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------------------------------------ routing prep
-// Pairs p (token p / topk, slot p % topk) whose expert lies in [e0, e0 + E) are bucketed by expert: off[E + 1] and
-// pairs sorted by expert (order inside an expert is irrelevant: each pair is its own MMA column).  `extra` rows
-// P .. P + extra - 1 all go to bucket E (a shared expert run as one more group of the same launch).
-__global__ void __launch_bounds__(1024) moe_align_kernel(const int* ids, int P, int e0, int E, int extra, int* off,
-                                                         int* pairs) {
+// Pairs p (token p / topk, slot p % topk) whose expert lies in [e0, e0 + E) are bucketed by expert: off[nb + 1] and
+// pairs sorted by expert (order inside an expert is irrelevant: each pair is its own MMA column).  With a shared
+// bucket (nb = E + 1) the `extra` rows P .. P + extra - 1 all go to bucket E (a shared expert run as one more group
+// of the same launch; extra may be 0).
+__global__ void __launch_bounds__(1024) moe_align_kernel(const int* ids, int P, int e0, int E, int nb, int extra,
+                                                         int* off, int* pairs) {
   __shared__ int cnt[kMaxExperts + 2];
   __shared__ int pos[kMaxExperts + 2];
-  const int nb = E + (extra > 0 ? 1 : 0);
   for (int e = threadIdx.x; e < nb; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
     const int e = ids[p] - e0;
     if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
   }
-  if (threadIdx.x == 0 && extra > 0) cnt[E] = extra;
+  if (threadIdx.x == 0 && nb > E) cnt[E] = extra;
   __syncthreads();
   if (threadIdx.x == 0) {
     int run = 0;
@@ -509,23 +519,24 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int* ids, int P, 
   for (int t = threadIdx.x; t < extra; t += blockDim.x) pairs[pos[E] + t] = P + t;
 }
 
-// y[t] = sum_k rows[t * topk + k] (+ rows[P + t] when shared), fp32 in slot order, bf16 out.
-__global__ void moe_combine_kernel(const __nv_bfloat16* rows, int T, int topk, int H, int shared,
-                                   __nv_bfloat16* y) {
+// y[t] = sum_k w[t, k] * rows[t * topk + k] (+ rows[shared_base + t] when shared_base >= 0), fp32 in slot order,
+// bf16 out.  w null: the rows already carry their routing weights.
+__global__ void moe_combine_kernel(const __nv_bfloat16* rows, int T, int topk, int H, int shared_base,
+                                   const float* w, __nv_bfloat16* y) {
   const int t = blockIdx.x;
-  const int P = T * topk;
   for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int k = 0; k <= topk; ++k) {
-      if (k == topk && !shared) break;
-      const size_t r = k < topk ? static_cast<size_t>(t) * topk + k : static_cast<size_t>(P) + t;
+      if (k == topk && shared_base < 0) break;
+      const size_t r = k < topk ? static_cast<size_t>(t) * topk + k : static_cast<size_t>(shared_base) + t;
+      const float wk = (k < topk && w) ? w[t * topk + k] : 1.f;
       const uint4 u = *reinterpret_cast<const uint4*>(rows + r * H + c * 8);
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 f = __bfloat1622float2(h[i]);
-        acc[2 * i] += f.x;
-        acc[2 * i + 1] += f.y;
+        acc[2 * i] += wk * f.x;
+        acc[2 * i + 1] += wk * f.y;
       }
     }
     uint4 o;
@@ -631,16 +642,18 @@ cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
   return cudaErrorInvalidValue;
 }
 
-cudaError_t moe_align(const int* ids, int P, int e0, int E, int extra, int* off, int* pairs, cudaStream_t s) {
-  if (E <= 0 || E > kMaxExperts) return cudaErrorInvalidValue;
-  moe_align_kernel<<<1, 1024, 0, s>>>(ids, P, e0, E, extra, off, pairs);
+cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, int extra, int* off, int* pairs,
+                      cudaStream_t s) {
+  if (E <= 0 || E > kMaxExperts || (!shared_bucket && extra)) return cudaErrorInvalidValue;
+  moe_align_kernel<<<1, 1024, 0, s>>>(ids, P, e0, E, E + (shared_bucket ? 1 : 0), extra, off, pairs);
   return cudaGetLastError();
 }
 
-cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared, void* y, cudaStream_t s) {
+cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_base, const float* w, void* y,
+                        cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   if (H % 8) return cudaErrorInvalidValue;
-  moe_combine_kernel<<<T, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(rows), T, topk, H, shared,
+  moe_combine_kernel<<<T, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(rows), T, topk, H, shared_base, w,
                                        static_cast<__nv_bfloat16*>(y));
   return cudaGetLastError();
 }

@@ -167,6 +167,16 @@ def pack_weights_nvfp4(qs: list, scs: list) -> torch.Tensor:
     return torch.cat(tiles + atoms, dim=-1).contiguous()
 
 
+def gemm(wpack, x, x_scale, off, pairs, out, status, *, n_tiles: int, kc: int, g: int, nt: int, mode: int,
+         src_div: int, src_limit: int = 1 << 30, src_shared_base: int = 0, pair_w=None, out_scale=None, out_mul: float = 1.0,
+         num_ctas: int = 148, kind: int = 0, expert_mul=None, out_peers=None, out_offset: int = 0, out_div: int = 1,
+         out_rank: int = 0, out_shared_base: int = 0, pairs_total: int = 0) -> None:
+    """One grouped block-scaled GEMM launch (argument meanings: `MoeGemmArgs` in csrc/kernels.h)."""
+    ext().moe_gemm(wpack, x, x_scale, off, pairs, pair_w, out, out_scale, status, n_tiles, kc, g, nt, mode, src_div,
+                   src_limit, src_shared_base, out_mul, num_ctas, kind, expert_mul, out_peers, out_offset, out_div, out_rank,
+                   out_shared_base, pairs_total)
+
+
 def pick_nt(rows_per_expert: int) -> int:
     for nt in (16, 32, 64):
         if rows_per_expert <= nt:
@@ -253,14 +263,14 @@ class BlockScaledExperts:
         else:
             h = torch.empty(P + extra, self.F // 2, dtype=torch.uint8, device=dev)
             hs = torch.empty(P + extra, self.F // 64, dtype=torch.int32, device=dev)
-        ext().moe_gemm(self.w1, xq, xs, off, pairs, None, h, hs, self.status, self.F // TILE, kc1, 2, nt,
-                       1, k, P, 1.0, self.num_ctas, self.kind, self.mul1)
+        gemm(self.w1, xq, xs, off, pairs, h, self.status, n_tiles=self.F // TILE, kc=kc1, g=2, nt=nt, mode=1,
+             src_div=k, src_limit=P, out_scale=hs, num_ctas=self.num_ctas, kind=self.kind, expert_mul=self.mul1)
         pw = torch.cat([w.float().reshape(-1), torch.ones(extra, device=dev)])
         rows = torch.empty(P + extra, self.H, dtype=torch.bfloat16, device=dev)
-        ext().moe_gemm(self.w2, h, hs, off, pairs, pw, rows, None, self.status, self.H // (TILE * self.g2),
-                       kc2, self.g2, nt, 2, 1, 1 << 30, 1.0, self.num_ctas, self.kind, self.mul2)
+        gemm(self.w2, h, hs, off, pairs, rows, self.status, n_tiles=self.H // (TILE * self.g2), kc=kc2, g=self.g2,
+             nt=nt, mode=2, src_div=1, pair_w=pw, num_ctas=self.num_ctas, kind=self.kind, expert_mul=self.mul2)
         y = torch.empty(t, self.H, dtype=torch.bfloat16, device=dev)
-        ext().moe_combine(rows, t, k, int(self.has_shared), y)
+        ext().moe_combine(rows, t, k, P if self.has_shared else -1, None, y)
         return y
 
     def forward_ref(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:

@@ -1,0 +1,137 @@
+"""Expert-parallel MoE over NVLink peer memory: dispatch by peer stores, grouped block-scaled expert GEMMs on the
+local experts, expert outputs stored by the GEMM epilogue straight into the owning rank's combine buffer, and a
+slot-ordered weighted combine on the owner (csrc/ep.cu, csrc/moe_gemm.cu).
+
+Every rank holds `E_total / world` routed experts plus a replica of the shared expert (run on the rank's own tokens
+as one more bucket of the same GEMM launches -- the reference's TP1-shared-under-DP arrangement,
+`upstream-fixes/hooks/glm_tp1_shared_hooks.py`).  One symmetric allocation per group (torch symmetric-memory
+rendezvous, mapped by every peer) holds, in this order:
+
+    recv_x    [world * T_max, row_bytes]     quantized token rows, slot (src, t)
+    recv_s    [world * T_max, scale_bytes]   their block scales
+    recv_ids  [world * T_max, topk] int32    routing ids (-1: empty slot)
+    comb      [T_max * topk + T_max, H] bf16 expert outputs of this rank's tokens (row t * topk + k), then the
+                                             shared expert's rows
+    flags     [world] int32                  barrier epochs
+
+Per layer: quantize -> dispatch -> barrier -> align -> GEMM gate/up (+SwiGLU, requant) -> GEMM down (peer-store
+epilogue) -> barrier -> combine.  A rank with no tokens runs the same launches (idle ranks join both barriers,
+`moe-gemm/dp-moe-symmetric-memory/numinous_dp_moe.py:539-545`).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .._ext import ext
+from ..ops import moe_gemm as MG
+
+
+def _align(n: int, a: int = 256) -> int:
+    return (n + a - 1) // a * a
+
+
+class EPLayout:
+    """Byte layout of the symmetric buffer (host-side arithmetic, testable without a GPU)."""
+
+    def __init__(self, world: int, T_max: int, topk: int, H: int, fmt: str):
+        self.world, self.T_max, self.topk, self.H = world, T_max, topk, H
+        self.row_bytes = H if fmt == "fp8" else H // 2
+        self.scale_words = H // 128 if fmt == "fp8" else H // 64
+        rows = world * T_max
+        self.off_x = 0
+        self.off_s = _align(rows * self.row_bytes)
+        self.off_ids = self.off_s + _align(rows * self.scale_words * 4)
+        self.off_comb = self.off_ids + _align(rows * topk * 4)
+        self.comb_rows = T_max * topk + T_max
+        self.off_flags = self.off_comb + _align(self.comb_rows * H * 2)
+        self.nbytes = self.off_flags + _align(world * 4)
+        self.pairs_total = rows * topk
+
+    def owner(self, expert: int, E_loc: int) -> int:
+        return expert // E_loc
+
+    def pair(self, src: int, t: int, k: int) -> int:
+        """Pair id of slot k of token t of rank src (the GEMM row space of every rank)."""
+        return (src * self.T_max + t) * self.topk + k
+
+    def comb_row(self, pair: int) -> tuple[int, int]:
+        """(rank, row) the expert output of `pair` is stored at."""
+        d = self.T_max * self.topk
+        return pair // d, pair % d
+
+
+class EPMoE:
+    def __init__(self, rank: int, world: int, E_total: int, T_max: int, topk: int, w_gate: torch.Tensor,
+                 w_up: torch.Tensor, w_down: torch.Tensor, shared: tuple | None = None, fmt: str = "fp8",
+                 group=None):
+        """w_gate / w_up [E_loc, F, H], w_down [E_loc, H, F]: this rank's experts (global ids rank * E_loc ..)."""
+        import torch.distributed._symmetric_memory as symm
+        self.rank, self.world, self.T_max, self.topk = rank, world, T_max, topk
+        self.E_loc = E_total // world
+        assert w_gate.shape[0] == self.E_loc, "pass this rank's slice of the experts"
+        self.ex = MG.BlockScaledExperts(w_gate, w_up, w_down, shared=shared, fmt=fmt)
+        self.fmt, self.kind, self.H, self.F = fmt, self.ex.kind, self.ex.H, self.ex.F
+        dev = w_gate.device
+        L = self.layout = EPLayout(world, T_max, topk, self.H, fmt)
+        self.buf = symm.empty(L.nbytes, dtype=torch.uint8, device=dev)
+        self.buf.zero_()
+        grp = group if group is not None else dist.group.WORLD
+        self.handle = symm.rendezvous(self.buf, grp)
+        self.peers = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64, device=dev)
+        rows = world * T_max
+        self.recv_x = self.buf[L.off_x:L.off_x + rows * L.row_bytes].view(rows, L.row_bytes)
+        self.recv_s = self.buf[L.off_s:L.off_s + rows * L.scale_words * 4].view(torch.int32).view(rows, L.scale_words)
+        self.recv_ids = self.buf[L.off_ids:L.off_ids + rows * topk * 4].view(torch.int32)
+        self.comb = self.buf[L.off_comb:L.off_comb + L.comb_rows * self.H * 2].view(torch.bfloat16).view(
+            L.comb_rows, self.H)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.xq = torch.zeros(T_max, L.row_bytes, dtype=torch.uint8, device=dev)
+        self.xs = torch.zeros(T_max, L.scale_words, dtype=torch.int32, device=dev)
+        nb = self.E_loc + (1 if shared is not None else 0)
+        self.off = torch.zeros(nb + 1, dtype=torch.int32, device=dev)
+        self.pairs = torch.zeros(L.pairs_total + T_max, dtype=torch.int32, device=dev)
+        hb = self.F if self.kind == 0 else self.F // 2
+        hw = self.F // 128 if self.kind == 0 else self.F // 64
+        self.h = torch.zeros(L.pairs_total + T_max, hb, dtype=torch.uint8, device=dev)
+        self.hs = torch.zeros(L.pairs_total + T_max, hw, dtype=torch.int32, device=dev)
+        self.nt = MG.pick_nt(max(1, -(-2 * L.pairs_total // (world * self.E_loc))))
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=grp)
+
+    def barrier(self) -> None:
+        ext().ep_barrier(self.peers, self.layout.off_flags, self.rank, self.world, self.epoch, self.status)
+
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """x bf16 [T, H] normalized, ids int32 [T, topk] global expert ids, w fp32 [T, topk] -> bf16 [T, H]."""
+        L, ex = self.layout, self.ex
+        T, k = ids.shape
+        if T > self.T_max:
+            raise ValueError(f"{T} tokens > T_max {self.T_max}")
+        if T:
+            ext().rmsnorm_quant(x.contiguous(), None, 0.0, 0.0, self.xq[:T], self.xs[:T], self.kind)
+        ext().ep_dispatch(self.peers, self.xq[:T], self.xs[:T], ids.contiguous(), L.off_x, L.off_s, L.off_ids,
+                          self.T_max, self.rank, self.world, self.E_loc)
+        self.barrier()
+        extra = T if ex.has_shared else 0
+        ext().moe_align(self.recv_ids, self.rank * self.E_loc, self.E_loc, extra, self.off, self.pairs)
+        P = L.pairs_total
+        vals = 128 if self.kind == 0 else 256
+        MG.gemm(ex.w1, self.recv_x, self.recv_s, self.off, self.pairs, self.h, self.status,
+                n_tiles=self.F // 128, kc=self.H // vals, g=2, nt=self.nt, mode=1, src_div=k,
+                src_limit=P, src_shared_base=self.rank * self.T_max, out_scale=self.hs, num_ctas=ex.num_ctas,
+                kind=self.kind, expert_mul=ex.mul1)
+        MG.gemm(ex.w2, self.h, self.hs, self.off, self.pairs, self.comb, self.status,
+                n_tiles=self.H // (128 * ex.g2), kc=self.F // vals, g=ex.g2, nt=self.nt, mode=0, src_div=1,
+                num_ctas=ex.num_ctas, kind=self.kind, expert_mul=ex.mul2, out_peers=self.peers,
+                out_offset=L.off_comb, out_div=self.T_max * k, out_rank=self.rank,
+                out_shared_base=self.T_max * k, pairs_total=P)
+        self.barrier()
+        y = torch.empty(T, self.H, dtype=torch.bfloat16, device=x.device)
+        ext().moe_combine(self.comb, T, k, self.T_max * k if ex.has_shared else -1, w.float().contiguous(), y)
+        return y
+
+    def check(self) -> None:
+        if int(self.status.item()) != 0:
+            raise RuntimeError(f"expert-parallel exchange: status {int(self.status.item())}")

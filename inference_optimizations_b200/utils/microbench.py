@@ -218,12 +218,12 @@ def moe_gemm_case(b: int, experts: int, total_experts: int, topk: int, hidden: i
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
 
     def gemm1():
-        ext().moe_gemm(w1, xq, xs, off, pairs, None, h, hs, status, F // 128, H // vals, 2, nt, 1, topk, P, 1.0,
-                       sms, kind, None)
+        MG.gemm(w1, xq, xs, off, pairs, h, status, n_tiles=F // 128, kc=H // vals, g=2, nt=nt, mode=1, src_div=topk,
+                src_limit=P, out_scale=hs, num_ctas=sms, kind=kind)
 
     def gemm2():
-        ext().moe_gemm(w2, h, hs, off, pairs, wts.view(-1), rows, None, status, H // (128 * gd), F // vals, gd, nt,
-                       2, 1, 1 << 30, 1.0, sms, kind, None)
+        MG.gemm(w2, h, hs, off, pairs, rows, status, n_tiles=H // (128 * gd), kc=F // vals, g=gd, nt=nt, mode=2,
+                src_div=1, pair_w=wts.view(-1), num_ctas=sms, kind=kind)
     if launches:
         for _ in range(launches):
             gemm1()

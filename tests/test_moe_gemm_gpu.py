@@ -42,8 +42,8 @@ def test_moe_gemm_plain(cuda, nt, ctas):
     assert off.cpu().tolist() == [0] + torch.cumsum(cnt, 0).tolist()
     out = torch.zeros(P, N, dtype=torch.bfloat16, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
-    ext().moe_gemm(pack, xq.to(cuda), xs.to(cuda), off, pairs, None, out, None, status, N // 128, K // 128, 1, nt,
-                   0, topk, P, 1.0, ctas, 0, None)
+    MG.gemm(pack, xq.to(cuda), xs.to(cuda), off, pairs, out, status, n_tiles=N // 128, kc=K // 128, g=1, nt=nt,
+            mode=0, src_div=topk, src_limit=P, num_ctas=ctas)
     torch.cuda.synchronize()
     assert status.item() == 0
     ref = torch.stack([xd[p // topk] @ wd[int(ids.view(-1)[p])].T for p in range(P)])
@@ -73,8 +73,8 @@ def test_moe_gemm_swiglu_quant(cuda, nt):
     h = torch.zeros(P, F, dtype=torch.uint8, device=cuda)
     hs = torch.zeros(P, F // 128, dtype=torch.int32, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
-    ext().moe_gemm(pack, xq.to(cuda), xs.to(cuda), off, pairs, None, h, hs, status, F // 128, K // 128, 2, nt, 1,
-                   topk, P, 1.0, 148, 0, None)
+    MG.gemm(pack, xq.to(cuda), xs.to(cuda), off, pairs, h, status, n_tiles=F // 128, kc=K // 128, g=2, nt=nt,
+            mode=1, src_div=topk, src_limit=P, out_scale=hs)
     torch.cuda.synchronize()
     assert status.item() == 0
     dg, du = MG.dequant_blocks(qg, eg), MG.dequant_blocks(qu, eu)
@@ -144,8 +144,8 @@ def test_moe_gemm_paired_tiles(cuda):
     outs = []
     for pack, g in (MG.pack_weights_paired(wq, web), (MG.pack_weights([wq], [web]), 1)):
         out = torch.zeros(P, N, dtype=torch.bfloat16, device=cuda)
-        ext().moe_gemm(pack.to(cuda), xq.to(cuda), xs.to(cuda), off, pairs, None, out, None, status, N // (128 * g),
-                       K // 128, g, 32, 0, topk, P, 1.0, 148, 0, None)
+        MG.gemm(pack.to(cuda), xq.to(cuda), xs.to(cuda), off, pairs, out, status, n_tiles=N // (128 * g),
+                kc=K // 128, g=g, nt=32, mode=0, src_div=topk, src_limit=P)
         outs.append(out)
     torch.cuda.synchronize()
     assert status.item() == 0
@@ -170,8 +170,8 @@ def test_moe_gemm_nvfp4_plain(cuda, nt):
     ext().moe_align(ids.view(-1).to(cuda), 0, E, 0, off, pairs)
     out = torch.zeros(P, N, dtype=torch.bfloat16, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
-    ext().moe_gemm(pack, xq.to(cuda), xs.to(cuda), off, pairs, None, out, None, status, N // 128, K // 256, 1, nt,
-                   0, topk, P, 1.0, 148, 1, wg.to(cuda))
+    MG.gemm(pack, xq.to(cuda), xs.to(cuda), off, pairs, out, status, n_tiles=N // 128, kc=K // 256, g=1, nt=nt,
+            mode=0, src_div=topk, src_limit=P, kind=1, expert_mul=wg.to(cuda))
     torch.cuda.synchronize()
     assert status.item() == 0
     ref = torch.stack([xd[p // topk] @ wd[int(ids.view(-1)[p])].T for p in range(P)])

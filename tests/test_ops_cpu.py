@@ -93,3 +93,20 @@ def test_index_pool_layout_roundtrip():
     if len(pos):
         i = int(pos[0])
         assert torch.equal(page[r * 128 + ((c ^ (r & 7)) * 16): r * 128 + ((c ^ (r & 7)) * 16) + 16], rows[i, 16 * c:16 * c + 16])
+
+
+def test_ep_layout_regions_and_pair_routing():
+    from inference_optimizations_b200.parallel.ep import EPLayout
+    for fmt in ("fp8", "nvfp4"):
+        L = EPLayout(world=8, T_max=16, topk=8, H=7168, fmt=fmt)
+        regions = [(L.off_x, 8 * 16 * L.row_bytes), (L.off_s, 8 * 16 * L.scale_words * 4),
+                   (L.off_ids, 8 * 16 * 8 * 4), (L.off_comb, L.comb_rows * 7168 * 2), (L.off_flags, 8 * 4)]
+        for (a, n), (b, _) in zip(regions, regions[1:]):
+            assert a % 256 == 0 and a + n <= b
+        assert L.off_flags + 32 <= L.nbytes
+        # every pair's output lands on the rank that owns its token, at row t * topk + k
+        for src in (0, 3, 7):
+            for t in (0, 5, 15):
+                for k in (0, 7):
+                    assert L.comb_row(L.pair(src, t, k)) == (src, t * 8 + k)
+        assert L.owner(255, 32) == 7 and L.owner(32, 32) == 1
