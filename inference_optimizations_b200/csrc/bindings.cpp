@@ -463,6 +463,34 @@ void ep_dispatch(const at::Tensor& peers, const at::Tensor& xq, const at::Tensor
   CHECK_CUDA_OK(iob::ep_dispatch(a, stream()));
 }
 
+void dcp_merge(const at::Tensor& peers, int64_t off_data, int64_t off_flags, int64_t T, int64_t T_max, int64_t H,
+               int64_t rank, int64_t nranks, int64_t half, at::Tensor epoch, at::Tensor out,
+               const c10::optional<at::Tensor>& lse_out, at::Tensor status) {
+  req(peers, at::kLong, "peers");
+  req(epoch, at::kInt, "epoch");
+  req(out, at::kBFloat16, "out");
+  req(status, at::kInt, "status");
+  TORCH_CHECK(out.is_contiguous() && out.size(0) >= T && out.size(1) == H / nranks && out.size(2) == 512, "out");
+  if (lse_out.has_value()) TORCH_CHECK(lse_out->scalar_type() == at::kFloat && lse_out->numel() >= T * H / nranks, "lse");
+  iob::DcpMergeArgs a{};
+  a.peers = reinterpret_cast<const long long*>(peers.data_ptr<int64_t>());
+  a.off_data = off_data;
+  a.off_flags = off_flags;
+  a.out = out.data_ptr();
+  a.lse_out = lse_out.has_value() ? lse_out->data_ptr<float>() : nullptr;
+  a.epoch = epoch.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  a.T = static_cast<int>(T);
+  a.T_max = static_cast<int>(T_max);
+  a.H = static_cast<int>(H);
+  a.Hg = static_cast<int>(H / nranks);
+  a.rank = static_cast<int>(rank);
+  a.nranks = static_cast<int>(nranks);
+  a.half = static_cast<int>(half);
+  const at::cuda::CUDAGuard g(out.device());
+  CHECK_CUDA_OK(iob::dcp_merge(a, stream()));
+}
+
 void ep_barrier(const at::Tensor& peers, int64_t off_flags, int64_t rank, int64_t world, at::Tensor epoch,
                 at::Tensor status) {
   req(peers, at::kLong, "peers");
@@ -546,6 +574,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_quant", &rmsnorm_quant);
   m.def("ep_dispatch", &ep_dispatch);
   m.def("ep_barrier", &ep_barrier);
+  m.def("dcp_merge", &dcp_merge);
   m.def("umma_gemm_test", &umma_gemm_test);
   m.def("umma_f8_mn_test", &umma_f8_mn_test);
   m.def("nvfp4_lut_test", &nvfp4_lut_test);

@@ -23,7 +23,6 @@ namespace iob {
 namespace {
 
 constexpr int kArThreads = 256;
-constexpr long long kArSpinLimit = 1ll << 26;   // polls of one flag before giving up (well above any real wait)
 
 __device__ __forceinline__ void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -70,10 +69,14 @@ __global__ void __launch_bounds__(kArThreads) ar_norm2_kernel(const ArNormArgs a
   if (threadIdx.x == 0) {
     const int* mine = reinterpret_cast<const int*>(reinterpret_cast<const char*>(a.peers[a.rank]) + a.flag_offset);
     int good = 1;
+    const unsigned long long t0 = global_ns();     // bounded: kWaitLimitNs for all peers together
     for (int r = 0; r < NR && good; ++r) {
-      long long it = 0;
-      while (ld_acquire_sys(mine + b * NR + r) < e) {
-        if (++it > kArSpinLimit) { good = 0; record_status(a.status, kTimeoutPeer); break; }
+      for (uint32_t it = 0; ld_acquire_sys(mine + b * NR + r) < e; ++it) {
+        if ((it & 255) == 255 && global_ns() - t0 > kWaitLimitNs) {
+          good = 0;
+          record_status(a.status, kTimeoutPeer);
+          break;
+        }
       }
     }
     ok_s = good;

@@ -180,6 +180,18 @@ cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, i
 cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_base, const float* w, void* y,
                         cudaStream_t s);
 
+// ---- decode context parallelism: partial-softmax merge over peer memory (dcp.cu)
+struct DcpMergeArgs {
+  const long long* peers;     // [nranks] symmetric buffer bases
+  long long off_data, off_flags;
+  void* out;                  // bf16 [T, Hg, 512]: this rank's head group, merged
+  float* lse_out;             // optional fp32 [T, Hg]
+  int* epoch;                 // device [2]
+  int* status;
+  int T, T_max, H, Hg, rank, nranks, half;
+};
+cudaError_t dcp_merge(const DcpMergeArgs& a, cudaStream_t s);
+
 // ---- expert-parallel exchange over peer memory (ep.cu)
 struct EpDispatchArgs {
   const long long* peers;     // [world] base address of every rank's symmetric buffer (device)

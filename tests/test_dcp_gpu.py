@@ -1,0 +1,78 @@
+"""Context-parallel sparse-MLA decode on 2 GPUs (parallel/dcp.py + csrc/dcp.cu): each rank decodes over the rows
+it owns and merges the partial softmax states of its head group over peer memory; the result matches the
+single-GPU decode over the whole pool (same E4M3 kernel), over repeated calls (both buffer halves) and with tokens
+whose selection a rank does not own at all.  Two child processes (needs >= 2 GPUs)."""
+import os
+import subprocess
+import sys
+import textwrap
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORKER = textwrap.dedent("""
+    import math, os, sys, torch, torch.distributed as dist
+    import torch.nn.functional as Fn
+    from inference_optimizations_b200.parallel.dcp import DCPAttention
+    from inference_optimizations_b200.ops import mla as M
+    from inference_optimizations_b200.utils.microbench import mla_pool_random
+    rank, S = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+    dev = torch.device("cuda", rank)
+    T_max, H, N, K = 8, 128, 8192, 640
+    fmt = M.FMT_NVFP4
+    pool = mla_pool_random(N, fmt, dev, seed=7)                 # identical on both ranks (seeded)
+    local = pool[rank::S].contiguous()
+    dc = DCPAttention(rank, S, T_max, H, dev)
+    sm = 1.0 / math.sqrt(576)
+    worst = 1.0
+    for it, T in enumerate([5, 8, 3]):
+        g = torch.Generator().manual_seed(10 + it)
+        q = (torch.randn(T, H, 576, generator=g) * 0.5).to(torch.bfloat16).to(dev)
+        sel = torch.stack([torch.randperm(N, generator=g)[:K] for _ in range(T)]).int()
+        sel[0, K // 2:] = -1
+        if T > 2:
+            sel[2] = torch.arange(K, dtype=torch.int32) * S            # token 2: rank 0 owns every row
+        sel = sel.to(dev)
+        o = dc.decode(q, local, sel, sm, fmt)
+        ref = M.mla_decode(q, pool, sel, sm, fmt)[:, rank * (H // S):(rank + 1) * (H // S)]
+        torch.cuda.synchronize()
+        dc.check()
+        cos = Fn.cosine_similarity(o.float().flatten(), ref.float().flatten(), dim=0).item()
+        err = ((o.float() - ref.float()).norm() / ref.float().norm()).item()
+        worst = min(worst, cos)
+        print(f"rank {rank} it {it} cos {cos:.6f} rel {err:.4f}", flush=True)
+    ok = worst > 0.999
+    del dc
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if ok else 1)
+""")
+
+
+def test_dcp_decode_two_gpus(cuda, tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    script = tmp_path / "dcp_worker.py"
+    script.write_text(WORKER)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT="29581", NCCL_NVLS_ENABLE="0",
+                   PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
+        procs.append(subprocess.Popen([sys.executable, str(script)], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    outs = []
+    for p in procs:
+        try:
+            out, _ = p.communicate(timeout=300)
+        except subprocess.TimeoutExpired:
+            p.kill()
+            out, _ = p.communicate()
+        outs.append(out)
+    for p, out in zip(procs, outs):
+        assert p.returncode == 0, out[-3000:]
