@@ -491,6 +491,31 @@ void dcp_merge(const at::Tensor& peers, int64_t off_data, int64_t off_flags, int
   CHECK_CUDA_OK(iob::dcp_merge(a, stream()));
 }
 
+void glmflash_write(const at::Tensor& nope, const at::Tensor& slot, at::Tensor pool) {
+  req(nope, at::kBFloat16, "nope");
+  req(slot, at::kInt, "slot");
+  req(pool, at::kByte, "pool");
+  TORCH_CHECK(nope.dim() == 2 && nope.size(1) == 512 && nope.stride(1) == 1 && pool.size(1) == 288 &&
+                  slot.numel() == nope.size(0),
+              "glmflash_write shapes");
+  const at::cuda::CUDAGuard g(nope.device());
+  CHECK_CUDA_OK(iob::glmflash_write(nope.data_ptr(), static_cast<int>(nope.stride(0)), slot.data_ptr<int>(),
+                                    pool.data_ptr<uint8_t>(), static_cast<int>(nope.size(0)), stream()));
+}
+
+void v4pro_write(const at::Tensor& x, const at::Tensor& slot, at::Tensor pool, int64_t rope_bf16) {
+  req(x, at::kBFloat16, "x");
+  req(slot, at::kInt, "slot");
+  req(pool, at::kByte, "pool");
+  TORCH_CHECK(x.dim() == 2 && x.size(1) == 512 && x.stride(1) == 1 && pool.size(1) == (rope_bf16 ? 384 : 320) &&
+                  slot.numel() == x.size(0),
+              "v4pro_write shapes");
+  const at::cuda::CUDAGuard g(x.device());
+  CHECK_CUDA_OK(iob::v4pro_write(x.data_ptr(), static_cast<int>(x.stride(0)), slot.data_ptr<int>(),
+                                 pool.data_ptr<uint8_t>(), static_cast<int>(x.size(0)), static_cast<int>(rope_bf16),
+                                 stream()));
+}
+
 void ep_barrier(const at::Tensor& peers, int64_t off_flags, int64_t rank, int64_t world, at::Tensor epoch,
                 at::Tensor status) {
   req(peers, at::kLong, "peers");
@@ -575,6 +600,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_dispatch", &ep_dispatch);
   m.def("ep_barrier", &ep_barrier);
   m.def("dcp_merge", &dcp_merge);
+  m.def("glmflash_write", &glmflash_write);
+  m.def("v4pro_write", &v4pro_write);
   m.def("umma_gemm_test", &umma_gemm_test);
   m.def("umma_f8_mn_test", &umma_f8_mn_test);
   m.def("nvfp4_lut_test", &nvfp4_lut_test);

@@ -2,8 +2,9 @@
 // rank; no NCCL on this path).
 //
 // Dispatch: each rank pushes its quantized token rows straight into the receive slots of the ranks that own at
-// least one of the token's top-k experts (16-byte peer stores issued by the SMs; a token goes to each owner once,
-// not once per expert), and its routing ids to every rank (tiny).  Slot (src, t) of every receiver is fixed, so no
+// least one of the token's top-k experts, and into its own slot (the local shared expert reads it there); 16-byte
+// peer stores issued by the SMs, a token goes to each owner once, not once per expert.  Routing ids go to every rank
+// (tiny).  Slot (src, t) of every receiver is fixed, so no
 // counts have to be exchanged before the data: a rank with fewer than T_max tokens marks the remaining slots' ids
 // -1.  The grouped expert GEMM then gathers its rows from the local receive buffer, and its epilogue stores each
 // expert output row directly into the owning rank's combine buffer over NVLink (see `out_peers` in moe_gemm.cu):
@@ -40,11 +41,13 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchArgs a
   __shared__ uint32_t dest_mask;
   if (threadIdx.x == 0) {
     uint32_t m = 0;
-    if (t < a.T)
+    if (t < a.T) {
+      m = 1u << a.rank;               // own slot always: the shared expert reads every local token from it
       for (int k = 0; k < a.topk; ++k) {
         const int e = a.ids[t * a.topk + k];
         if (e >= 0 && e < a.world * a.E_loc) m |= 1u << (e / a.E_loc);
       }
+    }
     dest_mask = m;
   }
   __syncthreads();

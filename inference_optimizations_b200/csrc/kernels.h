@@ -180,6 +180,11 @@ cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, i
 cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_base, const float* w, void* y,
                         cudaStream_t s);
 
+// ---- more latent-row formats (kv_formats.cu)
+cudaError_t glmflash_write(const void* nope, int stride, const int* slot, uint8_t* pool, int T, cudaStream_t s);
+cudaError_t v4pro_write(const void* x, int stride, const int* slot, uint8_t* pool, int T, int rope_bf16,
+                        cudaStream_t s);
+
 // ---- decode context parallelism: partial-softmax merge over peer memory (dcp.cu)
 struct DcpMergeArgs {
   const long long* peers;     // [nranks] symmetric buffer bases

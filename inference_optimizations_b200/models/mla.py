@@ -156,8 +156,46 @@ class MLAModel:
         """RoPE on the last dim of x [T, n, 64] (fp32 math, bf16 result)."""
         return B.apply_rope_ref(x.float(), pos, cs).to(torch.bfloat16)
 
+    def _block_scaled(self, i: int):
+        """Grouped block-scaled experts of layer i (FP8 128x128 or NVFP4, per `expert_dtype` / `weight_dtype`), built
+        from the layer's weights on first use; the dense FFN of the first layers runs as one expert with every token."""
+        from ..ops.moe_gemm import BlockScaledExperts
+        if not hasattr(self, "_bs"):
+            self._bs = {}
+        if i not in self._bs:
+            c, f = self.cfg, self.layers[i].ffn
+            if c.is_moe(i):
+                F = c.expert_ffn
+                sh = None
+                if f["shared_gu"] is not None:
+                    sh = (f["shared_gu"][:F], f["shared_gu"][F:], f["shared_down"])
+                self._bs[i] = BlockScaledExperts(f["w_gu"][:, :F], f["w_gu"][:, F:], f["w_down"], shared=sh,
+                                                 fmt=c.expert_dtype)
+            else:
+                F = c.dense_ffn
+                self._bs[i] = BlockScaledExperts(f["w_gu"][None, :F], f["w_gu"][None, F:], f["w_down"][None],
+                                                 fmt=c.weight_dtype)
+        return self._bs[i]
+
+    def _quantized_ffn(self, i: int) -> bool:
+        c = self.cfg
+        if self.device.type != "cuda":
+            return False
+        if c.is_moe(i):
+            return c.expert_dtype in ("fp8", "nvfp4") and c.num_shared <= 1
+        return c.weight_dtype in ("fp8", "nvfp4")
+
     def _ffn(self, i: int, x: torch.Tensor) -> torch.Tensor:
         c, f = self.cfg, self.layers[i].ffn
+        if self._quantized_ffn(i):
+            ex = self._block_scaled(i)
+            t = x.shape[0]
+            if not c.is_moe(i):
+                ids = torch.zeros(t, 1, dtype=torch.int32, device=x.device)
+                return ex.forward(x, ids, torch.ones(t, 1, device=x.device))
+            logits = Fn.linear(x.float(), f["gate"].float())
+            ids, w = MOE.route(logits, f["e_bias"], c.topk, c.n_group, c.topk_group, c.routed_scale, c.router)
+            return ex.forward(x, ids, w)
         if not c.is_moe(i):
             return MOE.swiglu(x, f["w_gu"], f["w_down"])
         return MOE.moe_forward(x, f["gate"], f["e_bias"], f["w_gu"], f["w_down"], f["shared_gu"], f["shared_down"],

@@ -17,6 +17,13 @@ Formats kept byte-compatible with the reference (the encoding is a contract betw
 * DSA indexer key, 132 bytes: 128 E4M3 values + one fp32 scale (`tooling/rooflines/glm_roofline.py:43-50`).
 * FP8 activation quant with per-128 power-of-two (UE8M0) scales (`moe-gemm/norm-quant-fused/pro_norm_quant.py:1-17`):
   e = ceil(log2(amax / 448)), scale = 2^e, q = e4m3(x / scale).
+* Rope-free NVFP4 row, 288 bytes (GLM-Flash DSA layers, kv_lora 512 and no rope; `kv-cache-4bit/glmflash-kv4/
+  glmflash_kv4.py:1-20`): the first 288 bytes of the 352-byte row, same encoding.
+* DeepSeek V4 Pro 4-bit cell, 320 bytes (rope E4M3) or 384 bytes (rope bf16) (`kv-cache-4bit/kv4pro-deepseek/
+  kv4pro_fp4.py:1-30`): [0, 224) 448 nope values as E2M1 pairs, [224, 252) 28 E4M3 scales (one per 16), [252, 256)
+  zero, [256, ..) rope.  Per 16-block the scale is e4m3(min(amax / 6 * f, 448)) for the f in (1, 0.93, 0.86, 0.8)
+  with the smallest squared error, q = x * (1 / scale), E2M1 rounding to nearest with ties to even (unlike the MLA
+  row's ties-down) and saturation at 6.
 """
 from __future__ import annotations
 
@@ -143,6 +150,87 @@ def sparse_mla_reference(q: torch.Tensor, kv: torch.Tensor, table: torch.Tensor,
 
 
 # ------------------------------------------------------------------------------------------------ activations
+
+
+GLMFLASH_ROW_BYTES = MLA_ROPE_OFF                      # 288
+
+
+def glmflash_row_quantize(nope: torch.Tensor) -> torch.Tensor:
+    """nope [T, 512] -> uint8 [T, 288] rope-free NVFP4 rows."""
+    q, s8 = nvfp4_quantize(nope.float())
+    return torch.cat([q, s8.view(torch.uint8)], dim=-1)
+
+
+def glmflash_row_dequantize(rows: torch.Tensor) -> torch.Tensor:
+    return nvfp4_dequantize(rows[:, :MLA_SCALE_OFF], rows[:, MLA_SCALE_OFF:GLMFLASH_ROW_BYTES].contiguous().view(
+        torch.float8_e4m3fn))
+
+
+V4P_NOPE, V4P_ROPE = 448, 64
+V4P_SCALE_OFF, V4P_ROPE_OFF = 224, 256
+V4P_SCALE_SEARCH = (1.0, 0.93, 0.86, 0.8)
+_E2M1_EVEN = (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0)       # > at 0.25 / 1.25 / 2.5 / 5, >= at 0.75 / 1.75 / 3.5
+
+
+def v4pro_cell_bytes(rope: str = "fp8") -> int:
+    return V4P_ROPE_OFF + (V4P_ROPE if rope == "fp8" else 2 * V4P_ROPE)
+
+
+def _e2m1_mag_even(a: torch.Tensor) -> torch.Tensor:
+    a = a.clamp(max=E2M1_MAX)
+    return ((a > 0.25).int() + (a >= 0.75).int() + (a > 1.25).int() + (a >= 1.75).int() + (a > 2.5).int()
+            + (a >= 3.5).int() + (a > 5.0).int())
+
+
+def v4pro_cell_quantize(x: torch.Tensor, rope: str = "fp8") -> torch.Tensor:
+    """x [N, 512] (448 nope + 64 rope) -> uint8 [N, 320 | 384] cells (scale search, ties-to-even E2M1).  The block
+    error is summed sequentially over the 16 values (the writer kernel's order)."""
+    x = x.float()
+    n = x.shape[0]
+    nope = x[:, :V4P_NOPE].reshape(n, V4P_NOPE // FP4_BLOCK, FP4_BLOCK)
+    amax = nope.abs().amax(-1)
+    table = torch.tensor(_E2M1_MAG, device=x.device)
+    best = None
+    for f in V4P_SCALE_SEARCH:
+        s8 = ((amax / E2M1_MAX) * torch.tensor(f, dtype=torch.float32)).clamp(max=E4M3_MAX).to(torch.float8_e4m3fn)
+        sf = s8.float()
+        inv = torch.where(sf > 0, 1.0 / torch.where(sf > 0, sf, torch.ones_like(sf)), torch.zeros_like(sf))
+        q = nope * inv[..., None]
+        mag = _e2m1_mag_even(q.abs())
+        code = mag | (((q < 0) & (mag > 0)).int() << 3)
+        d = torch.where(q < 0, -table[mag], table[mag]) * sf[..., None] - nope
+        err = torch.zeros_like(amax)
+        for j in range(FP4_BLOCK):
+            err = err + d[..., j] * d[..., j]
+        if best is None:
+            best = [code, s8.view(torch.uint8), err]
+        else:
+            m = err < best[2]
+            best = [torch.where(m[..., None], code, best[0]), torch.where(m, s8.view(torch.uint8), best[1]),
+                    torch.where(m, err, best[2])]
+    code = best[0].reshape(n, V4P_NOPE)
+    cells = torch.zeros(n, v4pro_cell_bytes(rope), dtype=torch.uint8, device=x.device)
+    cells[:, :V4P_SCALE_OFF] = pack_nibbles(code)
+    cells[:, V4P_SCALE_OFF:V4P_SCALE_OFF + V4P_NOPE // FP4_BLOCK] = best[1]
+    r = x[:, V4P_NOPE:]
+    if rope == "fp8":
+        cells[:, V4P_ROPE_OFF:] = r.clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn).view(torch.uint8)
+    else:
+        cells[:, V4P_ROPE_OFF:] = r.to(torch.bfloat16).contiguous().view(torch.uint8)
+    return cells
+
+
+def v4pro_cell_dequantize(cells: torch.Tensor, rope: str = "fp8") -> torch.Tensor:
+    """uint8 [N, 320 | 384] -> fp32 [N, 512]."""
+    n = cells.shape[0]
+    vals = e2m1_decode(unpack_nibbles(cells[:, :V4P_SCALE_OFF]))
+    sf = cells[:, V4P_SCALE_OFF:V4P_SCALE_OFF + V4P_NOPE // FP4_BLOCK].contiguous().view(torch.float8_e4m3fn).float()
+    nope = (vals.reshape(n, -1, FP4_BLOCK) * sf[..., None]).reshape(n, V4P_NOPE)
+    if rope == "fp8":
+        r = cells[:, V4P_ROPE_OFF:V4P_ROPE_OFF + V4P_ROPE].contiguous().view(torch.float8_e4m3fn).float()
+    else:
+        r = cells[:, V4P_ROPE_OFF:V4P_ROPE_OFF + 2 * V4P_ROPE].contiguous().view(torch.bfloat16).float()
+    return torch.cat([nope, r], 1)
 
 
 def fp8_quant_ue8m0(x: torch.Tensor, group: int = 128) -> tuple[torch.Tensor, torch.Tensor]:

@@ -51,3 +51,22 @@ def test_mla_model_gpu_vs_cpu_oracles(cuda, kv):
     assert cos.mean().item() > 0.98 and cos.min().item() > 0.9, (cos.mean().item(), cos.min().item())
     out = gpu.generate([prompt[:40], prompt[:7]], SamplingParams(max_new_tokens=6))
     assert all(len(o) == 6 for o in out)
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "nvfp4"])
+def test_block_scaled_experts_in_model(cuda, fmt):
+    """The MLA model with FP8 / NVFP4 block-scaled experts (grouped tcgen05 GEMMs) tracks its bf16 twin."""
+    import torch.nn.functional as Fn
+    from inference_optimizations_b200.models.mla import MLAModel
+    from inference_optimizations_b200.ops import moe as MOE
+    over = dict(expert_ffn=256, dense_ffn=512, weight_dtype=fmt, expert_dtype=fmt)
+    cq = model_config("tiny_mla", **over)
+    cb = model_config("tiny_mla", **dict(over, weight_dtype="bf16", expert_dtype="bf16"))
+    mq, mb = MLAModel(cq, cuda, seed=3), MLAModel(cb, cuda, seed=3)
+    mb.copy_from(mq)
+    torch.manual_seed(0)
+    x = (torch.randn(9, cq.hidden, device=cuda) * 0.5).to(torch.bfloat16)
+    for i in range(cq.num_layers):
+        yq, yb = mq._ffn(i, x), mb._ffn(i, x)
+        cos = Fn.cosine_similarity(yq.float().flatten(), yb.float().flatten(), dim=0).item()
+        assert cos > (0.99 if fmt == "fp8" else 0.95), (i, cos)
