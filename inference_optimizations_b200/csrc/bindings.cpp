@@ -516,6 +516,38 @@ void v4pro_write(const at::Tensor& x, const at::Tensor& slot, at::Tensor pool, i
                                  stream()));
 }
 
+void pd_copy(const at::Tensor& src, int64_t dst_ptr, const at::Tensor& src_pages, const at::Tensor& dst_pages,
+             int64_t page_bytes, int64_t layers, int64_t src_layer_stride, int64_t dst_layer_stride) {
+  req(src, at::kByte, "src");
+  req(src_pages, at::kInt, "src_pages");
+  req(dst_pages, at::kInt, "dst_pages");
+  TORCH_CHECK(src_pages.numel() == dst_pages.numel() && src.is_contiguous(), "pd_copy shapes");
+  iob::PdCopyArgs a{};
+  a.src = src.data_ptr<uint8_t>();
+  a.dst = reinterpret_cast<void*>(dst_ptr);
+  a.src_pages = src_pages.data_ptr<int>();
+  a.dst_pages = dst_pages.data_ptr<int>();
+  a.page_bytes = page_bytes;
+  a.src_layer_stride = src_layer_stride;
+  a.dst_layer_stride = dst_layer_stride;
+  a.n_pairs = static_cast<int>(src_pages.numel());
+  a.layers = static_cast<int>(layers);
+  const at::cuda::CUDAGuard g(src.device());
+  CHECK_CUDA_OK(iob::pd_copy(a, stream()));
+}
+
+void pd_signal(int64_t peer_flag_ptr, int64_t value, const at::Tensor& like) {
+  const at::cuda::CUDAGuard g(like.device());
+  CHECK_CUDA_OK(iob::pd_signal(reinterpret_cast<int*>(peer_flag_ptr), static_cast<int>(value), stream()));
+}
+
+void pd_wait(const at::Tensor& flag, int64_t value, at::Tensor status) {
+  req(flag, at::kInt, "flag");
+  req(status, at::kInt, "status");
+  const at::cuda::CUDAGuard g(flag.device());
+  CHECK_CUDA_OK(iob::pd_wait(flag.data_ptr<int>(), static_cast<int>(value), status.data_ptr<int>(), stream()));
+}
+
 void ep_barrier(const at::Tensor& peers, int64_t off_flags, int64_t rank, int64_t world, at::Tensor epoch,
                 at::Tensor status) {
   req(peers, at::kLong, "peers");
@@ -601,6 +633,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_barrier", &ep_barrier);
   m.def("dcp_merge", &dcp_merge);
   m.def("glmflash_write", &glmflash_write);
+  m.def("pd_copy", &pd_copy);
+  m.def("pd_signal", &pd_signal);
+  m.def("pd_wait", &pd_wait);
   m.def("v4pro_write", &v4pro_write);
   m.def("umma_gemm_test", &umma_gemm_test);
   m.def("umma_f8_mn_test", &umma_f8_mn_test);

@@ -180,6 +180,19 @@ cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, i
 cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_base, const float* w, void* y,
                         cudaStream_t s);
 
+// ---- prefill -> decode KV page transfer over peer memory (pd.cu)
+struct PdCopyArgs {
+  const uint8_t* src;         // this GPU's pool (layer 0), layer l at src + l * src_layer_stride
+  void* dst;                  // the decode GPU's pool (peer mapping), same layout with dst_layer_stride
+  const int* src_pages;       // [n_pairs]
+  const int* dst_pages;       // [n_pairs]
+  long long page_bytes, src_layer_stride, dst_layer_stride;
+  int n_pairs, layers;
+};
+cudaError_t pd_copy(const PdCopyArgs& a, cudaStream_t s);
+cudaError_t pd_signal(int* peer_flag, int value, cudaStream_t s);
+cudaError_t pd_wait(const int* flag, int value, int* status, cudaStream_t s);
+
 // ---- more latent-row formats (kv_formats.cu)
 cudaError_t glmflash_write(const void* nope, int stride, const int* slot, uint8_t* pool, int T, cudaStream_t s);
 cudaError_t v4pro_write(const void* x, int stride, const int* slot, uint8_t* pool, int T, int rope_bf16,

@@ -1,0 +1,76 @@
+"""Prefill -> decode page transfer over peer memory (parallel/pd.py) on 2 GPUs: pages of every layer land at the
+planned decode pages bit for bit, the decode side's device wait releases on the published sequence number, and a
+sequence number nobody publishes ends the wait with a status instead of a hang.  Two child processes."""
+import os
+import subprocess
+import sys
+import textwrap
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORKER = textwrap.dedent("""
+    import os, sys, torch, torch.distributed as dist
+    from inference_optimizations_b200.parallel.pd import PDPool
+    rank = int(os.environ["RANK"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+    dev = torch.device("cuda", rank)
+    L, P, PB = 3, 40, 64 * 352
+    pool = PDPool(L, P, PB, dev)
+    g = torch.Generator().manual_seed(1)
+    src_pages, dst_pages = [3, 17, 5, 39], [0, 22, 9, 1]
+    ok = True
+    if rank == 0:                      # prefill side
+        for l in range(L):
+            pool.layer(l).copy_(torch.randint(0, 256, (P, PB), generator=g, dtype=torch.uint8).to(dev))
+        pool.push(1, src_pages, dst_pages, seq=1)
+        torch.cuda.synchronize()
+        ref = torch.stack([pool.layer(l)[src_pages].cpu() for l in range(L)])
+        dist.broadcast_object_list([ref.numpy().tobytes()], src=0)
+    else:                              # decode side
+        pool.wait(1)
+        got = torch.stack([pool.layer(l)[dst_pages] for l in range(L)]).cpu()
+        torch.cuda.synchronize()
+        pool.check()
+        obj = [None]
+        dist.broadcast_object_list(obj, src=0)
+        import numpy as np
+        ref = torch.from_numpy(np.frombuffer(obj[0], dtype=np.uint8).copy()).view(L, len(src_pages), PB)
+        ok = torch.equal(got, ref)
+        pool.wait(2)                   # never published: bounded wait, status set
+        torch.cuda.synchronize()
+        ok = ok and int(pool.status.item()) == 4
+        print("rank 1 pages equal and timeout reported:", ok, flush=True)
+    dist.barrier()
+    del pool
+    dist.destroy_process_group()
+    sys.exit(0 if ok else 1)
+""")
+
+
+def test_pd_page_transfer_two_gpus(cuda, tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    script = tmp_path / "pd_worker.py"
+    script.write_text(WORKER)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT="29591", NCCL_NVLS_ENABLE="0",
+                   PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
+        procs.append(subprocess.Popen([sys.executable, str(script)], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    outs = []
+    for p in procs:
+        try:
+            out, _ = p.communicate(timeout=300)
+        except subprocess.TimeoutExpired:
+            p.kill()
+            out, _ = p.communicate()
+        outs.append(out)
+    for p, out in zip(procs, outs):
+        assert p.returncode == 0, out[-3000:]
