@@ -337,16 +337,16 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
               int64_t out_shared_base, int64_t pairs_total) {
   req(wpack, at::kByte, "wpack");
   req(x, at::kByte, "x");
-  req(x_scale, at::kInt, "x_scale");
   req(off, at::kInt, "off");
   req(pairs, at::kInt, "pairs");
   req(status, at::kInt, "status");
-  TORCH_CHECK(kind == 0 || kind == 1, "kind");
-  const int64_t sfw = kind == 0 ? 1 : 4;
+  TORCH_CHECK(kind == 0 || kind == 1 || kind == 2, "kind");
+  const int64_t sfw = kind == 0 ? 1 : (kind == 1 ? 4 : 0);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.size(1) == kc * 128, "x [rows, KC*128 bytes]");
-  TORCH_CHECK(x_scale.dim() == 2 && x_scale.is_contiguous() && x_scale.size(1) == kc * sfw &&
-                  x_scale.size(0) == x.size(0),
-              "x_scale [rows, KC * words]");
+  if (sfw)
+    TORCH_CHECK(x_scale.scalar_type() == at::kInt && x_scale.dim() == 2 && x_scale.is_contiguous() &&
+                    x_scale.size(1) == kc * sfw && x_scale.size(0) == x.size(0),
+                "x_scale [rows, KC * words]");
   const int64_t E = off.numel() - 1;
   TORCH_CHECK(wpack.numel() == E * n_tiles * kc * G * (16384 + 512 * sfw), "wpack size");
   if (expert_mul.has_value())
@@ -367,7 +367,7 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
   iob::MoeGemmArgs a{};
   a.wpack = wpack.data_ptr<uint8_t>();
   a.x = x.data_ptr<uint8_t>();
-  a.x_scale = reinterpret_cast<const uint32_t*>(x_scale.data_ptr<int>());
+  a.x_scale = sfw ? reinterpret_cast<const uint32_t*>(x_scale.data_ptr<int>()) : nullptr;
   a.expert_off = off.data_ptr<int>();
   a.pairs = pairs.data_ptr<int>();
   a.pair_w = pair_w.has_value() ? pair_w->data_ptr<float>() : nullptr;

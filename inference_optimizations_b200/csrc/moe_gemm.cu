@@ -42,9 +42,11 @@ constexpr uint32_t kSmemBudget = 227 * 1024;
 // KIND 0: E4M3 operands, UE8M0 scale per 32 K (one scale word per row per 128-byte chunk, 4 MMAs of K = 32 read
 // its four bytes).  KIND 1: packed E2M1 operands (256 values per 128-byte chunk), E4M3 scale per 16 K (four words
 // per row per chunk: MMA j of K = 64 reads word j's four bytes).
+// KIND 2: bf16 operands without block scales (kind::f16, K = 16 per MMA; 64 values per 128-byte chunk): the same
+// weight-streaming GEMM for dense bf16 linears (one "expert", every token).
 template <int NT, int G, int KIND>
 struct Cfg {
-  static constexpr int kSfw = KIND == 0 ? 1 : 4;                  // scale words (atoms) per row per chunk
+  static constexpr int kSfw = KIND == 0 ? 1 : (KIND == 1 ? 4 : 0);   // scale words (atoms) per row per chunk
   static constexpr uint32_t kX = NT * 128;
   static constexpr uint32_t kWBlk = G * (kTile + kSfw * kSfAtom);  // packed weight bytes per stage
   static constexpr uint32_t kRaw = kWBlk + kX + kSfw * kSfAtom;
@@ -53,7 +55,7 @@ struct Cfg {
   static constexpr int kStagesFit = (kSmemBudget - kCtrl - 1024) / kStage;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr int kAccCols = G * NT;
-  static constexpr int kSfCols = 4 * kSfw * (G + 1);
+  static constexpr int kSfCols = KIND == 2 ? 0 : 4 * kSfw * (G + 1);
   static constexpr int kAccBufs = (2 * kAccCols + kSfCols <= 512) ? 2 : 1;
   static constexpr int kUsed = kAccBufs * kAccCols + kSfCols;
   static constexpr uint32_t kTmemCols = kUsed <= 32 ? 32 : kUsed <= 64 ? 64 : kUsed <= 128 ? 128 : kUsed <= 256 ? 256 : 512;
@@ -283,12 +285,16 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
           for (int w = 0; w < G * kSfw; ++w) tmem_cp_sf(tmem + sfa_col + 4 * w, desc_sf(sfa_s + w * kSfAtom));
 #pragma unroll
           for (int w = 0; w < kSfw; ++w) tmem_cp_sf(tmem + sfb_col + 4 * w, desc_sf(sfb_s + w * kSfAtom));
+          (void)sfb_s;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint64_t bd = desc_sw128(x_s + 32 * j);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-              if constexpr (KIND == 0) {
+              if constexpr (KIND == 2) {
+                umma_f16_ss(acc + g * NT, desc_sw128(st + g * kTile + 32 * j), bd, idesc_dense(1, 1, 128, NT),
+                            (kc | j) ? 1u : 0u);
+              } else if constexpr (KIND == 0) {
                 umma_mxf8(acc + g * NT, desc_sw128(st + g * kTile + 32 * j), bd, idesc_mxf8(NT, j),
                           (tmem + sfa_col + 4 * g) | (static_cast<uint32_t>(j) << 30),
                           (tmem + sfb_col) | (static_cast<uint32_t>(j) << 30), (kc | j) ? 1u : 0u);
@@ -328,7 +334,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
 #pragma unroll
       for (int m = 0; m < 2; ++m) {
         const int r = t64 + 64 * m;
-        srow[m] = (r < rows && r < NT)
+        srow[m] = (KIND != 2 && r < rows && r < NT)
                       ? a.x_scale + static_cast<size_t>(src_row(a, a.pairs[row0 + r])) * (a.KC * kSfw)
                       : nullptr;
       }
@@ -630,7 +636,7 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* x, const __nv_bfloat16
 cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
   if (a.E <= 0 || a.E > kMaxGemmExperts || a.KC <= 0 || a.n_tiles <= 0 || a.num_ctas <= 0 || a.src_div <= 0 ||
       (a.x_stride % 16) || (reinterpret_cast<uintptr_t>(a.x) % 16) || (reinterpret_cast<uintptr_t>(a.wpack) % 16) ||
-      (a.mode == kMoeOutSwigluQuant && a.G != 2) || a.kind < 0 || a.kind > 1)
+      (a.mode == kMoeOutSwigluQuant && (a.G != 2 || a.kind == 2)) || a.kind < 0 || a.kind > 2)
     return cudaErrorInvalidValue;
 #define IOB_MG(NT_, G_, K_) \
   if (a.NT == NT_ && a.G == G_ && a.kind == K_) return launch_mg<NT_, G_, K_>(a, s);
@@ -638,6 +644,8 @@ cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
   IOB_MG(16, 2, 0) IOB_MG(32, 2, 0) IOB_MG(64, 2, 0) IOB_MG(128, 2, 0)
   IOB_MG(16, 1, 1) IOB_MG(32, 1, 1) IOB_MG(64, 1, 1) IOB_MG(128, 1, 1)
   IOB_MG(16, 2, 1) IOB_MG(32, 2, 1) IOB_MG(64, 2, 1) IOB_MG(128, 2, 1)
+  IOB_MG(16, 1, 2) IOB_MG(32, 1, 2) IOB_MG(64, 1, 2) IOB_MG(128, 1, 2)
+  IOB_MG(16, 2, 2) IOB_MG(32, 2, 2) IOB_MG(64, 2, 2) IOB_MG(128, 2, 2)
 #undef IOB_MG
   return cudaErrorInvalidValue;
 }

@@ -1,0 +1,56 @@
+"""Dense bf16 linear layers on the weight-streaming tcgen05 GEMM (csrc/moe_gemm.cu, kind::f16 variant).
+
+At decode the token count is small (tens of rows) and a linear layer is a pass over its weights.  The weights are
+packed once into UMMA-ready blocks (128 rows x 64 values, SW128, two adjacent 128-row tiles per block when N allows)
+so each pipeline stage is one contiguous bulk copy; the tokens are the MMA's N operand (swap-AB), so the weights
+stream at full tensor-core width whatever the batch.  y = x W^T exactly like `torch.nn.functional.linear` (fp32
+accumulation, bf16 out).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import moe_gemm as MG
+
+TILE = 128
+
+
+def pack_bf16(w: torch.Tensor, g: int) -> torch.Tensor:
+    """w bf16 [N, K] -> [1, N / (128 g), K / 64, g * 16384] uint8: g adjacent 128-row tiles per block."""
+    N, K = w.shape
+    kc = K // 64
+    b = w.contiguous().view(torch.uint8).view(N // (TILE * g), g, TILE, kc, 128)     # [nt, g, row, kc, 128 B]
+    t = b.permute(0, 3, 1, 2, 4).contiguous()                                         # [nt, kc, g, 128, 128]
+    t = MG._sw128(t)
+    return t.reshape(1, N // (TILE * g), kc, g * TILE * TILE)
+
+
+class DenseLinear:
+    def __init__(self, w: torch.Tensor):
+        N, K = w.shape
+        assert N % TILE == 0 and K % 64 == 0 and w.dtype == torch.bfloat16
+        self.N, self.K = N, K
+        self.g = 2 if N % 256 == 0 else 1
+        self.wpack = pack_bf16(w, self.g)
+        dev = w.device
+        self.num_ctas = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 1
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._rows: dict = {}
+
+    def _index(self, t: int, dev):
+        if t not in self._rows:
+            self._rows[t] = (torch.tensor([0, t], dtype=torch.int32, device=dev),
+                             torch.arange(t, dtype=torch.int32, device=dev))
+        return self._rows[t]
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        t = x.shape[0]
+        if out is None:
+            out = torch.empty(t, self.N, dtype=torch.bfloat16, device=x.device)
+        if t == 0:
+            return out
+        off, pairs = self._index(t, x.device)
+        xb = x.contiguous().view(torch.uint8)
+        MG.gemm(self.wpack, xb, xb, off, pairs, out, self.status, n_tiles=self.N // (TILE * self.g),
+                kc=self.K // 64, g=self.g, nt=MG.pick_nt(t), mode=0, src_div=1, num_ctas=self.num_ctas, kind=2)
+        return out

@@ -224,6 +224,34 @@ class BlockScaledExperts:
                                      if dev.type == "cuda" else 1)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
 
+    @classmethod
+    def random_packed(cls, E: int, F: int, H: int, fmt: str = "fp8", shared: bool = True, device="cuda",
+                      seed: int = 0) -> "BlockScaledExperts":
+        """Experts with random packed weights straight in the kernel layout (no bf16 master copy: benchmark-size
+        expert sets fit on the device).  Values are finite E4M3 / E2M1 codes with moderate scales."""
+        self = cls.__new__(cls)
+        self.fmt, self.kind = fmt, {"fp8": 0, "nvfp4": 1}[fmt]
+        self.has_shared, self.E, self.F, self.H = shared, E, F, H
+        n = E + int(shared)
+        g = torch.Generator(device=device).manual_seed(seed)
+        sfw, vals = (1, TILE) if self.kind == 0 else (4, 2 * TILE)
+
+        def rand(n_tiles, kc, gg):
+            w = torch.randint(0, 256, (n, n_tiles, kc, gg * (16384 + 512 * sfw)), dtype=torch.uint8, device=device,
+                              generator=g)
+            if self.kind == 0:
+                w[(w & 0x7F) == 0x7F] = 0
+            w[..., gg * 16384:] = 118 if self.kind == 0 else 0x18            # 2^-9 (UE8M0) / 2^-6 (E4M3)
+            return w
+        self.g2 = 2 if (self.kind == 0 and H % 256 == 0) else 1
+        self.w1 = rand(F // TILE, H // vals, 2)
+        self.w2 = rand(H // (TILE * self.g2), F // vals, self.g2)
+        self.mul1 = self.mul2 = None
+        self.q = None
+        self.num_ctas = torch.cuda.get_device_properties(device).multi_processor_count
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        return self
+
     def dequant(self):
         if self.fmt == "fp8":
             qg, eg, qu, eu, qd, ed = self.q

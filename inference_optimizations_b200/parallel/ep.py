@@ -62,18 +62,22 @@ class EPLayout:
 
 
 class EPMoE:
-    def __init__(self, rank: int, world: int, E_total: int, T_max: int, topk: int, w_gate: torch.Tensor,
-                 w_up: torch.Tensor, w_down: torch.Tensor, shared: tuple | None = None, fmt: str = "fp8",
-                 group=None):
-        """w_gate / w_up [E_loc, F, H], w_down [E_loc, H, F]: this rank's experts (global ids rank * E_loc ..)."""
+    def __init__(self, rank: int, world: int, E_total: int, T_max: int, topk: int, w_gate: torch.Tensor = None,
+                 w_up: torch.Tensor = None, w_down: torch.Tensor = None, shared: tuple | None = None,
+                 fmt: str = "fp8", group=None, experts: MG.BlockScaledExperts | None = None):
+        """w_gate / w_up [E_loc, F, H], w_down [E_loc, H, F]: this rank's experts (global ids rank * E_loc ..);
+        or `experts`: an already packed BlockScaledExperts of this rank's E_loc experts."""
         import torch.distributed._symmetric_memory as symm
         self.rank, self.world, self.T_max, self.topk = rank, world, T_max, topk
         self.E_loc = E_total // world
-        assert w_gate.shape[0] == self.E_loc, "pass this rank's slice of the experts"
-        self.ex = MG.BlockScaledExperts(w_gate, w_up, w_down, shared=shared, fmt=fmt)
-        self.fmt, self.kind, self.H, self.F = fmt, self.ex.kind, self.ex.H, self.ex.F
-        dev = w_gate.device
-        L = self.layout = EPLayout(world, T_max, topk, self.H, fmt)
+        if experts is None:
+            assert w_gate.shape[0] == self.E_loc, "pass this rank's slice of the experts"
+            experts = MG.BlockScaledExperts(w_gate, w_up, w_down, shared=shared, fmt=fmt)
+        self.ex = experts
+        self.fmt, self.kind, self.H, self.F = experts.fmt, self.ex.kind, self.ex.H, self.ex.F
+        shared = shared if shared is not None else (True if experts.has_shared else None)
+        dev = experts.w1.device
+        L = self.layout = EPLayout(world, T_max, topk, self.H, self.fmt)
         self.buf = symm.empty(L.nbytes, dtype=torch.uint8, device=dev)
         self.buf.zero_()
         grp = group if group is not None else dist.group.WORLD

@@ -245,6 +245,91 @@ def moe_gemm_case(b: int, experts: int, total_experts: int, topk: int, hidden: i
             "l2": "weights per launch exceed L2 (each touched expert read once)"}
 
 
+def ep_moe_case(tokens: int, total_experts: int, topk: int, hidden: int, ffn: int, wfmt: str = "fp8",
+                iters: int = 20) -> dict:
+    """Expert-parallel MoE layer (parallel/ep.py) under torchrun: each rank routes `tokens` tokens top-k over
+    `total_experts`, owns total_experts / world of them (+ a shared expert); one forward = quantize, dispatch,
+    barrier, align, two grouped GEMMs (peer-store epilogue), barrier, combine.  Device time per layer, max over
+    ranks (CUDA events around `iters` forwards, synchronized and barriered on both sides)."""
+    import torch.distributed as dist
+    from ..ops import moe_gemm as MG
+    from ..parallel.ep import EPMoE
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    E_loc = total_experts // world
+    ex = MG.BlockScaledExperts.random_packed(E_loc, ffn, hidden, wfmt, shared=True, device=dev, seed=rank)
+    ep = EPMoE(rank, world, total_experts, tokens, topk, experts=ex)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    x = torch.randn(tokens, hidden, device=dev, generator=g).to(torch.bfloat16)
+    ids = torch.rand(tokens, total_experts, device=dev, generator=g).topk(topk, dim=-1).indices.int()
+    w = torch.softmax(torch.randn(tokens, topk, device=dev, generator=g), -1)
+    for _ in range(3):
+        ep.forward(x, ids, w)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        ep.forward(x, ids, w)
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ep.check()
+    us = torch.tensor([e0.elapsed_time(e1) / iters * 1e3], device=dev)
+    dist.all_reduce(us, op=dist.ReduceOp.MAX)
+    # roofline: touched local experts' weights once (HBM) vs rows crossing NVLink
+    all_ids = [torch.empty_like(ids) for _ in range(world)]
+    dist.all_gather(all_ids, ids)
+    gids = torch.cat(all_ids).view(-1)
+    local = gids[(gids >= rank * E_loc) & (gids < (rank + 1) * E_loc)]
+    touched = int(torch.unique(local).numel()) + 1                                     # + shared expert
+    wb = (1.0 if wfmt == "fp8" else 0.5) * (1 + (1 / 32 if wfmt == "fp8" else 1 / 8))
+    w_bytes = touched * 3 * hidden * ffn * wb
+    row = hidden * (1.0 if wfmt == "fp8" else 0.5)
+    nv_bytes = tokens * topk * (row + 2 * hidden) * (world - 1) / world                  # out + back, remote share
+    t_hbm = w_bytes / (PEAKS["hbm_gbs"] * 1e3)
+    t_nvl = nv_bytes / (770.0 * 1e3)
+    floor = max(t_hbm, t_nvl)
+    res = {"kernel": "ep_moe_layer", "fmt": wfmt, "world": world, "tokens_per_rank": tokens, "topk": topk,
+           "experts_total": total_experts, "hidden": hidden, "ffn": ffn, "us_max_over_ranks": round(float(us), 1),
+           "touched_local_experts": touched, "roofline_us": round(floor, 1),
+           "frac_of_roofline": round(floor / float(us), 3),
+           "roofline_basis": "max(touched weights / measured HBM, remote rows / 770 GB/s)"}
+    del ep
+    return res if rank == 0 else {}
+
+
+def dense_linear_case(t: int, launches: int = 0) -> dict:
+    """Decode-size dense bf16 linears of the flagship model (Gemma-class 31B, TP1): the weight-streaming tcgen05
+    GEMM (ops/linear.py) against cuBLAS (torch.nn.functional.linear) on the same tensors, L2 flushed before each
+    launch."""
+    import torch.nn.functional as Fn
+    from ..ops.linear import DenseLinear
+    dev = torch.device("cuda:0")
+    shapes = {"qkv_swa": (16384, 5376), "o_swa": (5376, 8192), "gate_up": (43008, 5376), "down": (5376, 21504),
+              "qkv_global": (32768, 5376), "o_global": (5376, 16384), "lm_head": (262144, 5376)}
+    out = {"kernel": "dense_bf16_linear", "tokens": t, "l2": "flushed before each launch", "shapes": {}}
+    for name, (n, k) in shapes.items():
+        w = (torch.randn(n, k, device=dev) * 0.02).to(torch.bfloat16)
+        x = torch.randn(t, k, device=dev).to(torch.bfloat16)
+        lin = DenseLinear(w)
+        y = torch.empty(t, n, dtype=torch.bfloat16, device=dev)
+        if launches:
+            for _ in range(launches):
+                lin(x, y)
+            torch.cuda.synchronize()
+            return {}
+        ours = _time_flushed(lambda: lin(x, y))
+        cub = _time_flushed(lambda: Fn.linear(x, w))
+        nb = n * k * 2
+        err = float(((lin(x) .float() - Fn.linear(x, w).float()).abs().max()))
+        out["shapes"][name] = {"n": n, "k": k, "ours_us": round(ours, 1), "cublas_us": round(cub, 1),
+                               "ours_frac_hbm": round(nb / ours / 1e3 / PEAKS["hbm_gbs"], 3),
+                               "cublas_frac_hbm": round(nb / cub / 1e3 / PEAKS["hbm_gbs"], 3), "max_abs_diff": err}
+        del w, lin
+    return out
+
+
 def main() -> None:
     _load_peaks()
     p = argparse.ArgumentParser()
@@ -270,6 +355,18 @@ def main() -> None:
         r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches)
     elif a.kernel == "indexer":
         r = indexer_case(a.b, a.ctx, a.topk, launches=a.launches)
+    elif a.kernel == "dense_linear":
+        r = dense_linear_case(a.b, a.launches)
+    elif a.kernel == "ep_moe":
+        import torch.distributed as dist
+        rank = int(os.environ.get("RANK", "0"))
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", device_id=torch.device("cuda", torch.cuda.current_device()))
+        r = ep_moe_case(a.b, a.total_experts, a.topk, a.hidden, a.ffn, a.wfmt)
+        dist.barrier()
+        dist.destroy_process_group()
+        if rank:
+            r = {}
     elif a.kernel == "moe_gemm":
         r = moe_gemm_case(a.b, a.experts, a.total_experts, a.topk, a.hidden, a.ffn, a.wfmt, a.launches)
     elif a.kernel == "mla_decode":

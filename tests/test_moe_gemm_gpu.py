@@ -209,3 +209,19 @@ def test_nvfp4_experts_forward(cuda, shared):
     ref = ex.forward_ref(x, ids, w)
     cos = Fn.cosine_similarity(y.float().flatten(), ref.float().flatten(), dim=0).item()
     assert cos > 0.995, cos
+
+
+@pytest.mark.parametrize("t,n,k", [(5, 384, 256), (32, 1024, 512), (77, 256, 192)])
+def test_dense_bf16_linear(cuda, t, n, k):
+    """kind::f16 weight-streaming GEMM (tokens as N) against an fp32 matmul of the same bf16 values."""
+    from inference_optimizations_b200.ops.linear import DenseLinear
+    torch.manual_seed(t)
+    w = (torch.randn(n, k, device=cuda) * 0.05).to(torch.bfloat16)
+    x = torch.randn(t, k, device=cuda).to(torch.bfloat16)
+    lin = DenseLinear(w)
+    y = lin(x)
+    torch.cuda.synchronize()
+    assert lin.status.item() == 0
+    ref = x.float() @ w.float().T
+    err = (y.float() - ref).abs() / (ref.abs() + 1e-2 * ref.abs().max())
+    assert err.max().item() < 1e-2, err.max().item()
