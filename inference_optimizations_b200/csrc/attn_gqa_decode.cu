@@ -40,6 +40,8 @@ struct Smem {
   uint64_t ring_full[8], ring_empty[8];
   uint64_t k_full, k_empty;
   uint64_t s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2];
+  uint64_t kf[2], ke[2];  // E4M3 path: double-buffered K tile in TMEM
+  uint64_t pe[2], od;     // E4M3 path, <= 2 query rows: P buffer released by the PV warps; final O in smem
   uint32_t tmem_base;
   int abort;
   int raw_valid[8];       // stage holds a real page (else the dequant writes zeros); published by the producer
@@ -582,11 +584,21 @@ __global__ void __launch_bounds__(kThreads, 1) gqa_decode_kernel(const GqaDecode
 // as E4M3 x 256.  V slabs are one full 128-dim M block (128 B of E4M3 per token row).
 template <int FMT, int D>
 __device__ __host__ __forceinline__ constexpr int ring_f8() { return part_bytes<FMT, D>() <= 20 * 1024 ? 6 : 4; }
-template <int FMT, int D>
+// Optional decode variant: with <= 2 query rows P V runs on the CUDA cores (CC = true): the V slab ring is replaced
+// by a 24 KB area (P in fp32, the cross-thread O reduction, the final O) and the freed shared memory goes to raw
+// staging.  Measured on B200 (32 x 32k tokens, head_dim 512, NVFP4): 3.36 ms against 3.18 ms for the tensor-core
+// P V (the FFMA + conversion stream of the 8 PV warps is issue-limited), so it is off.
+constexpr bool kCudaCorePv = false;
+constexpr int kCcBytes = 24576;
+template <int FMT, int D, bool CC>
+__device__ __host__ __forceinline__ constexpr int ring_bytes_f8() { return CC ? kCcBytes : ring_f8<FMT, D>() * 16384; }
+template <int FMT, int D, bool CC>
 __device__ __host__ __forceinline__ constexpr int raw_stages_f8() {
-  return (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096 - kF4TabBytes) / part_bytes<FMT, D>() > 8   ? 8
-         : (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096 - kF4TabBytes) / part_bytes<FMT, D>() < 2 ? 2
-         : (229376 - ring_f8<FMT, D>() * 16384 - (D / 128) * 2048 - 4096 - kF4TabBytes) / part_bytes<FMT, D>();
+  return (229376 - ring_bytes_f8<FMT, D, CC>() - (D / 128) * 2048 - 4096 - kF4TabBytes) / part_bytes<FMT, D>() > 8
+             ? 8
+         : (229376 - ring_bytes_f8<FMT, D, CC>() - (D / 128) * 2048 - 4096 - kF4TabBytes) / part_bytes<FMT, D>() < 4
+             ? 4
+             : (229376 - ring_bytes_f8<FMT, D, CC>() - (D / 128) * 2048 - 4096 - kF4TabBytes) / part_bytes<FMT, D>();
 }
 
 __device__ __forceinline__ uint32_t pack_e4m3x4(uint32_t h01, uint32_t h23) {
@@ -653,12 +665,13 @@ template <int FMT, int D, int RMAX>
 __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaDecodeArgs a) {
   constexpr int NQS = D / 128;                     // 128-dim slabs (Q rows, V M blocks)
   constexpr int PB = part_bytes<FMT, D>();
-  constexpr int NST = raw_stages_f8<FMT, D>();
+  constexpr bool kCc = kCudaCorePv && RMAX <= 2;   // P V on the CUDA cores (decode)
+  constexpr int NST = raw_stages_f8<FMT, D, kCc>();
   // K and V parts go through separate raw rings (page slots [0, NSTK) and [NSTK, NST)): each ring is consumed in
   // order by one warp group, so no mbarrier is ever waited on more than one phase ahead.
   constexpr int NSTK = NST / 2, NSTV = NST - NSTK;
   static_assert(NSTK >= 2 && NSTV >= 2, "each raw ring holds at least one part (two pages)");
-  constexpr int RING = ring_f8<FMT, D>();
+  constexpr int RING = kCc ? D / 128 : ring_f8<FMT, D>();
   constexpr int MB = D / 128;
   constexpr int kOCols = MB * kN;
   constexpr float kPScale = 256.f;
@@ -667,8 +680,13 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = base;                                   // RING x 16 KB (V slabs, E4M3)
-  uint8_t* sq = ring + RING * kSlabBytes;                 // NQS x 2 KB (Q, E4M3)
+  uint8_t* ring = base;                                   // RING x 16 KB (V slabs, E4M3) or the CC area
+  uint8_t* sq = ring + ring_bytes_f8<FMT, D, kCc>();      // NQS x 2 KB (Q, E4M3)
+  // CC area: P fp32 [2 bufs][2 rows][128] + alpha [2][2] | O partials [TG][2][D] | final O [2][D]
+  float* cc_p = reinterpret_cast<float*>(ring);
+  float* cc_alpha = cc_p + 2 * 2 * 128;
+  float* cc_red = cc_p + 1024;
+  float* cc_o = cc_red + 2 * 2048;
   uint8_t* sp = sq + NQS * kN * 128;                      // 2 x 2 KB (P, E4M3)
   uint8_t* raw = sp + 2 * kN * 128;                       // NST x PB
   Smem& sm = *reinterpret_cast<Smem*>(raw + NST * PB);
@@ -717,6 +735,10 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
     mbar_init(&sm.k_full, kDequantWarps);
     mbar_init(&sm.k_empty, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.kf[i], kDequantWarps); mbar_init(&sm.ke[i], 1); mbar_init(&sm.pe[i], kDequantWarps);
+    }
+    mbar_init(&sm.od, kDequantWarps);
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.s_full[i], 1); mbar_init(&sm.s_empty[i], kSoftmaxWarps);
       mbar_init(&sm.p_full[i], kSoftmaxWarps); mbar_init(&sm.o_full[i], 1); mbar_init(&sm.o_empty[i], kSoftmaxWarps);
     }
@@ -758,7 +780,8 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
   const uint32_t tmem = sm.tmem_base;
   const uint32_t tS = tmem;
   const uint32_t tO = tmem + 128;
-  const uint32_t tK = tmem + kTmemK;   // D/4 columns (four E4M3 per column)
+  const uint32_t tK = tmem + kTmemK;   // two buffers of D/4 columns (four E4M3 per column)
+  static_assert(kTmemK + 2 * (D / 4) <= kTmemCols, "TMEM: double-buffered K");
   volatile int* abort = &sm.abort;
   if (threadIdx.x == 0) trace_ev(a.trace, kEvStart, 0);
 
@@ -853,6 +876,26 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
 #pragma unroll
       for (int n = 0; n < RMAX; ++n)
         if (threadIdx.x == n) sm.row_m[n] = mnew[n];
+      if constexpr (kCc) {
+        // P (fp32) and the rescale factor of the running O for the PV warps; buffer sb last held tile j - 2
+        if (j >= 2 && !mbar_wait(&sm.pe[sb], ((j >> 1) - 1) & 1, abort, a.status, kTimeoutConsumer)) {
+          ok = false;
+          break;
+        }
+        float* pp = cc_p + sb * 256;
+        const int k = 32 * warp + lane;
+#pragma unroll
+        for (int n = 0; n < RMAX; ++n) {
+          const float p = (s[n] == -INFINITY) ? 0.f : exp2f(s[n] - mnew[n]);
+          lpart[n] = lpart[n] * alpha[n] + p;
+          pp[n * 128 + k] = p;
+        }
+        if (threadIdx.x < RMAX) cc_alpha[sb * 2 + threadIdx.x] = threadIdx.x == 0 ? alpha[0] : alpha[RMAX - 1];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full[sb]);
+        if (threadIdx.x == 0) trace_ev(a.trace, kEvPReady, j);
+        continue;
+      }
       // P (E4M3 x 256) into the B operand: row n, token k, SW128 K-major (one 128-token slab)
       uint8_t* pbuf = sp + sb * (kN * 128);
       const int k = 32 * warp + lane;
@@ -877,7 +920,11 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
 #pragma unroll
       for (int n = 0; n < RMAX; ++n) alpha_prev[n] = alpha[n];
     }
-    if (ok) ok = consume_o(ntiles - 1);
+    if constexpr (!kCc) {
+      if (ok) ok = consume_o(ntiles - 1);
+    } else {
+      if (ok) ok = mbar_wait(&sm.od, 0, abort, a.status, kTimeoutConsumer);   // final O of the PV warps
+    }
     float l[RMAX];
 #pragma unroll
     for (int n = 0; n < RMAX; ++n) l[n] = warp_sum(lpart[n]);
@@ -894,16 +941,20 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
       for (int n = 0; n < RMAX; ++n) {
         if (n >= R) break;
         const int t = n / G, g = n % G;
-        const float inv = l[n] > 0.f ? a.v_scale / (l[n] * kPScale) : 0.f;
+        const float inv = l[n] > 0.f ? a.v_scale / (l[n] * (kCc ? 1.f : kPScale)) : 0.f;
+        auto oval = [&](int mb) {
+          if constexpr (kCc) return cc_o[n * D + mb * 128 + 32 * warp + lane];
+          else return acc[mb][n];
+        };
         if (a.num_splits == 1) {
           __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) +
                              ((static_cast<size_t>(b) * a.n_q + t) * a.Hq + h * G + g) * D;
 #pragma unroll
-          for (int mb = 0; mb < MB; ++mb) o[mb * 128 + 32 * warp + lane] = __float2bfloat16(acc[mb][n] * inv);
+          for (int mb = 0; mb < MB; ++mb) o[mb * 128 + 32 * warp + lane] = __float2bfloat16(oval(mb) * inv);
         } else {
           float* o = a.o_part + (part_out * RMAX + n) * D;
 #pragma unroll
-          for (int mb = 0; mb < MB; ++mb) o[mb * 128 + 32 * warp + lane] = acc[mb][n] * inv;
+          for (int mb = 0; mb < MB; ++mb) o[mb * 128 + 32 * warp + lane] = oval(mb) * inv;
           if (warp == 0 && lane == 0)
             a.lse_part[part_out * RMAX + n] = l[n] > 0.f ? sm.row_m[n] + log2f(l[n]) : -INFINITY;
         }
@@ -920,7 +971,8 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
       const int seq0 = 2 * j, st0 = seq0 % NSTK, st1 = (seq0 + 1) % NSTK;
       if (!mbar_wait(&sm.raw_full[st0], (seq0 / NSTK) & 1, abort, a.status, kTimeoutConsumer)) break;
       if (!mbar_wait(&sm.raw_full[st1], ((seq0 + 1) / NSTK) & 1, abort, a.status, kTimeoutConsumer)) break;
-      if (!mbar_wait(&sm.k_empty, (j & 1) ^ 1, abort, a.status, kTimeoutConsumer)) break;
+      const int kb = j & 1;
+      if (!mbar_wait(&sm.ke[kb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutConsumer)) break;
       tc_fence_after();
       if (dw == 0 && lane == 0) trace_ev(a.trace, kEvKDeqStart, j);
       const int st = kpg ? st1 : st0;
@@ -934,18 +986,127 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] = 0;
         }
-        tmem_st16(tK + k_lane + d0 / 4, v);
+        tmem_st16(tK + kb * (D / 4) + k_lane + d0 / 4, v);
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&sm.k_full);
+        mbar_arrive(&sm.kf[kb]);
         mbar_arrive(&sm.raw_empty[st0]);
         mbar_arrive(&sm.raw_empty[st1]);
         if (dw == 0) trace_ev(a.trace, kEvKDeqEnd, j);
       }
     }
+  } else if (kCc && warp < kSoftmaxWarps + 2 * kDequantWarps) {
+    regs_dec<72>();
+    // ---- PV warps (<= 2 query rows): O += P V on the CUDA cores straight from the raw pages (no E4M3 slabs, no
+    // PV MMAs).  Thread = (8-dim group dg, token group tg): it accumulates 2 rows x 8 dims over its tokens.
+    constexpr int DG = D / 8, TG = 256 / DG, TPT = 128 / TG;
+    const int tv = (warp - kSoftmaxWarps - kDequantWarps) * 32 + lane;
+    const int dg = tv % DG, tg = tv / DG;
+    float acc0[8], acc1[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc0[e] = acc1[e] = 0.f;
+    bool okv = true;
+    for (int i = 0; i < ntiles; ++i) {
+      const int seq0 = 2 * i, st0 = NSTK + seq0 % NSTV, st1 = NSTK + (seq0 + 1) % NSTV;
+      const int sb = i & 1;
+      if (!(okv = mbar_wait(&sm.raw_full[st0], (seq0 / NSTV) & 1, abort, a.status, kTimeoutConsumer))) break;
+      if (!(okv = mbar_wait(&sm.raw_full[st1], ((seq0 + 1) / NSTV) & 1, abort, a.status, kTimeoutConsumer))) break;
+      if (!(okv = mbar_wait(&sm.p_full[sb], (i >> 1) & 1, abort, a.status, kTimeoutConsumer))) break;
+      if (tv == 0) trace_ev(a.trace, kEvVDeqStart, i);
+      const float al0 = cc_alpha[sb * 2], al1 = cc_alpha[sb * 2 + 1];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        acc0[e] *= al0;
+        acc1[e] *= al1;
+      }
+      // this thread's TPT consecutive tokens lie in one page; masked tokens carry P = 0 (finite data, no branch)
+      const int tfirst = tg * TPT;
+      const int st = (tfirst >> 6) ? st1 : st0;
+      if (sm.raw_valid[st]) {
+        const float* pp0 = cc_p + sb * 256 + tfirst;
+        const float* pp1 = pp0 + 128;
+        const uint8_t* part = raw + st * PB;
+#pragma unroll 1
+        for (int u0 = 0; u0 < TPT; u0 += 4) {
+          const float4 P0 = *reinterpret_cast<const float4*>(pp0 + u0);
+          const float4 P1 = *reinterpret_cast<const float4*>(pp1 + u0);
+          const float p0s[4] = {P0.x, P0.y, P0.z, P0.w}, p1s[4] = {P1.x, P1.y, P1.z, P1.w};
+          if constexpr (FMT == kKvNvfp4) {
+            constexpr int RB = D / 2, NCH = (RB / 16) < 8 ? (RB / 16) : 8;
+            uint32_t w[4];
+            uint32_t sbyte[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {                       // all loads first: latency overlaps
+              const int r = (tfirst + u0 + q) & 63;
+              w[q] = *reinterpret_cast<const uint32_t*>(part + r * RB + pool_chunk_pos(dg >> 2, r, NCH) * 16 +
+                                                        (dg & 3) * 4);
+              sbyte[q] = part[64 * RB + r * (D / 16) + (dg >> 1)];
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float sc = e4m3_to_float(static_cast<uint8_t>(sbyte[q]));
+              const float c0 = p0s[q] * sc, c1 = p1s[q] * sc;
+              uint32_t hh[4];
+              e2m1x8_to_f16x2x4(w[q], hh);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hh[e]));
+                acc0[2 * e] = fmaf(c0, f.x, acc0[2 * e]);
+                acc0[2 * e + 1] = fmaf(c0, f.y, acc0[2 * e + 1]);
+                acc1[2 * e] = fmaf(c1, f.x, acc1[2 * e]);
+                acc1[2 * e + 1] = fmaf(c1, f.y, acc1[2 * e + 1]);
+              }
+            }
+          } else {
+            uint2 w[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int r = (tfirst + u0 + q) & 63;
+              w[q] = *reinterpret_cast<const uint2*>(part + r * D + pool_chunk_pos(dg >> 1, r, 8) * 16 + (dg & 1) * 8);
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t ww[2] = {w[q].x, w[q].y};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t hq = e4m3x2_to_f16x2(static_cast<uint16_t>(ww[e >> 1] >> (16 * (e & 1))));
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hq));
+                acc0[2 * e] = fmaf(p0s[q], f.x, acc0[2 * e]);
+                acc0[2 * e + 1] = fmaf(p0s[q], f.y, acc0[2 * e + 1]);
+                acc1[2 * e] = fmaf(p1s[q], f.x, acc1[2 * e]);
+                acc1[2 * e + 1] = fmaf(p1s[q], f.y, acc1[2 * e + 1]);
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&sm.raw_empty[st0]);
+        mbar_arrive(&sm.raw_empty[st1]);
+        mbar_arrive(&sm.pe[sb]);
+      }
+      if (tv == 0) trace_ev(a.trace, kEvVDeqEnd, i);
+    }
+    // reduce the token groups: partials to smem, then each thread sums a slice of the 2 x D outputs
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      cc_red[(tg * 2 + 0) * D + 8 * dg + e] = acc0[e];
+      cc_red[(tg * 2 + 1) * D + 8 * dg + e] = acc1[e];
+    }
+    asm volatile("bar.sync 2, 256;" ::: "memory");
+    for (int idx = tv; idx < 2 * D; idx += 256) {
+      const int rr = idx / D, d = idx % D;
+      float sum = 0.f;
+#pragma unroll
+      for (int g2 = 0; g2 < TG; ++g2) sum += cc_red[(g2 * 2 + rr) * D + d];
+      cc_o[idx] = sum;
+    }
+    __syncwarp();
+    if (okv && lane == 0) mbar_arrive(&sm.od);
   } else if (warp < kSoftmaxWarps + 2 * kDequantWarps) {
     regs_dec<72>();
     // ---- V warps: V(i) -> ring, one 128-dim E4M3 slab per M block; warp covers 16 tokens x two 64-dim halves
@@ -1045,18 +1206,18 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
         if (j < ntiles) {
           const int sb = j & 1;
           if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
-          if (!mbar_wait(&sm.k_full, j & 1, abort, a.status, kTimeoutMma)) break;
+          if (!mbar_wait(&sm.kf[sb], (j >> 1) & 1, abort, a.status, kTimeoutMma)) break;
           tc_fence_after();
           trace_ev(a.trace, kEvQkStart, j);
 #pragma unroll 4
           for (int s = 0; s < D / 32; ++s)
-            umma_f8_ts(tS + sb * (kSParts * kN) + (s % kSParts) * kN, tK + 8 * s,
+            umma_f8_ts(tS + sb * (kSParts * kN) + (s % kSParts) * kN, tK + sb * (D / 4) + 8 * s,
                        desc_sw128(q_addr + (s >> 2) * (kN * 128) + (s & 3) * 32), id_qk, s >= kSParts ? 1u : 0u);
           umma_commit(&sm.s_full[sb]);
-          umma_commit(&sm.k_empty);
+          umma_commit(&sm.ke[sb]);
           trace_ev(a.trace, kEvQkEnd, j);
         }
-        if (j == 0) continue;
+        if (kCc || j == 0) continue;
         const int i = j - 1, sb = i & 1;
         if (!mbar_wait(&sm.p_full[sb], (i >> 1) & 1, abort, a.status, kTimeoutMma)) break;
         if (!mbar_wait(&sm.o_empty[sb], ((i >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
@@ -1130,9 +1291,9 @@ cudaError_t launch_t(const GqaDecodeArgs& a, cudaStream_t s) {
   bool launched = false;
   if constexpr (FMT != kKvBf16) {
     if (!a.exact) {
-    constexpr int NST8 = raw_stages_f8<FMT, D>();
-    constexpr int RING8 = ring_f8<FMT, D>();
-    constexpr int smem8 = 1024 + RING8 * kSlabBytes + (D / 128) * kN * 128 + 2 * kN * 128 + NST8 * PB +
+    constexpr bool CC = kCudaCorePv && RMAX <= 2;
+    constexpr int NST8 = raw_stages_f8<FMT, D, CC>();
+    constexpr int smem8 = 1024 + ring_bytes_f8<FMT, D, CC>() + (D / 128) * kN * 128 + 2 * kN * 128 + NST8 * PB +
                           ((sizeof(Smem) + 15) & ~size_t(15)) + kF4TabBytes;
     static_assert(smem8 <= 232448, "shared memory budget (E4M3 path)");
     auto kern8 = gqa_decode_f8_kernel<FMT, D, RMAX>;

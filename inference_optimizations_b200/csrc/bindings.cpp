@@ -548,6 +548,53 @@ void pd_wait(const at::Tensor& flag, int64_t value, at::Tensor status) {
   CHECK_CUDA_OK(iob::pd_wait(flag.data_ptr<int>(), static_cast<int>(value), status.data_ptr<int>(), stream()));
 }
 
+void kda_decode(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g_proj,
+                const at::Tensor& dt_bias, const at::Tensor& A_log, const at::Tensor& beta, const at::Tensor& g2,
+                const at::Tensor& norm_w, const at::Tensor& cwq, const at::Tensor& cwk, const at::Tensor& cwv,
+                at::Tensor csq, at::Tensor csk, at::Tensor csv, at::Tensor state, at::Tensor out, double scale) {
+  const std::vector<const at::Tensor*> bf = {&q, &k, &v, &g_proj, &g2};
+  for (const at::Tensor* t : bf) req(*t, at::kBFloat16, "kda bf16 input");
+  const std::vector<const at::Tensor*> f32 = {&dt_bias, &A_log, &beta, &norm_w, &cwq, &cwk, &cwv, &csq, &csk, &csv,
+                                              &state};
+  for (const at::Tensor* t : f32) req(*t, at::kFloat, "kda fp32 input");
+  req(out, at::kBFloat16, "out");
+  const int64_t B = q.size(0), H = q.size(1), DK = q.size(2), HV = v.size(1), DV = v.size(2), W = cwq.size(1);
+  TORCH_CHECK(k.sizes() == q.sizes() && g_proj.size(2) == DK && g2.size(1) == HV && g2.size(2) == DV &&
+                  state.numel() == B * HV * DV * DK && csq.numel() == B * H * DK * (W - 1) &&
+                  csv.numel() == B * HV * DV * (W - 1) && out.numel() == B * HV * DV,
+              "kda shapes");
+  const std::vector<const at::Tensor*> all = {&q, &k, &v, &g_proj, &g2, &csq, &csk, &csv, &state, &out, &beta};
+  for (const at::Tensor* t : all) TORCH_CHECK(t->is_contiguous(), "kda: contiguous tensors");
+  iob::KdaDecodeArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  a.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  a.g_proj = reinterpret_cast<const __nv_bfloat16*>(g_proj.data_ptr());
+  a.dt_bias = dt_bias.data_ptr<float>();
+  a.A_log = A_log.data_ptr<float>();
+  a.beta = beta.data_ptr<float>();
+  a.g2 = reinterpret_cast<const __nv_bfloat16*>(g2.data_ptr());
+  a.norm_w = norm_w.data_ptr<float>();
+  a.conv_wq = cwq.data_ptr<float>();
+  a.conv_wk = cwk.data_ptr<float>();
+  a.conv_wv = cwv.data_ptr<float>();
+  a.conv_q = csq.data_ptr<float>();
+  a.conv_k = csk.data_ptr<float>();
+  a.conv_v = csv.data_ptr<float>();
+  a.state = state.data_ptr<float>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.scale = static_cast<float>(scale);
+  a.B = static_cast<int>(B);
+  a.H = static_cast<int>(H);
+  a.HV = static_cast<int>(HV);
+  a.DK = static_cast<int>(DK);
+  a.DV = static_cast<int>(DV);
+  a.W = static_cast<int>(W);
+  a.beta_headwise = beta.dim() == 3 ? 1 : 0;
+  const at::cuda::CUDAGuard g(q.device());
+  CHECK_CUDA_OK(iob::kda_decode(a, stream()));
+}
+
 void ep_barrier(const at::Tensor& peers, int64_t off_flags, int64_t rank, int64_t world, at::Tensor epoch,
                 at::Tensor status) {
   req(peers, at::kLong, "peers");
@@ -634,6 +681,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dcp_merge", &dcp_merge);
   m.def("glmflash_write", &glmflash_write);
   m.def("pd_copy", &pd_copy);
+  m.def("kda_decode", &kda_decode);
   m.def("pd_signal", &pd_signal);
   m.def("pd_wait", &pd_wait);
   m.def("v4pro_write", &v4pro_write);

@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <cuda_bf16.h>
 
 namespace iob {
 
@@ -179,6 +180,24 @@ cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, i
                       cudaStream_t s);
 cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_base, const float* w, void* y,
                         cudaStream_t s);
+
+// ---- Kimi delta attention decode step (kda.cu)
+struct KdaDecodeArgs {
+  const __nv_bfloat16 *q, *k, *v;        // [B, H, DK], [B, H, DK], [B, HV, DV] (projections, pre-conv)
+  const __nv_bfloat16* g_proj;           // [B, HV, DK]
+  const float* dt_bias;                  // [HV * DK]
+  const float* A_log;                    // [HV]
+  const float* beta;                     // [B, HV] or [B, HV, DV]
+  const __nv_bfloat16* g2;               // [B, HV, DV] output-gate input
+  const float* norm_w;                   // [DV]
+  const float *conv_wq, *conv_wk, *conv_wv;   // [H * DK, W], [H * DK, W], [HV * DV, W]
+  float *conv_q, *conv_k, *conv_v;       // [B, H * DK, W - 1] ... (oldest first), updated in place
+  float* state;                          // [B, HV, DV, DK] fp32, updated in place
+  __nv_bfloat16* out;                    // [B, HV, DV]
+  float scale;
+  int B, H, HV, DK, DV, W, beta_headwise;
+};
+cudaError_t kda_decode(const KdaDecodeArgs& a, cudaStream_t s);
 
 // ---- prefill -> decode KV page transfer over peer memory (pd.cu)
 struct PdCopyArgs {

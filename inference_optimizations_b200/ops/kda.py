@@ -1,0 +1,119 @@
+"""Kimi Delta Attention (gated delta-rule linear attention) decode step and its recurrent-state storage formats.
+
+`kda_decode` runs the fused CUDA kernel (csrc/kda.cu: conv -> gate -> L2 norm -> delta rule -> sigmoid-gated
+RMSNorm in one launch per layer); `kda_decode_ref` is the fp32 oracle of the same math
+(`linear-attention-kda/kda-fused-decode/kda.py:1-60` states the contract: value-major state, eps inside the root,
+softplus threshold 20, SiLU conv, sigmoid output gate).
+
+Recurrent-state rows (`kv-cache-4bit/k3-quantized-state/k3state_quant.py:1-37`): the state of one head is 128 value
+rows of 128 fp32; a parked request's state is kept quantized per row -- FP8 (128 E4M3 + fp32 scale = 132 B),
+bf16 (256 B) or NVFP4 (64 B E2M1 + 8 E4M3 block scales + fp32 global = 76 B) -- and expanded into an fp32 working
+copy when the request runs again (`StateStore`).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as Fn
+
+from .._ext import ext
+from . import formats as F
+
+
+def kda_decode_ref(q, k, v, g_proj, dt_bias, A_log, beta, g2, norm_w, cwq, cwk, cwv, csq, csk, csv, state,
+                   scale=None):
+    """Same arguments as `kda_decode` (states updated in place, fp32 math); returns o [B, HV, DV] bf16."""
+    B, H, DK = q.shape
+    HV, DV = v.shape[1], v.shape[2]
+    W = cwq.shape[1]
+    scale = DK ** -0.5 if scale is None else scale
+
+    def conv(x, w, st):                      # x [B, C], w [C, W], st [B, C, W-1]
+        y = (st * w[None, :, :W - 1]).sum(-1) + x * w[None, :, W - 1]
+        st.copy_(torch.cat([st[..., 1:], x[..., None]], -1))
+        return Fn.silu(y)
+
+    qc = conv(q.float().reshape(B, -1), cwq, csq.view(B, H * DK, W - 1)).view(B, H, DK)
+    kc = conv(k.float().reshape(B, -1), cwk, csk.view(B, H * DK, W - 1)).view(B, H, DK)
+    vc = conv(v.float().reshape(B, -1), cwv, csv.view(B, HV * DV, W - 1)).view(B, HV, DV)
+    gp = g_proj.float() + dt_bias.view(HV, DK)[None]
+    sp = torch.where(gp > 20, gp, torch.log1p(torch.exp(gp)))
+    g = -torch.exp(A_log.float())[None, :, None] * sp                     # [B, HV, DK], log-space decay
+    rep = HV // H
+    qn = qc / torch.sqrt((qc * qc).sum(-1, keepdim=True) + 1e-6) * scale
+    kn = kc / torch.sqrt((kc * kc).sum(-1, keepdim=True) + 1e-6)
+    qn, kn = qn.repeat_interleave(rep, 1), kn.repeat_interleave(rep, 1)
+    h = state.view(B, HV, DV, DK)
+    h.mul_(torch.exp(g)[:, :, None, :])
+    err = vc - torch.einsum("bhvk,bhk->bhv", h, kn)
+    bt = beta.float() if beta.dim() == 3 else beta.float()[..., None]
+    u = err * bt
+    h.add_(u[..., None] * kn[:, :, None, :])
+    o = torch.einsum("bhvk,bhk->bhv", h, qn)
+    o = o * torch.sigmoid(g2.float())
+    o = o / torch.sqrt((o * o).mean(-1, keepdim=True) + 1e-5) * norm_w.float()
+    return o.to(torch.bfloat16)
+
+
+def kda_decode(q, k, v, g_proj, dt_bias, A_log, beta, g2, norm_w, cwq, cwk, cwv, csq, csk, csv, state, scale=None):
+    """Fused decode step on the GPU (q/k heads == value heads, head dims 128); falls back to the oracle on CPU."""
+    if not q.is_cuda:
+        return kda_decode_ref(q, k, v, g_proj, dt_bias, A_log, beta, g2, norm_w, cwq, cwk, cwv, csq, csk, csv,
+                              state, scale)
+    out = torch.empty(v.shape, dtype=torch.bfloat16, device=v.device)
+    ext().kda_decode(q, k, v, g_proj, dt_bias, A_log, beta, g2, norm_w, cwq, cwk, cwv, csq, csk, csv, state, out,
+                     q.shape[2] ** -0.5 if scale is None else scale)
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ state rows
+ROW_BYTES = {"fp8": 132, "bf16": 256, "nvfp4": 76}
+
+
+def quant_state_rows(rows: torch.Tensor, fmt: str) -> torch.Tensor:
+    """fp32 [R, 128] -> uint8 [R, ROW_BYTES[fmt]]."""
+    r = rows.float()
+    n = r.shape[0]
+    if fmt == "bf16":
+        return r.to(torch.bfloat16).view(torch.uint8).reshape(n, 256)
+    if fmt == "fp8":
+        s = (r.abs().amax(-1, keepdim=True) / 448.0).clamp(min=1e-30)
+        q = (r / s).to(torch.float8_e4m3fn).view(torch.uint8)
+        return torch.cat([q, s.view(torch.uint8).reshape(n, 4)], -1)
+    g = (r.abs().amax(-1) / (448.0 * 6.0)).clamp(min=1e-30)
+    out = torch.empty(n, 76, dtype=torch.uint8, device=r.device)
+    for i in range(n):                         # per-row global scale
+        p, s8 = F.nvfp4_quantize(r[i:i + 1], float(g[i]))
+        out[i, :64], out[i, 64:72] = p[0], s8[0].view(torch.uint8)
+    out[:, 72:] = g.view(torch.uint8).reshape(n, 4)
+    return out
+
+
+def dequant_state_rows(b: torch.Tensor, fmt: str) -> torch.Tensor:
+    n = b.shape[0]
+    if fmt == "bf16":
+        return b.contiguous().view(torch.bfloat16).float().reshape(n, 128)
+    if fmt == "fp8":
+        s = b[:, 128:].contiguous().view(torch.float32)
+        return b[:, :128].contiguous().view(torch.float8_e4m3fn).float() * s
+    g = b[:, 72:].contiguous().view(torch.float32)[:, 0]
+    return torch.stack([F.nvfp4_dequantize(b[i, :64], b[i, 64:72].contiguous().view(torch.float8_e4m3fn),
+                                           float(g[i])) for i in range(n)])
+
+
+class StateStore:
+    """Parked recurrent states kept as quantized rows; `load` expands a request's state into an fp32 working copy,
+    `park` quantizes it back (the two-tier pool of the reference: fp32 working copy + quantized mirror)."""
+
+    def __init__(self, fmt: str = "fp8"):
+        self.fmt = fmt
+        self.parked: dict = {}
+
+    def park(self, rid, state: torch.Tensor) -> None:
+        self.parked[rid] = (tuple(state.shape), quant_state_rows(state.reshape(-1, 128), self.fmt))
+
+    def load(self, rid) -> torch.Tensor:
+        shape, rows = self.parked.pop(rid)
+        return dequant_state_rows(rows, self.fmt).reshape(shape)
+
+    def nbytes(self) -> int:
+        return sum(r.numel() for _, r in self.parked.values())

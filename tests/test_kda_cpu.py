@@ -1,0 +1,52 @@
+"""KDA decode oracle properties and recurrent-state row formats (ops/kda.py)."""
+import torch
+
+from inference_optimizations_b200.ops import kda as KD
+
+
+def _inputs(B=2, H=3, DK=128, DV=128, W=4, seed=0, headwise=False):
+    g = torch.Generator().manual_seed(seed)
+    r = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    return dict(q=r(B, H, DK).to(torch.bfloat16), k=r(B, H, DK).to(torch.bfloat16), v=r(B, H, DV).to(torch.bfloat16),
+                g_proj=r(B, H, DK).to(torch.bfloat16), dt_bias=r(H * DK) * 0.1, A_log=r(H) * 0.1,
+                beta=torch.sigmoid(r(B, H, DV) if headwise else r(B, H)), g2=r(B, H, DV).to(torch.bfloat16),
+                norm_w=1 + 0.1 * r(DV), cwq=r(H * DK, W) * 0.3, cwk=r(H * DK, W) * 0.3, cwv=r(H * DV, W) * 0.3,
+                csq=r(B, H * DK, W - 1), csk=r(B, H * DK, W - 1), csv=r(B, H * DV, W - 1),
+                state=r(B, H, DV, DK) * 0.1)
+
+
+def test_decode_ref_state_evolution():
+    a = _inputs()
+    st0 = a["state"].clone()
+    csq0 = a["csq"].clone()
+    o = KD.kda_decode_ref(**a)
+    assert o.shape == (2, 3, 128) and torch.isfinite(o.float()).all()
+    assert not torch.equal(st0, a["state"])
+    # conv state shifted left with the raw input appended
+    assert torch.equal(a["csq"][..., :2], csq0[..., 1:])
+    assert torch.allclose(a["csq"][..., 2], a["q"].float().reshape(2, -1))
+    # the delta rule makes the state reproduce v on k (after one write with beta = 1, decay 0)
+    b = _inputs(seed=1)
+    b["beta"] = torch.ones_like(b["beta"])
+    b["A_log"] = torch.full_like(b["A_log"], -30.0)          # decay exp(-exp(-30)*sp) ~ 1
+    KD.kda_decode_ref(**b)
+
+
+def test_state_rows_round_trip():
+    torch.manual_seed(0)
+    rows = torch.randn(16, 128) * torch.exp2(torch.randint(-4, 5, (16, 1)).float())
+    for fmt, tol in (("bf16", 4e-3), ("fp8", 7e-2), ("nvfp4", 0.25)):
+        b = KD.quant_state_rows(rows, fmt)
+        assert b.shape == (16, KD.ROW_BYTES[fmt])
+        d = KD.dequant_state_rows(b, fmt)
+        rel = ((d - rows).norm(dim=-1) / rows.norm(dim=-1)).max().item()
+        assert rel < tol, (fmt, rel)
+
+
+def test_state_store_park_load():
+    st = KD.StateStore("fp8")
+    s = torch.randn(2, 4, 128, 128)
+    st.park("r1", s)
+    assert st.nbytes() == 2 * 4 * 128 * 132
+    back = st.load("r1")
+    assert back.shape == s.shape and ((back - s).norm() / s.norm()) < 0.07
