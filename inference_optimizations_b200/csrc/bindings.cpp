@@ -595,6 +595,37 @@ void kda_decode(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, c
   CHECK_CUDA_OK(iob::kda_decode(a, stream()));
 }
 
+void qar_allreduce(const at::Tensor& peers, const std::vector<int64_t>& offs, const at::Tensor& x, at::Tensor y,
+                   int64_t T_max, int64_t rank, int64_t nranks, at::Tensor epoch, at::Tensor status) {
+  req(peers, at::kLong, "peers");
+  req(x, at::kBFloat16, "x");
+  req(y, at::kBFloat16, "y");
+  req(epoch, at::kInt, "epoch");
+  req(status, at::kInt, "status");
+  TORCH_CHECK(offs.size() == 5 && x.dim() == 2 && x.is_contiguous() && y.sizes() == x.sizes() && y.is_contiguous(),
+              "qar shapes");
+  iob::QarArgs a{};
+  a.peers = reinterpret_cast<const long long*>(peers.data_ptr<int64_t>());
+  a.off_recv_q = offs[0];
+  a.off_recv_s = offs[1];
+  a.off_gather_q = offs[2];
+  a.off_gather_s = offs[3];
+  a.off_flags = offs[4];
+  a.x = x.data_ptr();
+  a.y = y.data_ptr();
+  a.epoch = epoch.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  a.T = static_cast<int>(x.size(0));
+  a.T_max = static_cast<int>(T_max);
+  a.H = static_cast<int>(x.size(1));
+  a.G = a.H / 128;
+  a.nranks = static_cast<int>(nranks);
+  a.per = (a.G + a.nranks - 1) / a.nranks;
+  a.rank = static_cast<int>(rank);
+  const at::cuda::CUDAGuard g(x.device());
+  CHECK_CUDA_OK(iob::qar_allreduce(a, stream()));
+}
+
 void ep_barrier(const at::Tensor& peers, int64_t off_flags, int64_t rank, int64_t world, at::Tensor epoch,
                 at::Tensor status) {
   req(peers, at::kLong, "peers");
@@ -682,6 +713,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("glmflash_write", &glmflash_write);
   m.def("pd_copy", &pd_copy);
   m.def("kda_decode", &kda_decode);
+  m.def("qar_allreduce", &qar_allreduce);
   m.def("pd_signal", &pd_signal);
   m.def("pd_wait", &pd_wait);
   m.def("v4pro_write", &v4pro_write);

@@ -181,6 +181,18 @@ cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, i
 cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_base, const float* w, void* y,
                         cudaStream_t s);
 
+// ---- FP8-quantized two-shot all-reduce over peer memory (qar.cu)
+struct QarArgs {
+  const long long* peers;      // [nranks] symmetric buffer bases
+  long long off_recv_q, off_recv_s, off_gather_q, off_gather_s, off_flags;
+  const void* x;               // bf16 [T, H] this rank's addend
+  void* y;                     // bf16 [T, H] sum (identical on every rank)
+  int* epoch;                  // device [1]
+  int* status;
+  int T, T_max, H, G, per, rank, nranks;
+};
+cudaError_t qar_allreduce(const QarArgs& a, cudaStream_t s);
+
 // ---- Kimi delta attention decode step (kda.cu)
 struct KdaDecodeArgs {
   const __nv_bfloat16 *q, *k, *v;        // [B, H, DK], [B, H, DK], [B, HV, DV] (projections, pre-conv)

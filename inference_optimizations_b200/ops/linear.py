@@ -54,3 +54,64 @@ class DenseLinear:
         MG.gemm(self.wpack, xb, xb, off, pairs, out, self.status, n_tiles=self.N // (TILE * self.g),
                 kc=self.K // 64, g=self.g, nt=MG.pick_nt(t), mode=0, src_div=1, num_ctas=self.num_ctas, kind=2)
         return out
+
+
+class Fp8Linear:
+    """y = x W^T with W stored FP8 E4M3 + one UE8M0 scale per 128 x 128 block and x quantized per 1 x 128 on the fly
+    (the DeepSeek-V3 FP8 linear; the FP8 LM head of `moe-gemm/fp8-lm-head/pro_fp8_lm_head.py:1-15`), on the grouped
+    block-scaled GEMM with one "expert" holding every token."""
+
+    def __init__(self, w: torch.Tensor):
+        N, K = w.shape
+        assert N % TILE == 0 and K % TILE == 0
+        self.N, self.K = N, K
+        q, eb = MG.quant_blocks(w[None])
+        self.wpack, self.g = MG.pack_weights_paired(q, eb)
+        self.q, self.eb = q, eb
+        dev = w.device
+        self.num_ctas = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 1
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._rows: dict = {}
+
+    def dequant(self) -> torch.Tensor:
+        return MG.dequant_blocks(self.q, self.eb)[0]
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        from .._ext import ext
+        t = x.shape[0]
+        if out is None:
+            out = torch.empty(t, self.N, dtype=torch.bfloat16, device=x.device)
+        if t == 0:
+            return out
+        if t not in self._rows:
+            self._rows[t] = (torch.tensor([0, t], dtype=torch.int32, device=x.device),
+                             torch.arange(t, dtype=torch.int32, device=x.device))
+        off, pairs = self._rows[t]
+        xq = torch.empty(t, self.K, dtype=torch.uint8, device=x.device)
+        xs = torch.empty(t, self.K // TILE, dtype=torch.int32, device=x.device)
+        ext().rmsnorm_quant(x.contiguous(), None, 0.0, 0.0, xq, xs, 0)
+        MG.gemm(self.wpack, xq, xs, off, pairs, out, self.status, n_tiles=self.N // (TILE * self.g), kc=self.K // TILE,
+                g=self.g, nt=MG.pick_nt(t), mode=0, src_div=1, num_ctas=self.num_ctas, kind=0)
+        return out
+
+
+class ShardedLMHead:
+    """Vocabulary-parallel LM head: rank r holds rows [r V / n, (r + 1) V / n) (FP8 block-scaled or bf16) and returns
+    its local (max logit, argmax) per token; `parallel.dist.argmax_merge` picks the global winner (ties: lower id),
+    so the full logits never leave the GPU (the DP-LM-head shards of `moe-gemm/fp8-lm-head/pro_fp8_lm_head.py:59`)."""
+
+    def __init__(self, w: torch.Tensor, rank: int, world: int, fp8: bool = True):
+        V = w.shape[0]
+        per = -(-V // world)
+        self.v0 = rank * per
+        shard = w[self.v0:min(V, self.v0 + per)]
+        pad = (-shard.shape[0]) % 256
+        if pad:
+            shard = torch.cat([shard, torch.zeros(pad, w.shape[1], dtype=w.dtype, device=w.device)])
+        self.rows = min(V, self.v0 + per) - self.v0
+        self.lin = Fp8Linear(shard) if fp8 else DenseLinear(shard)
+
+    def local_argmax(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        logits = self.lin(x)[:, :self.rows].float()
+        val, idx = logits.max(-1)
+        return val, idx + self.v0

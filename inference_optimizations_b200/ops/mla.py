@@ -88,6 +88,26 @@ def mla_decode(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_scale:
     return (out, lse) if return_lse else out
 
 
+def dense_indices(page_table: torch.Tensor, kv_len: torch.Tensor, max_ctx: int, page: int = 64) -> torch.Tensor:
+    """Dense MLA (every cached position attended, e.g. Kimi K2.7's MLA over a paged FP4 pool; the reference's dense
+    mode of the same kernel, `kv-cache-4bit/kv4mla/csrc/api.cpp:167-257`): pool rows of positions [0, kv_len) from
+    the page table, -1 past the length, padded to a multiple of 128 (the kernel's tile)."""
+    t = kv_len.shape[0]
+    width = max(TILE, -(-max_ctx // TILE) * TILE)
+    pos = torch.arange(width, device=kv_len.device)
+    pages = page_table[:, :(-(-width // page))].long()
+    rows = pages.gather(1, (pos // page).expand(t, -1).clamp(max=pages.shape[1] - 1)) * page + pos % page
+    return torch.where(pos[None, :] < kv_len[:, None], rows, torch.full_like(rows, -1)).int()
+
+
+def mla_dense_decode(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor, kv_len: torch.Tensor,
+                     sm_scale: float, fmt: int = FMT_NVFP4, max_ctx: Optional[int] = None, **kw):
+    """Dense MLA decode over a paged latent pool (one query token per row of kv_len)."""
+    if max_ctx is None:
+        max_ctx = int(kv_len.max().item())
+    return mla_decode(q, pool, dense_indices(page_table, kv_len, max_ctx), sm_scale, fmt, **kw)
+
+
 def dequant_rows(pool: torch.Tensor, fmt: int) -> torch.Tensor:
     if fmt == FMT_NVFP4:
         return F.mla_row_dequantize(pool)

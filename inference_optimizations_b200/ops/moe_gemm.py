@@ -21,6 +21,8 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as Fn
 
+from typing import Optional
+
 from .._ext import ext
 from . import formats as FM
 
@@ -63,6 +65,13 @@ def quant_blocks(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     eb = ue8m0_exponent(b.abs().amax(dim=(-3, -1)))
     q = (b / _pow2(eb)[..., :, None, :, None]).to(torch.float8_e4m3fn).view(torch.uint8)
     return q.reshape(*lead, n, k), eb.to(torch.uint8)
+
+
+def _quant_blocks_per_expert(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """quant_blocks one expert at a time: the fp32 temporaries stay one expert large (weight preparation of big
+    expert sets must not need several times the weights in scratch memory)."""
+    qs, es = zip(*(quant_blocks(w[e]) for e in range(w.shape[0])))
+    return torch.stack(qs), torch.stack(es)
 
 
 def dequant_blocks(q: torch.Tensor, eb: torch.Tensor) -> torch.Tensor:
@@ -177,7 +186,38 @@ def gemm(wpack, x, x_scale, off, pairs, out, status, *, n_tiles: int, kc: int, g
                    out_shared_base, pairs_total)
 
 
+_TACTICS = None
+
+
+def _tactics() -> dict:
+    """Measured token-tile choice per routed-token count (`moe_tactics.json` next to this file, written by
+    `utils/microbench.py moe_tactics`): the per-token-count tactic table idea of
+    `moe-gemm/moe-tactic-tables/numinous_moe_tactics.py:1-25`, lookup = the smallest measured count >= n."""
+    global _TACTICS
+    if _TACTICS is None:
+        import json
+        import os
+        p = os.path.join(os.path.dirname(__file__), "moe_tactics.json")
+        _TACTICS = {}
+        if os.path.exists(p):
+            with open(p) as f:
+                _TACTICS = json.load(f)
+    return _TACTICS
+
+
+def tactic_nt(tokens: int, fmt: str = "fp8") -> Optional[int]:
+    table = _tactics().get(fmt)
+    if not table:
+        return None
+    keys = sorted(int(k) for k in table)
+    for k in keys:
+        if k >= tokens:
+            return int(table[str(k)])
+    return int(table[str(keys[-1])])
+
+
 def pick_nt(rows_per_expert: int) -> int:
+    """Token tile (the MMA's N) for an expected number of rows per expert."""
     for nt in (16, 32, 64):
         if rows_per_expert <= nt:
             return nt
@@ -204,9 +244,9 @@ class BlockScaledExperts:
         self.F, self.H = w_gate.shape[1], w_gate.shape[2]
         dev = w_gate.device
         if fmt == "fp8":
-            qg, eg = quant_blocks(w_gate)
-            qu, eu = quant_blocks(w_up)
-            qd, ed = quant_blocks(w_down)
+            qg, eg = _quant_blocks_per_expert(w_gate)
+            qu, eu = _quant_blocks_per_expert(w_up)
+            qd, ed = _quant_blocks_per_expert(w_down)
             self.q = (qg, eg, qu, eu, qd, ed)
             self.w1 = pack_weights([qg, qu], [eg, eu])
             self.w2, self.g2 = pack_weights_paired(qd, ed)
@@ -282,7 +322,7 @@ class BlockScaledExperts:
         off = torch.empty(E + 1, dtype=torch.int32, device=dev)
         pairs = torch.empty(P + extra, dtype=torch.int32, device=dev)
         ext().moe_align(ids.contiguous().view(-1), 0, self.E, extra, off, pairs)
-        nt = nt or pick_nt(max(1, -(-2 * P // self.E)))
+        nt = nt or tactic_nt(t, self.fmt) or pick_nt(max(1, -(-2 * P // self.E)))
         kc1 = self.H // (TILE if self.kind == 0 else 2 * TILE)
         kc2 = self.F // (TILE if self.kind == 0 else 2 * TILE)
         if self.kind == 0:

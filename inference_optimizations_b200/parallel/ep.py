@@ -100,7 +100,8 @@ class EPMoE:
         hw = self.F // 128 if self.kind == 0 else self.F // 64
         self.h = torch.zeros(L.pairs_total + T_max, hb, dtype=torch.uint8, device=dev)
         self.hs = torch.zeros(L.pairs_total + T_max, hw, dtype=torch.int32, device=dev)
-        self.nt = MG.pick_nt(max(1, -(-2 * L.pairs_total // (world * self.E_loc))))
+        self.nt = MG.tactic_nt(world * T_max, self.fmt) or MG.pick_nt(
+            max(1, -(-2 * L.pairs_total // (world * self.E_loc))))
         torch.cuda.synchronize(dev)
         dist.barrier(group=grp)
 

@@ -299,6 +299,45 @@ def ep_moe_case(tokens: int, total_experts: int, topk: int, hidden: int, ffn: in
     return res if rank == 0 else {}
 
 
+def moe_tactics_case(experts: int, total_experts: int, topk: int, hidden: int, ffn: int, wfmt: str) -> dict:
+    """Sweep the token tile (MMA N) of the grouped GEMMs over decode / prefill token counts; the fastest per count
+    (gate_up + down device time) forms the tactic table `ops/moe_tactics.json`."""
+    from .._ext import ext
+    from ..ops import moe_gemm as MG
+    dev = torch.device("cuda:0")
+    E, H, F = experts, hidden, ffn
+    kind = 0 if wfmt == "fp8" else 1
+    ex = MG.BlockScaledExperts.random_packed(E, F, H, wfmt, shared=False, device=dev)
+    vals = 128 if kind == 0 else 256
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    best, raw = {}, {}
+    for b in (1, 4, 8, 16, 32, 64, 128, 256, 512, 1024):
+        ids = torch.rand(b, total_experts, device=dev).topk(topk, dim=-1).indices.int()
+        x = torch.randn(b, H, device=dev)
+        xq, xs = MG.quant_rows(x) if kind == 0 else MG.quant_nvfp4_rows(x)
+        P = b * topk
+        off = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        pairs = torch.empty(P, dtype=torch.int32, device=dev)
+        ext().moe_align(ids.view(-1), 0, E, 0, off, pairs)
+        h = torch.empty(P, F if kind == 0 else F // 2, dtype=torch.uint8, device=dev)
+        hs = torch.empty(P, F // 128 if kind == 0 else F // 64, dtype=torch.int32, device=dev)
+        rows = torch.empty(P, H, dtype=torch.bfloat16, device=dev)
+        w = torch.ones(P, device=dev)
+        times = {}
+        for nt in (16, 32, 64, 128):
+            def run():
+                MG.gemm(ex.w1, xq, xs, off, pairs, h, status, n_tiles=F // 128, kc=H // vals, g=2, nt=nt, mode=1,
+                        src_div=topk, src_limit=P, out_scale=hs, num_ctas=sms, kind=kind)
+                MG.gemm(ex.w2, h, hs, off, pairs, rows, status, n_tiles=H // (128 * ex.g2), kc=F // vals, g=ex.g2,
+                        nt=nt, mode=2, src_div=1, pair_w=w, num_ctas=sms, kind=kind)
+            times[nt] = round(_time(run), 1)
+        raw[b] = times
+        best[str(b)] = min(times, key=times.get)
+    return {"kernel": "moe_tactics", "fmt": wfmt, "experts_local": E, "experts_total": total_experts,
+            "table": {wfmt: best}, "us": raw}
+
+
 def dense_linear_case(t: int, launches: int = 0) -> dict:
     """Decode-size dense bf16 linears of the flagship model (Gemma-class 31B, TP1): the weight-streaming tcgen05
     GEMM (ops/linear.py) against cuBLAS (torch.nn.functional.linear) on the same tensors, L2 flushed before each
@@ -355,6 +394,8 @@ def main() -> None:
         r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches)
     elif a.kernel == "indexer":
         r = indexer_case(a.b, a.ctx, a.topk, launches=a.launches)
+    elif a.kernel == "moe_tactics":
+        r = moe_tactics_case(a.experts, a.total_experts, a.topk, a.hidden, a.ffn, a.wfmt)
     elif a.kernel == "dense_linear":
         r = dense_linear_case(a.b, a.launches)
     elif a.kernel == "ep_moe":

@@ -60,3 +60,25 @@ def test_split_policy_fills_sms():
     assert ns * tps * M.TILE >= 2048 and 2 * ns <= 148 and ns > 4
     ns, tps = M.mla_split_policy(8, 200)
     assert ns * tps * M.TILE >= 200
+
+
+def test_dense_mla_indices_and_decode():
+    """Dense mode: indices from the page table cover exactly [0, kv_len); decode equals sparse decode over them."""
+    import math
+    from inference_optimizations_b200.ops import formats as F
+    from inference_optimizations_b200.ops import mla as M
+    torch.manual_seed(2)
+    pages = torch.randperm(20)[:12].view(3, 4).int()
+    kv_len = torch.tensor([70, 256, 1], dtype=torch.int32)
+    idx = M.dense_indices(pages, kv_len, 256)
+    assert idx.shape == (3, 256)
+    for b in range(3):
+        n = int(kv_len[b])
+        want = (pages[b].long()[torch.arange(n) // 64] * 64 + torch.arange(n) % 64).int()
+        assert torch.equal(idx[b, :n], want) and torch.all(idx[b, n:] == -1)
+    pool = F.mla_row_quantize(torch.randn(20 * 64, 512), torch.randn(20 * 64, 64))
+    q = torch.randn(3, 4, 576).to(torch.bfloat16)
+    sm = 1 / math.sqrt(576)
+    o1 = M.mla_dense_decode(q, pool, pages, kv_len, sm)
+    o2, _ = M.mla_decode_ref(q, pool, idx, sm, M.FMT_NVFP4)
+    assert torch.allclose(o1.float(), o2.float(), atol=1e-2)

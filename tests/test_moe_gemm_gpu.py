@@ -225,3 +225,24 @@ def test_dense_bf16_linear(cuda, t, n, k):
     ref = x.float() @ w.float().T
     err = (y.float() - ref).abs() / (ref.abs() + 1e-2 * ref.abs().max())
     assert err.max().item() < 1e-2, err.max().item()
+
+
+def test_fp8_linear_and_sharded_lm_head(cuda):
+    from inference_optimizations_b200.ops.linear import Fp8Linear, ShardedLMHead
+    torch.manual_seed(4)
+    w = (torch.randn(1000, 512, device=cuda) * 0.05).to(torch.bfloat16)
+    x = torch.randn(7, 512, device=cuda).to(torch.bfloat16)
+    lin = Fp8Linear(w[:896])
+    y = lin(x)
+    xq, xs = MG.quant_rows(x.float())
+    ref = MG.dequant_rows(xq, xs) @ lin.dequant().T
+    err = (y.float() - ref).abs() / (ref.abs() + 1e-2 * ref.abs().max())
+    assert err.max().item() < 1e-2
+    # vocabulary-parallel head over 2 shards (same GPU): merged argmax equals the argmax of the full FP8 logits
+    heads = [ShardedLMHead(w, r, 2) for r in range(2)]
+    vals, ids = zip(*[h.local_argmax(x) for h in heads])
+    v = torch.stack(vals, 1)
+    i = torch.stack(ids, 1)
+    best = i.gather(1, v.argmax(1, keepdim=True))[:, 0]
+    full = torch.cat([h.lin(x)[:, :h.rows].float() for h in heads], 1)
+    assert torch.equal(best, full.argmax(1))
