@@ -142,3 +142,25 @@ def pace_decide(prefillable: Sequence[bool], cont: Sequence[bool], running: Sequ
     if has_cont and peer:
         return "release", 0
     return "stock", 0
+
+
+def skew_chunk_cap(own_extend: int, other_extends: Sequence[int], floor: int = 1024, page: int = 64) -> int:
+    """Prefill chunk cap for a rank that would extend while others mostly decode
+    (`scheduler/dp-balance-and-pacing/pro_skew_budget_hooks.py:1-20`): max(floor, the largest extend on another
+    rank), page aligned, never below one page; 0 = no cap (this rank does not extend)."""
+    if own_extend <= 0:
+        return 0
+    cap = max(int(floor), max((int(x) for x in other_extends), default=0))
+    cap = max(page, cap // page * page)
+    return cap if cap < own_extend else 0
+
+
+def moe_pad_rows(counts: Sequence[int]) -> list:
+    """Rows each EP rank feeds the grouped expert GEMMs when per-rank token counts differ: the global per-rank mean,
+    never below the rank's own count (padding rows carry expert id -1 and are never dispatched) -- so every rank
+    sizes its token tiles for the load its experts actually receive
+    (`moe-gemm/megamoe-tile-balance/deepgemm_megamoe_hooks.py:7-20`)."""
+    if not counts:
+        return []
+    mean = -(-sum(int(c) for c in counts) // len(counts))
+    return [max(int(c), mean) for c in counts]

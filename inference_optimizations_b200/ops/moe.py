@@ -85,3 +85,23 @@ def moe_forward(x: torch.Tensor, gate: torch.Tensor, e_bias: torch.Tensor, w_gu:
     if shared_gu is not None:
         out += swiglu(x, shared_gu, shared_down).float()
     return out.to(torch.bfloat16)
+
+
+def piggyback_pack(scales: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, kmax: int) -> torch.Tensor:
+    """Routing that rides in the activation-scale tensor of a DP gather (one collective instead of two,
+    `moe-gemm/router-piggyback/dp_router_piggyback.py:1-25`): [rows, G] fp32 scales + top-k ids (as exact fp32
+    integers) + weights -> [rows, G + 2 kmax]; unused slots id -1, weight 0."""
+    rows, k = ids.shape
+    out = torch.zeros(rows, scales.shape[1] + 2 * kmax, dtype=torch.float32, device=scales.device)
+    out[:, :scales.shape[1]] = scales.float()
+    g = scales.shape[1]
+    out[:, g:g + kmax] = -1.0
+    out[:, g:g + k] = ids.float()
+    out[:, g + kmax:g + kmax + k] = w.float()
+    return out
+
+
+def piggyback_unpack(packed: torch.Tensor, groups: int, kmax: int, k: int):
+    """Inverse of piggyback_pack -> (scales [rows, G], ids int32 [rows, k], weights [rows, k])."""
+    return (packed[:, :groups], packed[:, groups:groups + k].round().int(),
+            packed[:, groups + kmax:groups + kmax + k])

@@ -57,3 +57,25 @@ def test_pace_park_and_release():
     assert P.pace_decide([False, True], [True, False], [0, 5], [0, 1], 0)[0] == "release"
     # nothing continuing: stock
     assert P.pace_decide([True, False], [False, False], [0, 5], [1, 0], 0) == ("stock", 0)
+
+
+def test_skew_chunk_cap_and_moe_pad_rows():
+    assert P.skew_chunk_cap(4096, [0, 1, 1], floor=1024) == 1024
+    assert P.skew_chunk_cap(4096, [4096, 0], floor=1024) == 0          # balanced prefills run uncapped
+    assert P.skew_chunk_cap(0, [10]) == 0
+    assert P.skew_chunk_cap(3000, [2000], floor=512, page=256) == 1792
+    assert P.moe_pad_rows([4096, 0, 96, 96]) == [4096, 1072, 1072, 1072]
+    assert P.moe_pad_rows([8, 8]) == [8, 8]
+
+
+def test_router_piggyback_round_trip():
+    import torch
+    from inference_optimizations_b200.ops import moe as MOE
+    sc = torch.rand(5, 56)
+    ids = torch.randint(0, 256, (5, 8), dtype=torch.int32)
+    w = torch.rand(5, 8)
+    packed = MOE.piggyback_pack(sc, ids, w, kmax=9)
+    assert packed.shape == (5, 56 + 18)
+    s2, i2, w2 = MOE.piggyback_unpack(packed, 56, 9, 8)
+    assert torch.equal(s2, sc) and torch.equal(i2, ids) and torch.equal(w2, w)
+    assert torch.all(packed[:, 56 + 8] == -1)

@@ -66,3 +66,18 @@ def test_bounds_check_catches_bad_page_table():
         table._dirty.add(r.slot)
         with pytest.raises(BoundsError):
             eng.step()
+
+
+def test_serving_gate_ab_record():
+    from inference_optimizations_b200.config import EngineConfig, model_config
+    from inference_optimizations_b200.tooling import serving_gate as SG
+    ecfg = EngineConfig(model="tiny_gqa", device="cpu", kv_dtype="nvfp4", max_running=3, chunked_prefill=64,
+                        cuda_graphs=False)
+    res = SG.gate(ecfg, model_config("tiny_gqa"), {"decode_burst": 2}, sessions=3, prompt=40, steps=3, warmup=1,
+                  repeats=2)
+    assert set(res["arms"]) == {"control", "delta"}
+    for arm in res["arms"].values():
+        assert len(arm["runs"]) == 2 and all(r["tokens"] > 0 for r in arm["runs"])
+        assert arm["config_digest"]
+    assert res["arms"]["control"]["config_digest"] != res["arms"]["delta"]["config_digest"]
+    assert res["verdict"] in ("neutral", "better", "worse")
