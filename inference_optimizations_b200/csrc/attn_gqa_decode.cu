@@ -645,12 +645,14 @@ __device__ __forceinline__ void dequant_e4m3_64(const uint8_t* part, int r, int 
   }
 }
 
-// E4M3 kernel roles: warps 0-3 softmax, 4-11 K dequant, 12-19 V dequant, 20 producer, 21 UMMA issuer, 22-23 idle
+// E4M3 kernel roles: warps 0-3 softmax, 4-11 K dequant, 12-19 V dequant, 20 producer, 21 QK issuer, 22 PV issuer,
+// 23 idle
 // (six full warpgroups so setmaxnreg can move registers: softmax 160, dequant 72, producer/issuer 32 per thread;
 // 128 x 160 + 512 x 72 + 128 x 32 = 61440 = 768 threads x 80 at launch).
 constexpr int kThreadsF8 = 768;
 constexpr int kProducerWarpF8 = 20;
 constexpr int kMmaWarpF8 = 21;
+constexpr int kPvWarpF8 = 22;
 
 // TMEM rows (columns) [0, RMAX) of this thread's lane.
 template <int RMAX>
@@ -1198,27 +1200,32 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
         mbar_wait(&sm.raw_full[NSTK + rs % NSTV], (rs / NSTV) & 1, nullptr, a.status, kTimeoutProducer);
     }
     } else if (warp == kMmaWarpF8) {
+    // QK issuer.  P V is issued by a second warp (kPvWarpF8): one thread's tcgen05.mma issue rate, not the tensor
+    // pipe, bounds a chain of small-N MMAs (measured: two issuing warps complete twice the MMAs per cycle).
     if (lane == 0) {
       const uint32_t id_qk = idesc_dense(0, 0, 128, kN);                 // E4M3 x E4M3, K-major both
-      const uint32_t id_pv = idesc_dense(0, 0, 128, kN) | (1u << 15);   // A (V^T) MN-major
-      const uint32_t ring_addr = smem_u32(ring), q_addr = smem_u32(sq), p_addr = smem_u32(sp);
-      for (int j = 0; j <= ntiles; ++j) {
-        if (j < ntiles) {
-          const int sb = j & 1;
-          if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
-          if (!mbar_wait(&sm.kf[sb], (j >> 1) & 1, abort, a.status, kTimeoutMma)) break;
-          tc_fence_after();
-          trace_ev(a.trace, kEvQkStart, j);
+      const uint32_t q_addr = smem_u32(sq);
+      for (int j = 0; j < ntiles; ++j) {
+        const int sb = j & 1;
+        if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
+        if (!mbar_wait(&sm.kf[sb], (j >> 1) & 1, abort, a.status, kTimeoutMma)) break;
+        tc_fence_after();
+        trace_ev(a.trace, kEvQkStart, j);
 #pragma unroll 4
-          for (int s = 0; s < D / 32; ++s)
-            umma_f8_ts(tS + sb * (kSParts * kN) + (s % kSParts) * kN, tK + sb * (D / 4) + 8 * s,
-                       desc_sw128(q_addr + (s >> 2) * (kN * 128) + (s & 3) * 32), id_qk, s >= kSParts ? 1u : 0u);
-          umma_commit(&sm.s_full[sb]);
-          umma_commit(&sm.ke[sb]);
-          trace_ev(a.trace, kEvQkEnd, j);
-        }
-        if (kCc || j == 0) continue;
-        const int i = j - 1, sb = i & 1;
+        for (int s = 0; s < D / 32; ++s)
+          umma_f8_ts(tS + sb * (kSParts * kN) + (s % kSParts) * kN, tK + sb * (D / 4) + 8 * s,
+                     desc_sw128(q_addr + (s >> 2) * (kN * 128) + (s & 3) * 32), id_qk, s >= kSParts ? 1u : 0u);
+        umma_commit(&sm.s_full[sb]);
+        umma_commit(&sm.ke[sb]);
+        trace_ev(a.trace, kEvQkEnd, j);
+      }
+    }
+    } else if (warp == kPvWarpF8 && !kCc) {
+    if (lane == 0) {
+      const uint32_t id_pv = idesc_dense(0, 0, 128, kN) | (1u << 15);   // A (V^T) MN-major
+      const uint32_t ring_addr = smem_u32(ring), p_addr = smem_u32(sp);
+      for (int i = 0; i < ntiles; ++i) {
+        const int sb = i & 1;
         if (!mbar_wait(&sm.p_full[sb], (i >> 1) & 1, abort, a.status, kTimeoutMma)) break;
         if (!mbar_wait(&sm.o_empty[sb], ((i >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
         trace_ev(a.trace, kEvPvStart, i);

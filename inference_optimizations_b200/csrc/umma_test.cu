@@ -144,9 +144,30 @@ __global__ void __launch_bounds__(128) umma_rate_kernel(int n, int count, int na
   tc_fence_after();
   const uint32_t t = tmem_base;
   const int issuers = variant == 6 ? 2 : 1;
-  if (lane_id() == 0 && warp_id() < issuers) {
-    const int m = variant == 5 ? 64 : 128;
-    const uint32_t idesc = variant == 3 ? idesc_dense(0, 0, m, n) : idesc_dense(1, 1, m, n);
+  if (variant == 10 && warp_id() == 0) {
+    // whole warp converged in the loop; one elected lane issues each MMA (E4M3, both operands K-major)
+    const uint32_t idesc = idesc_dense(0, 0, 128, n);
+    const uint64_t a = desc_sw128(smem_u32(smem)), b = desc_sw128(smem_u32(smem + 16384));
+    const long long c0 = clock64();
+    for (int i = 0; i < count; ++i) {
+      const uint32_t d = t + (i % nacc) * n;
+      if (elect_one()) umma_f8_ss(d, a, b, idesc, 1u);
+      __syncwarp();
+    }
+    const long long c1 = clock64();
+    if (elect_one()) umma_commit(&bar[0]);
+    __syncwarp();
+    mbar_wait(&bar[0], 0, nullptr, nullptr, 0);
+    const long long c2 = clock64();
+    if (threadIdx.x == 0) {
+      out[0] = c1 - c0;
+      out[1] = c2 - c0;
+    }
+  } else if (variant != 10 && lane_id() == 0 && warp_id() < issuers) {
+    const int m = (variant == 5 || variant == 9) ? 64 : 128;
+    const bool f8 = variant == 3 || variant >= 7;
+    uint32_t idesc = f8 ? idesc_dense(0, 0, m, n) : idesc_dense(1, 1, m, n);
+    if (variant == 8) idesc |= 1u << 15;                              // A MN-major
     const uint64_t a = desc_sw128(smem_u32(smem)), b = desc_sw128(smem_u32(smem + 16384));
     const uint32_t dbase = t + warp_id() * 128;
     const long long c0 = clock64();
@@ -157,6 +178,9 @@ __global__ void __launch_bounds__(128) umma_rate_kernel(int n, int count, int na
         case 2: umma_f16_ss_nc(d, a, b, idesc, 1u); break;
         case 3: umma_f8_ss(d, a, b, idesc, 1u); break;
         case 4: umma_f16_ws_ss(d, a, b, idesc, 1u); break;
+        case 7: umma_f8_ts(d, t + 256, b, idesc, 1u); break;                       // E4M3, A from TMEM
+        case 8: umma_f8_ss(d, desc_mn128(smem_u32(smem), 16384), b, idesc, 1u); break;  // E4M3, A MN-major
+        case 9: umma_f8_ss(d, a, b, idesc, 1u); break;                             // E4M3, M = 64
         default: umma_f16_ss(d, a, b, idesc, 1u); break;
       }
     }
