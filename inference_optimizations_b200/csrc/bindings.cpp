@@ -655,6 +655,22 @@ void rmsnorm_quant(const at::Tensor& x, const c10::optional<at::Tensor>& w, doub
                                    reinterpret_cast<uint32_t*>(sc.data_ptr<int>()), stream()));
 }
 
+void act_quant(const at::Tensor& gu, bool gelu, at::Tensor q, at::Tensor sc, int64_t fmt) {
+  req(gu, at::kBFloat16, "gate_up");
+  req(q, at::kByte, "q");
+  req(sc, at::kInt, "sc");
+  TORCH_CHECK(fmt == 0 || fmt == 1, "fmt");
+  const int64_t F = gu.size(1) / 2;
+  TORCH_CHECK(gu.dim() == 2 && gu.size(1) % 2 == 0 && gu.is_contiguous() && q.is_contiguous() && sc.is_contiguous() &&
+                  q.size(0) == gu.size(0) && q.size(1) * (fmt == 0 ? 1 : 2) == F && sc.size(0) == gu.size(0) &&
+                  sc.size(1) * (fmt == 0 ? 128 : 64) == F,
+              "act_quant shapes");
+  const at::cuda::CUDAGuard g(gu.device());
+  CHECK_CUDA_OK(iob::act_quant(gu.data_ptr(), static_cast<int>(gu.size(0)), static_cast<int>(F), gelu,
+                               static_cast<int>(fmt), q.data_ptr<uint8_t>(),
+                               reinterpret_cast<uint32_t*>(sc.data_ptr<int>()), stream()));
+}
+
 void umma_gemm_test(const at::Tensor& A, const at::Tensor& B, at::Tensor C, int64_t sw64) {
   req(A, at::kBFloat16, "A");
   req(B, at::kBFloat16, "B");
@@ -707,6 +723,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_align", &moe_align);
   m.def("moe_combine", &moe_combine);
   m.def("rmsnorm_quant", &rmsnorm_quant);
+  m.def("act_quant", &act_quant);
   m.def("ep_dispatch", &ep_dispatch);
   m.def("ep_barrier", &ep_barrier);
   m.def("dcp_merge", &dcp_merge);

@@ -534,6 +534,11 @@ __device__ __forceinline__ void f4_table_fill(uint2* tab) {
 __device__ __forceinline__ uint32_t e2m1_code_mag(float y) {
   return (y > 0.25f) + (y > 0.75f) + (y > 1.25f) + (y > 1.75f) + (y > 2.5f) + (y > 3.5f) + (y > 5.0f);
 }
+// GELU, tanh approximation: 0.5 g (1 + tanh(sqrt(2 / pi) (g + 0.044715 g^3))).
+__device__ __forceinline__ float gelu_tanh_f(float g) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
+  return 0.5f * g * (1.f + tanhf(k0 * (g + 0.044715f * g * g * g)));
+}
 __device__ __forceinline__ uint32_t e2m1_code(float y) {  // signed, no negative zero
   const uint32_t m = e2m1_code_mag(fabsf(y));
   return m | ((y < 0.f && m > 0) ? 8u : 0u);

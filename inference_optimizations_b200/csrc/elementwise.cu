@@ -73,10 +73,7 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat1
   }
 }
 
-__device__ __forceinline__ float gelu_tanh(float g) {
-  const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
-  return 0.5f * g * (1.f + tanhf(k0 * (g + 0.044715f * g * g * g)));
-}
+__device__ __forceinline__ float gelu_tanh(float g) { return gelu_tanh_f(g); }
 
 template <bool GELU>
 __global__ void act_mul_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out, int ffn) {

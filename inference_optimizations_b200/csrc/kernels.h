@@ -253,6 +253,8 @@ struct EpDispatchArgs {
 cudaError_t ep_dispatch(const EpDispatchArgs& a, cudaStream_t s);
 cudaError_t ep_barrier(const long long* peers, long long off_flags, int rank, int world, int* epoch, int* status,
                        cudaStream_t s);
+// act(gate) * up over gate_up [T, 2F] -> quantized (fmt 0 E4M3 + UE8M0 per 128, fmt 1 NVFP4 per 16).
+cudaError_t act_quant(const void* gate_up, int T, int F, bool gelu, int fmt, uint8_t* q, uint32_t* sc, cudaStream_t s);
 cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_one, int T, int H, int fmt, uint8_t* q,
                           uint32_t* sc, cudaStream_t s);
 

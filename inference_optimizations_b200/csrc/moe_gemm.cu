@@ -560,34 +560,11 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* rows, int T, int topk, i
 // 128 columns (scale words replicate the exponent byte four times: the layout the GEMM gathers).  fmt 1: NVFP4 --
 // E2M1 pairs (element 2i in the low nibble) with one E4M3 scale e4m3(clamp(amax / 6, 2^-9, 448)) per 16 columns.
 // `w` null: quantize x as is.
-__global__ void rmsnorm_quant_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, float plus_one,
-                                     int H, int fmt, uint8_t* q, uint32_t* sc) {
-  const int row = blockIdx.x;
-  const __nv_bfloat16* xr = x + static_cast<size_t>(row) * H;
-  __shared__ float red[32];
-  float inv = 1.f;
-  if (w) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) {
-      const float v = __bfloat162float(xr[i]);
-      ss += v * v;
-    }
-    ss = warp_sum(ss);
-    if (lane_id() == 0) red[warp_id()] = ss;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
-      v = warp_sum(v);
-      if (threadIdx.x == 0) red[0] = v;
-    }
-    __syncthreads();
-    inv = rsqrtf(red[0] / H + eps);
-  }
-  auto val = [&](int c) {
-    float f = __bfloat162float(xr[c]);
-    if (w) f = __bfloat162float(__float2bfloat16(f * inv * (__bfloat162float(w[c]) + plus_one)));
-    return f;
-  };
+// Quantize one row of H values given by val(c) (already rounded to bf16): fmt 0 = E4M3 + one UE8M0 scale per 128
+// (stored as four identical bytes, the layout the block-scaled GEMM reads), fmt 1 = NVFP4 (E2M1 pairs + one E4M3 scale
+// per 16).  Called by every thread of the block.
+template <class Val>
+__device__ __forceinline__ void quant_row(Val val, int row, int H, int fmt, uint8_t* q, uint32_t* sc) {
   if (fmt == 0) {
     // one warp per 128-column group: 4 values per lane
     for (int g = warp_id(); g < H / 128; g += blockDim.x / 32) {
@@ -631,6 +608,50 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* x, const __nv_bfloat16
   }
 }
 
+__global__ void rmsnorm_quant_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, float plus_one,
+                                     int H, int fmt, uint8_t* q, uint32_t* sc) {
+  const int row = blockIdx.x;
+  const __nv_bfloat16* xr = x + static_cast<size_t>(row) * H;
+  __shared__ float red[32];
+  float inv = 1.f;
+  if (w) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      const float v = __bfloat162float(xr[i]);
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if (lane_id() == 0) red[warp_id()] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+      v = warp_sum(v);
+      if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    inv = rsqrtf(red[0] / H + eps);
+  }
+  quant_row([&](int c) {
+    float f = __bfloat162float(xr[c]);
+    if (w) f = __bfloat162float(__float2bfloat16(f * inv * (__bfloat162float(w[c]) + plus_one)));
+    return f;
+  }, row, H, fmt, q, sc);
+}
+
+// act(gate) * up -> quantized, one pass over gate_up [T, 2F] (gate = first F columns): the GEMM1 -> GEMM2 glue of a
+// block-scaled dense MLP.  The product is rounded to bf16 before quantization, so the output equals quantizing the
+// bf16 act_mul result bit for bit (the reference's one-pass `attention/gemma-fused-glue/gelu_tanh_quant.cuh:1-25`).
+template <bool GELU>
+__global__ void act_quant_kernel(const __nv_bfloat16* gu, int F, int fmt, uint8_t* q, uint32_t* sc) {
+  const int row = blockIdx.x;
+  const __nv_bfloat16* g = gu + static_cast<size_t>(row) * 2 * F;
+  quant_row([&](int c) {
+    const float gv = __bfloat162float(g[c]);
+    const float a = GELU ? gelu_tanh_f(gv) : gv / (1.f + __expf(-gv));
+    return __bfloat162float(__float2bfloat16(a * __bfloat162float(g[F + c])));
+  }, row, F, fmt, q, sc);
+}
+
 }  // namespace
 
 cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
@@ -672,6 +693,17 @@ cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_on
   if ((fmt == 0 && H % 128) || (fmt == 1 && H % 64) || fmt < 0 || fmt > 1) return cudaErrorInvalidValue;
   rmsnorm_quant_kernel<<<T, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
                                          static_cast<const __nv_bfloat16*>(w), eps, plus_one, H, fmt, q, sc);
+  return cudaGetLastError();
+}
+
+cudaError_t act_quant(const void* gate_up, int T, int F, bool gelu, int fmt, uint8_t* q, uint32_t* sc, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if ((fmt == 0 && F % 128) || (fmt == 1 && F % 64) || fmt < 0 || fmt > 1) return cudaErrorInvalidValue;
+  const auto* gu = static_cast<const __nv_bfloat16*>(gate_up);
+  if (gelu)
+    act_quant_kernel<true><<<T, 256, 0, s>>>(gu, F, fmt, q, sc);
+  else
+    act_quant_kernel<false><<<T, 256, 0, s>>>(gu, F, fmt, q, sc);
   return cudaGetLastError();
 }
 

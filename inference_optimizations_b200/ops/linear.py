@@ -83,16 +83,68 @@ class Fp8Linear:
             out = torch.empty(t, self.N, dtype=torch.bfloat16, device=x.device)
         if t == 0:
             return out
-        if t not in self._rows:
-            self._rows[t] = (torch.tensor([0, t], dtype=torch.int32, device=x.device),
-                             torch.arange(t, dtype=torch.int32, device=x.device))
-        off, pairs = self._rows[t]
         xq = torch.empty(t, self.K, dtype=torch.uint8, device=x.device)
         xs = torch.empty(t, self.K // TILE, dtype=torch.int32, device=x.device)
         ext().rmsnorm_quant(x.contiguous(), None, 0.0, 0.0, xq, xs, 0)
+        return self.forward_quantized(xq, xs, out)
+
+    def forward_quantized(self, xq: torch.Tensor, xs: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """y = dequant(xq, xs) W^T for activations already quantized (E4M3 [T, K] + UE8M0 words [T, K / 128])."""
+        t = xq.shape[0]
+        if out is None:
+            out = torch.empty(t, self.N, dtype=torch.bfloat16, device=xq.device)
+        if t == 0:
+            return out
+        if t not in self._rows:
+            self._rows[t] = (torch.tensor([0, t], dtype=torch.int32, device=xq.device),
+                             torch.arange(t, dtype=torch.int32, device=xq.device))
+        off, pairs = self._rows[t]
         MG.gemm(self.wpack, xq, xs, off, pairs, out, self.status, n_tiles=self.N // (TILE * self.g), kc=self.K // TILE,
                 g=self.g, nt=MG.pick_nt(t), mode=0, src_div=1, num_ctas=self.num_ctas, kind=0)
         return out
+
+
+def act_quant(gate_up: torch.Tensor, gelu: bool = True, fmt: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """act(gate) * up over gate_up [T, 2F] (gate first), quantized in the same pass: fmt 0 -> (E4M3 [T, F], UE8M0
+    words [T, F / 128]); fmt 1 -> (E2M1 pairs [T, F / 2], E4M3 scale bytes as words [T, F / 64]).  Equals quantizing
+    the bf16 `act_mul` output bit for bit."""
+    t, f = gate_up.shape[0], gate_up.shape[1] // 2
+    if not gate_up.is_cuda:
+        return act_quant_ref(gate_up, gelu, fmt)
+    from .._ext import ext
+    q = torch.empty(t, f if fmt == 0 else f // 2, dtype=torch.uint8, device=gate_up.device)
+    sc = torch.empty(t, f // (128 if fmt == 0 else 64), dtype=torch.int32, device=gate_up.device)
+    ext().act_quant(gate_up.contiguous(), gelu, q, sc, fmt)
+    return q, sc
+
+
+def act_quant_ref(gate_up: torch.Tensor, gelu: bool = True, fmt: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    from . import basic as B
+    a = B.act_mul(gate_up.cpu(), gelu)
+    return MG.quant_rows(a) if fmt == 0 else MG.quant_nvfp4_rows(a)
+
+
+class Fp8Mlp:
+    """Block-scaled FP8 gated MLP: gate_up GEMM -> fused act * up + per-128 quant -> down GEMM on the quantized
+    activations (no bf16 intermediate round trip; the FP8 Gemma MLP glue of
+    `attention/gemma-fused-glue/gelu_quant.py:1-30`)."""
+
+    def __init__(self, w_gu: torch.Tensor, w_down: torch.Tensor, gelu: bool = True):
+        self.gu, self.down, self.gelu = Fp8Linear(w_gu), Fp8Linear(w_down), gelu
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        h = self.gu(x)
+        q, s = act_quant(h, self.gelu, 0)
+        return self.down.forward_quantized(q, s)
+
+    def reference(self, x: torch.Tensor) -> torch.Tensor:
+        """fp32 oracle over the dequantized weights with the same activation quantization points."""
+        from . import basic as B
+        xq, xs = MG.quant_rows(x.float())
+        h = (MG.dequant_rows(xq, xs) @ self.gu.dequant().float().t()).to(torch.bfloat16)
+        a = B.act_mul(h.cpu(), self.gelu).float()
+        aq, as_ = MG.quant_rows(a)
+        return MG.dequant_rows(aq, as_) @ self.down.dequant().float().cpu().t()
 
 
 class ShardedLMHead:

@@ -246,3 +246,30 @@ def test_fp8_linear_and_sharded_lm_head(cuda):
     best = i.gather(1, v.argmax(1, keepdim=True))[:, 0]
     full = torch.cat([h.lin(x)[:, :h.rows].float() for h in heads], 1)
     assert torch.equal(best, full.argmax(1))
+
+
+@pytest.mark.parametrize("gelu", [True, False])
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_act_quant_bitexact(cuda, gelu, fmt):
+    """One-pass act(gate) * up + quant equals quantizing the bf16 act_mul output, bit for bit."""
+    from inference_optimizations_b200.ops import basic as B
+    from inference_optimizations_b200.ops.linear import act_quant
+    torch.manual_seed(5)
+    gu = (torch.randn(37, 2 * 1024, device=cuda) * 2).to(torch.bfloat16)
+    q, s = act_quant(gu, gelu, fmt)
+    a = B.act_mul(gu, gelu)
+    rq, rs = MG.quant_rows(a) if fmt == 0 else MG.quant_nvfp4_rows(a)
+    assert torch.equal(q, rq) and torch.equal(s, rs)
+
+
+def test_fp8_mlp(cuda):
+    from inference_optimizations_b200.ops.linear import Fp8Mlp
+    torch.manual_seed(6)
+    wgu = (torch.randn(2 * 768, 512, device=cuda) * 0.05).to(torch.bfloat16)
+    wd = (torch.randn(512, 768, device=cuda) * 0.05).to(torch.bfloat16)
+    x = torch.randn(9, 512, device=cuda).to(torch.bfloat16)
+    mlp = Fp8Mlp(wgu, wd)
+    y = mlp(x).float()
+    ref = mlp.reference(x).to(y.device)
+    err = (y - ref).abs() / (ref.abs() + 1e-2 * ref.abs().max())
+    assert err.max().item() < 2e-2

@@ -110,3 +110,23 @@ def test_ep_layout_regions_and_pair_routing():
                 for k in (0, 7):
                     assert L.comb_row(L.pair(src, t, k)) == (src, t * 8 + k)
         assert L.owner(255, 32) == 7 and L.owner(32, 32) == 1
+
+
+def test_act_quant_ref_roundtrip():
+    """CPU path of the fused activation + quant: dequantized output tracks act_mul within the format's error."""
+    import torch
+    from inference_optimizations_b200.ops import basic as B
+    from inference_optimizations_b200.ops import moe_gemm as MG
+    from inference_optimizations_b200.ops.linear import act_quant
+    torch.manual_seed(0)
+    gu = torch.randn(5, 512).to(torch.bfloat16)
+    a = B.act_mul(gu, True).float()
+    q, s = act_quant(gu, True, 0)
+    assert q.shape == (5, 256) and s.shape == (5, 2)
+    d = MG.dequant_rows(q, s)
+    assert ((d - a).abs() <= a.abs().amax(-1, keepdim=True) / 16 + 1e-6).all()
+    q4, s4 = act_quant(gu, False, 1)
+    assert q4.shape == (5, 128) and s4.shape == (5, 4)
+    d4 = MG.dequant_nvfp4_rows(q4, s4)
+    a4 = B.act_mul(gu, False).float()
+    assert (d4 - a4).abs().max() <= a4.abs().max() / 3
