@@ -189,6 +189,7 @@ class EngineConfig:
     prefix_cache: bool = True            # radix prefix reuse (MLA family; sliding-window GQA models do not reuse)
     # runtime
     cuda_graphs: bool = True
+    extend_kernel: bool = True           # GQA prefill over NVFP4 / FP8 pools through the 128-row extend kernel
     graph_batch_sizes: str = "1,2,4,8,16,32,64"
     # parallelism
     tp: int = 1

@@ -1124,10 +1124,13 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
       const bool valid = sm.raw_valid[st] != 0;
       if (dw == 0 && lane == 0) trace_ev(a.trace, kEvVDeqStart, i);
       bool ok = true;
+      // every slab of the tile is written, then one proxy fence publishes them all (PV waits for the whole tile)
       for (int mb = 0; mb < MB; ++mb) {
         const int seq = MB * i + mb, buf = seq % RING;
         if (!(ok = mbar_wait(&sm.ring_empty[buf], ((seq / RING) & 1) ^ 1, abort, a.status, kTimeoutConsumer)))
           break;
+        if (dw == 0 && lane == 0 && (mb == 1 || mb == 2))   // slab timings (diagnostic timeline)
+          trace_ev(a.trace, mb == 1 ? kEvProdK : kEvProdV, i);
         uint32_t o[16];
         if (valid) dequant_e4m3_64<FMT, D>(raw + st * PB, vr, 128 * mb + 64 * vhalf, o, f4tab);
         else {
@@ -1139,11 +1142,13 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
         for (int q = 0; q < 4; ++q)
           *reinterpret_cast<uint4*>(slab + sw128_chunk(vtok, vhalf * 4 + q)) =
               make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm.ring_full[buf]);
       }
       if (!ok) break;
+      if (dw == 0 && lane == 0) trace_ev(a.trace, kEvKRaw, i);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0)
+        for (int mb = 0; mb < MB; ++mb) mbar_arrive(&sm.ring_full[(MB * i + mb) % RING]);
       __syncwarp();
       if (lane == 0) { mbar_arrive(&sm.raw_empty[st0]); mbar_arrive(&sm.raw_empty[st1]); }
       if (dw == 0 && lane == 0) trace_ev(a.trace, kEvVDeqEnd, i);
@@ -1200,55 +1205,89 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
         mbar_wait(&sm.raw_full[NSTK + rs % NSTV], (rs / NSTV) & 1, nullptr, a.status, kTimeoutProducer);
     }
     } else if (warp == kMmaWarpF8) {
-    // QK issuer.  P V is issued by a second warp (kPvWarpF8): one thread's tcgen05.mma issue rate, not the tensor
-    // pipe, bounds a chain of small-N MMAs (measured: two issuing warps complete twice the MMAs per cycle).
-    if (lane == 0) {
-      const uint32_t id_qk = idesc_dense(0, 0, 128, kN);                 // E4M3 x E4M3, K-major both
-      const uint32_t q_addr = smem_u32(sq);
-      for (int j = 0; j < ntiles; ++j) {
-        const int sb = j & 1;
-        if (!mbar_wait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
-        if (!mbar_wait(&sm.kf[sb], (j >> 1) & 1, abort, a.status, kTimeoutMma)) break;
-        tc_fence_after();
-        trace_ev(a.trace, kEvQkStart, j);
-#pragma unroll 4
-        for (int s = 0; s < D / 32; ++s)
-          umma_f8_ts(tS + sb * (kSParts * kN) + (s % kSParts) * kN, tK + sb * (D / 4) + 8 * s,
-                     desc_sw128(q_addr + (s >> 2) * (kN * 128) + (s & 3) * 32), id_qk, s >= kSParts ? 1u : 0u);
+    // QK issuer: the whole warp runs the loop (descriptor arithmetic stays warp-uniform), one elected lane issues
+    // the MMAs four per asm statement.  P V is issued by a second warp (kPvWarpF8).  (Issued one per statement by a
+    // lone lane, consecutive tcgen05.mma measured ~250 cycles apart whatever their shape; batched from a converged
+    // warp, ~65-80 cycles for these N = 16 MMAs.)
+    const bool el = elect_one();
+    auto wwait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, a.status, kTimeoutMma));
+    };
+    const uint32_t id_qk = idesc_dense(0, 0, 128, kN);                 // E4M3 x E4M3, K-major both
+    const uint32_t q_addr = smem_u32(sq);
+    for (int j = 0; j < ntiles; ++j) {
+      const int sb = j & 1;
+      if (!wwait(&sm.s_empty[sb], ((j >> 1) & 1) ^ 1)) break;
+      if (!wwait(&sm.kf[sb], (j >> 1) & 1)) break;
+      tc_fence_after();
+      if (el) trace_ev(a.trace, kEvQkStart, j);
+      static_assert(kSParts == 4, "one batch of four MMAs = one K step into each partial accumulator");
+#pragma unroll
+      for (int s0 = 0; s0 < D / 32; s0 += 4) {
+        uint32_t d4[4], a4[4];
+        uint64_t b4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int s = s0 + k;
+          d4[k] = tS + sb * (kSParts * kN) + k * kN;
+          a4[k] = tK + sb * (D / 4) + 8 * s;
+          b4[k] = desc_sw128(q_addr + (s >> 2) * (kN * 128) + (s & 3) * 32);
+        }
+        if (el) umma_f8_ts_x4(d4, a4, b4, id_qk, s0 > 0 ? 0xFu : 0u);
+      }
+      if (el) {
         umma_commit(&sm.s_full[sb]);
         umma_commit(&sm.ke[sb]);
         trace_ev(a.trace, kEvQkEnd, j);
       }
+      __syncwarp();
     }
     } else if (warp == kPvWarpF8 && !kCc) {
-    if (lane == 0) {
-      const uint32_t id_pv = idesc_dense(0, 0, 128, kN) | (1u << 15);   // A (V^T) MN-major
-      const uint32_t ring_addr = smem_u32(ring), p_addr = smem_u32(sp);
-      for (int i = 0; i < ntiles; ++i) {
-        const int sb = i & 1;
-        if (!mbar_wait(&sm.p_full[sb], (i >> 1) & 1, abort, a.status, kTimeoutMma)) break;
-        if (!mbar_wait(&sm.o_empty[sb], ((i >> 1) & 1) ^ 1, abort, a.status, kTimeoutMma)) break;
-        trace_ev(a.trace, kEvPvStart, i);
-        bool ok = true;
-        for (int mb = 0; mb < MB && ok; ++mb) {
-          const int seq = MB * i + mb;
-          ok = mbar_wait(&sm.ring_full[seq % RING], (seq / RING) & 1, abort, a.status, kTimeoutMma);
-        }
-        if (!ok) break;
-        tc_fence_after();
+    const bool el = elect_one();
+    auto wwait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, a.status, kTimeoutMma));
+    };
+    const uint32_t id_pv = idesc_dense(0, 0, 128, kN) | (1u << 15);   // A (V^T) MN-major
+    const uint32_t ring_addr = smem_u32(ring), p_addr = smem_u32(sp);
+    for (int i = 0; i < ntiles; ++i) {
+      const int sb = i & 1;
+      if (!wwait(&sm.p_full[sb], (i >> 1) & 1)) break;
+      if (!wwait(&sm.o_empty[sb], ((i >> 1) & 1) ^ 1)) break;
+      if (el) trace_ev(a.trace, kEvPvStart, i);
+      bool ok = true;
+      for (int mb = 0; mb < MB && ok; ++mb) {
+        const int seq = MB * i + mb;
+        ok = wwait(&sm.ring_full[seq % RING], (seq / RING) & 1);
+      }
+      if (!ok) break;
+      tc_fence_after();
+      static_assert((4 * MB) % 4 == 0, "PV MMAs come in batches of four");
+      uint32_t d4[4];
+      uint64_t a4[4], b4[4];
+      uint32_t mask = 0;
+      int n4 = 0;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+      for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
-          for (int mb = 0; mb < MB; ++mb) {
-            const int buf = (MB * i + mb) % RING;
-            umma_f8_ss(tO + sb * kOCols + mb * kN, desc_mn_sw128(ring_addr + buf * kSlabBytes + kk * 4096, kSlabBytes),
-                       desc_sw128(p_addr + sb * (kN * 128) + kk * 32), id_pv, kk > 0 ? 1u : 0u);
+        for (int mb = 0; mb < MB; ++mb) {
+          const int buf = (MB * i + mb) % RING;
+          d4[n4] = tO + sb * kOCols + mb * kN;
+          a4[n4] = desc_mn_sw128(ring_addr + buf * kSlabBytes + kk * 4096, kSlabBytes);
+          b4[n4] = desc_sw128(p_addr + sb * (kN * 128) + kk * 32);
+          if (kk > 0) mask |= 1u << n4;
+          if (++n4 == 4) {
+            if (el) umma_f8_ss_x4(d4, a4, b4, id_pv, mask);
+            n4 = 0;
+            mask = 0;
           }
         }
+      }
+      if (el) {
         for (int mb = 0; mb < MB; ++mb) umma_commit(&sm.ring_empty[(MB * i + mb) % RING]);
         umma_commit(&sm.o_full[sb]);
         trace_ev(a.trace, kEvPvEnd, i);
       }
+      __syncwarp();
     }
     }
   }

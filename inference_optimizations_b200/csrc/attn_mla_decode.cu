@@ -434,72 +434,98 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
   } else {
     regs_dec<48>();
     if (warp == kMMmaWarp) {
-      if (lane == 0) {
-        // ------------------------------------------------------------ MMA issue (one thread)
-        const uint32_t id_qk = idesc_dense(0, 0, 128, kMTile);
-        const uint32_t id_pv = idesc_dense(0, 0, 128, 256) | (1u << 16);  // B (V) MN-major
-        const uint32_t tiles_a = smem_u32(tiles), p_a = smem_u32(sp), qr_a = smem_u32(sqr);
-        const uint32_t tO = tmem + kMColO, tQ = tmem + kMColQ;
-        bool ok = mbar_wait(&sm.q_ready, 0, abort, a.status, kTimeoutMma);
-        mla_trace(a.trace, kMlaEvQReady, 0);
-        // Issue QK(nq) and PV(np) in whichever order their inputs become ready: QK(j) needs tile j and S free
-        // (softmax(j - 1) loaded it); PV(j) needs P(j).  The tensor pipe runs them in issue order.
-        int nq = 0, np = 0;
-        unsigned long long t0 = global_ns();
-        uint32_t idle = 0;
-        while (ok && np < ntiles) {
-          bool progressed = false;
-          if (nq < ntiles) {
-            const int rb = nq % kMRing;
-            if (mbar_test(&sm.tile_full[rb], (nq / kMRing) & 1) &&
-                (nq < 1 || mbar_test(&sm.s_free, (nq - 1) & 1))) {
-              tc_fence_after();
-              const uint32_t tile = tiles_a + rb * kMTileBytes;
-              const uint32_t tS = tmem + kMColS;
+      // ------------------------------------------------------------ MMA issue: the whole warp runs the loop
+      // (warp-uniform descriptor arithmetic), one elected lane issues the MMAs, four per asm statement
+      const bool el = elect_one();
+      const uint32_t id_qk = idesc_dense(0, 0, 128, kMTile);
+      const uint32_t id_pv = idesc_dense(0, 0, 128, 256) | (1u << 16);  // B (V) MN-major
+      const uint32_t tiles_a = smem_u32(tiles), p_a = smem_u32(sp), qr_a = smem_u32(sqr);
+      const uint32_t tO = tmem + kMColO, tQ = tmem + kMColQ;
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_ready, 0, abort, a.status, kTimeoutMma));
+      if (el) mla_trace(a.trace, kMlaEvQReady, 0);
+      auto test = [&](uint64_t* bar, uint32_t parity) {
+        return __shfl_sync(0xffffffffu, lane == 0 ? static_cast<int>(mbar_test(bar, parity)) : 0, 0) != 0;
+      };
+      // Issue QK(nq) and PV(np) in whichever order their inputs become ready: QK(j) needs tile j and S free
+      // (softmax(j - 1) loaded it); PV(j) needs P(j).  The tensor pipe runs them in issue order.
+      int nq = 0, np = 0;
+      unsigned long long t0 = global_ns();
+      uint32_t idle = 0;
+      while (ok && np < ntiles) {
+        bool progressed = false;
+        if (nq < ntiles) {
+          const int rb = nq % kMRing;
+          if (test(&sm.tile_full[rb], (nq / kMRing) & 1) && (nq < 1 || test(&sm.s_free, (nq - 1) & 1))) {
+            tc_fence_after();
+            const uint32_t tile = tiles_a + rb * kMTileBytes;
+            const uint32_t tS = tmem + kMColS;
 #pragma unroll
-              for (int kk = 0; kk < 16; ++kk)
-                umma_f8_ts(tS, tQ + 8 * kk, desc_sw128(tile + (kk >> 2) * kMBlk + (kk & 3) * 32), id_qk,
-                           kk > 0 ? 1u : 0u);
+            for (int k0 = 0; k0 < 16; k0 += 4) {
+              uint32_t d4[4], a4[4];
+              uint64_t b4[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int kk = k0 + k;
+                d4[k] = tS;
+                a4[k] = tQ + 8 * kk;
+                b4[k] = desc_sw128(tile + (kk >> 2) * kMBlk + (kk & 3) * 32);
+              }
+              if (el) umma_f8_ts_x4(d4, a4, b4, id_qk, k0 > 0 ? 0xFu : 0xEu);
+            }
+            if (el) {
 #pragma unroll
               for (int kk = 0; kk < 2; ++kk)
                 umma_f8_ss(tS, desc_sw64(qr_a + 32 * kk), desc_sw64(tile + kMRopeOff + 32 * kk), id_qk, 1u);
               umma_commit(&sm.s_full);
               mla_trace(a.trace, kMlaEvQk, nq);
-              ++nq;
-              progressed = true;
             }
-          }
-          if (np < nq) {
-            const int rb = np % kMRing;
-            if (mbar_test(&sm.p_full[rb], (np / kMRing) & 1)) {
-              tc_fence_after();
-              const uint32_t vt = tiles_a + rb * kMTileBytes + half * 2 * kMBlk;
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                umma_f8_ss(tO, desc_sw128(p_a + rb * kMPBytes + 32 * kk), desc_mn128(vt + kk * 32 * 128, kMBlk),
-                           id_pv, (np > 0 || kk > 0) ? 1u : 0u);
-              umma_commit(&sm.pv_done[rb]);
-              mla_trace(a.trace, kMlaEvPv, np);
-              ++np;
-              progressed = true;
-            }
-          }
-          if (progressed) {
-            t0 = global_ns();
-            idle = 0;
-          } else if ((++idle & 63) == 0) {
-            if (*abort) ok = false;
-            else if (global_ns() - t0 > kWaitLimitNs) {
-              *abort = 1;
-              record_status(a.status, kTimeoutMma);
-              ok = false;
-            }
+            __syncwarp();
+            ++nq;
+            progressed = true;
           }
         }
-        // every issued MMA has completed before TMEM is released
-        umma_commit(&sm.fin);
-        mbar_wait(&sm.fin, 0, nullptr, a.status, kTimeoutMma);
+        if (np < nq) {
+          const int rb = np % kMRing;
+          if (test(&sm.p_full[rb], (np / kMRing) & 1)) {
+            tc_fence_after();
+            const uint32_t vt = tiles_a + rb * kMTileBytes + half * 2 * kMBlk;
+            uint32_t d4[4];
+            uint64_t a4[4], b4[4];
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              d4[kk] = tO;
+              a4[kk] = desc_sw128(p_a + rb * kMPBytes + 32 * kk);
+              b4[kk] = desc_mn128(vt + kk * 32 * 128, kMBlk);
+            }
+            if (el) {
+              umma_f8_ss_x4(d4, a4, b4, id_pv, np > 0 ? 0xFu : 0xEu);
+              umma_commit(&sm.pv_done[rb]);
+              mla_trace(a.trace, kMlaEvPv, np);
+            }
+            __syncwarp();
+            ++np;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          t0 = global_ns();
+          idle = 0;
+        } else if ((++idle & 63) == 0) {
+          if (__shfl_sync(0xffffffffu, *abort, 0)) {
+            ok = false;
+          } else if (__shfl_sync(0xffffffffu, static_cast<int>(global_ns() - t0 > kWaitLimitNs), 0)) {
+            if (lane == 0) {
+              *abort = 1;
+              record_status(a.status, kTimeoutMma);
+            }
+            ok = false;
+          }
+        }
       }
+      // every issued MMA has completed before TMEM is released
+      if (el) umma_commit(&sm.fin);
+      __syncwarp();
+      mbar_wait(&sm.fin, 0, nullptr, a.status, kTimeoutMma);
     } else if (warp == kMPrefetchWarp) {
       // ------------------------------------------------------------ warm L2 with the split's rows, in order
       const int p0 = tile0 * kMTile, p1 = min(a.topk, (tile0 + ntiles) * kMTile);

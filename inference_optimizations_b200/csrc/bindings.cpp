@@ -133,6 +133,48 @@ void index_key_write(const at::Tensor& k, const at::Tensor& slot, at::Tensor poo
                                      k.size(0), stream()));
 }
 
+void gqa_extend(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& page_table, const at::Tensor& blocks,
+                at::Tensor out, at::Tensor status, int64_t Hk, int64_t window, int64_t fmt, double sm_scale,
+                double k_scale, double v_scale, c10::optional<at::Tensor> trace) {
+  req(q, at::kBFloat16, "q");
+  req(pool, at::kByte, "pool");
+  req(page_table, at::kInt, "page_table");
+  req(blocks, at::kInt, "blocks");
+  req(out, at::kBFloat16, "out");
+  req(status, at::kInt, "status");
+  TORCH_CHECK(q.dim() == 3 && q.is_contiguous() && out.is_contiguous() && out.sizes() == q.sizes(), "q / out [rows, Hq, D]");
+  TORCH_CHECK(page_table.dim() == 2 && page_table.is_contiguous(), "page_table");
+  TORCH_CHECK(blocks.dim() == 2 && blocks.size(1) == 4 && blocks.is_contiguous(), "blocks [n, 4]");
+  TORCH_CHECK(pool.dim() == 4 && pool.size(1) == Hk && pool.size(2) == 2, "pool [pages, Hk, 2, part]");
+  iob::GqaExtendArgs a{};
+  a.q = q.data_ptr();
+  a.pool = pool.data_ptr<uint8_t>();
+  a.page_table = page_table.data_ptr<int>();
+  a.blocks = blocks.data_ptr<int>();
+  a.out = out.data_ptr();
+  a.status = status.data_ptr<int>();
+  a.nblocks = static_cast<int>(blocks.size(0));
+  a.Hq = static_cast<int>(q.size(1));
+  a.Hk = static_cast<int>(Hk);
+  a.D = static_cast<int>(q.size(2));
+  a.pt_stride = static_cast<int>(page_table.size(1));
+  a.page = 64;
+  a.window = static_cast<int>(window);
+  a.fmt = static_cast<int>(fmt);
+  a.pool_pages = static_cast<int>(pool.size(0));
+  a.sm_scale = static_cast<float>(sm_scale);
+  a.k_scale = static_cast<float>(k_scale);
+  a.v_scale = static_cast<float>(v_scale);
+  if (trace.has_value()) {
+    req(*trace, at::kLong, "trace");
+    TORCH_CHECK(trace->numel() >= 8 * 64, "trace [8 x 64]");
+    a.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
+  }
+  TORCH_CHECK(2 * pool.size(3) == iob::gqa_block_bytes(a.fmt, a.D, 64), "pool part bytes");
+  const at::cuda::CUDAGuard g(q.device());
+  CHECK_CUDA_OK(iob::gqa_extend(a, stream()));
+}
+
 void gqa_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& page_table,
                 c10::optional<at::Tensor> req_idx, const at::Tensor& kv_len, at::Tensor out, at::Tensor o_part, at::Tensor lse_part, at::Tensor status, int64_t n_q, int64_t Hk,
                 int64_t page, int64_t window, int64_t fmt, int64_t tiles_per_split, int64_t num_splits,
@@ -723,6 +765,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_align", &moe_align);
   m.def("moe_combine", &moe_combine);
   m.def("rmsnorm_quant", &rmsnorm_quant);
+  m.def("gqa_extend", &gqa_extend);
   m.def("act_quant", &act_quant);
   m.def("ep_dispatch", &ep_dispatch);
   m.def("ep_barrier", &ep_barrier);

@@ -457,6 +457,71 @@ __device__ __forceinline__ void umma_f8_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Batched issue: four kind::f8f6f4 MMAs in one asm statement.  Issued one per statement, consecutive tcgen05.mma
+// instructions measured ~150 cycles apart (~250 with a memory clobber) whatever the MMA shape; four per statement
+// issue at the tensor pipe's rate (a 128 x 256 x 32 E4M3 MMA every 128 cycles, 128 x 128 x 32 every 64).  MMA i
+// writes d[i]; MMA 0 accumulates iff acc0 != 0, MMAs 1-3 iff the matching bit of acc_mask (bit i) is set.
+__device__ __forceinline__ void umma_f8_ss_x4(const uint32_t (&d)[4], const uint64_t (&a)[4], const uint64_t (&b)[4],
+                                              uint32_t idesc, uint32_t acc_mask) {
+  asm volatile(
+      "{\n\t.reg .pred p0, p1, p2, p3;\n\t"
+      "setp.ne.b32 p0, %13, 0;\n\t"
+      "setp.ne.b32 p1, %14, 0;\n\t"
+      "setp.ne.b32 p2, %15, 0;\n\t"
+      "setp.ne.b32 p3, %16, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %4, %8, %12, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%1], %5, %9, %12, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%2], %6, %10, %12, p2;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%3], %7, %11, %12, p3;\n\t}\n" ::"r"(d[0]),
+      "r"(d[1]), "r"(d[2]), "r"(d[3]), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]),
+      "l"(b[3]), "r"(idesc), "r"(acc_mask & 1u), "r"(acc_mask & 2u), "r"(acc_mask & 4u), "r"(acc_mask & 8u));
+}
+// The same with A in TMEM (a[i] = TMEM address of MMA i's A columns).
+__device__ __forceinline__ void umma_f8_ts_x4(const uint32_t (&d)[4], const uint32_t (&a)[4], const uint64_t (&b)[4],
+                                              uint32_t idesc, uint32_t acc_mask) {
+  asm volatile(
+      "{\n\t.reg .pred p0, p1, p2, p3;\n\t"
+      "setp.ne.b32 p0, %13, 0;\n\t"
+      "setp.ne.b32 p1, %14, 0;\n\t"
+      "setp.ne.b32 p2, %15, 0;\n\t"
+      "setp.ne.b32 p3, %16, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%4], %8, %12, p0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%1], [%5], %9, %12, p1;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%2], [%6], %10, %12, p2;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%3], [%7], %11, %12, p3;\n\t}\n" ::"r"(d[0]),
+      "r"(d[1]), "r"(d[2]), "r"(d[3]), "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]),
+      "l"(b[3]), "r"(idesc), "r"(acc_mask & 1u), "r"(acc_mask & 2u), "r"(acc_mask & 4u), "r"(acc_mask & 8u));
+}
+// Four K steps of one accumulation into d, one asm statement: MMA k reads A at a0 + k SA and B at b0 + k SB (the
+// descriptors' address fields, 16-byte units, advanced inside the statement so only two descriptors cross into
+// it).  MMA 0 accumulates iff acc0 != 0; MMAs 1-3 accumulate.
+template <int SA, int SB>
+__device__ __forceinline__ void umma_f8_ss_k4(uint32_t d, uint64_t a0, uint64_t b0, uint32_t idesc, uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\tsetp.eq.u32 q, 0, 0;\n\t"
+      "add.s64 a1, %1, %5;\n\tadd.s64 a2, %1, %6;\n\tadd.s64 a3, %1, %7;\n\t"
+      "add.s64 b1, %2, %8;\n\tadd.s64 b2, %2, %9;\n\tadd.s64 b3, %2, %10;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a1, b1, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a2, b2, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], a3, b3, %3, q;\n\t}\n" ::"r"(d),
+      "l"(a0), "l"(b0), "r"(idesc), "r"(acc0), "n"(SA), "n"(2 * SA), "n"(3 * SA), "n"(SB), "n"(2 * SB), "n"(3 * SB));
+}
+// The same with A in TMEM: MMA k reads A columns a0 + k SA.
+template <int SA, int SB>
+__device__ __forceinline__ void umma_f8_ts_k4(uint32_t d, uint32_t a0, uint64_t b0, uint32_t idesc, uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t.reg .b32 a1, a2, a3;\n\t.reg .b64 b1, b2, b3;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\tsetp.eq.u32 q, 0, 0;\n\t"
+      "add.s32 a1, %1, %5;\n\tadd.s32 a2, %1, %6;\n\tadd.s32 a3, %1, %7;\n\t"
+      "add.s64 b1, %2, %8;\n\tadd.s64 b2, %2, %9;\n\tadd.s64 b3, %2, %10;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [a1], b1, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [a2], b2, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [a3], b3, %3, q;\n\t}\n" ::"r"(d),
+      "r"(a0), "l"(b0), "r"(idesc), "r"(acc0), "n"(SA), "n"(2 * SA), "n"(3 * SA), "n"(SB), "n"(2 * SB), "n"(3 * SB));
+}
 // Warp w writes TMEM lanes 32(w%4)..+31; thread t writes lane 32(w%4)+t, columns [col, col+16).
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
   asm volatile(

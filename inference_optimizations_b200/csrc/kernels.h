@@ -89,6 +89,21 @@ struct GqaDecodeArgs {
 };
 cudaError_t gqa_decode(const GqaDecodeArgs& a, cudaStream_t s);
 
+// ---- GQA-packed extend / prefill attention (attn_gqa_extend.cu): 128 query rows (BT = 128 / G tokens x G heads)
+// of one kv head per CTA over an NVFP4 / FP8 pool, causal + sliding window.
+struct GqaExtendArgs {
+  const void* q;           // bf16 [rows, Hq, D] query tokens (normed + roped)
+  const uint8_t* pool;     // layer pool [num_pages, Hk, 2 parts (K, V), part_bytes]
+  const int* page_table;   // [requests, pt_stride]
+  const int* blocks;       // [nblocks, 4]: first q row, tokens (1..128 / G), position of the first token, page-table row
+  void* out;               // bf16 [rows, Hq, D]; rows outside every block are not written
+  int* status;             // device status word (bounded-wait timeouts, bad page ids)
+  int nblocks, Hq, Hk, D, pt_stride, page, window, fmt, pool_pages;
+  float sm_scale, k_scale, v_scale;
+  long long* trace;        // optional [8 events x 64 tiles] clock64 timeline of CTA (0, 0, 0) (diagnostics), else null
+};
+cudaError_t gqa_extend(const GqaExtendArgs& a, cudaStream_t s);
+
 // ---- sparse MLA decode (attn_mla_decode.cu): DSA attention over gathered latent rows, H <= 128 heads.
 struct MlaDecodeArgs {
   const void* q;           // bf16 [T, H, 576] (512 latent dims then 64 rope dims), quantized first into q8_out, or null

@@ -163,7 +163,118 @@ __global__ void __launch_bounds__(128) umma_rate_kernel(int n, int count, int na
       out[0] = c1 - c0;
       out[1] = c2 - c0;
     }
-  } else if (variant != 10 && lane_id() == 0 && warp_id() < issuers) {
+  } else if ((variant == 11 || variant == 12) && threadIdx.x == 0) {
+    // E4M3 K-major, descriptors and predicate hoisted; 11: one MMA per asm statement without a memory clobber,
+    // 12: four MMAs per asm statement
+    const uint32_t idesc = idesc_dense(0, 0, 128, n);
+    const uint64_t a = desc_sw128(smem_u32(smem)), b = desc_sw128(smem_u32(smem + 16384));
+    const long long c0 = clock64();
+    if (variant == 11) {
+      for (int i = 0; i < count; ++i) {
+        const uint32_t d = t + (i % nacc) * n;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+            "l"(a), "l"(b), "r"(idesc), "r"(1u));
+      }
+    } else {
+      for (int i = 0; i < count; i += 4) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(t),
+            "l"(a), "l"(b), "r"(idesc), "r"(1u));
+      }
+    }
+    const long long c1 = clock64();
+    umma_commit(&bar[0]);
+    mbar_wait(&bar[0], 0, nullptr, nullptr, 0);
+    const long long c2 = clock64();
+    out[0] = c1 - c0;
+    out[1] = c2 - c0;
+  } else if ((variant == 13 || variant == 14) && threadIdx.x == 0) {
+    // batched helpers with distinct operands per MMA (K steps of a 128 B slab), 13: A in smem, 14: A in TMEM
+    const uint32_t idesc = idesc_dense(0, 0, 128, n);
+    const long long c0 = clock64();
+    for (int i = 0; i < count; i += 4) {
+      uint32_t d[4];
+      uint64_t a[4], b[4];
+      uint32_t at[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        d[k] = t + ((i / 4) % nacc) * n;
+        a[k] = desc_sw128(smem_u32(smem) + 32 * k);
+        b[k] = desc_sw128(smem_u32(smem + 16384) + 32 * k);
+        at[k] = t + 256 + 8 * k;
+      }
+      if (variant == 13) umma_f8_ss_x4(d, a, b, idesc, 0xFu);
+      else umma_f8_ts_x4(d, at, b, idesc, 0xFu);
+    }
+    const long long c1 = clock64();
+    umma_commit(&bar[0]);
+    mbar_wait(&bar[0], 0, nullptr, nullptr, 0);
+    const long long c2 = clock64();
+    out[0] = c1 - c0;
+    out[1] = c2 - c0;
+  } else if (variant >= 17 && variant <= 19 && warp_id() == 0) {
+    // K-step batches: descriptors advanced inside the statement (17: one lane issues; 18: converged warp + elect;
+    // 19: converged warp + elect, A in TMEM)
+    const uint32_t idesc = idesc_dense(0, 0, 128, n);
+    const uint64_t a = desc_sw128(smem_u32(smem)), b = desc_sw128(smem_u32(smem + 16384));
+    const long long c0 = clock64();
+    for (int i = 0; i < count; i += 4) {
+      const uint32_t d = t + ((i / 4) % nacc) * n;
+      if (variant == 17) {
+        if (lane_id() == 0) umma_f8_ss_k4<2, 2>(d, a, b, idesc, 1u);
+      } else if (elect_one()) {
+        if (variant == 18) umma_f8_ss_k4<2, 2>(d, a, b, idesc, 1u);
+        else umma_f8_ts_k4<8, 2>(d, t + 256, b, idesc, 1u);
+      }
+      __syncwarp();
+    }
+    const long long c1 = clock64();
+    if (elect_one()) umma_commit(&bar[0]);
+    __syncwarp();
+    mbar_wait(&bar[0], 0, nullptr, nullptr, 0);
+    const long long c2 = clock64();
+    if (threadIdx.x == 0) {
+      out[0] = c1 - c0;
+      out[1] = c2 - c0;
+    }
+  } else if ((variant == 15 || variant == 16) && warp_id() == 0) {
+    // whole warp converged, operands computed by every lane, one elected lane issues batched MMAs
+    // (15: four per statement, distinct K-step descriptors; 16: the same with A in TMEM)
+    const uint32_t idesc = idesc_dense(0, 0, 128, n);
+    const uint32_t sa = smem_u32(smem), sb = smem_u32(smem + 16384);
+    const long long c0 = clock64();
+    for (int i = 0; i < count; i += 4) {
+      uint32_t d[4], at[4];
+      uint64_t a[4], b[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        d[k] = t + ((i / 4) % nacc) * n;
+        a[k] = desc_sw128(sa + 32 * k);
+        b[k] = desc_sw128(sb + 32 * k);
+        at[k] = t + 256 + 8 * k;
+      }
+      if (elect_one()) {
+        if (variant == 15) umma_f8_ss_x4(d, a, b, idesc, 0xFu);
+        else umma_f8_ts_x4(d, at, b, idesc, 0xFu);
+      }
+      __syncwarp();
+    }
+    const long long c1 = clock64();
+    if (elect_one()) umma_commit(&bar[0]);
+    __syncwarp();
+    mbar_wait(&bar[0], 0, nullptr, nullptr, 0);
+    const long long c2 = clock64();
+    if (threadIdx.x == 0) {
+      out[0] = c1 - c0;
+      out[1] = c2 - c0;
+    }
+  } else if (variant != 10 && variant < 11 && lane_id() == 0 && warp_id() < issuers) {
     const int m = (variant == 5 || variant == 9) ? 64 : 128;
     const bool f8 = variant == 3 || variant >= 7;
     uint32_t idesc = f8 ? idesc_dense(0, 0, m, n) : idesc_dense(1, 1, m, n);

@@ -203,6 +203,12 @@ class GQARunner:
             check_gqa_pack(p, self.kv, self.max_running + 1)
         return p
 
+    def _ext_segs(self, p: Packed) -> Optional[list]:
+        """Prefill segments for the extend kernel: (first q row, real tokens, first position, page-table row)."""
+        if not self.ecfg.extend_kernel:
+            return None
+        return [(r0, len(s.tokens), s.start, s.req.slot) for s, r0 in p.seg_rows]
+
     # ------------------------------------------------------------------------------------------ forward pieces
     def _target(self, st: StepTensors):
         return self.model.forward(st, self.kv)
@@ -227,6 +233,7 @@ class GQARunner:
         self.stage.upload()
         st = self.stage.step_tensors(len(p.ids), len(p.kv_len), p.n_q,
                                      {"global": (1, 1 << 20), "swa": (1, 1 << 20), "draft": (1, 1 << 20)})
+        st.ext_segs = self._ext_segs(p)
         x, resid = self._target(st)
         rows = torch.tensor(p.logit_rows, dtype=torch.long, device=self.device)
         res = {}
@@ -266,6 +273,7 @@ class GQARunner:
             self.stage.upload()
             st = self.stage.step_tensors(len(p.ids), len(p.kv_len), p.n_q,
                                          {"global": (1, 1 << 20), "swa": (1, 1 << 20), "draft": (1, 1 << 20)})
+            st.ext_segs = self._ext_segs(p)
             x, _ = self._target(st)
             rows = torch.arange(len(tokens), device=self.device)
             return self.model.logits_local(x[rows], self.model.embed).float().cpu()
@@ -456,7 +464,7 @@ class GQARunner:
         emb = B.embed(st.ids, self.model.embed, self.model.embed_scale)
         x0 = torch.nn.functional.linear(torch.cat([emb, hprev], dim=-1), d.fc)
         st_d = StepTensors(st.ids, st.pos, {"draft": st.slot["draft"]}, st.kv_len, st.req_idx, st.n_q,
-                           {"draft": st.splits.get("draft")})
+                           {"draft": st.splits.get("draft")}, st.ext_segs, st.ext_cache)
         return d.forward(st_d, self.kv, layer_offset=self.cfg.num_layers, inputs_embeds=x0)
 
     def _draft_logits_argmax(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:

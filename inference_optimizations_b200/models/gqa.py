@@ -178,9 +178,15 @@ class GQAModel:
         slot = st.slot[g.kind]
         q = K.gqa_prep(qkv, w.q_norm if cfg.qk_norm else None, w.k_norm if cfg.qk_norm else None, cs, st.pos, slot,
                        pool, kv.fmt, g.q_heads, g.kv_heads, g.head_dim, eps, True, kv.k_scale, kv.v_scale)
-        attn = A.gqa_decode(q, pool, kv.tables[g.kind].dev, st.kv_len, st.n_q, g.kv_heads, kv.fmt,
-                            1.0 / math.sqrt(g.head_dim), g.window, kv.k_scale, kv.v_scale,
-                            splits=st.splits.get(g.kind), ws=kv.workspace(g.head_dim, g.kv_heads), req_idx=st.req_idx)
+        if st.ext_segs is not None and kv.fmt != K.FMT_BF16 and g.head_dim in (256, 512) and q.is_cuda:
+            attn = A.gqa_extend(q, pool, kv.tables[g.kind].dev, st.ext_blocks(g.q_heads // g.kv_heads, q.device),
+                                g.kv_heads, kv.fmt, 1.0 / math.sqrt(g.head_dim), g.window, kv.k_scale, kv.v_scale,
+                                status=kv.ext_status)
+        else:
+            attn = A.gqa_decode(q, pool, kv.tables[g.kind].dev, st.kv_len, st.n_q, g.kv_heads, kv.fmt,
+                                1.0 / math.sqrt(g.head_dim), g.window, kv.k_scale, kv.v_scale,
+                                splits=st.splits.get(g.kind), ws=kv.workspace(g.head_dim, g.kv_heads),
+                                req_idx=st.req_idx)
         if self.tp > 1 and self.tp_comm is not None and attn.shape[0] <= self.tp_comm.rows_cap:
             # row-parallel GEMMs write their partials into the symmetric buffer; one kernel reduces over NVLink and
             # applies post-norm, residual add and the next pre-norm
@@ -255,6 +261,18 @@ class StepTensors:
     req_idx: torch.Tensor             # int32 [B] page-table row per group
     n_q: int
     splits: dict = field(default_factory=dict)   # kind -> (num_splits, tiles_per_split) or None
+    # prefill: [(first q row, real tokens, position of the first token, page-table row)] per segment; attention then
+    # runs the GQA-packed extend kernel over NVFP4 / FP8 pools (block lists cached per group size G)
+    ext_segs: Optional[list] = None
+    ext_cache: dict = field(default_factory=dict)
+
+    def ext_blocks(self, g: int, device) -> torch.Tensor:
+        if g not in self.ext_cache:
+            blk = A.extend_blocks(self.ext_segs, g)
+            t = torch.tensor(blk, dtype=torch.int32).reshape(-1, 4)
+            self.ext_cache[g] = t.pin_memory().to(device, non_blocking=True) if torch.device(device).type == "cuda" \
+                else t
+        return self.ext_cache[g]
 
 
 class GQAKVCache:
@@ -290,6 +308,7 @@ class GQAKVCache:
             self.alloc["draft"] = PageAllocator(draft_pages)
             self.tables["draft"] = PageTable(max_requests, max_pages, device)
         self._ws = {}
+        self.ext_status = torch.zeros(1, dtype=torch.int32, device=device)
 
     def workspace(self, d: int, hk: int) -> Optional[A.DecodeWorkspace]:
         return self._ws.get((d, hk))

@@ -2,7 +2,9 @@
 oracle.  Semantics of the reference's grouped decode and split-K verify (`attention/verify-splitk/gemma31_verify.py:1-24`,
 `kv-cache-4bit/kv4tri-triton-backend/kv4tri_nvfp4_attention.py:257`): request b has kv_len[b] tokens in the pool, the
 last n_q of which are its query tokens; query token t sees key positions p <= q_pos(t) and, with a sliding window W,
-only q_pos(t) - p < W (W = 1024 on Gemma sliding layers: each query sees 1024 keys including itself)."""
+only q_pos(t) - p < W (W = 1024 on Gemma sliding layers: each query sees 1024 keys including itself).
+Prefill chunks over NVFP4 / FP8 pools run the GQA-packed extend kernel (csrc/attn_gqa_extend.cu, `gqa_extend`): 128
+query rows (128 / G tokens x G heads) per kv head and CTA, the reference's `attention/extend-gqa` capability."""
 from __future__ import annotations
 
 import math
@@ -107,6 +109,49 @@ def gqa_decode_ref(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor
             pr = torch.softmax(s, dim=-1)
             out[i * n_q + t] = torch.einsum("hn,nhd->hd", pr, vv[vis])
     return out.to(q.device)
+
+
+def extend_blocks(segments: list, g: int) -> list:
+    """Extend-kernel work list for prefill segments [(first q row, tokens, position of the first token, page-table
+    row)]: each segment is cut into blocks of 128 / G consecutive tokens (128 query rows of one kv head)."""
+    bt = 128 // g
+    out = []
+    for r0, n, p0, row in segments:
+        for o in range(0, n, bt):
+            out.append((r0 + o, min(bt, n - o), p0 + o, row))
+    return out
+
+
+def gqa_extend(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor, blocks: torch.Tensor, hk: int,
+               fmt: int, sm_scale: float, window: int = 0, k_scale: float = 1.0, v_scale: float = 1.0,
+               out: Optional[torch.Tensor] = None, status: Optional[torch.Tensor] = None,
+               trace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Prefill attention of the query tokens listed in `blocks` (int32 [n, 4] from `extend_blocks`) over the paged
+    NVFP4 / FP8 pool: q bf16 [rows, Hq, D] -> out [rows, Hq, D] (rows outside every block are left as they are).
+    Row t of block (r0, n, p0, req) is the token at position p0 + t; it sees pool positions <= p0 + t (and > p0 + t -
+    window).  E4M3 tensor-core operands (Q per-row scale, K, V, P), fp32 accumulation."""
+    if out is None:
+        out = torch.zeros_like(q)
+    if not q.is_cuda:
+        out.copy_(gqa_extend_ref(q, pool, page_table, blocks, hk, fmt, sm_scale, window, k_scale, v_scale, out))
+        return out
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=q.device)
+    ext().gqa_extend(q, pool, page_table, blocks, out, status, hk, window, fmt, sm_scale, k_scale, v_scale, trace)
+    return out
+
+
+def gqa_extend_ref(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor, blocks: torch.Tensor, hk: int,
+                   fmt: int, sm_scale: float, window: int = 0, k_scale: float = 1.0, v_scale: float = 1.0,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp32 oracle of `gqa_extend` (dense attention over the dequantized pool)."""
+    res = (out.float().cpu().clone() if out is not None else torch.zeros(q.shape, dtype=torch.float32))
+    for r0, n, p0, row in blocks.tolist():
+        kv_n = p0 + n
+        k, v = gqa_pool_read_ref(pool, page_table[row].cpu(), kv_n, fmt, q.shape[2], k_scale, v_scale)
+        res[r0:r0 + n] = dense_attention_ref(q[r0:r0 + n].cpu(), k, v, sm_scale, torch.arange(p0, p0 + n),
+                                             torch.arange(kv_n), window)
+    return res
 
 
 def dense_attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: float, q_pos: torch.Tensor,

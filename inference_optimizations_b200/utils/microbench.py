@@ -73,6 +73,55 @@ def gqa_decode_case(b: int, hk: int, hq: int, d: int, ctx: int, fmt_name: str, n
             "gbs": round(nbytes / us / 1e3, 1), "frac_hbm": round(nbytes / us / 1e3 / PEAKS["hbm_gbs"], 3)}
 
 
+def gqa_extend_case(chunk: int, ctx: int, hk: int, hq: int, d: int, fmt_name: str, window: int,
+                    launches: int = 0) -> dict:
+    """One prefill chunk of `chunk` tokens ending at position ctx (prefix ctx - chunk) through the extend kernel,
+    against the same chunk through the decode kernel in n_q-token groups (the prefill path before the extend kernel)."""
+    from ..engine.synthetic import fill_pool_random
+    from ..ops import attention as A
+    from ..ops import kvcache as K
+    dev = torch.device("cuda:0")
+    fmt = K.FMT_IDS[fmt_name]
+    per = (ctx + 63) // 64 + 1
+    pool = torch.empty(per + 1, hk, 2, K.part_bytes(fmt, d), dtype=torch.uint8, device=dev)
+    fill_pool_random(pool, fmt, d, 1)
+    pt = (torch.randperm(per, device=dev) + 1).view(1, per).int()
+    g = hq // hk
+    p0 = ctx - chunk
+    q = torch.randn(chunk, hq, d, device=dev).to(torch.bfloat16)
+    blocks = torch.tensor(A.extend_blocks([(0, chunk, p0, 0)], g), dtype=torch.int32, device=dev)
+    out = torch.zeros_like(q)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    sm = 1 / math.sqrt(d)
+
+    def fn():
+        A.gqa_extend(q, pool, pt, blocks, hk, fmt, sm, window, out=out, status=status)
+    if launches:
+        for _ in range(launches):
+            fn()
+        torch.cuda.synchronize()
+        return {}
+    us = _time_flushed(fn)
+    n_q = max(1, 16 // g)
+    groups = chunk // n_q
+    kvl = (p0 + n_q * torch.arange(1, groups + 1, device=dev)).int()
+    rix = torch.zeros(groups, dtype=torch.int32, device=dev)
+    splits = (1, 1 << 20)
+    ws = A.DecodeWorkspace.allocate(groups, hk, 1, d, device=dev)
+    qd = q[: groups * n_q].contiguous()
+
+    def fn_dec():
+        A.gqa_decode(qd, pool, pt, kvl, n_q, hk, fmt, sm, window, splits=splits, ws=ws, req_idx=rix)
+    us_dec = _time_flushed(fn_dec)
+    vis = sum(min(p + 1, window) if window else p + 1 for p in range(p0, ctx))
+    flops = 4.0 * hq * d * vis
+    peak_f8 = 2 * PEAKS["bf16_tflops"]
+    return {"kernel": "gqa_extend", "chunk": chunk, "ctx": ctx, "hk": hk, "hq": hq, "d": d, "fmt": fmt_name,
+            "window": window, "blocks": int(blocks.shape[0]), "us": round(us, 2),
+            "tflops": round(flops / us / 1e6, 1), "frac_f8_peak": round(flops / us / 1e6 / peak_f8, 3),
+            "decode_path_us": round(us_dec, 2), "speedup_vs_decode_path": round(us_dec / us, 2)}
+
+
 def _time_flushed(fn, iters: int = 10) -> float:
     """Mean device time of fn over `iters` launches, L2 flushed (a 256 MB write) before each, flush not timed."""
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
@@ -381,6 +430,7 @@ def main() -> None:
     p.add_argument("--ctx", type=int, default=8192)
     p.add_argument("--fmt", default="nvfp4")
     p.add_argument("--nq", type=int, default=1)
+    p.add_argument("--chunk", type=int, default=2048)
     p.add_argument("--window", type=int, default=0)
     p.add_argument("--topk", type=int, default=2048)
     p.add_argument("--launches", type=int, default=0)
@@ -392,6 +442,8 @@ def main() -> None:
     a = p.parse_args()
     if a.kernel == "gqa_decode":
         r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches)
+    elif a.kernel == "gqa_extend":
+        r = gqa_extend_case(a.chunk, a.ctx, a.hk, a.hq, a.d, a.fmt, a.window, a.launches)
     elif a.kernel == "indexer":
         r = indexer_case(a.b, a.ctx, a.topk, launches=a.launches)
     elif a.kernel == "moe_tactics":

@@ -267,3 +267,38 @@ def test_indexer_scores_and_topk(cuda, hi, topk):
     # selection is exact against the oracle run on the kernel's own scores
     rs, rp = I.topk_ref(got, limit, topk, pt)
     assert torch.equal(pos.cpu(), rp) and torch.equal(slots.cpu(), rs)
+
+
+@pytest.mark.parametrize("fmt", [K.FMT_NVFP4, K.FMT_FP8])
+@pytest.mark.parametrize("d,window", [(512, 0), (256, 96), (256, 0), (512, 200)])
+def test_gqa_extend(cuda, fmt, d, window):
+    """Prefill blocks (with a cached prefix, several requests, a partial last block) against the fp32 oracle."""
+    hq, hk = 4, 2
+    lens = [300, 77, 700]          # tokens in the pool per request; the last `new` of each are the query tokens
+    new = [300, 77, 150]           # request 0: prefill from position 0; request 2: 550-token prefix
+    scale = (0.5, 0.25) if fmt == K.FMT_FP8 else (1.0, 1.0)
+    pool, pt, _ = _build_pool(cuda, fmt, d, hk, lens, scale, seed=3)
+    segs, r0 = [], 0
+    for i, (n, m) in enumerate(zip(lens, new)):
+        segs.append((r0, m, n - m, i))
+        r0 += m + 5                # gaps: rows outside every block stay untouched
+    q = torch.randn(r0, hq, d, device=cuda).to(torch.bfloat16)
+    blocks = torch.tensor(A.extend_blocks(segs, hq // hk), dtype=torch.int32, device=cuda)
+    sm = 1.0 / math.sqrt(d)
+    out = torch.full_like(q, 7.0)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    A.gqa_extend(q, pool, pt, blocks, hk, fmt, sm, window, *scale, out=out, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ref = A.gqa_extend_ref(q.cpu(), pool.cpu(), pt.cpu(), blocks.cpu(), hk, fmt, sm, window, *scale,
+                           out=torch.full(q.shape, 7.0))
+    tol = 0.06 * max(1.0, ref.abs().max().item())
+    err = (out.cpu().float() - ref).abs().max().item()
+    assert err < tol, err
+    # the decode kernel over the same tokens (n_q = 1 per token) agrees to the same tolerance
+    for s0, m, p0, i in segs[2:]:
+        kvl = torch.arange(p0 + 1, p0 + m + 1, dtype=torch.int32, device=cuda)
+        rix = torch.full((m,), i, dtype=torch.int32, device=cuda)
+        dec = A.gqa_decode(q[s0:s0 + m].contiguous(), pool, pt, kvl, 1, hk, fmt, sm, window, *scale, req_idx=rix)
+        torch.cuda.synchronize()
+        assert (dec.float() - out[s0:s0 + m].float()).abs().max().item() < tol

@@ -130,3 +130,28 @@ def test_act_quant_ref_roundtrip():
     d4 = MG.dequant_nvfp4_rows(q4, s4)
     a4 = B.act_mul(gu, False).float()
     assert (d4 - a4).abs().max() <= a4.abs().max() / 3
+
+
+def test_extend_blocks_and_oracle_match_decode_oracle():
+    """The extend work list covers every prefill token once, and the extend oracle equals the decode oracle run
+    token by token over the same pool."""
+    import math
+    import torch
+    from inference_optimizations_b200.ops import attention as A
+    from inference_optimizations_b200.ops import kvcache as K
+    assert A.extend_blocks([(0, 150, 10, 3)], 2) == [(0, 64, 10, 3), (64, 64, 74, 3), (128, 22, 138, 3)]
+    torch.manual_seed(0)
+    d, hk, hq, n = 128, 1, 2, 90
+    pool = torch.zeros(4, hk, 2, K.part_bytes(K.FMT_FP8, d), dtype=torch.uint8)
+    pt = torch.tensor([[2, 0]], dtype=torch.int32)
+    k = torch.randn(n, hk, d).to(torch.bfloat16).float()
+    v = torch.randn(n, hk, d).to(torch.bfloat16).float()
+    pos = torch.arange(n)
+    K.gqa_pool_write_ref(pool, pt[0][pos // 64].long() * 64 + pos % 64, k, v, K.FMT_FP8)
+    q = torch.randn(30, hq, d).to(torch.bfloat16)
+    blocks = torch.tensor(A.extend_blocks([(0, 30, 60, 0)], hq // hk), dtype=torch.int32)
+    for w in (0, 17):
+        ext = A.gqa_extend_ref(q, pool, pt, blocks, hk, K.FMT_FP8, 1 / math.sqrt(d), w)
+        dec = A.gqa_decode_ref(q, pool, pt.repeat(30, 1), torch.arange(61, 91, dtype=torch.int32), 1, hk, K.FMT_FP8,
+                               1 / math.sqrt(d), w)
+        assert torch.allclose(ext, dec, atol=1e-5)
