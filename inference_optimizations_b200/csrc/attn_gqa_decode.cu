@@ -790,8 +790,12 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
   auto parts_before = [&](int j) { return min(j, ntiles) + max(0, j - 1); };
   auto part_index = [&](int j, int which) { return parts_before(j) + ((which == 1 && j < ntiles) ? 1 : 0); };
 
+  // register split (per thread): softmax kSmRegs, dequant 72, producer / issuers kIssRegs; 128 kSmRegs + 512 x 72 +
+  // 128 kIssRegs = 61440 = the 768 x 80 the block is launched with.  The batched MMA issue needs more than 32.
+  constexpr uint32_t kSmRegs = RMAX > 8 ? 160 : 136, kIssRegs = RMAX > 8 ? 32 : 56;
+  static_assert(128 * kSmRegs + 512 * 72 + 128 * kIssRegs == kThreadsF8 * 80, "register split");
   if (warp < kSoftmaxWarps) {
-    regs_inc<160>();
+    regs_inc<kSmRegs>();
     const float base_scale = a.sm_scale * a.k_scale * 1.4426950408889634f;
     const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
     float acc[MB][RMAX];
@@ -1154,7 +1158,7 @@ __global__ void __launch_bounds__(kThreadsF8, 1) gqa_decode_f8_kernel(const GqaD
       if (dw == 0 && lane == 0) trace_ev(a.trace, kEvVDeqEnd, i);
     }
   } else {
-    regs_dec<32>();
+    regs_dec<kIssRegs>();
     if (warp == kProducerWarpF8) {
     if (lane == 0) {
       const uint8_t* pool = a.pool;

@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gqa_extend_kernel(const GqaExten
   if (threadIdx.x == 0) x_trace(a.trace, kXEvStart, 0);
 
   if (warp < kXSoftmaxWarps) {
-    regs_inc<200>();   // 128 x 200 (softmax) + 256 x 128 (dequant, unchanged) + 128 x 48 = 512 x 128 launched
+    regs_inc<200>();   // 128 x 200 (softmax) + 256 x 128 (dequant, unchanged) + 128 x 56 = 512 x 128 launched
     // ------------------------------------------------------------------ softmax: thread = row = TMEM lane
     const int qd = warp & 3;
     const int r = 32 * qd + lane;
@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(kXThreads, 1) gqa_extend_kernel(const GqaExten
       }
     }
   } else {
-    regs_dec<48>();
+    regs_dec<56>();
     if (warp == kXMmaWarp) {
       // ---------------------------------------------------------------- MMA issue: the whole warp runs the loop
       // (warp-uniform descriptor arithmetic), one elected lane issues four MMAs per asm statement

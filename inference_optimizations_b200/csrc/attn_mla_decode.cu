@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
   if (threadIdx.x == 0) mla_trace(a.trace, kMlaEvStart, 0);
 
   if (warp < kMSoftmaxWarps) {
-    regs_inc<200>();   // 128 x 200 (softmax) + 256 x 128 (dequant, unchanged) + 128 x 48 = 512 x 128 launched
+    regs_inc<200>();   // 128 x 200 (softmax) + 256 x 128 (dequant, unchanged) + 128 x 56 = 512 x 128 launched
     // ---------------------------------------------------------------- softmax: thread = head = TMEM lane
     const int qd = warp & 3, ch = 0;             // lane quadrant; one warp covers all S columns
     const int h = 32 * qd + lane;
@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
       }
     }
   } else {
-    regs_dec<48>();
+    regs_dec<56>();
     if (warp == kMMmaWarp) {
       // ------------------------------------------------------------ MMA issue: the whole warp runs the loop
       // (warp-uniform descriptor arithmetic), one elected lane issues the MMAs, four per asm statement
