@@ -91,6 +91,28 @@ __device__ __forceinline__ uint2 bf16x8_to_e4m3(const uint4& v, float inv) {
   return make_uint2(o[0], o[1]);
 }
 
+// f16x2 helpers for the softmax (value `lo` in the low half)
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
+  uint32_t r;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
+__device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint16_t h2_to_e4m3x2(uint32_t h2) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(h2));
+  return r;
+}
+
 __device__ __forceinline__ float bf16x8_amax(const uint4& v, float m) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -99,8 +121,9 @@ __device__ __forceinline__ float bf16x8_amax(const uint4& v, float m) {
   return m;
 }
 
-// Diagnostic timeline of CTA (0, 0, 0): clock64 per event and tile, [event][tile] for the first 64 tiles.
-enum ExtTraceEv { kXEvQk, kXEvPv, kXEvSSeen, kXEvPReady, kXEvDeqStart, kXEvDeqEnd, kXEvStart, kXEvEnd };
+// Diagnostic timeline of CTA (0, 0, 0): clock64 per event and tile, [kXEvCount][64] for the first 64 tiles.
+enum ExtTraceEv { kXEvQk, kXEvPv, kXEvSSeen, kXEvPReady, kXEvDeqStart, kXEvDeqEnd, kXEvStart, kXEvEnd, kXEvMax,
+                  kXEvPFree, kXEvSLoaded, kXEvPWritten, kXEvCount };
 __device__ __forceinline__ void x_trace(long long* tr, int ev, int j) {
   if (tr != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && j < 64) tr[ev * 64 + j] = clock64();
 }
@@ -221,23 +244,32 @@ __global__ void __launch_bounds__(kXThreads, 1) gqa_extend_kernel(const GqaExten
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.s_free);
-      // s = S * scale on columns inside [lo, hi] (causal: kv <= pos; window: kv > pos - W), -inf elsewhere
+      if (r == 0) x_trace(a.trace, kXEvSLoaded, j);
+      // columns inside [lo, hi] are visible (causal: kv <= pos; window: kv > pos - W).  Interior tiles (every row
+      // sees every column) skip the mask; masked scores become -inf.  The max is taken on the raw scores (the
+      // scale sc2 > 0 is applied to the max, and folded into one FFMA per score below).
       const int kv0 = t0 + j * kXTile;
       const int hi = live ? pos - kv0 : -1;
       const int lo = a.window > 0 ? pos - a.window + 1 - kv0 : -(1 << 30);
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (__all_sync(0xffffffffu, hi >= kXTile - 1 && lo <= 0)) {
 #pragma unroll
-      for (int c = 0; c < kXTile; ++c) {
-        const float v = (c <= hi && c >= lo) ? __uint_as_float(sr[c]) * sc2 : -INFINITY;
-        sr[c] = __float_as_uint(v);
-        mx[c & 3] = fmaxf(mx[c & 3], v);
+        for (int c = 0; c < kXTile; ++c) mx[c & 3] = fmaxf(mx[c & 3], __uint_as_float(sr[c]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < kXTile; ++c) {
+          if (!(c <= hi && c >= lo)) sr[c] = __float_as_uint(-INFINITY);
+          mx[c & 3] = fmaxf(mx[c & 3], __uint_as_float(sr[c]));
+        }
       }
-      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      const float mraw = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      const float mt = mraw * sc2;
       const bool first = (m_ref == -INFINITY) && (mt > -INFINITY);
       const bool grow = (m_ref > -INFINITY) && (mt > m_ref + kXTau);
       const float alpha = grow ? ex2x(m_ref - mt) : 1.f;
       if (first || grow) m_ref = mt;
       l *= alpha;
+      if (r == 0) x_trace(a.trace, kXEvMax, j);
       if (__any_sync(0xffffffffu, grow) && j > 0) {
         // O must hold PV(j - 1) before it is rescaled
         if (!wwait(&sm.pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) { ok = false; break; }
@@ -259,27 +291,34 @@ __global__ void __launch_bounds__(kXThreads, 1) gqa_extend_kernel(const GqaExten
         if (!wwait(&sm.pv_done[jj & 1], (jj >> 1) & 1)) { ok = false; break; }
       }
       const int pb = NP == 1 ? 0 : (j & 1);
+      if (r == 0) x_trace(a.trace, kXEvPFree, j);
       uint8_t* prow = sp + pb * kXPBytes + r * 128;   // SW128 row of 128 P columns
+      // P = 2^(S sc2 - m) <= 2^tau: two values per f16x2 exp2 (P is E4M3 anyway), row sums in f16x2 per 16-column
+      // chunk, then fp32
       float lsum[4] = {0.f, 0.f, 0.f, 0.f};
       const bool any = m_ref > -INFINITY;
       const float nm = any ? -m_ref : 0.f;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t w[4];
+        uint32_t hs = 0;                                   // f16x2 partial sums of this chunk
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          float p[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            p[e] = any ? ex2x(__uint_as_float(sr[16 * c + 4 * k + e]) + nm) : 0.f;
-            lsum[e] += p[e];
+          const int b0 = 16 * c + 4 * k;
+          uint32_t e01 = 0, e23 = 0;
+          if (any) {
+            e01 = ex2_h2(pack_h2(fmaf(__uint_as_float(sr[b0]), sc2, nm), fmaf(__uint_as_float(sr[b0 + 1]), sc2, nm)));
+            e23 = ex2_h2(pack_h2(fmaf(__uint_as_float(sr[b0 + 2]), sc2, nm), fmaf(__uint_as_float(sr[b0 + 3]), sc2, nm)));
           }
-          w[k] = static_cast<uint32_t>(f32x2_to_e4m3x2(p[0], p[1])) |
-                 (static_cast<uint32_t>(f32x2_to_e4m3x2(p[2], p[3])) << 16);
+          hs = k == 0 ? hadd2_u32(e01, e23) : hadd2_u32(hs, hadd2_u32(e01, e23));
+          w[k] = static_cast<uint32_t>(h2_to_e4m3x2(e01)) | (static_cast<uint32_t>(h2_to_e4m3x2(e23)) << 16);
         }
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hs));
+        lsum[c & 3] += f.x + f.y;
       }
       l += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
+      if (r == 0) x_trace(a.trace, kXEvPWritten, j);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.p_full[pb]);

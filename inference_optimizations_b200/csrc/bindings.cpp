@@ -167,7 +167,7 @@ void gqa_extend(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& p
   a.v_scale = static_cast<float>(v_scale);
   if (trace.has_value()) {
     req(*trace, at::kLong, "trace");
-    TORCH_CHECK(trace->numel() >= 8 * 64, "trace [8 x 64]");
+    TORCH_CHECK(trace->numel() >= 12 * 64, "trace [12 x 64]");
     a.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
   }
   TORCH_CHECK(2 * pool.size(3) == iob::gqa_block_bytes(a.fmt, a.D, 64), "pool part bytes");
@@ -739,6 +739,15 @@ void nvfp4_lut_test(const at::Tensor& words, at::Tensor out) {
                                     out.data_ptr<int>(), stream()));
 }
 
+void cvt_rate_test(int64_t iters, int64_t variant, at::Tensor out, at::Tensor sink) {
+  req(out, at::kLong, "out");
+  req(sink, at::kInt, "sink");
+  const at::cuda::CUDAGuard g(out.device());
+  CHECK_CUDA_OK(iob::cvt_rate_test(static_cast<int>(iters), static_cast<int>(variant),
+                                   reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
+                                   reinterpret_cast<uint32_t*>(sink.data_ptr<int>()), stream()));
+}
+
 void umma_rate_test(int64_t n, int64_t count, int64_t nacc, int64_t ts, at::Tensor out) {
   req(out, at::kLong, "out");
   const at::cuda::CUDAGuard g(out.device());
@@ -781,4 +790,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("umma_f8_mn_test", &umma_f8_mn_test);
   m.def("nvfp4_lut_test", &nvfp4_lut_test);
   m.def("umma_rate_test", &umma_rate_test);
+  m.def("cvt_rate_test", &cvt_rate_test);
 }

@@ -100,7 +100,7 @@ struct GqaExtendArgs {
   int* status;             // device status word (bounded-wait timeouts, bad page ids)
   int nblocks, Hq, Hk, D, pt_stride, page, window, fmt, pool_pages;
   float sm_scale, k_scale, v_scale;
-  long long* trace;        // optional [8 events x 64 tiles] clock64 timeline of CTA (0, 0, 0) (diagnostics), else null
+  long long* trace;        // optional [12 events x 64 tiles] clock64 timeline of CTA (0, 0, 0) (diagnostics), else null
 };
 cudaError_t gqa_extend(const GqaExtendArgs& a, cudaStream_t s);
 
@@ -275,6 +275,7 @@ cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_on
 
 cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, int sw64, cudaStream_t s);
 cudaError_t umma_f8_mn_test(const void* A, const void* B, float* C, int N, int K, cudaStream_t s);
+cudaError_t cvt_rate_test(int iters, int variant, long long* out, uint32_t* sink, cudaStream_t s);
 cudaError_t umma_rate_test(int n, int count, int nacc, int ts, long long* out, cudaStream_t s);
 cudaError_t nvfp4_lut_test(const uint32_t* words, int nwords, int* out, cudaStream_t s);
 

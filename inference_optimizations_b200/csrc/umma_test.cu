@@ -412,3 +412,66 @@ cudaError_t nvfp4_lut_test(const uint32_t* words, int nwords, int* out, cudaStre
   return cudaGetLastError();
 }
 }  // namespace iob
+
+// ---------------------------------------------------------------------------------------------------------------
+// Conversion / exp2 throughput probe: 4 warps (one per SM sub-partition), each thread runs `iters` rounds of 8
+// independent chains of one instruction kind.  out[variant] = cycles per round (one warp instruction per chain).
+namespace iob {
+namespace {
+template <int variant>
+__global__ void __launch_bounds__(128) cvt_rate_kernel(int iters, long long* out, uint32_t* sink) {
+  uint32_t x[8];
+  float f[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    x[i] = 0x3C003C00u + threadIdx.x + i;
+    f[i] = 0.5f + 0.01f * (threadIdx.x + i);
+  }
+  __syncthreads();
+  const long long c0 = clock64();
+  for (int it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      switch (variant) {   // compile-time
+        case 0: asm volatile("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(x[i]) : "f"(f[i]), "f"(__uint_as_float(x[i]))); break;
+        case 1: asm volatile("ex2.approx.f16x2 %0, %0;" : "+r"(x[i])); break;
+        case 2: asm volatile("ex2.approx.ftz.f32 %0, %0;" : "+f"(f[i])); break;
+        case 3: {
+          uint16_t h;
+          asm volatile("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(h) : "r"(x[i]));
+          x[i] = x[i] ^ h;
+          break;
+        }
+        case 4: {
+          uint16_t h;
+          asm volatile("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(h) : "f"(f[i]), "f"(f[(i + 1) & 7]));
+          x[i] = x[i] ^ h;
+          break;
+        }
+        case 5: asm volatile("add.rn.f16x2 %0, %0, %1;" : "+r"(x[i]) : "r"(x[(i + 3) & 7])); break;
+        default: asm volatile("fma.rn.f32 %0, %0, %1, %1;" : "+f"(f[i]) : "f"(f[(i + 1) & 7])); break;
+      }
+    }
+  }
+  const long long c1 = clock64();
+  uint32_t acc = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc ^= x[i] ^ __float_as_uint(f[i]);
+  sink[threadIdx.x] = acc;
+  if (threadIdx.x == 0) out[0] = (c1 - c0) / iters;
+}
+}  // namespace
+
+cudaError_t cvt_rate_test(int iters, int variant, long long* out, uint32_t* sink, cudaStream_t s) {
+  switch (variant) {
+    case 0: cvt_rate_kernel<0><<<1, 128, 0, s>>>(iters, out, sink); break;
+    case 1: cvt_rate_kernel<1><<<1, 128, 0, s>>>(iters, out, sink); break;
+    case 2: cvt_rate_kernel<2><<<1, 128, 0, s>>>(iters, out, sink); break;
+    case 3: cvt_rate_kernel<3><<<1, 128, 0, s>>>(iters, out, sink); break;
+    case 4: cvt_rate_kernel<4><<<1, 128, 0, s>>>(iters, out, sink); break;
+    case 5: cvt_rate_kernel<5><<<1, 128, 0, s>>>(iters, out, sink); break;
+    default: cvt_rate_kernel<6><<<1, 128, 0, s>>>(iters, out, sink); break;
+  }
+  return cudaGetLastError();
+}
+}  // namespace iob

@@ -62,15 +62,22 @@ def main(argv=None) -> None:
     ap.add_argument("--len", type=int, default=256)
     ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
     ap.add_argument("--kl-max", type=float, default=0.03)
+    ap.add_argument("--layers", type=int, default=0, help="truncate the model to its first N layers (0 = all)")
+    ap.add_argument("--first-dense", type=int, default=-1, help="MLA family: dense layers before the MoE layers")
     a = ap.parse_args(argv)
     cfg = model_config(a.model)
+    from dataclasses import replace
+    if a.layers:
+        cfg = replace(cfg, num_layers=a.layers)
+    if a.first_dense >= 0:
+        cfg = replace(cfg, first_dense=a.first_dense)
     mk = lambda kv: Engine(EngineConfig(model=a.model, device=a.device, kv_dtype=kv, max_running=2,  # noqa: E731
                                         chunked_prefill=a.len, cuda_graphs=False), cfg, max_seq=a.len + 64)
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, cfg.vocab, (a.len,), generator=g).tolist() for _ in range(a.prompts)]
     res = run_gate(mk(a.ref_kv), mk(a.test_kv), prompts)
-    print(json.dumps({"model": a.model, "ref_kv": a.ref_kv, "test_kv": a.test_kv, **vars(res),
-                      "pass": res.passed(a.kl_max)}))
+    print(json.dumps({"model": a.model, "layers": cfg.num_layers, "prompt_len": a.len, "ref_kv": a.ref_kv,
+                      "test_kv": a.test_kv, **vars(res), "pass": res.passed(a.kl_max)}))
 
 
 if __name__ == "__main__":
