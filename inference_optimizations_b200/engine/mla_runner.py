@@ -1,8 +1,11 @@
 """Model runner for the MLA + DSA + MoE family (`models/mla.py`): paged latent + index pools sharing one page table,
 chunked prefill and decode through the same forward (sparse attention makes every prompt token an independent
-query over its causal prefix), greedy sampling.  Runs eagerly: the MoE's per-step expert grouping has
-data-dependent shapes.  Same runner contract as `engine/runner.py GQARunner` (prefill / decode / attach / detach /
-can_admit)."""
+query over its causal prefix), greedy sampling.  Prefill runs eagerly; decode steps replay a CUDA graph per batch
+bucket: the step inputs (token, position, pool slot, visible length, page-table row per request) live in one static
+device tensor filled by one pinned host->device copy, padding entries point at the dummy page-table row (page 0,
+slot -1: nothing written), and every kernel on the path reads its counts from device memory (expert offsets, top-k
+rows), so the MoE's data-dependent grouping needs no host round trip.  Same runner contract as
+`engine/runner.py GQARunner` (prefill / decode / attach / detach / can_admit)."""
 from __future__ import annotations
 
 from typing import Optional
@@ -144,9 +147,79 @@ class MLARunner:
         return res
 
     def decode(self, reqs: list) -> dict:
-        segs = [Segment(r, r.kv_len, [r.pending], True) for r in reqs]
-        out = self._run(segs)
+        bucket = self._bucket(len(reqs))
+        if self._graphable() and bucket in self.ecfg.graph_sizes():
+            out = self._decode_graph(reqs, bucket)
+        else:
+            segs = [Segment(r, r.kv_len, [r.pending], True) for r in reqs]
+            out = self._run(segs)
         return {r.rid: [int(out[i])] for i, r in enumerate(reqs)}
+
+    # ------------------------------------------------------------------------------------------ CUDA graphs
+    def _bucket(self, n: int) -> int:
+        for b in self.ecfg.graph_sizes():
+            if b >= n:
+                return b
+        return n
+
+    def _graphable(self) -> bool:
+        """Graphs need every FFN on the block-scaled expert kernels (the bf16 reference MoE path groups tokens on
+        the host)."""
+        return (self.ecfg.cuda_graphs and self.device.type == "cuda"
+                and all(self.model._quantized_ffn(i) for i in range(self.cfg.num_layers)))
+
+    def _decode_body(self, st: MLAStep, out: torch.Tensor) -> None:
+        x = self.model.forward(st, self.kv)
+        B.argmax(self.model.logits(x), out=out)
+
+    def _graph(self, bucket: int):
+        """(graph, static step tensor [5, bucket] (ids, pos, slot, limit, row), output ids, pinned staging)."""
+        if bucket in self.graphs:
+            return self.graphs[bucket]
+        dev = self.device
+        host = torch.zeros(5, bucket, dtype=torch.int32).pin_memory()
+        host[2].fill_(-1)
+        host[3].fill_(1)
+        host[4].fill_(self.dummy_row)
+        step = host.to(dev)
+        st = MLAStep(step[0], step[1], step[2], step[3], step[4], self.max_seq + 1)
+        out = torch.zeros(bucket, dtype=torch.int32, device=dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):           # builds the lazily packed experts and workspaces outside capture
+            for _ in range(2):
+                self._decode_body(st, out)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self._decode_body(st, out)
+        self.graphs[bucket] = (g, step, out, host)
+        return self.graphs[bucket]
+
+    def _decode_graph(self, reqs: list, bucket: int) -> list:
+        g, step, out, host = self._graph(bucket)
+        n = len(reqs)
+        for i, r in enumerate(reqs):
+            rp = self.pages[r.rid]
+            p = r.kv_len
+            rp.ensure(p + 1)
+            host[0, i], host[1, i], host[2, i], host[3, i], host[4, i] = int(r.pending), p, rp.slot_of(p), p + 1, r.slot
+        host[0, n:] = 0
+        host[1, n:] = 0
+        host[2, n:] = -1
+        host[3, n:] = 1
+        host[4, n:] = self.dummy_row
+        self.kv.table.sync()
+        step.copy_(host, non_blocking=True)
+        if self.event_log is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            self.event_log.append((e0, e1))
+        else:
+            g.replay()
+        return out[:n].cpu().tolist()
 
     @torch.no_grad()
     def score(self, tokens: list) -> torch.Tensor:
@@ -161,7 +234,9 @@ class MLARunner:
             self.detach(r)
 
     def warm_graphs(self, n: int) -> None:
-        """Eager runner: nothing to capture."""
+        """Capture the decode graph of the bucket holding n requests (before any timed step)."""
+        if self._graphable():
+            self._graph(self._bucket(n))
 
     def count_step_launches(self, bucket: int, kind: Optional[str] = None) -> int:
         return 0
