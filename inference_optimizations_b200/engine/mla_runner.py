@@ -27,13 +27,16 @@ class MLARunner:
         self.cfg, self.ecfg, self.device = cfg, ecfg, torch.device(device)
         self.tp, self.tp_rank = tp, tp_rank
         self.max_seq = max_seq
-        self.spec = False
+        self.spec = bool(ecfg.spec) and cfg.draft_layers >= 1
         self.model = MLAModel(cfg, self.device, ecfg.seed)
+        if self.spec:
+            self.model.build_draft(ecfg.seed)
         fmt = FMT_NVFP4 if ecfg.kv_dtype == "nvfp4" else FMT_FP8
         self.max_running = ecfg.max_running
         per_req = (max_seq + 64 + 63) // 64 + 1
         pages = self.max_running * per_req + 2
-        self.kv = MLAKVCache(cfg, self.device, fmt, self.max_running + 1, per_req, pages)
+        self.kv = MLAKVCache(cfg, self.device, fmt, self.max_running + 1, per_req, pages,
+                             extra_layers=1 if self.spec else 0)
         self.dummy_row = self.max_running
         self.pages: dict[int, RequestPages] = {}
         self.graphs: dict = {}
@@ -138,6 +141,8 @@ class MLARunner:
         for s in batch.segments:
             if s.req.rid not in self.pages:
                 self.attach(s.req)
+        if self.spec:
+            return self._prefill_spec(batch.segments)
         out = self._run(batch.segments)
         res, k = {}, 0
         for s in batch.segments:
@@ -146,7 +151,81 @@ class MLARunner:
                 k += 1
         return res
 
+    # ------------------------------------------------------------------------------------------ MTP speculation
+    # Depth-1 multi-token prediction (the DeepSeek-V3 MTP draft; the reference's MLA draft models,
+    # `speculative/k3-mla-draft`, and frozen-KV MTP no-sync hooks): the draft layer keeps its own KV for every
+    # position the target has processed, so a plain decode step also runs it (one layer) and every step leaves a
+    # draft for the next.  A speculative step verifies [pending, draft] at positions (P, P + 1) in one target
+    # forward, then runs the draft layer over the same two positions with the true next tokens (o0, o1); the next
+    # draft is its prediction at P + 1 when the draft was accepted, else at P.  Greedy verification: the emitted
+    # tokens are exactly plain greedy decoding's.
+    def _mtp_step(self, st: MLAStep, ids: torch.Tensor) -> MLAStep:
+        return MLAStep(ids, st.pos, st.slot, st.limit, st.req_idx, st.max_ctx)
+
+    def _prefill_spec(self, segs: list) -> dict:
+        st, rows = self._step(segs)
+        x, h = self.model.forward_hidden(st, self.kv)
+        dev = self.device
+        nxt = []
+        for s in segs:
+            for j in range(len(s.tokens)):
+                p = s.start + j
+                nxt.append(int(s.tokens[j + 1]) if j + 1 < len(s.tokens)
+                           else int(s.req.prompt[p + 1]) if p + 1 < s.req.prompt_len else 0)
+        ids = torch.tensor(nxt, dtype=torch.int32).to(dev, non_blocking=True)
+        res = {}
+        if rows:
+            rt = torch.tensor(rows, dtype=torch.long).to(dev, non_blocking=True)
+            out = B.argmax(self.model.logits(x[rt]))
+            ids[rt] = out                                   # t_{i+1} of a prompt's last position: its first output
+        xm = self.model.draft_forward(self._mtp_step(st, ids), self.kv, h)
+        if rows:
+            d = B.argmax(self.model.logits(xm[rt]))
+            both = torch.stack([out, d]).cpu()
+            k = 0
+            for s in segs:
+                if s.logits:
+                    res[s.req.rid] = int(both[0, k])
+                    s.req.draft_state["d"] = int(both[1, k])
+                    k += 1
+        return res
+
+    def _decode_mtp(self, reqs: list) -> dict:
+        """Plain decode step that also advances the draft layer and leaves the next draft."""
+        segs = [Segment(r, r.kv_len, [r.pending], True) for r in reqs]
+        st, _ = self._step(segs)
+        x, h = self.model.forward_hidden(st, self.kv)
+        o = B.argmax(self.model.logits(x))
+        d = B.argmax(self.model.logits(self.model.draft_forward(self._mtp_step(st, o), self.kv, h)))
+        both = torch.stack([o, d]).cpu()
+        for i, r in enumerate(reqs):
+            r.draft_state["d"] = int(both[1, i])
+        return {r.rid: [int(both[0, i])] for i, r in enumerate(reqs)}
+
+    def spec_decode(self, reqs: list) -> dict:
+        segs = [Segment(r, r.kv_len, [r.pending, r.draft_state.get("d", 0)], False) for r in reqs]
+        st, _ = self._step(segs)
+        x, h = self.model.forward_hidden(st, self.kv)
+        o = B.argmax(self.model.logits(x))                               # [2n]: (o0, o1) per request
+        m = B.argmax(self.model.logits(self.model.draft_forward(self._mtp_step(st, o), self.kv, h)))
+        both = torch.stack([o, m]).cpu()
+        res = {}
+        for i, r in enumerate(reqs):
+            o0, o1 = int(both[0, 2 * i]), int(both[0, 2 * i + 1])
+            acc = o0 == r.draft_state.get("d", -1)
+            res[r.rid] = [o0, o1] if acc else [o0]
+            r.draft_state["d"] = int(both[1, 2 * i + 1] if acc else both[1, 2 * i])
+            r.accepted += int(acc)
+            r.spec_steps += 1
+        return res
+
+    def draft_row(self, r: Request) -> int:
+        """The draft layer's KV is current after every step (the engine's spec policy prices any step)."""
+        return 0
+
     def decode(self, reqs: list) -> dict:
+        if self.spec:
+            return self._decode_mtp(reqs)
         bucket = self._bucket(len(reqs))
         if self._graphable() and bucket in self.ecfg.graph_sizes():
             out = self._decode_graph(reqs, bucket)
@@ -165,7 +244,7 @@ class MLARunner:
     def _graphable(self) -> bool:
         """Graphs need every FFN on the block-scaled expert kernels (the bf16 reference MoE path groups tokens on
         the host)."""
-        return (self.ecfg.cuda_graphs and self.device.type == "cuda"
+        return (self.ecfg.cuda_graphs and self.device.type == "cuda" and not self.spec
                 and all(self.model._quantized_ffn(i) for i in range(self.cfg.num_layers)))
 
     def _decode_body(self, st: MLAStep, out: torch.Tensor) -> None:

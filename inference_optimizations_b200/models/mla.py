@@ -77,13 +77,14 @@ class MLAStep:
 
 
 class MLAKVCache:
-    def __init__(self, cfg: MLAMoEConfig, device, fmt: int, rows: int, max_pages: int, pages: int):
+    def __init__(self, cfg: MLAMoEConfig, device, fmt: int, rows: int, max_pages: int, pages: int,
+                 extra_layers: int = 0):
         self.cfg, self.device, self.fmt = cfg, torch.device(device), fmt
         rb = M.ROW_BYTES[fmt]
-        self.latent = [torch.zeros(pages * 64, rb, dtype=torch.uint8, device=self.device)
-                       for _ in range(cfg.num_layers)]
+        n = cfg.num_layers + extra_layers           # extra: the MTP draft layer's pools (same page ids)
+        self.latent = [torch.zeros(pages * 64, rb, dtype=torch.uint8, device=self.device) for _ in range(n)]
         self.index = [torch.zeros(pages, K.INDEX_PAGE_BYTES, dtype=torch.uint8, device=self.device)
-                      for _ in range(cfg.num_layers)]
+                      for _ in range(n)]
         from ..kv.allocator import PageAllocator, PageTable
         self.alloc = PageAllocator(pages)
         self.table = PageTable(rows, max_pages, self.device)
@@ -131,12 +132,62 @@ class MLAModel:
                 wi_w=r(f"{i}.wi_w", (c.index_heads, h)), ffn=ffn))
         self.rope = {}
         self.sm_scale = 1.0 / math.sqrt(c.qk_nope + c.qk_rope)
+        self.n_target = c.num_layers
+        self.draft = False
+
+    def build_draft(self, seed: int = 0) -> None:
+        """Multi-token-prediction draft head (DeepSeek-V3 MTP, depth 1): h'_i = W_eh [RMSNorm_e(Emb(t_{i+1}));
+        RMSNorm_h(h_i)] through one more MLA + DSA + MoE layer (its own latent / index pools, index
+        `num_layers`), a final norm and the shared LM head; it predicts t_{i+2}.  Weights random-init like the
+        target's."""
+        c, h = self.cfg, self.cfg.hidden
+        r = lambda name, shape, s=c.init_std: _rand(name, shape, s, self.device, seed)  # noqa: E731
+        ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
+        i = c.num_layers
+        # the draft layer is built exactly like a target layer with index num_layers (MoE, since i >= first_dense)
+        wkv_b = r(f"mtp.{i}.wkv_b", (c.num_heads * (c.qk_nope + c.v_head), c.kv_lora)).view(
+            c.num_heads, c.qk_nope + c.v_head, c.kv_lora)
+        ffn = {"gate": r(f"mtp.{i}.gate", (c.num_experts, h)),
+               "e_bias": torch.zeros(c.num_experts, dtype=torch.float32, device=self.device),
+               "w_gu": r(f"mtp.{i}.experts.gu", (c.num_experts, 2 * c.expert_ffn, h)),
+               "w_down": r(f"mtp.{i}.experts.down", (c.num_experts, h, c.expert_ffn)),
+               "shared_gu": r(f"mtp.{i}.shared.gu", (2 * c.expert_ffn * c.num_shared, h)) if c.num_shared else None,
+               "shared_down": r(f"mtp.{i}.shared.down", (h, c.expert_ffn * c.num_shared)) if c.num_shared else None}
+        self.layers.append(MLALayerWeights(
+            n_in=ones(h), n_post=ones(h),
+            wq_a=r(f"mtp.{i}.wq_a", (c.q_lora, h)), q_norm=ones(c.q_lora),
+            wq_b=r(f"mtp.{i}.wq_b", (c.num_heads * (c.qk_nope + c.qk_rope), c.q_lora)),
+            wkv_a=r(f"mtp.{i}.wkv_a", (c.kv_lora + c.qk_rope, h)), kv_norm=ones(c.kv_lora),
+            w_uk=wkv_b[:, :c.qk_nope, :].contiguous(),
+            w_uv=wkv_b[:, c.qk_nope:, :].transpose(1, 2).contiguous(),
+            wo=r(f"mtp.{i}.wo", (h, c.num_heads * c.v_head)),
+            wi_q=r(f"mtp.{i}.wi_q", (c.index_heads * c.index_dim, c.q_lora)),
+            wi_k=r(f"mtp.{i}.wi_k", (c.index_dim, h)), wi_kn=ones(c.index_dim),
+            wi_kb=torch.zeros(c.index_dim, dtype=torch.bfloat16, device=self.device),
+            wi_w=r(f"mtp.{i}.wi_w", (c.index_heads, h)), ffn=ffn))
+        self.eh_proj = r("mtp.eh_proj", (h, 2 * h))
+        self.enorm, self.hnorm, self.draft_norm = ones(h), ones(h), ones(h)
+        self.draft = True
+
+    def draft_forward(self, st: "MLAStep", kv: "MLAKVCache", h_prev: torch.Tensor) -> torch.Tensor:
+        """MTP head over the step's tokens: st.ids[j] = t_{i+1} for the position i of row j, h_prev[j] = the target's
+        residual stream at i.  Writes the draft layer's KV at st.slot; returns final-normed hidden [T, H]."""
+        c = self.cfg
+        e = B.embed(st.ids, self.embed)
+        x0 = torch.cat([B.rmsnorm(e, self.enorm, c.rms_eps), B.rmsnorm(h_prev, self.hnorm, c.rms_eps)], dim=-1)
+        h = Fn.linear(x0, self.eh_proj)
+        i = self.n_target
+        x = B.rmsnorm(h, self.layers[i].n_in, c.rms_eps)
+        return self.layer_forward(i, h, x, st, kv, self.draft_norm)
 
     def copy_from(self, other: "MLAModel") -> None:
         """Take another instance's weights (any device): device RNG streams differ, so tests that compare devices
         copy one model's weights into the other."""
         dev = self.device
-        for name in ("embed", "lm_head", "final_norm"):
+        names = ["embed", "lm_head", "final_norm"]
+        if self.draft and other.draft:
+            names += ["eh_proj", "enorm", "hnorm", "draft_norm"]
+        for name in names:
             setattr(self, name, getattr(other, name).to(dev))
         for mine, theirs in zip(self.layers, other.layers):
             for f in vars(theirs):
@@ -237,12 +288,17 @@ class MLAModel:
 
     def forward(self, st: MLAStep, kv: MLAKVCache) -> torch.Tensor:
         """-> final-normed hidden [T, H]."""
+        return self.forward_hidden(st, kv)[0]
+
+    def forward_hidden(self, st: MLAStep, kv: MLAKVCache) -> tuple[torch.Tensor, torch.Tensor]:
+        """-> (final-normed hidden [T, H], residual stream after the last target layer [T, H])."""
         h = B.embed(st.ids, self.embed)
         x = B.rmsnorm(h, self.layers[0].n_in, self.cfg.rms_eps)
-        for i in range(len(self.layers)):
-            nxt = self.layers[i + 1].n_in if i + 1 < len(self.layers) else self.final_norm
+        n = self.n_target
+        for i in range(n):
+            nxt = self.layers[i + 1].n_in if i + 1 < n else self.final_norm
             x = self.layer_forward(i, h, x, st, kv, nxt)
-        return x
+        return x, h
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
         return Fn.linear(x, self.lm_head)

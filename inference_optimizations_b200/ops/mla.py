@@ -199,3 +199,51 @@ def mla_decode_emul_e4m3(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor,
         out[i] = torch.where(ok[:, None], num / den.clamp(min=1e-30)[:, None], torch.zeros_like(num))
         lse[i] = torch.where(ok, (lmax + torch.log2(den.clamp(min=1e-30))) / log2e, torch.full_like(den, ninf))
     return out.to(q.device), lse.to(q.device)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# The two MLA layouts a draft (or target) layer can run in -- the reference's MLA draft models keep both
+# (`speculative/k3-mla-draft/k3_mla_draft/k3_mla_draft.py:1-25`: latent MQA 576/512 and expanded MHA padded to 256,
+# equal to 1e-9): the absorbed form attends once over the shared latent rows (what the sparse-MLA decode kernel and
+# the paged pools use); the expanded form decompresses per-head K = [c W_UK[h]^T ; k_pe] and V = c W_UV[h], zero-pads
+# both to `pad` dims and runs ordinary multi-head attention (what a dense MHA kernel or a prefill GEMM path wants).
+def mla_attention_latent(q_nope: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Tensor, k_pe: torch.Tensor,
+                         w_uk: torch.Tensor, w_uv: torch.Tensor, sm_scale: float,
+                         mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q_nope [T, H, dn], q_pe [T, H, dr], c_kv [S, L], k_pe [S, dr], w_uk [H, dn, L], w_uv [H, L, dv],
+    mask [T, S] bool (True = visible) -> out [T, H, dv]."""
+    q_lat = torch.einsum("thn,hnl->thl", q_nope, w_uk)
+    s = (torch.einsum("thl,sl->ths", q_lat, c_kv) + torch.einsum("thr,sr->ths", q_pe, k_pe)) * sm_scale
+    if mask is not None:
+        s = s.masked_fill(~mask[:, None, :], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("thl,hlv->thv", torch.einsum("ths,sl->thl", p, c_kv), w_uv)
+
+
+def mla_expand_kv(c_kv: torch.Tensor, k_pe: torch.Tensor, w_uk: torch.Tensor, w_uv: torch.Tensor,
+                  pad: int = 256) -> tuple[torch.Tensor, torch.Tensor]:
+    """Latent rows -> per-head K [S, H, pad] ([nope ; rope ; 0]) and V [S, H, pad] ([v ; 0])."""
+    s_, h, dn, dr, dv = c_kv.shape[0], w_uk.shape[0], w_uk.shape[1], k_pe.shape[1], w_uv.shape[2]
+    assert dn + dr <= pad and dv <= pad
+    k = torch.zeros(s_, h, pad, dtype=c_kv.dtype, device=c_kv.device)
+    k[..., :dn] = torch.einsum("sl,hnl->shn", c_kv, w_uk)
+    k[..., dn:dn + dr] = k_pe[:, None, :]
+    v = torch.zeros(s_, h, pad, dtype=c_kv.dtype, device=c_kv.device)
+    v[..., :dv] = torch.einsum("sl,hlv->shv", c_kv, w_uv)
+    return k, v
+
+
+def mla_attention_expanded(q_nope: torch.Tensor, q_pe: torch.Tensor, c_kv: torch.Tensor, k_pe: torch.Tensor,
+                           w_uk: torch.Tensor, w_uv: torch.Tensor, sm_scale: float,
+                           mask: Optional[torch.Tensor] = None, pad: int = 256) -> torch.Tensor:
+    """The same attention as `mla_attention_latent` through the expanded MHA layout."""
+    t, h, dn = q_nope.shape
+    dr, dv = q_pe.shape[2], w_uv.shape[2]
+    k, v = mla_expand_kv(c_kv, k_pe, w_uk, w_uv, pad)
+    q = torch.zeros(t, h, pad, dtype=q_nope.dtype, device=q_nope.device)
+    q[..., :dn] = q_nope
+    q[..., dn:dn + dr] = q_pe
+    s = torch.einsum("thd,shd->ths", q, k) * sm_scale
+    if mask is not None:
+        s = s.masked_fill(~mask[:, None, :], float("-inf"))
+    return torch.einsum("ths,shd->thd", torch.softmax(s, dim=-1), v)[..., :dv]

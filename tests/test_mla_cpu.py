@@ -82,3 +82,22 @@ def test_dense_mla_indices_and_decode():
     o1 = M.mla_dense_decode(q, pool, pages, kv_len, sm)
     o2, _ = M.mla_decode_ref(q, pool, idx, sm, M.FMT_NVFP4)
     assert torch.allclose(o1.float(), o2.float(), atol=1e-2)
+
+
+def test_mla_latent_and_expanded_layouts_agree():
+    """Absorbed latent (MQA over 576-dim rows) and expanded per-head MHA (padded to 256) give the same attention to
+    1e-9 in fp64, with a causal mask."""
+    import torch
+    from inference_optimizations_b200.ops import mla as M
+    torch.manual_seed(0)
+    t, s, h, dn, dr, dv, lat = 5, 40, 4, 128, 64, 128, 512
+    d = torch.float64
+    q_nope, q_pe = torch.randn(t, h, dn, dtype=d), torch.randn(t, h, dr, dtype=d)
+    c_kv, k_pe = torch.randn(s, lat, dtype=d), torch.randn(s, dr, dtype=d)
+    w_uk, w_uv = torch.randn(h, dn, lat, dtype=d) * 0.05, torch.randn(h, lat, dv, dtype=d) * 0.05
+    mask = torch.arange(s)[None, :] <= (torch.arange(t)[:, None] + s - t)
+    a = M.mla_attention_latent(q_nope, q_pe, c_kv, k_pe, w_uk, w_uv, 192 ** -0.5, mask)
+    b = M.mla_attention_expanded(q_nope, q_pe, c_kv, k_pe, w_uk, w_uv, 192 ** -0.5, mask)
+    assert a.shape == (t, h, dv) and (a - b).abs().max().item() < 1e-9
+    k, v = M.mla_expand_kv(c_kv, k_pe, w_uk, w_uv)
+    assert k.shape == (s, h, 256) and torch.all(k[..., dn + dr:] == 0) and torch.all(v[..., dv:] == 0)

@@ -68,3 +68,35 @@ def test_radix_prefix_cache_reuse_is_exact():
     held, free0 = eng.runner.prefix_cache.held, eng.runner.kv.alloc.free
     assert eng.runner.prefix_cache.clear() == held and eng.runner.prefix_cache.held == 0
     assert eng.runner.kv.alloc.free == free0 + held
+
+
+def test_mla_mtp_speculation_preserves_greedy_output():
+    """Depth-1 MTP speculation (verify [pending, draft] in one target forward) emits exactly the plain greedy tokens;
+    a draft that equals the target's next token is accepted (two tokens in one step)."""
+    import torch
+    from inference_optimizations_b200.config import EngineConfig, model_config
+    from inference_optimizations_b200.engine.engine import Engine
+    from inference_optimizations_b200.engine.scheduler import SamplingParams
+    cfg = model_config("tiny_mla")
+    torch.manual_seed(2)
+    prompts = [torch.randint(1, cfg.vocab, (n,)).tolist() for n in (70, 21)]
+    outs, engines = [], []
+    for spec in (False, True):
+        ecfg = EngineConfig(model="tiny_mla", device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=32,
+                            cuda_graphs=False, spec=spec, spec_policy="always", prefix_cache=False)
+        eng = Engine(ecfg, cfg, max_seq=256)
+        outs.append(eng.generate(prompts, SamplingParams(max_new_tokens=10)))
+        engines.append(eng)
+    assert outs[0] == outs[1], outs
+    assert all(r.spec_steps > 0 for r in engines[1].finished)
+    # forced acceptance: make the draft the target's own next token and check the step emits two tokens
+    eng = engines[1]
+    r = eng.add_request(prompts[1], SamplingParams(max_new_tokens=6))
+    while r.prefilled < r.prompt_len:
+        eng.step()
+    plain = Engine(EngineConfig(model="tiny_mla", device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=32,
+                                cuda_graphs=False, prefix_cache=False), cfg, max_seq=256)
+    want = plain.generate([prompts[1]], SamplingParams(max_new_tokens=6))[0]
+    r.draft_state["d"] = want[1]                    # the token greedy decoding produces after r.pending
+    got = eng.runner.spec_decode([r])[r.rid]
+    assert got == want[1:3], (got, want)

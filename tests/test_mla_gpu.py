@@ -88,3 +88,19 @@ def test_mla_decode_cuda_graph_matches_eager(cuda):
         if graphs:
             assert 4 in eng.runner.graphs
     assert outs[0] == outs[1], outs
+
+
+def test_mla_mtp_speculation_gpu(cuda):
+    """MTP speculation through the GPU kernels (FP8 block-scaled experts, NVFP4 latent rows) emits the plain greedy
+    tokens."""
+    over = dict(expert_ffn=256, dense_ffn=512, weight_dtype="fp8", expert_dtype="fp8")
+    cfg = model_config("tiny_mla", **over)
+    torch.manual_seed(4)
+    prompts = [torch.randint(1, cfg.vocab, (n,)).tolist() for n in (66, 12)]
+    outs = []
+    for spec in (False, True):
+        ecfg = EngineConfig(model="tiny_mla", device=str(cuda), kv_dtype="nvfp4", max_running=4, chunked_prefill=64,
+                            cuda_graphs=False, spec=spec, spec_policy="always", prefix_cache=False)
+        eng = Engine(ecfg, cfg, max_seq=256)
+        outs.append(eng.generate(prompts, SamplingParams(max_new_tokens=8)))
+    assert outs[0] == outs[1], outs
