@@ -57,7 +57,10 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchArgs a
     int* dst = reinterpret_cast<int*>(reinterpret_cast<char*>(a.peers[r]) + a.off_ids) + row * a.topk + k;
     *dst = t < a.T ? a.ids[t * a.topk + k] : -1;
   }
-  if (t >= a.T) return;
+  if (t >= a.T) {
+    __threadfence_system();
+    return;
+  }
   const uint32_t m = dest_mask;
   const int n16 = a.row_bytes / 16, s4 = a.scale_bytes / 4;
   const uint4* xs = reinterpret_cast<const uint4*>(a.xq + static_cast<size_t>(t) * a.row_bytes);
@@ -71,6 +74,9 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchArgs a
     for (int i = threadIdx.x; i < n16; i += blockDim.x) dx[i] = xs[i];
     for (int i = threadIdx.x; i < s4; i += blockDim.x) ds[i] = ss[i];
   }
+  // the peer stores (and the id stores above) are visible system-wide before the barrier kernel that follows
+  // releases its flag
+  __threadfence_system();
 }
 
 __global__ void ep_barrier_kernel(const long long* peers, long long off_flags, int rank, int world, int* epoch,

@@ -469,6 +469,9 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
       tc_fence_before();
       mbar_arrive(&ctl.acc_empty[buf]);
     }
+    // rows stored into peers' memory must be visible system-wide before the next kernel's barrier releases its
+    // flag (that release orders only the releasing thread's own writes)
+    if (a.out_peers) __threadfence_system();
   }
   tc_fence_before();
   __syncthreads();

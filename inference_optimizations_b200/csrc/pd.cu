@@ -29,6 +29,7 @@ __global__ void __launch_bounds__(256) pd_copy_kernel(const PdCopyArgs a) {
                                         static_cast<long long>(dp) * a.page_bytes);
   const int n16 = static_cast<int>(a.page_bytes / 16);
   for (int k = threadIdx.x; k < n16; k += blockDim.x) dst[k] = src[k];
+  __threadfence_system();   // the peer stores are visible before pd_signal's release (a separate kernel)
 }
 
 __global__ void pd_signal_kernel(int* peer_flag, int value) {

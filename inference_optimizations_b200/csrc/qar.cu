@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(256) qar_push_kernel(const QarArgs a) {
   const QarView peer{reinterpret_cast<char*>(a.peers[owner])};
   reinterpret_cast<uint32_t*>(peer.q(a, 0, a.rank, t, g))[lane] = w;
   if (lane == 0) *peer.s(a, 0, a.rank, t, g) = sc;
+  __threadfence_system();   // peer stores visible before the next kernel's barrier releases its flag
 }
 
 __global__ void __launch_bounds__(256) qar_reduce_kernel(const QarArgs a) {
@@ -117,6 +118,7 @@ __global__ void __launch_bounds__(256) qar_reduce_kernel(const QarArgs a) {
     reinterpret_cast<uint32_t*>(peer.q(a, 1, 0, t, g))[lane] = w;
     if (lane == 0) *peer.s(a, 1, 0, t, g) = sc;
   }
+  __threadfence_system();
 }
 
 __global__ void __launch_bounds__(256) qar_gather_kernel(const QarArgs a) {

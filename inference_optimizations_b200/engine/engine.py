@@ -27,7 +27,8 @@ class StepStats:
 
 class Engine:
     def __init__(self, ecfg: EngineConfig, model_cfg=None, max_seq: int = 4096, tp_rank: int = 0, tp: int = 1,
-                 all_reduce=None, argmax_merge=None, global_pages: Optional[int] = None):
+                 all_reduce=None, argmax_merge=None, global_pages: Optional[int] = None, ep_rank: int = 0,
+                 ep_group=None):
         self.ecfg = ecfg
         self.cfg = model_cfg if model_cfg is not None else model_config(ecfg.model)
         self.device = torch.device(ecfg.device)
@@ -36,7 +37,7 @@ class Engine:
                                     global_pages)
         else:
             from .mla_runner import MLARunner
-            self.runner = MLARunner(self.cfg, ecfg, self.device, max_seq, tp_rank, tp)
+            self.runner = MLARunner(self.cfg, ecfg, self.device, max_seq, tp_rank, tp, ep_rank, ep_group)
         self.sched = Scheduler(ecfg.max_running, ecfg.chunked_prefill, ecfg.decode_burst,
                                can_admit=self.runner.can_admit, on_admit=getattr(self.runner, "on_admit", None))
         self.stats: list[StepStats] = []
@@ -56,6 +57,8 @@ class Engine:
         rec = self.trace.begin() if self.trace else None
         batch = self.sched.schedule()
         if batch is None:
+            if getattr(self.runner, "ep_world", 1) > 1:
+                self.runner.idle_step()          # data-parallel attention: join the busy ranks' MoE exchanges
             return {}
         if rec is not None:
             t_s = self.trace.phase(rec, "schedule", t0)
@@ -105,6 +108,21 @@ class Engine:
                     del log[:-1]
             self.trace.end(rec, ev)
         return out
+
+    def generate_dp(self, prompts: list, params: Optional[SamplingParams] = None, group=None) -> list:
+        """Data-parallel serving loop: this rank's prompts; every rank steps until no rank has work (one small
+        all-reduce per step), so the expert-parallel exchanges stay in lockstep."""
+        import torch.distributed as dist
+        reqs = [self.add_request(p, params) for p in prompts]
+        dev = self.device if dist.get_backend(group) == "nccl" else torch.device("cpu")
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        while True:
+            flag.fill_(1 if self.sched.has_work() else 0)
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
+            if int(flag.item()) == 0:
+                break
+            self.step()
+        return [r.output for r in reqs]
 
     def generate(self, prompts: list, params: Optional[SamplingParams] = None, max_steps: int = 1 << 30) -> list:
         reqs = [self.add_request(p, params) for p in prompts]

@@ -21,16 +21,27 @@ from .scheduler import Batch, Request, SamplingParams, Segment
 
 
 class MLARunner:
-    def __init__(self, cfg: MLAMoEConfig, ecfg: EngineConfig, device, max_seq: int, tp_rank: int = 0, tp: int = 1):
+    def __init__(self, cfg: MLAMoEConfig, ecfg: EngineConfig, device, max_seq: int, tp_rank: int = 0, tp: int = 1,
+                 ep_rank: int = 0, ep_group=None):
+        """ecfg.ep > 1: data-parallel attention + expert-parallel MoE.  Every rank runs its own requests (its own
+        scheduler, pools and replicated attention weights); every MoE layer is an exchange over `ep_group` with
+        `ecfg.ep` ranks, so all ranks step in lockstep: before each forward the ranks agree on the largest token
+        count of the step (one small all-reduce), and a rank without work joins the exchanges with no tokens
+        (`idle_step`)."""
         if tp != 1:
-            raise NotImplementedError("the MLA family runs on one GPU per engine here (tp = 1)")
+            raise NotImplementedError("the MLA family runs attention data-parallel here (tp = 1 per rank)")
         self.cfg, self.ecfg, self.device = cfg, ecfg, torch.device(device)
         self.tp, self.tp_rank = tp, tp_rank
         self.max_seq = max_seq
         self.spec = bool(ecfg.spec) and cfg.draft_layers >= 1
-        self.model = MLAModel(cfg, self.device, ecfg.seed)
+        self.ep_world, self.ep_rank, self.ep_group = max(1, ecfg.ep), ep_rank, ep_group
+        self.model = MLAModel(cfg, self.device, ecfg.seed, ep_rank=ep_rank, ep_world=self.ep_world)
         if self.spec:
             self.model.build_draft(ecfg.seed)
+        if self.ep_world > 1:
+            # tokens per exchange: a decode step of every running request (with its draft), or a prefill piece
+            self.ep_T_max = max(2 * ecfg.max_running, min(ecfg.chunked_prefill, 1024))
+            self.model.attach_ep(ep_group, self.ep_T_max)
         fmt = FMT_NVFP4 if ecfg.kv_dtype == "nvfp4" else FMT_FP8
         self.max_running = ecfg.max_running
         per_req = (max_seq + 64 + 63) // 64 + 1
@@ -95,6 +106,26 @@ class MLARunner:
         rp.pages.clear()
         self.kv.table.clear(r.slot)
 
+    # ------------------------------------------------------------------------------------------ lockstep (EP)
+    def _agree(self, tokens: int) -> int:
+        """Largest token count of this step over the expert-parallel ranks; sets the exchanges per MoE layer."""
+        if self.ep_world == 1:
+            return tokens
+        import torch.distributed as dist
+        dev = self.device if dist.get_backend(self.ep_group) == "nccl" else torch.device("cpu")
+        v = torch.tensor([tokens], dtype=torch.int64, device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX, group=self.ep_group)
+        m = int(v.item())
+        self.model.ep_pieces = max(1, -(-m // self.ep_T_max))
+        return m
+
+    def idle_step(self) -> None:
+        """A rank without a batch this step: join every exchange the busy ranks run (target MoE layers, then the
+        draft layer when speculating), with no tokens."""
+        if self.ep_world == 1 or self._agree(0) == 0:
+            return
+        self.model.ep_idle(self.model.moe_layers())
+
     # ------------------------------------------------------------------------------------------ steps
     def _step(self, segs: list) -> tuple[MLAStep, list]:
         ids, pos, slot, limit, rix, logit_rows = [], [], [], [], [], []
@@ -117,6 +148,7 @@ class MLARunner:
         dev = self.device
         mk = lambda v: torch.tensor(v, dtype=torch.int32).to(dev, non_blocking=True)  # noqa: E731
         st = MLAStep(mk(ids), mk(pos), mk(slot), mk(limit), mk(rix), self.max_seq + 1)
+        self._agree(len(ids))
         return st, logit_rows
 
     def _run(self, segs: list) -> list:
@@ -244,7 +276,7 @@ class MLARunner:
     def _graphable(self) -> bool:
         """Graphs need every FFN on the block-scaled expert kernels (the bf16 reference MoE path groups tokens on
         the host)."""
-        return (self.ecfg.cuda_graphs and self.device.type == "cuda" and not self.spec
+        return (self.ecfg.cuda_graphs and self.device.type == "cuda" and not self.spec and self.ep_world == 1
                 and all(self.model._quantized_ffn(i) for i in range(self.cfg.num_layers)))
 
     def _decode_body(self, st: MLAStep, out: torch.Tensor) -> None:

@@ -45,6 +45,13 @@ def _rand(name: str, shape, std: float, device, seed: int) -> torch.Tensor:
     return t
 
 
+def _rand_experts(name: str, lo: int, hi: int, shape, std: float, device, seed: int) -> torch.Tensor:
+    """Experts lo..hi-1 of a stacked [E, ...] expert weight, each seeded by its own name: an expert-parallel rank
+    builds only its slice and every EP width builds the same model."""
+    return torch.stack([_rand(f"{name}.{e}", shape, std, device, seed) for e in range(lo, hi)]) if hi > lo else \
+        torch.empty(0, *shape, dtype=torch.bfloat16, device=device)
+
+
 @dataclass
 class MLALayerWeights:
     n_in: torch.Tensor
@@ -96,9 +103,16 @@ class MLAKVCache:
 
 
 class MLAModel:
-    def __init__(self, cfg: MLAMoEConfig, device, seed: int = 0):
+    def __init__(self, cfg: MLAMoEConfig, device, seed: int = 0, ep_rank: int = 0, ep_world: int = 1):
+        """ep_world > 1: this rank holds routed experts [ep_rank E / ep_world, (ep_rank + 1) E / ep_world) of every
+        MoE layer (plus the shared expert); attention, router and dense layers are replicated."""
         self.cfg, self.device = cfg, torch.device(device)
         h, c = cfg.hidden, cfg
+        if c.num_experts % ep_world:
+            raise ValueError("experts must divide evenly over the expert-parallel ranks")
+        self.ep_rank, self.ep_world = ep_rank, ep_world
+        e_lo, e_hi = ep_rank * c.num_experts // ep_world, (ep_rank + 1) * c.num_experts // ep_world
+        self.ep = None                                   # set by attach_ep(): per-layer expert-parallel MoE
         std = c.init_std
         ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
         r = lambda name, shape, s=std: _rand(name, shape, s, self.device, seed)  # noqa: E731
@@ -112,8 +126,10 @@ class MLAModel:
             if c.is_moe(i):
                 ffn = {"gate": r(f"{i}.gate", (c.num_experts, h)),
                        "e_bias": torch.zeros(c.num_experts, dtype=torch.float32, device=self.device),
-                       "w_gu": r(f"{i}.experts.gu", (c.num_experts, 2 * c.expert_ffn, h)),
-                       "w_down": r(f"{i}.experts.down", (c.num_experts, h, c.expert_ffn)),
+                       "w_gu": _rand_experts(f"{i}.experts.gu", e_lo, e_hi, (2 * c.expert_ffn, h), std,
+                                             self.device, seed),
+                       "w_down": _rand_experts(f"{i}.experts.down", e_lo, e_hi, (h, c.expert_ffn), std,
+                                               self.device, seed),
                        "shared_gu": r(f"{i}.shared.gu", (2 * c.expert_ffn * c.num_shared, h)) if c.num_shared else None,
                        "shared_down": r(f"{i}.shared.down", (h, c.expert_ffn * c.num_shared)) if c.num_shared else None}
             else:
@@ -143,14 +159,18 @@ class MLAModel:
         c, h = self.cfg, self.cfg.hidden
         r = lambda name, shape, s=c.init_std: _rand(name, shape, s, self.device, seed)  # noqa: E731
         ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
+        e_lo = self.ep_rank * c.num_experts // self.ep_world
+        e_hi = (self.ep_rank + 1) * c.num_experts // self.ep_world
         i = c.num_layers
         # the draft layer is built exactly like a target layer with index num_layers (MoE, since i >= first_dense)
         wkv_b = r(f"mtp.{i}.wkv_b", (c.num_heads * (c.qk_nope + c.v_head), c.kv_lora)).view(
             c.num_heads, c.qk_nope + c.v_head, c.kv_lora)
         ffn = {"gate": r(f"mtp.{i}.gate", (c.num_experts, h)),
                "e_bias": torch.zeros(c.num_experts, dtype=torch.float32, device=self.device),
-               "w_gu": r(f"mtp.{i}.experts.gu", (c.num_experts, 2 * c.expert_ffn, h)),
-               "w_down": r(f"mtp.{i}.experts.down", (c.num_experts, h, c.expert_ffn)),
+               "w_gu": _rand_experts(f"mtp.{i}.experts.gu", e_lo, e_hi, (2 * c.expert_ffn, h), c.init_std,
+                                     self.device, seed),
+               "w_down": _rand_experts(f"mtp.{i}.experts.down", e_lo, e_hi, (h, c.expert_ffn), c.init_std,
+                                       self.device, seed),
                "shared_gu": r(f"mtp.{i}.shared.gu", (2 * c.expert_ffn * c.num_shared, h)) if c.num_shared else None,
                "shared_down": r(f"mtp.{i}.shared.down", (h, c.expert_ffn * c.num_shared)) if c.num_shared else None}
         self.layers.append(MLALayerWeights(
@@ -168,6 +188,46 @@ class MLAModel:
         self.eh_proj = r("mtp.eh_proj", (h, 2 * h))
         self.enorm, self.hnorm, self.draft_norm = ones(h), ones(h), ones(h)
         self.draft = True
+
+    def moe_layers(self) -> list:
+        """Indices of the MoE layers in forward order (the MTP draft layer last)."""
+        return [i for i in range(len(self.layers)) if self.cfg.is_moe(i)]
+
+    def attach_ep(self, group, T_max: int) -> None:
+        """Route every MoE layer through expert parallelism over `group` (a collective, same order on every rank):
+        the peer-memory exchange with grouped block-scaled GEMMs (`parallel/ep.py EPMoE`, one shared symmetric
+        buffer) on CUDA with FP8 / NVFP4 experts, else the collective reference (`EPMoERef`, e.g. gloo on CPU)."""
+        from ..parallel import ep as EP
+        from ..ops.moe_gemm import BlockScaledExperts
+        c = self.cfg
+        self.ep, self.ep_pieces, self.ep_T_max = {}, 1, T_max
+        comm = None
+        cuda = self.device.type == "cuda" and c.expert_dtype in ("fp8", "nvfp4")
+        for i in self.moe_layers():
+            f, F = self.layers[i].ffn, c.expert_ffn
+            sh = (f["shared_gu"][:F], f["shared_gu"][F:], f["shared_down"]) if f["shared_gu"] is not None else None
+            if cuda:
+                ex = BlockScaledExperts(f["w_gu"][:, :F], f["w_gu"][:, F:], f["w_down"], shared=sh,
+                                        fmt=c.expert_dtype)
+                if comm is None:
+                    comm = EP.EPComm(self.ep_rank, self.ep_world, T_max, c.topk, c.hidden, F, c.expert_dtype,
+                                     c.num_experts // self.ep_world, ex.has_shared, self.device, group)
+                self.ep[i] = EP.EPMoE(self.ep_rank, self.ep_world, c.num_experts, T_max, c.topk, experts=ex,
+                                      comm=comm)
+            else:
+                shared = (f["shared_gu"], f["shared_down"]) if f["shared_gu"] is not None else None
+                self.ep[i] = EP.EPMoERef(self.ep_rank, self.ep_world, c.num_experts, T_max, c.topk, f["w_gu"],
+                                         f["w_down"], shared, group)
+
+    def ep_idle(self, layers: list) -> None:
+        """An idle rank's part of one step: the exchange of every listed MoE layer, `ep_pieces` times, no tokens."""
+        c = self.cfg
+        x = torch.zeros(0, c.hidden, dtype=torch.bfloat16, device=self.device)
+        ids = torch.zeros(0, c.topk, dtype=torch.int32, device=self.device)
+        w = torch.zeros(0, c.topk, dtype=torch.float32, device=self.device)
+        for i in layers:
+            for _ in range(self.ep_pieces):
+                self.ep[i].forward(x, ids, w)
 
     def draft_forward(self, st: "MLAStep", kv: "MLAKVCache", h_prev: torch.Tensor) -> torch.Tensor:
         """MTP head over the step's tokens: st.ids[j] = t_{i+1} for the position i of row j, h_prev[j] = the target's
@@ -238,6 +298,15 @@ class MLAModel:
 
     def _ffn(self, i: int, x: torch.Tensor) -> torch.Tensor:
         c, f = self.cfg, self.layers[i].ffn
+        if self.ep is not None and c.is_moe(i):
+            logits = Fn.linear(x.float(), f["gate"].float())
+            ids, w = MOE.route(logits, f["e_bias"], c.topk, c.n_group, c.topk_group, c.routed_scale, c.router)
+            t, per = x.shape[0], self.ep_T_max
+            outs = []
+            for p in range(self.ep_pieces):      # every rank runs the same number of exchanges (agreed per step)
+                lo, hi = min(t, p * per), min(t, (p + 1) * per)
+                outs.append(self.ep[i].forward(x[lo:hi], ids[lo:hi].to(torch.int32).contiguous(), w[lo:hi]))
+            return torch.cat(outs) if len(outs) > 1 else outs[0]
         if self._quantized_ffn(i):
             ex = self._block_scaled(i)
             t = x.shape[0]

@@ -68,23 +68,35 @@ def moe_forward(x: torch.Tensor, gate: torch.Tensor, e_bias: torch.Tensor, w_gu:
     """x bf16 [T, H]; w_gu [E, 2F, H]; w_down [E, H, F]; shared_* one shared expert (or None).  Dropless: every
     (token, expert) pair is computed; contributions are summed in fp32 in expert order then added to the shared
     expert's output."""
-    t = x.shape[0]
     logits = Fn.linear(x.float(), gate.float())
     ids, w = route(logits, e_bias, topk, n_group, topk_group, routed_scale, kind)
+    out = experts_ref(x, ids, w, w_gu, w_down, 0)
+    if shared_gu is not None:
+        out += swiglu(x, shared_gu, shared_down).float()
+    return out.to(torch.bfloat16)
+
+
+def experts_ref(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor,
+                e0: int) -> torch.Tensor:
+    """fp32 [T, H] sum over the (token, slot) pairs routed to experts e0 .. e0 + len(w_gu) - 1 (expert order) of
+    weight * SwiGLU expert output; other ids (and -1) contribute nothing."""
+    t, topk = ids.shape
     out = torch.zeros(t, x.shape[1], dtype=torch.float32, device=x.device)
-    flat = ids.long().view(-1)
+    flat = ids.long().view(-1) - e0
+    keep = (flat >= 0) & (flat < w_gu.shape[0])
+    flat = torch.where(keep, flat, torch.full_like(flat, w_gu.shape[0]))
     order = torch.argsort(flat, stable=True)
     experts, counts = torch.unique_consecutive(flat[order], return_counts=True)
     start = 0
     for e, c in zip(experts.tolist(), counts.tolist()):
         sel = order[start:start + c]
         start += c
+        if e >= w_gu.shape[0]:
+            continue
         rows = sel // topk
         y = swiglu(x[rows], w_gu[e], w_down[e])
         out.index_add_(0, rows, y.float() * w.view(-1)[sel, None])
-    if shared_gu is not None:
-        out += swiglu(x, shared_gu, shared_down).float()
-    return out.to(torch.bfloat16)
+    return out
 
 
 def piggyback_pack(scales: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, kmax: int) -> torch.Tensor:

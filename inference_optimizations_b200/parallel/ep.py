@@ -61,13 +61,50 @@ class EPLayout:
         return pair // d, pair % d
 
 
+class EPComm:
+    """The symmetric buffer, barrier epoch and scratch of the exchange: one per (group, T_max, shape), shared by every
+    MoE layer of a model (layers run one after another, so one buffer serves them all and the epoch keeps counting)."""
+
+    def __init__(self, rank: int, world: int, T_max: int, topk: int, H: int, F: int, fmt: str, E_loc: int,
+                 has_shared: bool, device, group=None):
+        import torch.distributed._symmetric_memory as symm
+        self.rank, self.world, self.T_max, self.topk, self.E_loc = rank, world, T_max, topk, E_loc
+        kind = 0 if fmt == "fp8" else 1
+        L = self.layout = EPLayout(world, T_max, topk, H, fmt)
+        self.buf = symm.empty(L.nbytes, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        grp = group if group is not None else dist.group.WORLD
+        self.handle = symm.rendezvous(self.buf, grp)
+        self.peers = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64, device=device)
+        rows = world * T_max
+        self.recv_x = self.buf[L.off_x:L.off_x + rows * L.row_bytes].view(rows, L.row_bytes)
+        self.recv_s = self.buf[L.off_s:L.off_s + rows * L.scale_words * 4].view(torch.int32).view(rows, L.scale_words)
+        self.recv_ids = self.buf[L.off_ids:L.off_ids + rows * topk * 4].view(torch.int32)
+        self.comb = self.buf[L.off_comb:L.off_comb + L.comb_rows * H * 2].view(torch.bfloat16).view(L.comb_rows, H)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.xq = torch.zeros(T_max, L.row_bytes, dtype=torch.uint8, device=device)
+        self.xs = torch.zeros(T_max, L.scale_words, dtype=torch.int32, device=device)
+        nb = E_loc + (1 if has_shared else 0)
+        self.off = torch.zeros(nb + 1, dtype=torch.int32, device=device)
+        self.pairs = torch.zeros(L.pairs_total + T_max, dtype=torch.int32, device=device)
+        hb = F if kind == 0 else F // 2
+        hw = F // 128 if kind == 0 else F // 64
+        self.h = torch.zeros(L.pairs_total + T_max, hb, dtype=torch.uint8, device=device)
+        self.hs = torch.zeros(L.pairs_total + T_max, hw, dtype=torch.int32, device=device)
+        self.nt = MG.tactic_nt(world * T_max, fmt) or MG.pick_nt(max(1, -(-2 * L.pairs_total // (world * E_loc))))
+        torch.cuda.synchronize(device)
+        dist.barrier(group=grp)
+
+
 class EPMoE:
     def __init__(self, rank: int, world: int, E_total: int, T_max: int, topk: int, w_gate: torch.Tensor = None,
                  w_up: torch.Tensor = None, w_down: torch.Tensor = None, shared: tuple | None = None,
-                 fmt: str = "fp8", group=None, experts: MG.BlockScaledExperts | None = None):
+                 fmt: str = "fp8", group=None, experts: MG.BlockScaledExperts | None = None,
+                 comm: EPComm | None = None):
         """w_gate / w_up [E_loc, F, H], w_down [E_loc, H, F]: this rank's experts (global ids rank * E_loc ..);
-        or `experts`: an already packed BlockScaledExperts of this rank's E_loc experts."""
-        import torch.distributed._symmetric_memory as symm
+        or `experts`: an already packed BlockScaledExperts of this rank's E_loc experts.  `comm`: a shared EPComm
+        (the layers of one model share it); None allocates one for this layer (a collective)."""
         self.rank, self.world, self.T_max, self.topk = rank, world, T_max, topk
         self.E_loc = E_total // world
         if experts is None:
@@ -75,35 +112,14 @@ class EPMoE:
             experts = MG.BlockScaledExperts(w_gate, w_up, w_down, shared=shared, fmt=fmt)
         self.ex = experts
         self.fmt, self.kind, self.H, self.F = experts.fmt, self.ex.kind, self.ex.H, self.ex.F
-        shared = shared if shared is not None else (True if experts.has_shared else None)
-        dev = experts.w1.device
-        L = self.layout = EPLayout(world, T_max, topk, self.H, self.fmt)
-        self.buf = symm.empty(L.nbytes, dtype=torch.uint8, device=dev)
-        self.buf.zero_()
-        grp = group if group is not None else dist.group.WORLD
-        self.handle = symm.rendezvous(self.buf, grp)
-        self.peers = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64, device=dev)
-        rows = world * T_max
-        self.recv_x = self.buf[L.off_x:L.off_x + rows * L.row_bytes].view(rows, L.row_bytes)
-        self.recv_s = self.buf[L.off_s:L.off_s + rows * L.scale_words * 4].view(torch.int32).view(rows, L.scale_words)
-        self.recv_ids = self.buf[L.off_ids:L.off_ids + rows * topk * 4].view(torch.int32)
-        self.comb = self.buf[L.off_comb:L.off_comb + L.comb_rows * self.H * 2].view(torch.bfloat16).view(
-            L.comb_rows, self.H)
-        self.epoch = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.xq = torch.zeros(T_max, L.row_bytes, dtype=torch.uint8, device=dev)
-        self.xs = torch.zeros(T_max, L.scale_words, dtype=torch.int32, device=dev)
-        nb = self.E_loc + (1 if shared is not None else 0)
-        self.off = torch.zeros(nb + 1, dtype=torch.int32, device=dev)
-        self.pairs = torch.zeros(L.pairs_total + T_max, dtype=torch.int32, device=dev)
-        hb = self.F if self.kind == 0 else self.F // 2
-        hw = self.F // 128 if self.kind == 0 else self.F // 64
-        self.h = torch.zeros(L.pairs_total + T_max, hb, dtype=torch.uint8, device=dev)
-        self.hs = torch.zeros(L.pairs_total + T_max, hw, dtype=torch.int32, device=dev)
-        self.nt = MG.tactic_nt(world * T_max, self.fmt) or MG.pick_nt(
-            max(1, -(-2 * L.pairs_total // (world * self.E_loc))))
-        torch.cuda.synchronize(dev)
-        dist.barrier(group=grp)
+        if comm is None:
+            comm = EPComm(rank, world, T_max, topk, self.H, self.F, self.fmt, self.E_loc, experts.has_shared,
+                          experts.w1.device, group)
+        assert (comm.T_max, comm.topk, comm.world, comm.E_loc) == (T_max, topk, world, self.E_loc)
+        self.comm = comm
+        for name in ("layout", "buf", "handle", "peers", "recv_x", "recv_s", "recv_ids", "comb", "epoch", "status",
+                     "xq", "xs", "off", "pairs", "h", "hs", "nt"):
+            setattr(self, name, getattr(comm, name))
 
     def barrier(self) -> None:
         ext().ep_barrier(self.peers, self.layout.off_flags, self.rank, self.world, self.epoch, self.status)
@@ -140,3 +156,45 @@ class EPMoE:
     def check(self) -> None:
         if int(self.status.item()) != 0:
             raise RuntimeError(f"expert-parallel exchange: status {int(self.status.item())}")
+
+
+class EPMoERef:
+    """Expert parallelism by plain collectives (any backend; gloo on the CPU): token rows, ids and weights of every
+    rank are all-gathered (padded to T_max), each rank applies its E / world routed experts to every pair routed to
+    them and its shared-expert replica to its own tokens, and a sum all-reduce hands every rank its rows.  Same
+    interface and lockstep contract as `EPMoE` (every rank calls forward for every MoE layer, idle ranks with T = 0);
+    the host-side oracle of the expert-parallel serving loop."""
+
+    def __init__(self, rank: int, world: int, E_total: int, T_max: int, topk: int, w_gu: torch.Tensor,
+                 w_down: torch.Tensor, shared: tuple | None = None, group=None):
+        self.rank, self.world, self.T_max, self.topk = rank, world, T_max, topk
+        self.E_loc = E_total // world
+        assert w_gu.shape[0] == self.E_loc, "pass this rank's slice of the experts"
+        self.w_gu, self.w_down, self.shared, self.group = w_gu, w_down, shared, group
+        self.H = w_down.shape[1]
+
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        from ..ops import moe as MOE
+        T, k = ids.shape
+        if T > self.T_max:
+            raise ValueError(f"{T} tokens > T_max {self.T_max}")
+        dev = x.device
+        xp = torch.zeros(self.T_max, self.H, dtype=x.dtype, device=dev)
+        ip = torch.full((self.T_max, k), -1, dtype=torch.int32, device=dev)
+        wp = torch.zeros(self.T_max, k, dtype=torch.float32, device=dev)
+        xp[:T], ip[:T], wp[:T] = x, ids, w.float()
+        xs = [torch.empty_like(xp) for _ in range(self.world)]
+        is_ = [torch.empty_like(ip) for _ in range(self.world)]
+        ws = [torch.empty_like(wp) for _ in range(self.world)]
+        dist.all_gather(xs, xp, group=self.group)
+        dist.all_gather(is_, ip, group=self.group)
+        dist.all_gather(ws, wp, group=self.group)
+        X, I, W = torch.cat(xs), torch.cat(is_), torch.cat(ws)
+        out = MOE.experts_ref(X, I, W, self.w_gu, self.w_down, self.rank * self.E_loc)
+        if self.shared is not None and T:
+            out[self.rank * self.T_max:self.rank * self.T_max + T] += MOE.swiglu(x, *self.shared).float()
+        dist.all_reduce(out, group=self.group)
+        return out[self.rank * self.T_max:self.rank * self.T_max + T].to(torch.bfloat16)
+
+    def check(self) -> None:
+        pass

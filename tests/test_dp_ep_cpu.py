@@ -1,0 +1,68 @@
+"""Data-parallel attention + expert-parallel MoE on CPU ranks (gloo): each rank serves its own requests, the MoE
+layers exchange tokens with the collective EP reference, idle ranks join the exchanges, and the outputs equal a
+single-process engine holding every expert.
+
+The random init is EP-invariant (each expert seeded by its own name), so the EP=2 model is the EP=1 model split.
+"""
+import os
+import socket
+
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from inference_optimizations_b200.config import EngineConfig, model_config
+from inference_optimizations_b200.engine.engine import Engine
+from inference_optimizations_b200.engine.scheduler import SamplingParams
+
+# rank 0 gets three prompts (one long: chunked prefill over several steps), rank 1 one short prompt -> rank 1 idles
+PROMPTS = [[(17 * i + 5 * j) % 500 + 1 for j in range(20 + 45 * i)] for i in range(4)]
+SPLIT = {0: [0, 2, 3], 1: [1]}
+
+
+def _engine(ep: int, rank: int, spec: bool = False) -> Engine:
+    ecfg = EngineConfig(model="tiny_mla", device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=32,
+                        cuda_graphs=False, ep=ep, prefix_cache=False, spec=spec, spec_policy="always")
+    return Engine(ecfg, model_config("tiny_mla"), max_seq=256, ep_rank=rank,
+                  ep_group=dist.group.WORLD if ep > 1 else None)
+
+
+def _worker(rank: int, port: int, spec: bool, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2")
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    try:
+        eng = _engine(2, rank, spec)
+        assert eng.runner.model.layers[-1].ffn["w_gu"].shape[0] == model_config("tiny_mla").num_experts // 2
+        outs = eng.generate_dp([PROMPTS[i] for i in SPLIT[rank]], SamplingParams(max_new_tokens=6))
+        q.put((rank, outs))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(spec: bool) -> None:
+    ref = _engine(1, 0, spec).generate(PROMPTS, SamplingParams(max_new_tokens=6))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, port, spec, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    for rank, idx in SPLIT.items():
+        assert got[rank] == [ref[i] for i in idx], (rank, got[rank], [ref[i] for i in idx])
+
+
+def test_dp_attention_ep_moe_matches_single_process():
+    _run(spec=False)
+
+
+def test_dp_ep_with_mtp_speculation():
+    _run(spec=True)
