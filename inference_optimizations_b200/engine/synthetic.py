@@ -64,3 +64,44 @@ def synth_decode_sessions(engine, n: int, ctx: int, max_new: int, seed: int = 0)
     if hasattr(runner, "after_synthetic"):
         runner.after_synthetic(reqs)
     return reqs
+
+
+def synth_mla_sessions(engine, n: int, ctx: int, max_new: int, seed: int = 0, chunk: int = 1 << 16) -> list:
+    """MLA family: register n running requests whose first `ctx` positions are in the latent and index pools (random
+    latents / rope / index keys written through the pool writers, so every row is well formed) and whose next input
+    token is set."""
+    from ..ops import kvcache as K
+    runner, sched = engine.runner, engine.sched
+    cfg = engine.cfg
+    g = torch.Generator()
+    g.manual_seed(seed)
+    reqs, slots = [], []
+    for _ in range(n):
+        prompt = torch.randint(1, cfg.vocab, (ctx,), generator=g).tolist()
+        r = sched.new_request(prompt, SamplingParams(max_new_tokens=max_new))
+        sched.waiting.remove(r)
+        r.slot = sched.free_slots.pop()
+        runner.attach(r)
+        rp = runner.pages[r.rid]
+        rp.ensure(ctx)
+        slots += [rp.slot_of(p) for p in range(ctx)]
+        r.prefilled = r.kv_len = ctx
+        r.pending = int(torch.randint(1, cfg.vocab, (1,), generator=g))
+        r.output.append(r.pending)
+        sched.running.append(r)
+        reqs.append(r)
+    runner.kv.table.sync()
+    dev = runner.device
+    slot_t = torch.tensor(slots, dtype=torch.int32, device=dev)
+    gd = torch.Generator(device=dev)
+    gd.manual_seed(seed)
+    for layer in range(len(runner.kv.latent)):
+        for lo in range(0, slot_t.numel(), chunk):
+            s = slot_t[lo:lo + chunk]
+            m = s.numel()
+            lat = torch.randn(m, cfg.kv_lora, generator=gd, device=dev).to(torch.bfloat16)
+            rope = torch.randn(m, cfg.qk_rope, generator=gd, device=dev).to(torch.bfloat16)
+            K.mla_write(lat, rope, s, runner.kv.latent[layer])
+            ik = torch.randn(m, cfg.index_dim, generator=gd, device=dev).to(torch.bfloat16)
+            K.index_key_write(ik, s, runner.kv.index[layer])
+    return reqs

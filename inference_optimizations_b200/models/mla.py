@@ -214,6 +214,7 @@ class MLAModel:
                                      c.num_experts // self.ep_world, ex.has_shared, self.device, group)
                 self.ep[i] = EP.EPMoE(self.ep_rank, self.ep_world, c.num_experts, T_max, c.topk, experts=ex,
                                       comm=comm)
+                f["w_gu"] = f["w_down"] = None   # the packed FP8 / NVFP4 copy is the only one kept
             else:
                 shared = (f["shared_gu"], f["shared_down"]) if f["shared_gu"] is not None else None
                 self.ep[i] = EP.EPMoERef(self.ep_rank, self.ep_world, c.num_experts, T_max, c.topk, f["w_gu"],

@@ -100,3 +100,17 @@ def test_mla_mtp_speculation_preserves_greedy_output():
     r.draft_state["d"] = want[1]                    # the token greedy decoding produces after r.pending
     got = eng.runner.spec_decode([r])[r.rid]
     assert got == want[1:3], (got, want)
+
+
+def test_synthetic_mla_sessions_decode():
+    """Synthetic MLA sessions (pools filled through the writers) decode like any running request."""
+    from inference_optimizations_b200.config import EngineConfig, model_config
+    from inference_optimizations_b200.engine.engine import Engine
+    from inference_optimizations_b200.engine.synthetic import synth_mla_sessions
+    ecfg = EngineConfig(model="tiny_mla", device="cpu", kv_dtype="nvfp4", max_running=3, chunked_prefill=32,
+                        cuda_graphs=False, prefix_cache=False)
+    eng = Engine(ecfg, model_config("tiny_mla"), max_seq=256)
+    reqs = synth_mla_sessions(eng, 3, 100, 4, seed=1)
+    assert all(r.kv_len == 100 for r in reqs)
+    out = eng.step()
+    assert sorted(out) == sorted(r.rid for r in reqs) and all(len(v) == 1 for v in out.values())
