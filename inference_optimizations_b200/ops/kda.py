@@ -65,6 +65,78 @@ def kda_decode(q, k, v, g_proj, dt_bias, A_log, beta, g2, norm_w, cwq, cwk, cwv,
     return out
 
 
+# ------------------------------------------------------------------------------------------------ chunked prefill
+def kda_prefill(q, k, v, g_proj, dt_bias, A_log, beta, g2, norm_w, cwq, cwk, cwv, csq, csk, csv, state,
+                scale=None, chunk: int = 64):
+    """Prefill of T tokens per sequence in chunks (the FlashKDA idea, `linear-attention-kda/flashkda-split`: the
+    sequential recurrence over T tokens becomes T / chunk sequential steps of dense chunk math).  Inputs are the
+    decode step's with a time axis: q/k [B, T, H, DK], v [B, T, HV, DV], g_proj [B, T, HV, DK], beta [B, T, HV]
+    (or [B, T, HV, DV]), g2 [B, T, HV, DV]; conv and recurrent states updated in place; returns o [B, T, HV, DV]
+    bf16, equal to T calls of `kda_decode_ref` up to fp32 rounding.
+
+    Within a chunk with state S0 (value-major [DV, DK]) and per-key-channel log decays G_t = cumsum(g) (so every
+    exponent below is G_t - G_i <= 0): S_t = S0 diag(e^{G_t}) + sum_{i <= t} w_i (k_i * e^{G_t - G_i})^T, where the
+    pseudo-values solve the unit-lower-triangular system
+        w_t + beta_t * sum_{i < t} [(k_i * e^{G_t - G_i}) . k_t] w_i = beta_t * (v_t - S0 (k_t * e^{G_t}));
+    then o_t = S_t q_t and S_C closes the chunk."""
+    B, T, H, DK = q.shape
+    HV, DV = v.shape[2], v.shape[3]
+    W = cwq.shape[1]
+    rep = HV // H
+    scale = DK ** -0.5 if scale is None else scale
+
+    def conv(x, w, st):                      # x [B, T, C], w [C, W], st [B, C, W-1]
+        xx = torch.cat([st.transpose(1, 2), x], 1)                          # [B, T + W - 1, C]
+        y = sum(xx[:, j:j + T] * w[None, None, :, j] for j in range(W))
+        st.copy_(xx[:, T:].transpose(1, 2))
+        return Fn.silu(y)
+
+    qc = conv(q.float().reshape(B, T, -1), cwq, csq.view(B, H * DK, W - 1)).view(B, T, H, DK)
+    kc = conv(k.float().reshape(B, T, -1), cwk, csk.view(B, H * DK, W - 1)).view(B, T, H, DK)
+    vc = conv(v.float().reshape(B, T, -1), cwv, csv.view(B, HV * DV, W - 1)).view(B, T, HV, DV)
+    gp = g_proj.float() + dt_bias.view(HV, DK)[None, None]
+    sp = torch.where(gp > 20, gp, torch.log1p(torch.exp(gp)))
+    g = -torch.exp(A_log.float())[None, None, :, None] * sp                 # [B, T, HV, DK]
+    qn = (qc / torch.sqrt((qc * qc).sum(-1, keepdim=True) + 1e-6) * scale).repeat_interleave(rep, 2)
+    kn = (kc / torch.sqrt((kc * kc).sum(-1, keepdim=True) + 1e-6)).repeat_interleave(rep, 2)
+    bt = beta.float()
+    # head-major [B, HV, T, .]
+    qn, kn, vc, g = (t.transpose(1, 2) for t in (qn, kn, vc, g))
+    bt = bt.transpose(1, 2)
+    S = state.view(B, HV, DV, DK)
+    out = torch.empty(B, HV, T, DV, dtype=torch.float32, device=q.device)
+    for c0 in range(0, T, chunk):
+        c1 = min(T, c0 + chunk)
+        C = c1 - c0
+        Kc, Qc, Vc = kn[:, :, c0:c1], qn[:, :, c0:c1], vc[:, :, c0:c1]
+        G = torch.cumsum(g[:, :, c0:c1], 2)                                # [B, HV, C, DK]
+        tri = torch.tril(torch.ones(C, C, dtype=torch.bool, device=q.device))
+        D = G[:, :, :, None, :] - G[:, :, None, :, :]                        # [B, HV, t, i, DK]
+        E = torch.exp(D.masked_fill(~tri[None, None, :, :, None], float("-inf")))   # i <= t only (exponent <= 0)
+        KK = torch.einsum("bhtd,bhid,bhtid->bhti", Kc, Kc, E)                # (k_i e^{G_t - G_i}) . k_t
+        QK = torch.einsum("bhtd,bhid,bhtid->bhti", Qc, Kc, E)                # (k_i e^{G_t - G_i}) . q_t, i <= t
+        strict = torch.tril(torch.ones(C, C, device=q.device), -1)
+        Kt = Kc * torch.exp(G)                                               # k_t * e^{G_t}
+        rhs = Vc - torch.einsum("bhtd,bhvd->bhtv", Kt, S)                   # v_t - S0 (k_t e^{G_t})
+        if bt.dim() == 3:                                                    # one beta per head and token
+            b_ = bt[:, :, c0:c1]
+            A = torch.eye(C, device=q.device) + b_[..., None] * KK * strict
+            Wv = torch.linalg.solve_triangular(A, b_[..., None] * rhs, upper=False, unitriangular=True)
+        else:                                                                # a beta per value row
+            b_ = bt[:, :, c0:c1].transpose(2, 3)                             # [B, HV, DV, C]
+            A = torch.eye(C, device=q.device) + b_[..., None] * (KK * strict)[:, :, None]
+            Wv = torch.linalg.solve_triangular(A, (b_ * rhs.transpose(2, 3))[..., None], upper=False,
+                                               unitriangular=True)[..., 0].transpose(2, 3)
+        out[:, :, c0:c1] = torch.einsum("bhtd,bhvd->bhtv", Qc * torch.exp(G), S) + torch.einsum(
+            "bhti,bhiv->bhtv", QK, Wv)
+        Gl = G[:, :, -1]                                                     # [B, HV, DK]
+        S.mul_(torch.exp(Gl)[:, :, None, :]).add_(
+            torch.einsum("bhiv,bhid->bhvd", Wv, Kc * torch.exp(Gl[:, :, None, :] - G)))
+    o = out.transpose(1, 2) * torch.sigmoid(g2.float())                     # [B, T, HV, DV]
+    o = o / torch.sqrt((o * o).mean(-1, keepdim=True) + 1e-5) * norm_w.float()
+    return o.to(torch.bfloat16)
+
+
 # ------------------------------------------------------------------------------------------------ state rows
 ROW_BYTES = {"fp8": 132, "bf16": 256, "nvfp4": 76}
 

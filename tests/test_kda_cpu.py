@@ -50,3 +50,40 @@ def test_state_store_park_load():
     assert st.nbytes() == 2 * 4 * 128 * 132
     back = st.load("r1")
     assert back.shape == s.shape and ((back - s).norm() / s.norm()) < 0.07
+
+
+def _seq_inputs(B, T, H, seed, headwise):
+    g = torch.Generator().manual_seed(seed)
+    r = lambda *s: torch.randn(*s, generator=g)  # noqa: E731
+    DK = DV = 128
+    W = 4
+    return dict(q=r(B, T, H, DK).to(torch.bfloat16), k=r(B, T, H, DK).to(torch.bfloat16),
+                v=r(B, T, H, DV).to(torch.bfloat16), g_proj=r(B, T, H, DK).to(torch.bfloat16),
+                dt_bias=r(H * DK) * 0.1, A_log=r(H) * 0.1,
+                beta=torch.sigmoid(r(B, T, H, DV) if headwise else r(B, T, H)),
+                g2=r(B, T, H, DV).to(torch.bfloat16), norm_w=1 + 0.1 * r(DV), cwq=r(H * DK, W) * 0.3,
+                cwk=r(H * DK, W) * 0.3, cwv=r(H * DV, W) * 0.3, csq=r(B, H * DK, W - 1), csk=r(B, H * DK, W - 1),
+                csv=r(B, H * DV, W - 1), state=r(B, H, DV, DK) * 0.1)
+
+
+import pytest  # noqa: E402
+
+
+@pytest.mark.parametrize("headwise", [False, True])
+def test_chunked_prefill_matches_recurrence(headwise):
+    """The chunked prefill (a 100-token sequence: one full 64-token chunk and a partial one) equals 100 decode steps
+    of the oracle: outputs, recurrent state and conv states."""
+    B, T, H = 2, 100, 2
+    a = _seq_inputs(B, T, H, 3, headwise)
+    ref = {k: (v.clone() if k in ("csq", "csk", "csv", "state") else v) for k, v in a.items()}
+    outs = []
+    for t in range(T):
+        step = {k: (v[:, t] if k in ("q", "k", "v", "g_proj", "beta", "g2") else v) for k, v in ref.items()}
+        outs.append(KD.kda_decode_ref(**step))
+    want = torch.stack(outs, 1).float()
+    got = KD.kda_prefill(**a, chunk=64).float()
+    assert got.shape == want.shape
+    assert (got - want).abs().max().item() < 3e-2          # bf16 outputs: one rounding step apart at most
+    assert torch.allclose(a["state"], ref["state"], rtol=1e-4, atol=1e-5)
+    for c in ("csq", "csk", "csv"):
+        assert torch.allclose(a[c], ref[c])
