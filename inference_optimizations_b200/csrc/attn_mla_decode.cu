@@ -40,7 +40,7 @@ constexpr int kMPBytes = 128 * kMTile;                 // P: 128 heads x 128 row
 constexpr uint32_t kMColO = 0, kMColS = 256, kMColQ = 384;
 constexpr float kMTau = 8.f;                           // lazy-rescale threshold, log2 units
 constexpr int kMSoftmaxWarps = 4, kMDequantWarps = 8, kMMmaWarp = 12, kMPrefetchWarp = 13;
-constexpr int kF4Row = 352, kF8Row = 576;
+constexpr int kF4Row = 352, kF4FlashRow = 288, kF8Row = 576;
 
 struct MlaSmem {
   uint64_t tile_full[kMRing];   // tile rows stored                       (4 dequant-warp arrivals)
@@ -100,21 +100,25 @@ __device__ __forceinline__ uint32_t u4_get(const uint4& v, int k) {
 // 16 scales; E4M3: 256 bytes) and rope values [32 q, 32 q + 32).
 template <int FMT>
 struct RawRow {
-  uint4 v[FMT == kKvNvfp4 ? 8 : 16];
+  uint4 v[FMT == kKvFp8 ? 16 : 8];
   uint4 sc;
   uint4 rope[2];
 };
 
 template <int FMT>
 __device__ __forceinline__ void load_row(const uint8_t* row, int q, RawRow<FMT>& x) {
-  constexpr int NV = FMT == kKvNvfp4 ? 8 : 16;
+  constexpr int NV = FMT == kKvFp8 ? 16 : 8;
   if (row) {
-    if constexpr (FMT == kKvNvfp4) {
+    if constexpr (FMT != kKvFp8) {            // NVFP4 latent (352-B row; the 288-B row has no rope block)
 #pragma unroll
       for (int i = 0; i < NV; ++i) x.v[i] = ldg16(row + 128 * q + 16 * i);
       x.sc = ldg16(row + 256 + 16 * q);
-      x.rope[0] = ldg16(row + 288 + 32 * q);
-      x.rope[1] = ldg16(row + 288 + 32 * q + 16);
+      if constexpr (FMT == kKvNvfp4) {
+        x.rope[0] = ldg16(row + 288 + 32 * q);
+        x.rope[1] = ldg16(row + 288 + 32 * q + 16);
+      } else {
+        x.rope[0] = x.rope[1] = make_uint4(0, 0, 0, 0);
+      }
     } else {
 #pragma unroll
       for (int i = 0; i < NV; ++i) x.v[i] = ldg16(row + 256 * q + 16 * i);
@@ -134,7 +138,7 @@ __device__ __forceinline__ void load_row(const uint8_t* row, int q, RawRow<FMT>&
 // CTA's scale-byte -> E4M3 product table (f4_table_fill).
 template <int FMT>
 __device__ __forceinline__ uint4 row_chunk(const RawRow<FMT>& x, int c, const uint2* tabs) {
-  if constexpr (FMT == kKvNvfp4) {
+  if constexpr (FMT != kKvFp8) {
     const uint4& cw = x.v[c >> 1];                    // 32 values per code chunk
     const uint32_t sb = (u4_get(x.sc, c >> 2) >> (8 * (c & 3))) & 0xFFu;   // scale of these 16 values
     const uint2 tab = tabs[sb];
@@ -148,7 +152,7 @@ __device__ __forceinline__ uint4 row_chunk(const RawRow<FMT>& x, int c, const ui
 
 template <int FMT>
 __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecodeArgs a) {
-  constexpr int RB = FMT == kKvNvfp4 ? kF4Row : kF8Row;
+  constexpr int RB = FMT == kKvNvfp4 ? kF4Row : FMT == kKvNvfp4NoRope ? kF4FlashRow : kF8Row;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = base;                                  // 2 x 72 KB
@@ -182,7 +186,7 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
     sm.abort = 0;
     fence_mbar_init();
   }
-  if constexpr (FMT == kKvNvfp4) f4_table_fill(sm.f4tab);
+  if constexpr (FMT != kKvFp8) f4_table_fill(sm.f4tab);
   if (warp == kMMmaWarp) { tmem_alloc(&sm.tmem_base, 512); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
@@ -220,7 +224,9 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
         tmem_st32(tmem + lane_base + kMColQ + 64 * hf + 32 * b, w);
       }
 #pragma unroll
-      for (int c = 0; c < 2; ++c) *reinterpret_cast<uint4*>(sqr + sw64_chunk(h, 2 * hf + c)) = qv[16 + c];
+      for (int c = 0; c < 2; ++c)     // rope-free rows: the rope MMAs add q_pe . 0 (query rope zeroed)
+        *reinterpret_cast<uint4*>(sqr + sw64_chunk(h, 2 * hf + c)) =
+            FMT == kKvNvfp4NoRope ? make_uint4(0, 0, 0, 0) : qv[16 + c];
     }
     const float qs = hv ? a.q_scale[static_cast<size_t>(t) * a.H + h] : 1.f;
     tmem_st_wait();
@@ -379,7 +385,7 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
     auto row_ptr = [&](int id) -> const uint8_t* {
       return (id >= 0 && MLA_IN_RANGE(id < a.pool_rows, 3)) ? a.pool + static_cast<size_t>(id) * RB : nullptr;
     };
-    if constexpr (FMT == kKvNvfp4) {
+    if constexpr (FMT != kKvFp8) {
       // NVFP4: raw rows are loaded into registers a tile ahead.  The loads for tile j + 1 are issued right after
       // tile j is published: the proxy fence before the arrival would otherwise also wait for them.
       int id_cur = row_id(0), id_nxt = row_id(1);
@@ -642,6 +648,7 @@ cudaError_t mla_decode(const MlaDecodeArgs& a, cudaStream_t s) {
   if (a.num_splits > 1 && (!a.o_part || !a.lse_part)) return cudaErrorInvalidValue;
   switch (a.fmt) {
     case kKvNvfp4: return launch_mla<kKvNvfp4>(a, s);
+    case kKvNvfp4NoRope: return launch_mla<kKvNvfp4NoRope>(a, s);
     case kKvFp8: return launch_mla<kKvFp8>(a, s);
     default: return cudaErrorInvalidValue;
   }

@@ -3,7 +3,8 @@
 Semantics of the reference's sparse FP4 decode (`kv-cache-4bit/glm-kv4/glm_kv4.py:575-622` `sparse_mla`, the native
 `kv-cache-4bit/kv4mla/csrc/api.cpp:73` `sparse_decode`): query token t (H heads x 576 = 512 latent + 64 rope) attends to
 the pool rows idx[t, :] (-1 = masked); K = the full row, V = its 512 latent values; returns out [T, H, 512] and the
-natural-log LSE [T, H].  Rows are NVFP4 352-B rows (FMT_NVFP4) or E4M3 576-B rows (FMT_FP8)."""
+natural-log LSE [T, H].  Rows are NVFP4 352-B rows (FMT_NVFP4), E4M3 576-B rows (FMT_FP8) or rope-free NVFP4
+288-B rows (FMT_NVFP4_NOROPE, the GLM-Flash latent)."""
 from __future__ import annotations
 
 import math
@@ -16,9 +17,10 @@ from .._ext import ext
 from . import formats as F
 from .kvcache import FMT_FP8, FMT_NVFP4
 
+FMT_NVFP4_NOROPE = 3      # the rope-free 288-byte NVFP4 row (GLM-Flash latent): attention over the 512 latent dims
 NUM_SMS = 148
 TILE = 128                # rows per kernel tile (split granularity and lazy-rescale step)
-ROW_BYTES = {FMT_NVFP4: F.MLA_ROW_BYTES, FMT_FP8: F.MLA_FP8_ROW_BYTES}
+ROW_BYTES = {FMT_NVFP4: F.MLA_ROW_BYTES, FMT_FP8: F.MLA_FP8_ROW_BYTES, FMT_NVFP4_NOROPE: F.GLMFLASH_ROW_BYTES}
 
 
 def mla_split_policy(tokens: int, topk: int, overhead_tiles: float = 2.0) -> tuple[int, int]:
@@ -109,10 +111,14 @@ def mla_dense_decode(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tens
 
 
 def dequant_rows(pool: torch.Tensor, fmt: int) -> torch.Tensor:
+    """Rows -> fp32 [rows, 576] (latent, rope); the rope-free row's rope part is zero."""
     if fmt == FMT_NVFP4:
         return F.mla_row_dequantize(pool)
     if fmt == FMT_FP8:
         return F.mla_fp8_row_dequantize(pool)
+    if fmt == FMT_NVFP4_NOROPE:
+        lat = F.glmflash_row_dequantize(pool)
+        return torch.cat([lat, torch.zeros(lat.shape[0], 64, dtype=lat.dtype, device=lat.device)], -1)
     raise ValueError(fmt)
 
 
