@@ -333,12 +333,13 @@ class BlockScaledExperts:
             hs = torch.empty(P + extra, self.F // 64, dtype=torch.int32, device=dev)
         gemm(self.w1, xq, xs, off, pairs, h, self.status, n_tiles=self.F // TILE, kc=kc1, g=2, nt=nt, mode=1,
              src_div=k, src_limit=P, out_scale=hs, num_ctas=self.num_ctas, kind=self.kind, expert_mul=self.mul1)
-        pw = torch.cat([w.float().reshape(-1), torch.ones(extra, device=dev)])
+        # expert rows stay unweighted in bf16; the combine applies the routing weights in fp32 -- the same rounding
+        # points as the expert-parallel exchange (parallel/ep.py), so EP at any width reproduces this path bit for bit
         rows = torch.empty(P + extra, self.H, dtype=torch.bfloat16, device=dev)
         gemm(self.w2, h, hs, off, pairs, rows, self.status, n_tiles=self.H // (TILE * self.g2), kc=kc2, g=self.g2,
-             nt=nt, mode=2, src_div=1, pair_w=pw, num_ctas=self.num_ctas, kind=self.kind, expert_mul=self.mul2)
+             nt=nt, mode=0, src_div=1, num_ctas=self.num_ctas, kind=self.kind, expert_mul=self.mul2)
         y = torch.empty(t, self.H, dtype=torch.bfloat16, device=dev)
-        ext().moe_combine(rows, t, k, P if self.has_shared else -1, None, y)
+        ext().moe_combine(rows, t, k, P if self.has_shared else -1, w.float().contiguous(), y)
         return y
 
     def forward_ref(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
