@@ -40,7 +40,7 @@ constexpr int kMPBytes = 128 * kMTile;                 // P: 128 heads x 128 row
 constexpr uint32_t kMColO = 0, kMColS = 256, kMColQ = 384;
 constexpr float kMTau = 8.f;                           // lazy-rescale threshold, log2 units
 constexpr int kMSoftmaxWarps = 4, kMDequantWarps = 8, kMMmaWarp = 12, kMPrefetchWarp = 13;
-constexpr int kF4Row = 352, kF4FlashRow = 288, kF8Row = 576;
+constexpr int kF4Row = 352, kF4FlashRow = 288, kV4ProRow = 320, kF8Row = 576;
 
 struct MlaSmem {
   uint64_t tile_full[kMRing];   // tile rows stored                       (4 dequant-warp arrivals)
@@ -109,7 +109,15 @@ template <int FMT>
 __device__ __forceinline__ void load_row(const uint8_t* row, int q, RawRow<FMT>& x) {
   constexpr int NV = FMT == kKvFp8 ? 16 : 8;
   if (row) {
-    if constexpr (FMT != kKvFp8) {            // NVFP4 latent (352-B row; the 288-B row has no rope block)
+    if constexpr (FMT == kKvV4Pro) {
+      // 320-byte cell: 448 latent values (codes at 0..223, scales at 224..251, zero pad to 256) + 64 E4M3 rope at
+      // 256; latent dims 448..511 read as zero codes (thread 1's last two code chunks) under the zero pad scales
+#pragma unroll
+      for (int i = 0; i < NV; ++i) x.v[i] = (q == 0 || i < 6) ? ldg16(row + 128 * q + 16 * i) : make_uint4(0, 0, 0, 0);
+      x.sc = ldg16(row + 224 + 16 * q);
+      x.rope[0] = ldg16(row + 256 + 32 * q);
+      x.rope[1] = ldg16(row + 256 + 32 * q + 16);
+    } else if constexpr (FMT != kKvFp8) {     // NVFP4 latent (352-B row; the 288-B row has no rope block)
 #pragma unroll
       for (int i = 0; i < NV; ++i) x.v[i] = ldg16(row + 128 * q + 16 * i);
       x.sc = ldg16(row + 256 + 16 * q);
@@ -152,7 +160,8 @@ __device__ __forceinline__ uint4 row_chunk(const RawRow<FMT>& x, int c, const ui
 
 template <int FMT>
 __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecodeArgs a) {
-  constexpr int RB = FMT == kKvNvfp4 ? kF4Row : FMT == kKvNvfp4NoRope ? kF4FlashRow : kF8Row;
+  constexpr int RB = FMT == kKvNvfp4 ? kF4Row : FMT == kKvNvfp4NoRope ? kF4FlashRow : FMT == kKvV4Pro ? kV4ProRow
+                                                                                                    : kF8Row;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = base;                                  // 2 x 72 KB
@@ -649,6 +658,7 @@ cudaError_t mla_decode(const MlaDecodeArgs& a, cudaStream_t s) {
   switch (a.fmt) {
     case kKvNvfp4: return launch_mla<kKvNvfp4>(a, s);
     case kKvNvfp4NoRope: return launch_mla<kKvNvfp4NoRope>(a, s);
+    case kKvV4Pro: return launch_mla<kKvV4Pro>(a, s);
     case kKvFp8: return launch_mla<kKvFp8>(a, s);
     default: return cudaErrorInvalidValue;
   }
