@@ -42,7 +42,7 @@ def _time(fn, iters: int = 10) -> float:
 
 
 def gqa_decode_case(b: int, hk: int, hq: int, d: int, ctx: int, fmt_name: str, n_q: int, window: int,
-                    launches: int = 0) -> dict:
+                    launches: int = 0, splits_override: str = "") -> dict:
     from ..engine.synthetic import fill_pool_random
     from ..ops import attention as A
     from ..ops import kvcache as K
@@ -56,6 +56,8 @@ def gqa_decode_case(b: int, hk: int, hq: int, d: int, ctx: int, fmt_name: str, n
     kv_len = torch.full((b,), ctx, dtype=torch.int32, device=dev)
     q = torch.randn(b * n_q, hq, d, device=dev).to(torch.bfloat16)
     splits = A.split_policy(b * hk, ctx, window)
+    if splits_override:                       # "num_splits,tiles_per_split"
+        splits = tuple(int(v) for v in splits_override.split(","))
     ws = A.DecodeWorkspace.allocate(b, hk, splits[0], d, device=dev)
 
     def fn():
@@ -431,6 +433,7 @@ def main() -> None:
     p.add_argument("--fmt", default="nvfp4")
     p.add_argument("--nq", type=int, default=1)
     p.add_argument("--chunk", type=int, default=2048)
+    p.add_argument("--splits", default="", help="gqa_decode: force (num_splits,tiles_per_split)")
     p.add_argument("--window", type=int, default=0)
     p.add_argument("--topk", type=int, default=2048)
     p.add_argument("--launches", type=int, default=0)
@@ -441,7 +444,7 @@ def main() -> None:
     p.add_argument("--wfmt", default="fp8", choices=["fp8", "nvfp4"])
     a = p.parse_args()
     if a.kernel == "gqa_decode":
-        r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches)
+        r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches, a.splits)
     elif a.kernel == "gqa_extend":
         r = gqa_extend_case(a.chunk, a.ctx, a.hk, a.hq, a.d, a.fmt, a.window, a.launches)
     elif a.kernel == "indexer":
