@@ -87,27 +87,55 @@ __device__ __forceinline__ uint64_t desc_sf(uint32_t addr) {
 __device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
-// Block-scaled E4M3 x E4M3 MMA with UE8M0 scales per 32 K-values (scale TMEM addresses carry the byte index in
-// their top two bits, mirrored in the descriptor's scale-factor id fields).
-__device__ __forceinline__ void umma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                          uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
-      : "memory");
-}
-// Block-scaled packed-E2M1 MMA with E4M3 scales per 16 K-values (NVFP4), K = 64 per instruction.
-__device__ __forceinline__ void umma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                          uint32_t sfa, uint32_t sfb, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
-          d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
-      : "memory");
+// Block-scaled MMAs: scale TMEM addresses carry the byte index in their top two bits, mirrored in the instruction
+// descriptor's scale-factor id fields; kind::mxf8f6f4 takes UE8M0 scales per 32 K values (E4M3 operands, K = 32),
+// kind::mxf4nvf4 E4M3 scales per 16 (packed E2M1 operands, K = 64).
+// Four MMAs per asm statement (MMA i: d[i], a[i], b[i], idesc[i], scale TMEM addresses sfa[i] / sfb[i],
+// accumulate iff bit i of acc_mask): issued one per statement, consecutive tcgen05.mma instructions were measured
+// ~250 cycles apart from one lane whatever their shape; in batches of four they issue several times faster.
+// KIND 0: kind::mxf8f6f4.block_scale (UE8M0 / 32), 1: kind::mxf4nvf4.block_scale.block16, 2: kind::f16 (no scales).
+template <int KIND>
+__device__ __forceinline__ void umma_bs_x4(const uint32_t (&d)[4], const uint64_t (&a)[4], const uint64_t (&b)[4],
+                                           const uint32_t (&idesc)[4], const uint32_t (&sfa)[4],
+                                           const uint32_t (&sfb)[4], uint32_t acc_mask) {
+  if constexpr (KIND == 2) {
+    asm volatile(
+        "{\n\t.reg .pred p0, p1, p2, p3;\n\t"
+        "setp.ne.b32 p0, %16, 0;\n\tsetp.ne.b32 p1, %17, 0;\n\tsetp.ne.b32 p2, %18, 0;\n\tsetp.ne.b32 p3, %19, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %12, p0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%1], %5, %9, %13, p1;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%2], %6, %10, %14, p2;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%3], %7, %11, %15, p3;\n\t}\n" ::"r"(d[0]),
+        "r"(d[1]), "r"(d[2]), "r"(d[3]), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]),
+        "l"(b[2]), "l"(b[3]), "r"(idesc[0]), "r"(idesc[1]), "r"(idesc[2]), "r"(idesc[3]), "r"(acc_mask & 1u),
+        "r"(acc_mask & 2u), "r"(acc_mask & 4u), "r"(acc_mask & 8u));
+  } else {
+    if constexpr (KIND == 0) {
+      asm volatile(
+          "{\n\t.reg .pred p0, p1, p2, p3;\n\t"
+          "setp.ne.b32 p0, %24, 0;\n\tsetp.ne.b32 p1, %25, 0;\n\tsetp.ne.b32 p2, %26, 0;\n\tsetp.ne.b32 p3, %27, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %4, %8, %12, [%16], [%20], p0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%1], %5, %9, %13, [%17], [%21], p1;\n\t"
+          "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%2], %6, %10, %14, [%18], [%22], p2;\n\t"
+          "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%3], %7, %11, %15, [%19], [%23], p3;\n\t}\n" ::"r"(d[0]),
+          "r"(d[1]), "r"(d[2]), "r"(d[3]), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]),
+          "l"(b[2]), "l"(b[3]), "r"(idesc[0]), "r"(idesc[1]), "r"(idesc[2]), "r"(idesc[3]), "r"(sfa[0]), "r"(sfa[1]),
+          "r"(sfa[2]), "r"(sfa[3]), "r"(sfb[0]), "r"(sfb[1]), "r"(sfb[2]), "r"(sfb[3]), "r"(acc_mask & 1u),
+          "r"(acc_mask & 2u), "r"(acc_mask & 4u), "r"(acc_mask & 8u));
+    } else {
+      asm volatile(
+          "{\n\t.reg .pred p0, p1, p2, p3;\n\t"
+          "setp.ne.b32 p0, %24, 0;\n\tsetp.ne.b32 p1, %25, 0;\n\tsetp.ne.b32 p2, %26, 0;\n\tsetp.ne.b32 p3, %27, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %4, %8, %12, [%16], [%20], p0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%1], %5, %9, %13, [%17], [%21], p1;\n\t"
+          "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%2], %6, %10, %14, [%18], [%22], p2;\n\t"
+          "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%3], %7, %11, %15, [%19], [%23], p3;\n\t}\n" ::"r"(d[0]),
+          "r"(d[1]), "r"(d[2]), "r"(d[3]), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]),
+          "l"(b[2]), "l"(b[3]), "r"(idesc[0]), "r"(idesc[1]), "r"(idesc[2]), "r"(idesc[3]), "r"(sfa[0]), "r"(sfa[1]),
+          "r"(sfa[2]), "r"(sfa[3]), "r"(sfb[0]), "r"(sfb[1]), "r"(sfb[2]), "r"(sfb[3]), "r"(acc_mask & 1u),
+          "r"(acc_mask & 2u), "r"(acc_mask & 4u), "r"(acc_mask & 8u));
+    }
+  }
 }
 // kind::mxf4nvf4 descriptor: E2M1 x E2M1 (format code 1), both K-major, E4M3 scales, M = 128, K = 64.
 __host__ __device__ constexpr uint32_t idesc_nvf4(uint32_t n) {
@@ -286,21 +314,35 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
 #pragma unroll
           for (int w = 0; w < kSfw; ++w) tmem_cp_sf(tmem + sfb_col + 4 * w, desc_sf(sfb_s + w * kSfAtom));
           (void)sfb_s;
+          // the 4 G MMAs of this stage (K steps j outer, weight tiles g inner), four per asm statement
+          static_assert((4 * G) % 4 == 0, "MMAs come in batches of four");
+          uint32_t d4[4], i4[4], fa4[4], fb4[4], mask = 0;
+          uint64_t a4[4], b4[4];
+          int n4 = 0;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint64_t bd = desc_sw128(x_s + 32 * j);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
+              d4[n4] = acc + g * NT;
+              a4[n4] = desc_sw128(st + g * kTile + 32 * j);
+              b4[n4] = desc_sw128(x_s + 32 * j);
               if constexpr (KIND == 2) {
-                umma_f16_ss(acc + g * NT, desc_sw128(st + g * kTile + 32 * j), bd, idesc_dense(1, 1, 128, NT),
-                            (kc | j) ? 1u : 0u);
+                i4[n4] = idesc_dense(1, 1, 128, NT);
+                fa4[n4] = fb4[n4] = 0;
               } else if constexpr (KIND == 0) {
-                umma_mxf8(acc + g * NT, desc_sw128(st + g * kTile + 32 * j), bd, idesc_mxf8(NT, j),
-                          (tmem + sfa_col + 4 * g) | (static_cast<uint32_t>(j) << 30),
-                          (tmem + sfb_col) | (static_cast<uint32_t>(j) << 30), (kc | j) ? 1u : 0u);
+                i4[n4] = idesc_mxf8(NT, j);
+                fa4[n4] = (tmem + sfa_col + 4 * g) | (static_cast<uint32_t>(j) << 30);
+                fb4[n4] = (tmem + sfb_col) | (static_cast<uint32_t>(j) << 30);
               } else {
-                umma_nvf4(acc + g * NT, desc_sw128(st + g * kTile + 32 * j), bd, idesc_nvf4(NT),
-                          tmem + sfa_col + 4 * (g * 4 + j), tmem + sfb_col + 4 * j, (kc | j) ? 1u : 0u);
+                i4[n4] = idesc_nvf4(NT);
+                fa4[n4] = tmem + sfa_col + 4 * (g * 4 + j);
+                fb4[n4] = tmem + sfb_col + 4 * j;
+              }
+              if (kc | j) mask |= 1u << n4;
+              if (++n4 == 4) {
+                umma_bs_x4<KIND>(d4, a4, b4, i4, fa4, fb4, mask);
+                n4 = 0;
+                mask = 0;
               }
             }
           }
