@@ -376,7 +376,7 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
               int64_t num_ctas,
               int64_t kind, const c10::optional<at::Tensor>& expert_mul,
               const c10::optional<at::Tensor>& out_peers, int64_t out_offset, int64_t out_div, int64_t out_rank,
-              int64_t out_shared_base, int64_t pairs_total) {
+              int64_t out_shared_base, int64_t pairs_total, int64_t ksplit, int64_t split_rows) {
   req(wpack, at::kByte, "wpack");
   req(x, at::kByte, "x");
   req(off, at::kInt, "off");
@@ -400,9 +400,14 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
                     out_scale->is_contiguous() && out_scale->size(1) >= n_tiles * (kind == 0 ? 1 : 2) &&
                     out.size(1) >= n_tiles * (kind == 0 ? 128 : 64),
                 "out_scale [pairs, n_tiles words] / out [pairs, F bytes]");
+  } else if (mode == iob::kMoeOutF32Split) {
+    req(out, at::kFloat, "out");
+    TORCH_CHECK(ksplit >= 1 && ksplit <= kc && out.size(1) >= n_tiles * G * 128 && out.size(0) >= ksplit * split_rows,
+                "split-K partials [ksplit * split_rows, N] fp32");
   } else {
     req(out, at::kBFloat16, "out");
     TORCH_CHECK(out.size(1) >= n_tiles * G * 128, "out width");
+    TORCH_CHECK(ksplit == 1, "split-K needs the fp32 partials mode");
   }
   if (mode == iob::kMoeOutBf16Weighted)
     TORCH_CHECK(pair_w.has_value() && pair_w->scalar_type() == at::kFloat, "pair_w fp32");
@@ -428,6 +433,8 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
   a.x_stride = static_cast<int>(x.stride(0));
   a.out_stride = static_cast<int>(out.stride(0));
   a.out_scale_stride = out_scale.has_value() ? static_cast<int>(out_scale->stride(0)) : 0;
+  a.ksplit = static_cast<int>(ksplit);
+  a.split_rows = static_cast<int>(split_rows);
   a.num_ctas = static_cast<int>(num_ctas);
   a.out_mul = static_cast<float>(out_mul);
   a.kind = static_cast<int>(kind);
@@ -444,6 +451,17 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
   a.pairs_total = static_cast<int>(pairs_total);
   const at::cuda::CUDAGuard g(x.device());
   CHECK_CUDA_OK(iob::moe_gemm(a, stream()));
+}
+
+void splitk_reduce(const at::Tensor& part, int64_t ksplit, at::Tensor out) {
+  req(part, at::kFloat, "part");
+  req(out, at::kBFloat16, "out");
+  TORCH_CHECK(part.is_contiguous() && out.is_contiguous() && out.dim() == 2 &&
+                  part.numel() >= ksplit * out.size(0) * out.size(1),
+              "splitk_reduce shapes");
+  const at::cuda::CUDAGuard g(out.device());
+  CHECK_CUDA_OK(iob::splitk_reduce(part.data_ptr<float>(), static_cast<int>(ksplit), static_cast<int>(out.size(0)),
+                                   static_cast<int>(out.size(1)), out.data_ptr(), stream()));
 }
 
 void moe_align(const at::Tensor& ids, int64_t e0, int64_t E, int64_t extra, at::Tensor off, at::Tensor pairs) {
@@ -776,6 +794,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_quant", &rmsnorm_quant);
   m.def("gqa_extend", &gqa_extend);
   m.def("act_quant", &act_quant);
+  m.def("splitk_reduce", &splitk_reduce);
   m.def("ep_dispatch", &ep_dispatch);
   m.def("ep_barrier", &ep_barrier);
   m.def("dcp_merge", &dcp_merge);

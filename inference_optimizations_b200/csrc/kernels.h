@@ -168,7 +168,8 @@ cudaError_t moe_route(const float* logits, const float* bias, int* ids, float* w
 
 // ---- primitive check (umma_test.cu): C[M, N] fp32 = A[M, K] * B[N, K]^T, bf16 inputs, one CTA per 128 rows.
 // ---- grouped block-scaled expert GEMM + routing prep (moe_gemm.cu)
-enum MoeOutMode { kMoeOutBf16 = 0, kMoeOutSwigluQuant = 1, kMoeOutBf16Weighted = 2 };
+enum MoeOutMode { kMoeOutBf16 = 0, kMoeOutSwigluQuant = 1, kMoeOutBf16Weighted = 2,
+                  kMoeOutF32Split = 3 };   // split-K: fp32 partials [ksplit][split_rows][out_stride] into `out`
 struct MoeGemmArgs {
   const uint8_t* wpack;       // [E][n_tiles][KC] blocks: G SW128 tiles (128 x 128 B) then G scale atoms (512 B);
                               // plain modes: the G tiles are output columns (nt G + g) 128 ..; SwiGLU: gate, up
@@ -188,6 +189,8 @@ struct MoeGemmArgs {
   int out_div, out_rank, out_shared_base, pairs_total;
   int* status;
   int E, n_tiles, KC, G, NT, mode, src_div, src_limit, src_shared_base, x_stride, out_stride, out_scale_stride;
+  int ksplit;                 // split-K factor (>= 1): item = (expert, token tile, weight tile, K range)
+  int split_rows;             // kMoeOutF32Split: rows between two splits' partials
   int num_ctas;
   int kind;                   // 0: FP8 E4M3 + UE8M0 per 32 (128-blocks replicated); 1: NVFP4 (E2M1 + E4M3 per 16)
   float out_mul;
@@ -195,6 +198,8 @@ struct MoeGemmArgs {
 cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s);
 cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, int extra, int* off, int* pairs,
                       cudaStream_t s);
+// out bf16 [rows][N] = sum over splits of part fp32 [ksplit][rows][N] (fixed split order: deterministic).
+cudaError_t splitk_reduce(const float* part, int ksplit, int rows, int N, void* out, cudaStream_t s);
 cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_base, const float* w, void* y,
                         cudaStream_t s);
 

@@ -159,17 +159,26 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n)); }
 
-// Item i of this launch -> (expert, token tile, weight tile), via the per-expert prefix of item counts.
-__device__ __forceinline__ void item_coords(const int* prefix, int E, int n_tiles, int i, int& e, int& tt, int& nt) {
+// Item i of this launch -> (expert, token tile, weight tile, K split), via the per-expert prefix of item counts.
+__device__ __forceinline__ void item_coords(const int* prefix, int E, int n_tiles, int ksplit, int i, int& e, int& tt,
+                                            int& nt, int& ks) {
   int lo = 0, hi = E;                 // find e with prefix[e] <= i < prefix[e + 1]
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (prefix[mid] <= i) lo = mid; else hi = mid;
   }
   e = lo;
-  const int local = i - prefix[e];
+  int local = i - prefix[e];
+  ks = local % ksplit;
+  local /= ksplit;
   tt = local / n_tiles;
   nt = local - tt * n_tiles;
+}
+// K chunks [kc0, kc1) of split ks.
+__device__ __forceinline__ void split_range(int KC, int ksplit, int ks, int& kc0, int& kc1) {
+  const int per = (KC + ksplit - 1) / ksplit;
+  kc0 = min(KC, ks * per);
+  kc1 = min(KC, kc0 + per);
 }
 
 // Activation row of pair p: p / src_div for routed pairs, src_shared_base + p - src_limit for the shared-expert
@@ -226,7 +235,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
       const int e = lane * per + j;
       if (e < a.E) {
         const int cnt = a.expert_off[e + 1] - a.expert_off[e];
-        local += (cnt + NT - 1) / NT * a.n_tiles;
+        local += (cnt + NT - 1) / NT * a.n_tiles * a.ksplit;
       }
     }
     int incl = local;
@@ -241,7 +250,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
       if (e < a.E) {
         prefix[e] = run;
         const int cnt = a.expert_off[e + 1] - a.expert_off[e];
-        run += (cnt + NT - 1) / NT * a.n_tiles;
+        run += (cnt + NT - 1) / NT * a.n_tiles * a.ksplit;
       }
     }
     if (lane == 31) {
@@ -263,10 +272,11 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
       uint32_t it = 0;
       bool ok = true;
       for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-        int e, tt, nt;
-        item_coords(prefix, a.E, a.n_tiles, i, e, tt, nt);
+        int e, tt, nt, ks, kc0, kc1;
+        item_coords(prefix, a.E, a.n_tiles, a.ksplit, i, e, tt, nt, ks);
+        split_range(a.KC, a.ksplit, ks, kc0, kc1);
         const uint8_t* src = a.wpack + ((static_cast<size_t>(e) * a.n_tiles + nt) * a.KC) * C::kWBlk;
-        for (int kc = 0; kc < a.KC; ++kc, ++it) {
+        for (int kc = kc0; kc < kc1; ++kc, ++it) {
           const uint32_t s = it % C::kStages;
           if (it >= static_cast<uint32_t>(C::kStages) &&
               !mbar_wait(&ctl.empty[s], ((it / C::kStages) - 1) & 1, abort, a.status, kTimeoutProducer)) {
@@ -296,7 +306,10 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
         if (use > 0 && !mbar_wait(&ctl.acc_empty[buf], (use - 1) & 1, abort, a.status, kTimeoutMma)) break;
         tc_fence_after();
         const uint32_t acc = tmem + buf * C::kAccCols;
-        for (int kc = 0; kc < a.KC; ++kc, ++it) {
+        int e_, tt_, nt_, ks, kc0, kc1;
+        item_coords(prefix, a.E, a.n_tiles, a.ksplit, i, e_, tt_, nt_, ks);
+        split_range(a.KC, a.ksplit, ks, kc0, kc1);
+        for (int kc = kc0; kc < kc1; ++kc, ++it) {
           const uint32_t s = it % C::kStages, ph = (it / C::kStages) & 1;
           if (!mbar_wait(&ctl.w_full[s], ph, abort, a.status, kTimeoutMma) ||
               !mbar_wait(&ctl.x_full[s], ph, abort, a.status, kTimeoutMma)) {
@@ -338,7 +351,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
                 fa4[n4] = tmem + sfa_col + 4 * (g * 4 + j);
                 fb4[n4] = tmem + sfb_col + 4 * j;
               }
-              if (kc | j) mask |= 1u << n4;
+              if (kc != kc0 || j) mask |= 1u << n4;
               if (++n4 == 4) {
                 umma_bs_x4<KIND>(d4, a4, b4, i4, fa4, fb4, mask);
                 n4 = 0;
@@ -360,8 +373,9 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
     uint32_t it = 0;
     bool ok = true;
     for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-      int e, tt, nt;
-      item_coords(prefix, a.E, a.n_tiles, i, e, tt, nt);
+      int e, tt, nt, ks, kc0, kc1;
+      item_coords(prefix, a.E, a.n_tiles, a.ksplit, i, e, tt, nt, ks);
+      split_range(a.KC, a.ksplit, ks, kc0, kc1);
       const int row0 = a.expert_off[e] + tt * NT;
       const int rows = min(NT, a.expert_off[e + 1] - row0);
       // rows handled by this thread: r = t64 / 8 + 8 m (chunk t64 % 8); scale rows t64, t64 + 64
@@ -380,7 +394,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
                       ? a.x_scale + static_cast<size_t>(src_row(a, a.pairs[row0 + r])) * (a.KC * kSfw)
                       : nullptr;
       }
-      for (int kc = 0; kc < a.KC; ++kc, ++it) {
+      for (int kc = kc0; kc < kc1; ++kc, ++it) {
         const uint32_t s = it % C::kStages;
         if (it >= static_cast<uint32_t>(C::kStages) &&
             !mbar_wait(&ctl.empty[s], ((it / C::kStages) - 1) & 1, abort, a.status, kTimeoutProducer)) {
@@ -415,8 +429,8 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     int li = 0;
     for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++li) {
-      int e, tt, nt;
-      item_coords(prefix, a.E, a.n_tiles, i, e, tt, nt);
+      int e, tt, nt, ks;
+      item_coords(prefix, a.E, a.n_tiles, a.ksplit, i, e, tt, nt, ks);
       const int row0 = a.expert_off[e] + tt * NT;
       const int rows = min(NT, a.expert_off[e + 1] - row0);
       const int buf = li % C::kAccBufs, use = li / C::kAccBufs;
@@ -492,6 +506,11 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
                 const int p = a.pairs[row0 + r];
                 float v = __uint_as_float(g == 0 ? v0[t] : v1[t]) * emul;
                 if (a.mode == kMoeOutBf16Weighted) v *= a.pair_w[p];
+                if (a.mode == kMoeOutF32Split) {        // split-K partial, summed by splitk_reduce
+                  reinterpret_cast<float*>(a.out)[(static_cast<size_t>(ks) * a.split_rows + p) * a.out_stride +
+                                                  (nt * G + g) * 128 + n_local] = v;
+                  continue;
+                }
                 __nv_bfloat16* dst;
                 if (a.out_peers) {                      // expert parallelism: the row goes to its token's owner
                   const bool sh = p >= a.pairs_total;
@@ -697,9 +716,29 @@ __global__ void act_quant_kernel(const __nv_bfloat16* gu, int F, int fmt, uint8_
   }, row, F, fmt, q, sc);
 }
 
+// One CTA per output row: the K splits' fp32 partials summed in split order, rounded once to bf16.
+__global__ void splitk_reduce_kernel(const float* part, int ksplit, int rows, int N, __nv_bfloat16* out) {
+  const int r = blockIdx.x;
+  for (int c = threadIdx.x; c < N / 4; c += blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < ksplit; ++k) {
+      const float4 v = reinterpret_cast<const float4*>(part + (static_cast<size_t>(k) * rows + r) * N)[c];
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 w;
+    w.x = *reinterpret_cast<const uint32_t*>(&lo);
+    w.y = *reinterpret_cast<const uint32_t*>(&hi);
+    reinterpret_cast<uint2*>(out + static_cast<size_t>(r) * N)[c] = w;
+  }
+}
+
 }  // namespace
 
 cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
+  if (a.ksplit < 1 || a.ksplit > a.KC || (a.ksplit > 1 && a.mode != kMoeOutF32Split) ||
+      (a.mode == kMoeOutF32Split && a.out_peers))
+    return cudaErrorInvalidValue;
   if (a.E <= 0 || a.E > kMaxGemmExperts || a.KC <= 0 || a.n_tiles <= 0 || a.num_ctas <= 0 || a.src_div <= 0 ||
       (a.x_stride % 16) || (reinterpret_cast<uintptr_t>(a.x) % 16) || (reinterpret_cast<uintptr_t>(a.wpack) % 16) ||
       (a.mode == kMoeOutSwigluQuant && (a.G != 2 || a.kind == 2)) || a.kind < 0 || a.kind > 2)
@@ -714,6 +753,13 @@ cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
   IOB_MG(16, 2, 2) IOB_MG(32, 2, 2) IOB_MG(64, 2, 2) IOB_MG(128, 2, 2)
 #undef IOB_MG
   return cudaErrorInvalidValue;
+}
+
+cudaError_t splitk_reduce(const float* part, int ksplit, int rows, int N, void* out, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  if (N % 4 || ksplit < 1) return cudaErrorInvalidValue;
+  splitk_reduce_kernel<<<rows, 256, 0, s>>>(part, ksplit, rows, N, static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
 }
 
 cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, int extra, int* off, int* pairs,

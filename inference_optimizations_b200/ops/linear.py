@@ -4,7 +4,9 @@ At decode the token count is small (tens of rows) and a linear layer is a pass o
 packed once into UMMA-ready blocks (128 rows x 64 values, SW128, two adjacent 128-row tiles per block when N allows)
 so each pipeline stage is one contiguous bulk copy; the tokens are the MMA's N operand (swap-AB), so the weights
 stream at full tensor-core width whatever the batch.  y = x W^T exactly like `torch.nn.functional.linear` (fp32
-accumulation, bf16 out).
+accumulation, bf16 out).  When the output tiles alone cannot occupy every SM (small N, long K: o_proj, down), K is
+split into ranges: each (weight tile, token tile, K range) item writes fp32 partials and one kernel sums them in
+split order (deterministic) and rounds once.
 """
 from __future__ import annotations
 
@@ -25,6 +27,45 @@ def pack_bf16(w: torch.Tensor, g: int) -> torch.Tensor:
     return t.reshape(1, N // (TILE * g), kc, g * TILE * TILE)
 
 
+def split_k(n_tiles: int, tokens: int, nt: int, kc: int, ctas: int, min_chunks: int = 4, fill: int = 6) -> int:
+    """K splits for a weight-streaming GEMM with n_tiles output tiles.  None while the items fill a quarter of the
+    SMs or more; else the split count minimizing the critical path
+    waves x (K chunks per split + `fill`, the pipeline start of an item in chunk units), each K range at least
+    `min_chunks` chunks; ties keep fewer splits (no partials to reduce)."""
+    items = n_tiles * -(-tokens // nt)
+    if 4 * items > ctas:          # measured: splitting pays only when the output tiles fill under a quarter of the SMs
+        return 1
+    best, best_cost = 1, None
+    for ks in range(1, max(1, kc // min_chunks) + 1):
+        cost = -(-items * ks // ctas) * (-(-kc // ks) + fill)
+        if best_cost is None or cost < best_cost:
+            best, best_cost = ks, cost
+    return best
+
+
+def _splitk_gemm(lin, x, xs, out, t: int, kc: int, kind: int) -> None:
+    """Run lin's GEMM with split-K when it helps: fp32 partials, then one deterministic reduction to bf16."""
+    from .._ext import ext
+    nt = MG.pick_nt(t)
+    n_tiles = lin.N // (TILE * lin.g)
+    ks = split_k(n_tiles, t, nt, kc, lin.num_ctas)
+    off, pairs = lin._index(t, x.device)
+    if ks == 1:
+        MG.gemm(lin.wpack, x, xs, off, pairs, out, lin.status, n_tiles=n_tiles, kc=kc, g=lin.g, nt=nt, mode=0,
+                src_div=1, num_ctas=lin.num_ctas, kind=kind)
+        return
+    key = (t, ks)
+    if key not in lin._parts:
+        lin._parts[key] = torch.empty(ks * t, lin.N, dtype=torch.float32, device=x.device)
+    part = lin._parts[key]
+    MG.gemm(lin.wpack, x, xs, off, pairs, part, lin.status, n_tiles=n_tiles, kc=kc, g=lin.g, nt=nt,
+            mode=MODE_F32_SPLIT, src_div=1, num_ctas=lin.num_ctas, kind=kind, ksplit=ks, split_rows=t)
+    ext().splitk_reduce(part, ks, out)
+
+
+MODE_F32_SPLIT = 3
+
+
 class DenseLinear:
     def __init__(self, w: torch.Tensor):
         N, K = w.shape
@@ -36,6 +77,7 @@ class DenseLinear:
         self.num_ctas = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 1
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self._rows: dict = {}
+        self._parts: dict = {}
 
     def _index(self, t: int, dev):
         if t not in self._rows:
@@ -49,10 +91,8 @@ class DenseLinear:
             out = torch.empty(t, self.N, dtype=torch.bfloat16, device=x.device)
         if t == 0:
             return out
-        off, pairs = self._index(t, x.device)
         xb = x.contiguous().view(torch.uint8)
-        MG.gemm(self.wpack, xb, xb, off, pairs, out, self.status, n_tiles=self.N // (TILE * self.g),
-                kc=self.K // 64, g=self.g, nt=MG.pick_nt(t), mode=0, src_div=1, num_ctas=self.num_ctas, kind=2)
+        _splitk_gemm(self, xb, xb, out, t, self.K // 64, 2)
         return out
 
 
@@ -72,6 +112,13 @@ class Fp8Linear:
         self.num_ctas = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 1
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         self._rows: dict = {}
+        self._parts: dict = {}
+
+    def _index(self, t: int, dev):
+        if t not in self._rows:
+            self._rows[t] = (torch.tensor([0, t], dtype=torch.int32, device=dev),
+                             torch.arange(t, dtype=torch.int32, device=dev))
+        return self._rows[t]
 
     def dequant(self) -> torch.Tensor:
         return MG.dequant_blocks(self.q, self.eb)[0]
@@ -95,12 +142,7 @@ class Fp8Linear:
             out = torch.empty(t, self.N, dtype=torch.bfloat16, device=xq.device)
         if t == 0:
             return out
-        if t not in self._rows:
-            self._rows[t] = (torch.tensor([0, t], dtype=torch.int32, device=xq.device),
-                             torch.arange(t, dtype=torch.int32, device=xq.device))
-        off, pairs = self._rows[t]
-        MG.gemm(self.wpack, xq, xs, off, pairs, out, self.status, n_tiles=self.N // (TILE * self.g), kc=self.K // TILE,
-                g=self.g, nt=MG.pick_nt(t), mode=0, src_div=1, num_ctas=self.num_ctas, kind=0)
+        _splitk_gemm(self, xq, xs, out, t, self.K // TILE, 0)
         return out
 
 

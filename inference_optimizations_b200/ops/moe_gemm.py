@@ -179,11 +179,12 @@ def pack_weights_nvfp4(qs: list, scs: list) -> torch.Tensor:
 def gemm(wpack, x, x_scale, off, pairs, out, status, *, n_tiles: int, kc: int, g: int, nt: int, mode: int,
          src_div: int, src_limit: int = 1 << 30, src_shared_base: int = 0, pair_w=None, out_scale=None, out_mul: float = 1.0,
          num_ctas: int = 148, kind: int = 0, expert_mul=None, out_peers=None, out_offset: int = 0, out_div: int = 1,
-         out_rank: int = 0, out_shared_base: int = 0, pairs_total: int = 0) -> None:
+         out_rank: int = 0, out_shared_base: int = 0, pairs_total: int = 0, ksplit: int = 1,
+         split_rows: int = 0) -> None:
     """One grouped block-scaled GEMM launch (argument meanings: `MoeGemmArgs` in csrc/kernels.h)."""
     ext().moe_gemm(wpack, x, x_scale, off, pairs, pair_w, out, out_scale, status, n_tiles, kc, g, nt, mode, src_div,
                    src_limit, src_shared_base, out_mul, num_ctas, kind, expert_mul, out_peers, out_offset, out_div, out_rank,
-                   out_shared_base, pairs_total)
+                   out_shared_base, pairs_total, ksplit, split_rows)
 
 
 _TACTICS = None

@@ -273,3 +273,23 @@ def test_fp8_mlp(cuda):
     ref = mlp.reference(x).to(y.device)
     err = (y - ref).abs() / (ref.abs() + 1e-2 * ref.abs().max())
     assert err.max().item() < 2e-2
+
+
+@pytest.mark.parametrize("t,n,k", [(5, 256, 4096), (33, 384, 8192), (16, 5376, 21504)])
+def test_dense_linear_split_k(cuda, t, n, k):
+    """Split-K weight streaming (few output tiles, long K: fp32 partials per K range, one ordered reduction) against
+    an fp32 matmul, and run to run identical."""
+    from inference_optimizations_b200.ops.linear import DenseLinear, split_k
+    import inference_optimizations_b200.ops.moe_gemm as MGm
+    torch.manual_seed(t)
+    w = (torch.randn(n, k, device=cuda) * 0.05).to(torch.bfloat16)
+    x = torch.randn(t, k, device=cuda).to(torch.bfloat16)
+    lin = DenseLinear(w)
+    assert split_k(n // (128 * lin.g), t, MGm.pick_nt(t), k // 64, lin.num_ctas) > 1
+    y = lin(x)
+    y2 = lin(x)
+    torch.cuda.synchronize()
+    assert lin.status.item() == 0 and torch.equal(y, y2)
+    ref = x.float() @ w.float().T
+    err = (y.float() - ref).abs() / (ref.abs() + 1e-2 * ref.abs().max())
+    assert err.max().item() < 1e-2, err.max().item()
