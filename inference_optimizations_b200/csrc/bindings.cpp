@@ -766,6 +766,15 @@ void cvt_rate_test(int64_t iters, int64_t variant, at::Tensor out, at::Tensor si
                                    reinterpret_cast<uint32_t*>(sink.data_ptr<int>()), stream()));
 }
 
+std::vector<int64_t> sm_lanes(int64_t device, int64_t first_sms) {
+  unsigned long long streams[2] = {0, 0};
+  int sms[2] = {0, 0};
+  char err[256] = {0};
+  TORCH_CHECK(iob::sm_lanes_create(static_cast<int>(device), static_cast<int>(first_sms), streams, sms, err,
+                                   sizeof(err)) == 0, "sm_lanes: ", err);
+  return {static_cast<int64_t>(streams[0]), static_cast<int64_t>(streams[1]), sms[0], sms[1]};
+}
+
 void umma_rate_test(int64_t n, int64_t count, int64_t nacc, int64_t ts, at::Tensor out) {
   req(out, at::kLong, "out");
   const at::cuda::CUDAGuard g(out.device());
@@ -810,4 +819,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvfp4_lut_test", &nvfp4_lut_test);
   m.def("umma_rate_test", &umma_rate_test);
   m.def("cvt_rate_test", &cvt_rate_test);
+  m.def("sm_lanes", &sm_lanes);
 }

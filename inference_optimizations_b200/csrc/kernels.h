@@ -286,4 +286,8 @@ cudaError_t cvt_rate_test(int iters, int variant, long long* out, uint32_t* sink
 cudaError_t umma_rate_test(int n, int count, int nacc, int ts, long long* out, cudaStream_t s);
 cudaError_t nvfp4_lut_test(const uint32_t* words, int nwords, int* out, cudaStream_t s);
 
+// Two green contexts over disjoint SM sets (first_sms rounded up by the driver, and the rest), one stream each:
+// streams[0..1] (CUstream handles), sms[0..1].  Returns 0, or -1 with a message in err.
+int sm_lanes_create(int device, int first_sms, unsigned long long* streams, int* sms, char* err, int errlen);
+
 }  // namespace iob

@@ -256,6 +256,61 @@ class GQARunner:
         self._trim(batch.segments)
         return res
 
+    # ------------------------------------------------------------------------------------------ split prefill
+    # The prefill lane of the SM-partitioned prefill / decode lanes (engine/pdmux.py): one prefill chunk advances a
+    # few decoder layers per engine iteration on its own stream while decode steps run on the other lane's stream
+    # (`parallelism/in-node-pd-disaggregation/glm_pdmux_split_hooks.py:1-30`).  The lane has its own staging
+    # buffers and output ids; the decode lane keeps `self.stage`.
+    def split_begin(self, batch: Batch) -> dict:
+        if self.spec or self.tp != 1:
+            raise NotImplementedError("split prefill lanes: speculative decoding and tp > 1 are not supported")
+        if not hasattr(self, "p_stage"):
+            self.p_stage = StagingBuffers(self.max_tok, self.max_groups, KINDS, self.device)
+            self.p_out = torch.zeros(self.max_tok, dtype=torch.int32, device=self.device)
+            self.p_out_host = torch.zeros(self.max_tok, dtype=torch.int32, pin_memory=self.device.type == "cuda")
+        for s in batch.segments:
+            if s.req.rid not in self.pages:
+                self.attach(s.req)
+        p = self._pack(batch.segments, self.n_q_prefill, ("global", "swa"))
+        self.kv.sync_tables()
+        self.p_stage.fill(p)
+        self.p_stage.upload()
+        st = self.p_stage.step_tensors(len(p.ids), len(p.kv_len), p.n_q, {"global": (1, 1 << 20),
+                                                                          "swa": (1, 1 << 20)})
+        st.ext_segs = self._ext_segs(p)
+        st.lane = 1
+        return {"batch": batch, "p": p, "st": st, "x": None, "resid": None, "index": 0}
+
+    def split_layers(self, sp: dict, count: int) -> bool:
+        """Enqueue layers [index, index + count) of the split on the current stream; after the last layer also the
+        logits / argmax of the rows that want a token.  Returns True when the split's device work is all enqueued."""
+        n_layers = len(self.model.layers)
+        lo = sp["index"]
+        hi = min(lo + max(1, count), n_layers)
+        sp["x"], sp["resid"] = self.model.forward_layers(sp["st"], self.kv, lo, hi, sp["x"], sp["resid"])
+        sp["index"] = hi
+        if hi < n_layers:
+            return False
+        p = sp["p"]
+        if len(p.logit_rows):
+            rows = torch.tensor(p.logit_rows, dtype=torch.long)     # pinned + async: the host never waits on the lane
+            rows = rows.pin_memory().to(self.device, non_blocking=True) if self.device.type == "cuda" else rows
+            self._greedy(sp["x"][rows], self.p_out)
+            self.p_out_host[: len(p.logit_rows)].copy_(self.p_out[: len(p.logit_rows)], non_blocking=True)
+        sp["x"] = sp["resid"] = None
+        return True
+
+    def split_finish(self, sp: dict) -> dict:
+        """Host side of a finished split, after its stream's work completed: rid -> first generated token."""
+        res, k = {}, 0
+        for s in sp["batch"].segments:
+            if s.logits:
+                res[s.req.rid] = int(self.p_out_host[k])
+                s.req.draft_state["ld"] = s.start + len(s.tokens)
+                k += 1
+        self._trim(sp["batch"].segments)
+        return res
+
     @torch.no_grad()
     def score(self, tokens: list) -> torch.Tensor:
         """Teacher-forced full logits [T, V] (fp32, CPU) of one sequence through the paged pool (tp = 1): the

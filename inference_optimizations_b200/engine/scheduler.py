@@ -108,25 +108,41 @@ class Scheduler:
             if not hold:
                 self.prefilling = self._admit()
         if self.prefilling is not None:
-            segs, budget = [], self.chunk
-            while self.prefilling is not None and budget > 0:
-                r = self.prefilling
-                n = min(budget, r.prompt_len - r.prefilled)
-                last = r.prefilled + n == r.prompt_len
-                segs.append(Segment(r, r.prefilled, r.prompt[r.prefilled:r.prefilled + n], last))
-                r.prefilled += n
-                budget -= n
-                if not last:
-                    break
-                self.prefilling = self._admit() if budget > 0 else None
             self.streak = next_streak(self.burst, self.streak, True)
             self.last_was_extend = True
-            return Batch("prefill", segs)
+            return self._prefill_chunk()
         if self.running:
             self.streak = next_streak(self.burst, self.streak, False)
             self.last_was_extend = False
             return Batch("decode", [Segment(r, r.kv_len, [r.pending], True) for r in self.running])
         return None
+
+    def _prefill_chunk(self) -> Batch:
+        segs, budget = [], self.chunk
+        while self.prefilling is not None and budget > 0:
+            r = self.prefilling
+            n = min(budget, r.prompt_len - r.prefilled)
+            last = r.prefilled + n == r.prompt_len
+            segs.append(Segment(r, r.prefilled, r.prompt[r.prefilled:r.prefilled + n], last))
+            r.prefilled += n
+            budget -= n
+            if not last:
+                break
+            self.prefilling = self._admit() if budget > 0 else None
+        return Batch("prefill", segs)
+
+    def plan_prefill(self) -> Optional[Batch]:
+        """The next prefill chunk regardless of the decode-burst rule, or None: the prefill lane of the SM-partitioned
+        lanes runs beside decode, so it never holds prefill back."""
+        if self.prefilling is None:
+            self.prefilling = self._admit()
+        return self._prefill_chunk() if self.prefilling is not None else None
+
+    def decode_batch(self) -> Optional[Batch]:
+        """Every running request, one decode token each (the decode lane's batch)."""
+        if not self.running:
+            return None
+        return Batch("decode", [Segment(r, r.kv_len, [r.pending], True) for r in self.running])
 
     def commit_prefill(self, batch: Batch, next_tokens: dict) -> None:
         for s in batch.segments:

@@ -185,7 +185,7 @@ class GQAModel:
         else:
             attn = A.gqa_decode(q, pool, kv.tables[g.kind].dev, st.kv_len, st.n_q, g.kv_heads, kv.fmt,
                                 1.0 / math.sqrt(g.head_dim), g.window, kv.k_scale, kv.v_scale,
-                                splits=st.splits.get(g.kind), ws=kv.workspace(g.head_dim, g.kv_heads),
+                                splits=st.splits.get(g.kind), ws=kv.workspace(g.head_dim, g.kv_heads, st.lane),
                                 req_idx=st.req_idx)
         if self.tp > 1 and self.tp_comm is not None and attn.shape[0] <= self.tp_comm.rows_cap:
             # row-parallel GEMMs write their partials into the symmetric buffer; one kernel reduces over NVLink and
@@ -205,13 +205,19 @@ class GQAModel:
     def forward(self, st: "StepTensors", kv: "GQAKVCache", layer_offset: int = 0,
                 inputs_embeds: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
         """Returns (final-normed hidden [T, H], pre-norm residual stream [T, H])."""
+        return self.forward_layers(st, kv, 0, len(self.layers), None, None, layer_offset, inputs_embeds)
+
+    def forward_layers(self, st: "StepTensors", kv: "GQAKVCache", lo: int, hi: int, x: Optional[torch.Tensor],
+                       resid: Optional[torch.Tensor], layer_offset: int = 0,
+                       inputs_embeds: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Decoder layers [lo, hi) of one step: the split prefill of the SM-partitioned prefill / decode lanes
+        (`parallelism/in-node-pd-disaggregation/glm_pdmux_split_hooks.py:1-30`).  lo == 0 embeds; (x, resid) carry
+        the normed input and the residual stream between ranges; after the last layer x is final-normed."""
         cfg = self.cfg
-        if inputs_embeds is None:
-            resid = B.embed(st.ids, self.embed, self.embed_scale)
-        else:
-            resid = inputs_embeds
-        x = B.rmsnorm(resid, self.layers[0].n_in, cfg.rms_eps, True)
-        for i in range(len(self.layers)):
+        if lo == 0:
+            resid = B.embed(st.ids, self.embed, self.embed_scale) if inputs_embeds is None else inputs_embeds
+            x = B.rmsnorm(resid, self.layers[0].n_in, cfg.rms_eps, True)
+        for i in range(lo, hi):
             nxt = self.layers[i + 1].n_in if i + 1 < len(self.layers) else self.final_norm
             x = self.layer_forward(i, x, resid, st, kv, layer_offset + i, nxt)
         return x, resid
@@ -265,6 +271,7 @@ class StepTensors:
     # runs the GQA-packed extend kernel over NVFP4 / FP8 pools (block lists cached per group size G)
     ext_segs: Optional[list] = None
     ext_cache: dict = field(default_factory=dict)
+    lane: int = 0                     # 1 = the prefill lane of the SM-partitioned lanes (its own decode workspace)
 
     def ext_blocks(self, g: int, device) -> torch.Tensor:
         if g not in self.ext_cache:
@@ -310,8 +317,10 @@ class GQAKVCache:
         self._ws = {}
         self.ext_status = torch.zeros(1, dtype=torch.int32, device=device)
 
-    def workspace(self, d: int, hk: int) -> Optional[A.DecodeWorkspace]:
-        return self._ws.get((d, hk))
+    def workspace(self, d: int, hk: int, lane: int = 0) -> Optional[A.DecodeWorkspace]:
+        """The decode lane's reserved split workspace; the prefill lane (lane 1) gets None, so each call allocates
+        its own on the prefill stream and the two lanes never share partial buffers."""
+        return self._ws.get((d, hk)) if lane == 0 else None
 
     def reserve_workspace(self, max_groups: int, max_splits: int) -> None:
         if self.device.type != "cuda":
