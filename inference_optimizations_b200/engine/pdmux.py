@@ -15,8 +15,9 @@ partitions whose decode share grows with the index.  Under data parallelism ever
 rank in the same iteration (an idle split where a rank has no prefill), advances the same layer range and finishes in
 the same iteration.
 
-The prefill lane of a finished split hands over on the host: the decode stream is not made to wait, the host waits on
-the split's event and commits its first tokens, and the requests join the next iteration's decode batch.
+A split whose last layers are enqueued stays pending while decode iterations go on; it is committed (first tokens, the
+requests join the decode batch) in the first iteration in which its event has fired on every rank, so neither the host
+nor the decode stream ever waits on the prefill lane.
 Not supported with the lanes: speculative decoding and tensor parallelism (the runner raises).
 """
 from __future__ import annotations
@@ -138,6 +139,7 @@ class PdmuxEngine:
         self.lanes = Lanes(engine.device, n_groups, divisions)
         self.num_layers = len(engine.runner.model.layers)
         self.split: Optional[dict] = None
+        self.pending: Optional[dict] = None   # a split whose device work is all enqueued, not yet committed
         self._p_event = None
         self._p_stream = None
         self.log: list = []               # per iteration: (group, split layers [lo, hi), decode batch size)
@@ -153,20 +155,27 @@ class PdmuxEngine:
 
     def step(self) -> dict:
         """One iteration: maybe start a split, advance it by its layer range on the prefill lane, one decode step on
-        the decode lane, and commit a finished split.  Returns rid -> tokens produced."""
+        the decode lane, and commit a split whose device work has completed on every rank.  A split whose last layers
+        are enqueued stays pending (decode keeps running) until its event has fired: the host never blocks on the
+        prefill lane.  Returns rid -> tokens produced."""
         eng = self.engine
         sched, run = eng.sched, eng.runner
-        batch = sched.plan_prefill() if self.split is None else None
+        if self.group is None and self.pending is not None and self.pending.get("event") is not None and \
+                not sched.running:
+            self.pending["event"].synchronize()      # nothing to decode: waiting on the prefill lane costs nothing
+        busy = 1 if (self.pending is not None and self.pending.get("event") is not None
+                     and not self.pending["event"].query()) else 0
+        batch = sched.plan_prefill() if self.split is None and self.pending is None else None
         if self.split is not None:
             p_tok = self.split["tokens"]
         else:
             p_tok = sum(len(s.tokens) for s in batch.segments) if batch is not None else 0
         dbatch = sched.decode_batch()
-        gp, gd, _ = self._global(p_tok, len(dbatch.segments) if dbatch is not None else 0, 0)
+        gp, gd, any_busy = self._global(p_tok, len(dbatch.segments) if dbatch is not None else 0, busy)
         split_active = self.split is not None or max(gp) > 0
-        grp = choose_group(self.n_groups, split_active, max(gd) > 0, max(gd), self.thresholds, self.divisor)
+        lane_busy = split_active or self.pending is not None
+        grp = choose_group(self.n_groups, lane_busy, max(gd) > 0, max(gd), self.thresholds, self.divisor)
         ps, ds = self.lanes.streams(grp)
-        finished = None
         span = None
         if split_active:
             with _StreamCtx(ps):
@@ -188,7 +197,9 @@ class PdmuxEngine:
                     self._p_event.record(ps)
                     self._p_stream = ps
             if done:
-                finished, self.split = self.split, None
+                self.split["event"] = self._p_event if not self.split.get("idle") else None
+                self.pending, self.split = self.split, None
+                any_busy = 1                              # committed in a later iteration, on every rank together
         out: dict = {}
         if dbatch is not None:
             reqs = [s.req for s in dbatch.segments]
@@ -198,13 +209,16 @@ class PdmuxEngine:
             with _StreamCtx(ds):
                 out = run.decode(reqs)
             sched.commit_decode(out)
-        if finished is not None and not finished.get("idle"):
-            if self._p_event is not None:
-                self._p_event.synchronize()
-            nxt = run.split_finish(finished)
-            sched.commit_prefill(finished["batch"], nxt)
-            for rid, t in nxt.items():
-                out.setdefault(rid, []).append(t)
+        finished = None
+        if self.pending is not None and not any_busy:
+            finished, self.pending = self.pending, None
+            if not finished.get("idle"):
+                if finished.get("event") is not None:
+                    finished["event"].synchronize()      # already complete: no wait
+                nxt = run.split_finish(finished)
+                sched.commit_prefill(finished["batch"], nxt)
+                for rid, t in nxt.items():
+                    out.setdefault(rid, []).append(t)
         cand = [sg.req for sg in dbatch.segments] if dbatch is not None else []
         if finished is not None and not finished.get("idle"):
             cand += [sg.req for sg in finished["batch"].segments]
@@ -216,7 +230,7 @@ class PdmuxEngine:
         return out
 
     def has_work(self) -> bool:
-        return self.engine.sched.has_work() or self.split is not None
+        return self.engine.sched.has_work() or self.split is not None or self.pending is not None
 
     def generate(self, prompts: list, params: Optional[SamplingParams] = None, max_steps: int = 1 << 30) -> list:
         reqs = [self.engine.add_request(p, params) for p in prompts]
@@ -292,7 +306,8 @@ def main() -> None:
             eng.add_request(torch.randint(1, min(1000, cfg.vocab), (a.ctx,), generator=g).tolist(),
                             SamplingParams(max_new_tokens=2048, ignore_eos=True))
         for _ in range(10000):
-            if not (eng.sched.waiting or eng.sched.prefilling or (pm is not None and pm.split is not None)):
+            if not (eng.sched.waiting or eng.sched.prefilling or
+                    (pm is not None and (pm.split is not None or pm.pending is not None))):
                 break
             step()
         else:
