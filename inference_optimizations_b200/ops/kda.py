@@ -189,3 +189,49 @@ class StateStore:
 
     def nbytes(self) -> int:
         return sum(r.numel() for _, r in self.parked.values())
+
+
+class KDASmallProjections:
+    """The five small bf16 projections of a KDA layer: beta (b: H -> nb), the low-rank forget gate (f_a: H -> d,
+    f_b: d -> P) and the low-rank output gate (g_a: H -> d, g_b: d -> P).
+
+    Run separately they are five launch-bound GEMMs per layer.  `fuse()` packs them into one GEMM H -> nb + 2d
+    (b | f_a | g_a) and one batched GEMM [2, M, d] x [2, d, P] (f_b, g_b), and re-points the five weights at views of
+    the packed storage, so memory does not grow and the separate path stays valid
+    (`linear-attention-kda/small-projection-fuse/kda_smallproj_fuse_hooks.py:1-40`).  Call `fuse()` before capturing
+    a CUDA graph that reads the weights: it moves them."""
+
+    def __init__(self, w_b: torch.Tensor, w_fa: torch.Tensor, w_fb: torch.Tensor, w_ga: torch.Tensor,
+                 w_gb: torch.Tensor):
+        h = w_b.shape[1]
+        if not (w_fa.shape[1] == w_ga.shape[1] == h and w_fb.shape[1] == w_fa.shape[0] == w_ga.shape[0]
+                == w_gb.shape[1] and w_fb.shape[0] == w_gb.shape[0]):
+            raise ValueError("KDA small projections: shapes disagree")
+        self.w_b, self.w_fa, self.w_fb, self.w_ga, self.w_gb = w_b, w_fa, w_fb, w_ga, w_gb
+        self.w_a = None            # [nb + 2d, H] once fused
+        self.w_lr = None           # [2, d, P] once fused
+
+    def forward_separate(self, x: torch.Tensor) -> tuple:
+        """x [M, H] -> (beta logits [M, nb], forget-gate projection [M, P], output-gate projection [M, P])."""
+        b = Fn.linear(x, self.w_b)
+        f = Fn.linear(Fn.linear(x, self.w_fa), self.w_fb)
+        g = Fn.linear(Fn.linear(x, self.w_ga), self.w_gb)
+        return b, f, g
+
+    def fuse(self) -> None:
+        if self.w_a is not None:
+            return
+        nb, d = self.w_b.shape[0], self.w_fa.shape[0]
+        self.w_a = torch.cat([self.w_b, self.w_fa, self.w_ga], 0).contiguous()
+        self.w_lr = torch.stack([self.w_fb.t(), self.w_gb.t()], 0).contiguous()          # [2, d, P]
+        self.w_b, self.w_fa, self.w_ga = self.w_a[:nb], self.w_a[nb:nb + d], self.w_a[nb + d:]
+        self.w_fb, self.w_gb = self.w_lr[0].t(), self.w_lr[1].t()
+
+    def forward(self, x: torch.Tensor) -> tuple:
+        if self.w_a is None:
+            return self.forward_separate(x)
+        nb, d = self.w_b.shape[0], self.w_fa.shape[0]
+        a = Fn.linear(x, self.w_a)                                                       # [M, nb + 2d]
+        lo = a[:, nb:].unflatten(1, (2, d)).transpose(0, 1)                              # [2, M, d]
+        fg = torch.bmm(lo, self.w_lr)                                                    # [2, M, P]
+        return a[:, :nb], fg[0], fg[1]

@@ -87,3 +87,22 @@ def test_chunked_prefill_matches_recurrence(headwise):
     assert torch.allclose(a["state"], ref["state"], rtol=1e-4, atol=1e-5)
     for c in ("csq", "csk", "csv"):
         assert torch.allclose(a[c], ref[c])
+
+
+def test_small_projection_fuse_cpu():
+    from inference_optimizations_b200.ops.kda import KDASmallProjections
+    torch.manual_seed(0)
+    H, nb, d, P, M = 256, 8, 32, 256, 37
+    ws = [torch.randn(s, dtype=torch.bfloat16) * 0.05 for s in ((nb, H), (d, H), (P, d), (d, H), (P, d))]
+    sp = KDASmallProjections(*ws)
+    x = torch.randn(M, H, dtype=torch.bfloat16)
+    ref = sp.forward_separate(x)
+    sp.fuse()
+    assert sp.w_a.shape == (nb + 2 * d, H) and sp.w_lr.shape == (2, d, P)
+    assert sp.w_b.data_ptr() == sp.w_a.data_ptr()                  # separate weights now view the packed storage
+    out = sp.forward(x)
+    sep = sp.forward_separate(x)                                   # the separate path stays valid after the fuse
+    for a, b, c in zip(ref, out, sep):
+        assert a.shape == b.shape
+        assert torch.allclose(a.float(), b.float(), atol=1e-2, rtol=1e-2)
+        assert torch.equal(a, c)

@@ -24,3 +24,44 @@ def test_kda_decode_matches_oracle(cuda, headwise, W):
         for k in ("q", "k", "v", "g_proj", "g2"):
             nv = torch.randn_like(r[k].float()).to(r[k].dtype)
             r[k], g[k] = nv, nv.to(cuda)
+
+
+@pytest.mark.parametrize("m", [4096, 120, 24])
+def test_small_projection_fuse_gpu(m):
+    """Fused (one GEMM + one bmm) vs separate (five GEMMs) KDA small projections: equal within a bf16 ulp; prints the
+    CUDA-graph replay time of both."""
+    from inference_optimizations_b200.ops.kda import KDASmallProjections
+    torch.manual_seed(0)
+    H, nb, d, P = 2048, 32, 128, 4096
+    ws = [torch.randn(s, device="cuda", dtype=torch.bfloat16) * 0.03 for s in ((nb, H), (d, H), (P, d), (d, H),
+                                                                                 (P, d))]
+    sp = KDASmallProjections(*ws)
+    x = torch.randn(m, H, device="cuda", dtype=torch.bfloat16)
+
+    def graph_us(fn):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(50):
+            g.replay()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / 50, out
+
+    t_sep, ref = graph_us(lambda: sp.forward_separate(x))
+    ref = [r.clone() for r in ref]
+    sp.fuse()
+    t_fused, out = graph_us(lambda: sp.forward(x))
+    for a, b in zip(ref, out):
+        ulp = a.float().abs().clamp_min(1e-3) * 2 ** -7
+        assert ((a.float() - b.float()).abs() <= ulp).all()
+    print(f"KDA small projections M={m}: separate {t_sep:.1f} us, fused {t_fused:.1f} us")
