@@ -40,7 +40,8 @@ constexpr int kMPBytes = 128 * kMTile;                 // P: 128 heads x 128 row
 constexpr uint32_t kMColO = 0, kMColS = 256, kMColQ = 384;
 constexpr float kMTau = 8.f;                           // lazy-rescale threshold, log2 units
 constexpr int kMSoftmaxWarps = 4, kMDequantWarps = 8, kMMmaWarp = 12, kMPrefetchWarp = 13;
-constexpr int kF4Row = 352, kF4FlashRow = 288, kV4ProRow = 320, kF8Row = 576;
+constexpr int kF4Row = 352, kF4FlashRow = 288, kV4ProRow = 320, kV4ProBf16Row = 384, kF8Row = 576;
+constexpr bool is_v4pro(int fmt) { return fmt == kKvV4Pro || fmt == kKvV4ProBf16Rope; }
 
 struct MlaSmem {
   uint64_t tile_full[kMRing];   // tile rows stored                       (4 dequant-warp arrivals)
@@ -102,21 +103,27 @@ template <int FMT>
 struct RawRow {
   uint4 v[FMT == kKvFp8 ? 16 : 8];
   uint4 sc;
-  uint4 rope[2];
+  uint4 rope[FMT == kKvV4ProBf16Rope ? 4 : 2];   // 32 E4M3 values, or 32 bf16 values of the 384-byte cell
 };
 
 template <int FMT>
 __device__ __forceinline__ void load_row(const uint8_t* row, int q, RawRow<FMT>& x) {
   constexpr int NV = FMT == kKvFp8 ? 16 : 8;
   if (row) {
-    if constexpr (FMT == kKvV4Pro) {
-      // 320-byte cell: 448 latent values (codes at 0..223, scales at 224..251, zero pad to 256) + 64 E4M3 rope at
-      // 256; latent dims 448..511 read as zero codes (thread 1's last two code chunks) under the zero pad scales
+    if constexpr (is_v4pro(FMT)) {
+      // 320 / 384-byte cell: 448 latent values (codes at 0..223, scales at 224..251, zero pad to 256) + 64 rope
+      // values at 256 (E4M3, or bf16 in the 384-byte cell); latent dims 448..511 read as zero codes (thread 1's last
+      // two code chunks) under the zero pad scales
 #pragma unroll
       for (int i = 0; i < NV; ++i) x.v[i] = (q == 0 || i < 6) ? ldg16(row + 128 * q + 16 * i) : make_uint4(0, 0, 0, 0);
       x.sc = ldg16(row + 224 + 16 * q);
-      x.rope[0] = ldg16(row + 256 + 32 * q);
-      x.rope[1] = ldg16(row + 256 + 32 * q + 16);
+      if constexpr (FMT == kKvV4ProBf16Rope) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x.rope[i] = ldg16(row + 256 + 64 * q + 16 * i);
+      } else {
+        x.rope[0] = ldg16(row + 256 + 32 * q);
+        x.rope[1] = ldg16(row + 256 + 32 * q + 16);
+      }
     } else if constexpr (FMT != kKvFp8) {     // NVFP4 latent (352-B row; the 288-B row has no rope block)
 #pragma unroll
       for (int i = 0; i < NV; ++i) x.v[i] = ldg16(row + 128 * q + 16 * i);
@@ -138,7 +145,31 @@ __device__ __forceinline__ void load_row(const uint8_t* row, int q, RawRow<FMT>&
 #pragma unroll
     for (int i = 0; i < NV; ++i) x.v[i] = make_uint4(0, 0, 0, 0);
     x.sc = make_uint4(0, 0, 0, 0);
-    x.rope[0] = x.rope[1] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int i = 0; i < (FMT == kKvV4ProBf16Rope ? 4 : 2); ++i) x.rope[i] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Rope chunk c (16 values) of a raw row share as E4M3: the stored bytes, or the 384-byte cell's bf16 values rounded
+// to nearest-even E4M3 (saturating) for the FP8 tensor-core QK product.
+template <int FMT>
+__device__ __forceinline__ uint4 rope_chunk(const RawRow<FMT>& x, int c) {
+  if constexpr (FMT == kKvV4ProBf16Rope) {
+    uint32_t w[4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 b = x.rope[2 * c + h];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const uint32_t p0 = u4_get(b, 2 * k), p1 = u4_get(b, 2 * k + 1);
+        const uint32_t lo = f32x2_to_e4m3x2(__uint_as_float(p0 << 16), __uint_as_float(p0 & 0xFFFF0000u));
+        const uint32_t hi = f32x2_to_e4m3x2(__uint_as_float(p1 << 16), __uint_as_float(p1 & 0xFFFF0000u));
+        w[2 * h + k] = lo | (hi << 16);
+      }
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  } else {
+    return x.rope[c];
   }
 }
 
@@ -160,7 +191,7 @@ __device__ __forceinline__ uint4 row_chunk(const RawRow<FMT>& x, int c, const ui
 
 template <int FMT>
 __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecodeArgs a) {
-  constexpr int RB = FMT == kKvNvfp4 ? kF4Row : FMT == kKvNvfp4NoRope ? kF4FlashRow : FMT == kKvV4Pro ? kV4ProRow
+  constexpr int RB = FMT == kKvNvfp4 ? kF4Row : FMT == kKvNvfp4NoRope ? kF4FlashRow : FMT == kKvV4Pro ? kV4ProRow : FMT == kKvV4ProBf16Rope ? kV4ProBf16Row
                                                                                                     : kF8Row;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -411,7 +442,7 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
           *reinterpret_cast<uint4*>(tb + (2 * q + (c >> 3)) * kMBlk + sw128_chunk(trow, c & 7)) = row_chunk<FMT>(cur, c, sm.f4tab);
 #pragma unroll
         for (int c = 0; c < 2; ++c)
-          *reinterpret_cast<uint4*>(tb + kMRopeOff + sw64_chunk(trow, 2 * q + c)) = cur.rope[c];
+          *reinterpret_cast<uint4*>(tb + kMRopeOff + sw64_chunk(trow, 2 * q + c)) = rope_chunk<FMT>(cur, c);
         if (q == 0) sm.bias[rb][trow] = id_cur >= 0 ? 0.f : -INFINITY;
         fence_proxy_async_smem();
         __syncwarp();
@@ -659,6 +690,7 @@ cudaError_t mla_decode(const MlaDecodeArgs& a, cudaStream_t s) {
     case kKvNvfp4: return launch_mla<kKvNvfp4>(a, s);
     case kKvNvfp4NoRope: return launch_mla<kKvNvfp4NoRope>(a, s);
     case kKvV4Pro: return launch_mla<kKvV4Pro>(a, s);
+    case kKvV4ProBf16Rope: return launch_mla<kKvV4ProBf16Rope>(a, s);
     case kKvFp8: return launch_mla<kKvFp8>(a, s);
     default: return cudaErrorInvalidValue;
   }

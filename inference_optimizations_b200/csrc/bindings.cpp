@@ -244,7 +244,8 @@ void mla_decode(c10::optional<at::Tensor> q, at::Tensor q8, at::Tensor q_scale, 
   TORCH_CHECK(q_scale.numel() >= T * H, "q_scale [T, H]");
   TORCH_CHECK(idx.dim() == 2 && idx.stride(1) == 1 && idx.size(0) == T, "idx [T, topk]");
   TORCH_CHECK(out.size(0) == T && out.size(1) == H && out.size(2) == 512, "out [T, H, 512]");
-  const int64_t rb = fmt == iob::kKvNvfp4 ? 352 : fmt == iob::kKvNvfp4NoRope ? 288 : fmt == iob::kKvV4Pro ? 320 : 576;
+  const int64_t rb = fmt == iob::kKvNvfp4 ? 352 : fmt == iob::kKvNvfp4NoRope ? 288 : fmt == iob::kKvV4Pro ? 320 :
+                     fmt == iob::kKvV4ProBf16Rope ? 384 : 576;
   TORCH_CHECK(pool.dim() == 2 && pool.size(1) == rb, "pool row bytes");
   iob::MlaDecodeArgs a{};
   if (q.has_value()) {

@@ -9,7 +9,8 @@ namespace iob {
 
 enum KvFormat : int { kKvBf16 = 0, kKvFp8 = 1, kKvNvfp4 = 2,
                       kKvNvfp4NoRope = 3,     // MLA only: the rope-free 288-byte NVFP4 row (GLM-Flash latent)
-                      kKvV4Pro = 4 };         // MLA only: the 320-byte DeepSeek V4 Pro cell (448 NVFP4 + 64 E4M3 rope)
+                      kKvV4Pro = 4,           // MLA only: the 320-byte DeepSeek V4 Pro cell (448 NVFP4 + 64 E4M3 rope)
+                      kKvV4ProBf16Rope = 5 }; // MLA only: the 384-byte V4 Pro cell (448 NVFP4 + 64 bf16 rope)
 
 // Bytes of one (page, kv_head) block of a GQA pool page: K then V, each page_size tokens of head_dim values.
 //   bf16 : [K 64 x D x 2][V 64 x D x 2]

@@ -4,7 +4,8 @@ Semantics of the reference's sparse FP4 decode (`kv-cache-4bit/glm-kv4/glm_kv4.p
 `kv-cache-4bit/kv4mla/csrc/api.cpp:73` `sparse_decode`): query token t (H heads x 576 = 512 latent + 64 rope) attends to
 the pool rows idx[t, :] (-1 = masked); K = the full row, V = its 512 latent values; returns out [T, H, 512] and the
 natural-log LSE [T, H].  Rows are NVFP4 352-B rows (FMT_NVFP4), E4M3 576-B rows (FMT_FP8) or rope-free NVFP4
-288-B rows (FMT_NVFP4_NOROPE, the GLM-Flash latent) or 320-B DeepSeek V4 Pro cells (FMT_V4PRO)."""
+288-B rows (FMT_NVFP4_NOROPE, the GLM-Flash latent) or 320-B / 384-B DeepSeek V4 Pro cells (FMT_V4PRO, E4M3 rope;
+FMT_V4PRO_BF16, bf16 rope)."""
 from __future__ import annotations
 
 import math
@@ -19,11 +20,12 @@ from .kvcache import FMT_FP8, FMT_NVFP4
 
 FMT_NVFP4_NOROPE = 3      # the rope-free 288-byte NVFP4 row (GLM-Flash latent): attention over the 512 latent dims
 FMT_V4PRO = 4             # the 320-byte DeepSeek V4 Pro cell: 448 NVFP4 latent dims (dims 448..511 read as zero) + 64 E4M3
+FMT_V4PRO_BF16 = 5        # the 384-byte V4 Pro cell: as FMT_V4PRO with 64 bf16 rope values (rounded to E4M3 for the QK MMA)
                           # rope; the output's dims 448..511 are zero
 NUM_SMS = 148
 TILE = 128                # rows per kernel tile (split granularity and lazy-rescale step)
 ROW_BYTES = {FMT_NVFP4: F.MLA_ROW_BYTES, FMT_FP8: F.MLA_FP8_ROW_BYTES, FMT_NVFP4_NOROPE: F.GLMFLASH_ROW_BYTES,
-             FMT_V4PRO: F.v4pro_cell_bytes("fp8")}
+             FMT_V4PRO: F.v4pro_cell_bytes("fp8"), FMT_V4PRO_BF16: F.v4pro_cell_bytes("bf16")}
 
 
 def mla_split_policy(tokens: int, topk: int, overhead_tiles: float = 2.0) -> tuple[int, int]:
@@ -122,8 +124,8 @@ def dequant_rows(pool: torch.Tensor, fmt: int) -> torch.Tensor:
     if fmt == FMT_NVFP4_NOROPE:
         lat = F.glmflash_row_dequantize(pool)
         return torch.cat([lat, torch.zeros(lat.shape[0], 64, dtype=lat.dtype, device=lat.device)], -1)
-    if fmt == FMT_V4PRO:
-        c = F.v4pro_cell_dequantize(pool, "fp8")                             # [rows, 448 latent + 64 rope]
+    if fmt in (FMT_V4PRO, FMT_V4PRO_BF16):
+        c = F.v4pro_cell_dequantize(pool, "fp8" if fmt == FMT_V4PRO else "bf16")                           # [rows, 448 latent + 64 rope]
         z = torch.zeros(c.shape[0], F.MLA_NOPE - F.V4P_NOPE, dtype=c.dtype, device=c.device)
         return torch.cat([c[:, :F.V4P_NOPE], z, c[:, F.V4P_NOPE:]], -1)
     raise ValueError(fmt)

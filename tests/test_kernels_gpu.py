@@ -194,6 +194,7 @@ def _mla_case(cuda, t, h, topk, fmt, rows=3000, mask_frac=0.1, seed=5):
     rope = torch.randn(rows, 64)
     pool = (F.mla_row_quantize(nope, rope) if fmt == K.FMT_NVFP4 else F.glmflash_row_quantize(nope) if fmt == 3
             else F.v4pro_cell_quantize(torch.cat([nope[:, :F.V4P_NOPE], rope], 1)) if fmt == 4
+            else F.v4pro_cell_quantize(torch.cat([nope[:, :F.V4P_NOPE], rope], 1), "bf16") if fmt == 5
             else F.mla_fp8_row_quantize(nope, rope)).to(cuda)
     idx = torch.stack([torch.randperm(rows)[:topk] for _ in range(t)]).int()
     idx[torch.rand(t, topk) < mask_frac] = -1
@@ -202,7 +203,8 @@ def _mla_case(cuda, t, h, topk, fmt, rows=3000, mask_frac=0.1, seed=5):
     return M, pool, idx.to(cuda), q
 
 
-@pytest.mark.parametrize("fmt", [K.FMT_NVFP4, K.FMT_FP8, 3, 4])   # 3: rope-free 288-B row, 4: V4 Pro 320-B cell
+@pytest.mark.parametrize("fmt", [K.FMT_NVFP4, K.FMT_FP8, 3, 4, 5])   # 3: rope-free 288-B row, 4 / 5: V4 Pro
+                                                                    # 320-B (E4M3 rope) / 384-B (bf16 rope) cell
 @pytest.mark.parametrize("t,h,topk", [(3, 128, 2048), (5, 64, 200), (2, 16, 64), (1, 128, 640)])
 def test_mla_decode(cuda, fmt, t, h, topk):
     M, pool, idx, q = _mla_case(cuda, t, h, topk, fmt)
