@@ -190,6 +190,8 @@ class EngineConfig:
     # runtime
     cuda_graphs: bool = True
     extend_kernel: bool = True           # GQA prefill over NVFP4 / FP8 pools through the 128-row extend kernel
+    pdmux: bool = False                  # GQA, tp = 1, no spec: prefill and decode as lanes on disjoint SM partitions
+    pdmux_budget: int = 65536            # tokens x layers the split prefill advances per engine iteration
     graph_batch_sizes: str = "1,2,4,8,16,32,64"
     # parallelism
     tp: int = 1

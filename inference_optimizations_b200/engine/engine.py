@@ -43,16 +43,25 @@ class Engine:
         self.stats: list[StepStats] = []
         self.finished: list[Request] = []
         self.spec_policy = SpecPolicy(ecfg.draft_tokens, ecfg.spec_policy)
+        self.pdmux = None
+        if getattr(ecfg, "pdmux", False):
+            from .pdmux import PdmuxEngine
+            self.pdmux = PdmuxEngine(self, token_budget=ecfg.pdmux_budget)
         self.trace = None
         if ecfg.trace:
             from ..tooling.trace import StepTrace
             self.trace = StepTrace(ecfg.trace, tp_rank)
+
+    def has_work(self) -> bool:
+        return self.pdmux.has_work() if self.pdmux is not None else self.sched.has_work()
 
     def add_request(self, prompt: list, params: Optional[SamplingParams] = None) -> Request:
         return self.sched.new_request(prompt, params or SamplingParams())
 
     def step(self) -> dict:
         """One engine iteration.  Returns rid -> tokens produced this step."""
+        if self.pdmux is not None:
+            return self.pdmux.step()
         t0 = time.perf_counter()
         rec = self.trace.begin() if self.trace else None
         batch = self.sched.schedule()
@@ -127,7 +136,7 @@ class Engine:
     def generate(self, prompts: list, params: Optional[SamplingParams] = None, max_steps: int = 1 << 30) -> list:
         reqs = [self.add_request(p, params) for p in prompts]
         steps = 0
-        while self.sched.has_work() and steps < max_steps:
+        while self.has_work() and steps < max_steps:
             self.step()
             steps += 1
         return [r.output for r in reqs]

@@ -54,7 +54,7 @@ class EngineLoop:
     def _run(self) -> None:
         while not self.stop:
             with self.lock:
-                if not self.engine.sched.has_work():
+                if not self.engine.has_work():
                     self.cv.wait(0.05)
                     continue
                 out = self.engine.step()

@@ -95,3 +95,14 @@ def test_pdmux_dp_lockstep():
     log0, log1 = res[0][1], res[1][1]
     assert len(log0) == len(log1)
     assert [(g, s) for g, s, _ in log0] == [(g, s) for g, s, _ in log1]   # same group and layer range every iteration
+
+
+def test_engine_config_flag():
+    """EngineConfig(pdmux=True): Engine.step / generate run through the lanes and give the plain tokens."""
+    params = SamplingParams(max_new_tokens=5)
+    ref = _engine().generate(PROMPTS, params)
+    ecfg = EngineConfig(model="tiny_gqa", device="cpu", kv_dtype="bf16", max_running=4, chunked_prefill=40,
+                        cuda_graphs=False, pdmux=True, pdmux_budget=40)
+    eng = Engine(ecfg, max_seq=256)
+    assert eng.generate(PROMPTS, params) == ref
+    assert eng.pdmux.log and not eng.has_work()
