@@ -291,15 +291,18 @@ def main() -> None:
     ap.add_argument("--burst", type=int, default=1)
     ap.add_argument("--device", default="cuda:0")
     ap.add_argument("--kv", default="nvfp4")
+    ap.add_argument("--groups", type=int, default=3)
+    ap.add_argument("--divisor", type=int, default=36)
     a = ap.parse_args()
     cfg = replace(model_config(a.model), num_layers=a.layers)
     res = {"model": a.model, "layers": a.layers, "decode_batch": a.decode, "ctx": a.ctx, "prompt": a.prompt,
-           "chunk": a.chunk}
+           "chunk": a.chunk, "groups": a.groups, "divisor": a.divisor}
     for mode in ("plain", "pdmux"):
         ecfg = EngineConfig(model=a.model, device=a.device, kv_dtype=a.kv, max_running=a.decode + 2,
                             chunked_prefill=a.chunk, decode_burst=a.burst)
         eng = Engine(ecfg, cfg, max_seq=max(a.ctx + 2048, a.prompt) + 1024)
-        pm = PdmuxEngine(eng, token_budget=a.budget) if mode == "pdmux" else None
+        pm = PdmuxEngine(eng, n_groups=a.groups, token_budget=a.budget, decode_bs_divisor=a.divisor) \
+            if mode == "pdmux" else None
         step = pm.step if pm is not None else eng.step
         g = torch.Generator().manual_seed(0)
         for _ in range(a.decode):
@@ -319,6 +322,7 @@ def main() -> None:
         res[mode] = _window(step, eng, prompt)
         if pm is not None:
             res["lanes_sms"] = pm.lanes.sms
+            res["groups_used"] = sorted({g for g, _, _ in pm.log})
         del eng, pm
         torch.cuda.empty_cache()
     print(json.dumps(res))
