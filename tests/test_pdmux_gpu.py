@@ -54,3 +54,15 @@ def test_pdmux_matches_plain_engine(kv):
     assert outs == ref
     assert any(g == 1 and s is not None and n > 0 for g, s, n in pm.log)   # both lanes busy on the split partitions
     assert pm.engine.runner.kv.alloc["global"].used == 0
+
+
+def test_pdmux_five_groups():
+    """Five stream groups: the decode batch picks the largest decode partition; tokens stay the plain engine's."""
+    params = SamplingParams(max_new_tokens=6, ignore_eos=True)
+    ecfg = EngineConfig(model="tiny_gqa", device="cuda:0", kv_dtype="nvfp4", max_running=4, chunked_prefill=128)
+    ref = Engine(ecfg, max_seq=1024).generate(PROMPTS, params)
+    pm = PdmuxEngine(Engine(ecfg, max_seq=1024), n_groups=5, token_budget=256, decode_bs_divisor=1)
+    assert pm.generate(PROMPTS, params) == ref
+    used = {g for g, s, n in pm.log if s is not None and n > 0}
+    assert used == {3}
+    assert pm.lanes.sms[3][1] > pm.lanes.sms[3][0]
