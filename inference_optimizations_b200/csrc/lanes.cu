@@ -15,10 +15,32 @@
 
 namespace iob {
 namespace {
-int fail(char* err, int errlen, const char* what, CUresult r) {
+// Driver entry points are looked up through the runtime (cudaGetDriverEntryPoint), so the extension does not link
+// libcuda and still imports on a machine without a GPU driver.
+typedef CUresult (*PfnDeviceGet)(CUdevice*, int);
+typedef CUresult (*PfnGetDevResource)(CUdevice, CUdevResource*, CUdevResourceType);
+typedef CUresult (*PfnSplitByCount)(CUdevResource*, unsigned int*, const CUdevResource*, CUdevResource*, unsigned int,
+                                    unsigned int);
+typedef CUresult (*PfnGenerateDesc)(CUdevResourceDesc*, CUdevResource*, unsigned int);
+typedef CUresult (*PfnGreenCtxCreate)(CUgreenCtx*, CUdevResourceDesc, CUdevice, unsigned int);
+typedef CUresult (*PfnGreenCtxStreamCreate)(CUstream*, CUgreenCtx, unsigned int, int);
+typedef CUresult (*PfnGetErrorString)(CUresult, const char**);
+
+template <typename T>
+bool entry(const char* name, T& fn) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess ||
+      p == nullptr)
+    return false;
+  fn = reinterpret_cast<T>(p);
+  return true;
+}
+
+int fail(char* err, int errlen, const char* what, CUresult r, PfnGetErrorString es) {
   const char* s = nullptr;
-  cuGetErrorString(r, &s);
-  snprintf(err, errlen, "%s: %s", what, s ? s : "unknown driver error");
+  if (es) es(r, &s);
+  snprintf(err, errlen, "%s: %s", what, s ? s : "driver error");
   return -1;
 }
 }  // namespace
@@ -28,15 +50,29 @@ int sm_lanes_create(int device, int first_sms, unsigned long long* streams, int*
     snprintf(err, errlen, "cudaSetDevice(%d) failed", device);
     return -1;
   }
+  PfnDeviceGet device_get;
+  PfnGetDevResource get_res;
+  PfnSplitByCount split;
+  PfnGenerateDesc gen_desc;
+  PfnGreenCtxCreate gctx_create;
+  PfnGreenCtxStreamCreate gstream_create;
+  PfnGetErrorString es = nullptr;
+  entry("cuGetErrorString", es);
+  if (!entry("cuDeviceGet", device_get) || !entry("cuDeviceGetDevResource", get_res) ||
+      !entry("cuDevSmResourceSplitByCount", split) || !entry("cuDevResourceGenerateDesc", gen_desc) ||
+      !entry("cuGreenCtxCreate", gctx_create) || !entry("cuGreenCtxStreamCreate", gstream_create)) {
+    snprintf(err, errlen, "the driver has no green-context entry points");
+    return -1;
+  }
   CUdevice dev;
-  CUresult r = cuDeviceGet(&dev, device);
-  if (r != CUDA_SUCCESS) return fail(err, errlen, "cuDeviceGet", r);
+  CUresult r = device_get(&dev, device);
+  if (r != CUDA_SUCCESS) return fail(err, errlen, "cuDeviceGet", r, es);
   CUdevResource full, part, rest;
-  r = cuDeviceGetDevResource(dev, &full, CU_DEV_RESOURCE_TYPE_SM);
-  if (r != CUDA_SUCCESS) return fail(err, errlen, "cuDeviceGetDevResource", r);
+  r = get_res(dev, &full, CU_DEV_RESOURCE_TYPE_SM);
+  if (r != CUDA_SUCCESS) return fail(err, errlen, "cuDeviceGetDevResource", r, es);
   unsigned int n = 1;
-  r = cuDevSmResourceSplitByCount(&part, &n, &full, &rest, 0, (unsigned)first_sms);
-  if (r != CUDA_SUCCESS) return fail(err, errlen, "cuDevSmResourceSplitByCount", r);
+  r = split(&part, &n, &full, &rest, 0, (unsigned)first_sms);
+  if (r != CUDA_SUCCESS) return fail(err, errlen, "cuDevSmResourceSplitByCount", r, es);
   if (n != 1 || rest.sm.smCount == 0) {
     snprintf(err, errlen, "SM split of %d gave %u group(s), %u SMs left", first_sms, n, rest.sm.smCount);
     return -1;
@@ -44,14 +80,14 @@ int sm_lanes_create(int device, int first_sms, unsigned long long* streams, int*
   CUdevResource* sets[2] = {&part, &rest};
   for (int i = 0; i < 2; ++i) {
     CUdevResourceDesc desc;
-    r = cuDevResourceGenerateDesc(&desc, sets[i], 1);
-    if (r != CUDA_SUCCESS) return fail(err, errlen, "cuDevResourceGenerateDesc", r);
+    r = gen_desc(&desc, sets[i], 1);
+    if (r != CUDA_SUCCESS) return fail(err, errlen, "cuDevResourceGenerateDesc", r, es);
     CUgreenCtx g;
-    r = cuGreenCtxCreate(&g, desc, dev, CU_GREEN_CTX_DEFAULT_STREAM);
-    if (r != CUDA_SUCCESS) return fail(err, errlen, "cuGreenCtxCreate", r);
+    r = gctx_create(&g, desc, dev, CU_GREEN_CTX_DEFAULT_STREAM);
+    if (r != CUDA_SUCCESS) return fail(err, errlen, "cuGreenCtxCreate", r, es);
     CUstream s;
-    r = cuGreenCtxStreamCreate(&s, g, CU_STREAM_NON_BLOCKING, 0);
-    if (r != CUDA_SUCCESS) return fail(err, errlen, "cuGreenCtxStreamCreate", r);
+    r = gstream_create(&s, g, CU_STREAM_NON_BLOCKING, 0);
+    if (r != CUDA_SUCCESS) return fail(err, errlen, "cuGreenCtxStreamCreate", r, es);
     streams[i] = reinterpret_cast<unsigned long long>(s);
     sms[i] = (int)sets[i]->sm.smCount;
   }
