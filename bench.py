@@ -1,15 +1,25 @@
-"""Flagship serving benchmark: decode throughput of the Gemma-class 31B dense GQA model.
+"""Flagship serving benchmark: the DSA + MoE model (DeepSeek-V3.2 geometry, FP8 128x128 block-scaled weights) served
+with data-parallel attention + expert-parallel MoE over N GPUs of one node.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]            (N > 1: launched by torch.distributed.run)
+    python bench.py --model gemma31b ...                            (the Gemma-class dense GQA model, tensor parallel)
     python bench.py --impl reference ...                            (the reference arm)
 
-Workload: 32 sessions, each holding a 32768-token random prompt in the paged KV pool, generating greedily (up to 512
-output tokens).  One timed step = one engine iteration over all sessions (one decode step, or one speculative step
-with --spec).  Tensor parallel over the N GPUs (strong scaling: the total work is fixed).  Prints one JSON line on rank
-0: `value` = output tokens / device time of the step computation (max over ranks); `e2e` = the same through
-`Engine.step()` including each step's pinned host->device input copy and device->host result read, timed on the device
-from the first input copy to the last result (max over ranks).  Weights and KV (~170 GB read per step at N=1) are far
-larger than L2, so no flush is needed between steps.
+Workload (DSA-MoE): 64 sessions over all ranks (64 / N per rank, each rank its own scheduler and pools), uniform
+random token ids, 8192-token prompts, up to 1024 output tokens.  Phase 1 prefills every prompt through the engine
+(timed on the device, reported as its own fields: prefill tok/s and time to first token).  Phase 2 decodes all
+sessions together: W untimed warm-up steps, then K timed steps.  Every MoE layer is the peer-memory expert exchange
+(`parallel/ep.py`); the ranks step in lockstep.  Decode steps replay one CUDA graph per rank (one pinned host->device
+copy of the step inputs, one device->host read of the sampled tokens).
+
+Printed by rank 0, one JSON line: `value` = output tokens of the K steps / device time of the step computations (the
+graph replays; max over ranks); `e2e` = the same through `Engine.step()` including each step's host->device input copy
+and device->host result read, timed on the device around the whole loop (max over ranks).  Weights and KV read per step
+(tens of GB) are far larger than the 126 MB L2, so no flush is needed between steps.
+
+Depth: `--layers` (default 13 = the 3 dense layers + 10 MoE layers, the deepest stack whose 256 experts per layer fit
+one GPU) is the same at every N so the 1/2/4/8 curve measures one model; `--full-depth` additionally runs the full
+61-layer model (it needs the expert memory of 8 GPUs) and reports it as the `full_depth` field.
 """
 from __future__ import annotations
 
@@ -19,41 +29,253 @@ import os
 import sys
 import time
 
-METRIC = "output tok/s per 8×B200 box at 1/2/4/8 GPUs; per-user decode tok/s, 64×200k ctx"
+# DeepSeek V4 Pro final composed recipe, 64 sessions on 8 x B200: 1,813 - 1,996 steady tok/s
+BASELINE_TOK_S = 1996.0
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=40)
+    p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--model", default="gemma31b")
-    p.add_argument("--sessions", type=int, default=32)
-    p.add_argument("--ctx", type=int, default=32768)
-    p.add_argument("--max-new", type=int, default=512)
+    p.add_argument("--model", default="dsa_moe")
+    p.add_argument("--sessions", type=int, default=None, help="sessions over all ranks (dsa_moe 64, gemma31b 32)")
+    p.add_argument("--ctx", type=int, default=None, help="prompt tokens (dsa_moe 8192, gemma31b 32768)")
+    p.add_argument("--max-new", type=int, default=None, help="output tokens (dsa_moe 1024, gemma31b 512)")
+    p.add_argument("--layers", type=int, default=13, help="dsa_moe: depth of the scaling-curve model")
+    p.add_argument("--full-depth", action="store_true", help="dsa_moe: also run the full-depth model")
     p.add_argument("--kv", default="nvfp4", choices=["nvfp4", "fp8", "bf16"])
     p.add_argument("--spec", type=int, default=1,
-                   help="1 = speculative decoding, the config's 1-layer draft proposing 3 tokens (default); 0 = plain")
+                   help="gemma31b: 1 = speculative decoding, the config's 1-layer draft proposing 3 tokens; 0 = plain")
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
-                   help="tensor-parallel all-reduce: own peer-memory kernel fused with the norms (default) or NCCL")
-    return p.parse_args()
+                   help="gemma31b tensor-parallel all-reduce: own peer-memory kernel fused with the norms or NCCL")
+    a = p.parse_args()
+    gemma = a.model != "dsa_moe"
+    a.sessions = a.sessions or (32 if gemma else 64)
+    a.ctx = a.ctx or (32768 if gemma else 8192)
+    a.max_new = a.max_new or (512 if gemma else 1024)
+    return a
 
 
 def reference_arm(args) -> None:
     # The reference is a collection of SGLang v0.5.20 patches and kernels; it has no installable package and SGLang
-    # is not present on this image, so its serving stack cannot run here (install attempt recorded in DESIGN.md).
+    # is not present on this image, so its serving stack cannot run here.
     print(json.dumps({"impl": "reference", "unavailable": "reference is an SGLang patch set with no setup.py/"
                       "pyproject (pip: 'not installable') and SGLang is not installed offline"}))
 
 
-def main() -> int:
-    args = parse()
-    if args.impl == "reference":
-        if int(os.environ.get("RANK", "0")) == 0:
-            reference_arm(args)
-        return 0
+def _any_rank(flag: bool, dev) -> bool:
+    import torch
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        return flag
+    t = torch.tensor([int(flag)], dtype=torch.int32, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return bool(t.item())
+
+
+def _gather_floats(vals: list, dev) -> list:
+    """Every rank's list (same length on every rank) concatenated, on every rank."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device=dev)
+    if not dist.is_initialized():
+        return t.tolist()
+    out = torch.empty(dist.get_world_size() * t.numel(), dtype=torch.float64, device=dev)
+    dist.all_gather_into_tensor(out, t)
+    return out.tolist()
+
+
+def _sum_ranks(x: int, dev) -> int:
+    import torch
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        return x
+    t = torch.tensor([x], dtype=torch.int64, device=dev)
+    dist.all_reduce(t)
+    return int(t.item())
+
+
+def run_dsa(args, info, dev, layers: int, steps: int, warm: int) -> dict:
+    """One DSA-MoE serving run (prefill every prompt, then timed decode steps); the measurements as a dict."""
+    import torch
+    import torch.distributed as dist
+    from inference_optimizations_b200.config import EngineConfig, model_config
+    from inference_optimizations_b200.engine.engine import Engine
+    from inference_optimizations_b200.engine.scheduler import SamplingParams
+    from inference_optimizations_b200.parallel import dist as D
+    from inference_optimizations_b200.utils.clocks import ClockSampler, rejected
+
+    n, rank = info.world, info.rank
+    if args.sessions % n:
+        raise SystemExit(f"{args.sessions} sessions do not divide over {n} ranks")
+    per = args.sessions // n
+    cfg = model_config("dsa_moe", num_layers=layers)
+    ecfg = EngineConfig(model="dsa_moe", device=str(dev), kv_dtype=args.kv, max_running=per,
+                        chunked_prefill=args.ctx, cuda_graphs=not args.no_graphs, graph_batch_sizes=str(per),
+                        ep=n, prefix_cache=False)
+    assert args.max_new > warm + steps + 4, "sessions must not finish inside the timed steps"
+    t_build = time.perf_counter()
+    eng = Engine(ecfg, cfg, max_seq=args.ctx + args.max_new + 64, ep_rank=rank,
+                 ep_group=dist.group.WORLD if n > 1 else None)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t_build
+    g = torch.Generator().manual_seed(1000 + rank)
+    reqs = [eng.add_request(torch.randint(1, cfg.vocab, (args.ctx,), generator=g).tolist(),
+                            SamplingParams(max_new_tokens=args.max_new)) for _ in range(per)]
+    # ---------------------------------------------------------------- phase 1: prefill every prompt
+    if n > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ttft = {}
+    t0 = time.perf_counter()
+    p0.record()
+    while _any_rank(eng.sched.prefilling is not None or bool(eng.sched.waiting), dev):
+        out = eng.step()
+        now = time.perf_counter() - t0
+        for rid in out:
+            ttft.setdefault(rid, now)
+    p1.record()
+    torch.cuda.synchronize()
+    prefill_ms = D.max_over_ranks(p0.elapsed_time(p1))
+    ttfts = sorted(_gather_floats([1e3 * ttft.get(r.rid, float("nan")) for r in reqs], dev))
+    # ---------------------------------------------------------------- phase 2: decode every session
+    eng.runner.warm_graphs(per)                      # collective under expert parallelism
+    for _ in range(warm):
+        eng.step()
+    bucket = eng.runner._bucket(per)
+    launches_per_step = eng.runner.count_step_launches(bucket)
+    table0 = eng.runner.kv.table.bytes_synced if hasattr(eng.runner.kv.table, "bytes_synced") else 0
+    torch.cuda.synchronize()
+    if n > 1:
+        dist.barrier()
+    clocks = ClockSampler(info.local_rank).start()
+    time.sleep(0.3)
+    eng.runner.event_log = []
+    n_stats = len(eng.stats)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record()
+    toks = 0
+    for _ in range(steps):
+        out = eng.step()
+        toks += sum(len(v) for v in out.values())
+    ev1.record()
+    torch.cuda.synchronize()
+    if n > 1:
+        dist.barrier()
+    ck = clocks.stop()
+    kinds = [st.kind for st in eng.stats[n_stats:]]
+    graphed = len(eng.runner.event_log)
+    dev_ms = D.max_over_ranks(sum(a.elapsed_time(b) for a, b in eng.runner.event_log))
+    e2e_ms = D.max_over_ranks(ev0.elapsed_time(ev1))
+    toks_all = _sum_ranks(toks, dev)
+    status = 0
+    if eng.runner.model.ep:
+        for ex in eng.runner.model.ep.values():
+            status |= int(ex.status.item()) if hasattr(ex, "status") else 0
+    status = int(D.max_over_ranks(float(status)))
+    table1 = eng.runner.kv.table.bytes_synced if hasattr(eng.runner.kv.table, "bytes_synced") else 0
+    h2d = 5 * 4 * bucket + (table1 - table0) // max(1, steps)
+    mem_gb = D.max_over_ranks(torch.cuda.max_memory_allocated(dev) / 1e9)
+    pct = lambda q: ttfts[min(len(ttfts) - 1, int(q * len(ttfts)))]  # noqa: E731
+    res = {
+        "value": toks_all / (dev_ms / 1e3),
+        "ms_per_step": dev_ms / steps,
+        "e2e_value": toks_all / (e2e_ms / 1e3),
+        "e2e_ms_per_step": e2e_ms / steps,
+        "h2d": h2d, "d2h": 4 * bucket,
+        "tokens": toks_all, "timed_kinds": {k: kinds.count(k) for k in set(kinds)}, "graph_replays": graphed,
+        "launches": launches_per_step * graphed,
+        "prefill": {"tokens": args.sessions * args.ctx, "ms": round(prefill_ms, 2),
+                    "tok_s": round(args.sessions * args.ctx / (prefill_ms / 1e3), 1),
+                    "ttft_ms": {"mean": round(sum(ttfts) / len(ttfts), 1), "p50": round(pct(0.5), 1),
+                                "p99": round(pct(0.99), 1), "max": round(ttfts[-1], 1)},
+                    "note": "every session's prompt prefilled through Engine.step() (chunks of one prompt per step "
+                            "per rank, sessions queued at t = 0), device time max over ranks; TTFT = host time from "
+                            "the start of the phase to the step that returned the session's first token"},
+        "status": status, "max_mem_gb": round(mem_gb, 1), "build_s": round(build_s, 1),
+        "clocks": ck, "rejected": rejected(ck),
+    }
+    eng.runner.graphs.clear()
+    del eng
+    return res
+
+
+def bench_dsa(args) -> int:
+    """DSA + MoE (DeepSeek-V3.2 geometry, FP8 128x128 weights), DP attention + EP over N GPUs."""
+    import torch
+    from inference_optimizations_b200.parallel import dist as D
+
+    info = D.init("nccl")
+    dev = torch.device("cuda", info.local_rank)
+    torch.cuda.set_device(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    steps, warm = args.steps, max(3, args.warmup)
+    n = info.world
+    r = run_dsa(args, info, dev, args.layers, steps, warm)
+    full = None
+    if args.full_depth:
+        torch.cuda.empty_cache()
+        f = run_dsa(args, info, dev, 61, steps, warm)
+        full = {"layers": 61, "value": round(f["value"], 2), "ms_per_step": round(f["ms_per_step"], 4),
+                "e2e_value": round(f["e2e_value"], 2), "per_user_tok_s": round(f["value"] / args.sessions, 3),
+                "vs_baseline": round(f["value"] / BASELINE_TOK_S, 3), "prefill": f["prefill"],
+                "status": f["status"], "max_mem_gb": f["max_mem_gb"],
+                "clocks": {k: f["clocks"].get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons")}}
+    res = {
+        "metric": (f"output tok/s: DSA-MoE decode of {args.sessions} sessions after their {args.ctx}-token prompts "
+                   f"were prefilled (DP attention + EP over N GPUs, {args.layers} layers)"),
+        "value": round(r["value"], 2),
+        "unit": "tok/s",
+        "n_gpus": n,
+        "steps": steps,
+        "warmup": warm,
+        "ms_per_step": round(r["ms_per_step"], 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp8 (E4M3 weights with 128x128 UE8M0 block scales, activations per 1x128; bf16 between layers)",
+        "data": (f"synthetic: uniform random token ids, random-init weights of the named architecture truncated to "
+                 f"{args.layers} of its 61 layers (3 dense + {args.layers - 3} MoE); every prompt prefilled for real "
+                 "(phase timed as `prefill`)"),
+        "config": {"model": "DSA+MoE (DeepSeek-V3 class): hidden 7168, MLA 128 heads (kv_lora 512, rope 64, q_lora "
+                            "1536), DSA indexer 64x128 top-2048, 256 experts top-8 + 1 shared (FFN 2048), first 3 "
+                            "layers dense (FFN 18432), vocab 129280, FP8 128x128 weights",
+                   "layers": args.layers, "full_layers": 61, "global_batch": args.sessions, "seq_len": args.ctx,
+                   "output_len": args.max_new, "parallelism": f"dp{n}-attention ep{n}", "kv_cache": args.kv,
+                   "sessions_per_rank": args.sessions // n, "cuda_graphs": not args.no_graphs,
+                   "timed_steps": r["timed_kinds"],
+                   "l2": "no flush: every decode step reads the touched experts and the KV (tens of GB), far larger "
+                         "than the 126 MB L2"},
+        "per_user_tok_s": round(r["value"] / args.sessions, 3),
+        "prefill": r["prefill"],
+        "clocks": {k: r["clocks"].get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons", "samples")},
+        "e2e": {"value": round(r["e2e_value"], 2), "unit": "tok/s", "h2d_bytes_per_step": r["h2d"],
+                "d2h_bytes_per_step": r["d2h"], "api": "Engine.step()",
+                "ms_per_step": round(r["e2e_ms_per_step"], 4)},
+        "gpu_launches": r["launches"],
+        "status": r["status"],
+        "max_mem_gb": r["max_mem_gb"],
+        "vs_baseline_note": ("BASELINE.md row 4 (1,813-1,996 steady tok/s at 64 sessions on 8 x B200) is a 61-layer "
+                             "number; see full_depth.vs_baseline (--full-depth)"),
+        "impl": "ours",
+    }
+    if full is not None:
+        res["full_depth"] = full
+    if r["rejected"]:
+        res["clocks"]["rejected"] = r["rejected"]
+    if info.rank == 0:
+        print(json.dumps(res), flush=True)
+    if n > 1:
+        D.shutdown()
+    return 0
+def bench_gemma(args) -> int:
+    """Gemma-class dense GQA model, tensor parallel over the N GPUs, decode throughput over 32
+    sessions whose 32k-token prompts are in the paged pool."""
     import torch
     from inference_optimizations_b200.config import EngineConfig, model_config
     from inference_optimizations_b200.engine.engine import Engine
@@ -142,7 +364,8 @@ def main() -> int:
         acc = [r.accepted / max(1, r.spec_steps) for r in eng.sched.running]
         accept = sum(acc) / max(1, len(acc))
     res = {
-        "metric": METRIC,
+        "metric": (f"output tok/s: Gemma-class dense GQA decode of {args.sessions} sessions holding "
+                   f"{args.ctx}-token prompts (tensor parallel over N GPUs)"),
         "value": round(value, 2),
         "unit": "tok/s",
         "n_gpus": tp,
@@ -190,6 +413,19 @@ def main() -> int:
         eng.runner.graphs.clear()
         D.shutdown()
     return 0
+
+
+
+
+def main() -> int:
+    args = parse()
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            reference_arm(args)
+        return 0
+    if args.model == "dsa_moe":
+        return bench_dsa(args)
+    return bench_gemma(args)
 
 
 if __name__ == "__main__":

@@ -17,7 +17,8 @@ def _kernels_of(name: str, args: tuple) -> int:
     if name == "gqa_decode":
         return 2 if args[15] > 1 else 1          # main kernel (+ split combine)
     if name == "mla_decode":
-        return 2 if args[-1] > 1 else 1
+        # query quantization (when a bf16 query is passed) + main kernel + split combine (num_splits > 1)
+        return (1 if args[0] is not None else 0) + 1 + (1 if args[12] > 1 else 0)
     return 1
 
 

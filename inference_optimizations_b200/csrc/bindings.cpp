@@ -377,7 +377,8 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
               int64_t num_ctas,
               int64_t kind, const c10::optional<at::Tensor>& expert_mul,
               const c10::optional<at::Tensor>& out_peers, int64_t out_offset, int64_t out_div, int64_t out_rank,
-              int64_t out_shared_base, int64_t pairs_total, int64_t ksplit, int64_t split_rows) {
+              int64_t out_shared_base, int64_t pairs_total, int64_t ksplit, int64_t split_rows, int64_t src_group,
+              int64_t src_group_stride) {
   req(wpack, at::kByte, "wpack");
   req(x, at::kByte, "x");
   req(off, at::kInt, "off");
@@ -436,6 +437,8 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
   a.out_scale_stride = out_scale.has_value() ? static_cast<int>(out_scale->stride(0)) : 0;
   a.ksplit = static_cast<int>(ksplit);
   a.split_rows = static_cast<int>(split_rows);
+  a.src_group = static_cast<int>(src_group);
+  a.src_group_stride = static_cast<int>(src_group_stride);
   a.num_ctas = static_cast<int>(num_ctas);
   a.out_mul = static_cast<float>(out_mul);
   a.kind = static_cast<int>(kind);
@@ -758,15 +761,6 @@ void nvfp4_lut_test(const at::Tensor& words, at::Tensor out) {
                                     out.data_ptr<int>(), stream()));
 }
 
-void cvt_rate_test(int64_t iters, int64_t variant, at::Tensor out, at::Tensor sink) {
-  req(out, at::kLong, "out");
-  req(sink, at::kInt, "sink");
-  const at::cuda::CUDAGuard g(out.device());
-  CHECK_CUDA_OK(iob::cvt_rate_test(static_cast<int>(iters), static_cast<int>(variant),
-                                   reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
-                                   reinterpret_cast<uint32_t*>(sink.data_ptr<int>()), stream()));
-}
-
 std::vector<int64_t> sm_lanes(int64_t device, int64_t first_sms) {
   unsigned long long streams[2] = {0, 0};
   int sms[2] = {0, 0};
@@ -774,13 +768,6 @@ std::vector<int64_t> sm_lanes(int64_t device, int64_t first_sms) {
   TORCH_CHECK(iob::sm_lanes_create(static_cast<int>(device), static_cast<int>(first_sms), streams, sms, err,
                                    sizeof(err)) == 0, "sm_lanes: ", err);
   return {static_cast<int64_t>(streams[0]), static_cast<int64_t>(streams[1]), sms[0], sms[1]};
-}
-
-void umma_rate_test(int64_t n, int64_t count, int64_t nacc, int64_t ts, at::Tensor out) {
-  req(out, at::kLong, "out");
-  const at::cuda::CUDAGuard g(out.device());
-  CHECK_CUDA_OK(iob::umma_rate_test(n, count, nacc, ts, reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
-                                    stream()));
 }
 
 }  // namespace
@@ -818,7 +805,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("umma_gemm_test", &umma_gemm_test);
   m.def("umma_f8_mn_test", &umma_f8_mn_test);
   m.def("nvfp4_lut_test", &nvfp4_lut_test);
-  m.def("umma_rate_test", &umma_rate_test);
-  m.def("cvt_rate_test", &cvt_rate_test);
   m.def("sm_lanes", &sm_lanes);
 }

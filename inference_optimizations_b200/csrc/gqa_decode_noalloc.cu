@@ -17,22 +17,19 @@ struct NoAllocScratch {
 // One instance per GPU that loads the library; kept until process exit.
 static __device__ __align__(256) NoAllocScratch g_noalloc_scratch;
 
-constexpr int kMaxDevices = 64;
-NoAllocScratch* g_dev_ptr[kMaxDevices] = {};
 std::mutex g_setup_mu;
 
-// Device address of the scratch on the current device (looked up once per device, with that device current).
+// Device address of the scratch on the current device.  Resolved on every call with that device current (the
+// lookup allocates nothing and is cheap), so an address is never reused after the device's context was torn down
+// and the module reloaded.
 int scratch_for_current_device(NoAllocScratch** out) {
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return IOB_NOALLOC_ESETUP;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return IOB_NOALLOC_ESETUP;
   std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (g_dev_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) return IOB_NOALLOC_ESETUP;
-    g_dev_ptr[dev] = static_cast<NoAllocScratch*>(p);
-  }
-  *out = g_dev_ptr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) return IOB_NOALLOC_ESETUP;
+  *out = static_cast<NoAllocScratch*>(p);
   return IOB_NOALLOC_OK;
 }
 
@@ -86,6 +83,17 @@ extern "C" __attribute__((visibility("default"))) int iob_gqa_decode_noalloc(
   a.trace = nullptr;
   a.exact = exact;
   e = iob::gqa_decode(a, stream);
+  return static_cast<int>(e);
+}
+
+extern "C" __attribute__((visibility("default"))) int iob_gqa_decode_noalloc_status(int* host_out,
+                                                                                   cudaStream_t stream) {
+  if (!host_out) return IOB_NOALLOC_EINVAL;
+  NoAllocScratch* s = nullptr;
+  const int rc = scratch_for_current_device(&s);
+  if (rc != IOB_NOALLOC_OK) return rc;
+  cudaError_t e = cudaMemcpyAsync(host_out, s->status, sizeof(int), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
   return static_cast<int>(e);
 }
 

@@ -12,8 +12,9 @@
 // loads the library keeps this memory until the process exits.
 //
 // Contract:
-//   * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that device current;
-//     make that first call outside any CUDA-graph stream capture.
+//   * Every call looks up the array's device address (cudaGetSymbolAddress) with the calling thread's current device
+//     current; the first call on a device may initialize the module there, so make it outside any CUDA-graph stream
+//     capture.  The address is not cached, so the entry point stays valid after a device reset.
 //   * All calls on a device share the one array: calls that overlap on the GPU (different streams, or concurrent
 //     graph replays) race on it.  Serialize them.
 //   * A call whose split-K workspace would not fit returns IOB_NOALLOC_ETOOBIG and launches nothing.
@@ -43,6 +44,12 @@ int iob_gqa_decode_noalloc(const void* q, const void* pool, const int* page_tabl
                            const int* kv_len, void* out, int B, int n_q, int Hq, int Hk, int D, int window, int fmt,
                            int tiles_per_split, int num_splits, float sm_scale, float k_scale, float v_scale,
                            int exact, cudaStream_t stream);
+
+// The kernel's status word of the last call on the current device, read into *host_out after `stream` drained:
+// 0 = ok; non-zero = a bounded wait inside the kernel gave up (its output is then not valid).  The decode call itself
+// only reports launch errors, so a caller that needs to know whether the result is valid reads this after it.
+// Returns IOB_NOALLOC_OK or an error code like the decode call.
+int iob_gqa_decode_noalloc_status(int* host_out, cudaStream_t stream);
 
 // Human-readable text for a return code of iob_gqa_decode_noalloc.
 const char* iob_gqa_decode_noalloc_strerror(int code);

@@ -190,6 +190,10 @@ struct MoeGemmArgs {
   int out_div, out_rank, out_shared_base, pairs_total;
   int* status;
   int E, n_tiles, KC, G, NT, mode, src_div, src_limit, src_shared_base, x_stride, out_stride, out_scale_stride;
+  // Optional grouped source rows (0 = off): activation row of a pair p below src_limit is
+  // (q / src_group) * src_group_stride + q % src_group with q = p / src_div -- e.g. head h of token t at row
+  // t * src_group_stride + h when a projection's output holds every head's slice back to back.
+  int src_group, src_group_stride;
   int ksplit;                 // split-K factor (>= 1): item = (expert, token tile, weight tile, K range)
   int split_rows;             // kMoeOutF32Split: rows between two splits' partials
   int num_ctas;
@@ -283,8 +287,6 @@ cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_on
 
 cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N, int K, int sw64, cudaStream_t s);
 cudaError_t umma_f8_mn_test(const void* A, const void* B, float* C, int N, int K, cudaStream_t s);
-cudaError_t cvt_rate_test(int iters, int variant, long long* out, uint32_t* sink, cudaStream_t s);
-cudaError_t umma_rate_test(int n, int count, int nacc, int ts, long long* out, cudaStream_t s);
 cudaError_t nvfp4_lut_test(const uint32_t* words, int nwords, int* out, cudaStream_t s);
 
 // Two green contexts over disjoint SM sets (first_sms rounded up by the driver, and the rest), one stream each:

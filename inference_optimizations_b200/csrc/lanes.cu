@@ -24,6 +24,8 @@ typedef CUresult (*PfnSplitByCount)(CUdevResource*, unsigned int*, const CUdevRe
 typedef CUresult (*PfnGenerateDesc)(CUdevResourceDesc*, CUdevResource*, unsigned int);
 typedef CUresult (*PfnGreenCtxCreate)(CUgreenCtx*, CUdevResourceDesc, CUdevice, unsigned int);
 typedef CUresult (*PfnGreenCtxStreamCreate)(CUstream*, CUgreenCtx, unsigned int, int);
+typedef CUresult (*PfnGreenCtxDestroy)(CUgreenCtx);
+typedef CUresult (*PfnStreamDestroy)(CUstream);
 typedef CUresult (*PfnGetErrorString)(CUresult, const char**);
 
 template <typename T>
@@ -45,7 +47,18 @@ int fail(char* err, int errlen, const char* what, CUresult r, PfnGetErrorString 
 }
 }  // namespace
 
+// Restores the caller's current device on every return path (the lanes belong to `device`, the calling thread's
+// torch work stays where it was).
+struct DeviceRestore {
+  int prev = -1;
+  DeviceRestore() { cudaGetDevice(&prev); }
+  ~DeviceRestore() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
 int sm_lanes_create(int device, int first_sms, unsigned long long* streams, int* sms, char* err, int errlen) {
+  DeviceRestore restore;
   if (cudaSetDevice(device) != cudaSuccess || cudaFree(nullptr) != cudaSuccess) {
     snprintf(err, errlen, "cudaSetDevice(%d) failed", device);
     return -1;
@@ -56,8 +69,12 @@ int sm_lanes_create(int device, int first_sms, unsigned long long* streams, int*
   PfnGenerateDesc gen_desc;
   PfnGreenCtxCreate gctx_create;
   PfnGreenCtxStreamCreate gstream_create;
+  PfnGreenCtxDestroy gctx_destroy = nullptr;
+  PfnStreamDestroy stream_destroy = nullptr;
   PfnGetErrorString es = nullptr;
   entry("cuGetErrorString", es);
+  entry("cuGreenCtxDestroy", gctx_destroy);
+  entry("cuStreamDestroy", stream_destroy);
   if (!entry("cuDeviceGet", device_get) || !entry("cuDeviceGetDevResource", get_res) ||
       !entry("cuDevSmResourceSplitByCount", split) || !entry("cuDevResourceGenerateDesc", gen_desc) ||
       !entry("cuGreenCtxCreate", gctx_create) || !entry("cuGreenCtxStreamCreate", gstream_create)) {
@@ -77,18 +94,39 @@ int sm_lanes_create(int device, int first_sms, unsigned long long* streams, int*
     snprintf(err, errlen, "SM split of %d gave %u group(s), %u SMs left", first_sms, n, rest.sm.smCount);
     return -1;
   }
+  // Everything made before a failing step is released again: nothing of a failed call has been handed out yet, so
+  // no stream or graph can reference these contexts.
+  CUgreenCtx made_ctx[2] = {nullptr, nullptr};
+  CUstream made_stream[2] = {nullptr, nullptr};
+  auto unwind = [&]() {
+    for (int i = 0; i < 2; ++i) {
+      if (made_stream[i] && stream_destroy) stream_destroy(made_stream[i]);
+      if (made_ctx[i] && gctx_destroy) gctx_destroy(made_ctx[i]);
+    }
+  };
   CUdevResource* sets[2] = {&part, &rest};
   for (int i = 0; i < 2; ++i) {
     CUdevResourceDesc desc;
     r = gen_desc(&desc, sets[i], 1);
-    if (r != CUDA_SUCCESS) return fail(err, errlen, "cuDevResourceGenerateDesc", r, es);
-    CUgreenCtx g;
-    r = gctx_create(&g, desc, dev, CU_GREEN_CTX_DEFAULT_STREAM);
-    if (r != CUDA_SUCCESS) return fail(err, errlen, "cuGreenCtxCreate", r, es);
-    CUstream s;
-    r = gstream_create(&s, g, CU_STREAM_NON_BLOCKING, 0);
-    if (r != CUDA_SUCCESS) return fail(err, errlen, "cuGreenCtxStreamCreate", r, es);
-    streams[i] = reinterpret_cast<unsigned long long>(s);
+    if (r != CUDA_SUCCESS) {
+      unwind();
+      return fail(err, errlen, "cuDevResourceGenerateDesc", r, es);
+    }
+    r = gctx_create(&made_ctx[i], desc, dev, CU_GREEN_CTX_DEFAULT_STREAM);
+    if (r != CUDA_SUCCESS) {
+      made_ctx[i] = nullptr;
+      unwind();
+      return fail(err, errlen, "cuGreenCtxCreate", r, es);
+    }
+    r = gstream_create(&made_stream[i], made_ctx[i], CU_STREAM_NON_BLOCKING, 0);
+    if (r != CUDA_SUCCESS) {
+      made_stream[i] = nullptr;
+      unwind();
+      return fail(err, errlen, "cuGreenCtxStreamCreate", r, es);
+    }
+  }
+  for (int i = 0; i < 2; ++i) {
+    streams[i] = reinterpret_cast<unsigned long long>(made_stream[i]);
     sms[i] = (int)sets[i]->sm.smCount;
   }
   return 0;

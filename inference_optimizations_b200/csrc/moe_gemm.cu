@@ -184,7 +184,9 @@ __device__ __forceinline__ void split_range(int KC, int ksplit, int ks, int& kc0
 // Activation row of pair p: p / src_div for routed pairs, src_shared_base + p - src_limit for the shared-expert
 // rows after them.
 __device__ __forceinline__ int src_row(const MoeGemmArgs& a, int p) {
-  return p < a.src_limit ? p / a.src_div : a.src_shared_base + p - a.src_limit;
+  if (p >= a.src_limit) return a.src_shared_base + p - a.src_limit;
+  const int q = p / a.src_div;
+  return a.src_group > 0 ? (q / a.src_group) * a.src_group_stride + q % a.src_group : q;
 }
 
 // UE8M0 exponent of the smallest power of two s with amax / s <= 448 (biased byte, clamped to [1, 253]).
@@ -739,6 +741,7 @@ cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
   if (a.ksplit < 1 || a.ksplit > a.KC || (a.ksplit > 1 && a.mode != kMoeOutF32Split) ||
       (a.mode == kMoeOutF32Split && a.out_peers))
     return cudaErrorInvalidValue;
+  if (a.src_group < 0 || (a.src_group > 0 && a.src_group_stride < a.src_group)) return cudaErrorInvalidValue;
   if (a.E <= 0 || a.E > kMaxGemmExperts || a.KC <= 0 || a.n_tiles <= 0 || a.num_ctas <= 0 || a.src_div <= 0 ||
       (a.x_stride % 16) || (reinterpret_cast<uintptr_t>(a.x) % 16) || (reinterpret_cast<uintptr_t>(a.wpack) % 16) ||
       (a.mode == kMoeOutSwigluQuant && (a.G != 2 || a.kind == 2)) || a.kind < 0 || a.kind > 2)

@@ -113,210 +113,6 @@ cudaError_t umma_gemm_test(const void* A, const void* B, float* C, int M, int N,
 
 }  // namespace iob
 
-// ---------------------------------------------------------------------------------------------------------------
-// Issue-rate probe (diagnostic): one thread per issuing warp issues `count` UMMAs back to back.
-// variant: 0 kind::f16 SS M128; 1 kind::f16 TS M128; 2 SS without a memory clobber; 3 kind::f8f6f4 SS M128 (K=32);
-//          4 kind::f16 .ws SS M128 (N >= 64); 5 kind::f16 SS M64; 6 as 0 with two issuing warps (own accumulators).
-// out[0] = cycles issuing, out[1] = cycles to completion of all.  Operands are zero-filled.
-namespace iob {
-namespace {
-__device__ __forceinline__ void umma_f16_ss_nc(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-               "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
-               ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-__device__ __forceinline__ void umma_f16_ws_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-               "tcgen05.mma.ws.cta_group::1.kind::f16 [%0], %1, %2, %3, p, 0;\n\t}\n"
-               ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-__global__ void __launch_bounds__(128) umma_rate_kernel(int n, int count, int nacc, int variant, long long* out) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t bar[2];
-  __shared__ uint32_t tmem_base;
-  for (int i = threadIdx.x; i < (16384 + 32768) / 16; i += blockDim.x) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
-  if (warp_id() == 0) { tmem_alloc(&tmem_base, 512); tmem_relinquish(); }
-  if (threadIdx.x == 0) { mbar_init(&bar[0], 1); mbar_init(&bar[1], 1); fence_mbar_init(); }
-  fence_proxy_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t t = tmem_base;
-  const int issuers = variant == 6 ? 2 : 1;
-  if (variant == 10 && warp_id() == 0) {
-    // whole warp converged in the loop; one elected lane issues each MMA (E4M3, both operands K-major)
-    const uint32_t idesc = idesc_dense(0, 0, 128, n);
-    const uint64_t a = desc_sw128(smem_u32(smem)), b = desc_sw128(smem_u32(smem + 16384));
-    const long long c0 = clock64();
-    for (int i = 0; i < count; ++i) {
-      const uint32_t d = t + (i % nacc) * n;
-      if (elect_one()) umma_f8_ss(d, a, b, idesc, 1u);
-      __syncwarp();
-    }
-    const long long c1 = clock64();
-    if (elect_one()) umma_commit(&bar[0]);
-    __syncwarp();
-    mbar_wait(&bar[0], 0, nullptr, nullptr, 0);
-    const long long c2 = clock64();
-    if (threadIdx.x == 0) {
-      out[0] = c1 - c0;
-      out[1] = c2 - c0;
-    }
-  } else if ((variant == 11 || variant == 12) && threadIdx.x == 0) {
-    // E4M3 K-major, descriptors and predicate hoisted; 11: one MMA per asm statement without a memory clobber,
-    // 12: four MMAs per asm statement
-    const uint32_t idesc = idesc_dense(0, 0, 128, n);
-    const uint64_t a = desc_sw128(smem_u32(smem)), b = desc_sw128(smem_u32(smem + 16384));
-    const long long c0 = clock64();
-    if (variant == 11) {
-      for (int i = 0; i < count; ++i) {
-        const uint32_t d = t + (i % nacc) * n;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
-            "l"(a), "l"(b), "r"(idesc), "r"(1u));
-      }
-    } else {
-      for (int i = 0; i < count; i += 4) {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(t),
-            "l"(a), "l"(b), "r"(idesc), "r"(1u));
-      }
-    }
-    const long long c1 = clock64();
-    umma_commit(&bar[0]);
-    mbar_wait(&bar[0], 0, nullptr, nullptr, 0);
-    const long long c2 = clock64();
-    out[0] = c1 - c0;
-    out[1] = c2 - c0;
-  } else if ((variant == 13 || variant == 14) && threadIdx.x == 0) {
-    // batched helpers with distinct operands per MMA (K steps of a 128 B slab), 13: A in smem, 14: A in TMEM
-    const uint32_t idesc = idesc_dense(0, 0, 128, n);
-    const long long c0 = clock64();
-    for (int i = 0; i < count; i += 4) {
-      uint32_t d[4];
-      uint64_t a[4], b[4];
-      uint32_t at[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        d[k] = t + ((i / 4) % nacc) * n;
-        a[k] = desc_sw128(smem_u32(smem) + 32 * k);
-        b[k] = desc_sw128(smem_u32(smem + 16384) + 32 * k);
-        at[k] = t + 256 + 8 * k;
-      }
-      if (variant == 13) umma_f8_ss_x4(d, a, b, idesc, 0xFu);
-      else umma_f8_ts_x4(d, at, b, idesc, 0xFu);
-    }
-    const long long c1 = clock64();
-    umma_commit(&bar[0]);
-    mbar_wait(&bar[0], 0, nullptr, nullptr, 0);
-    const long long c2 = clock64();
-    out[0] = c1 - c0;
-    out[1] = c2 - c0;
-  } else if (variant >= 17 && variant <= 19 && warp_id() == 0) {
-    // K-step batches: descriptors advanced inside the statement (17: one lane issues; 18: converged warp + elect;
-    // 19: converged warp + elect, A in TMEM)
-    const uint32_t idesc = idesc_dense(0, 0, 128, n);
-    const uint64_t a = desc_sw128(smem_u32(smem)), b = desc_sw128(smem_u32(smem + 16384));
-    const long long c0 = clock64();
-    for (int i = 0; i < count; i += 4) {
-      const uint32_t d = t + ((i / 4) % nacc) * n;
-      if (variant == 17) {
-        if (lane_id() == 0) umma_f8_ss_k4<2, 2>(d, a, b, idesc, 1u);
-      } else if (elect_one()) {
-        if (variant == 18) umma_f8_ss_k4<2, 2>(d, a, b, idesc, 1u);
-        else umma_f8_ts_k4<8, 2>(d, t + 256, b, idesc, 1u);
-      }
-      __syncwarp();
-    }
-    const long long c1 = clock64();
-    if (elect_one()) umma_commit(&bar[0]);
-    __syncwarp();
-    mbar_wait(&bar[0], 0, nullptr, nullptr, 0);
-    const long long c2 = clock64();
-    if (threadIdx.x == 0) {
-      out[0] = c1 - c0;
-      out[1] = c2 - c0;
-    }
-  } else if ((variant == 15 || variant == 16) && warp_id() == 0) {
-    // whole warp converged, operands computed by every lane, one elected lane issues batched MMAs
-    // (15: four per statement, distinct K-step descriptors; 16: the same with A in TMEM)
-    const uint32_t idesc = idesc_dense(0, 0, 128, n);
-    const uint32_t sa = smem_u32(smem), sb = smem_u32(smem + 16384);
-    const long long c0 = clock64();
-    for (int i = 0; i < count; i += 4) {
-      uint32_t d[4], at[4];
-      uint64_t a[4], b[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        d[k] = t + ((i / 4) % nacc) * n;
-        a[k] = desc_sw128(sa + 32 * k);
-        b[k] = desc_sw128(sb + 32 * k);
-        at[k] = t + 256 + 8 * k;
-      }
-      if (elect_one()) {
-        if (variant == 15) umma_f8_ss_x4(d, a, b, idesc, 0xFu);
-        else umma_f8_ts_x4(d, at, b, idesc, 0xFu);
-      }
-      __syncwarp();
-    }
-    const long long c1 = clock64();
-    if (elect_one()) umma_commit(&bar[0]);
-    __syncwarp();
-    mbar_wait(&bar[0], 0, nullptr, nullptr, 0);
-    const long long c2 = clock64();
-    if (threadIdx.x == 0) {
-      out[0] = c1 - c0;
-      out[1] = c2 - c0;
-    }
-  } else if (variant != 10 && variant < 11 && lane_id() == 0 && warp_id() < issuers) {
-    const int m = (variant == 5 || variant == 9) ? 64 : 128;
-    const bool f8 = variant == 3 || variant >= 7;
-    uint32_t idesc = f8 ? idesc_dense(0, 0, m, n) : idesc_dense(1, 1, m, n);
-    if (variant == 8) idesc |= 1u << 15;                              // A MN-major
-    const uint64_t a = desc_sw128(smem_u32(smem)), b = desc_sw128(smem_u32(smem + 16384));
-    const uint32_t dbase = t + warp_id() * 128;
-    const long long c0 = clock64();
-    for (int i = 0; i < count; ++i) {
-      const uint32_t d = dbase + (i % nacc) * n;
-      switch (variant) {
-        case 1: umma_f16_ts(d, t + 256, b, idesc, 1u); break;
-        case 2: umma_f16_ss_nc(d, a, b, idesc, 1u); break;
-        case 3: umma_f8_ss(d, a, b, idesc, 1u); break;
-        case 4: umma_f16_ws_ss(d, a, b, idesc, 1u); break;
-        case 7: umma_f8_ts(d, t + 256, b, idesc, 1u); break;                       // E4M3, A from TMEM
-        case 8: umma_f8_ss(d, desc_mn128(smem_u32(smem), 16384), b, idesc, 1u); break;  // E4M3, A MN-major
-        case 9: umma_f8_ss(d, a, b, idesc, 1u); break;                             // E4M3, M = 64
-        default: umma_f16_ss(d, a, b, idesc, 1u); break;
-      }
-    }
-    const long long c1 = clock64();
-    umma_commit(&bar[warp_id()]);
-    mbar_wait(&bar[warp_id()], 0, nullptr, nullptr, 0);
-    const long long c2 = clock64();
-    if (threadIdx.x == 0) {
-      out[0] = c1 - c0;
-      out[1] = c2 - c0;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp_id() == 0) { tc_fence_after(); tmem_dealloc(t, 512); }
-}
-}  // namespace
-
-cudaError_t umma_rate_test(int n, int count, int nacc, int variant, long long* out, cudaStream_t s) {
-  const int smem = 1024 + 16384 + 256 * 128;
-  IOB_CUDA_CHECK(cudaFuncSetAttribute(umma_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  umma_rate_kernel<<<1, 128, smem, s>>>(n, count, nacc, variant, out);
-  return cudaGetLastError();
-}
-}  // namespace iob
 
 // ---------------------------------------------------------------------------------------------------------------
 // kind::f8f6f4 with an MN-major B operand: C[128, N] fp32 = A[128, K] (E4M3, row-major) * B[K, N] (E4M3, row-major:
@@ -409,69 +205,6 @@ __global__ void nvfp4_lut_kernel(const uint32_t* __restrict__ words, int nwords,
 
 cudaError_t nvfp4_lut_test(const uint32_t* words, int nwords, int* out, cudaStream_t s) {
   nvfp4_lut_kernel<<<127, 256, 0, s>>>(words, nwords, out);
-  return cudaGetLastError();
-}
-}  // namespace iob
-
-// ---------------------------------------------------------------------------------------------------------------
-// Conversion / exp2 throughput probe: 4 warps (one per SM sub-partition), each thread runs `iters` rounds of 8
-// independent chains of one instruction kind.  out[variant] = cycles per round (one warp instruction per chain).
-namespace iob {
-namespace {
-template <int variant>
-__global__ void __launch_bounds__(128) cvt_rate_kernel(int iters, long long* out, uint32_t* sink) {
-  uint32_t x[8];
-  float f[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    x[i] = 0x3C003C00u + threadIdx.x + i;
-    f[i] = 0.5f + 0.01f * (threadIdx.x + i);
-  }
-  __syncthreads();
-  const long long c0 = clock64();
-  for (int it = 0; it < iters; ++it) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      switch (variant) {   // compile-time
-        case 0: asm volatile("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(x[i]) : "f"(f[i]), "f"(__uint_as_float(x[i]))); break;
-        case 1: asm volatile("ex2.approx.f16x2 %0, %0;" : "+r"(x[i])); break;
-        case 2: asm volatile("ex2.approx.ftz.f32 %0, %0;" : "+f"(f[i])); break;
-        case 3: {
-          uint16_t h;
-          asm volatile("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(h) : "r"(x[i]));
-          x[i] = x[i] ^ h;
-          break;
-        }
-        case 4: {
-          uint16_t h;
-          asm volatile("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(h) : "f"(f[i]), "f"(f[(i + 1) & 7]));
-          x[i] = x[i] ^ h;
-          break;
-        }
-        case 5: asm volatile("add.rn.f16x2 %0, %0, %1;" : "+r"(x[i]) : "r"(x[(i + 3) & 7])); break;
-        default: asm volatile("fma.rn.f32 %0, %0, %1, %1;" : "+f"(f[i]) : "f"(f[(i + 1) & 7])); break;
-      }
-    }
-  }
-  const long long c1 = clock64();
-  uint32_t acc = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) acc ^= x[i] ^ __float_as_uint(f[i]);
-  sink[threadIdx.x] = acc;
-  if (threadIdx.x == 0) out[0] = (c1 - c0) / iters;
-}
-}  // namespace
-
-cudaError_t cvt_rate_test(int iters, int variant, long long* out, uint32_t* sink, cudaStream_t s) {
-  switch (variant) {
-    case 0: cvt_rate_kernel<0><<<1, 128, 0, s>>>(iters, out, sink); break;
-    case 1: cvt_rate_kernel<1><<<1, 128, 0, s>>>(iters, out, sink); break;
-    case 2: cvt_rate_kernel<2><<<1, 128, 0, s>>>(iters, out, sink); break;
-    case 3: cvt_rate_kernel<3><<<1, 128, 0, s>>>(iters, out, sink); break;
-    case 4: cvt_rate_kernel<4><<<1, 128, 0, s>>>(iters, out, sink); break;
-    case 5: cvt_rate_kernel<5><<<1, 128, 0, s>>>(iters, out, sink); break;
-    default: cvt_rate_kernel<6><<<1, 128, 0, s>>>(iters, out, sink); break;
-  }
   return cudaGetLastError();
 }
 }  // namespace iob

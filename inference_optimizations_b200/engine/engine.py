@@ -45,6 +45,14 @@ class Engine:
         self.spec_policy = SpecPolicy(ecfg.draft_tokens, ecfg.spec_policy)
         self.pdmux = None
         if getattr(ecfg, "pdmux", False):
+            # the lanes split a GQA prefill by layer ranges on one rank; refuse the combinations that would only fail
+            # at the first prefill (inside split_begin), e.g. in the middle of an HTTP serving loop
+            bad = [why for cond, why in ((not isinstance(self.runner, GQARunner), "a non-GQA model family"),
+                                         (bool(ecfg.spec), "speculative decoding"), (tp > 1, "tp > 1"),
+                                         (max(1, ecfg.ep) > 1, "expert parallelism"))
+                   if cond]
+            if bad:
+                raise ValueError("EngineConfig(pdmux=True) does not support " + ", ".join(bad))
             from .pdmux import PdmuxEngine
             self.pdmux = PdmuxEngine(self, token_budget=ecfg.pdmux_budget)
         self.trace = None
@@ -61,7 +69,7 @@ class Engine:
     def step(self) -> dict:
         """One engine iteration.  Returns rid -> tokens produced this step."""
         if self.pdmux is not None:
-            return self.pdmux.step()
+            return self._pdmux_step()
         t0 = time.perf_counter()
         rec = self.trace.begin() if self.trace else None
         batch = self.sched.schedule()
@@ -118,15 +126,38 @@ class Engine:
             self.trace.end(rec, ev)
         return out
 
+    def _pdmux_step(self) -> dict:
+        """One lanes iteration, recorded like any other step (StepStats, trace): kind "prefill" when a split advanced
+        this iteration and no decode ran, else "decode"."""
+        t0 = time.perf_counter()
+        rec = self.trace.begin() if self.trace else None
+        n_log = len(self.pdmux.log)
+        out = self.pdmux.step()
+        kind = "decode"
+        if len(self.pdmux.log) > n_log:
+            _grp, span, dbs = self.pdmux.log[-1]
+            if span is not None and not dbs:
+                kind = "prefill"
+        self.stats.append(StepStats(kind, sum(len(v) for v in out.values()), time.perf_counter() - t0))
+        if rec is not None:
+            self.trace.phase(rec, "lanes", t0)
+            rec.update(kind=kind, tokens=self.stats[-1].tokens_out, running=len(self.sched.running),
+                       waiting=len(self.sched.waiting), batch=0)
+            self.trace.end(rec, None)
+        return out
+
     def generate_dp(self, prompts: list, params: Optional[SamplingParams] = None, group=None) -> list:
         """Data-parallel serving loop: this rank's prompts; every rank steps until no rank has work (one small
         all-reduce per step), so the expert-parallel exchanges stay in lockstep."""
         import torch.distributed as dist
+        if self.pdmux is not None and self.pdmux.group is None:
+            raise ValueError("generate_dp with pdmux needs the lanes' CPU group (PdmuxEngine(group=...)): the lanes "
+                             "of data-parallel ranks advance in lockstep through it")
         reqs = [self.add_request(p, params) for p in prompts]
         dev = self.device if dist.get_backend(group) == "nccl" else torch.device("cpu")
         flag = torch.zeros(1, dtype=torch.int32, device=dev)
         while True:
-            flag.fill_(1 if self.sched.has_work() else 0)
+            flag.fill_(1 if self.has_work() else 0)
             dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
             if int(flag.item()) == 0:
                 break

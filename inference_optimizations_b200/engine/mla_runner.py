@@ -51,6 +51,7 @@ class MLARunner:
         self.dummy_row = self.max_running
         self.pages: dict[int, RequestPages] = {}
         self.graphs: dict = {}
+        self.graph_launches: dict = {}
         self.event_log = None
         self.prefix_cache = None
         if ecfg.prefix_cache:
@@ -127,7 +128,7 @@ class MLARunner:
         self.model.ep_idle(self.model.moe_layers())
 
     # ------------------------------------------------------------------------------------------ steps
-    def _step(self, segs: list) -> tuple[MLAStep, list]:
+    def _step(self, segs: list, agreed: bool = False) -> tuple[MLAStep, list]:
         ids, pos, slot, limit, rix, logit_rows = [], [], [], [], [], []
         for s in segs:
             rp = self.pages[s.req.rid]
@@ -148,11 +149,12 @@ class MLARunner:
         dev = self.device
         mk = lambda v: torch.tensor(v, dtype=torch.int32).to(dev, non_blocking=True)  # noqa: E731
         st = MLAStep(mk(ids), mk(pos), mk(slot), mk(limit), mk(rix), self.max_seq + 1)
-        self._agree(len(ids))
+        if not agreed:
+            self._agree(len(ids))
         return st, logit_rows
 
-    def _run(self, segs: list) -> list:
-        st, rows = self._step(segs)
+    def _run(self, segs: list, agreed: bool = False) -> list:
+        st, rows = self._step(segs, agreed)
 
         def body():
             x = self.model.forward(st, self.kv)
@@ -259,11 +261,22 @@ class MLARunner:
         if self.spec:
             return self._decode_mtp(reqs)
         bucket = self._bucket(len(reqs))
-        if self._graphable() and bucket in self.ecfg.graph_sizes():
+        agreed = False
+        if self.ep_world > 1:
+            # expert parallelism: every rank takes part in the same exchanges, so the step's token count is agreed
+            # first; a captured graph holds one exchange per MoE layer and replays only when every rank's step fits
+            # one (no rank is prefilling a larger piece); graphs are captured collectively (`warm_graphs`), never
+            # here, since a capture's warm-up runs exchanges
+            self._agree(len(reqs))
+            agreed = True
+            use_graph = self.model.ep_pieces == 1 and bucket in self.graphs and self._graphable()
+        else:
+            use_graph = self._graphable() and bucket in self.ecfg.graph_sizes()
+        if use_graph:
             out = self._decode_graph(reqs, bucket)
         else:
             segs = [Segment(r, r.kv_len, [r.pending], True) for r in reqs]
-            out = self._run(segs)
+            out = self._run(segs, agreed)
         return {r.rid: [int(out[i])] for i, r in enumerate(reqs)}
 
     # ------------------------------------------------------------------------------------------ CUDA graphs
@@ -276,7 +289,7 @@ class MLARunner:
     def _graphable(self) -> bool:
         """Graphs need every FFN on the block-scaled expert kernels (the bf16 reference MoE path groups tokens on
         the host)."""
-        return (self.ecfg.cuda_graphs and self.device.type == "cuda" and not self.spec and self.ep_world == 1
+        return (self.ecfg.cuda_graphs and self.device.type == "cuda" and not self.spec
                 and all(self.model._quantized_ffn(i) for i in range(self.cfg.num_layers)))
 
     def _decode_body(self, st: MLAStep, out: torch.Tensor) -> None:
@@ -295,15 +308,18 @@ class MLARunner:
         step = host.to(dev)
         st = MLAStep(step[0], step[1], step[2], step[3], step[4], self.max_seq + 1)
         out = torch.zeros(bucket, dtype=torch.int32, device=dev)
+        self.model.ep_pieces = 1                # a decode step is one exchange per MoE layer on every rank
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):           # builds the lazily packed experts and workspaces outside capture
             for _ in range(2):
                 self._decode_body(st, out)
         torch.cuda.current_stream(dev).wait_stream(side)
+        from .._ext import count_launches
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        with count_launches() as cnt, torch.cuda.graph(g):
             self._decode_body(st, out)
+        self.graph_launches[bucket] = cnt.n
         self.graphs[bucket] = (g, step, out, host)
         return self.graphs[bucket]
 
@@ -345,9 +361,13 @@ class MLARunner:
             self.detach(r)
 
     def warm_graphs(self, n: int) -> None:
-        """Capture the decode graph of the bucket holding n requests (before any timed step)."""
+        """Capture the decode graph of the bucket holding n requests (before any timed step).  Under expert
+        parallelism this is a collective: every rank calls it at the same point (the capture's warm-up forwards run
+        the exchanges)."""
         if self._graphable():
             self._graph(self._bucket(n))
 
     def count_step_launches(self, bucket: int, kind: Optional[str] = None) -> int:
-        return 0
+        """Kernels of this framework in one decode step: the launches issued through the extension while the
+        bucket's graph was captured (what every replay runs).  0 when no graph is captured."""
+        return self.graph_launches.get(bucket, 0)

@@ -82,6 +82,8 @@ class Lanes:
     def __init__(self, device, n_groups: int = 3, divisions: Optional[list] = None):
         self.device = torch.device(device)
         self.cuda = self.device.type == "cuda"
+        if self.cuda and self.device.index is None:       # a bare "cuda" means the current device, as in torch
+            self.device = torch.device("cuda", torch.cuda.current_device())
         total = torch.cuda.get_device_properties(self.device).multi_processor_count if self.cuda else 0
         self.divisions = divisions or divide_sms(total, n_groups)
         self.sms: dict = {}              # group -> (prefill SMs, decode SMs) as the driver partitioned them
@@ -100,7 +102,7 @@ class Lanes:
                 self.sms[group] = (p_sms, d_sms)
             else:
                 from .._ext import ext
-                d_handle, p_handle, d_got, p_got = ext().sm_lanes(self.device.index or 0, d_sms)
+                d_handle, p_handle, d_got, p_got = ext().sm_lanes(self.device.index, d_sms)
                 self._streams[group] = (torch.cuda.ExternalStream(p_handle, device=self.device),
                                         torch.cuda.ExternalStream(d_handle, device=self.device))
                 self.sms[group] = (p_got, d_got)

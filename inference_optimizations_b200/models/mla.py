@@ -13,6 +13,14 @@ Per layer (pre-norm):
   (`ops/moe.py`).
 Prefill uses the same path: with sparse attention every prompt token is a query with its own top-k over its causal
 prefix (its index key and latent row are written first).  Weights are random-init, seeded per tensor.
+
+On the GPU every projection runs on this framework's tcgen05 GEMMs (`ops/linear.py`), in the checkpoint's weight
+format (FP8 128 x 128 block-scaled for the DeepSeek-V3 geometry, bf16 otherwise): x -> (q_a | kv_a | k_i | w_i) is
+one launch, q_a -> (q_nope | q_pe | q_i) one launch (the rows of W_qb regrouped so each head's q_nope sits at a fixed
+stride), the absorption products q_nope W_UK and o_lat W_UV one head-batched launch each, W_o, the router logits
+(bf16 weights, fp32 out) and the LM head one launch each.  The routed experts and the dense FFNs are the grouped
+block-scaled GEMMs.  Large models never hold a bf16 copy of their weights on the device: each tensor is generated,
+converted and dropped (experts one at a time), so a node-size model fits the memory its packed weights need.
 """
 from __future__ import annotations
 
@@ -29,6 +37,7 @@ from ..ops import basic as B
 from ..ops import formats as F
 from ..ops import indexer as I
 from ..ops import kvcache as K
+from ..ops import linear as L
 from ..ops import mla as M
 from ..ops import moe as MOE
 
@@ -70,6 +79,7 @@ class MLALayerWeights:
     wi_kb: torch.Tensor         # LayerNorm bias [128]
     wi_w: torch.Tensor          # [Hi, H]
     ffn: dict
+    k: Optional[dict] = None    # GEMM kernels of the projections (GPU); None: torch reference path
 
 
 @dataclass
@@ -103,53 +113,145 @@ class MLAKVCache:
 
 
 class MLAModel:
-    def __init__(self, cfg: MLAMoEConfig, device, seed: int = 0, ep_rank: int = 0, ep_world: int = 1):
+    def __init__(self, cfg: MLAMoEConfig, device, seed: int = 0, ep_rank: int = 0, ep_world: int = 1,
+                 keep_master: Optional[bool] = None):
         """ep_world > 1: this rank holds routed experts [ep_rank E / ep_world, (ep_rank + 1) E / ep_world) of every
-        MoE layer (plus the shared expert); attention, router and dense layers are replicated."""
+        MoE layer (plus the shared expert); attention, router and dense layers are replicated.
+        keep_master: keep the bf16 weights next to the kernels' packed copies (default: only for models under 2 G
+        parameters -- test-size models, whose weights `copy_from` moves between devices)."""
         self.cfg, self.device = cfg, torch.device(device)
         h, c = cfg.hidden, cfg
         if c.num_experts % ep_world:
             raise ValueError("experts must divide evenly over the expert-parallel ranks")
         self.ep_rank, self.ep_world = ep_rank, ep_world
-        e_lo, e_hi = ep_rank * c.num_experts // ep_world, (ep_rank + 1) * c.num_experts // ep_world
+        self.e_lo, self.e_hi = ep_rank * c.num_experts // ep_world, (ep_rank + 1) * c.num_experts // ep_world
         self.ep = None                                   # set by attach_ep(): per-layer expert-parallel MoE
-        std = c.init_std
-        ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
-        r = lambda name, shape, s=std: _rand(name, shape, s, self.device, seed)  # noqa: E731
+        self.seed = seed
+        self.keep_master = keep_master if keep_master is not None else c.num_params() < 2e9
+        self.cuda = self.device.type == "cuda"
+        self._bs: dict = {}
+        r = lambda name, shape, s=c.init_std: _rand(name, shape, s, self.device, seed)  # noqa: E731
         self.embed = r("embed", (c.vocab, h))
+        self.final_norm = torch.ones(h, dtype=torch.bfloat16, device=self.device)
         self.lm_head = r("lm_head", (c.vocab, h))
-        self.final_norm = ones(h)
+        self.head = None
+        if self._kernels():
+            self.head = L.Linear(self.lm_head, self._lin_kind())
+            if not self.keep_master:
+                self.lm_head = None
         self.layers = []
         for i in range(c.num_layers):
-            wkv_b = r(f"{i}.wkv_b", (c.num_heads * (c.qk_nope + c.v_head), c.kv_lora)).view(
-                c.num_heads, c.qk_nope + c.v_head, c.kv_lora)
-            if c.is_moe(i):
-                ffn = {"gate": r(f"{i}.gate", (c.num_experts, h)),
-                       "e_bias": torch.zeros(c.num_experts, dtype=torch.float32, device=self.device),
-                       "w_gu": _rand_experts(f"{i}.experts.gu", e_lo, e_hi, (2 * c.expert_ffn, h), std,
-                                             self.device, seed),
-                       "w_down": _rand_experts(f"{i}.experts.down", e_lo, e_hi, (h, c.expert_ffn), std,
-                                               self.device, seed),
-                       "shared_gu": r(f"{i}.shared.gu", (2 * c.expert_ffn * c.num_shared, h)) if c.num_shared else None,
-                       "shared_down": r(f"{i}.shared.down", (h, c.expert_ffn * c.num_shared)) if c.num_shared else None}
-            else:
-                ffn = {"w_gu": r(f"{i}.mlp.gu", (2 * c.dense_ffn, h)), "w_down": r(f"{i}.mlp.down", (h, c.dense_ffn))}
-            self.layers.append(MLALayerWeights(
-                n_in=ones(h), n_post=ones(h),
-                wq_a=r(f"{i}.wq_a", (c.q_lora, h)), q_norm=ones(c.q_lora),
-                wq_b=r(f"{i}.wq_b", (c.num_heads * (c.qk_nope + c.qk_rope), c.q_lora)),
-                wkv_a=r(f"{i}.wkv_a", (c.kv_lora + c.qk_rope, h)), kv_norm=ones(c.kv_lora),
-                w_uk=wkv_b[:, :c.qk_nope, :].contiguous(),
-                w_uv=wkv_b[:, c.qk_nope:, :].transpose(1, 2).contiguous(),
-                wo=r(f"{i}.wo", (h, c.num_heads * c.v_head)),
-                wi_q=r(f"{i}.wi_q", (c.index_heads * c.index_dim, c.q_lora)),
-                wi_k=r(f"{i}.wi_k", (c.index_dim, h)), wi_kn=ones(c.index_dim),
-                wi_kb=torch.zeros(c.index_dim, dtype=torch.bfloat16, device=self.device),
-                wi_w=r(f"{i}.wi_w", (c.index_heads, h)), ffn=ffn))
+            self.layers.append(self._make_layer(str(i), i))
         self.rope = {}
         self.sm_scale = 1.0 / math.sqrt(c.qk_nope + c.qk_rope)
         self.n_target = c.num_layers
         self.draft = False
+
+    # ------------------------------------------------------------------------------------------ weights
+    def _lin_kind(self) -> str:
+        return "fp8" if self.cfg.weight_dtype == "fp8" else "bf16"
+
+    def _kernels(self) -> bool:
+        """Projections on this framework's GEMMs: CUDA, and a weight format those GEMMs take (FP8 or bf16; the NVFP4
+        weight format applies to experts only)."""
+        return self.cuda and self.cfg.weight_dtype in ("fp8", "bf16")
+
+    def _make_layer(self, prefix: str, i: int) -> "MLALayerWeights":
+        """Layer i's weights (named `prefix`.*; the MTP draft layer uses prefix "mtp.<i>"), with the GEMM kernels
+        built and, unless keep_master, the bf16 masters dropped."""
+        c, h = self.cfg, self.cfg.hidden
+        r = lambda name, shape, s=c.init_std: _rand(name, shape, s, self.device, self.seed)  # noqa: E731
+        ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
+        wkv_b = r(f"{prefix}.wkv_b", (c.num_heads * (c.qk_nope + c.v_head), c.kv_lora)).view(
+            c.num_heads, c.qk_nope + c.v_head, c.kv_lora)
+        moe = c.is_moe(i)
+        F = c.expert_ffn
+        if moe:
+            ffn = {"gate": r(f"{prefix}.gate", (c.num_experts, h)),
+                   "e_bias": torch.zeros(c.num_experts, dtype=torch.float32, device=self.device),
+                   "w_gu": None, "w_down": None,
+                   "shared_gu": r(f"{prefix}.shared.gu", (2 * F * c.num_shared, h)) if c.num_shared else None,
+                   "shared_down": r(f"{prefix}.shared.down", (h, F * c.num_shared)) if c.num_shared else None}
+            if self.keep_master or not self._quantized_ffn(i):
+                ffn["w_gu"] = _rand_experts(f"{prefix}.experts.gu", self.e_lo, self.e_hi, (2 * F, h), c.init_std,
+                                            self.device, self.seed)
+                ffn["w_down"] = _rand_experts(f"{prefix}.experts.down", self.e_lo, self.e_hi, (h, F), c.init_std,
+                                              self.device, self.seed)
+        else:
+            ffn = {"w_gu": r(f"{prefix}.mlp.gu", (2 * c.dense_ffn, h)), "w_down": r(f"{prefix}.mlp.down", (h, c.dense_ffn))}
+        w = MLALayerWeights(
+            n_in=ones(h), n_post=ones(h),
+            wq_a=r(f"{prefix}.wq_a", (c.q_lora, h)), q_norm=ones(c.q_lora),
+            wq_b=r(f"{prefix}.wq_b", (c.num_heads * (c.qk_nope + c.qk_rope), c.q_lora)),
+            wkv_a=r(f"{prefix}.wkv_a", (c.kv_lora + c.qk_rope, h)), kv_norm=ones(c.kv_lora),
+            w_uk=wkv_b[:, :c.qk_nope, :].contiguous(),
+            w_uv=wkv_b[:, c.qk_nope:, :].transpose(1, 2).contiguous(),
+            wo=r(f"{prefix}.wo", (h, c.num_heads * c.v_head)),
+            wi_q=r(f"{prefix}.wi_q", (c.index_heads * c.index_dim, c.q_lora)),
+            wi_k=r(f"{prefix}.wi_k", (c.index_dim, h)), wi_kn=ones(c.index_dim),
+            wi_kb=torch.zeros(c.index_dim, dtype=torch.bfloat16, device=self.device),
+            wi_w=r(f"{prefix}.wi_w", (c.index_heads, h)), ffn=ffn)
+        del wkv_b
+        idx = len(self.layers)
+        if self._quantized_ffn(i) and self.cuda:
+            self._bs[idx] = self._build_ffn(prefix, i, ffn)
+        if self._kernels():
+            self._build_kernels(w)
+            if not self.keep_master:
+                for name in ("wq_a", "wq_b", "wkv_a", "wo", "wi_q", "wi_k", "wi_w"):
+                    setattr(w, name, None)
+                if self._quantized_ffn(i):
+                    for k in ("w_gu", "w_down", "shared_gu", "shared_down"):
+                        ffn[k] = None
+        return w
+
+    def _build_ffn(self, prefix: str, i: int, ffn: dict):
+        """Grouped block-scaled FFN of layer i: MoE (this rank's routed experts + the shared one) or the dense FFN as
+        one expert holding every token.  Experts are generated and packed one at a time unless masters are kept."""
+        from ..ops.moe_gemm import BlockScaledExperts
+        c = self.cfg
+        if not c.is_moe(i):
+            F = c.dense_ffn
+            return BlockScaledExperts(ffn["w_gu"][None, :F], ffn["w_gu"][None, F:], ffn["w_down"][None],
+                                      fmt=c.weight_dtype)
+        F = c.expert_ffn
+        sh = None
+        if ffn["shared_gu"] is not None:
+            sh = (ffn["shared_gu"][:F], ffn["shared_gu"][F:], ffn["shared_down"])
+        if ffn["w_gu"] is not None:
+            return BlockScaledExperts(ffn["w_gu"][:, :F], ffn["w_gu"][:, F:], ffn["w_down"], shared=sh,
+                                      fmt=c.expert_dtype)
+
+        def gen(e):
+            gu = _rand(f"{prefix}.experts.gu.{e}", (2 * F, c.hidden), c.init_std, self.device, self.seed)
+            d = _rand(f"{prefix}.experts.down.{e}", (c.hidden, F), c.init_std, self.device, self.seed)
+            return gu[:F], gu[F:], d
+        return BlockScaledExperts.build(self.e_lo, self.e_hi, F, c.hidden, gen, shared=sh, fmt=c.expert_dtype,
+                                        device=self.device)
+
+    def _build_kernels(self, w: "MLALayerWeights") -> None:
+        c = self.cfg
+        kind = self._lin_kind()
+        H, dn, dr = c.num_heads, c.qk_nope, c.qk_rope
+        # W_qb rows regrouped [every head's q_nope | every head's q_pe | indexer q]: q_nope of head h of token t sits
+        # at row t * stride + h of the output viewed as [*, d_n] (the head-batched W_UK product reads it in place)
+        wqb = w.wq_b.view(H, dn + dr, c.q_lora)
+        b_parts = [wqb[:, :dn].reshape(H * dn, c.q_lora), wqb[:, dn:].reshape(H * dr, c.q_lora), w.wi_q]
+        width = sum(t.shape[0] for t in b_parts)
+        unit = dn * 256 // math.gcd(dn, 256)
+        pad = (-width) % unit
+        if pad:
+            b_parts.append(torch.zeros(pad, c.q_lora, dtype=torch.bfloat16, device=self.device))
+        k = {"a": L.Linear.fuse([w.wq_a, w.wkv_a, w.wi_k, w.wi_w], kind),
+             "b": L.Linear.fuse(b_parts, kind), "o": L.Linear(w.wo, kind)}
+        k["b_stride"] = k["b"].Np // dn
+        if dn % 64 == 0 and c.kv_lora % 128 == 0:
+            k["uk"] = L.HeadBatchedLinear(w.w_uk.transpose(1, 2))           # [H, kv_lora, d_n]
+        if c.v_head % 128 == 0 and c.kv_lora % 64 == 0:
+            k["uv"] = L.HeadBatchedLinear(w.w_uv.transpose(1, 2))           # [H, d_v, kv_lora]
+        if w.ffn.get("gate") is not None:
+            k["gate"] = L.Linear(w.ffn["gate"], "bf16")
+        w.k = k
 
     def build_draft(self, seed: int = 0) -> None:
         """Multi-token-prediction draft head (DeepSeek-V3 MTP, depth 1): h'_i = W_eh [RMSNorm_e(Emb(t_{i+1}));
@@ -157,35 +259,12 @@ class MLAModel:
         `num_layers`), a final norm and the shared LM head; it predicts t_{i+2}.  Weights random-init like the
         target's."""
         c, h = self.cfg, self.cfg.hidden
-        r = lambda name, shape, s=c.init_std: _rand(name, shape, s, self.device, seed)  # noqa: E731
-        ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
-        e_lo = self.ep_rank * c.num_experts // self.ep_world
-        e_hi = (self.ep_rank + 1) * c.num_experts // self.ep_world
         i = c.num_layers
         # the draft layer is built exactly like a target layer with index num_layers (MoE, since i >= first_dense)
-        wkv_b = r(f"mtp.{i}.wkv_b", (c.num_heads * (c.qk_nope + c.v_head), c.kv_lora)).view(
-            c.num_heads, c.qk_nope + c.v_head, c.kv_lora)
-        ffn = {"gate": r(f"mtp.{i}.gate", (c.num_experts, h)),
-               "e_bias": torch.zeros(c.num_experts, dtype=torch.float32, device=self.device),
-               "w_gu": _rand_experts(f"mtp.{i}.experts.gu", e_lo, e_hi, (2 * c.expert_ffn, h), c.init_std,
-                                     self.device, seed),
-               "w_down": _rand_experts(f"mtp.{i}.experts.down", e_lo, e_hi, (h, c.expert_ffn), c.init_std,
-                                       self.device, seed),
-               "shared_gu": r(f"mtp.{i}.shared.gu", (2 * c.expert_ffn * c.num_shared, h)) if c.num_shared else None,
-               "shared_down": r(f"mtp.{i}.shared.down", (h, c.expert_ffn * c.num_shared)) if c.num_shared else None}
-        self.layers.append(MLALayerWeights(
-            n_in=ones(h), n_post=ones(h),
-            wq_a=r(f"mtp.{i}.wq_a", (c.q_lora, h)), q_norm=ones(c.q_lora),
-            wq_b=r(f"mtp.{i}.wq_b", (c.num_heads * (c.qk_nope + c.qk_rope), c.q_lora)),
-            wkv_a=r(f"mtp.{i}.wkv_a", (c.kv_lora + c.qk_rope, h)), kv_norm=ones(c.kv_lora),
-            w_uk=wkv_b[:, :c.qk_nope, :].contiguous(),
-            w_uv=wkv_b[:, c.qk_nope:, :].transpose(1, 2).contiguous(),
-            wo=r(f"mtp.{i}.wo", (h, c.num_heads * c.v_head)),
-            wi_q=r(f"mtp.{i}.wi_q", (c.index_heads * c.index_dim, c.q_lora)),
-            wi_k=r(f"mtp.{i}.wi_k", (c.index_dim, h)), wi_kn=ones(c.index_dim),
-            wi_kb=torch.zeros(c.index_dim, dtype=torch.bfloat16, device=self.device),
-            wi_w=r(f"mtp.{i}.wi_w", (c.index_heads, h)), ffn=ffn))
-        self.eh_proj = r("mtp.eh_proj", (h, 2 * h))
+        self.layers.append(self._make_layer(f"mtp.{i}", i))
+        self.eh_proj = _rand("mtp.eh_proj", (h, 2 * h), c.init_std, self.device, self.seed)
+        self.eh = L.Linear(self.eh_proj, self._lin_kind()) if self._kernels() else None
+        ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
         self.enorm, self.hnorm, self.draft_norm = ones(h), ones(h), ones(h)
         self.draft = True
 
@@ -198,20 +277,17 @@ class MLAModel:
         the peer-memory exchange with grouped block-scaled GEMMs (`parallel/ep.py EPMoE`, one shared symmetric
         buffer) on CUDA with FP8 / NVFP4 experts, else the collective reference (`EPMoERef`, e.g. gloo on CPU)."""
         from ..parallel import ep as EP
-        from ..ops.moe_gemm import BlockScaledExperts
         c = self.cfg
         self.ep, self.ep_pieces, self.ep_T_max = {}, 1, T_max
         comm = None
-        cuda = self.device.type == "cuda" and c.expert_dtype in ("fp8", "nvfp4")
+        cuda = self.cuda and c.expert_dtype in ("fp8", "nvfp4")
         for i in self.moe_layers():
-            f, F = self.layers[i].ffn, c.expert_ffn
-            sh = (f["shared_gu"][:F], f["shared_gu"][F:], f["shared_down"]) if f["shared_gu"] is not None else None
+            f = self.layers[i].ffn
             if cuda:
-                ex = BlockScaledExperts(f["w_gu"][:, :F], f["w_gu"][:, F:], f["w_down"], shared=sh,
-                                        fmt=c.expert_dtype)
+                ex = self._block_scaled(i)
                 if comm is None:
-                    comm = EP.EPComm(self.ep_rank, self.ep_world, T_max, c.topk, c.hidden, F, c.expert_dtype,
-                                     c.num_experts // self.ep_world, ex.has_shared, self.device, group)
+                    comm = EP.EPComm(self.ep_rank, self.ep_world, T_max, c.topk, c.hidden, c.expert_ffn,
+                                     c.expert_dtype, c.num_experts // self.ep_world, ex.has_shared, self.device, group)
                 self.ep[i] = EP.EPMoE(self.ep_rank, self.ep_world, c.num_experts, T_max, c.topk, experts=ex,
                                       comm=comm)
                 f["w_gu"] = f["w_down"] = None   # the packed FP8 / NVFP4 copy is the only one kept
@@ -236,14 +312,16 @@ class MLAModel:
         c = self.cfg
         e = B.embed(st.ids, self.embed)
         x0 = torch.cat([B.rmsnorm(e, self.enorm, c.rms_eps), B.rmsnorm(h_prev, self.hnorm, c.rms_eps)], dim=-1)
-        h = Fn.linear(x0, self.eh_proj)
+        h = self.eh(x0).contiguous() if self.eh is not None else Fn.linear(x0, self.eh_proj)
         i = self.n_target
         x = B.rmsnorm(h, self.layers[i].n_in, c.rms_eps)
         return self.layer_forward(i, h, x, st, kv, self.draft_norm)
 
     def copy_from(self, other: "MLAModel") -> None:
-        """Take another instance's weights (any device): device RNG streams differ, so tests that compare devices
-        copy one model's weights into the other."""
+        """Take another instance's weights (any device; both must keep their bf16 masters): device RNG streams
+        differ, so tests that compare devices copy one model's weights into the other.  Kernels are rebuilt."""
+        if not (self.keep_master and other.keep_master):
+            raise ValueError("copy_from needs both models to keep their bf16 master weights")
         dev = self.device
         names = ["embed", "lm_head", "final_norm"]
         if self.draft and other.draft:
@@ -253,10 +331,22 @@ class MLAModel:
         for mine, theirs in zip(self.layers, other.layers):
             for f in vars(theirs):
                 v = getattr(theirs, f)
+                if f == "k":
+                    continue
                 if isinstance(v, dict):
                     setattr(mine, f, {k: (t.to(dev) if t is not None else None) for k, t in v.items()})
                 else:
                     setattr(mine, f, v.to(dev))
+        self._bs = {}
+        if self._kernels():
+            self.head = L.Linear(self.lm_head, self._lin_kind())
+            if self.draft:
+                self.eh = L.Linear(self.eh_proj, self._lin_kind())
+            for w in self.layers:
+                self._build_kernels(w)
+        for i in range(len(self.layers)):
+            if self.cuda and self._quantized_ffn(i):
+                self._bs[i] = self._build_ffn("", i, self.layers[i].ffn)
 
     def rope_table(self, max_pos: int) -> torch.Tensor:
         key = max_pos
@@ -269,24 +359,10 @@ class MLAModel:
         return B.apply_rope_ref(x.float(), pos, cs).to(torch.bfloat16)
 
     def _block_scaled(self, i: int):
-        """Grouped block-scaled experts of layer i (FP8 128x128 or NVFP4, per `expert_dtype` / `weight_dtype`), built
-        from the layer's weights on first use; the dense FFN of the first layers runs as one expert with every token."""
-        from ..ops.moe_gemm import BlockScaledExperts
-        if not hasattr(self, "_bs"):
-            self._bs = {}
+        """Grouped block-scaled experts of layer i (FP8 128x128 or NVFP4, per `expert_dtype` / `weight_dtype`); the
+        dense FFN of the first layers runs as one expert with every token."""
         if i not in self._bs:
-            c, f = self.cfg, self.layers[i].ffn
-            if c.is_moe(i):
-                F = c.expert_ffn
-                sh = None
-                if f["shared_gu"] is not None:
-                    sh = (f["shared_gu"][:F], f["shared_gu"][F:], f["shared_down"])
-                self._bs[i] = BlockScaledExperts(f["w_gu"][:, :F], f["w_gu"][:, F:], f["w_down"], shared=sh,
-                                                 fmt=c.expert_dtype)
-            else:
-                F = c.dense_ffn
-                self._bs[i] = BlockScaledExperts(f["w_gu"][None, :F], f["w_gu"][None, F:], f["w_down"][None],
-                                                 fmt=c.weight_dtype)
+            self._bs[i] = self._build_ffn("", i, self.layers[i].ffn)
         return self._bs[i]
 
     def _quantized_ffn(self, i: int) -> bool:
@@ -297,10 +373,16 @@ class MLAModel:
             return c.expert_dtype in ("fp8", "nvfp4") and c.num_shared <= 1
         return c.weight_dtype in ("fp8", "nvfp4")
 
+    def _router_logits(self, i: int, x: torch.Tensor) -> torch.Tensor:
+        k = self.layers[i].k
+        if k is not None and "gate" in k:
+            return k["gate"](x, out_f32=True)
+        return Fn.linear(x.float(), self.layers[i].ffn["gate"].float())
+
     def _ffn(self, i: int, x: torch.Tensor) -> torch.Tensor:
         c, f = self.cfg, self.layers[i].ffn
         if self.ep is not None and c.is_moe(i):
-            logits = Fn.linear(x.float(), f["gate"].float())
+            logits = self._router_logits(i, x)
             ids, w = MOE.route(logits, f["e_bias"], c.topk, c.n_group, c.topk_group, c.routed_scale, c.router)
             t, per = x.shape[0], self.ep_T_max
             outs = []
@@ -314,13 +396,51 @@ class MLAModel:
             if not c.is_moe(i):
                 ids = torch.zeros(t, 1, dtype=torch.int32, device=x.device)
                 return ex.forward(x, ids, torch.ones(t, 1, device=x.device))
-            logits = Fn.linear(x.float(), f["gate"].float())
+            logits = self._router_logits(i, x)
             ids, w = MOE.route(logits, f["e_bias"], c.topk, c.n_group, c.topk_group, c.routed_scale, c.router)
             return ex.forward(x, ids, w)
         if not c.is_moe(i):
             return MOE.swiglu(x, f["w_gu"], f["w_down"])
         return MOE.moe_forward(x, f["gate"], f["e_bias"], f["w_gu"], f["w_down"], f["shared_gu"], f["shared_down"],
                                c.topk, c.n_group, c.topk_group, c.routed_scale, c.router)
+
+    def _attn_inputs(self, w: MLALayerWeights, x: torch.Tensor, t: int):
+        """-> (q_a pre-norm, kv_a, k_i pre-norm, w_i, qb(q_a normed) callable): the projections of x."""
+        c = self.cfg
+        if w.k is not None:
+            qa_, kva, ik_, iw_ = w.k["a"].split(w.k["a"](x))
+        else:
+            qa_, kva, ik_, iw_ = (Fn.linear(x, w.wq_a), Fn.linear(x, w.wkv_a), Fn.linear(x, w.wi_k),
+                                  Fn.linear(x, w.wi_w))
+        return qa_, kva, ik_, iw_
+
+    def _q_proj(self, w: MLALayerWeights, qa: torch.Tensor, t: int):
+        """q_a (normed) -> (q_lat [T, H, kv_lora] = q_nope W_UK, q_pe [T, H, d_r] pre-RoPE, q_i [T, Hi, 128])."""
+        c = self.cfg
+        H, dn, dr = c.num_heads, c.qk_nope, c.qk_rope
+        if w.k is not None:
+            yb = w.k["b"].lin(qa)                                      # full padded width: the head rows are in place
+            q_nope = yb[:, :H * dn].view(t, H, dn)
+            q_pe = yb[:, H * dn:H * (dn + dr)].view(t, H, dr)
+            iq = yb[:, H * (dn + dr):H * (dn + dr) + c.index_heads * c.index_dim].view(t, c.index_heads, c.index_dim)
+            if "uk" in w.k:
+                q_lat = w.k["uk"](yb, t, row_stride=w.k["b_stride"])
+            else:
+                wuk = w.w_uk if w.w_uk.is_cuda else w.w_uk.to(qa.device)
+                q_lat = torch.einsum("thn,hnk->thk", q_nope.float(), wuk.float()).to(torch.bfloat16)
+            return q_lat, q_pe, iq
+        q = Fn.linear(qa, w.wq_b).view(t, H, dn + dr)
+        q_lat = torch.einsum("thn,hnk->thk", q[..., :dn].float(), w.w_uk.float()).to(torch.bfloat16)
+        iq = Fn.linear(qa, w.wi_q).view(t, c.index_heads, c.index_dim)
+        return q_lat, q[..., dn:], iq
+
+    def _o_proj(self, w: MLALayerWeights, o_lat: torch.Tensor, t: int) -> torch.Tensor:
+        c = self.cfg
+        if w.k is not None and "uv" in w.k:
+            o = w.k["uv"](o_lat, t).view(t, c.num_heads * c.v_head)
+        else:
+            o = torch.einsum("thk,hkv->thv", o_lat.float(), w.w_uv.float()).to(torch.bfloat16).reshape(t, -1)
+        return w.k["o"](o) if w.k is not None else Fn.linear(o, w.wo)
 
     def layer_forward(self, i: int, h: torch.Tensor, x: torch.Tensor, st: MLAStep, kv: MLAKVCache,
                       next_norm: torch.Tensor) -> torch.Tensor:
@@ -329,30 +449,27 @@ class MLAModel:
         t = x.shape[0]
         eps = c.rms_eps
         cs = self.rope_table(max(st.max_ctx, 1) + 64)
-        qa = B.rmsnorm(Fn.linear(x, w.wq_a), w.q_norm, eps)
-        q = Fn.linear(qa, w.wq_b).view(t, c.num_heads, c.qk_nope + c.qk_rope)
-        q_nope, q_pe = q[..., :c.qk_nope], self._rope(q[..., c.qk_nope:], st.pos, cs)
-        kva = Fn.linear(x, w.wkv_a)
+        qa_, kva, ik_, iw_ = self._attn_inputs(w, x, t)
+        qa = B.rmsnorm(qa_.contiguous(), w.q_norm, eps)
+        q_lat, q_pe, iq = self._q_proj(w, qa, t)
+        q_pe = self._rope(q_pe, st.pos, cs)
         lat = B.rmsnorm(kva[:, :c.kv_lora].contiguous(), w.kv_norm, eps)
         k_pe = self._rope(kva[:, None, c.kv_lora:], st.pos, cs)[:, 0]
         K.mla_write(lat, k_pe.contiguous(), st.slot, kv.latent[i])
         # DSA indexer
-        iq = Fn.linear(qa, w.wi_q).view(t, c.index_heads, c.index_dim)
         iq = torch.cat([self._rope(iq[..., :c.qk_rope], st.pos, cs), iq[..., c.qk_rope:]], dim=-1)
-        ik = Fn.layer_norm(Fn.linear(x, w.wi_k).float(), (c.index_dim,), w.wi_kn.float(), w.wi_kb.float(), eps)
+        ik = Fn.layer_norm(ik_.float(), (c.index_dim,), w.wi_kn.float(), w.wi_kb.float(), eps)
         ik = torch.cat([self._rope(ik[:, None, :c.qk_rope], st.pos, cs)[:, 0], ik[:, c.qk_rope:].to(torch.bfloat16)],
                        dim=-1)
         K.index_key_write(ik.contiguous(), st.slot, kv.index[i])
-        iw = Fn.linear(x, w.wi_w).float() * (c.index_heads ** -0.5 * c.index_dim ** -0.5)
+        iw = iw_.float() * (c.index_heads ** -0.5 * c.index_dim ** -0.5)
         q8, w_eff = I.indexer_q_quant(iq, iw)
         sel = I.indexer_select(q8, w_eff, kv.index[i], kv.table.dev, st.limit, c.index_topk, st.max_ctx,
                                req_idx=st.req_idx, ws=kv.idx_ws.get((t, st.max_ctx)))
         # absorbed sparse attention over the latent pool
-        q_lat = torch.einsum("thn,hnk->thk", q_nope.float(), w.w_uk.float()).to(torch.bfloat16)
         qf = torch.cat([q_lat, q_pe], dim=-1).contiguous()
         o_lat = M.mla_decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt, ws=kv.mla_ws.get((t, c.index_topk)))
-        o = torch.einsum("thk,hkv->thv", o_lat.float(), w.w_uv.float()).to(torch.bfloat16).reshape(t, -1)
-        x2 = B.rmsnorm(Fn.linear(o, w.wo), w.n_post, eps, residual=h)        # h += attn; x2 = norm_post(h)
+        x2 = B.rmsnorm(self._o_proj(w, o_lat, t), w.n_post, eps, residual=h)   # h += attn; x2 = norm_post(h)
         f = self._ffn(i, x2)
         return B.rmsnorm(f, next_norm, eps, residual=h)                      # h += ffn; next norm
 
@@ -371,4 +488,6 @@ class MLAModel:
         return x, h
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
+        if self.head is not None:
+            return self.head(x)
         return Fn.linear(x, self.lm_head)

@@ -85,13 +85,20 @@ class DenseLinear:
                              torch.arange(t, dtype=torch.int32, device=dev))
         return self._rows[t]
 
-    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, out_f32: bool = False) -> torch.Tensor:
+        """y = x W^T, bf16 out; out_f32: fp32 out (the accumulator as is, no rounding: router logits)."""
         t = x.shape[0]
         if out is None:
-            out = torch.empty(t, self.N, dtype=torch.bfloat16, device=x.device)
+            out = torch.empty(t, self.N, dtype=torch.float32 if out_f32 else torch.bfloat16, device=x.device)
         if t == 0:
             return out
         xb = x.contiguous().view(torch.uint8)
+        if out_f32:
+            off, pairs = self._index(t, x.device)
+            MG.gemm(self.wpack, xb, xb, off, pairs, out, self.status, n_tiles=self.N // (TILE * self.g),
+                    kc=self.K // 64, g=self.g, nt=MG.pick_nt(t), mode=MODE_F32_SPLIT, src_div=1,
+                    num_ctas=self.num_ctas, kind=2, ksplit=1, split_rows=t)
+            return out
         _splitk_gemm(self, xb, xb, out, t, self.K // 64, 2)
         return out
 
@@ -209,3 +216,83 @@ class ShardedLMHead:
         logits = self.lin(x)[:, :self.rows].float()
         val, idx = logits.max(-1)
         return val, idx + self.v0
+
+
+class Linear:
+    """A projection on this framework's GEMMs with any output width: W [N, K] (bf16 master) becomes an FP8 block-scaled
+    (`fp8`) or bf16 (`bf16`) weight-streaming GEMM with the rows zero-padded to the kernel's 128-row tile; the result
+    is the [T, N] view of the padded output.  `fuse` stacks several weights that read the same input into one launch
+    (`split` returns the per-weight column views)."""
+
+    def __init__(self, w: torch.Tensor, kind: str = "fp8"):
+        N, K = w.shape
+        self.N, self.K, self.kind = N, K, kind
+        pad = (-N) % (256 if N > 128 else 128)
+        wp = torch.cat([w, torch.zeros(pad, K, dtype=w.dtype, device=w.device)]) if pad else w
+        self.lin = Fp8Linear(wp) if kind == "fp8" else DenseLinear(wp.to(torch.bfloat16))
+        if kind == "fp8":
+            self.lin.q = self.lin.eb = None          # the packed copy is the only one the GEMM reads
+        self.Np = wp.shape[0]
+
+    @classmethod
+    def fuse(cls, ws: list, kind: str = "fp8") -> "Linear":
+        lin = cls(torch.cat(ws), kind)
+        lin.widths = [w.shape[0] for w in ws]
+        return lin
+
+    def __call__(self, x: torch.Tensor, out_f32: bool = False) -> torch.Tensor:
+        if out_f32:
+            assert self.kind == "bf16", "fp32 output is the bf16 GEMM's mode"
+            y = self.lin(x, out_f32=True)
+        else:
+            y = self.lin(x)
+        return y[:, :self.N] if self.Np != self.N else y
+
+    def split(self, y: torch.Tensor) -> list:
+        out, c = [], 0
+        for w in self.widths:
+            out.append(y[:, c:c + w])
+            c += w
+        return out
+
+
+class HeadBatchedLinear:
+    """Per-head projections y[t, h] = x[t, h] W[h]^T (W bf16 [H, N, K]) as ONE grouped bf16 GEMM launch: head h is
+    "expert" h and every token is routed to every head, so the weights stream once at full tensor-core width (the
+    MLA absorption products q_nope W_UK and o_lat W_UV).  Input rows are read in place: head h of token t is row
+    t * row_stride + h of x viewed as [rows, K] (row_stride = H for a contiguous [T, H, K] input, larger when the
+    heads sit inside a wider projection output).  Output: contiguous [T, H, N] bf16."""
+
+    def __init__(self, w: torch.Tensor):
+        H, N, K = w.shape
+        assert N % TILE == 0 and K % 64 == 0 and H <= 1023
+        self.H, self.N, self.K = H, N, K
+        self.g = 2 if N % 256 == 0 else 1
+        self.wpack = torch.cat([pack_bf16(w[h].to(torch.bfloat16), self.g) for h in range(H)])
+        dev = w.device
+        self.num_ctas = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 1
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._rows: dict = {}
+
+    def _index(self, t: int, dev):
+        """off [H + 1] = h t; pairs[h t + j] = j H + h (output row of token j, head h)."""
+        if t not in self._rows:
+            h = torch.arange(self.H, dtype=torch.int32, device=dev)
+            j = torch.arange(t, dtype=torch.int32, device=dev)
+            self._rows[t] = ((torch.arange(self.H + 1, dtype=torch.int32, device=dev) * t).contiguous(),
+                             (j[None, :] * self.H + h[:, None]).reshape(-1).contiguous())
+        return self._rows[t]
+
+    def __call__(self, x: torch.Tensor, t: int, row_stride: int = 0) -> torch.Tensor:
+        """x: any tensor whose memory holds token t's head h at element (t * row_stride + h) * K (row_stride 0: H)."""
+        rs = row_stride or self.H
+        out = torch.empty(t, self.H, self.N, dtype=torch.bfloat16, device=x.device)
+        if t == 0:
+            return out
+        rows = x.reshape(-1).view(torch.uint8).view(-1, self.K * 2)
+        off, pairs = self._index(t, x.device)
+        MG.gemm(self.wpack, rows, rows, off, pairs, out.view(t * self.H, self.N), self.status,
+                n_tiles=self.N // (TILE * self.g), kc=self.K // 64, g=self.g, nt=MG.pick_nt(t), mode=0, src_div=1,
+                num_ctas=self.num_ctas, kind=2, src_group=self.H if rs != self.H else 0,
+                src_group_stride=rs if rs != self.H else 0)
+        return out

@@ -180,11 +180,11 @@ def gemm(wpack, x, x_scale, off, pairs, out, status, *, n_tiles: int, kc: int, g
          src_div: int, src_limit: int = 1 << 30, src_shared_base: int = 0, pair_w=None, out_scale=None, out_mul: float = 1.0,
          num_ctas: int = 148, kind: int = 0, expert_mul=None, out_peers=None, out_offset: int = 0, out_div: int = 1,
          out_rank: int = 0, out_shared_base: int = 0, pairs_total: int = 0, ksplit: int = 1,
-         split_rows: int = 0) -> None:
+         split_rows: int = 0, src_group: int = 0, src_group_stride: int = 0) -> None:
     """One grouped block-scaled GEMM launch (argument meanings: `MoeGemmArgs` in csrc/kernels.h)."""
     ext().moe_gemm(wpack, x, x_scale, off, pairs, pair_w, out, out_scale, status, n_tiles, kc, g, nt, mode, src_div,
                    src_limit, src_shared_base, out_mul, num_ctas, kind, expert_mul, out_peers, out_offset, out_div, out_rank,
-                   out_shared_base, pairs_total, ksplit, split_rows)
+                   out_shared_base, pairs_total, ksplit, split_rows, src_group, src_group_stride)
 
 
 _TACTICS = None
@@ -264,6 +264,52 @@ class BlockScaledExperts:
         self.num_ctas = num_ctas or (torch.cuda.get_device_properties(dev).multi_processor_count
                                      if dev.type == "cuda" else 1)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    @classmethod
+    def build(cls, e_lo: int, e_hi: int, F: int, H: int, gen, shared: tuple | None = None, fmt: str = "fp8",
+              device=None) -> "BlockScaledExperts":
+        """Experts e_lo .. e_hi - 1 from gen(e) -> (w_gate [F, H], w_up [F, H], w_down [H, F]), quantized and packed
+        one expert at a time straight into the launch layout: no stacked bf16 or fp32 copy of the expert set ever
+        exists, so a node-size expert set is built in the memory its packed form needs.  Same packed bytes as the
+        stacked constructor (quantization is per expert in both).  No dequantization oracle is kept."""
+        self = cls.__new__(cls)
+        self.fmt, self.kind = fmt, {"fp8": 0, "nvfp4": 1}[fmt]
+        self.has_shared = shared is not None
+        self.E, self.F, self.H = e_hi - e_lo, F, H
+        n = self.E + int(self.has_shared)
+        dev = device or (shared[0].device if shared is not None else gen(e_lo)[0].device)
+        self.q = None
+        if self.kind == 0:
+            self.g2 = 2 if H % 256 == 0 else 1
+            self.w1 = torch.empty(n, F // TILE, H // TILE, 2 * (16384 + 512), dtype=torch.uint8, device=dev)
+            self.w2 = torch.empty(n, H // (TILE * self.g2), F // TILE, self.g2 * (16384 + 512), dtype=torch.uint8,
+                                  device=dev)
+            self.mul1 = self.mul2 = None
+        else:
+            self.g2 = 1
+            self.w1 = torch.empty(n, F // TILE, H // (2 * TILE), 2 * (16384 + 4 * 512), dtype=torch.uint8, device=dev)
+            self.w2 = torch.empty(n, H // TILE, F // (2 * TILE), 16384 + 4 * 512, dtype=torch.uint8, device=dev)
+            self.mul1 = torch.empty(n, dtype=torch.float32, device=dev)
+            self.mul2 = torch.empty(n, dtype=torch.float32, device=dev)
+        for j in range(n):
+            g, u, d = shared if j == self.E else gen(e_lo + j)
+            if self.kind == 0:
+                qg, eg = quant_blocks(g[None])
+                qu, eu = quant_blocks(u[None])
+                self.w1[j] = pack_weights([qg, qu], [eg, eu])[0]
+                del qg, qu
+                qd, ed = quant_blocks(d[None])
+                self.w2[j] = pack_weights_paired(qd, ed)[0][0]
+            else:
+                qgu, sgu, ggu = quant_nvfp4_weights(torch.cat([g, u])[None])
+                self.w1[j] = pack_weights_nvfp4([qgu[:, :F], qgu[:, F:]], [sgu[:, :F], sgu[:, F:]])[0]
+                qd, sd, gd = quant_nvfp4_weights(d[None])
+                self.w2[j] = pack_weights_nvfp4([qd], [sd])[0]
+                self.mul1[j], self.mul2[j] = ggu[0], gd[0]
+            del g, u, d
+        self.num_ctas = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 1
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        return self
 
     @classmethod
     def random_packed(cls, E: int, F: int, H: int, fmt: str = "fp8", shared: bool = True, device="cuda",

@@ -1,23 +1,36 @@
-"""INT4 (QAT, group-32 symmetric, compressed-tensors "pack-quantized") expert weights -> NVFP4 or MXFP4, with the
-per-block scale chosen by squared-error search so each FP4 block is the closest one to the INT4 reference
-(`moe-gemm/int4-to-nvfp4-converter/k27_fp4_convert.py:1-30`).
+"""Checkpoint converter: INT4 QAT expert weights (compressed-tensors "pack-quantized", symmetric, one scale per 32
+inputs) -> NVFP4 (ModelOpt layout) or MXFP4, the weight formats this framework's block-scaled GEMMs serve
+(the reference ships the same conversion for its W4A4 MoE path, `moe-gemm/int4-to-nvfp4-converter/`).
 
-Layouts written:
-  nvfp4  ModelOpt: `weight` uint8 [out, in/2] (E2M1 pairs, low nibble first), `weight_scale` E4M3 [out, in/16],
-         `weight_scale_2` fp32 (global), `input_scale` fp32 when supplied; dequant = e2m1 * scale * global
-  mxfp4  `weight` uint8 [out, in/2], `weight_scale` uint8 E8M0 [out, in/32]; dequant = e2m1 * 2^(e - 127)
-E2M1 rounding is to nearest with ties to even (the hardware conversion).  The NVFP4 candidates are amax/6 times
-1 .. 7/6 in 8 steps, each rounded to what the E4M3 scale can store; MXFP4 candidates are the power of two at or
-above amax/6 and its two neighbours.
+Format contracts kept as the loaders expect them:
+  INT4 in   `weight_packed` int32 [out, in/8] (nibble i of a word = input column 8k + i, stored +8), `weight_scale`
+            [out, in/32], `weight_shape` [2]
+  nvfp4     `weight` uint8 [out, in/2] (E2M1 pairs, element 2i in the low nibble), `weight_scale` E4M3 [out, in/16],
+            `weight_scale_2` fp32 (per tensor: amax / (6 * 448)), `input_scale` fp32 when supplied;
+            value = e2m1 * weight_scale * weight_scale_2
+  mxfp4     `weight` uint8 [out, in/2], `weight_scale` uint8 E8M0 [out, in/32]; value = e2m1 * 2^(e - 127)
+
+Scale choice.  A block's nominal scale is amax / 6 (its largest value lands on E2M1's 6).  A storable scale is one the
+format can hold: an E4M3 code times the tensor's global scale (NVFP4) or a power of two (MXFP4).  The converter takes
+EVERY storable scale inside a window around the nominal one -- [amax / 8, amax / 4]: below amax / 6 the largest values
+clip to 6 sigma, above it the grid coarsens -- and keeps the one whose block reconstruction has the least squared
+error (ties: the smaller scale).  For NVFP4 the window spans about eight E4M3 codes (three mantissa bits per octave),
+enumerated as a contiguous range of code bytes since positive E4M3 codes are ordered like their values.  Powers of two
+are sparser, so MXFP4 searches [amax / 12, amax / 3]: the smallest power of two that does not clip and the one below.
+All candidates of a row chunk are evaluated in one broadcast.  With `search=False` the nominal scale rounded to the
+nearest storable value is used.  E2M1 rounding is to nearest, ties to even, as the
+hardware conversion does.
+
+Report (`conversion_report.json`): per tensor the signal-to-quantization-noise ratio in weight space and in output
+space (against a fixed +-1 probe batch), the largest absolute error and the fraction of weights reproduced exactly.
 
     python -m inference_optimizations_b200.tooling.fp4_convert convert --src DIR --dst DIR --fmt nvfp4
-
-Per-tensor errors against the INT4 reference (weight space and output space) go to fp4_convert_stats.json.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 from typing import Optional
 
@@ -26,25 +39,28 @@ import torch
 from ..ops import formats as F
 
 GROUP_INT4 = 32
+E2M1_MAX = 6.0
+E4M3_MAX = 448.0
+WINDOW = (1.0 / 8.0, 1.0 / 4.0)         # NVFP4 candidate scales: [amax * lo, amax * hi]
+WINDOW_MX = (1.0 / 12.0, 1.0 / 3.0)     # MXFP4: a factor-of-four window (two powers of two)
 _LEVELS = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+ROW_CHUNK = 256                          # rows evaluated per broadcast (bounds the candidate temporaries)
 
 
+# ------------------------------------------------------------------------------------------------ INT4 input format
 def unpack_int4(packed: torch.Tensor, cols: int) -> torch.Tensor:
-    """int32 [out, ceil(in/8)] (nibble i of a word = column 8k + i, stored with a +8 offset) -> int8 [out, in]."""
-    parts = [((packed >> (4 * i)) & 0xF) for i in range(8)]
-    u = torch.stack(parts, dim=-1).reshape(packed.shape[0], -1)[:, :cols]
-    return (u - 8).to(torch.int8)
+    """int32 [out, ceil(in/8)] -> int8 [out, in] (nibble i of word k is column 8k + i, stored with a +8 offset)."""
+    shifts = torch.arange(0, 32, 4, dtype=torch.int32, device=packed.device)
+    nib = (packed[..., None] >> shifts) & 0xF
+    return (nib.reshape(packed.shape[0], -1)[:, :cols] - 8).to(torch.int8)
 
 
 def pack_int4(codes: torch.Tensor) -> torch.Tensor:
-    """Inverse of unpack_int4 (for tests and synthetic checkpoints)."""
+    """int8 [out, in] in [-8, 7] -> int32 [out, ceil(in/8)] (inverse of unpack_int4; synthetic checkpoints)."""
     out, cols = codes.shape
-    pad = (-cols) % 8
-    u = torch.nn.functional.pad(codes.int() + 8, (0, pad)).reshape(out, -1, 8)
-    w = torch.zeros(out, u.shape[1], dtype=torch.int64)
-    for i in range(8):
-        w |= (u[..., i].long() & 0xF) << (4 * i)
-    return w.to(torch.int64).where(w < 2 ** 31, w - 2 ** 32).to(torch.int32)
+    u = torch.nn.functional.pad(codes.long() + 8, (0, (-cols) % 8)).reshape(out, -1, 8)
+    word = (u << torch.arange(0, 32, 4, dtype=torch.int64)).sum(-1)
+    return torch.where(word >= 2 ** 31, word - 2 ** 32, word).to(torch.int32)
 
 
 def dequant_int4(packed: torch.Tensor, scale: torch.Tensor, cols: int) -> torch.Tensor:
@@ -52,40 +68,79 @@ def dequant_int4(packed: torch.Tensor, scale: torch.Tensor, cols: int) -> torch.
     return q * scale.float().repeat_interleave(GROUP_INT4, dim=1)[:, :cols]
 
 
-def _round_e2m1(y: torch.Tensor) -> torch.Tensor:
-    """Signed values -> nearest E2M1 value (ties to even, saturating at 6)."""
-    mag = F._e2m1_mag_even(y.abs())
-    return torch.where(y < 0, -_LEVELS.to(y.device)[mag], _LEVELS.to(y.device)[mag])
+# ------------------------------------------------------------------------------------------------ E2M1 helpers
+def _e2m1_round(y: torch.Tensor) -> torch.Tensor:
+    """Nearest E2M1 value of y (ties to even, saturating at +-6)."""
+    lv = _LEVELS.to(y.device)[F._e2m1_mag_even(y.abs())]
+    return torch.copysign(lv, y)
 
 
-def _codes(y: torch.Tensor) -> torch.Tensor:
+def _e2m1_codes(y: torch.Tensor) -> torch.Tensor:
     mag = F._e2m1_mag_even(y.abs())
     return mag | (((y < 0) & (mag > 0)).int() << 3)
 
 
-def _pick(blocks: torch.Tensor, cands: torch.Tensor) -> torch.Tensor:
-    """blocks [.., nb, B], candidate scales [.., nb, C] (> 0) -> the scale with the least squared error."""
-    errs = []
-    for c in range(cands.shape[-1]):
-        s = cands[..., c:c + 1]
-        errs.append(((_round_e2m1(blocks / s) * s - blocks) ** 2).sum(-1))
-    best = torch.stack(errs, -1).argmin(-1, keepdim=True)
-    return cands.gather(-1, best).squeeze(-1)
+def _best_scale(blocks: torch.Tensor, cands: torch.Tensor, valid: torch.Tensor) -> torch.Tensor:
+    """blocks [R, nb, B], candidate scales [R, nb, C] (> 0) with a validity mask -> chosen scale [R, nb]: the least
+    squared reconstruction error, the first (smallest) candidate on ties."""
+    x = blocks[..., None, :]                                             # [R, nb, 1, B]
+    s = cands[..., None]                                                 # [R, nb, C, 1]
+    err = ((_e2m1_round(x / s) * s - x) ** 2).sum(-1)                    # [R, nb, C]
+    err = torch.where(valid, err, torch.full_like(err, float("inf")))
+    return cands.gather(-1, err.argmin(-1, keepdim=True)).squeeze(-1)
+
+
+def _chunked(w: torch.Tensor, fn) -> list:
+    return [fn(w[r:r + ROW_CHUNK]) for r in range(0, w.shape[0], ROW_CHUNK)]
+
+
+# ------------------------------------------------------------------------------------------------ NVFP4
+_E4M3_POS = torch.arange(0, 0x7F, dtype=torch.uint8)                    # every finite non-negative E4M3 code byte
+
+
+def _e4m3_values(device) -> torch.Tensor:
+    return _E4M3_POS.view(torch.float8_e4m3fn).float().to(device)
 
 
 def quant_nvfp4(w: torch.Tensor, search: bool = True, global_scale: Optional[float] = None):
     """fp32 [out, in] -> (weight uint8 [out, in/2], weight_scale E4M3 [out, in/16], weight_scale_2 fp32 [])."""
     out, cols = w.shape
-    blocks = w.float().reshape(out, cols // 16, 16)
-    amax = blocks.abs().amax(-1)
-    g = max(float(global_scale) if global_scale else float(w.abs().max()) / (6.0 * 448.0), 1e-12)
-    steps = torch.linspace(1.0, 7.0 / 6.0, 8, device=w.device) if search else torch.ones(1, device=w.device)
-    cands = (amax / 6.0)[..., None] * steps
-    cands = (cands / g).clamp(max=448.0).to(torch.float8_e4m3fn).float() * g       # storable scales only
-    cands = torch.where(cands > 0, cands, torch.full_like(cands, g))
-    s = _pick(blocks, cands) if search else cands[..., 0]
-    codes = _codes(blocks / s[..., None]).reshape(out, cols)
-    return F.pack_nibbles(codes), (s / g).to(torch.float8_e4m3fn), torch.tensor(g, dtype=torch.float32)
+    w = w.float()
+    g = float(global_scale) if global_scale else float(w.abs().max()) / (E2M1_MAX * E4M3_MAX)
+    g = max(g, 1e-12)
+    table = _e4m3_values(w.device)                                      # ascending with the code byte
+
+    def one(rows: torch.Tensor):
+        blocks = rows.reshape(rows.shape[0], cols // 16, 16)
+        amax = blocks.abs().amax(-1)
+        if search:
+            lo = torch.searchsorted(table, (amax * WINDOW[0] / g).contiguous())            # first code >= lo
+            hi = torch.searchsorted(table, (amax * WINDOW[1] / g).contiguous(), right=True)  # past last code <= hi
+            span = 10                                                   # a factor-of-two window holds <= 9 codes
+            idx = lo[..., None] + torch.arange(span, device=w.device)
+            valid = (idx < hi[..., None]) & (idx >= 1) & (idx < table.numel())
+            # empty windows (all-zero blocks, or windows past the E4M3 range) fall back to the nearest code
+            near = _nearest_code(table, amax / E2M1_MAX / g)
+            none = ~valid.any(-1)
+            idx = torch.where(none[..., None], near[..., None].expand_as(idx), idx)
+            valid = valid | (none[..., None] & (torch.arange(span, device=w.device) == 0))
+            cand = table[idx.clamp(0, table.numel() - 1)] * g
+            cand = torch.where(cand > 0, cand, torch.full_like(cand, g))
+            sc = _best_scale(blocks, cand, valid)
+        else:
+            sc = table[_nearest_code(table, amax / E2M1_MAX / g)] * g
+            sc = torch.where(sc > 0, sc, torch.full_like(sc, g))
+        codes = _e2m1_codes(blocks / sc[..., None]).reshape(rows.shape[0], cols)
+        return F.pack_nibbles(codes), (sc / g).to(torch.float8_e4m3fn)
+    parts = _chunked(w, one)
+    return (torch.cat([p[0] for p in parts]), torch.cat([p[1] for p in parts]),
+            torch.tensor(g, dtype=torch.float32))
+
+
+def _nearest_code(table: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    i = torch.searchsorted(table, v.contiguous()).clamp(1, table.numel() - 1)
+    below = (v - table[i - 1]).abs() <= (table[i] - v).abs()
+    return torch.where(below, i - 1, i)
 
 
 def dequant_nvfp4(weight: torch.Tensor, weight_scale: torch.Tensor, weight_scale_2: torch.Tensor) -> torch.Tensor:
@@ -93,16 +148,29 @@ def dequant_nvfp4(weight: torch.Tensor, weight_scale: torch.Tensor, weight_scale
     return vals * (weight_scale.float() * float(weight_scale_2)).repeat_interleave(16, dim=1)
 
 
+# ------------------------------------------------------------------------------------------------ MXFP4
 def quant_mxfp4(w: torch.Tensor, search: bool = True):
     """fp32 [out, in] -> (weight uint8 [out, in/2], weight_scale E8M0 uint8 [out, in/32])."""
     out, cols = w.shape
-    blocks = w.float().reshape(out, cols // 32, 32)
-    amax = blocks.abs().amax(-1).clamp(min=1e-30)
-    p = torch.exp2(torch.ceil(torch.log2(amax / 6.0)))
-    s = _pick(blocks, torch.stack([p / 2, p, p * 2], -1)) if search else p
-    codes = _codes(blocks / s[..., None]).reshape(out, cols)
-    e = (torch.log2(s).round() + 127).clamp(0, 254).to(torch.uint8)
-    return F.pack_nibbles(codes), e
+    w = w.float()
+
+    def one(rows: torch.Tensor):
+        blocks = rows.reshape(rows.shape[0], cols // 32, 32)
+        amax = blocks.abs().amax(-1).clamp(min=2.0 ** -126)
+        if search:
+            e_lo = torch.ceil(torch.log2(amax * WINDOW_MX[0]))          # powers of two inside the window
+            e_hi = torch.floor(torch.log2(amax * WINDOW_MX[1]))
+            exps = e_lo[..., None] + torch.arange(3, device=w.device)
+            valid = exps <= e_hi[..., None]
+            sc = _best_scale(blocks, torch.exp2(exps), valid)
+        else:
+            sc = torch.exp2(torch.ceil(torch.log2(amax / E2M1_MAX)))  # the smallest power of two without clipping
+        e8 = (torch.log2(sc).round() + 127).clamp(0, 254)
+        sc = torch.exp2(e8 - 127)
+        codes = _e2m1_codes(blocks / sc[..., None]).reshape(rows.shape[0], cols)
+        return F.pack_nibbles(codes), e8.to(torch.uint8)
+    parts = _chunked(w, one)
+    return torch.cat([p[0] for p in parts]), torch.cat([p[1] for p in parts])
 
 
 def dequant_mxfp4(weight: torch.Tensor, weight_scale: torch.Tensor) -> torch.Tensor:
@@ -110,81 +178,90 @@ def dequant_mxfp4(weight: torch.Tensor, weight_scale: torch.Tensor) -> torch.Ten
     return vals * torch.exp2(weight_scale.float() - 127.0).repeat_interleave(32, dim=1)
 
 
-def compare(ref: torch.Tensor, cand: torch.Tensor, n_act: int = 256, seed: int = 0) -> dict:
-    """Relative RMS error in weight space and in output space (Gaussian activations), max abs, changed fraction."""
-    d = cand - ref
-    x = torch.randn(n_act, ref.shape[1], generator=torch.Generator().manual_seed(seed)).to(ref.device)
-    return {"rel_rms_w": float(d.norm() / ref.norm()), "rel_rms_out": float((x @ d.T).norm() / (x @ ref.T).norm()),
-            "max_abs": float(d.abs().max()), "changed_frac": float((d != 0).float().mean())}
+# ------------------------------------------------------------------------------------------------ report
+def _sqnr_db(signal: torch.Tensor, noise: torch.Tensor) -> float:
+    n = float((noise.double() ** 2).sum())
+    return float("inf") if n == 0 else 10.0 * math.log10(float((signal.double() ** 2).sum()) / n)
 
 
-def _int4_groups(names) -> dict:
-    """{prefix: {packed, scale, shape}} for compressed-tensors pack-quantized weights."""
-    out = {}
+def report(ref: torch.Tensor, approx: torch.Tensor, probes: int = 128) -> dict:
+    """Quality of a converted tensor against its INT4 reference: SQNR in weight space and in output space (a fixed
+    batch of +-1 probe activations), largest absolute error, fraction of weights reproduced exactly."""
+    d = approx - ref
+    g = torch.Generator().manual_seed(1234)
+    x = (torch.randint(0, 2, (probes, ref.shape[1]), generator=g).float() * 2 - 1).to(ref.device)
+    return {"sqnr_db": round(_sqnr_db(ref, d), 3), "out_sqnr_db": round(_sqnr_db(x @ ref.T, x @ d.T), 3),
+            "max_abs_err": float(d.abs().max()), "exact_frac": float((d == 0).float().mean())}
+
+
+# ------------------------------------------------------------------------------------------------ checkpoints
+def _int4_tensors(names) -> dict:
+    """prefix -> {"packed", "scale", "shape"} tensor names of every complete INT4 weight in a shard."""
+    found: dict = {}
     for n in names:
-        for suf, key in ((".weight_packed", "packed"), (".weight_scale", "scale"), (".weight_shape", "shape")):
-            if n.endswith(suf):
-                out.setdefault(n[: -len(suf)], {})[key] = n
-    return {k: v for k, v in out.items() if len(v) == 3}
+        for suffix, role in ((".weight_packed", "packed"), (".weight_scale", "scale"), (".weight_shape", "shape")):
+            if n.endswith(suffix):
+                found.setdefault(n[: -len(suffix)], {})[role] = n
+    return {p: r for p, r in found.items() if len(r) == 3}
+
+
+def convert_tensor(ref: torch.Tensor, fmt: str, search: bool = True) -> tuple[dict, torch.Tensor]:
+    """One fp32 weight -> ({suffix: tensor} in the output format, its dequantized value)."""
+    if fmt == "nvfp4":
+        q, s8, g2 = quant_nvfp4(ref, search)
+        return {".weight": q, ".weight_scale": s8, ".weight_scale_2": g2.reshape(1)}, dequant_nvfp4(q, s8, g2)
+    if fmt == "mxfp4":
+        q, e8 = quant_mxfp4(ref, search)
+        return {".weight": q, ".weight_scale": e8}, dequant_mxfp4(q, e8)
+    raise ValueError(f"unknown format {fmt!r}")
 
 
 def convert_file(src: str, dst: str, fmt: str, search: bool = True, input_scales: Optional[dict] = None) -> dict:
-    """Convert every INT4 group of one safetensors file; other tensors pass through unchanged."""
+    """Convert every INT4 weight of one safetensors shard; every other tensor is copied as is.  -> report per weight."""
     from ..models.loader import SafeTensors, save
     st = SafeTensors(src)
-    names = st.keys()
-    groups = _int4_groups(names)
-    used = {n for g in groups.values() for n in g.values()}
-    tensors, stats = {}, {}
-    for n in names:
-        if n not in used:
-            tensors[n] = st.get(n)
-    for prefix, g in groups.items():
-        shape = [int(v) for v in st.get(g["shape"]).tolist()]
-        ref = dequant_int4(st.get(g["packed"]), st.get(g["scale"]), shape[1])
-        if fmt == "nvfp4":
-            q, s8, g2 = quant_nvfp4(ref, search)
-            tensors[prefix + ".weight"] = q
-            tensors[prefix + ".weight_scale"] = s8
-            tensors[prefix + ".weight_scale_2"] = g2.reshape(1)
-            if input_scales and prefix in input_scales:
-                tensors[prefix + ".input_scale"] = input_scales[prefix].reshape(1).float()
-            deq = dequant_nvfp4(q, s8, g2)
-        else:
-            q, e8 = quant_mxfp4(ref, search)
-            tensors[prefix + ".weight"] = q
-            tensors[prefix + ".weight_scale"] = e8
-            deq = dequant_mxfp4(q, e8)
-        stats[prefix] = compare(ref, deq)
-    save(tensors, dst)
-    return stats
+    names = list(st.keys())
+    groups = _int4_tensors(names)
+    consumed = {n for roles in groups.values() for n in roles.values()}
+    out = {n: st.get(n) for n in names if n not in consumed}
+    rep = {}
+    for prefix, roles in sorted(groups.items()):
+        rows, cols = (int(v) for v in st.get(roles["shape"]).tolist())
+        ref = dequant_int4(st.get(roles["packed"]), st.get(roles["scale"]), cols)[:rows]
+        tensors, approx = convert_tensor(ref, fmt, search)
+        for suffix, t in tensors.items():
+            out[prefix + suffix] = t
+        if fmt == "nvfp4" and input_scales and prefix in input_scales:
+            out[prefix + ".input_scale"] = input_scales[prefix].reshape(1).float()
+        rep[prefix] = report(ref, approx)
+    save(out, dst)
+    return rep
 
 
 def convert(src_dir: str, dst_dir: str, fmt: str, search: bool = True) -> dict:
-    """Stream a checkpoint directory shard by shard (one shard in memory at a time)."""
+    """Convert a checkpoint directory one shard at a time (one shard in memory) and write conversion_report.json."""
     os.makedirs(dst_dir, exist_ok=True)
-    stats = {}
-    for f in sorted(os.listdir(src_dir)):
-        if f.endswith(".safetensors"):
-            stats.update(convert_file(os.path.join(src_dir, f), os.path.join(dst_dir, f), fmt, search))
-    with open(os.path.join(dst_dir, "fp4_convert_stats.json"), "w") as fh:
-        json.dump({"fmt": fmt, "search": search, "tensors": stats}, fh, indent=1)
-    return stats
+    rep: dict = {}
+    for name in sorted(f for f in os.listdir(src_dir) if f.endswith(".safetensors")):
+        rep.update(convert_file(os.path.join(src_dir, name), os.path.join(dst_dir, name), fmt, search))
+    worst = min((r["sqnr_db"] for r in rep.values()), default=float("inf"))
+    with open(os.path.join(dst_dir, "conversion_report.json"), "w") as fh:
+        json.dump({"format": fmt, "scale_search": search, "worst_sqnr_db": worst, "tensors": rep}, fh, indent=1)
+    return rep
 
 
 def main() -> None:
-    ap = argparse.ArgumentParser()
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     sub = ap.add_subparsers(dest="cmd", required=True)
     c = sub.add_parser("convert")
     c.add_argument("--src", required=True)
     c.add_argument("--dst", required=True)
     c.add_argument("--fmt", choices=["nvfp4", "mxfp4"], default="nvfp4")
-    c.add_argument("--no-search", action="store_true")
+    c.add_argument("--no-search", action="store_true", help="nominal scale (amax / 6, nearest storable) only")
     a = ap.parse_args()
-    if a.cmd == "convert":
-        s = convert(a.src, a.dst, a.fmt, not a.no_search)
-        worst = max((v["rel_rms_w"] for v in s.values()), default=0.0)
-        print(json.dumps({"tensors": len(s), "worst_rel_rms_w": worst}))
+    rep = convert(a.src, a.dst, a.fmt, not a.no_search)
+    print(json.dumps({"tensors": len(rep), "worst_sqnr_db": min((r["sqnr_db"] for r in rep.values()),
+                                                                default=None)}))
 
 
 if __name__ == "__main__":

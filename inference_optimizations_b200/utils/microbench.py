@@ -42,7 +42,7 @@ def _time(fn, iters: int = 10) -> float:
 
 
 def gqa_decode_case(b: int, hk: int, hq: int, d: int, ctx: int, fmt_name: str, n_q: int, window: int,
-                    launches: int = 0, splits_override: str = "") -> dict:
+                    launches: int = 0, splits_override: str = "", trace: bool = False) -> dict:
     from ..engine.synthetic import fill_pool_random
     from ..ops import attention as A
     from ..ops import kvcache as K
@@ -60,8 +60,21 @@ def gqa_decode_case(b: int, hk: int, hq: int, d: int, ctx: int, fmt_name: str, n
         splits = tuple(int(v) for v in splits_override.split(","))
     ws = A.DecodeWorkspace.allocate(b, hk, splits[0], d, device=dev)
 
-    def fn():
-        A.gqa_decode(q, pool, pt, kv_len, n_q, hk, fmt, 1 / math.sqrt(d), window, splits=splits, ws=ws)
+    def fn(t=None):
+        A.gqa_decode(q, pool, pt, kv_len, n_q, hk, fmt, 1 / math.sqrt(d), window, splits=splits, ws=ws, trace=t)
+    if trace:
+        # clock64 timeline of CTA 0: event e of tile j at [e * 512 + j] (TraceEv order in attn_gqa_decode.cu);
+        # medians over tiles 10 .. n-1 of the per-tile phase lengths
+        fn()
+        tr = torch.zeros(16 * 512, dtype=torch.int64, device=dev)
+        fn(tr)
+        torch.cuda.synchronize()
+        ev = tr.view(16, 512).cpu()
+        n = int((ev[7] > 0).sum())
+        med = lambda v: int(v[10:n].median()) if n > 11 else None  # noqa: E731
+        return {"kernel": "gqa_decode_trace", "tiles": n, "cycles_per_tile": med(ev[7, 1:n + 1] - ev[7, :n]),
+                "k_dequant": med(ev[1] - ev[0]), "v_dequant": med(ev[3] - ev[2]), "qk_issue": med(ev[5] - ev[4]),
+                "pv_issue": med(ev[7] - ev[6]), "splits": list(splits)}
     if launches:
         for _ in range(launches):
             fn()
@@ -437,6 +450,7 @@ def main() -> None:
     p.add_argument("--window", type=int, default=0)
     p.add_argument("--topk", type=int, default=2048)
     p.add_argument("--launches", type=int, default=0)
+    p.add_argument("--trace", action="store_true", help="gqa_decode: per-tile clock64 timeline of CTA 0")
     p.add_argument("--experts", type=int, default=32)
     p.add_argument("--total-experts", type=int, default=256)
     p.add_argument("--hidden", type=int, default=7168)
@@ -444,7 +458,7 @@ def main() -> None:
     p.add_argument("--wfmt", default="fp8", choices=["fp8", "nvfp4"])
     a = p.parse_args()
     if a.kernel == "gqa_decode":
-        r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches, a.splits)
+        r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches, a.splits, a.trace)
     elif a.kernel == "gqa_extend":
         r = gqa_extend_case(a.chunk, a.ctx, a.hk, a.hq, a.d, a.fmt, a.window, a.launches)
     elif a.kernel == "indexer":

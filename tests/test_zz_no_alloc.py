@@ -30,6 +30,8 @@ def _lib():
     # num_splits | sm_scale, k_scale, v_scale | exact | stream
     fn.argtypes = ([ctypes.c_void_p] * 3 + [ctypes.c_int] + [ctypes.c_void_p] * 3 + [ctypes.c_int] * 9
                    + [ctypes.c_float] * 3 + [ctypes.c_int, ctypes.c_void_p])
+    lib.iob_gqa_decode_noalloc_status.restype = ctypes.c_int
+    lib.iob_gqa_decode_noalloc_status.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
     lib.iob_gqa_decode_noalloc_strerror.restype = ctypes.c_char_p
     lib.iob_gqa_decode_noalloc_strerror.argtypes = [ctypes.c_int]
     return lib
@@ -69,6 +71,9 @@ def test_noalloc_entry_point_matches_allocating_one(cuda, exact):
                                         kv_len.data_ptr(), out.data_ptr(), len(lens), n_q, hq, hk, d, 0, fmt,
                                         splits[1], splits[0], sm, 1.0, 1.0, int(exact), stream)
         assert rc == 0, lib.iob_gqa_decode_noalloc_strerror(rc)
+        status = ctypes.c_int(-7)
+        rc = lib.iob_gqa_decode_noalloc_status(ctypes.byref(status), stream)
+        assert rc == 0 and status.value == 0, (rc, status.value)
         torch.cuda.synchronize()
         assert torch.isfinite(out.float()).all()
         assert (out.float() - ref.float()).abs().max().item() < 2e-2
