@@ -459,13 +459,15 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
 
 void splitk_reduce(const at::Tensor& part, int64_t ksplit, at::Tensor out) {
   req(part, at::kFloat, "part");
-  req(out, at::kBFloat16, "out");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kFloat, "splitk_reduce: bf16 or fp32 out");
+  TORCH_CHECK(out.is_cuda(), "splitk_reduce: CUDA tensors");
   TORCH_CHECK(part.is_contiguous() && out.is_contiguous() && out.dim() == 2 &&
                   part.numel() >= ksplit * out.size(0) * out.size(1),
               "splitk_reduce shapes");
   const at::cuda::CUDAGuard g(out.device());
   CHECK_CUDA_OK(iob::splitk_reduce(part.data_ptr<float>(), static_cast<int>(ksplit), static_cast<int>(out.size(0)),
-                                   static_cast<int>(out.size(1)), out.data_ptr(), stream()));
+                                   static_cast<int>(out.size(1)), out.data_ptr(), out.scalar_type() == at::kFloat,
+                                   stream()));
 }
 
 void moe_align(const at::Tensor& ids, int64_t e0, int64_t E, int64_t extra, at::Tensor off, at::Tensor pairs) {

@@ -203,8 +203,9 @@ struct MoeGemmArgs {
 cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s);
 cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, int extra, int* off, int* pairs,
                       cudaStream_t s);
-// out bf16 [rows][N] = sum over splits of part fp32 [ksplit][rows][N] (fixed split order: deterministic).
-cudaError_t splitk_reduce(const float* part, int ksplit, int rows, int N, void* out, cudaStream_t s);
+// out [rows][N] (bf16, or fp32 with out_f32) = sum over splits of part fp32 [ksplit][rows][N] (fixed split order:
+// deterministic).
+cudaError_t splitk_reduce(const float* part, int ksplit, int rows, int N, void* out, bool out_f32, cudaStream_t s);
 cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_base, const float* w, void* y,
                         cudaStream_t s);
 

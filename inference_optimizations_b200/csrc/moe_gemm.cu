@@ -52,14 +52,17 @@ struct Cfg {
   static constexpr uint32_t kRaw = kWBlk + kX + kSfw * kSfAtom;
   static constexpr uint32_t kStage = (kRaw + 1023) / 1024 * 1024;
   static constexpr uint32_t kCtrl = 5120;                         // barriers, work prefix, reduction scratch
-  static constexpr int kStagesFit = (kSmemBudget - kCtrl - 1024) / kStage;
+  // pipeline stages first (keeping at least 4 KB back), then what is left (up to 16 KB) stages the epilogue's rows
+  static constexpr int kStagesFit = (kSmemBudget - kCtrl - 1024 - 4096) / kStage;
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr uint32_t kLeft = kSmemBudget - kCtrl - 1024 - kStages * kStage;
+  static constexpr uint32_t kEpi = kLeft >= 16384 ? 16384 : (kLeft / 1024) * 1024;
   static constexpr int kAccCols = G * NT;
   static constexpr int kSfCols = KIND == 2 ? 0 : 4 * kSfw * (G + 1);
   static constexpr int kAccBufs = (2 * kAccCols + kSfCols <= 512) ? 2 : 1;
   static constexpr int kUsed = kAccBufs * kAccCols + kSfCols;
   static constexpr uint32_t kTmemCols = kUsed <= 32 ? 32 : kUsed <= 64 ? 64 : kUsed <= 128 ? 128 : kUsed <= 256 ? 256 : 512;
-  static constexpr uint32_t kSmem = kCtrl + 1024 + kStages * kStage;
+  static constexpr uint32_t kSmem = kCtrl + 1024 + kEpi + kStages * kStage;
   static_assert(kStages >= 2, "pipeline too shallow");
   static_assert(kUsed <= 512, "TMEM overflow");
   static_assert(kSmem <= kSmemBudget, "smem overflow");
@@ -199,6 +202,63 @@ __device__ __forceinline__ uint32_t ue8m0_for(float amax) {
   return static_cast<uint32_t>(e + 127);
 }
 
+// Plain-output epilogue of one TMEM chunk (KCH tokens x G 128-column tiles, this thread = column n_local): the four
+// epilogue warps stage the chunk as token rows in shared memory (conflict-free: a warp writes 32 consecutive
+// columns of one token), then each warp stores whole rows, one 16-byte store per lane, to the row's destination
+// (bf16 out, fp32 split-K partial, or the owning peer's combine buffer).  One pair-id load per row instead of one
+// per element, and 512-byte row segments instead of 64-byte scattered ones.  ESZ: bytes per output element.
+template <class C, int G, int ESZ, int KCH>
+__device__ __forceinline__ void store_rows(const MoeGemmArgs& a, uint8_t* epi, const uint32_t (&v0)[KCH],
+                                           const uint32_t (&v1)[KCH], float emul, int c0, int rows, int row0, int nt,
+                                           int ks, int q, int lane, int n_local) {
+  constexpr int kRowB = G * 128 * ESZ;
+  constexpr int kFit = static_cast<int>(C::kEpi) / kRowB;
+  static_assert(kFit >= 4, "epilogue staging too small");
+  constexpr int kPer = kFit >= 32 ? 32 : kFit >= 16 ? 16 : kFit >= 8 ? 8 : 4;
+  constexpr int kP = kPer > KCH ? KCH : kPer;
+#pragma unroll
+  for (int t0 = 0; t0 < KCH; t0 += kP) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+      for (int t = 0; t < kP; ++t) {
+        float v = __uint_as_float(g == 0 ? v0[t0 + t] : v1[t0 + t]) * emul;
+        if (a.mode == kMoeOutBf16Weighted) {
+          const int r = c0 + t0 + t;
+          v *= r < rows ? a.pair_w[a.pairs[row0 + r]] : 0.f;
+        }
+        if constexpr (ESZ == 4)
+          reinterpret_cast<float*>(epi)[t * (G * 128) + g * 128 + n_local] = v;
+        else
+          reinterpret_cast<__nv_bfloat16*>(epi)[t * (G * 128) + g * 128 + n_local] = __float2bfloat16(v);
+      }
+    }
+    named_bar(2, 128);
+    for (int t = q; t < kP; t += 4) {
+      const int r = c0 + t0 + t;
+      if (r >= rows) continue;
+      const int p = a.pairs[row0 + r];
+      char* dst;
+      if constexpr (ESZ == 4) {
+        dst = reinterpret_cast<char*>(a.out) +
+              ((static_cast<size_t>(ks) * a.split_rows + p) * a.out_stride + static_cast<size_t>(nt) * G * 128) * 4;
+      } else if (a.out_peers) {                 // expert parallelism: the row goes to its token's owner
+        const bool sh = p >= a.pairs_total;
+        const int rr = sh ? a.out_rank : p / a.out_div;
+        const long long row = sh ? a.out_shared_base + (p - a.pairs_total) : p % a.out_div;
+        dst = reinterpret_cast<char*>(a.out_peers[rr]) + a.out_offset +
+              (row * a.out_stride + static_cast<long long>(nt) * G * 128) * 2;
+      } else {
+        dst = reinterpret_cast<char*>(a.out) + (static_cast<size_t>(p) * a.out_stride + static_cast<size_t>(nt) * G * 128) * 2;
+      }
+      const uint4* src = reinterpret_cast<const uint4*>(epi + t * kRowB);
+#pragma unroll
+      for (int c = lane; c < kRowB / 16; c += 32) reinterpret_cast<uint4*>(dst)[c] = src[c];
+    }
+    named_bar(2, 128);
+  }
+}
+
 template <int NT, int G, int KIND>
 __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmArgs a) {
   using C = Cfg<NT, G, KIND>;
@@ -208,7 +268,8 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
   MgCtrl& ctl = *reinterpret_cast<MgCtrl*>(base);
   int* prefix = reinterpret_cast<int*>(base + 256);                // [E + 1], E <= kMaxGemmExperts
   float* red = reinterpret_cast<float*>(base + 4608);              // [4 warps][32 tokens]
-  uint8_t* stages = base + C::kCtrl;
+  uint8_t* epi = base + C::kCtrl;                                  // epilogue row staging (kEpi bytes)
+  uint8_t* stages = base + C::kCtrl + C::kEpi;
   const int warp = warp_id(), lane = lane_id();
   volatile int* abort = &ctl.abort;
 
@@ -498,35 +559,10 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
                     sb;
             }
           }
+        } else if (a.mode == kMoeOutF32Split) {      // split-K partial, summed by splitk_reduce
+          store_rows<C, G, 4, kChunk>(a, epi, v0, v1, emul, c0, rows, row0, nt, ks, q, lane, n_local);
         } else {
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-#pragma unroll
-            for (int t = 0; t < kChunk; ++t) {
-              const int r = c0 + t;
-              if (r < rows) {
-                const int p = a.pairs[row0 + r];
-                float v = __uint_as_float(g == 0 ? v0[t] : v1[t]) * emul;
-                if (a.mode == kMoeOutBf16Weighted) v *= a.pair_w[p];
-                if (a.mode == kMoeOutF32Split) {        // split-K partial, summed by splitk_reduce
-                  reinterpret_cast<float*>(a.out)[(static_cast<size_t>(ks) * a.split_rows + p) * a.out_stride +
-                                                  (nt * G + g) * 128 + n_local] = v;
-                  continue;
-                }
-                __nv_bfloat16* dst;
-                if (a.out_peers) {                      // expert parallelism: the row goes to its token's owner
-                  const bool sh = p >= a.pairs_total;
-                  const int rr = sh ? a.out_rank : p / a.out_div;
-                  const long long row = sh ? a.out_shared_base + (p - a.pairs_total) : p % a.out_div;
-                  dst = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<char*>(a.out_peers[rr]) + a.out_offset) +
-                        row * a.out_stride;
-                } else {
-                  dst = reinterpret_cast<__nv_bfloat16*>(a.out) + static_cast<size_t>(p) * a.out_stride;
-                }
-                dst[(nt * G + g) * 128 + n_local] = __float2bfloat16(v);
-              }
-            }
-          }
+          store_rows<C, G, 2, kChunk>(a, epi, v0, v1, emul, c0, rows, row0, nt, ks, q, lane, n_local);
         }
       }
       tc_fence_before();
@@ -718,8 +754,10 @@ __global__ void act_quant_kernel(const __nv_bfloat16* gu, int F, int fmt, uint8_
   }, row, F, fmt, q, sc);
 }
 
-// One CTA per output row: the K splits' fp32 partials summed in split order, rounded once to bf16.
-__global__ void splitk_reduce_kernel(const float* part, int ksplit, int rows, int N, __nv_bfloat16* out) {
+// One CTA per output row: the K splits' fp32 partials summed in split order, then rounded once to bf16 (OutT = bf16)
+// or kept in fp32 (OutT = float: router logits).
+template <class OutT>
+__global__ void splitk_reduce_kernel(const float* part, int ksplit, int rows, int N, OutT* out) {
   const int r = blockIdx.x;
   for (int c = threadIdx.x; c < N / 4; c += blockDim.x) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -727,11 +765,15 @@ __global__ void splitk_reduce_kernel(const float* part, int ksplit, int rows, in
       const float4 v = reinterpret_cast<const float4*>(part + (static_cast<size_t>(k) * rows + r) * N)[c];
       acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
     }
-    const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
-    uint2 w;
-    w.x = *reinterpret_cast<const uint32_t*>(&lo);
-    w.y = *reinterpret_cast<const uint32_t*>(&hi);
-    reinterpret_cast<uint2*>(out + static_cast<size_t>(r) * N)[c] = w;
+    if constexpr (sizeof(OutT) == 4) {
+      reinterpret_cast<float4*>(out + static_cast<size_t>(r) * N)[c] = acc;
+    } else {
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+      uint2 w;
+      w.x = *reinterpret_cast<const uint32_t*>(&lo);
+      w.y = *reinterpret_cast<const uint32_t*>(&hi);
+      reinterpret_cast<uint2*>(out + static_cast<size_t>(r) * N)[c] = w;
+    }
   }
 }
 
@@ -742,6 +784,12 @@ cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
       (a.mode == kMoeOutF32Split && a.out_peers))
     return cudaErrorInvalidValue;
   if (a.src_group < 0 || (a.src_group > 0 && a.src_group_stride < a.src_group)) return cudaErrorInvalidValue;
+  if (a.mode != kMoeOutSwigluQuant) {         // plain epilogues store 16-byte row segments
+    const int esz = a.mode == kMoeOutF32Split ? 4 : 2;
+    if ((static_cast<long long>(a.out_stride) * esz) % 16 || a.out_offset % 16 ||
+        (!a.out_peers && reinterpret_cast<uintptr_t>(a.out) % 16))
+      return cudaErrorInvalidValue;
+  }
   if (a.E <= 0 || a.E > kMaxGemmExperts || a.KC <= 0 || a.n_tiles <= 0 || a.num_ctas <= 0 || a.src_div <= 0 ||
       (a.x_stride % 16) || (reinterpret_cast<uintptr_t>(a.x) % 16) || (reinterpret_cast<uintptr_t>(a.wpack) % 16) ||
       (a.mode == kMoeOutSwigluQuant && (a.G != 2 || a.kind == 2)) || a.kind < 0 || a.kind > 2)
@@ -758,10 +806,13 @@ cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
   return cudaErrorInvalidValue;
 }
 
-cudaError_t splitk_reduce(const float* part, int ksplit, int rows, int N, void* out, cudaStream_t s) {
+cudaError_t splitk_reduce(const float* part, int ksplit, int rows, int N, void* out, bool out_f32, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
   if (N % 4 || ksplit < 1) return cudaErrorInvalidValue;
-  splitk_reduce_kernel<<<rows, 256, 0, s>>>(part, ksplit, rows, N, static_cast<__nv_bfloat16*>(out));
+  if (out_f32)
+    splitk_reduce_kernel<float><<<rows, 256, 0, s>>>(part, ksplit, rows, N, static_cast<float*>(out));
+  else
+    splitk_reduce_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>(part, ksplit, rows, N, static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError();
 }
 

@@ -44,15 +44,18 @@ def split_k(n_tiles: int, tokens: int, nt: int, kc: int, ctas: int, min_chunks: 
 
 
 def _splitk_gemm(lin, x, xs, out, t: int, kc: int, kind: int) -> None:
-    """Run lin's GEMM with split-K when it helps: fp32 partials, then one deterministic reduction to bf16."""
+    """Run lin's GEMM with split-K when it helps: fp32 partials, then one deterministic reduction (to out's dtype:
+    bf16, or fp32 for an fp32 `out`)."""
     from .._ext import ext
-    nt = MG.pick_nt(t)
+    nt = FORCE["nt"] or MG.pick_nt(t)
     n_tiles = lin.N // (TILE * lin.g)
-    ks = split_k(n_tiles, t, nt, kc, lin.num_ctas)
+    ks = FORCE["ks"] or split_k(n_tiles, t, nt, kc, lin.num_ctas)
     off, pairs = lin._index(t, x.device)
+    f32 = out.dtype == torch.float32
     if ks == 1:
-        MG.gemm(lin.wpack, x, xs, off, pairs, out, lin.status, n_tiles=n_tiles, kc=kc, g=lin.g, nt=nt, mode=0,
-                src_div=1, num_ctas=lin.num_ctas, kind=kind)
+        MG.gemm(lin.wpack, x, xs, off, pairs, out, lin.status, n_tiles=n_tiles, kc=kc, g=lin.g, nt=nt,
+                mode=MODE_F32_SPLIT if f32 else 0, src_div=1, num_ctas=lin.num_ctas, kind=kind,
+                split_rows=t if f32 else 0)
         return
     key = (t, ks)
     if key not in lin._parts:
@@ -64,6 +67,8 @@ def _splitk_gemm(lin, x, xs, out, t: int, kc: int, kind: int) -> None:
 
 
 MODE_F32_SPLIT = 3
+# tactic overrides for sweeps (utils/microbench.py proj_gemms --nt / --ks); None = the heuristics
+FORCE: dict = {"nt": None, "ks": None}
 
 
 class DenseLinear:
@@ -93,12 +98,6 @@ class DenseLinear:
         if t == 0:
             return out
         xb = x.contiguous().view(torch.uint8)
-        if out_f32:
-            off, pairs = self._index(t, x.device)
-            MG.gemm(self.wpack, xb, xb, off, pairs, out, self.status, n_tiles=self.N // (TILE * self.g),
-                    kc=self.K // 64, g=self.g, nt=MG.pick_nt(t), mode=MODE_F32_SPLIT, src_div=1,
-                    num_ctas=self.num_ctas, kind=2, ksplit=1, split_rows=t)
-            return out
         _splitk_gemm(self, xb, xb, out, t, self.K // 64, 2)
         return out
 

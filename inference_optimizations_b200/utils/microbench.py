@@ -138,13 +138,15 @@ def gqa_extend_case(chunk: int, ctx: int, hk: int, hq: int, d: int, fmt_name: st
 
 
 def _time_flushed(fn, iters: int = 10) -> float:
-    """Mean device time of fn over `iters` launches, L2 flushed (a 256 MB write) before each, flush not timed."""
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    """Mean device time of fn over `iters` launches, L2 flushed before each by READING a 512 MB buffer (a write flush
+    would leave ~126 MB of dirty lines whose write-back the timed kernel would pay for), flush not timed."""
+    flush = torch.ones(128 << 20, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
     for _ in range(3):
         fn()
     total = 0.0
     for _ in range(iters):
-        flush.fill_(1)
+        torch.sum(flush, dim=0, out=sink)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()
@@ -433,6 +435,105 @@ def dense_linear_case(t: int, launches: int = 0) -> dict:
     return out
 
 
+def proj_gemms_case(tokens: list, only: str = "") -> list:
+    """The MLA projection GEMMs of the DSA-MoE layer on the tcgen05 kernels (`ops/linear.py`), each timed alone with
+    CUDA events (L2 flushed before each launch): FP8 fused a/b projections, W_o and the LM head, the head-batched bf16
+    absorption products, the fp32 router logits.  Reported with the weight-stream bandwidth and the tensor rate."""
+    from ..ops import linear as L
+    dev = torch.device("cuda:0")
+    H, ql, nh = 7168, 1536, 128
+    w = lambda n, k: (torch.randn(n, k, device=dev) * 0.02).to(torch.bfloat16)  # noqa: E731
+    mods = {"a_fp8": (L.Linear(w(2304, H), "fp8"), H, 2304, 1),
+            "b_fp8": (L.Linear(w(32768, ql), "fp8"), ql, 32768, 1),
+            "o_fp8": (L.Linear(w(H, nh * 128), "fp8"), nh * 128, H, 1),
+            "head_fp8": (L.Linear(w(129280, H), "fp8"), H, 129280, 1),
+            "router_bf16_f32out": (L.Linear(w(256, H), "bf16"), H, 256, 2),
+            "uk_bf16": (L.HeadBatchedLinear((torch.randn(nh, 512, 128, device=dev) * 0.05).to(torch.bfloat16)),
+                        128, 512, 2),
+            "uv_bf16": (L.HeadBatchedLinear((torch.randn(nh, 128, 512, device=dev) * 0.05).to(torch.bfloat16)),
+                        512, 128, 2)}
+    out = []
+    for t in tokens:
+        for name, (m, K, N, wb) in mods.items():
+            if (name == "head_fp8" and t > 512) or (only and name not in only.split(",")):
+                continue
+            if name.startswith("uk"):
+                x = torch.randn(t, 256 * 128, device=dev).to(torch.bfloat16)
+                fn = lambda m=m, x=x: m(x, t, row_stride=256)  # noqa: E731
+                flops, wbytes = 2 * t * nh * K * N, nh * K * N * wb
+            elif name.startswith("uv"):
+                x = torch.randn(t, nh, 512, device=dev).to(torch.bfloat16)
+                fn = lambda m=m, x=x: m(x, t)  # noqa: E731
+                flops, wbytes = 2 * t * nh * K * N, nh * K * N * wb
+            else:
+                x = torch.randn(t, K, device=dev).to(torch.bfloat16)
+                f32 = name.startswith("router")
+                fn = lambda m=m, x=x, f32=f32: m(x, out_f32=f32) if f32 else m(x)  # noqa: E731
+                flops, wbytes = 2 * t * K * N, K * N * wb
+            us = _time_flushed(fn)
+            out.append({"op": name, "tokens": t, "us": round(us, 1), "weight_tb_s": round(wbytes / us / 1e6, 3),
+                        "frac_hbm": round(wbytes / us / 1e3 / PEAKS["hbm_gbs"], 3),
+                        "tflops": round(flops / us / 1e6, 1)})
+    return out
+
+
+def dsa_profile_case(layers: int, sessions: int, ctx: int, steps: int, prefill: int, top: int = 40) -> dict:
+    """Per-kernel device time of the DSA-MoE serving step (the bench's engine: DP attention + EP over the launched
+    ranks, CUDA-graph decode), from the CUDA activity records of the torch profiler (kernel durations as CUPTI reports
+    them; the shares, not the absolutes, are the point: the bench's own CUDA-event timing is the throughput figure).
+    Sessions hold `ctx` positions of random well-formed KV written by the pool writers (no prefill compute before the
+    decode steps); with `prefill` > 0 one more request of that many tokens per rank is prefilled and profiled too."""
+    import torch.distributed as dist
+    from torch.profiler import ProfilerActivity, profile
+    from ..config import EngineConfig, model_config
+    from ..engine.engine import Engine
+    from ..engine.scheduler import SamplingParams
+    from ..engine.synthetic import synth_mla_sessions
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    dev = torch.device("cuda", torch.cuda.current_device())
+    per = sessions // world
+    cfg = model_config("dsa_moe", num_layers=layers)
+    ecfg = EngineConfig(model="dsa_moe", device=str(dev), kv_dtype="nvfp4", max_running=per + 1,
+                        chunked_prefill=max(prefill, 64), graph_batch_sizes=str(per), ep=world, prefix_cache=False)
+    eng = Engine(ecfg, cfg, max_seq=ctx + max(prefill, 0) + 256, ep_rank=rank,
+                 ep_group=dist.group.WORLD if world > 1 else None)
+    synth_mla_sessions(eng, per, ctx, 200, seed=1 + rank)
+    eng.runner.warm_graphs(per)
+    for _ in range(3):
+        eng.step()
+    torch.cuda.synchronize()
+
+    def table(prof, n):
+        rows = []
+        for e in prof.key_averages():
+            t = getattr(e, "device_time_total", None)
+            if t is None:
+                t = getattr(e, "cuda_time_total", 0)
+            if t > 0 and e.count > 0:
+                rows.append((e.key[:110], t / n, e.count // n))
+        rows.sort(key=lambda r: -r[1])
+        tot = sum(r[1] for r in rows)
+        return {"total_us": round(tot, 1), "kernels": [{"name": k, "us": round(u, 1), "launches": c,
+                                                          "share": round(u / tot, 4)} for k, u, c in rows[:top]]}
+    res = {"layers": layers, "sessions": sessions, "ctx": ctx, "world": world}
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            eng.step()
+        torch.cuda.synchronize()
+    res["decode_step"] = table(prof, steps)
+    if prefill:
+        g = torch.Generator().manual_seed(7 + rank)
+        eng.add_request(torch.randint(1, cfg.vocab, (prefill,), generator=g).tolist(), SamplingParams(max_new_tokens=4))
+        eng.sched.burst = 1
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            eng.step()
+            torch.cuda.synchronize()
+        res["prefill_chunk"] = table(prof, 1)
+        res["prefill_chunk"]["tokens"] = prefill
+    return res if rank == 0 else {}
+
+
 def main() -> None:
     _load_peaks()
     p = argparse.ArgumentParser()
@@ -456,6 +557,14 @@ def main() -> None:
     p.add_argument("--hidden", type=int, default=7168)
     p.add_argument("--ffn", type=int, default=2048)
     p.add_argument("--wfmt", default="fp8", choices=["fp8", "nvfp4"])
+    p.add_argument("--layers", type=int, default=13)
+    p.add_argument("--sessions", type=int, default=64)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--prefill", type=int, default=0)
+    p.add_argument("--tokens", default="8,64,8192")
+    p.add_argument("--only", default="", help="proj_gemms: comma-separated op names")
+    p.add_argument("--nt", default="", help="proj_gemms: token tiles to sweep (comma-separated)")
+    p.add_argument("--ks", default="", help="proj_gemms: K splits to sweep (comma-separated)")
     a = p.parse_args()
     if a.kernel == "gqa_decode":
         r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches, a.splits, a.trace)
@@ -479,6 +588,26 @@ def main() -> None:
             r = {}
     elif a.kernel == "moe_gemm":
         r = moe_gemm_case(a.b, a.experts, a.total_experts, a.topk, a.hidden, a.ffn, a.wfmt, a.launches)
+    elif a.kernel == "proj_gemms":
+        from ..ops import linear as L
+        for nt in [int(v) for v in a.nt.split(",")] if a.nt else [None]:
+            for ks in [int(v) for v in a.ks.split(",")] if a.ks else [None]:
+                L.FORCE.update(nt=nt, ks=ks)
+                for row in proj_gemms_case([int(v) for v in a.tokens.split(",")], a.only):
+                    row.update(nt=nt, ks=ks)
+                    print(json.dumps(row), flush=True)
+        L.FORCE.update(nt=None, ks=None)
+        r = {}
+    elif a.kernel == "dsa_profile":
+        import torch.distributed as dist
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if world > 1:
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+            dist.init_process_group("nccl", device_id=torch.device("cuda", torch.cuda.current_device()))
+        r = dsa_profile_case(a.layers, a.sessions, a.ctx, a.steps, a.prefill)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
     elif a.kernel == "mla_decode":
         r = mla_decode_case(a.b, a.heads, a.ctx, a.topk, a.fmt, a.nq, a.launches)
     else:
