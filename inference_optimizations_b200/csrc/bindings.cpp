@@ -763,6 +763,84 @@ void nvfp4_lut_test(const at::Tensor& words, at::Tensor out) {
                                     out.data_ptr<int>(), stream()));
 }
 
+void mla_prep_kv(const at::Tensor& ya, const at::Tensor& q_norm, const at::Tensor& kv_norm, const at::Tensor& ik_w,
+                 const at::Tensor& ik_b, const at::Tensor& rope, const at::Tensor& pos, const at::Tensor& slot,
+                 at::Tensor qa_out, at::Tensor latent_pool, at::Tensor index_pool, at::Tensor iw_out, double iw_scale,
+                 int64_t q_lora, int64_t Hi, double eps) {
+  req(ya, at::kBFloat16, "ya");
+  req(rope, at::kFloat, "rope");
+  req(pos, at::kInt, "pos");
+  req(slot, at::kInt, "slot");
+  req(qa_out, at::kBFloat16, "qa_out");
+  req(latent_pool, at::kByte, "latent_pool");
+  req(index_pool, at::kByte, "index_pool");
+  req(iw_out, at::kFloat, "iw_out");
+  const int64_t T = pos.numel();
+  TORCH_CHECK(ya.dim() == 2 && ya.stride(1) == 1 && ya.size(0) == T && ya.size(1) >= q_lora + 576 + 128 + Hi,
+              "ya [T, >= q_lora + 704 + Hi]");
+  TORCH_CHECK(rope.dim() == 2 && rope.size(1) == 64 && rope.is_contiguous(), "rope [max_pos, 64]");
+  TORCH_CHECK(qa_out.is_contiguous() && qa_out.numel() == T * q_lora && iw_out.is_contiguous() &&
+                  iw_out.numel() == T * Hi && slot.numel() == T,
+              "qa_out [T, q_lora], iw_out [T, Hi]");
+  TORCH_CHECK(latent_pool.dim() == 2 && (latent_pool.size(1) == 352 || latent_pool.size(1) == 576) &&
+                  latent_pool.is_contiguous() && index_pool.is_contiguous() && index_pool.size(-1) == 64 * 132,
+              "pools");
+  iob::MlaPrepArgs a{};
+  a.ya = ya.data_ptr();
+  a.ya_stride = static_cast<int>(ya.stride(0));
+  a.q_norm = q_norm.data_ptr();
+  a.kv_norm = kv_norm.data_ptr();
+  a.ik_w = ik_w.data_ptr();
+  a.ik_b = ik_b.data_ptr();
+  a.rope = rope.data_ptr<float>();
+  a.pos = pos.data_ptr<int>();
+  a.slot = slot.data_ptr<int>();
+  a.qa_out = qa_out.data_ptr();
+  a.latent_pool = latent_pool.data_ptr<uint8_t>();
+  a.latent_fmt = latent_pool.size(1) == 352 ? iob::kKvNvfp4 : iob::kKvFp8;
+  a.index_pool = index_pool.data_ptr<uint8_t>();
+  a.iw_out = iw_out.data_ptr<float>();
+  a.iw_scale = static_cast<float>(iw_scale);
+  a.T = static_cast<int>(T);
+  a.q_lora = static_cast<int>(q_lora);
+  a.Hi = static_cast<int>(Hi);
+  a.eps = static_cast<float>(eps);
+  const at::cuda::CUDAGuard g(ya.device());
+  CHECK_CUDA_OK(iob::mla_prep_kv(a, stream()));
+}
+
+void mla_prep_q(const at::Tensor& yb, const at::Tensor& rope, const at::Tensor& pos, at::Tensor qf, at::Tensor q8,
+                at::Tensor w_eff, const at::Tensor& iw, int64_t H, int64_t dn, int64_t Hi) {
+  req(yb, at::kBFloat16, "yb");
+  req(rope, at::kFloat, "rope");
+  req(pos, at::kInt, "pos");
+  req(qf, at::kBFloat16, "qf");
+  req(q8, at::kByte, "q8");
+  req(w_eff, at::kFloat, "w_eff");
+  req(iw, at::kFloat, "iw");
+  const int64_t T = pos.numel();
+  TORCH_CHECK(yb.dim() == 2 && yb.stride(1) == 1 && yb.size(0) == T && yb.size(1) >= H * (dn + 64) + Hi * 128,
+              "yb [T, >= H (dn + 64) + Hi 128]");
+  TORCH_CHECK(qf.is_contiguous() && qf.numel() == T * H * 576 && q8.is_contiguous() && q8.numel() == T * Hi * 128 &&
+                  w_eff.numel() == T * Hi && iw.numel() == T * Hi && rope.size(1) == 64,
+              "qf [T, H, 576], q8 [T, Hi, 128], w_eff / iw [T, Hi]");
+  iob::MlaPrepArgs a{};
+  a.yb = yb.data_ptr();
+  a.yb_stride = static_cast<int>(yb.stride(0));
+  a.rope = rope.data_ptr<float>();
+  a.pos = pos.data_ptr<int>();
+  a.qf = qf.data_ptr();
+  a.q8 = q8.data_ptr<uint8_t>();
+  a.w_eff = w_eff.data_ptr<float>();
+  a.iw_out = const_cast<float*>(iw.data_ptr<float>());
+  a.T = static_cast<int>(T);
+  a.H = static_cast<int>(H);
+  a.dn = static_cast<int>(dn);
+  a.Hi = static_cast<int>(Hi);
+  const at::cuda::CUDAGuard g(yb.device());
+  CHECK_CUDA_OK(iob::mla_prep_q(a, stream()));
+}
+
 std::vector<int64_t> sm_lanes(int64_t device, int64_t first_sms) {
   unsigned long long streams[2] = {0, 0};
   int sms[2] = {0, 0};
@@ -808,4 +886,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("umma_f8_mn_test", &umma_f8_mn_test);
   m.def("nvfp4_lut_test", &nvfp4_lut_test);
   m.def("sm_lanes", &sm_lanes);
+  m.def("mla_prep_kv", &mla_prep_kv);
+  m.def("mla_prep_q", &mla_prep_q);
 }

@@ -209,6 +209,34 @@ cudaError_t splitk_reduce(const float* part, int ksplit, int rows, int N, void* 
 cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_base, const float* w, void* y,
                         cudaStream_t s);
 
+// ---- fused MLA attention-block glue (mla_prep.cu)
+struct MlaPrepArgs {
+  const void* ya;             // bf16 [T, ya_stride]: q_a (q_lora) | kv latent (512) | k_pe (64) | k_i (128) | w_i (Hi)
+  int ya_stride;
+  const void* q_norm;         // bf16 [q_lora]
+  const void* kv_norm;        // bf16 [512]
+  const void* ik_w;           // bf16 [128] LayerNorm weight / bias of the indexer key
+  const void* ik_b;
+  const float* rope;          // fp32 [max_pos, 64]: cos (32) | sin (32)
+  const int* pos;             // [T]
+  const int* slot;            // [T] pool slot (-1: not written)
+  void* qa_out;               // bf16 [T, q_lora]
+  uint8_t* latent_pool;       // [slots, 352] NVFP4 or [slots, 576] E4M3
+  int latent_fmt;
+  uint8_t* index_pool;        // [pages, 64 * 132]
+  float* iw_out;              // fp32 [T, Hi]: w_i * iw_scale
+  float iw_scale;
+  const void* yb;             // bf16 [T, yb_stride]: q_nope (H dn) | q_pe (H 64) | q_i (Hi 128)
+  int yb_stride;
+  void* qf;                   // bf16 [T, H, 576]; columns 512.. written
+  uint8_t* q8;                // E4M3 [T, Hi, 128]
+  float* w_eff;               // fp32 [T, Hi]
+  int T, q_lora, H, dn, Hi;
+  float eps;
+};
+cudaError_t mla_prep_kv(const MlaPrepArgs& a, cudaStream_t s);
+cudaError_t mla_prep_q(const MlaPrepArgs& a, cudaStream_t s);
+
 // ---- FP8-quantized two-shot all-reduce over peer memory (qar.cu)
 struct QarArgs {
   const long long* peers;      // [nranks] symmetric buffer bases

@@ -129,6 +129,7 @@ class MLAModel:
         self.seed = seed
         self.keep_master = keep_master if keep_master is not None else c.num_params() < 2e9
         self.cuda = self.device.type == "cuda"
+        self.fuse_glue = True                            # the fused attention-block glue kernels where they apply
         self._bs: dict = {}
         r = lambda name, shape, s=c.init_std: _rand(name, shape, s, self.device, seed)  # noqa: E731
         self.embed = r("embed", (c.vocab, h))
@@ -442,9 +443,47 @@ class MLAModel:
             o = torch.einsum("thk,hkv->thv", o_lat.float(), w.w_uv.float()).to(torch.bfloat16).reshape(t, -1)
         return w.k["o"](o) if w.k is not None else Fn.linear(o, w.wo)
 
+    def _fused_glue(self, w: MLALayerWeights) -> bool:
+        """The two fused glue kernels (csrc/mla_prep.cu) serve this layer: CUDA kernels for every projection, the
+        head-batched W_UK product, and the DeepSeek dims those kernels are written for (rope 64, latent 512, index
+        key 128)."""
+        c = self.cfg
+        return (self.fuse_glue and w.k is not None and "uk" in w.k and c.qk_rope == 64 and c.kv_lora == 512
+                and c.index_dim == 128)
+
+    def _layer_forward_fused(self, i: int, h: torch.Tensor, x: torch.Tensor, st: MLAStep, kv: MLAKVCache,
+                             next_norm: torch.Tensor) -> torch.Tensor:
+        """layer_forward with the attention block's glue in two kernels: x -> (q_a | kv_a | k_i | w_i) -> [q_a norm,
+        latent norm + k_pe RoPE + pool write, index key LayerNorm + RoPE + pool write, head weights]; q_a ->
+        (q_nope | q_pe | q_i); q_nope W_UK written straight into the attention query's first 512 columns; then
+        [q_pe RoPE into the query's last 64 columns, index query RoPE + E4M3 quantization]."""
+        from .._ext import ext
+        c, w = self.cfg, self.layers[i]
+        t, dev, eps = x.shape[0], x.device, c.rms_eps
+        cs = self.rope_table(max(st.max_ctx, 1) + 64)
+        ya = w.k["a"].lin(x)
+        qa = torch.empty(t, c.q_lora, dtype=torch.bfloat16, device=dev)
+        iw = torch.empty(t, c.index_heads, dtype=torch.float32, device=dev)
+        ext().mla_prep_kv(ya, w.q_norm, w.kv_norm, w.wi_kn, w.wi_kb, cs, st.pos, st.slot, qa, kv.latent[i],
+                          kv.index[i], iw, c.index_heads ** -0.5 * c.index_dim ** -0.5, c.q_lora, c.index_heads, eps)
+        yb = w.k["b"].lin(qa)
+        qf = torch.empty(t, c.num_heads, 576, dtype=torch.bfloat16, device=dev)
+        w.k["uk"](yb, t, row_stride=w.k["b_stride"], out=qf.view(t * c.num_heads, 576)[:, :512])
+        q8 = torch.empty(t, c.index_heads, c.index_dim, dtype=torch.uint8, device=dev)
+        w_eff = torch.empty(t, c.index_heads, dtype=torch.float32, device=dev)
+        ext().mla_prep_q(yb, cs, st.pos, qf, q8, w_eff, iw, c.num_heads, c.qk_nope, c.index_heads)
+        sel = I.indexer_select(q8, w_eff, kv.index[i], kv.table.dev, st.limit, c.index_topk, st.max_ctx,
+                               req_idx=st.req_idx, ws=kv.idx_ws.get((t, st.max_ctx)))
+        o_lat = M.mla_decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt, ws=kv.mla_ws.get((t, c.index_topk)))
+        x2 = B.rmsnorm(self._o_proj(w, o_lat, t), w.n_post, eps, residual=h)
+        f = self._ffn(i, x2)
+        return B.rmsnorm(f, next_norm, eps, residual=h)
+
     def layer_forward(self, i: int, h: torch.Tensor, x: torch.Tensor, st: MLAStep, kv: MLAKVCache,
                       next_norm: torch.Tensor) -> torch.Tensor:
         """x = norm_in(h); h updated in place.  Returns the next norm of h."""
+        if self._fused_glue(self.layers[i]):
+            return self._layer_forward_fused(i, h, x, st, kv, next_norm)
         c, w = self.cfg, self.layers[i]
         t = x.shape[0]
         eps = c.rms_eps

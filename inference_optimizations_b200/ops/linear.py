@@ -282,15 +282,18 @@ class HeadBatchedLinear:
                              (j[None, :] * self.H + h[:, None]).reshape(-1).contiguous())
         return self._rows[t]
 
-    def __call__(self, x: torch.Tensor, t: int, row_stride: int = 0) -> torch.Tensor:
-        """x: any tensor whose memory holds token t's head h at element (t * row_stride + h) * K (row_stride 0: H)."""
+    def __call__(self, x: torch.Tensor, t: int, row_stride: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+        """x: any tensor whose memory holds token t's head h at element (t * row_stride + h) * K (row_stride 0: H).
+        out: optional [t H, >= N] bf16 view with unit column stride (e.g. the first N columns of a wider per-head
+        row); default a new contiguous [t, H, N]."""
         rs = row_stride or self.H
-        out = torch.empty(t, self.H, self.N, dtype=torch.bfloat16, device=x.device)
+        if out is None:
+            out = torch.empty(t, self.H, self.N, dtype=torch.bfloat16, device=x.device)
         if t == 0:
             return out
         rows = x.reshape(-1).view(torch.uint8).view(-1, self.K * 2)
         off, pairs = self._index(t, x.device)
-        MG.gemm(self.wpack, rows, rows, off, pairs, out.view(t * self.H, self.N), self.status,
+        MG.gemm(self.wpack, rows, rows, off, pairs, out.view(t * self.H, -1) if out.dim() == 3 else out, self.status,
                 n_tiles=self.N // (TILE * self.g), kc=self.K // 64, g=self.g, nt=MG.pick_nt(t), mode=0, src_div=1,
                 num_ctas=self.num_ctas, kind=2, src_group=self.H if rs != self.H else 0,
                 src_group_stride=rs if rs != self.H else 0)

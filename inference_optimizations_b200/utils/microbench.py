@@ -471,10 +471,37 @@ def proj_gemms_case(tokens: list, only: str = "") -> list:
                 fn = lambda m=m, x=x, f32=f32: m(x, out_f32=f32) if f32 else m(x)  # noqa: E731
                 flops, wbytes = 2 * t * K * N, K * N * wb
             us = _time_flushed(fn)
-            out.append({"op": name, "tokens": t, "us": round(us, 1), "weight_tb_s": round(wbytes / us / 1e6, 3),
-                        "frac_hbm": round(wbytes / us / 1e3 / PEAKS["hbm_gbs"], 3),
-                        "tflops": round(flops / us / 1e6, 1)})
+            row = {"op": name, "tokens": t, "us": round(us, 1), "weight_tb_s": round(wbytes / us / 1e6, 3),
+                   "frac_hbm": round(wbytes / us / 1e3 / PEAKS["hbm_gbs"], 3), "tflops": round(flops / us / 1e6, 1)}
+            row["kernels_us"] = _kernel_times(fn)
+            gemm = sum(v for k, v in row["kernels_us"].items() if "moe_gemm" in k)
+            if gemm:
+                row["gemm_kernel_frac_hbm"] = round(wbytes / gemm / 1e3 / PEAKS["hbm_gbs"], 3)
+            out.append(row)
     return out
+
+
+def _kernel_times(fn, reps: int = 5) -> dict:
+    """Mean device duration per kernel name of one fn() call (CUDA activity records of the torch profiler, L2
+    flushed before each call): the kernel-only split of a call that also has CPU launch gaps."""
+    from torch.profiler import ProfilerActivity, profile
+    flush = torch.ones(128 << 20, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            torch.sum(flush, dim=0, out=sink)
+            fn()
+        torch.cuda.synchronize()
+    res = {}
+    for e in prof.key_averages():
+        t = getattr(e, "device_time_total", None)
+        if t is None:
+            t = getattr(e, "cuda_time_total", 0)
+        if t > 0 and "reduce_kernel<" not in e.key:
+            k = e.key.split("(")[0].replace("void ", "").replace("iob::(anonymous namespace)::", "")[:48]
+            res[k] = round(res.get(k, 0.0) + t / reps, 2)
+    return res
 
 
 def dsa_profile_case(layers: int, sessions: int, ctx: int, steps: int, prefill: int, top: int = 40) -> dict:

@@ -113,3 +113,37 @@ def test_mla_model_fp8_projections_track_bf16(cuda):
         logits.append(eng.runner.model.logits(eng.runner.model.forward(st, eng.runner.kv)).float().cpu())
     cos = torch.nn.functional.cosine_similarity(logits[0], logits[1], dim=-1)
     assert cos.mean().item() > 0.97 and cos.min().item() > 0.85, (cos.mean().item(), cos.min().item())
+
+
+@pytest.mark.parametrize("kv", ["nvfp4", "fp8"])
+def test_mla_fused_glue_matches_torch_glue(cuda, kv):
+    """The two fused glue kernels (norms, RoPE, pool writes, indexer query quantization) reproduce the torch glue of
+    the same layer: same latent / index pool bytes up to rounding flips, logits within bf16 noise."""
+    from inference_optimizations_b200.config import EngineConfig, model_config
+    from inference_optimizations_b200.engine.engine import Engine
+    from inference_optimizations_b200.engine.scheduler import Request, SamplingParams, Segment
+    over = dict(expert_ffn=256, dense_ffn=512, weight_dtype="fp8", expert_dtype="fp8", hidden=512, q_lora=256,
+                qk_nope=128, v_head=128, index_heads=8, num_heads=8)
+    cfg = model_config("tiny_mla", **over)
+    ecfg = EngineConfig(model="tiny_mla", device=str(cuda), kv_dtype=kv, max_running=4, chunked_prefill=128,
+                        cuda_graphs=False, prefix_cache=False)
+    torch.manual_seed(6)
+    prompt = torch.randint(0, cfg.vocab, (100,)).tolist()
+    res = []
+    for fused in (False, True):
+        eng = Engine(ecfg, cfg, max_seq=256)
+        eng.runner.model.fuse_glue = fused
+        assert eng.runner.model._fused_glue(eng.runner.model.layers[0]) == fused
+        r = Request(rid=0, prompt=prompt, params=SamplingParams(max_new_tokens=1))
+        r.slot = 0
+        eng.runner.attach(r)
+        st, _ = eng.runner._step([Segment(r, 0, prompt, True)])
+        logits = eng.runner.model.logits(eng.runner.model.forward(st, eng.runner.kv)).float()
+        torch.cuda.synchronize()
+        res.append((logits.cpu(), [p.clone().cpu() for p in eng.runner.kv.latent],
+                    [p.clone().cpu() for p in eng.runner.kv.index]))
+    (l0, lat0, idx0), (l1, lat1, idx1) = res
+    for a, b in zip(lat0 + idx0, lat1 + idx1):
+        assert (a != b).float().mean().item() < 0.01          # a few rounding-boundary flips at most
+    cos = torch.nn.functional.cosine_similarity(l0, l1, dim=-1)
+    assert cos.min().item() > 0.999, cos.min().item()
