@@ -199,7 +199,14 @@ struct MoeGemmArgs {
   int num_ctas;
   int kind;                   // 0: FP8 E4M3 + UE8M0 per 32 (128-blocks replicated); 1: NVFP4 (E2M1 + E4M3 per 16)
   float out_mul;
+  long long* trace;           // optional diagnostic timeline of CTA 0 (kMgEv* events, clock64), null = off
 };
+// GEMM timeline events (trace[ev]): kernel start, setup done, first weight copy issued, first stage ready at the
+// MMA warp, last MMA committed, first accumulator seen by the epilogue, epilogue done, kernel end.
+// Slots 8 + 4 c + {0, 1, 2}: chunk c (32 tokens, c < 3) of the epilogue: accumulator loaded, first pass staged,
+// first pass stored.
+enum MgTraceEv { kMgEvStart, kMgEvSetup, kMgEvFirstCopy, kMgEvFirstReady, kMgEvLastMma, kMgEvAccSeen, kMgEvEpiDone,
+                 kMgEvEnd, kMgEvCount = 20 };
 cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s);
 cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, int extra, int* off, int* pairs,
                       cudaStream_t s);

@@ -162,6 +162,14 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n)); }
 
+__device__ __forceinline__ void mg_trace(const MoeGemmArgs& a, int ev) {
+  if (a.trace && blockIdx.x == 0) {
+    long long t;
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+    a.trace[ev] = t;
+  }
+}
+
 // Item i of this launch -> (expert, token tile, weight tile, K split), via the per-expert prefix of item counts.
 __device__ __forceinline__ void item_coords(const int* prefix, int E, int n_tiles, int ksplit, int i, int& e, int& tt,
                                             int& nt, int& ks) {
@@ -202,42 +210,45 @@ __device__ __forceinline__ uint32_t ue8m0_for(float amax) {
   return static_cast<uint32_t>(e + 127);
 }
 
-// Plain-output epilogue of one TMEM chunk (KCH tokens x G 128-column tiles, this thread = column n_local): the four
-// epilogue warps stage the chunk as token rows in shared memory (conflict-free: a warp writes 32 consecutive
-// columns of one token), then each warp stores whole rows, one 16-byte store per lane, to the row's destination
-// (bf16 out, fp32 split-K partial, or the owning peer's combine buffer).  One pair-id load per row instead of one
-// per element, and 512-byte row segments instead of 64-byte scattered ones.  ESZ: bytes per output element.
-template <class C, int G, int ESZ, int KCH>
-__device__ __forceinline__ void store_rows(const MoeGemmArgs& a, uint8_t* epi, const uint32_t (&v0)[KCH],
-                                           const uint32_t (&v1)[KCH], float emul, int c0, int rows, int row0, int nt,
-                                           int ks, int q, int lane, int n_local) {
+// Plain-output epilogue of one item (this thread = TMEM lane = output column n_local of each of the G column tiles):
+// groups of kGrp tokens are loaded from TMEM, staged as token rows in shared memory (a warp writes 32 consecutive
+// columns of one token: conflict-free), then each warp stores whole rows, one 16-byte store per lane, to the row's
+// destination (bf16 out, fp32 split-K partial, or the owning peer's combine buffer).  The code is a short rolled loop
+// on purpose: a small GEMM runs each CTA's epilogue once, from a cold instruction cache, and fully unrolled staging
+// code cost more in instruction fetch than in execution.  Groups past the item's valid tokens are skipped.
+// pid: the item's pair ids in shared memory.  ESZ: bytes per output element.
+template <class C, int NT, int G, int ESZ>
+__device__ __forceinline__ void store_rows(const MoeGemmArgs& a, uint8_t* epi, const int* pid, uint32_t acc,
+                                           float emul, int rows, int nt, int ks, int q, int lane, int n_local) {
   constexpr int kRowB = G * 128 * ESZ;
-  constexpr int kFit = static_cast<int>(C::kEpi) / kRowB;
-  static_assert(kFit >= 4, "epilogue staging too small");
-  constexpr int kPer = kFit >= 32 ? 32 : kFit >= 16 ? 16 : kFit >= 8 ? 8 : 4;
-  constexpr int kP = kPer > KCH ? KCH : kPer;
+  constexpr int kGrp = (static_cast<int>(C::kEpi) / kRowB) >= 8 ? 8 : 4;
+  static_assert(static_cast<int>(C::kEpi) / kRowB >= 4, "epilogue staging too small");
+#pragma unroll 1
+  for (int c = 0; c < NT && c < rows; c += kGrp) {
+    uint32_t v[G][kGrp];
 #pragma unroll
-  for (int t0 = 0; t0 < KCH; t0 += kP) {
+    for (int g = 0; g < G; ++g) {
+      if constexpr (kGrp == 8) tmem_ld8(acc + g * NT + c, v[g]); else tmem_ld4(acc + g * NT + c, v[g]);
+    }
+    tmem_ld_wait();
 #pragma unroll
     for (int g = 0; g < G; ++g) {
 #pragma unroll
-      for (int t = 0; t < kP; ++t) {
-        float v = __uint_as_float(g == 0 ? v0[t0 + t] : v1[t0 + t]) * emul;
-        if (a.mode == kMoeOutBf16Weighted) {
-          const int r = c0 + t0 + t;
-          v *= r < rows ? a.pair_w[a.pairs[row0 + r]] : 0.f;
-        }
+      for (int t = 0; t < kGrp; ++t) {
+        float x = __uint_as_float(v[g][t]) * emul;
+        if (a.mode == kMoeOutBf16Weighted) x *= c + t < rows ? a.pair_w[pid[c + t]] : 0.f;
         if constexpr (ESZ == 4)
-          reinterpret_cast<float*>(epi)[t * (G * 128) + g * 128 + n_local] = v;
+          reinterpret_cast<float*>(epi)[t * (G * 128) + g * 128 + n_local] = x;
         else
-          reinterpret_cast<__nv_bfloat16*>(epi)[t * (G * 128) + g * 128 + n_local] = __float2bfloat16(v);
+          reinterpret_cast<__nv_bfloat16*>(epi)[t * (G * 128) + g * 128 + n_local] = __float2bfloat16(x);
       }
     }
     named_bar(2, 128);
-    for (int t = q; t < kP; t += 4) {
-      const int r = c0 + t0 + t;
-      if (r >= rows) continue;
-      const int p = a.pairs[row0 + r];
+#pragma unroll 1
+    for (int t = q; t < kGrp; t += 4) {
+      const int r = c + t;
+      if (r >= rows) break;
+      const int p = pid[r];
       char* dst;
       if constexpr (ESZ == 4) {
         dst = reinterpret_cast<char*>(a.out) +
@@ -252,8 +263,8 @@ __device__ __forceinline__ void store_rows(const MoeGemmArgs& a, uint8_t* epi, c
         dst = reinterpret_cast<char*>(a.out) + (static_cast<size_t>(p) * a.out_stride + static_cast<size_t>(nt) * G * 128) * 2;
       }
       const uint4* src = reinterpret_cast<const uint4*>(epi + t * kRowB);
-#pragma unroll
-      for (int c = lane; c < kRowB / 16; c += 32) reinterpret_cast<uint4*>(dst)[c] = src[c];
+#pragma unroll 1
+      for (int k = lane; k < kRowB / 16; k += 32) reinterpret_cast<uint4*>(dst)[k] = src[k];
     }
     named_bar(2, 128);
   }
@@ -274,6 +285,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
   volatile int* abort = &ctl.abort;
 
   if (threadIdx.x == 0) {
+    mg_trace(a, kMgEvStart);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&ctl.w_full[s], 1);
       mbar_init(&ctl.x_full[s], 64);
@@ -326,6 +338,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
   tc_fence_after();
   const int n_items = ctl.n_items;
   const uint32_t tmem = ctl.tmem_base;
+  if (threadIdx.x == 0) mg_trace(a, kMgEvSetup);
   const uint32_t sfa_col = C::kAccBufs * C::kAccCols;
   const uint32_t sfb_col = sfa_col + 4 * G * kSfw;
 
@@ -347,6 +360,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
             break;
           }
           uint8_t* st = stages + s * C::kStage;
+          if (it == 0) mg_trace(a, kMgEvFirstCopy);
           mbar_expect_tx(&ctl.w_full[s], C::kWBlk);
           const uint8_t* blk = src + static_cast<size_t>(kc) * C::kWBlk;
           bulk_g2s(st, blk, G * kTile, &ctl.w_full[s]);
@@ -381,6 +395,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
           }
           tc_fence_after();
           fence_proxy_async_smem();
+          if (it == 0) mg_trace(a, kMgEvFirstReady);
           const uint32_t st = smem_u32(stages + s * C::kStage);
           const uint32_t x_s = st + G * kTile;
           const uint32_t sfa_s = x_s + C::kX;
@@ -426,6 +441,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
         }
         if (!ok) break;
         umma_commit(&ctl.acc_full[buf]);
+        mg_trace(a, kMgEvLastMma);
       }
       umma_commit(&ctl.fin);          // every MMA issued above has completed before TMEM is freed
       mbar_wait(&ctl.fin, 0, nullptr, a.status, kTimeoutMma);
@@ -497,11 +513,26 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
       const int row0 = a.expert_off[e] + tt * NT;
       const int rows = min(NT, a.expert_off[e + 1] - row0);
       const int buf = li % C::kAccBufs, use = li / C::kAccBufs;
+      // plain modes: the item's pair ids go to shared memory with one load per thread, issued before the
+      // accumulator wait so their latency hides under the mainloop (the previous item's row stores ended with a
+      // barrier, so the array is free; the SwiGLU mode uses this scratch for its row maxima instead)
+      int* pid = reinterpret_cast<int*>(red);
+      if (a.mode != kMoeOutSwigluQuant) {
+        const int tid = threadIdx.x - 128;
+        if (tid < rows) pid[tid] = a.pairs[row0 + tid];
+        named_bar(2, 128);
+      }
       if (!mbar_wait(&ctl.acc_full[buf], use & 1, abort, a.status, kTimeoutConsumer)) break;
       tc_fence_after();
+      if (li == 0 && threadIdx.x == 128) mg_trace(a, kMgEvAccSeen);
       const uint32_t acc = tmem + lane_addr + buf * C::kAccCols;
       const float emul = a.out_mul * (a.expert_mul ? a.expert_mul[e] : 1.f);
       constexpr int kChunk = NT < 32 ? NT : 32;
+      if (a.mode == kMoeOutF32Split) {               // split-K partial, summed by splitk_reduce
+        store_rows<C, NT, G, 4>(a, epi, pid, acc, emul, rows, nt, ks, q, lane, n_local);
+      } else if (a.mode != kMoeOutSwigluQuant) {
+        store_rows<C, NT, G, 2>(a, epi, pid, acc, emul, rows, nt, ks, q, lane, n_local);
+      } else
       for (int c0 = 0; c0 < NT; c0 += kChunk) {
         uint32_t v0[kChunk], v1[kChunk];
         if constexpr (kChunk == 16) tmem_ld16(acc + c0, v0); else tmem_ld32(acc + c0, v0);
@@ -559,14 +590,11 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
                     sb;
             }
           }
-        } else if (a.mode == kMoeOutF32Split) {      // split-K partial, summed by splitk_reduce
-          store_rows<C, G, 4, kChunk>(a, epi, v0, v1, emul, c0, rows, row0, nt, ks, q, lane, n_local);
-        } else {
-          store_rows<C, G, 2, kChunk>(a, epi, v0, v1, emul, c0, rows, row0, nt, ks, q, lane, n_local);
         }
       }
       tc_fence_before();
       mbar_arrive(&ctl.acc_empty[buf]);
+      if (threadIdx.x == 128) mg_trace(a, kMgEvEpiDone);
     }
     // rows stored into peers' memory must be visible system-wide before the next kernel's barrier releases its
     // flag (that release orders only the releasing thread's own writes)
@@ -578,6 +606,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }
+  if (threadIdx.x == 0) mg_trace(a, kMgEvEnd);
 }
 
 template <int NT, int G, int KIND>

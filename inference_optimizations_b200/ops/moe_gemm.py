@@ -181,10 +181,14 @@ def gemm(wpack, x, x_scale, off, pairs, out, status, *, n_tiles: int, kc: int, g
          num_ctas: int = 148, kind: int = 0, expert_mul=None, out_peers=None, out_offset: int = 0, out_div: int = 1,
          out_rank: int = 0, out_shared_base: int = 0, pairs_total: int = 0, ksplit: int = 1,
          split_rows: int = 0, src_group: int = 0, src_group_stride: int = 0) -> None:
-    """One grouped block-scaled GEMM launch (argument meanings: `MoeGemmArgs` in csrc/kernels.h)."""
+    """One grouped block-scaled GEMM launch (argument meanings: `MoeGemmArgs` in csrc/kernels.h).  When `TRACE` holds
+    an int64 CUDA tensor, CTA 0's phase timeline (clock64, `MgTraceEv` order) is written into it (diagnostics)."""
     ext().moe_gemm(wpack, x, x_scale, off, pairs, pair_w, out, out_scale, status, n_tiles, kc, g, nt, mode, src_div,
                    src_limit, src_shared_base, out_mul, num_ctas, kind, expert_mul, out_peers, out_offset, out_div, out_rank,
-                   out_shared_base, pairs_total, ksplit, split_rows, src_group, src_group_stride)
+                   out_shared_base, pairs_total, ksplit, split_rows, src_group, src_group_stride, TRACE[0])
+
+
+TRACE: list = [None]
 
 
 _TACTICS = None

@@ -474,11 +474,32 @@ def proj_gemms_case(tokens: list, only: str = "") -> list:
             row = {"op": name, "tokens": t, "us": round(us, 1), "weight_tb_s": round(wbytes / us / 1e6, 3),
                    "frac_hbm": round(wbytes / us / 1e3 / PEAKS["hbm_gbs"], 3), "tflops": round(flops / us / 1e6, 1)}
             row["kernels_us"] = _kernel_times(fn)
+            row["trace_cycles"] = _gemm_trace(fn)
             gemm = sum(v for k, v in row["kernels_us"].items() if "moe_gemm" in k)
             if gemm:
                 row["gemm_kernel_frac_hbm"] = round(wbytes / gemm / 1e3 / PEAKS["hbm_gbs"], 3)
             out.append(row)
     return out
+
+
+def _gemm_trace(fn) -> dict:
+    """CTA 0's phase timeline (clock64 cycles from kernel start) of the LAST GEMM launch of one fn() call, L2 flushed
+    before the call (`MgTraceEv` order in csrc/kernels.h)."""
+    from ..ops import moe_gemm as MG
+    names = ["start", "setup", "first_copy", "first_ready", "last_mma", "acc_seen", "epi_done", "end"] + [
+        f"c{c}_{k}" for c in range(3) for k in ("tmem", "staged", "stored", "_")]
+    flush = torch.ones(128 << 20, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
+    tr = torch.zeros(len(names), dtype=torch.int64, device="cuda")
+    torch.sum(flush, dim=0, out=sink)
+    MG.TRACE[0] = tr
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        MG.TRACE[0] = None
+    v = tr.cpu().tolist()
+    return {n: int(x - v[0]) for n, x in zip(names, v)}
 
 
 def _kernel_times(fn, reps: int = 5) -> dict:
