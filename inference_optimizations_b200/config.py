@@ -173,10 +173,9 @@ class EngineConfig:
     # KV pool
     page_size: int = 64
     kv_dtype: str = "nvfp4"              # "nvfp4" | "fp8" | "bf16" (GQA pools); MLA: "nvfp4" (352 B) | "fp8" (576 B)
-    kv_mix_threshold: int = 262144       # kvmix: requests longer than this move to the FP4 half of the slot space
     max_running: int = 64
-    max_total_tokens: int = 0            # 0 = size the pool from free memory
-    mem_fraction: float = 0.90
+    max_total_tokens: int = 0            # KV pool cap in tokens; 0 = the requests' need, bounded by free memory
+    mem_fraction: float = 0.90           # share of the device memory free at boot (less a reserve) the pool may take
     # scheduling
     chunked_prefill: int = 8192
     decode_burst: int = 1                # --num-continuous-decode-steps semantics (`scheduler/decode-burst/decode_burst.py`)

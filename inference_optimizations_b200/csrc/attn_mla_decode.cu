@@ -200,6 +200,7 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
   uint8_t* sqr = sp + kMRing * kMPBytes;                  // Q rope, SW64 128 x 64 B
   MlaSmem& sm = *reinterpret_cast<MlaSmem*>(sqr + 128 * 64);
 
+  griddep_launch();                                       // the W_UV GEMM after this may set up meanwhile
   const int half = blockIdx.x;                            // V half
   const int t = blockIdx.y, split = blockIdx.z;
   const int ntiles_all = (a.topk + kMTile - 1) / kMTile;
@@ -633,6 +634,7 @@ __global__ void __launch_bounds__(128) mla_q_quant_kernel(const __nv_bfloat16* _
 
 // out[t, h] = sum_s 2^(lse_s - M) o_s / sum_s 2^(lse_s - M); lse in natural log.  One CTA (128 threads) per (t, h).
 __global__ void __launch_bounds__(128) mla_combine_kernel(const MlaDecodeArgs a) {
+  griddep_launch();
   const int row = blockIdx.x;  // t * H + h
   const size_t plane = static_cast<size_t>(a.T) * a.H;
   float m = -INFINITY;

@@ -378,7 +378,7 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
               int64_t kind, const c10::optional<at::Tensor>& expert_mul,
               const c10::optional<at::Tensor>& out_peers, int64_t out_offset, int64_t out_div, int64_t out_rank,
               int64_t out_shared_base, int64_t pairs_total, int64_t ksplit, int64_t split_rows, int64_t src_group,
-              int64_t src_group_stride, const c10::optional<at::Tensor>& trace) {
+              int64_t src_group_stride, const c10::optional<at::Tensor>& trace, bool pdl, bool static_index) {
   req(wpack, at::kByte, "wpack");
   req(x, at::kByte, "x");
   req(off, at::kInt, "off");
@@ -439,6 +439,8 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
   a.split_rows = static_cast<int>(split_rows);
   a.src_group = static_cast<int>(src_group);
   a.src_group_stride = static_cast<int>(src_group_stride);
+  a.pdl = pdl ? 1 : 0;
+  a.static_index = static_index ? 1 : 0;
   if (trace.has_value()) {
     TORCH_CHECK(trace->scalar_type() == at::kLong && trace->numel() >= iob::kMgEvCount && trace->is_cuda(),
                 "trace int64 [>= kMgEvCount]");

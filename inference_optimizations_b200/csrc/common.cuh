@@ -27,6 +27,14 @@ enum StatusCode : int {
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitimate wait
 
+// Programmatic dependent launch.  A kernel launched with the programmatic-serialization attribute may start while
+// the previous kernel of its stream is still running; before reading anything that kernel wrote it calls
+// griddep_wait() (returns once the previous grid has completed and its writes are visible; a no-op for a kernel
+// launched normally).  griddep_launch() lets the NEXT kernel's CTAs be scheduled once every CTA of this grid has
+// issued it (no effect when the next kernel was launched normally).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -15,6 +15,7 @@ template <int VPT>
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
                                __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ w, int hidden,
                                int x_stride, float eps, bool plus_one, bool add_residual) {
+  griddep_launch();                   // a GEMM launched after this may set up and stream weights meanwhile
   const int row = blockIdx.x;
   const int nvec = hidden / 8;
   float v[VPT][8];

@@ -200,6 +200,11 @@ struct MoeGemmArgs {
   int kind;                   // 0: FP8 E4M3 + UE8M0 per 32 (128-blocks replicated); 1: NVFP4 (E2M1 + E4M3 per 16)
   float out_mul;
   long long* trace;           // optional diagnostic timeline of CTA 0 (kMgEv* events, clock64), null = off
+  // Programmatic dependent launch: the kernel may start while the previous kernel of the stream runs; it sets up and
+  // (static_index) streams its first weight stages before waiting for that kernel's outputs.  static_index: the
+  // expert offsets and pair ids were written before the previous kernel (cached index tensors), so the work list can
+  // be built before the wait; else everything waits first.
+  int pdl, static_index;
 };
 // GEMM timeline events (trace[ev]): kernel start, setup done, first weight copy issued, first stage ready at the
 // MMA warp, last MMA committed, first accumulator seen by the epilogue, epilogue done, kernel end.

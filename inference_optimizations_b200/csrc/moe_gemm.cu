@@ -303,6 +303,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
     tmem_alloc(&ctl.tmem_base, C::kTmemCols);
     tmem_relinquish();
   }
+  if (!a.static_index) griddep_wait();  // expert offsets / pair ids come from the previous kernel
   if (warp == 2) {                    // per-expert prefix of item counts (warp scan over chunks of experts)
     const int per = (a.E + 31) / 32;
     int local = 0;
@@ -339,6 +340,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
   const int n_items = ctl.n_items;
   const uint32_t tmem = ctl.tmem_base;
   if (threadIdx.x == 0) mg_trace(a, kMgEvSetup);
+  griddep_launch();                   // the next kernel may be scheduled as this grid's CTAs retire
   const uint32_t sfa_col = C::kAccBufs * C::kAccCols;
   const uint32_t sfb_col = sfa_col + 4 * G * kSfw;
 
@@ -448,6 +450,7 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
     }
   } else if (warp < 4) {
     // ---------------------------------------------------------------- activation gather (64 threads)
+    griddep_wait();                   // activations (and their scales) are the previous kernel's output
     const int t64 = threadIdx.x - 64;
     uint32_t it = 0;
     bool ok = true;
@@ -618,8 +621,17 @@ cudaError_t launch_mg(const MoeGemmArgs& a, cudaStream_t s) {
                                         static_cast<int>(C::kSmem)));
     attr = true;
   }
-  moe_gemm_kernel<NT, G, KIND><<<a.num_ctas, kMgThreads, C::kSmem, s>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.num_ctas);
+  cfg.blockDim = dim3(kMgThreads);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute pdl_attr[1];
+  pdl_attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl_attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl_attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, moe_gemm_kernel<NT, G, KIND>, a);
 }
 
 // ------------------------------------------------------------------------------------------------ routing prep
@@ -629,6 +641,7 @@ cudaError_t launch_mg(const MoeGemmArgs& a, cudaStream_t s) {
 // of the same launch; extra may be 0).
 __global__ void __launch_bounds__(1024) moe_align_kernel(const int* ids, int P, int e0, int E, int nb, int extra,
                                                          int* off, int* pairs) {
+  griddep_launch();
   __shared__ int cnt[kMaxExperts + 2];
   __shared__ int pos[kMaxExperts + 2];
   for (int e = threadIdx.x; e < nb; e += blockDim.x) cnt[e] = 0;
@@ -741,6 +754,7 @@ __device__ __forceinline__ void quant_row(Val val, int row, int H, int fmt, uint
 
 __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, float plus_one,
                                      int H, int fmt, uint8_t* q, uint32_t* sc) {
+  griddep_launch();                   // a GEMM launched after this may set up and stream weights meanwhile
   const int row = blockIdx.x;
   const __nv_bfloat16* xr = x + static_cast<size_t>(row) * H;
   __shared__ float red[32];
@@ -787,6 +801,7 @@ __global__ void act_quant_kernel(const __nv_bfloat16* gu, int F, int fmt, uint8_
 // or kept in fp32 (OutT = float: router logits).
 template <class OutT>
 __global__ void splitk_reduce_kernel(const float* part, int ksplit, int rows, int N, OutT* out) {
+  griddep_launch();
   const int r = blockIdx.x;
   for (int c = threadIdx.x; c < N / 4; c += blockDim.x) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);

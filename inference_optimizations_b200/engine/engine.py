@@ -66,13 +66,14 @@ class Engine:
     def add_request(self, prompt: list, params: Optional[SamplingParams] = None) -> Request:
         return self.sched.new_request(prompt, params or SamplingParams())
 
-    def step(self) -> dict:
-        """One engine iteration.  Returns rid -> tokens produced this step."""
+    def step(self, hold: Optional[bool] = None, chunk_cap: int = 0) -> dict:
+        """One engine iteration.  Returns rid -> tokens produced this step.  hold / chunk_cap: the data-parallel
+        ranks' joint decode-burst decision and prefill budget for this pass (`generate_dp`); default: local rules."""
         if self.pdmux is not None:
             return self._pdmux_step()
         t0 = time.perf_counter()
         rec = self.trace.begin() if self.trace else None
-        batch = self.sched.schedule()
+        batch = self.sched.schedule(hold, chunk_cap)
         if batch is None:
             if getattr(self.runner, "ep_world", 1) > 1:
                 self.runner.idle_step()          # data-parallel attention: join the busy ranks' MoE exchanges
@@ -146,23 +147,51 @@ class Engine:
             self.trace.end(rec, None)
         return out
 
-    def generate_dp(self, prompts: list, params: Optional[SamplingParams] = None, group=None) -> list:
-        """Data-parallel serving loop: this rank's prompts; every rank steps until no rank has work (one small
-        all-reduce per step), so the expert-parallel exchanges stay in lockstep."""
+    def generate_dp(self, prompts: list, params: Optional[SamplingParams] = None, group=None,
+                    route: bool = False) -> list:
+        """Data-parallel serving loop.  Every pass the ranks all-gather one row of scheduler facts (waiting, running,
+        decode streak, last pass kind, chunked prefill pending, passes delayed, prefill backlog) and take the same
+        decisions from it: stop when no rank has work; hold prefill admission everywhere while decode bursts run
+        (`burst.dp_hold`: streak below the burst on a decoding rank, queues short, bounded delay); cap every rank's
+        prefill at the budget of the ranks' backlogs (`dp_policy.prefill_budget`).  The expert-parallel exchanges
+        stay in lockstep since every rank steps once per pass.
+        route=False: `prompts` are this rank's; returns their outputs.  route=True: `prompts` is the global list
+        (identical on every rank); the cache-aware balancer (`dp_policy.DPBalancer`) assigns each prompt to a rank
+        (the same assignment on every rank) and the return value is {global index: output} for this rank's share."""
         import torch.distributed as dist
+        from .burst import RankFacts, dp_hold
+        from .dp_policy import DPBalancer, prefill_budget
         if self.pdmux is not None and self.pdmux.group is None:
             raise ValueError("generate_dp with pdmux needs the lanes' CPU group (PdmuxEngine(group=...)): the lanes "
                              "of data-parallel ranks advance in lockstep through it")
-        reqs = [self.add_request(p, params) for p in prompts]
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        if route:
+            bal = DPBalancer(world)
+            mine = [i for i, p in enumerate(prompts) if bal.route(p, t=0.0) == rank]
+            reqs = {i: self.add_request(prompts[i], params) for i in mine}
+        else:
+            reqs = {i: self.add_request(p, params) for i, p in enumerate(prompts)}
         dev = self.device if dist.get_backend(group) == "nccl" else torch.device("cpu")
-        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        delayed = 0
+        self.dp_log: list = []
         while True:
-            flag.fill_(1 if self.has_work() else 0)
-            dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
-            if int(flag.item()) == 0:
+            f = self.sched.facts()
+            row = torch.tensor(f[:5] + [delayed, f[5], int(self.has_work())], dtype=torch.int64, device=dev)
+            parts = [torch.empty_like(row) for _ in range(world)]
+            dist.all_gather(parts, row, group=group)
+            rows = [p.cpu().tolist() for p in parts]
+            if not any(r[7] for r in rows):
                 break
-            self.step()
-        return [r.output for r in reqs]
+            hold = dp_hold([RankFacts.from_row(r[:6]) for r in rows], self.ecfg.decode_burst,
+                           self.ecfg.burst_queue_cap, self.ecfg.max_delay_passes)
+            cap = prefill_budget([r[6] for r in rows], self.ecfg.chunked_prefill, min_tokens=min(
+                2048, self.ecfg.chunked_prefill), page=self.ecfg.page_size)
+            self.dp_log.append((hold, cap))
+            self.step(hold=hold, chunk_cap=cap)
+            delayed = delayed + 1 if hold else 0
+        if route:
+            return {i: r.output for i, r in reqs.items()}
+        return [r.output for r in reqs.values()]
 
     def generate(self, prompts: list, params: Optional[SamplingParams] = None, max_steps: int = 1 << 30) -> list:
         reqs = [self.add_request(p, params) for p in prompts]

@@ -18,6 +18,23 @@ from ..models.mla import MLAKVCache, MLAModel, MLAStep
 from ..ops import basic as B
 from ..ops.kvcache import FMT_FP8, FMT_NVFP4
 from .scheduler import Batch, Request, SamplingParams, Segment
+from ..ops.formats import INDEX_ROW_BYTES
+from ..ops.mla import ROW_BYTES as M_ROW_BYTES
+
+
+def pool_pages(ecfg: EngineConfig, need: int, page_bytes: int, device) -> int:
+    """KV pool size in 64-token pages: what `max_running` requests of `max_seq` need, bounded by
+    `max_total_tokens` when set, else by `mem_fraction` of the device memory still free at boot (less a reserve for
+    activations) -- the pool never claims memory the weights or the forward need."""
+    if ecfg.page_size != 64:
+        raise ValueError("KV pools use 64-token pages (page_size must be 64)")
+    if ecfg.max_total_tokens > 0:
+        return max(3, min(need, ecfg.max_total_tokens // 64 + 2))
+    if torch.device(device).type == "cuda":
+        free, _total = torch.cuda.mem_get_info(torch.device(device))
+        fit = int(max(0, free - (8 << 30)) * ecfg.mem_fraction) // max(1, page_bytes)
+        return max(3, min(need, fit))
+    return need
 
 
 class MLARunner:
@@ -45,9 +62,11 @@ class MLARunner:
         fmt = FMT_NVFP4 if ecfg.kv_dtype == "nvfp4" else FMT_FP8
         self.max_running = ecfg.max_running
         per_req = (max_seq + 64 + 63) // 64 + 1
-        pages = self.max_running * per_req + 2
+        pages = pool_pages(ecfg, self.max_running * per_req + 2,
+                           (cfg.num_layers + int(self.spec)) * 64 * (M_ROW_BYTES[fmt] + INDEX_ROW_BYTES), self.device)
         self.kv = MLAKVCache(cfg, self.device, fmt, self.max_running + 1, per_req, pages,
                              extra_layers=1 if self.spec else 0)
+        self.pool_tokens = 64 * (pages - 2)           # KV positions the pool holds (the boot-time capacity)
         self.dummy_row = self.max_running
         self.pages: dict[int, RequestPages] = {}
         self.graphs: dict = {}

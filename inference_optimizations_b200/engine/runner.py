@@ -24,6 +24,7 @@ from ..kv.allocator import DUMMY_PAGE, OutOfPages, RequestPages
 from ..models.gqa import GQAKVCache, GQAModel, StepTensors
 from ..ops import attention as A
 from ..ops import basic as B
+from ..ops import kvcache as K
 from .scheduler import SamplingParams, Batch, Request, Segment
 
 KINDS = ("global", "swa", "draft")
@@ -105,9 +106,16 @@ class GQARunner:
         self.max_running = ecfg.max_running
         w = cfg.sliding_window
         per_req_swa = (w + self.ecfg.chunked_prefill) // 64 + 3
-        if global_pages is None:
-            global_pages = self.max_running * ((max_seq + 64 + 63) // 64) + 2
         swa_pages = self.max_running * (w // 64 + 4) + per_req_swa + 2
+        if global_pages is None:
+            # global-layer pages (sliding-window pools are sized by the window): the requests' need, bounded by
+            # max_total_tokens / mem_fraction of the memory free at boot
+            from .mla_runner import pool_pages
+            fmt = K.FMT_IDS[ecfg.kv_dtype]
+            n_glob = sum(1 for i in range(cfg.num_layers) if cfg.is_global(i))
+            page_bytes = n_glob * (cfg.num_kv_heads_global // tp) * 2 * K.part_bytes(fmt, cfg.head_dim_global)
+            global_pages = pool_pages(ecfg, self.max_running * ((max_seq + 64 + 63) // 64) + 2, page_bytes, device)
+        self.pool_tokens = 64 * (global_pages - 2)
         self.kv = GQAKVCache(cfg, tp, device, ecfg.kv_dtype, self.max_running + 1, max_seq + 64, global_pages,
                              swa_pages, draft_pages=swa_pages if self.spec else 0)
         self.dummy_row = self.max_running

@@ -101,24 +101,36 @@ class Scheduler:
             self.on_admit(r)
         return r
 
-    def schedule(self) -> Optional[Batch]:
+    def schedule(self, hold: Optional[bool] = None, chunk_cap: int = 0) -> Optional[Batch]:
+        """hold: the decode-burst decision taken elsewhere (data-parallel ranks decide together, `burst.dp_hold`);
+        None = this scheduler's own rule.  chunk_cap: prefill tokens this pass may take (0 = the chunk size)."""
         # an unfinished chunked prefill always continues; otherwise admission follows the decode-burst rule
         if self.prefilling is None:
-            hold = hold_prefill(self.burst, self.streak, self.last_was_extend, bool(self.running))
+            if hold is None:
+                hold = hold_prefill(self.burst, self.streak, self.last_was_extend, bool(self.running))
             if not hold:
                 self.prefilling = self._admit()
         if self.prefilling is not None:
             self.streak = next_streak(self.burst, self.streak, True)
             self.last_was_extend = True
-            return self._prefill_chunk()
+            return self._prefill_chunk(chunk_cap)
         if self.running:
             self.streak = next_streak(self.burst, self.streak, False)
             self.last_was_extend = False
             return Batch("decode", [Segment(r, r.kv_len, [r.pending], True) for r in self.running])
         return None
 
-    def _prefill_chunk(self) -> Batch:
-        segs, budget = [], self.chunk
+    def facts(self) -> list:
+        """This scheduler's row of the data-parallel negotiation (`burst.RankFacts` order) plus its prefill backlog
+        (prompt tokens not yet in the pool, the `prefill_budget` input)."""
+        ext = -1 if self.last_was_extend is None else int(self.last_was_extend)
+        backlog = sum(r.prompt_len - r.prefilled for r in self.waiting)
+        if self.prefilling is not None:
+            backlog += self.prefilling.prompt_len - self.prefilling.prefilled
+        return [len(self.waiting), len(self.running), self.streak, ext, int(self.prefilling is not None), backlog]
+
+    def _prefill_chunk(self, cap: int = 0) -> Batch:
+        segs, budget = [], min(self.chunk, cap) if cap > 0 else self.chunk
         while self.prefilling is not None and budget > 0:
             r = self.prefilling
             n = min(budget, r.prompt_len - r.prefilled)

@@ -50,19 +50,20 @@ def _splitk_gemm(lin, x, xs, out, t: int, kc: int, kind: int) -> None:
     nt = FORCE["nt"] or MG.pick_nt(t)
     n_tiles = lin.N // (TILE * lin.g)
     ks = FORCE["ks"] or split_k(n_tiles, t, nt, kc, lin.num_ctas)
-    off, pairs = lin._index(t, x.device)
+    off, pairs, static = lin._index(t, x.device)
     f32 = out.dtype == torch.float32
     if ks == 1:
         MG.gemm(lin.wpack, x, xs, off, pairs, out, lin.status, n_tiles=n_tiles, kc=kc, g=lin.g, nt=nt,
                 mode=MODE_F32_SPLIT if f32 else 0, src_div=1, num_ctas=lin.num_ctas, kind=kind,
-                split_rows=t if f32 else 0)
+                split_rows=t if f32 else 0, static_index=static)
         return
     key = (t, ks)
     if key not in lin._parts:
         lin._parts[key] = torch.empty(ks * t, lin.N, dtype=torch.float32, device=x.device)
     part = lin._parts[key]
     MG.gemm(lin.wpack, x, xs, off, pairs, part, lin.status, n_tiles=n_tiles, kc=kc, g=lin.g, nt=nt,
-            mode=MODE_F32_SPLIT, src_div=1, num_ctas=lin.num_ctas, kind=kind, ksplit=ks, split_rows=t)
+            mode=MODE_F32_SPLIT, src_div=1, num_ctas=lin.num_ctas, kind=kind, ksplit=ks, split_rows=t,
+            static_index=static)
     ext().splitk_reduce(part, ks, out)
 
 
@@ -86,8 +87,8 @@ class DenseLinear:
 
     def _index(self, t: int, dev):
         if t not in self._rows:
-            self._rows[t] = (torch.tensor([0, t], dtype=torch.int32, device=dev),
-                             torch.arange(t, dtype=torch.int32, device=dev))
+            self._rows[t] = MG.static_index_tensors(lambda: (torch.tensor([0, t], dtype=torch.int32, device=dev),
+                                                             torch.arange(t, dtype=torch.int32, device=dev)))
         return self._rows[t]
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, out_f32: bool = False) -> torch.Tensor:
@@ -122,8 +123,8 @@ class Fp8Linear:
 
     def _index(self, t: int, dev):
         if t not in self._rows:
-            self._rows[t] = (torch.tensor([0, t], dtype=torch.int32, device=dev),
-                             torch.arange(t, dtype=torch.int32, device=dev))
+            self._rows[t] = MG.static_index_tensors(lambda: (torch.tensor([0, t], dtype=torch.int32, device=dev),
+                                                             torch.arange(t, dtype=torch.int32, device=dev)))
         return self._rows[t]
 
     def dequant(self) -> torch.Tensor:
@@ -276,10 +277,12 @@ class HeadBatchedLinear:
     def _index(self, t: int, dev):
         """off [H + 1] = h t; pairs[h t + j] = j H + h (output row of token j, head h)."""
         if t not in self._rows:
-            h = torch.arange(self.H, dtype=torch.int32, device=dev)
-            j = torch.arange(t, dtype=torch.int32, device=dev)
-            self._rows[t] = ((torch.arange(self.H + 1, dtype=torch.int32, device=dev) * t).contiguous(),
-                             (j[None, :] * self.H + h[:, None]).reshape(-1).contiguous())
+            def make():
+                h = torch.arange(self.H, dtype=torch.int32, device=dev)
+                j = torch.arange(t, dtype=torch.int32, device=dev)
+                return ((torch.arange(self.H + 1, dtype=torch.int32, device=dev) * t).contiguous(),
+                        (j[None, :] * self.H + h[:, None]).reshape(-1).contiguous())
+            self._rows[t] = MG.static_index_tensors(make)
         return self._rows[t]
 
     def __call__(self, x: torch.Tensor, t: int, row_stride: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -292,9 +295,9 @@ class HeadBatchedLinear:
         if t == 0:
             return out
         rows = x.reshape(-1).view(torch.uint8).view(-1, self.K * 2)
-        off, pairs = self._index(t, x.device)
+        off, pairs, static = self._index(t, x.device)
         MG.gemm(self.wpack, rows, rows, off, pairs, out.view(t * self.H, -1) if out.dim() == 3 else out, self.status,
                 n_tiles=self.N // (TILE * self.g), kc=self.K // 64, g=self.g, nt=MG.pick_nt(t), mode=0, src_div=1,
                 num_ctas=self.num_ctas, kind=2, src_group=self.H if rs != self.H else 0,
-                src_group_stride=rs if rs != self.H else 0)
+                src_group_stride=rs if rs != self.H else 0, static_index=static)
         return out

@@ -180,15 +180,31 @@ def gemm(wpack, x, x_scale, off, pairs, out, status, *, n_tiles: int, kc: int, g
          src_div: int, src_limit: int = 1 << 30, src_shared_base: int = 0, pair_w=None, out_scale=None, out_mul: float = 1.0,
          num_ctas: int = 148, kind: int = 0, expert_mul=None, out_peers=None, out_offset: int = 0, out_div: int = 1,
          out_rank: int = 0, out_shared_base: int = 0, pairs_total: int = 0, ksplit: int = 1,
-         split_rows: int = 0, src_group: int = 0, src_group_stride: int = 0) -> None:
-    """One grouped block-scaled GEMM launch (argument meanings: `MoeGemmArgs` in csrc/kernels.h).  When `TRACE` holds
-    an int64 CUDA tensor, CTA 0's phase timeline (clock64, `MgTraceEv` order) is written into it (diagnostics)."""
+         split_rows: int = 0, src_group: int = 0, src_group_stride: int = 0, static_index: bool = False) -> None:
+    """One grouped block-scaled GEMM launch (argument meanings: `MoeGemmArgs` in csrc/kernels.h).  Launched with
+    programmatic dependent launch unless `PDL` is off: the kernel sets up (and, with `static_index` -- off / pairs
+    complete before the previous kernel ran -- starts streaming weights) while the previous kernel finishes.  When
+    `TRACE` holds an int64 CUDA tensor, CTA 0's phase timeline (clock64, `MgTraceEv` order) is written into it."""
     ext().moe_gemm(wpack, x, x_scale, off, pairs, pair_w, out, out_scale, status, n_tiles, kc, g, nt, mode, src_div,
                    src_limit, src_shared_base, out_mul, num_ctas, kind, expert_mul, out_peers, out_offset, out_div, out_rank,
-                   out_shared_base, pairs_total, ksplit, split_rows, src_group, src_group_stride, TRACE[0])
+                   out_shared_base, pairs_total, ksplit, split_rows, src_group, src_group_stride, TRACE[0], PDL[0],
+                   static_index)
 
 
 TRACE: list = [None]
+PDL: list = [True]
+
+
+def static_index_tensors(make) -> tuple:
+    """Index tensors for a GEMM whose work list never changes (dense linears, head-batched products): built by
+    `make()` and, outside stream capture, completed before returning, so launches may read them before waiting on the
+    previous kernel.  -> (tensors..., complete flag)."""
+    t = make()
+    done = False
+    if torch.cuda.is_available() and t[0].is_cuda and not torch.cuda.is_current_stream_capturing():
+        torch.cuda.current_stream(t[0].device).synchronize()
+        done = True
+    return (*t, done)
 
 
 _TACTICS = None

@@ -66,3 +66,44 @@ def test_dp_attention_ep_moe_matches_single_process():
 
 def test_dp_ep_with_mtp_speculation():
     _run(spec=True)
+
+
+def _policy_worker(rank: int, port: int, q):
+    """generate_dp with the DP policies on: decode burst 3 (joint dp_hold), a prefill budget from the backlogs, and
+    cache-aware routing of the global prompt list."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2")
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    try:
+        ecfg = EngineConfig(model="tiny_mla", device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=32,
+                            cuda_graphs=False, ep=2, prefix_cache=False, decode_burst=3)
+        eng = Engine(ecfg, model_config("tiny_mla"), max_seq=256, ep_rank=rank, ep_group=dist.group.WORLD)
+        outs = eng.generate_dp(PROMPTS, SamplingParams(max_new_tokens=6), route=True)
+        q.put((rank, outs, eng.dp_log))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dp_policies_in_the_serving_loop():
+    """Routed prompts are each served once; every rank took the same hold / budget decision every pass; bursts held
+    prefill admission on some passes; greedy outputs equal the single-process engine's."""
+    ref = _engine(1, 0).generate(PROMPTS, SamplingParams(max_new_tokens=6))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_policy_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        rank, outs, log = q.get(timeout=600)
+        got[rank] = (outs, log)
+    for p in procs:
+        p.join(timeout=120)
+    served = {}
+    for rank in (0, 1):
+        served.update(got[rank][0])
+    assert sorted(served) == list(range(len(PROMPTS)))
+    assert set(got[0][0]).isdisjoint(got[1][0]) and got[0][0] and got[1][0]
+    assert all(served[i] == ref[i] for i in served), (served, ref)
+    assert got[0][1] == got[1][1]                     # identical joint decisions on both ranks
+    assert any(h for h, _ in got[0][1])               # decode bursts held prefill on some passes
