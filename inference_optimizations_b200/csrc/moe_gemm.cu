@@ -673,8 +673,9 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int* ids, int P, 
 // bf16 out.  w null: the rows already carry their routing weights.
 __global__ void moe_combine_kernel(const __nv_bfloat16* rows, int T, int topk, int H, int shared_base,
                                    const float* w, __nv_bfloat16* y) {
-  const int t = blockIdx.x;
-  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+  griddep_launch();
+  const int t = blockIdx.x;           // grid (T, column blocks): a decode step's few tokens still spread over SMs
+  for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < H / 8; c += gridDim.y * blockDim.x) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int k = 0; k <= topk; ++k) {
       if (k == topk && shared_base < 0) break;
@@ -871,8 +872,8 @@ cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_bas
                         cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   if (H % 8) return cudaErrorInvalidValue;
-  moe_combine_kernel<<<T, 128, 0, s>>>(static_cast<const __nv_bfloat16*>(rows), T, topk, H, shared_base, w,
-                                       static_cast<__nv_bfloat16*>(y));
+  moe_combine_kernel<<<dim3(T, (H / 8 + 127) / 128), 128, 0, s>>>(static_cast<const __nv_bfloat16*>(rows), T, topk,
+                                                                  H, shared_base, w, static_cast<__nv_bfloat16*>(y));
   return cudaGetLastError();
 }
 

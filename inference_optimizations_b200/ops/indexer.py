@@ -85,9 +85,11 @@ class IndexerWorkspace:
 
 def indexer_select(q8: torch.Tensor, w: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor,
                    limit: torch.Tensor, topk: int, max_ctx: int, req_idx: Optional[torch.Tensor] = None,
-                   ws: Optional[IndexerWorkspace] = None, tiles_per_cta: int = 32,
+                   ws: Optional[IndexerWorkspace] = None, tiles_per_cta: int = 0,
                    with_pos: bool = False):
-    """-> slots int32 [T, topk] (and positions with `with_pos`).  `max_ctx` bounds limit (fixed per CUDA graph)."""
+    """-> slots int32 [T, topk] (and positions with `with_pos`).  `max_ctx` bounds limit (fixed per CUDA graph).
+    tiles_per_cta 0: as many 128-position tiles per CTA as fill every SM about once (at most 32), so a decode step
+    of a few tokens still spreads its score pass over the GPU; depends only on (T, max_ctx), so graphs stay valid."""
     t = q8.shape[0]
     slots = torch.empty(t, topk, dtype=torch.int32, device=q8.device)
     pos = torch.empty(t, topk, dtype=torch.int32, device=q8.device) if with_pos else None
@@ -101,6 +103,8 @@ def indexer_select(q8: torch.Tensor, w: torch.Tensor, pool: torch.Tensor, page_t
     if ws is None:
         ws = IndexerWorkspace.allocate(t, max_ctx, q8.device)
     max_tiles = max(1, -(-max_ctx // TILE))
+    if tiles_per_cta <= 0:
+        tiles_per_cta = max(1, min(32, -(-t * max_tiles // 148)))
     ext().indexer(q8, w, pool, page_table, req_idx, limit, ws.scores, slots, pos, ws.status,
                   min(tiles_per_cta, max_tiles), max_tiles, 1, 1)
     return (slots, pos) if with_pos else slots

@@ -525,6 +525,80 @@ def _kernel_times(fn, reps: int = 5) -> dict:
     return res
 
 
+def _graph_time_flushed(fn, iters: int = 20) -> float:
+    """Mean device time of one CUDA-graph replay of fn (captured after two warm-up calls), L2 flushed by a 512 MB
+    read before each replay (not timed)."""
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return _time_flushed(g.replay, iters)
+
+
+def kv4mla_compare_case(tokens: list, topk: int = 2048, rows: int = 600000, heads: int = 64) -> list:
+    """This framework's sparse-MLA decode (csrc/attn_mla_decode.cu) against the reference's own sm_100 kernel
+    (kv4mla, fp8 mode), same box, same shapes: NVFP4 352-byte rows, `rows`-row pool, top-`topk` random rows per
+    token, `heads` query heads; both fed the same E4M3 query values, each replayed from a CUDA graph with the L2
+    flushed in between.  The reference module is the reference repository's kernel compiled unmodified into
+    baseline/kv4mla_build/ (git-ignored); absent -> the row says so."""
+    import glob
+    import importlib.util
+    from ..ops import kvcache as K
+    from ..ops import mla as M
+    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    so = sorted(glob.glob(os.path.join(root, "baseline", "kv4mla_build", "*", "kv4mla_ext_*.so")))
+    if not so:
+        return [{"kernel": "kv4mla_compare", "unavailable": "reference module not built into baseline/kv4mla_build"}]
+    spec = importlib.util.spec_from_file_location(os.path.basename(so[0]).split(".")[0], so[0])
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    dev = torch.device("cuda:0")
+    pool = mla_pool_random(rows, K.FMT_NVFP4, dev)
+    parts = int(ref.num_sm_parts(1))
+    sm = 1.0 / math.sqrt(576)
+    out_rows = []
+    for t in tokens:
+        g = torch.Generator(device=dev).manual_seed(t)
+        idx = torch.randint(0, rows, (t, topk), generator=g, device=dev, dtype=torch.int32)
+        q8 = (torch.randn(t, heads, 576, generator=g, device=dev)).to(torch.float8_e4m3fn)
+        qb = q8.float().to(torch.bfloat16)                       # the same query values for both kernels
+        ours_out = torch.empty(t, heads, 512, dtype=torch.bfloat16, device=dev)
+        splits = M.mla_split_policy(t, topk)
+        ws = M.MlaWorkspace.allocate(t, heads, splits[0], device=dev)
+
+        def ours():
+            M.mla_decode(qb, pool, idx, sm, K.FMT_NVFP4, splits=splits, ws=ws, out=ours_out)
+        # the reference's split rule (kv4mla.py split_policy / sched_overhead), its workspace layout
+        split = topk > 640 and not (96 <= t <= 136 or t >= 224)
+        ref_out = torch.empty(t, 1, heads, 512, dtype=torch.bfloat16, device=dev)
+        ref_lse = torch.empty(t, 1, heads, dtype=torch.float32, device=dev)
+        meta = ns = oa = la = None
+        if split:
+            meta = torch.empty(parts, 8, dtype=torch.int32, device=dev)
+            ns = torch.empty(t + 1, dtype=torch.int32, device=dev)
+            ref.sched_meta(t, 1, topk, None, meta, ns, 10 if t <= 16 else 5)
+            oa = torch.empty(t + parts, 1, heads, 512, dtype=torch.float32, device=dev)
+            la = torch.empty(t + parts, 1, heads, dtype=torch.float32, device=dev)
+        q4 = q8.view(t, 1, heads, 576)
+        idx3 = idx.view(t, 1, topk)
+
+        def theirs():
+            ref.sparse_decode(q4, pool, idx3, None, float(sm), ref_out, ref_lse, meta, ns, oa, la, True)
+        us_ours = _graph_time_flushed(ours)
+        us_ref = _graph_time_flushed(theirs)
+        ours()
+        theirs()
+        torch.cuda.synchronize()
+        cos = torch.nn.functional.cosine_similarity(ours_out.float().flatten(), ref_out.float().flatten(), dim=0)
+        out_rows.append({"kernel": "kv4mla_compare", "tokens": t, "heads": heads, "topk": topk, "pool_rows": rows,
+                         "ours_us": round(us_ours, 2), "kv4mla_us": round(us_ref, 2),
+                         "ratio_ref_over_ours": round(us_ref / us_ours, 3), "ours_splits": list(splits),
+                         "kv4mla_split": split, "output_cosine": round(cos.item(), 5)})
+    return out_rows
+
+
 def dsa_profile_case(layers: int, sessions: int, ctx: int, steps: int, prefill: int, top: int = 40) -> dict:
     """Per-kernel device time of the DSA-MoE serving step (the bench's engine: DP attention + EP over the launched
     ranks, CUDA-graph decode), from the CUDA activity records of the torch profiler (kernel durations as CUPTI reports
@@ -645,6 +719,10 @@ def main() -> None:
                     row.update(nt=nt, ks=ks)
                     print(json.dumps(row), flush=True)
         L.FORCE.update(nt=None, ks=None)
+        r = {}
+    elif a.kernel == "kv4mla_compare":
+        for row in kv4mla_compare_case([int(v) for v in a.tokens.split(",")], a.topk, heads=a.heads):
+            print(json.dumps(row), flush=True)
         r = {}
     elif a.kernel == "dsa_profile":
         import torch.distributed as dist
