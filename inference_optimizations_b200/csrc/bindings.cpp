@@ -773,7 +773,7 @@ void nvfp4_lut_test(const at::Tensor& words, at::Tensor out) {
 void mla_prep_kv(const at::Tensor& ya, const at::Tensor& q_norm, const at::Tensor& kv_norm, const at::Tensor& ik_w,
                  const at::Tensor& ik_b, const at::Tensor& rope, const at::Tensor& pos, const at::Tensor& slot,
                  at::Tensor qa_out, at::Tensor latent_pool, at::Tensor index_pool, at::Tensor iw_out, double iw_scale,
-                 int64_t q_lora, int64_t Hi, double eps) {
+                 int64_t q_lora, int64_t Hi, double eps, const c10::optional<at::Tensor>& lat_slot) {
   req(ya, at::kBFloat16, "ya");
   req(rope, at::kFloat, "rope");
   req(pos, at::kInt, "pos");
@@ -802,6 +802,11 @@ void mla_prep_kv(const at::Tensor& ya, const at::Tensor& q_norm, const at::Tenso
   a.rope = rope.data_ptr<float>();
   a.pos = pos.data_ptr<int>();
   a.slot = slot.data_ptr<int>();
+  if (lat_slot.has_value()) {
+    req(*lat_slot, at::kInt, "lat_slot");
+    TORCH_CHECK(lat_slot->numel() == T, "lat_slot [T]");
+    a.lat_slot = lat_slot->data_ptr<int>();
+  }
   a.qa_out = qa_out.data_ptr();
   a.latent_pool = latent_pool.data_ptr<uint8_t>();
   a.latent_fmt = latent_pool.size(1) == 352 ? iob::kKvNvfp4 : iob::kKvFp8;

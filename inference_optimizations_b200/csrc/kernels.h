@@ -232,6 +232,8 @@ struct MlaPrepArgs {
   const float* rope;          // fp32 [max_pos, 64]: cos (32) | sin (32)
   const int* pos;             // [T]
   const int* slot;            // [T] pool slot (-1: not written)
+  const int* lat_slot;        // [T] latent pool row when it differs from `slot` (context parallelism: the owning
+                              // rank's local row, -1 elsewhere); null = slot
   void* qa_out;               // bf16 [T, q_lora]
   uint8_t* latent_pool;       // [slots, 352] NVFP4 or [slots, 576] E4M3
   int latent_fmt;

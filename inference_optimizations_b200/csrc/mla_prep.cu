@@ -46,6 +46,7 @@ __global__ void __launch_bounds__(256) mla_prep_kv_kernel(const MlaPrepArgs a) {
   const int pos = a.pos[t];
   const float* cs = a.rope + static_cast<size_t>(pos) * 64;
   const int slot = a.slot[t];
+  const int lat_slot = a.lat_slot ? a.lat_slot[t] : slot;
   __shared__ float red[4];
   if (warp < 4) {
     // ---------------------------------------------------------------- q_a RMSNorm (128 threads)
@@ -80,9 +81,9 @@ __global__ void __launch_bounds__(256) mla_prep_kv_kernel(const MlaPrepArgs a) {
     const float x1 = bfv(kv, 512 + lane), x2 = bfv(kv, 512 + 32 + lane);
     const float c = cs[lane], s = cs[32 + lane];
     const float r1 = rbf(x1 * c - x2 * s), r2 = rbf(x2 * c + x1 * s);
-    if (slot >= 0) {
+    if (lat_slot >= 0) {
       if (a.latent_fmt == kKvNvfp4) {
-        uint8_t* row = a.latent_pool + static_cast<size_t>(slot) * 352;
+        uint8_t* row = a.latent_pool + static_cast<size_t>(lat_slot) * 352;
         float amax = 0.f;
 #pragma unroll
         for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
@@ -98,7 +99,7 @@ __global__ void __launch_bounds__(256) mla_prep_kv_kernel(const MlaPrepArgs a) {
         row[288 + lane] = float_to_e4m3(r1);
         row[288 + 32 + lane] = float_to_e4m3(r2);
       } else {
-        uint8_t* row = a.latent_pool + static_cast<size_t>(slot) * 576;
+        uint8_t* row = a.latent_pool + static_cast<size_t>(lat_slot) * 576;
         uint32_t wq[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {

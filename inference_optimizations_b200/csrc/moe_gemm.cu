@@ -681,6 +681,7 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* rows, int T, int topk, i
       if (k == topk && shared_base < 0) break;
       const size_t r = k < topk ? static_cast<size_t>(t) * topk + k : static_cast<size_t>(shared_base) + t;
       const float wk = (k < topk && w) ? w[t * topk + k] : 1.f;
+      if (wk == 0.f) continue;        // a pair this launch did not compute (experts of other ranks): row unwritten
       const uint4 u = *reinterpret_cast<const uint4*>(rows + r * H + c * 8);
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll

@@ -39,7 +39,7 @@ def pool_pages(ecfg: EngineConfig, need: int, page_bytes: int, device) -> int:
 
 class MLARunner:
     def __init__(self, cfg: MLAMoEConfig, ecfg: EngineConfig, device, max_seq: int, tp_rank: int = 0, tp: int = 1,
-                 ep_rank: int = 0, ep_group=None):
+                 ep_rank: int = 0, ep_group=None, dcp_rank: int = 0, dcp_group=None):
         """ecfg.ep > 1: data-parallel attention + expert-parallel MoE.  Every rank runs its own requests (its own
         scheduler, pools and replicated attention weights); every MoE layer is an exchange over `ep_group` with
         `ecfg.ep` ranks, so all ranks step in lockstep: before each forward the ranks agree on the largest token
@@ -52,7 +52,14 @@ class MLARunner:
         self.max_seq = max_seq
         self.spec = bool(ecfg.spec) and cfg.draft_layers >= 1
         self.ep_world, self.ep_rank, self.ep_group = max(1, ecfg.ep), ep_rank, ep_group
-        self.model = MLAModel(cfg, self.device, ecfg.seed, ep_rank=ep_rank, ep_world=self.ep_world)
+        # decode context parallelism (ecfg.dcp ranks, every rank runs the same requests): KV sharded by position
+        self.dcp_world, self.dcp_rank = max(1, ecfg.dcp), dcp_rank
+        if self.dcp_world > 1 and (self.spec or self.ep_world > 1):
+            raise NotImplementedError("decode context parallelism runs without speculation or expert parallelism")
+        self.model = MLAModel(cfg, self.device, ecfg.seed, ep_rank=ep_rank, ep_world=self.ep_world,
+                              dcp_rank=dcp_rank, dcp_world=self.dcp_world)
+        if self.dcp_world > 1:
+            self.model.attach_dcp(dcp_group, max(2 * ecfg.max_running, ecfg.chunked_prefill))
         if self.spec:
             self.model.build_draft(ecfg.seed)
         if self.ep_world > 1:
@@ -65,7 +72,7 @@ class MLARunner:
         pages = pool_pages(ecfg, self.max_running * per_req + 2,
                            (cfg.num_layers + int(self.spec)) * 64 * (M_ROW_BYTES[fmt] + INDEX_ROW_BYTES), self.device)
         self.kv = MLAKVCache(cfg, self.device, fmt, self.max_running + 1, per_req, pages,
-                             extra_layers=1 if self.spec else 0)
+                             extra_layers=1 if self.spec else 0, latent_div=self.dcp_world)
         self.pool_tokens = 64 * (pages - 2)           # KV positions the pool holds (the boot-time capacity)
         self.dummy_row = self.max_running
         self.pages: dict[int, RequestPages] = {}
@@ -308,7 +315,8 @@ class MLARunner:
     def _graphable(self) -> bool:
         """Graphs need every FFN on the block-scaled expert kernels (the bf16 reference MoE path groups tokens on
         the host)."""
-        return (self.ecfg.cuda_graphs and self.device.type == "cuda" and not self.spec
+        # context parallelism: the merge and reduce kernels pick their buffer half on the host, per call
+        return (self.ecfg.cuda_graphs and self.device.type == "cuda" and not self.spec and self.dcp_world == 1
                 and all(self.model._quantized_ffn(i) for i in range(self.cfg.num_layers)))
 
     def _decode_body(self, st: MLAStep, out: torch.Tensor) -> None:

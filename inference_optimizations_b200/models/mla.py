@@ -95,11 +95,14 @@ class MLAStep:
 
 class MLAKVCache:
     def __init__(self, cfg: MLAMoEConfig, device, fmt: int, rows: int, max_pages: int, pages: int,
-                 extra_layers: int = 0):
+                 extra_layers: int = 0, latent_div: int = 1):
+        """latent_div S > 1 (decode context parallelism): this rank's latent pools hold the rows it owns, 1 / S of
+        the page space (pool row v at local row v // S); the index pools stay whole (every rank scores every row)."""
         self.cfg, self.device, self.fmt = cfg, torch.device(device), fmt
         rb = M.ROW_BYTES[fmt]
         n = cfg.num_layers + extra_layers           # extra: the MTP draft layer's pools (same page ids)
-        self.latent = [torch.zeros(pages * 64, rb, dtype=torch.uint8, device=self.device) for _ in range(n)]
+        lat_rows = -(-pages * 64 // latent_div)
+        self.latent = [torch.zeros(lat_rows, rb, dtype=torch.uint8, device=self.device) for _ in range(n)]
         self.index = [torch.zeros(pages, K.INDEX_PAGE_BYTES, dtype=torch.uint8, device=self.device)
                       for _ in range(n)]
         from ..kv.allocator import PageAllocator, PageTable
@@ -114,17 +117,26 @@ class MLAKVCache:
 
 class MLAModel:
     def __init__(self, cfg: MLAMoEConfig, device, seed: int = 0, ep_rank: int = 0, ep_world: int = 1,
-                 keep_master: Optional[bool] = None):
+                 keep_master: Optional[bool] = None, dcp_rank: int = 0, dcp_world: int = 1):
         """ep_world > 1: this rank holds routed experts [ep_rank E / ep_world, (ep_rank + 1) E / ep_world) of every
         MoE layer (plus the shared expert); attention, router and dense layers are replicated.
+        dcp_world > 1 (decode context parallelism; every rank runs the same tokens): the latent KV is sharded by the
+        owner rule, the attention output is merged per head group over peer memory, W_UV / W_o are split by head
+        group, the routed experts by rank (shared expert on rank 0), the dense FFNs by FFN columns; the partial
+        outputs are summed by a fused all-reduce + norm (`attach_dcp`).
         keep_master: keep the bf16 weights next to the kernels' packed copies (default: only for models under 2 G
         parameters -- test-size models, whose weights `copy_from` moves between devices)."""
         self.cfg, self.device = cfg, torch.device(device)
         h, c = cfg.hidden, cfg
-        if c.num_experts % ep_world:
-            raise ValueError("experts must divide evenly over the expert-parallel ranks")
+        if ep_world > 1 and dcp_world > 1:
+            raise ValueError("expert parallelism and decode context parallelism are separate deployments")
+        if c.num_experts % max(ep_world, dcp_world) or c.num_heads % dcp_world or c.dense_ffn % (128 * dcp_world):
+            raise ValueError("experts / heads / dense FFN columns must divide evenly over the ranks")
         self.ep_rank, self.ep_world = ep_rank, ep_world
-        self.e_lo, self.e_hi = ep_rank * c.num_experts // ep_world, (ep_rank + 1) * c.num_experts // ep_world
+        self.dcp_rank, self.dcp_world = dcp_rank, dcp_world
+        self.dcp = None                                  # attach_dcp(): merge + reduce communicators
+        pr, pw = (dcp_rank, dcp_world) if dcp_world > 1 else (ep_rank, ep_world)
+        self.e_lo, self.e_hi = pr * c.num_experts // pw, (pr + 1) * c.num_experts // pw
         self.ep = None                                   # set by attach_ep(): per-layer expert-parallel MoE
         self.seed = seed
         self.keep_master = keep_master if keep_master is not None else c.num_params() < 2e9
@@ -167,12 +179,13 @@ class MLAModel:
             c.num_heads, c.qk_nope + c.v_head, c.kv_lora)
         moe = c.is_moe(i)
         F = c.expert_ffn
+        shared = c.num_shared and self.dcp_rank == 0     # context parallelism: the shared expert runs on rank 0
         if moe:
             ffn = {"gate": r(f"{prefix}.gate", (c.num_experts, h)),
                    "e_bias": torch.zeros(c.num_experts, dtype=torch.float32, device=self.device),
                    "w_gu": None, "w_down": None,
-                   "shared_gu": r(f"{prefix}.shared.gu", (2 * F * c.num_shared, h)) if c.num_shared else None,
-                   "shared_down": r(f"{prefix}.shared.down", (h, F * c.num_shared)) if c.num_shared else None}
+                   "shared_gu": r(f"{prefix}.shared.gu", (2 * F * c.num_shared, h)) if shared else None,
+                   "shared_down": r(f"{prefix}.shared.down", (h, F * c.num_shared)) if shared else None}
             if self.keep_master or not self._quantized_ffn(i):
                 ffn["w_gu"] = _rand_experts(f"{prefix}.experts.gu", self.e_lo, self.e_hi, (2 * F, h), c.init_std,
                                             self.device, self.seed)
@@ -180,6 +193,11 @@ class MLAModel:
                                               self.device, self.seed)
         else:
             ffn = {"w_gu": r(f"{prefix}.mlp.gu", (2 * c.dense_ffn, h)), "w_down": r(f"{prefix}.mlp.down", (h, c.dense_ffn))}
+            if self.dcp_world > 1:                      # this rank's FFN columns (gate and up rows, down columns)
+                D, S, rk = c.dense_ffn, self.dcp_world, self.dcp_rank
+                lo, hi = rk * D // S, (rk + 1) * D // S
+                ffn["w_gu"] = torch.cat([ffn["w_gu"][lo:hi], ffn["w_gu"][D + lo:D + hi]]).contiguous()
+                ffn["w_down"] = ffn["w_down"][:, lo:hi].contiguous()
         w = MLALayerWeights(
             n_in=ones(h), n_post=ones(h),
             wq_a=r(f"{prefix}.wq_a", (c.q_lora, h)), q_norm=ones(c.q_lora),
@@ -193,6 +211,11 @@ class MLAModel:
             wi_kb=torch.zeros(c.index_dim, dtype=torch.bfloat16, device=self.device),
             wi_w=r(f"{prefix}.wi_w", (c.index_heads, h)), ffn=ffn)
         del wkv_b
+        if self.dcp_world > 1:                          # this rank's head group feeds a row-parallel W_UV / W_o
+            Hg = c.num_heads // self.dcp_world
+            g0 = self.dcp_rank * Hg
+            w.w_uv = w.w_uv[g0:g0 + Hg].contiguous()
+            w.wo = w.wo[:, g0 * c.v_head:(g0 + Hg) * c.v_head].contiguous()
         idx = len(self.layers)
         if self._quantized_ffn(i) and self.cuda:
             self._bs[idx] = self._build_ffn(prefix, i, ffn)
@@ -212,7 +235,7 @@ class MLAModel:
         from ..ops.moe_gemm import BlockScaledExperts
         c = self.cfg
         if not c.is_moe(i):
-            F = c.dense_ffn
+            F = ffn["w_gu"].shape[0] // 2                # the FFN columns this rank holds
             return BlockScaledExperts(ffn["w_gu"][None, :F], ffn["w_gu"][None, F:], ffn["w_down"][None],
                                       fmt=c.weight_dtype)
         F = c.expert_ffn
@@ -438,10 +461,76 @@ class MLAModel:
     def _o_proj(self, w: MLALayerWeights, o_lat: torch.Tensor, t: int) -> torch.Tensor:
         c = self.cfg
         if w.k is not None and "uv" in w.k:
-            o = w.k["uv"](o_lat, t).view(t, c.num_heads * c.v_head)
+            o = w.k["uv"](o_lat, t).view(t, -1)
         else:
-            o = torch.einsum("thk,hkv->thv", o_lat.float(), w.w_uv.float()).to(torch.bfloat16).reshape(t, -1)
+            wuv = w.w_uv if w.w_uv.device == o_lat.device else w.w_uv.to(o_lat.device)
+            o = torch.einsum("thk,hkv->thv", o_lat.float(), wuv.float()).to(torch.bfloat16).reshape(t, -1)
         return w.k["o"](o) if w.k is not None else Fn.linear(o, w.wo)
+
+    # ------------------------------------------------------------------------------------------ context parallel
+    def attach_dcp(self, group, T_max: int) -> None:
+        """Decode context parallelism over `group` (a collective; every rank runs the same tokens): on CUDA the
+        owned-row decode + peer-memory merge (`parallel/dcp.DCPAttention`) and the fused peer-memory all-reduce +
+        residual + norm (`parallel/symm.TPComm`); elsewhere their collective references (gloo on CPU)."""
+        from ..parallel import dcp as D
+        c = self.cfg
+        if self.cuda:
+            from ..parallel.symm import TPComm
+            self.dcp = D.DCPAttention(self.dcp_rank, self.dcp_world, T_max, c.num_heads, self.device, group)
+            self.dcp_comm = TPComm(self.dcp_rank, self.dcp_world, T_max, c.hidden, self.device, group)
+        else:
+            self.dcp = D.DCPAttentionRef(self.dcp_rank, self.dcp_world, c.num_heads, group)
+            self.dcp_comm = None
+        self.dcp_group = group
+
+    def _dcp_reduce(self, partial: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor) -> torch.Tensor:
+        """h += sum over ranks of partial (every rank's share of a row-parallel product); -> rmsnorm(h, norm_w)."""
+        t, eps = partial.shape[0], self.cfg.rms_eps
+        if self.dcp_comm is not None:
+            buf = self.dcp_comm.out_buffer(t)
+            if buf.data_ptr() != partial.data_ptr():
+                buf.copy_(partial)
+            return self.dcp_comm.reduce_norm2(t, h, None, norm_w, eps, plus_one=False)
+        import torch.distributed as dist
+        p32 = partial.float()
+        dist.all_reduce(p32, group=self.dcp_group)
+        return B.rmsnorm(p32.to(torch.bfloat16), norm_w, eps, residual=h)
+
+    def _ffn_dcp(self, i: int, x: torch.Tensor) -> torch.Tensor:
+        """This rank's share of layer i's FFN for every token: its routed experts (pairs routed elsewhere weigh 0)
+        plus the shared expert on rank 0, or its dense FFN columns.  -> partial [T, H] (summed over the ranks)."""
+        c, f = self.cfg, self.layers[i].ffn
+        t = x.shape[0]
+        if not c.is_moe(i):
+            if self._quantized_ffn(i):
+                ids = torch.zeros(t, 1, dtype=torch.int32, device=x.device)
+                return self._block_scaled(i).forward(x, ids, torch.ones(t, 1, device=x.device))
+            return MOE.swiglu(x, f["w_gu"], f["w_down"])
+        logits = self._router_logits(i, x)
+        ids, w = MOE.route(logits, f["e_bias"], c.topk, c.n_group, c.topk_group, c.routed_scale, c.router)
+        local = (ids >= self.e_lo) & (ids < self.e_hi)
+        w = torch.where(local, w, torch.zeros_like(w))
+        if self._quantized_ffn(i):
+            return self._block_scaled(i).forward(x, ids.to(torch.int32).contiguous(), w, e0=self.e_lo)
+        out = MOE.experts_ref(x, ids, w, f["w_gu"], f["w_down"], self.e_lo)
+        if f["shared_gu"] is not None:
+            out += MOE.swiglu(x, f["shared_gu"], f["shared_down"]).float()
+        return out.to(torch.bfloat16)
+
+    def _layer_forward_dcp(self, i: int, h: torch.Tensor, x: torch.Tensor, st: MLAStep, kv: MLAKVCache,
+                           next_norm: torch.Tensor) -> torch.Tensor:
+        """One layer under decode context parallelism: the replicated query and top-k, the latent row written by its
+        owner only (pool row v -> rank v % S, local row v // S), sparse attention over the owned rows merged for
+        this rank's head group, row-parallel W_UV / W_o and FFN shares summed by the fused all-reduce + norm."""
+        c, w = self.cfg, self.layers[i]
+        t = x.shape[0]
+        S, rk = self.dcp_world, self.dcp_rank
+        lat_slot = torch.where((st.slot >= 0) & (st.slot % S == rk), st.slot // S,
+                               torch.full_like(st.slot, -1)).to(torch.int32)
+        qf, sel = (self._query_fused if self._fused_glue(w) else self._query_torch)(i, x, st, kv, lat_slot)
+        o_g = self.dcp.decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt)          # [T, H / S, 512] merged
+        x2 = self._dcp_reduce(self._o_proj(w, o_g.contiguous(), t), h, w.n_post)   # h += attn; x2 = norm_post(h)
+        return self._dcp_reduce(self._ffn_dcp(i, x2), h, next_norm)                 # h += ffn; next norm
 
     def _fused_glue(self, w: MLALayerWeights) -> bool:
         """The two fused glue kernels (csrc/mla_prep.cu) serve this layer: CUDA kernels for every projection, the
@@ -451,12 +540,14 @@ class MLAModel:
         return (self.fuse_glue and w.k is not None and "uk" in w.k and c.qk_rope == 64 and c.kv_lora == 512
                 and c.index_dim == 128)
 
-    def _layer_forward_fused(self, i: int, h: torch.Tensor, x: torch.Tensor, st: MLAStep, kv: MLAKVCache,
-                             next_norm: torch.Tensor) -> torch.Tensor:
-        """layer_forward with the attention block's glue in two kernels: x -> (q_a | kv_a | k_i | w_i) -> [q_a norm,
-        latent norm + k_pe RoPE + pool write, index key LayerNorm + RoPE + pool write, head weights]; q_a ->
-        (q_nope | q_pe | q_i); q_nope W_UK written straight into the attention query's first 512 columns; then
-        [q_pe RoPE into the query's last 64 columns, index query RoPE + E4M3 quantization]."""
+    def _query_fused(self, i: int, x: torch.Tensor, st: MLAStep, kv: MLAKVCache,
+                     lat_slot: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """The attention block up to the sparse-attention inputs with the glue in two kernels: x -> (q_a | kv_a | k_i
+        | w_i) -> [q_a norm, latent norm + k_pe RoPE + pool write, index key LayerNorm + RoPE + pool write, head
+        weights]; q_a -> (q_nope | q_pe | q_i); q_nope W_UK written straight into the attention query's first 512
+        columns; then [q_pe RoPE into its last 64 columns, index query RoPE + E4M3 quantization]; the indexer's
+        top-k.  -> (query bf16 [T, H, 576], selected pool slots int32 [T, topk]).  lat_slot: latent pool rows when
+        they differ from the token slots (context parallelism)."""
         from .._ext import ext
         c, w = self.cfg, self.layers[i]
         t, dev, eps = x.shape[0], x.device, c.rms_eps
@@ -465,7 +556,8 @@ class MLAModel:
         qa = torch.empty(t, c.q_lora, dtype=torch.bfloat16, device=dev)
         iw = torch.empty(t, c.index_heads, dtype=torch.float32, device=dev)
         ext().mla_prep_kv(ya, w.q_norm, w.kv_norm, w.wi_kn, w.wi_kb, cs, st.pos, st.slot, qa, kv.latent[i],
-                          kv.index[i], iw, c.index_heads ** -0.5 * c.index_dim ** -0.5, c.q_lora, c.index_heads, eps)
+                          kv.index[i], iw, c.index_heads ** -0.5 * c.index_dim ** -0.5, c.q_lora, c.index_heads, eps,
+                          lat_slot)
         yb = w.k["b"].lin(qa)
         qf = torch.empty(t, c.num_heads, 576, dtype=torch.bfloat16, device=dev)
         w.k["uk"](yb, t, row_stride=w.k["b_stride"], out=qf.view(t * c.num_heads, 576)[:, :512])
@@ -474,16 +566,12 @@ class MLAModel:
         ext().mla_prep_q(yb, cs, st.pos, qf, q8, w_eff, iw, c.num_heads, c.qk_nope, c.index_heads)
         sel = I.indexer_select(q8, w_eff, kv.index[i], kv.table.dev, st.limit, c.index_topk, st.max_ctx,
                                req_idx=st.req_idx, ws=kv.idx_ws.get((t, st.max_ctx)))
-        o_lat = M.mla_decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt, ws=kv.mla_ws.get((t, c.index_topk)))
-        x2 = B.rmsnorm(self._o_proj(w, o_lat, t), w.n_post, eps, residual=h)
-        f = self._ffn(i, x2)
-        return B.rmsnorm(f, next_norm, eps, residual=h)
+        return qf, sel
 
-    def layer_forward(self, i: int, h: torch.Tensor, x: torch.Tensor, st: MLAStep, kv: MLAKVCache,
-                      next_norm: torch.Tensor) -> torch.Tensor:
-        """x = norm_in(h); h updated in place.  Returns the next norm of h."""
-        if self._fused_glue(self.layers[i]):
-            return self._layer_forward_fused(i, h, x, st, kv, next_norm)
+    def _query_torch(self, i: int, x: torch.Tensor, st: MLAStep, kv: MLAKVCache,
+                     lat_slot: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """The same as `_query_fused` through torch ops and the separate writer kernels (CPU, and shapes the fused
+        kernels do not take)."""
         c, w = self.cfg, self.layers[i]
         t = x.shape[0]
         eps = c.rms_eps
@@ -494,7 +582,7 @@ class MLAModel:
         q_pe = self._rope(q_pe, st.pos, cs)
         lat = B.rmsnorm(kva[:, :c.kv_lora].contiguous(), w.kv_norm, eps)
         k_pe = self._rope(kva[:, None, c.kv_lora:], st.pos, cs)[:, 0]
-        K.mla_write(lat, k_pe.contiguous(), st.slot, kv.latent[i])
+        K.mla_write(lat, k_pe.contiguous(), st.slot if lat_slot is None else lat_slot, kv.latent[i])
         # DSA indexer
         iq = torch.cat([self._rope(iq[..., :c.qk_rope], st.pos, cs), iq[..., c.qk_rope:]], dim=-1)
         ik = Fn.layer_norm(ik_.float(), (c.index_dim,), w.wi_kn.float(), w.wi_kb.float(), eps)
@@ -505,8 +593,17 @@ class MLAModel:
         q8, w_eff = I.indexer_q_quant(iq, iw)
         sel = I.indexer_select(q8, w_eff, kv.index[i], kv.table.dev, st.limit, c.index_topk, st.max_ctx,
                                req_idx=st.req_idx, ws=kv.idx_ws.get((t, st.max_ctx)))
+        return torch.cat([q_lat, q_pe], dim=-1).contiguous(), sel
+
+    def layer_forward(self, i: int, h: torch.Tensor, x: torch.Tensor, st: MLAStep, kv: MLAKVCache,
+                      next_norm: torch.Tensor) -> torch.Tensor:
+        """x = norm_in(h); h updated in place.  Returns the next norm of h."""
+        if self.dcp is not None:
+            return self._layer_forward_dcp(i, h, x, st, kv, next_norm)
+        c, w = self.cfg, self.layers[i]
+        t, eps = x.shape[0], c.rms_eps
+        qf, sel = (self._query_fused if self._fused_glue(w) else self._query_torch)(i, x, st, kv)
         # absorbed sparse attention over the latent pool
-        qf = torch.cat([q_lat, q_pe], dim=-1).contiguous()
         o_lat = M.mla_decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt, ws=kv.mla_ws.get((t, c.index_topk)))
         x2 = B.rmsnorm(self._o_proj(w, o_lat, t), w.n_post, eps, residual=h)   # h += attn; x2 = norm_post(h)
         f = self._ffn(i, x2)

@@ -378,8 +378,10 @@ class BlockScaledExperts:
         ext().rmsnorm_quant(x.contiguous(), None, 0.0, 0.0, xq, xs, self.kind)
         return xq, xs
 
-    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, nt: int | None = None) -> torch.Tensor:
-        """x bf16 [T, H] (already normalized), ids int32 [T, k] (expert ids in [0, E)), w fp32 [T, k] -> bf16 [T, H]."""
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, nt: int | None = None,
+                e0: int = 0) -> torch.Tensor:
+        """x bf16 [T, H] (already normalized), ids int32 [T, k] (expert ids; this set holds experts e0 .. e0 + E - 1:
+        pairs routed to others are not computed and must carry weight 0), w fp32 [T, k] -> bf16 [T, H]."""
         t, k = ids.shape
         dev = x.device
         P = t * k
@@ -388,7 +390,7 @@ class BlockScaledExperts:
         xq, xs = self._quant_x(x)
         off = torch.empty(E + 1, dtype=torch.int32, device=dev)
         pairs = torch.empty(P + extra, dtype=torch.int32, device=dev)
-        ext().moe_align(ids.contiguous().view(-1), 0, self.E, extra, off, pairs)
+        ext().moe_align(ids.contiguous().view(-1), e0, self.E, extra, off, pairs)
         nt = nt or tactic_nt(t, self.fmt) or pick_nt(max(1, -(-2 * P // self.E)))
         kc1 = self.H // (TILE if self.kind == 0 else 2 * TILE)
         kc2 = self.F // (TILE if self.kind == 0 else 2 * TILE)

@@ -137,3 +137,30 @@ class DCPAttention:
     def check(self) -> None:
         if int(self.status.item()) != 0:
             raise RuntimeError(f"DCP merge: status {int(self.status.item())} (a peer did not arrive)")
+
+
+class DCPAttentionRef:
+    """Collective reference of `DCPAttention` for any backend (gloo on CPU): each rank decodes over the rows it owns,
+    the (o, lse) partials of every rank are all-gathered and merged in fp32 (`merge_partials_ref`), and the rank keeps
+    its head group -- the same inputs and outputs as the peer-memory path."""
+
+    def __init__(self, rank: int, S: int, H: int, group=None):
+        self.rank, self.S, self.H, self.Hg, self.group = rank, S, H, H // S, group
+
+    def decode(self, q: torch.Tensor, local_pool: torch.Tensor, sel: torch.Tensor, sm_scale: float, fmt: int,
+               lse_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        from ..ops import mla as M
+        local = owned_local_rows(sel, self.rank, self.S).int()
+        o, lse = M.mla_decode(q, local_pool, local, sm_scale, fmt, return_lse=True)
+        os_ = [torch.empty_like(o, dtype=torch.float32) for _ in range(self.S)]
+        ls = [torch.empty_like(lse) for _ in range(self.S)]
+        dist.all_gather(os_, o.float().contiguous(), group=self.group)
+        dist.all_gather(ls, lse.contiguous(), group=self.group)
+        om, lm = merge_partials_ref(os_, ls)
+        g0 = self.rank * self.Hg
+        if lse_out is not None:
+            lse_out.copy_(lm[:, g0:g0 + self.Hg])
+        return om[:, g0:g0 + self.Hg].to(torch.bfloat16)
+
+    def check(self) -> None:
+        pass

@@ -76,3 +76,80 @@ def test_dcp_decode_two_gpus(cuda, tmp_path):
         outs.append(out)
     for p, out in zip(procs, outs):
         assert p.returncode == 0, out[-3000:]
+
+
+MODEL_WORKER = textwrap.dedent("""
+    import os, sys, torch, torch.distributed as dist
+    import torch.nn.functional as Fn
+    from inference_optimizations_b200.config import EngineConfig, model_config
+    from inference_optimizations_b200.engine.engine import Engine
+    from inference_optimizations_b200.engine.scheduler import Request, SamplingParams, Segment
+    rank, S = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+    dev = torch.device("cuda", rank)
+    over = dict(expert_ffn=256, dense_ffn=512, weight_dtype="fp8", expert_dtype="fp8", hidden=512, q_lora=256,
+                qk_nope=128, v_head=128, index_heads=8, num_heads=8)
+    cfg = model_config("tiny_mla", **over)
+    prompt = [(13 * j + 7) % 500 + 1 for j in range(150)]
+
+    def logits(eng):
+        r = Request(rid=0, prompt=prompt, params=SamplingParams(max_new_tokens=1))
+        r.slot = 0
+        eng.runner.attach(r)
+        st, _ = eng.runner._step([Segment(r, 0, prompt, True)])
+        x = eng.runner.model.forward(st, eng.runner.kv)
+        eng.runner.detach(r)
+        return eng.runner.model.logits(x).float()
+
+    def engine(dcp):
+        ecfg = EngineConfig(model="tiny_mla", device=str(dev), kv_dtype="nvfp4", max_running=4, chunked_prefill=256,
+                            cuda_graphs=False, dcp=dcp, prefix_cache=False)
+        return Engine(ecfg, cfg, max_seq=256, dcp_rank=rank, dcp_group=dist.group.WORLD if dcp > 1 else None)
+    ref = logits(engine(1))                      # the whole model on this GPU (same seeded weights)
+    eng = engine(S)
+    got = logits(eng)
+    outs = eng.generate([prompt[:70], prompt[:33]], SamplingParams(max_new_tokens=5))
+    torch.cuda.synchronize()
+    eng.runner.model.dcp.check()
+    eng.runner.model.dcp_comm.check()
+    cos = Fn.cosine_similarity(got, ref, dim=-1)
+    # identical activations on both ranks, greedy tokens included
+    both = [torch.empty_like(got) for _ in range(S)]
+    dist.all_gather(both, got.contiguous())
+    same = torch.equal(both[0], both[1])
+    print(f"rank {rank} cos median {cos.median().item():.5f} min {cos.min().item():.5f} same {same} {outs}",
+          flush=True)
+    ok = cos.median().item() > 0.995 and (cos > 0.98).float().mean().item() > 0.9 and same
+    dist.barrier()
+    del eng
+    dist.destroy_process_group()
+    sys.exit(0 if ok else 1)
+""")
+
+
+def test_dcp_model_two_gpus(cuda, tmp_path):
+    """The MLA model with decode context parallelism on 2 GPUs (owned latent rows, peer-memory merge, fused
+    all-reduce + norm of the row-parallel products) tracks the whole model on one GPU; both ranks agree exactly."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    script = tmp_path / "dcp_model_worker.py"
+    script.write_text(MODEL_WORKER)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT="29583", NCCL_NVLS_ENABLE="0",
+                   PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
+        procs.append(subprocess.Popen([sys.executable, str(script)], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    outs = []
+    for p in procs:
+        try:
+            out, _ = p.communicate(timeout=300)
+        except subprocess.TimeoutExpired:
+            p.kill()
+            out, _ = p.communicate()
+        outs.append(out)
+    for p, out in zip(procs, outs):
+        assert p.returncode == 0, out[-3000:]
