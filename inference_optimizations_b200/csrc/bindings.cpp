@@ -773,7 +773,8 @@ void nvfp4_lut_test(const at::Tensor& words, at::Tensor out) {
 void mla_prep_kv(const at::Tensor& ya, const at::Tensor& q_norm, const at::Tensor& kv_norm, const at::Tensor& ik_w,
                  const at::Tensor& ik_b, const at::Tensor& rope, const at::Tensor& pos, const at::Tensor& slot,
                  at::Tensor qa_out, at::Tensor latent_pool, at::Tensor index_pool, at::Tensor iw_out, double iw_scale,
-                 int64_t q_lora, int64_t Hi, double eps, const c10::optional<at::Tensor>& lat_slot) {
+                 int64_t q_lora, int64_t Hi, double eps, const c10::optional<at::Tensor>& lat_slot,
+                 const c10::optional<at::Tensor>& qa_q, const c10::optional<at::Tensor>& qa_s) {
   req(ya, at::kBFloat16, "ya");
   req(rope, at::kFloat, "rope");
   req(pos, at::kInt, "pos");
@@ -806,6 +807,14 @@ void mla_prep_kv(const at::Tensor& ya, const at::Tensor& q_norm, const at::Tenso
     req(*lat_slot, at::kInt, "lat_slot");
     TORCH_CHECK(lat_slot->numel() == T, "lat_slot [T]");
     a.lat_slot = lat_slot->data_ptr<int>();
+  }
+  if (qa_q.has_value()) {
+    TORCH_CHECK(qa_s.has_value() && qa_q->scalar_type() == at::kByte && qa_s->scalar_type() == at::kInt &&
+                    qa_q->is_contiguous() && qa_s->is_contiguous() && qa_q->numel() == T * q_lora &&
+                    qa_s->numel() == T * (q_lora / 128) && q_lora % 128 == 0,
+                "qa_q uint8 [T, q_lora], qa_s int32 [T, q_lora / 128]");
+    a.qa_q = qa_q->data_ptr<uint8_t>();
+    a.qa_s = reinterpret_cast<uint32_t*>(qa_s->data_ptr<int>());
   }
   a.qa_out = qa_out.data_ptr();
   a.latent_pool = latent_pool.data_ptr<uint8_t>();

@@ -235,6 +235,8 @@ struct MlaPrepArgs {
   const int* lat_slot;        // [T] latent pool row when it differs from `slot` (context parallelism: the owning
                               // rank's local row, -1 elsewhere); null = slot
   void* qa_out;               // bf16 [T, q_lora]
+  uint8_t* qa_q;              // optional E4M3 [T, q_lora] + UE8M0 x4 words [T, q_lora / 128] of the normed q_a (the
+  uint32_t* qa_s;             // FP8 block-scaled input of the next projection; null = not written)
   uint8_t* latent_pool;       // [slots, 352] NVFP4 or [slots, 576] E4M3
   int latent_fmt;
   uint8_t* index_pool;        // [pages, 64 * 132]

@@ -22,6 +22,16 @@ namespace {
 
 __device__ __forceinline__ float bfv(const __nv_bfloat16* p, size_t i) { return __bfloat162float(p[i]); }
 __device__ __forceinline__ float rbf(float v) { return __bfloat162float(__float2bfloat16(v)); }
+// UE8M0 exponent byte of the smallest power of two s with amax / s <= 448 (clamped to [1, 253]); the activation
+// scale rule of the block-scaled GEMMs (rmsnorm_quant in moe_gemm.cu).
+__device__ __forceinline__ uint32_t ue8m0_exp(float amax) {
+  const float x = amax * (1.0f / 448.0f);
+  const uint32_t b = __float_as_uint(x);
+  int e = static_cast<int>((b >> 23) & 0xFF) - 127 + ((b & 0x7FFFFF) ? 1 : 0);
+  if (x == 0.f) e = -126;
+  e = max(-126, min(126, e));
+  return static_cast<uint32_t>(e + 127);
+}
 
 // NeoX rotate-half on a 64-wide vector held as 4 values per lane in lanes 0..15 (dims 4 l .. 4 l + 3): dim i < 32
 // pairs with i + 32, held by lane l ^ 8.  Lanes 16..31 hold dims 64.. and pass through.
@@ -62,7 +72,22 @@ __global__ void __launch_bounds__(256) mla_prep_kv_kernel(const MlaPrepArgs a) {
     const float inv = rsqrtf((red[0] + red[1] + red[2] + red[3]) / a.q_lora + a.eps);
     const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(a.q_norm);
     __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.qa_out) + static_cast<size_t>(t) * a.q_lora;
-    for (int c = tid; c < a.q_lora; c += 128) o[c] = __float2bfloat16(bfv(y, c) * inv * bfv(w, c));
+    // thread tid holds element tid of every 128-wide block: the block amax for the FP8 output is a 4-warp max
+    __shared__ float bmax[4];
+    for (int c = tid; c < a.q_lora; c += 128) {
+      const __nv_bfloat16 v = __float2bfloat16(bfv(y, c) * inv * bfv(w, c));
+      o[c] = v;
+      if (a.qa_q) {
+        const float f = __bfloat162float(v);
+        const float m = warp_max(fabsf(f));
+        asm volatile("bar.sync 1, 128;");                 // the previous block's maxima are consumed
+        if (lane == 0) bmax[warp] = m;
+        asm volatile("bar.sync 1, 128;");
+        const uint32_t eb = ue8m0_exp(fmaxf(fmaxf(bmax[0], bmax[1]), fmaxf(bmax[2], bmax[3])));
+        a.qa_q[static_cast<size_t>(t) * a.q_lora + c] = float_to_e4m3(f * __uint_as_float((254u - eb) << 23));
+        if (tid == 0) a.qa_s[static_cast<size_t>(t) * (a.q_lora / 128) + c / 128] = eb * 0x01010101u;
+      }
+    }
   } else if (warp == 4) {
     // ---------------------------------------------------------------- latent row
     const __nv_bfloat16* kv = y + a.q_lora;
@@ -165,13 +190,14 @@ __global__ void __launch_bounds__(256) mla_prep_q_kernel(const MlaPrepArgs a) {
   const float c = cs[lane], s = cs[32 + lane];
   __nv_bfloat16* qf = static_cast<__nv_bfloat16*>(a.qf) + static_cast<size_t>(t) * a.H * 576;
   const __nv_bfloat16* qpe = y + a.H * a.dn;
-  for (int h = warp; h < a.H; h += 8) {
+  const int hw = blockIdx.y * 8 + warp, hstep = gridDim.y * 8;     // heads over the CTAs of this token
+  for (int h = hw; h < a.H; h += hstep) {
     const float x1 = bfv(qpe, h * 64 + lane), x2 = bfv(qpe, h * 64 + 32 + lane);
     qf[h * 576 + 512 + lane] = __float2bfloat16(x1 * c - x2 * s);
     qf[h * 576 + 512 + 32 + lane] = __float2bfloat16(x2 * c + x1 * s);
   }
   const __nv_bfloat16* iq = y + a.H * (a.dn + 64);
-  for (int h = warp; h < a.Hi; h += 8) {
+  for (int h = hw; h < a.Hi; h += hstep) {
     float v[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) v[j] = bfv(iq, h * 128 + 4 * lane + j);
@@ -198,7 +224,8 @@ __global__ void __launch_bounds__(256) mla_prep_q_kernel(const MlaPrepArgs a) {
 cudaError_t mla_prep_kv(const MlaPrepArgs& a, cudaStream_t s) {
   if (a.T == 0) return cudaSuccess;
   if (a.q_lora <= 0 || a.Hi <= 0 || (a.latent_fmt != kKvNvfp4 && a.latent_fmt != kKvFp8) || !a.ya || !a.rope ||
-      !a.pos || !a.slot || !a.qa_out || !a.latent_pool || !a.index_pool || !a.iw_out)
+      !a.pos || !a.slot || !a.qa_out || !a.latent_pool || !a.index_pool || !a.iw_out ||
+      (a.qa_q && (!a.qa_s || a.q_lora % 128)))
     return cudaErrorInvalidValue;
   mla_prep_kv_kernel<<<a.T, 256, 0, s>>>(a);
   return cudaGetLastError();
@@ -209,7 +236,8 @@ cudaError_t mla_prep_q(const MlaPrepArgs& a, cudaStream_t s) {
   if (a.H <= 0 || a.Hi <= 0 || a.dn <= 0 || !a.yb || !a.qf || !a.q8 || !a.w_eff || !a.iw_out ||
       (reinterpret_cast<uintptr_t>(a.q8) & 3))
     return cudaErrorInvalidValue;
-  mla_prep_q_kernel<<<a.T, 256, 0, s>>>(a);
+  const int per_token = max(1, min(16, (max(a.H, a.Hi) + 15) / 16));   // ~2 heads per warp
+  mla_prep_q_kernel<<<dim3(a.T, per_token), 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -555,10 +555,13 @@ class MLAModel:
         ya = w.k["a"].lin(x)
         qa = torch.empty(t, c.q_lora, dtype=torch.bfloat16, device=dev)
         iw = torch.empty(t, c.index_heads, dtype=torch.float32, device=dev)
+        fp8_b = w.k["b"].kind == "fp8" and c.q_lora % 128 == 0     # q_a leaves the kernel already block-quantized
+        qa_q = torch.empty(t, c.q_lora, dtype=torch.uint8, device=dev) if fp8_b else None
+        qa_s = torch.empty(t, c.q_lora // 128, dtype=torch.int32, device=dev) if fp8_b else None
         ext().mla_prep_kv(ya, w.q_norm, w.kv_norm, w.wi_kn, w.wi_kb, cs, st.pos, st.slot, qa, kv.latent[i],
                           kv.index[i], iw, c.index_heads ** -0.5 * c.index_dim ** -0.5, c.q_lora, c.index_heads, eps,
-                          lat_slot)
-        yb = w.k["b"].lin(qa)
+                          lat_slot, qa_q, qa_s)
+        yb = w.k["b"].lin.forward_quantized(qa_q, qa_s) if fp8_b else w.k["b"].lin(qa)
         qf = torch.empty(t, c.num_heads, 576, dtype=torch.bfloat16, device=dev)
         w.k["uk"](yb, t, row_stride=w.k["b_stride"], out=qf.view(t * c.num_heads, 576)[:, :512])
         q8 = torch.empty(t, c.index_heads, c.index_dim, dtype=torch.uint8, device=dev)
