@@ -22,7 +22,7 @@ void req(const at::Tensor& t, at::ScalarType dt, const char* name) {
 }
 
 void rmsnorm(const at::Tensor& x, c10::optional<at::Tensor> residual, at::Tensor out, const at::Tensor& w, double eps,
-             bool plus_one) {
+             bool plus_one, const c10::optional<at::Tensor>& q8, const c10::optional<at::Tensor>& qs) {
   req(x, at::kBFloat16, "x");
   req(out, at::kBFloat16, "out");
   req(w, at::kBFloat16, "weight");
@@ -37,8 +37,18 @@ void rmsnorm(const at::Tensor& x, c10::optional<at::Tensor> residual, at::Tensor
     res = residual->data_ptr();
   }
   const at::cuda::CUDAGuard g(x.device());
+  uint8_t* q8p = nullptr;
+  uint32_t* qsp = nullptr;
+  if (q8.has_value()) {
+    TORCH_CHECK(qs.has_value() && q8->scalar_type() == at::kByte && qs->scalar_type() == at::kInt &&
+                    q8->is_contiguous() && qs->is_contiguous() && q8->numel() == static_cast<int64_t>(rows) * hidden &&
+                    qs->numel() == static_cast<int64_t>(rows) * (hidden / 128) && hidden % 128 == 0,
+                "rmsnorm FP8 output: q8 uint8 [rows, hidden], qs int32 [rows, hidden / 128]");
+    q8p = q8->data_ptr<uint8_t>();
+    qsp = reinterpret_cast<uint32_t*>(qs->data_ptr<int>());
+  }
   CHECK_CUDA_OK(iob::rmsnorm(x.data_ptr(), res, out.data_ptr(), w.data_ptr(), rows, hidden, stride, eps, plus_one,
-                             res != nullptr, stream()));
+                             res != nullptr, stream(), q8p, qsp));
 }
 
 void act_mul(const at::Tensor& gu, at::Tensor out, bool gelu) {
@@ -329,7 +339,8 @@ void indexer(const at::Tensor& q8, const at::Tensor& w, const at::Tensor& pool, 
 
 void ar_norm2(const at::Tensor& peers, int64_t flag_offset, int64_t rows_cap, int64_t half, int64_t rank,
               at::Tensor epoch, at::Tensor resid, at::Tensor out, c10::optional<at::Tensor> w1,
-              c10::optional<at::Tensor> w2, double eps, double plus_one, at::Tensor status) {
+              c10::optional<at::Tensor> w2, double eps, double plus_one, at::Tensor status, bool slots,
+              int64_t mc, int64_t res_offset, int64_t rowflag_offset) {
   req(peers, at::kLong, "peers");
   req(epoch, at::kInt, "epoch");
   req(resid, at::kBFloat16, "resid");
@@ -353,6 +364,10 @@ void ar_norm2(const at::Tensor& peers, int64_t flag_offset, int64_t rows_cap, in
   a.eps = eps;
   a.plus_one = plus_one;
   a.status = status.data_ptr<int>();
+  a.slots = slots ? 1 : 0;
+  a.mc = reinterpret_cast<void*>(static_cast<uintptr_t>(mc));
+  a.res_offset = res_offset;
+  a.rowflag_offset = rowflag_offset;
   const at::cuda::CUDAGuard g(resid.device());
   CHECK_CUDA_OK(iob::ar_norm2(a, stream()));
 }
@@ -378,7 +393,9 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
               int64_t kind, const c10::optional<at::Tensor>& expert_mul,
               const c10::optional<at::Tensor>& out_peers, int64_t out_offset, int64_t out_div, int64_t out_rank,
               int64_t out_shared_base, int64_t pairs_total, int64_t ksplit, int64_t split_rows, int64_t src_group,
-              int64_t src_group_stride, const c10::optional<at::Tensor>& trace, bool pdl, bool static_index) {
+              int64_t src_group_stride, const c10::optional<at::Tensor>& trace, bool pdl, bool static_index,
+              const c10::optional<at::Tensor>& red_out, const c10::optional<at::Tensor>& tile_cnt,
+              int64_t out_bcast) {
   req(wpack, at::kByte, "wpack");
   req(x, at::kByte, "x");
   req(off, at::kInt, "off");
@@ -441,6 +458,17 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
   a.src_group_stride = static_cast<int>(src_group_stride);
   a.pdl = pdl ? 1 : 0;
   a.static_index = static_index ? 1 : 0;
+  if (red_out.has_value()) {
+    TORCH_CHECK(mode == iob::kMoeOutF32Split && tile_cnt.has_value() && tile_cnt->scalar_type() == at::kInt &&
+                    tile_cnt->is_contiguous() && red_out->dim() == 2 && red_out->stride(1) == 1 &&
+                    (red_out->scalar_type() == at::kBFloat16 || red_out->scalar_type() == at::kFloat) &&
+                    red_out->size(1) >= n_tiles * G * 128 && red_out->size(0) >= split_rows,
+                "folded split-K: red_out [rows, N] bf16 / fp32 and an int32 tile counter array");
+    a.red_out = red_out->data_ptr();
+    a.tile_cnt = tile_cnt->data_ptr<int>();
+    a.red_stride = static_cast<int>(red_out->stride(0));
+    a.red_f32 = red_out->scalar_type() == at::kFloat ? 1 : 0;
+  }
   if (trace.has_value()) {
     TORCH_CHECK(trace->scalar_type() == at::kLong && trace->numel() >= iob::kMgEvCount && trace->is_cuda(),
                 "trace int64 [>= kMgEvCount]");
@@ -460,21 +488,33 @@ void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_
   a.out_rank = static_cast<int>(out_rank);
   a.out_shared_base = static_cast<int>(out_shared_base);
   a.pairs_total = static_cast<int>(pairs_total);
+  a.out_bcast = static_cast<int>(out_bcast);
+  TORCH_CHECK(out_bcast == 0 || (out_peers.has_value() && out_peers->numel() >= out_bcast &&
+                                 out_rank < out_bcast && out_peers->is_cuda()),
+              "out_bcast: a peer table of out_bcast entries, out_rank below it");
   const at::cuda::CUDAGuard g(x.device());
   CHECK_CUDA_OK(iob::moe_gemm(a, stream()));
 }
 
-void splitk_reduce(const at::Tensor& part, int64_t ksplit, at::Tensor out) {
+void splitk_reduce(const at::Tensor& part, int64_t ksplit, at::Tensor out, const c10::optional<at::Tensor>& peers,
+                   int64_t peer_offset, int64_t nbcast, int64_t rank) {
   req(part, at::kFloat, "part");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kFloat, "splitk_reduce: bf16 or fp32 out");
   TORCH_CHECK(out.is_cuda(), "splitk_reduce: CUDA tensors");
   TORCH_CHECK(part.is_contiguous() && out.is_contiguous() && out.dim() == 2 &&
                   part.numel() >= ksplit * out.size(0) * out.size(1),
               "splitk_reduce shapes");
+  if (peers.has_value())
+    TORCH_CHECK(peers->scalar_type() == at::kLong && peers->is_cuda() && peers->numel() >= nbcast && nbcast >= 1 &&
+                    rank >= 0 && rank < nbcast && out.scalar_type() == at::kBFloat16,
+                "splitk_reduce push: int64 peer table of nbcast entries, bf16 rows");
   const at::cuda::CUDAGuard g(out.device());
   CHECK_CUDA_OK(iob::splitk_reduce(part.data_ptr<float>(), static_cast<int>(ksplit), static_cast<int>(out.size(0)),
                                    static_cast<int>(out.size(1)), out.data_ptr(), out.scalar_type() == at::kFloat,
-                                   stream()));
+                                   stream(),
+                                   peers.has_value() ? reinterpret_cast<const long long*>(peers->data_ptr<int64_t>())
+                                                     : nullptr,
+                                   peer_offset, static_cast<int>(nbcast), static_cast<int>(rank)));
 }
 
 void moe_align(const at::Tensor& ids, int64_t e0, int64_t E, int64_t extra, at::Tensor off, at::Tensor pairs) {

@@ -1,7 +1,9 @@
 // Tensor-parallel all-reduce fused with the normalisation that follows it, over NVLink peer memory.
 //
 // Every rank's row-parallel GEMM (o_proj / down_proj) writes its partial [T, H] into its own half of a symmetric
-// buffer (same offset on every rank, mapped into every peer's address space).  One kernel then, per row:
+// buffer (same offset on every rank, mapped into every peer's address space) -- or, in the push form, the GEMM's own
+// epilogue stores each finished tile into this rank's slot of EVERY rank's buffer, so the NVLink transfer overlaps the
+// remaining tiles' math and the sum below reads local memory only.  One kernel then, per row:
 //   1. signals "my partial of call k is ready" to every peer (one flag store per peer, release at system scope) and
 //      waits, bounded, until every peer's flag for call k has arrived (acquire);
 //   2. reads the N partials over NVLink (16-byte peer loads) and sums them in fp32 in rank order 0..N-1, so every
@@ -11,6 +13,14 @@
 // Semantics of the reference's symmetric-memory pull-reduce (`moe-gemm/dp-moe-symmetric-memory/symm_collectives.py:
 // 57-90`, fixed peer order, fp32 accumulation) applied to the TP all-reduce, with the norm chain of
 // `attention/gemma-fused-glue/rtx_glue.py:68-195` folded in.
+//
+// NVLS form (NVLink SHARP through a multicast mapping of the same buffer, `multimem` instructions): after the
+// partials-ready barrier, rank r reduces column shard r of each row in the switch (one multimem.ld_reduce per 16
+// bytes: the switch reads and adds every rank's copy, fp32 accumulation) and writes it to every rank's reduced-rows
+// area with one multimem.st; a per-row flag, itself multicast, says the shard arrived everywhere.  A rank's NVLink
+// traffic is one partial row out of the switch's reduction and the reduced row in, instead of (nranks - 1) partial
+// rows; all ranks read the same reduced bytes.  The reference measures these instructions for its decode push /
+// pull (`moe-gemm/dp-moe-symmetric-memory/symm_collectives.py:240-271`).
 //
 // Call k uses buffer half b = k % 2 and flag value e = epoch[b]; CTA 0 bumps epoch[1 - b] for call k + 1 (no CTA of
 // call k + 1 can run before call k ends, stream order).  Rank r rewrites half b only at call k + 2, after passing call
@@ -55,7 +65,23 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
-template <int NR, int VPT>
+// NVLink SHARP (NVLS) accesses through a multicast address: the switch reduces the loads of every rank's copy
+// (fp32 accumulation of bf16 pairs) and replicates the stores into every rank's copy.
+__device__ __forceinline__ uint4 mc_ld_reduce_bf16x8(const void* p) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void mc_st16(void* p, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};"
+               :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+__device__ __forceinline__ void mc_st_release_u32(int* p, int v) {
+  asm volatile("multimem.st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+template <int NR, int VPT, bool NVLS>
 __global__ void __launch_bounds__(kArThreads) ar_norm2_kernel(const ArNormArgs a) {
   __shared__ float red[33];
   __shared__ int ok_s;
@@ -84,9 +110,43 @@ __global__ void __launch_bounds__(kArThreads) ar_norm2_kernel(const ArNormArgs a
   }
   __syncthreads();
   if (!ok_s) return;
-  // 2. sum the partials of this row in rank order
   const int row = blockIdx.x;
-  const size_t off = (static_cast<size_t>(b) * a.rows_cap + row) * a.H;   // element offset in the data area
+  if constexpr (NVLS) {
+    // 2'. this rank's column shard of the row: reduced in the switch, multicast into every rank's reduced rows
+    const int chunks = a.H / 8, c0 = a.rank * chunks / NR, c1 = (a.rank + 1) * chunks / NR;
+    const size_t poff = (static_cast<size_t>(b) * a.rows_cap + row) * a.H * 2;        // bytes
+    char* mc = reinterpret_cast<char*>(a.mc);
+    for (int c = c0 + threadIdx.x; c < c1; c += kArThreads)
+      mc_st16(mc + a.res_offset + poff + c * 16, mc_ld_reduce_bf16x8(mc + poff + c * 16));
+    __syncthreads();
+    int* rflags = reinterpret_cast<int*>(mc + a.rowflag_offset) + (static_cast<size_t>(b) * a.rows_cap + row) * NR;
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      mc_st_release_u32(rflags + a.rank, e);                    // "my shard of this row is in every copy"
+      const int* mine = reinterpret_cast<const int*>(reinterpret_cast<const char*>(a.peers[a.rank]) +
+                                                     a.rowflag_offset) + (static_cast<size_t>(b) * a.rows_cap + row) * NR;
+      int good = 1;
+      const unsigned long long t0 = global_ns();
+      for (int r = 0; r < NR && good; ++r) {
+        for (uint32_t it = 0; ld_acquire_sys(mine + r) < e; ++it) {
+          if ((it & 255) == 255 && global_ns() - t0 > kWaitLimitNs) {
+            good = 0;
+            record_status(a.status, kTimeoutPeer);
+            break;
+          }
+        }
+      }
+      asm volatile("fence.proxy.alias;" ::: "memory");         // the rows arrived through the multicast alias
+      ok_s = good;
+    }
+    __syncthreads();
+    if (!ok_s) return;
+  }
+  // 2. sum the partials of this row in rank order (pull: rank r's own buffer; push: slot r of this rank's buffer;
+  // NVLS: the switch-reduced row, read once from this rank's buffer)
+
+  const size_t off = (static_cast<size_t>(b) * (a.slots ? NR : 1) * a.rows_cap + row) * a.H;
+  const size_t slot_elems = a.slots ? static_cast<size_t>(a.rows_cap) * a.H : 0;
   float v[VPT][8];
   float ss = 0.f;
 #pragma unroll
@@ -96,8 +156,11 @@ __global__ void __launch_bounds__(kArThreads) ar_norm2_kernel(const ArNormArgs a
     for (int i = 0; i < 8; ++i) v[k][i] = 0.f;
     if (c * 8 >= a.H) continue;
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
-      const uint4 u = ld_peer16(reinterpret_cast<const __nv_bfloat16*>(a.peers[r]) + off + c * 8);
+    for (int r = 0; r < (NVLS ? 1 : NR); ++r) {
+      const uint4 u = NVLS ? ld_peer16(reinterpret_cast<const char*>(a.peers[a.rank]) + a.res_offset +
+                                       (static_cast<size_t>(b) * a.rows_cap + row) * a.H * 2 + c * 16)
+                           : ld_peer16(reinterpret_cast<const __nv_bfloat16*>(a.peers[a.slots ? a.rank : r]) + off +
+                                       r * slot_elems + c * 8);
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -169,18 +232,23 @@ __global__ void __launch_bounds__(kArThreads) ar_norm2_kernel(const ArNormArgs a
   }
 }
 
-template <int NR>
+template <int NR, bool NVLS>
 cudaError_t launch_nr(const ArNormArgs& a, cudaStream_t s) {
   const int chunks = a.H / 8;
   const int vpt = (chunks + kArThreads - 1) / kArThreads;
   switch (vpt) {
-    case 1: ar_norm2_kernel<NR, 1><<<a.T, kArThreads, 0, s>>>(a); break;
-    case 2: ar_norm2_kernel<NR, 2><<<a.T, kArThreads, 0, s>>>(a); break;
-    case 3: ar_norm2_kernel<NR, 3><<<a.T, kArThreads, 0, s>>>(a); break;
-    case 4: ar_norm2_kernel<NR, 4><<<a.T, kArThreads, 0, s>>>(a); break;
+    case 1: ar_norm2_kernel<NR, 1, NVLS><<<a.T, kArThreads, 0, s>>>(a); break;
+    case 2: ar_norm2_kernel<NR, 2, NVLS><<<a.T, kArThreads, 0, s>>>(a); break;
+    case 3: ar_norm2_kernel<NR, 3, NVLS><<<a.T, kArThreads, 0, s>>>(a); break;
+    case 4: ar_norm2_kernel<NR, 4, NVLS><<<a.T, kArThreads, 0, s>>>(a); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
+}
+
+template <int NR>
+cudaError_t launch_mode(const ArNormArgs& a, cudaStream_t s) {
+  return a.mc ? launch_nr<NR, true>(a, s) : launch_nr<NR, false>(a, s);
 }
 
 }  // namespace
@@ -189,11 +257,14 @@ cudaError_t ar_norm2(const ArNormArgs& a, cudaStream_t s) {
   if (a.T == 0) return cudaSuccess;
   if (a.H % 8 || a.T > a.rows_cap || (a.half != 0 && a.half != 1) || a.rank < 0 || a.rank >= a.nranks)
     return cudaErrorInvalidValue;
+  if (a.mc && (a.slots || a.nranks < 2 || a.res_offset % 16 || a.rowflag_offset % 16 ||
+               reinterpret_cast<uintptr_t>(a.mc) % 16))
+    return cudaErrorInvalidValue;
   switch (a.nranks) {
-    case 1: return launch_nr<1>(a, s);
-    case 2: return launch_nr<2>(a, s);
-    case 4: return launch_nr<4>(a, s);
-    case 8: return launch_nr<8>(a, s);
+    case 1: return launch_mode<1>(a, s);
+    case 2: return launch_mode<2>(a, s);
+    case 4: return launch_mode<4>(a, s);
+    case 8: return launch_mode<8>(a, s);
     default: return cudaErrorInvalidValue;
   }
 }

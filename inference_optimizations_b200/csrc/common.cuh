@@ -616,6 +616,16 @@ __device__ __forceinline__ uint32_t e2m1_code(float y) {  // signed, no negative
   const uint32_t m = e2m1_code_mag(fabsf(y));
   return m | ((y < 0.f && m > 0) ? 8u : 0u);
 }
+// UE8M0 exponent byte of the smallest power of two s with amax / s <= 448 (clamped to [1, 253]): the activation
+// scale rule of the FP8 block-scaled GEMMs (one scale per 128 values), shared by every kernel that quantizes for them.
+__device__ __forceinline__ uint32_t ue8m0_for(float amax) {
+  const float x = amax * (1.0f / 448.0f);
+  const uint32_t b = __float_as_uint(x);
+  int e = static_cast<int>((b >> 23) & 0xFF) - 127 + ((b & 0x7FFFFF) ? 1 : 0);
+  if (x == 0.f) e = -126;
+  e = max(-126, min(126, e));
+  return static_cast<uint32_t>(e + 127);
+}
 // Block scale rule shared by every NVFP4 writer: e4m3(clamp(amax / 6, 2^-9, 448)).
 __device__ __forceinline__ uint8_t nvfp4_block_scale(float amax) {
   const float s = fminf(fmaxf(amax / 6.0f, 0.001953125f), 448.0f);

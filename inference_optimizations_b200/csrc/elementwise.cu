@@ -14,7 +14,8 @@ __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162f
 template <int VPT>
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ residual,
                                __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ w, int hidden,
-                               int x_stride, float eps, bool plus_one, bool add_residual) {
+                               int x_stride, float eps, bool plus_one, bool add_residual, uint8_t* __restrict__ q8,
+                               uint32_t* __restrict__ qs) {
   griddep_launch();                   // a GEMM launched after this may set up and stream weights meanwhile
   const int row = blockIdx.x;
   const int nvec = hidden / 8;
@@ -59,6 +60,7 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat1
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int c = threadIdx.x + i * blockDim.x;
+    float y[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (c < nvec) {
       uint4 wr = reinterpret_cast<const uint4*>(w)[c];
       const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wr);
@@ -68,8 +70,29 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat1
       for (int j = 0; j < 8; ++j) {
         const float g = plus_one ? 1.f + bf(we[j]) : bf(we[j]);
         oe[j] = __float2bfloat16(v[i][j] * inv * g);
+        y[j] = bf(oe[j]);
       }
       reinterpret_cast<uint4*>(out + (size_t)row * hidden)[c] = o;
+    }
+    if (q8) {
+      // FP8 copy for a block-scaled GEMM (E4M3 + one UE8M0 scale per 128 values = 16 consecutive threads' groups):
+      // the same bytes as quantizing the bf16 output afterwards, without the extra launch
+      float m = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(y[j]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (c < nvec) {
+        const uint32_t eb = ue8m0_for(m);
+        const float sc = __uint_as_float((254u - eb) << 23);
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) lo |= static_cast<uint32_t>(float_to_e4m3(y[j] * sc)) << (8 * j);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) hi |= static_cast<uint32_t>(float_to_e4m3(y[4 + j] * sc)) << (8 * j);
+        *reinterpret_cast<uint2*>(q8 + (size_t)row * hidden + 8 * c) = make_uint2(lo, hi);
+        if ((c & 15) == 0) qs[(size_t)row * (hidden / 128) + c / 16] = eb * 0x01010101u;
+      }
     }
   }
 }
@@ -356,8 +379,9 @@ __global__ void index_key_kernel(const __nv_bfloat16* __restrict__ k, int k_stri
 }  // namespace
 
 cudaError_t rmsnorm(const void* x, void* residual, void* out, const void* weight, int rows, int hidden, int x_stride,
-                    float eps, bool plus_one, bool add_residual, cudaStream_t s) {
+                    float eps, bool plus_one, bool add_residual, cudaStream_t s, uint8_t* q8, uint32_t* qs) {
   if (hidden % 8 != 0 || rows == 0) return rows == 0 ? cudaSuccess : cudaErrorInvalidValue;
+  if (q8 && (hidden % 128 || !qs)) return cudaErrorInvalidValue;
   const int nvec = hidden / 8;
   const int threads = nvec >= 1024 ? 1024 : ((nvec + 31) / 32) * 32;
   const int vpt = (nvec + threads - 1) / threads;
@@ -365,9 +389,12 @@ cudaError_t rmsnorm(const void* x, void* residual, void* out, const void* weight
   auto R = reinterpret_cast<__nv_bfloat16*>(residual);
   auto O = reinterpret_cast<__nv_bfloat16*>(out);
   auto W = reinterpret_cast<const __nv_bfloat16*>(weight);
-  if (vpt == 1) rmsnorm_kernel<1><<<rows, threads, 0, s>>>(X, R, O, W, hidden, x_stride, eps, plus_one, add_residual);
-  else if (vpt == 2) rmsnorm_kernel<2><<<rows, threads, 0, s>>>(X, R, O, W, hidden, x_stride, eps, plus_one, add_residual);
-  else if (vpt <= 4) rmsnorm_kernel<4><<<rows, threads, 0, s>>>(X, R, O, W, hidden, x_stride, eps, plus_one, add_residual);
+  if (vpt == 1)
+    rmsnorm_kernel<1><<<rows, threads, 0, s>>>(X, R, O, W, hidden, x_stride, eps, plus_one, add_residual, q8, qs);
+  else if (vpt == 2)
+    rmsnorm_kernel<2><<<rows, threads, 0, s>>>(X, R, O, W, hidden, x_stride, eps, plus_one, add_residual, q8, qs);
+  else if (vpt <= 4)
+    rmsnorm_kernel<4><<<rows, threads, 0, s>>>(X, R, O, W, hidden, x_stride, eps, plus_one, add_residual, q8, qs);
   else return cudaErrorInvalidValue;
   return cudaGetLastError();
 }

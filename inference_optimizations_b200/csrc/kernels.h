@@ -26,8 +26,10 @@ inline int gqa_block_bytes(int fmt, int head_dim, int page) {
 }
 
 // ---- elementwise / normalisation (elementwise.cu)
+// q8 / qs (optional): also write the output as E4M3 + one UE8M0 scale word per 128 values (the FP8 GEMM input).
 cudaError_t rmsnorm(const void* x, void* residual, void* out, const void* weight, int rows, int hidden,
-                    int x_stride, float eps, bool plus_one, bool add_residual, cudaStream_t s);
+                    int x_stride, float eps, bool plus_one, bool add_residual, cudaStream_t s,
+                    uint8_t* q8 = nullptr, uint32_t* qs = nullptr);
 cudaError_t gelu_tanh_mul(const void* gate_up, void* out, int rows, int ffn, cudaStream_t s);
 cudaError_t silu_mul(const void* gate_up, void* out, int rows, int ffn, cudaStream_t s);
 cudaError_t embed(const int* ids, const void* table, void* out, int rows, int hidden, float scale, cudaStream_t s);
@@ -160,6 +162,16 @@ struct ArNormArgs {
   const void* w2;          // bf16 [H] norm of the new residual (null: out is not written)
   float eps, plus_one;
   int* status;
+  // 0: pull -- each rank's partial sits in its own buffer, data [2][rows_cap][H], read over NVLink.  1: push -- the
+  // row-parallel GEMM stored its partial into slot `rank` of every rank's buffer, data [2][nranks][rows_cap][H],
+  // so the sum reads local memory only.
+  int slots;
+  // NVLS (mc != null; pull layout for the partials): the NVLink multicast address of the same buffer.  Rank r sums
+  // column shard r of each row inside the switch (multimem.ld_reduce over every rank's partial) and multicasts the
+  // reduced shard into the reduced-rows area [2][rows_cap][H] at res_offset of every rank; per-row arrival flags
+  // [2][rows_cap][nranks] ints at rowflag_offset.
+  void* mc;
+  long long res_offset, rowflag_offset;
 };
 cudaError_t ar_norm2(const ArNormArgs& a, cudaStream_t s);
 
@@ -185,9 +197,11 @@ struct MoeGemmArgs {
   // Optional peer-memory output (expert parallelism): row p < pairs_total goes to rank p / out_div, row p % out_div
   // of the region at byte offset out_offset of that rank's symmetric buffer; shared-expert rows p >= pairs_total
   // go to this rank (out_rank), row out_shared_base + p - pairs_total.  Plain bf16 modes only.
+  // Broadcast form (tensor parallelism, out_bcast = ranks > 0): row p goes to EVERY rank rr < out_bcast, row p of
+  // the region at out_offset of rank rr's buffer (this rank's slot there), starting with rank out_rank.
   const long long* out_peers;
   long long out_offset;
-  int out_div, out_rank, out_shared_base, pairs_total;
+  int out_div, out_rank, out_shared_base, pairs_total, out_bcast;
   int* status;
   int E, n_tiles, KC, G, NT, mode, src_div, src_limit, src_shared_base, x_stride, out_stride, out_scale_stride;
   // Optional grouped source rows (0 = off): activation row of a pair p below src_limit is
@@ -205,6 +219,12 @@ struct MoeGemmArgs {
   // expert offsets and pair ids were written before the previous kernel (cached index tensors), so the work list can
   // be built before the wait; else everything waits first.
   int pdl, static_index;
+  // Split-K with the reduction folded in (kMoeOutF32Split): after writing its partial, a split bumps the tile's
+  // counter; the split that completes the tile sums the partials in split order and writes red_out (bf16, or fp32
+  // with red_f32; row stride red_stride), then re-arms the counter (zero before and after every launch).
+  void* red_out;
+  int* tile_cnt;
+  int red_stride, red_f32;
 };
 // GEMM timeline events (trace[ev]): kernel start, setup done, first weight copy issued, first stage ready at the
 // MMA warp, last MMA committed, first accumulator seen by the epilogue, epilogue done, kernel end.
@@ -217,7 +237,10 @@ cudaError_t moe_align(const int* ids, int P, int e0, int E, int shared_bucket, i
                       cudaStream_t s);
 // out [rows][N] (bf16, or fp32 with out_f32) = sum over splits of part fp32 [ksplit][rows][N] (fixed split order:
 // deterministic).
-cudaError_t splitk_reduce(const float* part, int ksplit, int rows, int N, void* out, bool out_f32, cudaStream_t s);
+// peers (optional, bf16 only): the rows also go, at byte offset peer_offset, to every rank's buffer in peers[nbcast]
+// (this rank's slot there; tensor-parallel push of a row-parallel GEMM's result), starting with rank `rank`.
+cudaError_t splitk_reduce(const float* part, int ksplit, int rows, int N, void* out, bool out_f32, cudaStream_t s,
+                          const long long* peers = nullptr, long long peer_offset = 0, int nbcast = 0, int rank = 0);
 cudaError_t moe_combine(const void* rows, int T, int topk, int H, int shared_base, const float* w, void* y,
                         cudaStream_t s);
 

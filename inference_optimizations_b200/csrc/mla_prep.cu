@@ -22,16 +22,6 @@ namespace {
 
 __device__ __forceinline__ float bfv(const __nv_bfloat16* p, size_t i) { return __bfloat162float(p[i]); }
 __device__ __forceinline__ float rbf(float v) { return __bfloat162float(__float2bfloat16(v)); }
-// UE8M0 exponent byte of the smallest power of two s with amax / s <= 448 (clamped to [1, 253]); the activation
-// scale rule of the block-scaled GEMMs (rmsnorm_quant in moe_gemm.cu).
-__device__ __forceinline__ uint32_t ue8m0_exp(float amax) {
-  const float x = amax * (1.0f / 448.0f);
-  const uint32_t b = __float_as_uint(x);
-  int e = static_cast<int>((b >> 23) & 0xFF) - 127 + ((b & 0x7FFFFF) ? 1 : 0);
-  if (x == 0.f) e = -126;
-  e = max(-126, min(126, e));
-  return static_cast<uint32_t>(e + 127);
-}
 
 // NeoX rotate-half on a 64-wide vector held as 4 values per lane in lanes 0..15 (dims 4 l .. 4 l + 3): dim i < 32
 // pairs with i + 32, held by lane l ^ 8.  Lanes 16..31 hold dims 64.. and pass through.
@@ -83,7 +73,7 @@ __global__ void __launch_bounds__(256) mla_prep_kv_kernel(const MlaPrepArgs a) {
         asm volatile("bar.sync 1, 128;");                 // the previous block's maxima are consumed
         if (lane == 0) bmax[warp] = m;
         asm volatile("bar.sync 1, 128;");
-        const uint32_t eb = ue8m0_exp(fmaxf(fmaxf(bmax[0], bmax[1]), fmaxf(bmax[2], bmax[3])));
+        const uint32_t eb = ue8m0_for(fmaxf(fmaxf(bmax[0], bmax[1]), fmaxf(bmax[2], bmax[3])));
         a.qa_q[static_cast<size_t>(t) * a.q_lora + c] = float_to_e4m3(f * __uint_as_float((254u - eb) << 23));
         if (tid == 0) a.qa_s[static_cast<size_t>(t) * (a.q_lora / 128) + c / 128] = eb * 0x01010101u;
       }

@@ -74,6 +74,7 @@ struct MgCtrl {
   uint32_t tmem_base;
   int abort;
   int n_items;
+  int tile_last;                      // folded split-K: this CTA completed the tile
 };
 
 // Shared-memory matrix descriptor for a 32-row x 16-byte no-swizzle source (tcgen05.cp 32x128b): 8-row core
@@ -200,15 +201,6 @@ __device__ __forceinline__ int src_row(const MoeGemmArgs& a, int p) {
   return a.src_group > 0 ? (q / a.src_group) * a.src_group_stride + q % a.src_group : q;
 }
 
-// UE8M0 exponent of the smallest power of two s with amax / s <= 448 (biased byte, clamped to [1, 253]).
-__device__ __forceinline__ uint32_t ue8m0_for(float amax) {
-  const float x = amax * (1.0f / 448.0f);
-  const uint32_t b = __float_as_uint(x);
-  int e = static_cast<int>((b >> 23) & 0xFF) - 127 + ((b & 0x7FFFFF) ? 1 : 0);
-  if (x == 0.f) e = -126;
-  e = max(-126, min(126, e));
-  return static_cast<uint32_t>(e + 127);
-}
 
 // Plain-output epilogue of one item (this thread = TMEM lane = output column n_local of each of the G column tiles):
 // groups of kGrp tokens are loaded from TMEM, staged as token rows in shared memory (a warp writes 32 consecutive
@@ -249,24 +241,77 @@ __device__ __forceinline__ void store_rows(const MoeGemmArgs& a, uint8_t* epi, c
       const int r = c + t;
       if (r >= rows) break;
       const int p = pid[r];
-      char* dst;
-      if constexpr (ESZ == 4) {
-        dst = reinterpret_cast<char*>(a.out) +
-              ((static_cast<size_t>(ks) * a.split_rows + p) * a.out_stride + static_cast<size_t>(nt) * G * 128) * 4;
-      } else if (a.out_peers) {                 // expert parallelism: the row goes to its token's owner
-        const bool sh = p >= a.pairs_total;
-        const int rr = sh ? a.out_rank : p / a.out_div;
-        const long long row = sh ? a.out_shared_base + (p - a.pairs_total) : p % a.out_div;
-        dst = reinterpret_cast<char*>(a.out_peers[rr]) + a.out_offset +
-              (row * a.out_stride + static_cast<long long>(nt) * G * 128) * 2;
-      } else {
-        dst = reinterpret_cast<char*>(a.out) + (static_cast<size_t>(p) * a.out_stride + static_cast<size_t>(nt) * G * 128) * 2;
-      }
       const uint4* src = reinterpret_cast<const uint4*>(epi + t * kRowB);
+      // tensor-parallel broadcast: the row goes to every rank (own first, then the next ranks in ring order)
+      const int nd = (ESZ == 2 && a.out_peers && a.out_bcast > 0) ? a.out_bcast : 1;
 #pragma unroll 1
-      for (int k = lane; k < kRowB / 16; k += 32) reinterpret_cast<uint4*>(dst)[k] = src[k];
+      for (int d = 0; d < nd; ++d) {
+        char* dst;
+        if constexpr (ESZ == 4) {
+          dst = reinterpret_cast<char*>(a.out) +
+                ((static_cast<size_t>(ks) * a.split_rows + p) * a.out_stride + static_cast<size_t>(nt) * G * 128) * 4;
+        } else if (a.out_peers) {               // expert parallelism: the row goes to its token's owner
+          const bool bc = a.out_bcast > 0, sh = !bc && p >= a.pairs_total;
+          const int rr = bc ? (a.out_rank + d) % a.out_bcast : (sh ? a.out_rank : p / a.out_div);
+          const long long row = bc ? p : (sh ? a.out_shared_base + (p - a.pairs_total) : p % a.out_div);
+          dst = reinterpret_cast<char*>(a.out_peers[rr]) + a.out_offset +
+                (row * a.out_stride + static_cast<long long>(nt) * G * 128) * 2;
+        } else {
+          dst = reinterpret_cast<char*>(a.out) +
+                (static_cast<size_t>(p) * a.out_stride + static_cast<size_t>(nt) * G * 128) * 2;
+        }
+#pragma unroll 1
+        for (int k = lane; k < kRowB / 16; k += 32) reinterpret_cast<uint4*>(dst)[k] = src[k];
+      }
     }
     named_bar(2, 128);
+  }
+}
+
+// Folded split-K reduction (the epilogue's 128 threads, after this split's partial rows were stored): the split that
+// brings the tile's counter to ksplit sums the ksplit partials of the tile's rows in split order (as splitk_reduce:
+// deterministic, whichever split finishes last) and writes the final rows; it re-arms the counter.
+template <int G>
+__device__ __forceinline__ void split_reduce_tail(const MoeGemmArgs& a, MgCtrl& ctl, int tile, const int* pid,
+                                                  int rows, int nt) {
+  __threadfence();                    // this split's partial rows are visible device-wide before it is counted
+  named_bar(2, 128);
+  if (threadIdx.x == 128) {
+    const int old = atomicAdd(a.tile_cnt + tile, 1);
+    const int last = old == a.ksplit - 1;
+    if (last) a.tile_cnt[tile] = 0;
+    ctl.tile_last = last;
+  }
+  named_bar(2, 128);
+  const bool last = ctl.tile_last;
+  named_bar(2, 128);                  // every thread read the flag before the next item may overwrite it
+  if (!last) return;
+  __threadfence();
+  const int tid = threadIdx.x - 128;
+  const float* part = reinterpret_cast<const float*>(a.out);
+  constexpr int kQuads = G * 128 / 4;                 // float4 columns of the tile
+#pragma unroll 1
+  for (int e = tid; e < rows * kQuads; e += 128) {    // (row, float4 column) over all 128 threads
+    const int r = e / kQuads, c4 = e - r * kQuads;
+    const int p = pid[r];
+    const size_t col = static_cast<size_t>(nt) * G * 128 + 4 * c4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < a.ksplit; ++k) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(
+          part + (static_cast<size_t>(k) * a.split_rows + p) * a.out_stride + col));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    if (a.red_f32) {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.red_out) + static_cast<size_t>(p) * a.red_stride + col) =
+          acc;
+    } else {
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+      uint2 w;
+      w.x = *reinterpret_cast<const uint32_t*>(&lo);
+      w.y = *reinterpret_cast<const uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.red_out) + static_cast<size_t>(p) * a.red_stride +
+                                col) = w;
+    }
   }
 }
 
@@ -531,8 +576,9 @@ __global__ void __launch_bounds__(kMgThreads, 1) moe_gemm_kernel(const MoeGemmAr
       const uint32_t acc = tmem + lane_addr + buf * C::kAccCols;
       const float emul = a.out_mul * (a.expert_mul ? a.expert_mul[e] : 1.f);
       constexpr int kChunk = NT < 32 ? NT : 32;
-      if (a.mode == kMoeOutF32Split) {               // split-K partial, summed by splitk_reduce
+      if (a.mode == kMoeOutF32Split) {               // split-K partial, summed by splitk_reduce or folded in
         store_rows<C, NT, G, 4>(a, epi, pid, acc, emul, rows, nt, ks, q, lane, n_local);
+        if (a.red_out) split_reduce_tail<G>(a, ctl, i / a.ksplit, pid, rows, nt);
       } else if (a.mode != kMoeOutSwigluQuant) {
         store_rows<C, NT, G, 2>(a, epi, pid, acc, emul, rows, nt, ks, q, lane, n_local);
       } else
@@ -802,10 +848,11 @@ __global__ void act_quant_kernel(const __nv_bfloat16* gu, int F, int fmt, uint8_
 // One CTA per output row: the K splits' fp32 partials summed in split order, then rounded once to bf16 (OutT = bf16)
 // or kept in fp32 (OutT = float: router logits).
 template <class OutT>
-__global__ void splitk_reduce_kernel(const float* part, int ksplit, int rows, int N, OutT* out) {
+__global__ void splitk_reduce_kernel(const float* part, int ksplit, int rows, int N, OutT* out,
+                                     const long long* peers, long long peer_offset, int nbcast, int rank) {
   griddep_launch();
   const int r = blockIdx.x;
-  for (int c = threadIdx.x; c < N / 4; c += blockDim.x) {
+  for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < N / 4; c += gridDim.y * blockDim.x) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < ksplit; ++k) {
       const float4 v = reinterpret_cast<const float4*>(part + (static_cast<size_t>(k) * rows + r) * N)[c];
@@ -818,18 +865,32 @@ __global__ void splitk_reduce_kernel(const float* part, int ksplit, int rows, in
       uint2 w;
       w.x = *reinterpret_cast<const uint32_t*>(&lo);
       w.y = *reinterpret_cast<const uint32_t*>(&hi);
-      reinterpret_cast<uint2*>(out + static_cast<size_t>(r) * N)[c] = w;
+      if (!peers) {
+        reinterpret_cast<uint2*>(out + static_cast<size_t>(r) * N)[c] = w;
+      } else {
+        // tensor-parallel push: the row into this rank's slot of every rank's buffer (own first)
+        for (int d = 0; d < nbcast; ++d) {
+          char* dst = reinterpret_cast<char*>(peers[(rank + d) % nbcast]) + peer_offset;
+          reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(dst) + static_cast<size_t>(r) * N)[c] = w;
+        }
+      }
     }
   }
+  // the rows stored into peers' memory are visible system-wide before the next kernel releases its ready flag
+  if (peers) __threadfence_system();
 }
 
 }  // namespace
 
 cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
   if (a.ksplit < 1 || a.ksplit > a.KC || (a.ksplit > 1 && a.mode != kMoeOutF32Split) ||
-      (a.mode == kMoeOutF32Split && a.out_peers))
+      (a.mode == kMoeOutF32Split && a.out_peers) || (a.red_out && (a.mode != kMoeOutF32Split || !a.tile_cnt)) ||
+      (a.red_out && (a.red_stride % 4 || reinterpret_cast<uintptr_t>(a.red_out) % 16)))
     return cudaErrorInvalidValue;
   if (a.src_group < 0 || (a.src_group > 0 && a.src_group_stride < a.src_group)) return cudaErrorInvalidValue;
+  if (a.out_bcast < 0 || (a.out_bcast > 0 && (!a.out_peers || a.out_rank < 0 || a.out_rank >= a.out_bcast ||
+                                               (a.mode != kMoeOutBf16 && a.mode != kMoeOutBf16Weighted))))
+    return cudaErrorInvalidValue;
   if (a.mode != kMoeOutSwigluQuant) {         // plain epilogues store 16-byte row segments
     const int esz = a.mode == kMoeOutF32Split ? 4 : 2;
     if ((static_cast<long long>(a.out_stride) * esz) % 16 || a.out_offset % 16 ||
@@ -852,13 +913,18 @@ cudaError_t moe_gemm(const MoeGemmArgs& a, cudaStream_t s) {
   return cudaErrorInvalidValue;
 }
 
-cudaError_t splitk_reduce(const float* part, int ksplit, int rows, int N, void* out, bool out_f32, cudaStream_t s) {
+cudaError_t splitk_reduce(const float* part, int ksplit, int rows, int N, void* out, bool out_f32, cudaStream_t s,
+                          const long long* peers, long long peer_offset, int nbcast, int rank) {
   if (rows == 0) return cudaSuccess;
   if (N % 4 || ksplit < 1) return cudaErrorInvalidValue;
+  if (peers && (out_f32 || nbcast < 1 || rank < 0 || rank >= nbcast || peer_offset % 16)) return cudaErrorInvalidValue;
+  // (row, column block of 256 float4s): a wide output is reduced by enough CTAs to stream the partials at full rate
+  const dim3 grid(rows, (N / 4 + 255) / 256);
   if (out_f32)
-    splitk_reduce_kernel<float><<<rows, 256, 0, s>>>(part, ksplit, rows, N, static_cast<float*>(out));
+    splitk_reduce_kernel<float><<<grid, 256, 0, s>>>(part, ksplit, rows, N, static_cast<float*>(out), nullptr, 0, 0, 0);
   else
-    splitk_reduce_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>(part, ksplit, rows, N, static_cast<__nv_bfloat16*>(out));
+    splitk_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(part, ksplit, rows, N, static_cast<__nv_bfloat16*>(out),
+                                                             peers, peer_offset, nbcast, rank);
   return cudaGetLastError();
 }
 

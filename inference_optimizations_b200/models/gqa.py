@@ -12,6 +12,12 @@ max over ranks of the local argmax.  Weights are random-init (seeded) or loaded 
 
 The draft head for speculative decoding (EAGLE-style, one sliding-window layer, `speculative/` in the reference)
 shares the embedding / LM head: x = W_fc [emb(token); h_prev] -> layer -> norm -> logits.
+
+On a GPU every projection and the LM head run on this framework's weight-streaming tcgen05 GEMM (`ops/linear.py`,
+bf16 packed weights); with tensor parallelism and a push-form `parallel.symm.TPComm`, W_o and W_d are the fused
+GEMM -> all-reduce: the GEMM's epilogue stores each output tile into every rank's symmetric buffer and one kernel sums
+the slots locally and applies the norm chain.  The bf16 masters are kept only for small models (the cache-free
+oracle and checkpoint export read them).
 """
 from __future__ import annotations
 
@@ -27,6 +33,7 @@ from ..config import GQAConfig
 from ..ops import attention as A
 from ..ops import basic as B
 from ..ops import kvcache as K
+from ..ops import linear as L
 
 
 def _randn(shape, std, gen, device, dtype=torch.bfloat16):
@@ -66,7 +73,9 @@ class LayerGeom:
 class GQAModel:
     def __init__(self, cfg: GQAConfig, device, tp_rank: int = 0, tp: int = 1, seed: int = 0,
                  all_reduce: Optional[Callable[[torch.Tensor], torch.Tensor]] = None,
-                 weights: Optional[dict] = None, draft: bool = False):
+                 weights: Optional[dict] = None, draft: bool = False, keep_master: Optional[bool] = None):
+        """keep_master: keep the bf16 weights next to the GEMM's packed copies on a GPU (default: models under 2 G
+        parameters; the cache-free oracle and checkpoint export need them)."""
         self.cfg, self.device, self.tp_rank, self.tp = cfg, torch.device(device), tp_rank, tp
         self.all_reduce = all_reduce
         self.tp_comm = None          # parallel.symm.TPComm: fused peer-memory all-reduce + norms (tp > 1)
@@ -123,6 +132,42 @@ class GQAModel:
             self._adopt(weights, draft)
         self.rope = {}
         self.embed_scale = math.sqrt(h) if cfg.embed_scale else 1.0
+        self.keep_master = keep_master if keep_master is not None else cfg.num_params() < 2e9
+        self._build_linears()
+
+    def _build_linears(self) -> None:
+        """Pack every projection (and this rank's LM-head rows) for the weight-streaming GEMM; without keep_master
+        the bf16 masters are dropped as each is packed, so a node-size model holds one copy."""
+        self.lins, self.head = None, None
+        if self.device.type != "cuda":
+            return
+
+        def mk(w):
+            return L.Linear(w, "bf16") if w.shape[1] % 64 == 0 else None
+
+        self.lins = []
+        for w in self.layers:
+            d = {}
+            for name in ("qkv", "o", "gu", "down"):
+                d[name] = mk(getattr(w, name))
+                if d[name] is not None and not self.keep_master:
+                    setattr(w, name, None)
+            self.lins.append(d)
+        if self.embed is not None:
+            lo = self.tp_rank * self.vocab_local
+            self.head = mk(self.embed[lo:lo + self.vocab_local])
+
+    def can_push(self) -> bool:
+        """Every row-parallel projection (W_o, W_d) is on the GEMM with an unpadded output: the push form of the
+        fused tensor-parallel all-reduce applies."""
+        return self.lins is not None and all(d[n] is not None and d[n].Np == d[n].N
+                                             for d in self.lins for n in ("o", "down"))
+
+    def _lin(self, i: int, name: str, x: torch.Tensor, push=None) -> torch.Tensor:
+        lin = self.lins[i][name] if self.lins is not None else None
+        if lin is None or not x.is_cuda:
+            return Fn.linear(x, getattr(self.layers[i], name))
+        return lin(x, push=push)
 
     # ------------------------------------------------------------------------------------------------ weights
     def _adopt(self, w: dict, draft: bool) -> None:
@@ -155,7 +200,10 @@ class GQAModel:
         return t
 
     def num_bytes(self) -> int:
-        n = sum(t.numel() * t.element_size() for l in self.layers for t in vars(l).values())
+        n = sum(t.numel() * t.element_size() for l in self.layers for t in vars(l).values() if t is not None)
+        if self.lins is not None:
+            n += sum(lin.lin.wpack.numel() for d in self.lins for name, lin in d.items()
+                     if lin is not None and getattr(self.layers[0], name) is None)
         if self.embed is not None:
             n += self.embed.numel() * 2
         return n
@@ -171,7 +219,7 @@ class GQAModel:
         """x_norm = norm_in(h) [T, H]; resid = h (updated in place).  Returns the next layer's normed input."""
         cfg, w, g = self.cfg, self.layers[i], self.geoms[i]
         eps = cfg.rms_eps
-        qkv = Fn.linear(x_norm, w.qkv)
+        qkv = self._lin(i, "qkv", x_norm)
         theta = cfg.rope_theta_global if g.kind == "global" else cfg.rope_theta
         cs = self.rope_table(g.head_dim, theta, kv.max_pos)
         pool = kv.pools[layer_id]
@@ -188,17 +236,24 @@ class GQAModel:
                                 splits=st.splits.get(g.kind), ws=kv.workspace(g.head_dim, g.kv_heads, st.lane),
                                 req_idx=st.req_idx)
         if self.tp > 1 and self.tp_comm is not None and attn.shape[0] <= self.tp_comm.rows_cap:
-            # row-parallel GEMMs write their partials into the symmetric buffer; one kernel reduces over NVLink and
-            # applies post-norm, residual add and the next pre-norm
             comm, t = self.tp_comm, attn.shape[0]
-            torch.matmul(attn.view(t, -1), w.o.t(), out=comm.out_buffer(t))
+            if comm.push:
+                # fused GEMM -> all-reduce: the GEMM pushes its tiles into every rank's slot; one kernel sums the
+                # slots locally and applies post-norm, residual add and the next pre-norm
+                self._lin(i, "o", attn.view(t, -1), push=comm)
+                x = comm.reduce_norm2(t, resid, w.n_post_attn, w.n_pre_ffn, eps)
+                self._lin(i, "down", B.act_mul(self._lin(i, "gu", x), gelu=True), push=comm)
+                return comm.reduce_norm2(t, resid, w.n_post_ffn, next_norm, eps)
+            # pull form: row-parallel GEMMs write their partials into the symmetric buffer; one kernel reduces over
+            # NVLink and applies post-norm, residual add and the next pre-norm
+            comm.out_buffer(t).copy_(self._lin(i, "o", attn.view(t, -1)))
             x = comm.reduce_norm2(t, resid, w.n_post_attn, w.n_pre_ffn, eps)
-            torch.matmul(B.act_mul(Fn.linear(x, w.gu), gelu=True), w.down.t(), out=comm.out_buffer(t))
+            comm.out_buffer(t).copy_(self._lin(i, "down", B.act_mul(self._lin(i, "gu", x), gelu=True)))
             return comm.reduce_norm2(t, resid, w.n_post_ffn, next_norm, eps)
-        o = self._reduce(Fn.linear(attn.view(attn.shape[0], -1), w.o))
+        o = self._reduce(self._lin(i, "o", attn.view(attn.shape[0], -1)))
         o = B.rmsnorm(o, w.n_post_attn, eps, True)
         x = B.rmsnorm(o, w.n_pre_ffn, eps, True, residual=resid)          # resid += o; x = norm(resid)
-        f = self._reduce(Fn.linear(B.act_mul(Fn.linear(x, w.gu), gelu=True), w.down))
+        f = self._reduce(self._lin(i, "down", B.act_mul(self._lin(i, "gu", x), gelu=True)))
         f = B.rmsnorm(f, w.n_post_ffn, eps, True)
         return B.rmsnorm(f, next_norm, eps, True, residual=resid)       # resid += f; x = norm_next(resid)
 
@@ -223,6 +278,8 @@ class GQAModel:
         return x, resid
 
     def logits_local(self, x_final: torch.Tensor, embed: torch.Tensor) -> torch.Tensor:
+        if self.head is not None and embed is self.embed and x_final.is_cuda:
+            return self.head(x_final)
         lo = self.tp_rank * self.vocab_local
         return Fn.linear(x_final, embed[lo:lo + self.vocab_local])
 
@@ -233,6 +290,8 @@ class GQAModel:
         from ..ops.attention import dense_attention_ref
         from ..ops.kvcache import _head_rmsnorm
         cfg, eps = self.cfg, self.cfg.rms_eps
+        if self.layers and self.layers[0].qkv is None:
+            raise RuntimeError("reference_logits needs the bf16 masters (GQAModel(keep_master=True))")
         t = len(tokens)
         ids = torch.tensor(tokens, dtype=torch.int32, device=self.device)
         pos = torch.arange(t, device=self.device)

@@ -135,6 +135,7 @@ class MLAModel:
         self.ep_rank, self.ep_world = ep_rank, ep_world
         self.dcp_rank, self.dcp_world = dcp_rank, dcp_world
         self.dcp = None                                  # attach_dcp(): merge + reduce communicators
+        self.dcp_push = None                             # push-form reduce for the row-parallel W_o (CUDA)
         pr, pw = (dcp_rank, dcp_world) if dcp_world > 1 else (ep_rank, ep_world)
         self.e_lo, self.e_hi = pr * c.num_experts // pw, (pr + 1) * c.num_experts // pw
         self.ep = None                                   # set by attach_ep(): per-layer expert-parallel MoE
@@ -142,6 +143,7 @@ class MLAModel:
         self.keep_master = keep_master if keep_master is not None else c.num_params() < 2e9
         self.cuda = self.device.type == "cuda"
         self.fuse_glue = True                            # the fused attention-block glue kernels where they apply
+        self._x8 = None                                  # (data_ptr of x, E4M3 x, scales) written by the last norm
         self._bs: dict = {}
         r = lambda name, shape, s=c.init_std: _rand(name, shape, s, self.device, seed)  # noqa: E731
         self.embed = r("embed", (c.vocab, h))
@@ -403,7 +405,8 @@ class MLAModel:
             return k["gate"](x, out_f32=True)
         return Fn.linear(x.float(), self.layers[i].ffn["gate"].float())
 
-    def _ffn(self, i: int, x: torch.Tensor) -> torch.Tensor:
+    def _ffn(self, i: int, x: torch.Tensor, xq8: Optional[tuple] = None) -> torch.Tensor:
+        """xq8: x block-quantized by the norm that produced it (FP8 FFN weights), or None."""
         c, f = self.cfg, self.layers[i].ffn
         if self.ep is not None and c.is_moe(i):
             logits = self._router_logits(i, x)
@@ -412,17 +415,18 @@ class MLAModel:
             outs = []
             for p in range(self.ep_pieces):      # every rank runs the same number of exchanges (agreed per step)
                 lo, hi = min(t, p * per), min(t, (p + 1) * per)
-                outs.append(self.ep[i].forward(x[lo:hi], ids[lo:hi].to(torch.int32).contiguous(), w[lo:hi]))
+                q = (xq8[0][lo:hi], xq8[1][lo:hi]) if xq8 is not None else None
+                outs.append(self.ep[i].forward(x[lo:hi], ids[lo:hi].to(torch.int32).contiguous(), w[lo:hi], q))
             return torch.cat(outs) if len(outs) > 1 else outs[0]
         if self._quantized_ffn(i):
             ex = self._block_scaled(i)
             t = x.shape[0]
             if not c.is_moe(i):
                 ids = torch.zeros(t, 1, dtype=torch.int32, device=x.device)
-                return ex.forward(x, ids, torch.ones(t, 1, device=x.device))
+                return ex.forward(x, ids, torch.ones(t, 1, device=x.device), xq8=xq8)
             logits = self._router_logits(i, x)
             ids, w = MOE.route(logits, f["e_bias"], c.topk, c.n_group, c.topk_group, c.routed_scale, c.router)
-            return ex.forward(x, ids, w)
+            return ex.forward(x, ids, w, xq8=xq8)
         if not c.is_moe(i):
             return MOE.swiglu(x, f["w_gu"], f["w_down"])
         return MOE.moe_forward(x, f["gate"], f["e_bias"], f["w_gu"], f["w_down"], f["shared_gu"], f["shared_down"],
@@ -458,13 +462,16 @@ class MLAModel:
         iq = Fn.linear(qa, w.wi_q).view(t, c.index_heads, c.index_dim)
         return q_lat, q[..., dn:], iq
 
-    def _o_proj(self, w: MLALayerWeights, o_lat: torch.Tensor, t: int) -> torch.Tensor:
+    def _o_proj(self, w: MLALayerWeights, o_lat: torch.Tensor, t: int, push=None) -> torch.Tensor:
+        """push: a push-form TPComm -- W_o's GEMM stores its rows into every rank's slot (fused GEMM -> all-reduce)."""
         c = self.cfg
         if w.k is not None and "uv" in w.k:
             o = w.k["uv"](o_lat, t).view(t, -1)
         else:
             wuv = w.w_uv if w.w_uv.device == o_lat.device else w.w_uv.to(o_lat.device)
             o = torch.einsum("thk,hkv->thv", o_lat.float(), wuv.float()).to(torch.bfloat16).reshape(t, -1)
+        if push is not None:
+            return w.k["o"](o, push=push)
         return w.k["o"](o) if w.k is not None else Fn.linear(o, w.wo)
 
     # ------------------------------------------------------------------------------------------ context parallel
@@ -478,6 +485,9 @@ class MLAModel:
             from ..parallel.symm import TPComm
             self.dcp = D.DCPAttention(self.dcp_rank, self.dcp_world, T_max, c.num_heads, self.device, group)
             self.dcp_comm = TPComm(self.dcp_rank, self.dcp_world, T_max, c.hidden, self.device, group)
+            if all(l.k is not None and "o" in l.k and l.k["o"].Np == l.k["o"].N for l in self.layers):
+                # W_o's GEMM pushes its rows to every rank (the FFN share, a combine output, uses the pull form)
+                self.dcp_push = TPComm(self.dcp_rank, self.dcp_world, T_max, c.hidden, self.device, group, push=True)
         else:
             self.dcp = D.DCPAttentionRef(self.dcp_rank, self.dcp_world, c.num_heads, group)
             self.dcp_comm = None
@@ -529,7 +539,11 @@ class MLAModel:
                                torch.full_like(st.slot, -1)).to(torch.int32)
         qf, sel = (self._query_fused if self._fused_glue(w) else self._query_torch)(i, x, st, kv, lat_slot)
         o_g = self.dcp.decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt)          # [T, H / S, 512] merged
-        x2 = self._dcp_reduce(self._o_proj(w, o_g.contiguous(), t), h, w.n_post)   # h += attn; x2 = norm_post(h)
+        if self.dcp_push is not None:                                                # fused W_o -> all-reduce
+            self._o_proj(w, o_g.contiguous(), t, push=self.dcp_push)
+            x2 = self.dcp_push.reduce_norm2(t, h, None, w.n_post, c.rms_eps, plus_one=False)
+        else:
+            x2 = self._dcp_reduce(self._o_proj(w, o_g.contiguous(), t), h, w.n_post)   # h += attn; x2 = norm(h)
         return self._dcp_reduce(self._ffn_dcp(i, x2), h, next_norm)                 # h += ffn; next norm
 
     def _fused_glue(self, w: MLALayerWeights) -> bool:
@@ -552,7 +566,11 @@ class MLAModel:
         c, w = self.cfg, self.layers[i]
         t, dev, eps = x.shape[0], x.device, c.rms_eps
         cs = self.rope_table(max(st.max_ctx, 1) + 64)
-        ya = w.k["a"].lin(x)
+        x8, self._x8 = self._x8, None
+        if x8 is not None and x8[0] == x.data_ptr():    # the previous norm already wrote x block-quantized
+            ya = w.k["a"].lin.forward_quantized(x8[1], x8[2])
+        else:
+            ya = w.k["a"].lin(x)
         qa = torch.empty(t, c.q_lora, dtype=torch.bfloat16, device=dev)
         iw = torch.empty(t, c.index_heads, dtype=torch.float32, device=dev)
         fp8_b = w.k["b"].kind == "fp8" and c.q_lora % 128 == 0     # q_a leaves the kernel already block-quantized
@@ -608,9 +626,33 @@ class MLAModel:
         qf, sel = (self._query_fused if self._fused_glue(w) else self._query_torch)(i, x, st, kv)
         # absorbed sparse attention over the latent pool
         o_lat = M.mla_decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt, ws=kv.mla_ws.get((t, c.index_topk)))
-        x2 = B.rmsnorm(self._o_proj(w, o_lat, t), w.n_post, eps, residual=h)   # h += attn; x2 = norm_post(h)
-        f = self._ffn(i, x2)
-        return B.rmsnorm(f, next_norm, eps, residual=h)                      # h += ffn; next norm
+        # h += attn; x2 = norm_post(h), also block-quantized when the FFN's expert GEMMs take FP8 input
+        o = self._o_proj(w, o_lat, t)
+        xq8 = None
+        fp8_ffn = (self._quantized_ffn(i) and c.hidden % 128 == 0 and
+                   (c.expert_dtype if c.is_moe(i) else c.weight_dtype) == "fp8")
+        if fp8_ffn:
+            xq8 = (torch.empty(t, c.hidden, dtype=torch.uint8, device=o.device),
+                   torch.empty(t, c.hidden // 128, dtype=torch.int32, device=o.device))
+        x2 = B.rmsnorm(o, w.n_post, eps, residual=h, fp8=xq8)
+        f = self._ffn(i, x2, xq8)
+        return self._norm_out(f, next_norm, h, i + 1)                         # h += ffn; next norm
+
+    def _norm_out(self, f: torch.Tensor, norm_w: torch.Tensor, h: Optional[torch.Tensor], nxt: int) -> torch.Tensor:
+        """rmsnorm(h + f) with h updated (or rmsnorm(f) without h); when layer `nxt` takes its input through the
+        fused path with an FP8 first projection, the same kernel also writes the block-quantized copy that
+        projection reads (`_x8`, consumed once by `_query_fused`)."""
+        c = self.cfg
+        eps = c.rms_eps
+        if (nxt < self.n_target and self.cuda and c.hidden % 128 == 0 and self._fused_glue(self.layers[nxt])
+                and self.layers[nxt].k["a"].kind == "fp8"):
+            t = f.shape[0]
+            q8 = torch.empty(t, c.hidden, dtype=torch.uint8, device=f.device)
+            qs = torch.empty(t, c.hidden // 128, dtype=torch.int32, device=f.device)
+            out = B.rmsnorm(f, norm_w, eps, residual=h, fp8=(q8, qs))
+            self._x8 = (out.data_ptr(), q8, qs)
+            return out
+        return B.rmsnorm(f, norm_w, eps, residual=h)
 
     def forward(self, st: MLAStep, kv: MLAKVCache) -> torch.Tensor:
         """-> final-normed hidden [T, H]."""
@@ -619,7 +661,7 @@ class MLAModel:
     def forward_hidden(self, st: MLAStep, kv: MLAKVCache) -> tuple[torch.Tensor, torch.Tensor]:
         """-> (final-normed hidden [T, H], residual stream after the last target layer [T, H])."""
         h = B.embed(st.ids, self.embed)
-        x = B.rmsnorm(h, self.layers[0].n_in, self.cfg.rms_eps)
+        x = self._norm_out(h, self.layers[0].n_in, None, 0)
         n = self.n_target
         for i in range(n):
             nxt = self.layers[i + 1].n_in if i + 1 < n else self.final_norm

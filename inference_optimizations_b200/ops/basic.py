@@ -10,13 +10,16 @@ from .._ext import ext
 
 
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, plus_one: bool = False,
-            residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+            residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+            fp8: Optional[tuple] = None) -> torch.Tensor:
     """y = x * rsqrt(mean(x^2) + eps) * (1 + w if plus_one else w).  With `residual`, first residual <- x + residual
-    (in place, bf16) and normalise that sum (the fused add+norm of `attention/gemma-fused-glue/rtx_glue.py`)."""
+    (in place, bf16) and normalise that sum (the fused add+norm of `attention/gemma-fused-glue/rtx_glue.py`).
+    fp8 = (q8 uint8 [rows, H], qs int32 [rows, H / 128]): the CUDA kernel also writes y block-quantized for an FP8
+    GEMM (E4M3 + UE8M0 per 128; the bytes of quantizing y afterwards)."""
     if out is None:
         out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
     if x.is_cuda:
-        ext().rmsnorm(x, residual, out, weight, eps, plus_one)
+        ext().rmsnorm(x, residual, out, weight, eps, plus_one, *(fp8 if fp8 is not None else (None, None)))
         return out
     xf = x.float()
     if residual is not None:

@@ -27,49 +27,79 @@ def pack_bf16(w: torch.Tensor, g: int) -> torch.Tensor:
     return t.reshape(1, N // (TILE * g), kc, g * TILE * TILE)
 
 
-def split_k(n_tiles: int, tokens: int, nt: int, kc: int, ctas: int, min_chunks: int = 4, fill: int = 6) -> int:
-    """K splits for a weight-streaming GEMM with n_tiles output tiles.  None while the items fill a quarter of the
-    SMs or more; else the split count minimizing the critical path
-    waves x (K chunks per split + `fill`, the pipeline start of an item in chunk units), each K range at least
-    `min_chunks` chunks; ties keep fewer splits (no partials to reduce)."""
+def split_k(n_tiles: int, tokens: int, nt: int, kc: int, ctas: int, min_chunks: int = 4, fill: int = 6,
+            red: int = 8, g: int = 1) -> int:
+    """K splits for a weight-streaming GEMM with n_tiles output tiles (of 128 g columns): the split count minimizing
+    the critical path in units of one CTA's weight chunk (16 KB per 128-column tile):
+    waves x (K chunks per split + `fill`, an item's pipeline start) and, when split, + `red` (the reduction launch)
+    + the fp32 partials written and read back, spread over the CTAs; each K range at least `min_chunks` chunks; ties
+    keep fewer splits.  Unsplit once the items fill half the SMs.  (64 output tiles on 148 SMs: 60.7 us unsplit,
+    50.1 us split two ways, for the Gemma-31B sliding-window qkv projection at 32 tokens.)"""
     items = n_tiles * -(-tokens // nt)
-    if 4 * items > ctas:          # measured: splitting pays only when the output tiles fill under a quarter of the SMs
+    if 2 * items > ctas:
+        # measured (bf16 Gemma-31B and FP8 DSA shapes): with half the SMs busy or more, a last partial wave streams
+        # faster than the partials cost (168 tiles: 105 us unsplit, 115-143 us split 2-6 ways)
         return 1
     best, best_cost = 1, None
     for ks in range(1, max(1, kc // min_chunks) + 1):
         cost = -(-items * ks // ctas) * (-(-kc // ks) + fill)
+        if ks > 1:
+            cost += red + ks * tokens * n_tiles * 128 * g * 8 / (ctas * 16384 * g)
         if best_cost is None or cost < best_cost:
             best, best_cost = ks, cost
     return best
 
 
-def _splitk_gemm(lin, x, xs, out, t: int, kc: int, kind: int) -> None:
+def _splitk_gemm(lin, x, xs, out, t: int, kc: int, kind: int, push=None) -> None:
     """Run lin's GEMM with split-K when it helps: fp32 partials, then one deterministic reduction (to out's dtype:
-    bf16, or fp32 for an fp32 `out`)."""
+    bf16, or fp32 for an fp32 `out`).  push = (peers int64 [n], byte offset, n, rank): tensor-parallel push -- the
+    kernel writing the final bf16 rows (the GEMM itself, or the split-K reduction) stores each row into this rank's
+    slot of all n ranks' symmetric buffers (`out` is the local view of that slot, for the row stride)."""
     from .._ext import ext
     nt = FORCE["nt"] or MG.pick_nt(t)
     n_tiles = lin.N // (TILE * lin.g)
-    ks = FORCE["ks"] or split_k(n_tiles, t, nt, kc, lin.num_ctas)
+    ks = FORCE["ks"] or split_k(n_tiles, t, nt, kc, lin.num_ctas, g=lin.g)
     off, pairs, static = lin._index(t, x.device)
     f32 = out.dtype == torch.float32
+    if push is not None:
+        assert not f32 and out.stride(0) == lin.N, "push: bf16 rows of the full width"
     if ks == 1:
+        pk = {} if push is None else dict(out_peers=push[0], out_offset=push[1], out_bcast=push[2], out_rank=push[3])
         MG.gemm(lin.wpack, x, xs, off, pairs, out, lin.status, n_tiles=n_tiles, kc=kc, g=lin.g, nt=nt,
                 mode=MODE_F32_SPLIT if f32 else 0, src_div=1, num_ctas=lin.num_ctas, kind=kind,
-                split_rows=t if f32 else 0, static_index=static)
+                split_rows=t if f32 else 0, static_index=static, **pk)
         return
     key = (t, ks)
     if key not in lin._parts:
-        lin._parts[key] = torch.empty(ks * t, lin.N, dtype=torch.float32, device=x.device)
-    part = lin._parts[key]
+        # fp32 partials and the per-tile counters of the folded reduction (zero between launches: the split that
+        # completes a tile re-arms its counter)
+        lin._parts[key] = (torch.empty(ks * t, lin.N, dtype=torch.float32, device=x.device),
+                           torch.zeros(n_tiles * -(-t // nt), dtype=torch.int32, device=x.device))
+    part, cnt = lin._parts[key]
+    if FOLD_SPLITK[0] and t <= FOLD_MAX_TOKENS and push is None:
+        # few tokens: the split completing a tile reduces it (no reduction launch); with many tokens one CTA's share
+        # of the reduction would sit on the critical path, so the separate reduction kernel spreads it instead
+        MG.gemm(lin.wpack, x, xs, off, pairs, part, lin.status, n_tiles=n_tiles, kc=kc, g=lin.g, nt=nt,
+                mode=MODE_F32_SPLIT, src_div=1, num_ctas=lin.num_ctas, kind=kind, ksplit=ks, split_rows=t,
+                static_index=static, red_out=out, tile_cnt=cnt)
+        return
     MG.gemm(lin.wpack, x, xs, off, pairs, part, lin.status, n_tiles=n_tiles, kc=kc, g=lin.g, nt=nt,
             mode=MODE_F32_SPLIT, src_div=1, num_ctas=lin.num_ctas, kind=kind, ksplit=ks, split_rows=t,
             static_index=static)
-    ext().splitk_reduce(part, ks, out)
+    if push is None:
+        ext().splitk_reduce(part, ks, out, None, 0, 0, 0)
+    else:
+        ext().splitk_reduce(part, ks, out, push[0], push[1], push[2], push[3])
 
 
 MODE_F32_SPLIT = 3
 # tactic overrides for sweeps (utils/microbench.py proj_gemms --nt / --ks); None = the heuristics
 FORCE: dict = {"nt": None, "ks": None}
+# split-K reduction folded into the GEMM (the split completing a tile reduces it) instead of the separate reduction
+# kernel.  Off by default: measured at 8 and 64 decode tokens, the completing split's serial partial sums cost more
+# than the separate launch, whose start the programmatic dependent launch already overlaps.
+FOLD_SPLITK: list = [False]
+FOLD_MAX_TOKENS = 16
 
 
 class DenseLinear:
@@ -91,15 +121,21 @@ class DenseLinear:
                                                              torch.arange(t, dtype=torch.int32, device=dev)))
         return self._rows[t]
 
-    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, out_f32: bool = False) -> torch.Tensor:
-        """y = x W^T, bf16 out; out_f32: fp32 out (the accumulator as is, no rounding: router logits)."""
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, out_f32: bool = False,
+                 push=None) -> torch.Tensor:
+        """y = x W^T, bf16 out; out_f32: fp32 out (the accumulator as is, no rounding: router logits).  push: a
+        push-mode `parallel.symm.TPComm` -- the rows go to this rank's slot of every rank's buffer (the returned
+        tensor is the local copy) for the fused all-reduce that follows."""
         t = x.shape[0]
+        pk = None
+        if push is not None:
+            out, *pk = push.push_args(t)
         if out is None:
             out = torch.empty(t, self.N, dtype=torch.float32 if out_f32 else torch.bfloat16, device=x.device)
         if t == 0:
             return out
         xb = x.contiguous().view(torch.uint8)
-        _splitk_gemm(self, xb, xb, out, t, self.K // 64, 2)
+        _splitk_gemm(self, xb, xb, out, t, self.K // 64, 2, pk)
         return out
 
 
@@ -130,26 +166,31 @@ class Fp8Linear:
     def dequant(self) -> torch.Tensor:
         return MG.dequant_blocks(self.q, self.eb)[0]
 
-    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, push=None) -> torch.Tensor:
         from .._ext import ext
         t = x.shape[0]
-        if out is None:
+        if out is None and push is None:
             out = torch.empty(t, self.N, dtype=torch.bfloat16, device=x.device)
         if t == 0:
-            return out
+            return out if push is None else push.push_args(0)[0]
         xq = torch.empty(t, self.K, dtype=torch.uint8, device=x.device)
         xs = torch.empty(t, self.K // TILE, dtype=torch.int32, device=x.device)
         ext().rmsnorm_quant(x.contiguous(), None, 0.0, 0.0, xq, xs, 0)
-        return self.forward_quantized(xq, xs, out)
+        return self.forward_quantized(xq, xs, out, push)
 
-    def forward_quantized(self, xq: torch.Tensor, xs: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        """y = dequant(xq, xs) W^T for activations already quantized (E4M3 [T, K] + UE8M0 words [T, K / 128])."""
+    def forward_quantized(self, xq: torch.Tensor, xs: torch.Tensor, out: torch.Tensor | None = None,
+                          push=None) -> torch.Tensor:
+        """y = dequant(xq, xs) W^T for activations already quantized (E4M3 [T, K] + UE8M0 words [T, K / 128]).
+        push: a push-mode TPComm (see `DenseLinear`)."""
         t = xq.shape[0]
+        pk = None
+        if push is not None:
+            out, *pk = push.push_args(t)
         if out is None:
             out = torch.empty(t, self.N, dtype=torch.bfloat16, device=xq.device)
         if t == 0:
             return out
-        _splitk_gemm(self, xq, xs, out, t, self.K // TILE, 0)
+        _splitk_gemm(self, xq, xs, out, t, self.K // TILE, 0, pk)
         return out
 
 
@@ -240,10 +281,15 @@ class Linear:
         lin.widths = [w.shape[0] for w in ws]
         return lin
 
-    def __call__(self, x: torch.Tensor, out_f32: bool = False) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, out_f32: bool = False, push=None) -> torch.Tensor:
+        """push: a push-mode `parallel.symm.TPComm` (row-parallel projection whose all-reduce follows; the output
+        width must be the kernel's, no padding)."""
         if out_f32:
             assert self.kind == "bf16", "fp32 output is the bf16 GEMM's mode"
             y = self.lin(x, out_f32=True)
+        elif push is not None:
+            assert self.Np == self.N, "push: unpadded output width"
+            y = self.lin(x, push=push)
         else:
             y = self.lin(x)
         return y[:, :self.N] if self.Np != self.N else y

@@ -180,7 +180,8 @@ def gemm(wpack, x, x_scale, off, pairs, out, status, *, n_tiles: int, kc: int, g
          src_div: int, src_limit: int = 1 << 30, src_shared_base: int = 0, pair_w=None, out_scale=None, out_mul: float = 1.0,
          num_ctas: int = 148, kind: int = 0, expert_mul=None, out_peers=None, out_offset: int = 0, out_div: int = 1,
          out_rank: int = 0, out_shared_base: int = 0, pairs_total: int = 0, ksplit: int = 1,
-         split_rows: int = 0, src_group: int = 0, src_group_stride: int = 0, static_index: bool = False) -> None:
+         split_rows: int = 0, src_group: int = 0, src_group_stride: int = 0, static_index: bool = False,
+         red_out=None, tile_cnt=None, out_bcast: int = 0) -> None:
     """One grouped block-scaled GEMM launch (argument meanings: `MoeGemmArgs` in csrc/kernels.h).  Launched with
     programmatic dependent launch unless `PDL` is off: the kernel sets up (and, with `static_index` -- off / pairs
     complete before the previous kernel ran -- starts streaming weights) while the previous kernel finishes.  When
@@ -188,7 +189,7 @@ def gemm(wpack, x, x_scale, off, pairs, out, status, *, n_tiles: int, kc: int, g
     ext().moe_gemm(wpack, x, x_scale, off, pairs, pair_w, out, out_scale, status, n_tiles, kc, g, nt, mode, src_div,
                    src_limit, src_shared_base, out_mul, num_ctas, kind, expert_mul, out_peers, out_offset, out_div, out_rank,
                    out_shared_base, pairs_total, ksplit, split_rows, src_group, src_group_stride, TRACE[0], PDL[0],
-                   static_index)
+                   static_index, red_out, tile_cnt, out_bcast)
 
 
 TRACE: list = [None]
@@ -379,7 +380,7 @@ class BlockScaledExperts:
         return xq, xs
 
     def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, nt: int | None = None,
-                e0: int = 0) -> torch.Tensor:
+                e0: int = 0, xq8: Optional[tuple] = None) -> torch.Tensor:
         """x bf16 [T, H] (already normalized), ids int32 [T, k] (expert ids; this set holds experts e0 .. e0 + E - 1:
         pairs routed to others are not computed and must carry weight 0), w fp32 [T, k] -> bf16 [T, H]."""
         t, k = ids.shape
@@ -387,7 +388,8 @@ class BlockScaledExperts:
         P = t * k
         extra = t if self.has_shared else 0
         E = self.E + int(self.has_shared)
-        xq, xs = self._quant_x(x)
+        # xq8: x already block-quantized by the norm that produced it (FP8 experts only)
+        xq, xs = xq8 if (xq8 is not None and self.kind == 0) else self._quant_x(x)
         off = torch.empty(E + 1, dtype=torch.int32, device=dev)
         pairs = torch.empty(P + extra, dtype=torch.int32, device=dev)
         ext().moe_align(ids.contiguous().view(-1), e0, self.E, extra, off, pairs)

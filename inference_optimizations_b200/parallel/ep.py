@@ -124,16 +124,20 @@ class EPMoE:
     def barrier(self) -> None:
         ext().ep_barrier(self.peers, self.layout.off_flags, self.rank, self.world, self.epoch, self.status)
 
-    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        """x bf16 [T, H] normalized, ids int32 [T, topk] global expert ids, w fp32 [T, topk] -> bf16 [T, H]."""
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, xq8: tuple | None = None) -> torch.Tensor:
+        """x bf16 [T, H] normalized, ids int32 [T, topk] global expert ids, w fp32 [T, topk] -> bf16 [T, H].
+        xq8: (E4M3 [T, H], scales [T, H / 128]) when the norm that produced x already quantized it (FP8 experts)."""
         L, ex = self.layout, self.ex
         T, k = ids.shape
         if T > self.T_max:
             raise ValueError(f"{T} tokens > T_max {self.T_max}")
-        if T:
-            ext().rmsnorm_quant(x.contiguous(), None, 0.0, 0.0, self.xq[:T], self.xs[:T], self.kind)
-        ext().ep_dispatch(self.peers, self.xq[:T], self.xs[:T], ids.contiguous(), L.off_x, L.off_s, L.off_ids,
-                          self.T_max, self.rank, self.world, self.E_loc)
+        xq, xs = self.xq[:T], self.xs[:T]
+        if xq8 is not None and self.kind == 0 and T:
+            xq, xs = xq8
+        elif T:
+            ext().rmsnorm_quant(x.contiguous(), None, 0.0, 0.0, xq, xs, self.kind)
+        ext().ep_dispatch(self.peers, xq, xs, ids.contiguous(), L.off_x, L.off_s, L.off_ids, self.T_max, self.rank,
+                          self.world, self.E_loc)
         self.barrier()
         extra = T if ex.has_shared else 0
         ext().moe_align(self.recv_ids, self.rank * self.E_loc, self.E_loc, extra, self.off, self.pairs)
@@ -173,7 +177,7 @@ class EPMoERef:
         self.w_gu, self.w_down, self.shared, self.group = w_gu, w_down, shared, group
         self.H = w_down.shape[1]
 
-    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, xq8: tuple | None = None) -> torch.Tensor:
         from ..ops import moe as MOE
         T, k = ids.shape
         if T > self.T_max:

@@ -365,6 +365,104 @@ def ep_moe_case(tokens: int, total_experts: int, topk: int, hidden: int, ffn: in
     return res if rank == 0 else {}
 
 
+def tp_gemm_ar_case(tokens: list, K: int, N: int, reps: int = 10, iters: int = 20) -> list:
+    """Row-parallel projection + all-reduce + the Gemma norm chain under torchrun (one rank per GPU), three ways:
+    `push` -- this framework's GEMM stores its tiles into every rank's slot, then the slot-sum + norm kernel (the
+    fused GEMM -> all-reduce); `pull` -- the same GEMM into the own buffer, then the peer-load reduce + norm kernel;
+    `nccl` -- the same GEMM, NCCL all-reduce, two RMSNorm kernels; `nvls` (where the buffer has an NVLink multicast
+    mapping) -- the same GEMM, then the switch-side reduce + norm kernel.  Each variant is `reps` layers captured in one CUDA
+    graph, cycling over enough weight copies that the weights stream from HBM (> 2x L2); device time per layer, max
+    over ranks.  Roofline per layer: max(weight bytes / measured HBM, partial rows crossing NVLink / 770 GB/s)."""
+    import torch.distributed as dist
+    from ..ops import basic as B
+    from ..ops import linear as L
+    from ..parallel.symm import TPComm
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    n_w = max(2, -(-(256 << 20) // (N * K * 2)))
+    lins = [L.Linear((torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16), "bf16")
+            for _ in range(n_w)]
+    tmax = max(tokens)
+    cp = TPComm(rank, world, tmax, N, dev, push=True)
+    cq = TPComm(rank, world, tmax, N, dev, push=False)
+    try:
+        cn = TPComm(rank, world, tmax, N, dev, nvls=True)
+    except RuntimeError:
+        cn = None
+    have = torch.tensor([0.0 if cn is None else 1.0], device=dev)
+    dist.all_reduce(have, op=dist.ReduceOp.MIN)          # every rank runs the same variants
+    if have.item() == 0:
+        cn = None
+    w1 = (torch.randn(N, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+    w2 = (torch.randn(N, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+    rows = []
+    for t in tokens:
+        x = torch.randn(t, K, device=dev, generator=g).to(torch.bfloat16)
+        resid = torch.randn(t, N, device=dev, generator=g).to(torch.bfloat16)
+
+        def push():
+            for r in range(reps):
+                lins[r % n_w](x, push=cp)
+                cp.reduce_norm2(t, resid, w1, w2, 1e-6)
+
+        def pull():
+            for r in range(reps):
+                lins[r % n_w].lin(x, out=cq.out_buffer(t))
+                cq.reduce_norm2(t, resid, w1, w2, 1e-6)
+
+        def nvls():
+            for r in range(reps):
+                lins[r % n_w].lin(x, out=cn.out_buffer(t))
+                cn.reduce_norm2(t, resid, w1, w2, 1e-6)
+
+        def nccl():
+            for r in range(reps):
+                y = lins[r % n_w](x)
+                dist.all_reduce(y)
+                o = B.rmsnorm(y, w1, 1e-6, True)
+                B.rmsnorm(o, w2, 1e-6, True, residual=resid)
+
+        row = {"kernel": "tp_gemm_ar", "world": world, "tokens": t, "K": K, "N": N}
+        variants = [("push", push), ("pull", pull), ("nccl", nccl)] + ([("nvls", nvls)] if cn is not None else [])
+        for name, fn in variants:
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            dist.barrier()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                fn()
+            for _ in range(3):
+                gr.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                gr.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            dist.barrier()
+            us = torch.tensor([e0.elapsed_time(e1) * 1e3 / (iters * reps)], device=dev)
+            dist.all_reduce(us, op=dist.ReduceOp.MAX)
+            row[f"{name}_us"] = round(float(us), 2)
+            del gr
+        cp.check()
+        cq.check()
+        if cn is not None:
+            cn.check()
+        t_hbm = N * K * 2 / (PEAKS["hbm_gbs"] * 1e3)
+        t_nvl = (world - 1) * t * N * 2 / (770.0 * 1e3)
+        row.update(roofline_us=round(max(t_hbm, t_nvl), 2), hbm_us=round(t_hbm, 2), nvlink_us=round(t_nvl, 2),
+                   push_frac_of_roofline=round(max(t_hbm, t_nvl) / row["push_us"], 3),
+                   roofline_basis="max(weights / measured HBM, (world-1) x partial rows / 770 GB/s)")
+        rows.append(row)
+    torch.cuda.synchronize()
+    dist.barrier()
+    return rows if rank == 0 else []
+
+
 def moe_tactics_case(experts: int, total_experts: int, topk: int, hidden: int, ffn: int, wfmt: str) -> dict:
     """Sweep the token tile (MMA N) of the grouped GEMMs over decode / prefill token counts; the fastest per count
     (gate_up + down device time) forms the tactic table `ops/moe_tactics.json`."""
@@ -479,6 +577,39 @@ def proj_gemms_case(tokens: list, only: str = "") -> list:
             if gemm:
                 row["gemm_kernel_frac_hbm"] = round(wbytes / gemm / 1e3 / PEAKS["hbm_gbs"], 3)
             out.append(row)
+    return out
+
+
+def dense_gemms_case(tokens: list, only: str = "") -> list:
+    """The Gemma-class (31B) dense projections at one GPU's full width, bf16: this framework's weight-streaming GEMM
+    (`ops/linear.py Linear`, split-K by `split_k`) against cuBLAS (`torch.nn.functional.linear`) on the same weights,
+    each call timed alone with CUDA events and the L2 flushed before it."""
+    import torch.nn.functional as Fn
+    from ..ops import linear as L
+    from ..ops import moe_gemm as MG
+    dev = torch.device("cuda:0")
+    h = 5376
+    shapes = {"qkv_swa": (16384, h), "qkv_global": (32768, h), "o_swa": (h, 8192), "o_global": (h, 16384),
+              "gate_up": (43008, h), "down": (h, 21504), "lm_head": (262144, h)}
+    out = []
+    for name, (N, K) in shapes.items():
+        if only and name not in only.split(","):
+            continue
+        w = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
+        lin = L.Linear(w, "bf16")
+        for t in tokens:
+            x = torch.randn(t, K, device=dev).to(torch.bfloat16)
+            ours = _time_flushed(lambda: lin(x))
+            cub = _time_flushed(lambda: Fn.linear(x, w))
+            wbytes = N * K * 2
+            nt = L.FORCE["nt"] or MG.pick_nt(t)
+            ks = L.FORCE["ks"] or L.split_k(N // (128 * lin.lin.g), t, nt, K // 64, lin.lin.num_ctas, g=lin.lin.g)
+            row = {"op": name, "N": N, "K": K, "tokens": t, "nt": nt, "ksplit": ks, "ours_us": round(ours, 1),
+                   "cublas_us": round(cub, 1), "ours_frac_hbm": round(wbytes / ours / 1e3 / PEAKS["hbm_gbs"], 3),
+                   "cublas_frac_hbm": round(wbytes / cub / 1e3 / PEAKS["hbm_gbs"], 3),
+                   "kernels_us": _kernel_times(lambda: lin(x))}
+            out.append(row)
+        del lin, w
     return out
 
 
@@ -708,6 +839,15 @@ def main() -> None:
         dist.destroy_process_group()
         if rank:
             r = {}
+    elif a.kernel == "tp_gemm_ar":
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", device_id=torch.device("cuda", torch.cuda.current_device()))
+        for row in tp_gemm_ar_case([int(v) for v in a.tokens.split(",")], a.ffn, a.hidden):
+            print(json.dumps(row), flush=True)
+        dist.barrier()
+        dist.destroy_process_group()
+        r = {}
     elif a.kernel == "moe_gemm":
         r = moe_gemm_case(a.b, a.experts, a.total_experts, a.topk, a.hidden, a.ffn, a.wfmt, a.launches)
     elif a.kernel == "proj_gemms":
@@ -717,6 +857,15 @@ def main() -> None:
                 L.FORCE.update(nt=nt, ks=ks)
                 for row in proj_gemms_case([int(v) for v in a.tokens.split(",")], a.only):
                     row.update(nt=nt, ks=ks)
+                    print(json.dumps(row), flush=True)
+        L.FORCE.update(nt=None, ks=None)
+        r = {}
+    elif a.kernel == "dense_gemms":
+        from ..ops import linear as L
+        for nt in [int(v) for v in a.nt.split(",")] if a.nt else [None]:
+            for ks in [int(v) for v in a.ks.split(",")] if a.ks else [None]:
+                L.FORCE.update(nt=nt, ks=ks)
+                for row in dense_gemms_case([int(v) for v in a.tokens.split(",")], a.only):
                     print(json.dumps(row), flush=True)
         L.FORCE.update(nt=None, ks=None)
         r = {}

@@ -147,3 +147,51 @@ def test_mla_fused_glue_matches_torch_glue(cuda, kv):
         assert (a != b).float().mean().item() < 0.01          # a few rounding-boundary flips at most
     cos = torch.nn.functional.cosine_similarity(l0, l1, dim=-1)
     assert cos.min().item() > 0.999, cos.min().item()
+
+
+@pytest.mark.parametrize("kind,t", [("fp8", 8), ("fp8", 64), ("bf16", 8)])
+def test_folded_splitk_equals_separate_reduction(cuda, kind, t):
+    """The split-K reduction folded into the GEMM (the split completing a tile sums the partials) gives the separate
+    reduction kernel's bits, on repeated calls (the tile counters re-arm) and for fp32 output."""
+    torch.manual_seed(t)
+    w = (torch.randn(7168, 16384, device=cuda) * 0.02).to(torch.bfloat16)
+    x = torch.randn(t, 16384, device=cuda).to(torch.bfloat16)
+    lin = L.Linear(w, kind)
+    ref = lin(x).clone()
+    fold_max, L.FOLD_MAX_TOKENS = L.FOLD_MAX_TOKENS, 1 << 20      # fold at every token count for this test
+    L.FOLD_SPLITK[0] = True
+    try:
+        for _ in range(3):
+            assert torch.equal(lin(x), ref)
+    finally:
+        L.FOLD_MAX_TOKENS = fold_max
+        L.FOLD_SPLITK[0] = False
+    if kind == "bf16":
+        ref32 = lin(x, out_f32=True).clone()
+        L.FOLD_SPLITK[0] = True
+        try:
+            assert torch.equal(lin(x, out_f32=True), ref32)
+        finally:
+            L.FOLD_SPLITK[0] = False
+
+
+def test_rmsnorm_fp8_output_equals_separate_quant(cuda):
+    """RMSNorm (+ residual) writing the FP8 block-scaled copy gives the bytes of quantizing its bf16 output with the
+    activation-quantization kernel afterwards."""
+    from inference_optimizations_b200._ext import ext
+    from inference_optimizations_b200.ops import basic as B
+    torch.manual_seed(9)
+    t, h = 37, 7168
+    x = torch.randn(t, h, device=cuda).to(torch.bfloat16)
+    res = torch.randn(t, h, device=cuda).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(h, device=cuda)).to(torch.bfloat16)
+    res2 = res.clone()
+    q8 = torch.empty(t, h, dtype=torch.uint8, device=cuda)
+    qs = torch.empty(t, h // 128, dtype=torch.int32, device=cuda)
+    y = B.rmsnorm(x, w, 1e-6, residual=res, fp8=(q8, qs))
+    y_ref = B.rmsnorm(x, w, 1e-6, residual=res2)
+    rq = torch.empty_like(q8)
+    rs = torch.empty_like(qs)
+    ext().rmsnorm_quant(y_ref, None, 0.0, 0.0, rq, rs, 0)
+    assert torch.equal(y, y_ref) and torch.equal(res, res2)
+    assert torch.equal(q8, rq) and torch.equal(qs, rs)
