@@ -49,6 +49,9 @@ def parse():
     p.add_argument("--spec", type=int, default=1,
                    help="gemma31b: 1 = speculative decoding, the config's 1-layer draft proposing 3 tokens; 0 = plain")
     p.add_argument("--no-graphs", action="store_true")
+    p.add_argument("--tp-form", default="push", choices=["push", "pull", "nvls"],
+                   help="gemma31b, tp > 1: fused GEMM -> all-reduce form (push: GEMM epilogue stores to every rank; "
+                        "pull: peer-load reduce; nvls: switch-side reduction)")
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                    help="gemma31b tensor-parallel all-reduce: own peer-memory kernel fused with the norms or NCCL")
     a = p.parse_args()
@@ -295,7 +298,8 @@ def bench_gemma(args) -> int:
     max_new = max(args.max_new, 4 * (steps + warm) + 2 * steps + 16)
     ecfg = EngineConfig(model=args.model, device=str(dev), kv_dtype=args.kv, max_running=args.sessions,
                         chunked_prefill=2048, spec=bool(args.spec), cuda_graphs=not args.no_graphs,
-                        graph_batch_sizes=str(args.sessions), tp=tp, fused_comm=args.comm == "fused")
+                        graph_batch_sizes=str(args.sessions), tp=tp, fused_comm=args.comm == "fused",
+                        tp_push=args.tp_form == "push", tp_nvls=args.tp_form == "nvls")
     max_seq = args.ctx + max_new + 64
     eng = Engine(ecfg, cfg, max_seq=max_seq, tp_rank=rank, tp=tp,
                  all_reduce=D.nccl_all_reduce if tp > 1 else None,
@@ -383,7 +387,7 @@ def bench_gemma(args) -> int:
                             "head_dim 256 on SWA-1024 layers and 512 on every 6th (global) layer, GeGLU 21504, "
                             "vocab 262144",
                    "global_batch": args.sessions, "seq_len": args.ctx, "parallelism": f"tp{tp}",
-                   "kv_cache": args.kv, "tp_comm": args.comm if tp > 1 else None, "speculative": bool(ecfg.spec), "draft_tokens": ecfg.draft_tokens if ecfg.spec else 0,
+                   "kv_cache": args.kv, "tp_comm": (args.tp_form if args.comm == "fused" else "nccl") if tp > 1 else None, "speculative": bool(ecfg.spec), "draft_tokens": ecfg.draft_tokens if ecfg.spec else 0,
                    "accept_per_step": accept,
                    "l2": "no flush: every step reads weights + KV (~170 GB at N=1), far larger than the 126 MB L2"},
         "per_user_tok_s": round(value / args.sessions, 3),

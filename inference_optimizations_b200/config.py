@@ -200,6 +200,7 @@ class EngineConfig:
     fused_comm: bool = True              # own peer-memory kernels for collectives; False = NCCL baseline
     tp_push: bool = True                 # TP: row-parallel GEMMs push their tiles to every rank (fused GEMM ->
                                          # all-reduce); False = GEMM, then a pull-form reduce over NVLink
+    tp_nvls: bool = False                # TP: switch-side reduction (NVLS multimem) after the GEMM instead of push
     # diagnostics
     trace: str = ""                      # directory for the per-rank scheduler trace (JSONL); empty = off
     bounds_check: bool = False           # host-polled index checks before kernels (the IMA locator)

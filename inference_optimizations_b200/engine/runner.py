@@ -97,8 +97,9 @@ class GQARunner:
         if tp > 1 and ecfg.fused_comm and self.device.type == "cuda":
             from ..parallel.symm import TPComm
             rows = max(ecfg.chunked_prefill, 4 * max(ecfg.graph_sizes() + [ecfg.max_running]))
-            push = ecfg.tp_push and self.model.can_push() and (self.draft is None or self.draft.can_push())
-            self.tp_comm = TPComm(tp_rank, tp, rows, cfg.hidden, self.device, push=push)
+            push = (ecfg.tp_push and not ecfg.tp_nvls and self.model.can_push()
+                    and (self.draft is None or self.draft.can_push()))
+            self.tp_comm = TPComm(tp_rank, tp, rows, cfg.hidden, self.device, push=push, nvls=ecfg.tp_nvls)
             self.model.tp_comm = self.tp_comm
             if self.draft is not None:
                 self.draft.tp_comm = self.tp_comm

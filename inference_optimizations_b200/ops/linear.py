@@ -33,13 +33,10 @@ def split_k(n_tiles: int, tokens: int, nt: int, kc: int, ctas: int, min_chunks: 
     the critical path in units of one CTA's weight chunk (16 KB per 128-column tile):
     waves x (K chunks per split + `fill`, an item's pipeline start) and, when split, + `red` (the reduction launch)
     + the fp32 partials written and read back, spread over the CTAs; each K range at least `min_chunks` chunks; ties
-    keep fewer splits.  Unsplit once the items fill half the SMs.  (64 output tiles on 148 SMs: 60.7 us unsplit,
-    50.1 us split two ways, for the Gemma-31B sliding-window qkv projection at 32 tokens.)"""
+    keep fewer splits.  Measured kernel time at 32 tokens, Gemma-31B bf16 shapes: 64 output tiles (sliding qkv)
+    47.9 us unsplit / 35.6 us in 2; 168 tiles (gate_up) 101 us unsplit / 84 us in 2-6; 21 tiles (o) 67.9 us unsplit
+    / 22 us in 6-7."""
     items = n_tiles * -(-tokens // nt)
-    if 2 * items > ctas:
-        # measured (bf16 Gemma-31B and FP8 DSA shapes): with half the SMs busy or more, a last partial wave streams
-        # faster than the partials cost (168 tiles: 105 us unsplit, 115-143 us split 2-6 ways)
-        return 1
     best, best_cost = 1, None
     for ks in range(1, max(1, kc // min_chunks) + 1):
         cost = -(-items * ks // ctas) * (-(-kc // ks) + fill)
