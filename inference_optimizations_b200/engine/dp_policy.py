@@ -103,6 +103,10 @@ class DPBalancer:
     def route(self, tokens: Sequence[int], t: float) -> int:
         c = self.costs(tokens)
         rank = min(range(self.dp), key=lambda i: (c[i], self.ranks[i].requests, i))
+        return self.pin(tokens, rank, t)
+
+    def pin(self, tokens: Sequence[int], rank: int, t: float) -> int:
+        """Account a request the client pinned to `rank` (the balancer's state stays the same on every rank)."""
         r = self.ranks[rank]
         hs = block_hashes(tokens, self.block)
         uncached = len(tokens) - r.index.match_blocks(hs) * self.block

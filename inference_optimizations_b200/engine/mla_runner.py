@@ -113,7 +113,7 @@ class MLARunner:
             self.kv.table.set(r.slot, lp, node.page)
         rp.high = len(path)
         rp.cached = path
-        r.prefilled = r.kv_len = 64 * len(path)
+        r.prefilled = r.kv_len = r.cached_tokens = 64 * len(path)
 
     def detach(self, r: Request) -> None:
         rp = self.pages.pop(r.rid, None)

@@ -43,6 +43,7 @@ class Request:
     draft_state: dict = field(default_factory=dict)
     accepted: int = 0              # speculative: drafts accepted in total
     spec_steps: int = 0
+    cached_tokens: int = 0         # prompt tokens whose KV came from the prefix cache at admission
 
     @property
     def prompt_len(self) -> int:

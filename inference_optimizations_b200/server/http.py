@@ -2,6 +2,10 @@
 
     POST /generate     {"input_ids": [...], "max_new_tokens": n}  or {"prompts": [[...], ...], ...}
                        -> {"output_ids": [...]} / {"outputs": [[...], ...]}
+                       "stream": true (one prompt) -> newline-delimited JSON as the tokens are produced:
+                       {"token_ids": [...]} per engine step, then {"done": true, "output_ids": [...]}
+                       "dp_rank": r pins the request to data-parallel rank r of a ranked deployment (a session's turns
+                       stay on the rank that caches its prefix); default: the cache-aware balancer
     POST /flush_cache  drops cached prefixes (radix cache) once no request is running
     GET  /health       {"ok": true, "running": r, "waiting": w}
     GET  /metrics      Prometheus text: request / token / step counters, time to first token and per-request decode
@@ -36,18 +40,55 @@ class EngineLoop:
         self.t_first: dict = {}
         self.ttft: list = []                      # seconds, finished requests
         self.user_rate: list = []                 # decode tok/s per finished request (after its first token)
+        self.stream: dict = {}                    # rid -> tokens produced so far (streamed requests)
+        self.meta: dict = {}                      # rid -> {"prompt_tokens", "cached_tokens"} of finished requests
         self.stop = False
         self.idle_sleep = idle_sleep
         self.thread = threading.Thread(target=self._run, daemon=True)
         self.thread.start()
 
-    def submit(self, prompt: list, max_new: int) -> int:
+    def submit(self, prompt: list, max_new: int, stream: bool = False, dp_rank: Optional[int] = None) -> int:
         with self.lock:
             r = self.engine.add_request(list(prompt), SamplingParams(max_new_tokens=max_new))
             self.counters["requests"] += 1
             self.t_submit[r.rid] = time.perf_counter()
+            if stream:
+                self.stream[r.rid] = []
             self.cv.notify_all()
             return r.rid
+
+    def _emit(self, rid, toks) -> None:
+        """Tokens of one engine step for request rid (lock held)."""
+        if rid in self.stream:
+            self.stream[rid].extend(toks)
+
+    def stream_tokens(self, rid: int, timeout: float = 600.0):
+        """Generator of newline-delimited JSON for a streamed request: each batch of new tokens, then the final
+        record (the request's output)."""
+        import json
+        sent, deadline = 0, time.time() + timeout
+        while True:
+            with self.lock:
+                while True:
+                    toks = self.stream.get(rid, [])
+                    done = rid in self.done
+                    if len(toks) > sent or done:
+                        break
+                    if time.time() > deadline:
+                        raise TimeoutError(f"request {rid} not finished in {timeout} s")
+                    self.cv.wait(1.0)
+                new = toks[sent:]
+                sent = len(toks)
+                final = None
+                if done:
+                    final = self.done.pop(rid)
+                    meta = self.meta.pop(rid, {})
+                    self.stream.pop(rid, None)
+            if new:
+                yield json.dumps({"token_ids": new}) + "\n"
+            if final is not None:
+                yield json.dumps({"done": True, "output_ids": final, "meta_info": meta}) + "\n"
+                return
 
     def wait(self, rid: int, timeout: float = 600.0) -> list:
         deadline = time.time() + timeout
@@ -69,11 +110,13 @@ class EngineLoop:
                 now = time.perf_counter()
                 self.counters["steps"] += 1
                 self.counters["tokens_out"] += sum(len(v) for v in out.values())
-                for rid in out:
+                for rid, toks in out.items():
                     self.t_first.setdefault(rid, now)
+                    self._emit(rid, toks)
                 for r in self.engine.finished:
                     if r.rid not in self.done:
                         self.done[r.rid] = list(r.output)
+                        self.meta[r.rid] = {"prompt_tokens": r.prompt_len, "cached_tokens": r.cached_tokens}
                         self._record(r, now)
                 self.engine.finished.clear()
                 self.cv.notify_all()
@@ -124,13 +167,16 @@ class RankedEngineLoop(EngineLoop):
             self.balancer = DPBalancer(world)
         super().__init__(engine)
 
-    def submit(self, prompt: list, max_new: int) -> int:
+    def submit(self, prompt: list, max_new: int, stream: bool = False, dp_rank: Optional[int] = None) -> int:
         with self.lock:
             gid = self.next_id
             self.next_id += 1
-            self.inbox.append((gid, list(prompt), int(max_new)))
+            pin = None if dp_rank is None or self.mode != "dp" else int(dp_rank) % self.world
+            self.inbox.append((gid, list(prompt), int(max_new), pin))
             self.counters["requests"] += 1
             self.t_submit[gid] = time.perf_counter()
+            if stream:
+                self.stream[gid] = []
             self.cv.notify_all()
             return gid
 
@@ -152,8 +198,13 @@ class RankedEngineLoop(EngineLoop):
             if stop:
                 return
             with self.lock:
-                for gid, prompt, max_new in new:
-                    if self.mode == "tp" or self.balancer.route(prompt, t=float(gid)) == self.rank:
+                for gid, prompt, max_new, pin in new:
+                    if self.mode == "dp" and pin is not None:
+                        self.balancer.pin(prompt, pin, t=float(gid))
+                        mine = pin == self.rank
+                    else:
+                        mine = self.mode == "tp" or self.balancer.route(prompt, t=float(gid)) == self.rank
+                    if mine:
                         r = eng.add_request(prompt, SamplingParams(max_new_tokens=max_new))
                         self.local_to_global[r.rid] = gid
                 hold, cap, work = None, 0, eng.has_work()
@@ -170,31 +221,44 @@ class RankedEngineLoop(EngineLoop):
                         cap = prefill_budget([r[6] for r in rows], eng.ecfg.chunked_prefill,
                                              min_tokens=min(2048, eng.ecfg.chunked_prefill), page=eng.ecfg.page_size)
                 any_work = work
-                finished = []
+                finished, emitted = [], []
                 if work:
                     out = eng.step(hold=hold, chunk_cap=cap)
                     self.delayed = self.delayed + 1 if hold else 0
                     now = time.perf_counter()
                     self.counters["steps"] += 1
                     self.counters["tokens_out"] += sum(len(v) for v in out.values())
-                    for rid in out:
+                    for rid, toks in out.items():
                         gid = self.local_to_global.get(rid)
                         if gid is not None:
                             self.t_first.setdefault(gid, now)
+                            emitted.append((gid, list(toks)))
                     for r in eng.finished:
                         gid = self.local_to_global.pop(r.rid, None)
                         if gid is not None:
-                            finished.append((gid, list(r.output), len(r.output)))
+                            finished.append((gid, list(r.output), len(r.output), r.prompt_len, r.cached_tokens))
                     eng.finished.clear()
-            if self.mode == "dp":                 # every rank's finished requests reach rank 0
+            if self.mode == "dp":                 # every rank's new tokens and finished requests reach rank 0
                 got = [None] * self.world if self.rank == 0 else None
-                dist.gather_object(finished, got, dst=0, group=self.group)
-                finished = [x for part in got for x in part] if self.rank == 0 else []
+                dist.gather_object((emitted, finished), got, dst=0, group=self.group)
+                if self.rank == 0:
+                    emitted = [x for part in got for x in part[0]]
+                    finished = [x for part in got for x in part[1]]
+                else:
+                    emitted, finished = [], []
+            if self.rank == 0 and emitted:
+                with self.lock:
+                    now = time.perf_counter()
+                    for gid, toks in emitted:
+                        self.t_first.setdefault(gid, now)
+                        self._emit(gid, toks)
+                    self.cv.notify_all()
             if self.rank == 0 and finished:
                 with self.lock:
                     now = time.perf_counter()
-                    for gid, output, n in finished:
+                    for gid, output, n, plen, cached in finished:
                         self.done[gid] = output
+                        self.meta[gid] = {"prompt_tokens": plen, "cached_tokens": cached}
                         t0, t1 = self.t_submit.pop(gid, None), self.t_first.pop(gid, None)
                         if t0 is not None:
                             self.ttft.append((t1 or now) - t0)
@@ -211,19 +275,31 @@ class RankedEngineLoop(EngineLoop):
 
 def make_app(loop: EngineLoop):
     from fastapi import FastAPI, HTTPException
-    from fastapi.responses import PlainTextResponse
+    from fastapi.responses import PlainTextResponse, StreamingResponse
 
     app = FastAPI()
 
     @app.post("/generate")
     def generate(body: dict):
         max_new = int(body.get("max_new_tokens", body.get("sampling_params", {}).get("max_new_tokens", 16)))
+        pin = body.get("dp_rank")
         if "prompts" in body:
-            rids = [loop.submit(p, max_new) for p in body["prompts"]]
-            return {"outputs": [loop.wait(r) for r in rids]}
+            rids = [loop.submit(p, max_new, dp_rank=pin) for p in body["prompts"]]
+            outs = [loop.wait(r) for r in rids]
+            with loop.lock:
+                for r in rids:
+                    loop.meta.pop(r, None)
+            return {"outputs": outs}
         if "input_ids" not in body:
             raise HTTPException(400, "input_ids or prompts required")
-        return {"output_ids": loop.wait(loop.submit(body["input_ids"], max_new))}
+        if body.get("stream"):
+            rid = loop.submit(body["input_ids"], max_new, stream=True, dp_rank=pin)
+            return StreamingResponse(loop.stream_tokens(rid), media_type="application/x-ndjson")
+        rid = loop.submit(body["input_ids"], max_new, dp_rank=pin)
+        out = loop.wait(rid)
+        with loop.lock:
+            meta = loop.meta.pop(rid, {})
+        return {"output_ids": out, "meta_info": meta}
 
     @app.post("/flush_cache")
     def flush_cache():
