@@ -170,6 +170,7 @@ class EngineConfig:
     model: str = "gemma31b"
     device: str = "cuda"
     seed: int = 0
+    checkpoint: str = ""                 # HuggingFace safetensors directory (empty: seeded random-init weights)
     # KV pool
     page_size: int = 64
     kv_dtype: str = "nvfp4"              # "nvfp4" | "fp8" | "bf16" (GQA pools); MLA: "nvfp4" (352 B) | "fp8" (576 B)

@@ -56,12 +56,18 @@ class MLARunner:
         self.dcp_world, self.dcp_rank = max(1, ecfg.dcp), dcp_rank
         if self.dcp_world > 1 and (self.spec or self.ep_world > 1):
             raise NotImplementedError("decode context parallelism runs without speculation or expert parallelism")
+        src = None
+        if ecfg.checkpoint:                          # HuggingFace DeepSeek-V3-layout checkpoint (this rank's experts)
+            from ..models.mla_loader import HFMLASource
+            src = HFMLASource(ecfg.checkpoint, cfg, self.device)
         self.model = MLAModel(cfg, self.device, ecfg.seed, ep_rank=ep_rank, ep_world=self.ep_world,
-                              dcp_rank=dcp_rank, dcp_world=self.dcp_world)
+                              dcp_rank=dcp_rank, dcp_world=self.dcp_world, source=src)
         if self.dcp_world > 1:
             self.model.attach_dcp(dcp_group, max(2 * ecfg.max_running, ecfg.chunked_prefill))
         if self.spec:
             self.model.build_draft(ecfg.seed)
+        if src is not None:
+            src.close()
         if self.ep_world > 1:
             # tokens per exchange: a decode step of every running request (with its draft), or a prefill piece
             self.ep_T_max = max(2 * ecfg.max_running, min(ecfg.chunked_prefill, 1024))

@@ -89,10 +89,17 @@ class GQARunner:
         self.tp, self.tp_rank = tp, tp_rank
         self.max_seq = max_seq
         self.argmax_merge = argmax_merge
-        self.model = GQAModel(cfg, device, tp_rank, tp, ecfg.seed, all_reduce)
+        ck = None
+        if ecfg.checkpoint:                          # this rank's tensor-parallel shards of a HuggingFace checkpoint
+            from ..models.loader import open_checkpoint, shard_gqa
+            ck = open_checkpoint(ecfg.checkpoint)
+        self.model = GQAModel(cfg, device, tp_rank, tp, ecfg.seed, all_reduce,
+                              weights=shard_gqa(ck, cfg, tp_rank, tp, device) if ck else None)
         self.spec = ecfg.spec
         self.n_draft = ecfg.draft_tokens if ecfg.spec else 0
-        self.draft = GQAModel(cfg, device, tp_rank, tp, ecfg.seed, all_reduce, draft=True) if self.spec else None
+        self.draft = GQAModel(cfg, device, tp_rank, tp, ecfg.seed, all_reduce, draft=True,
+                              weights=shard_gqa(ck, cfg, tp_rank, tp, device, draft=True) if ck else None) \
+            if self.spec else None
         self.tp_comm = None
         if tp > 1 and ecfg.fused_comm and self.device.type == "cuda":
             from ..parallel.symm import TPComm

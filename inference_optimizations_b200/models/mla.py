@@ -54,11 +54,18 @@ def _rand(name: str, shape, std: float, device, seed: int) -> torch.Tensor:
     return t
 
 
-def _rand_experts(name: str, lo: int, hi: int, shape, std: float, device, seed: int) -> torch.Tensor:
-    """Experts lo..hi-1 of a stacked [E, ...] expert weight, each seeded by its own name: an expert-parallel rank
-    builds only its slice and every EP width builds the same model."""
-    return torch.stack([_rand(f"{name}.{e}", shape, std, device, seed) for e in range(lo, hi)]) if hi > lo else \
-        torch.empty(0, *shape, dtype=torch.bfloat16, device=device)
+class RandomSource:
+    """Seeded random-init weights (each tensor from its own name's seed, so every parallel layout builds the same
+    model); norms at their identity values."""
+
+    def __init__(self, seed: int, device):
+        self.seed, self.device = seed, torch.device(device)
+
+    def tensor(self, name: str, shape, std: float) -> torch.Tensor:
+        return _rand(name, shape, std, self.device, self.seed)
+
+    def norm(self, name: str, n: int, fill: float, dtype=torch.bfloat16) -> torch.Tensor:
+        return torch.full((n,), fill, dtype=dtype, device=self.device)
 
 
 @dataclass
@@ -117,7 +124,7 @@ class MLAKVCache:
 
 class MLAModel:
     def __init__(self, cfg: MLAMoEConfig, device, seed: int = 0, ep_rank: int = 0, ep_world: int = 1,
-                 keep_master: Optional[bool] = None, dcp_rank: int = 0, dcp_world: int = 1):
+                 keep_master: Optional[bool] = None, dcp_rank: int = 0, dcp_world: int = 1, source=None):
         """ep_world > 1: this rank holds routed experts [ep_rank E / ep_world, (ep_rank + 1) E / ep_world) of every
         MoE layer (plus the shared expert); attention, router and dense layers are replicated.
         dcp_world > 1 (decode context parallelism; every rank runs the same tokens): the latent KV is sharded by the
@@ -125,7 +132,10 @@ class MLAModel:
         group, the routed experts by rank (shared expert on rank 0), the dense FFNs by FFN columns; the partial
         outputs are summed by a fused all-reduce + norm (`attach_dcp`).
         keep_master: keep the bf16 weights next to the kernels' packed copies (default: only for models under 2 G
-        parameters -- test-size models, whose weights `copy_from` moves between devices)."""
+        parameters -- test-size models, whose weights `copy_from` moves between devices).
+        source: where the weights come from -- `tensor(name, shape, std)` / `norm(name, n, fill, dtype)` by this
+        model's weight names (default `RandomSource`; `models/mla_loader.HFMLASource` reads a HuggingFace
+        DeepSeek-V3-layout checkpoint).  Each tensor is fetched, packed for the kernels and dropped in turn."""
         self.cfg, self.device = cfg, torch.device(device)
         h, c = cfg.hidden, cfg
         if ep_world > 1 and dcp_world > 1:
@@ -145,9 +155,10 @@ class MLAModel:
         self.fuse_glue = True                            # the fused attention-block glue kernels where they apply
         self._x8 = None                                  # (data_ptr of x, E4M3 x, scales) written by the last norm
         self._bs: dict = {}
-        r = lambda name, shape, s=c.init_std: _rand(name, shape, s, self.device, seed)  # noqa: E731
+        self.src = source if source is not None else RandomSource(seed, self.device)
+        r = lambda name, shape, s=c.init_std: self.src.tensor(name, shape, s)  # noqa: E731
         self.embed = r("embed", (c.vocab, h))
-        self.final_norm = torch.ones(h, dtype=torch.bfloat16, device=self.device)
+        self.final_norm = self.src.norm("final_norm", h, 1.0)
         self.lm_head = r("lm_head", (c.vocab, h))
         self.head = None
         if self._kernels():
@@ -175,8 +186,8 @@ class MLAModel:
         """Layer i's weights (named `prefix`.*; the MTP draft layer uses prefix "mtp.<i>"), with the GEMM kernels
         built and, unless keep_master, the bf16 masters dropped."""
         c, h = self.cfg, self.cfg.hidden
-        r = lambda name, shape, s=c.init_std: _rand(name, shape, s, self.device, self.seed)  # noqa: E731
-        ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
+        r = lambda name, shape, s=c.init_std: self.src.tensor(name, shape, s)  # noqa: E731
+        nrm = lambda name, n, fill=1.0: self.src.norm(f"{prefix}.{name}", n, fill)  # noqa: E731
         wkv_b = r(f"{prefix}.wkv_b", (c.num_heads * (c.qk_nope + c.v_head), c.kv_lora)).view(
             c.num_heads, c.qk_nope + c.v_head, c.kv_lora)
         moe = c.is_moe(i)
@@ -184,15 +195,13 @@ class MLAModel:
         shared = c.num_shared and self.dcp_rank == 0     # context parallelism: the shared expert runs on rank 0
         if moe:
             ffn = {"gate": r(f"{prefix}.gate", (c.num_experts, h)),
-                   "e_bias": torch.zeros(c.num_experts, dtype=torch.float32, device=self.device),
+                   "e_bias": self.src.norm(f"{prefix}.e_bias", c.num_experts, 0.0, torch.float32),
                    "w_gu": None, "w_down": None,
                    "shared_gu": r(f"{prefix}.shared.gu", (2 * F * c.num_shared, h)) if shared else None,
                    "shared_down": r(f"{prefix}.shared.down", (h, F * c.num_shared)) if shared else None}
             if self.keep_master or not self._quantized_ffn(i):
-                ffn["w_gu"] = _rand_experts(f"{prefix}.experts.gu", self.e_lo, self.e_hi, (2 * F, h), c.init_std,
-                                            self.device, self.seed)
-                ffn["w_down"] = _rand_experts(f"{prefix}.experts.down", self.e_lo, self.e_hi, (h, F), c.init_std,
-                                              self.device, self.seed)
+                ffn["w_gu"] = self._experts(f"{prefix}.experts.gu", (2 * F, h))
+                ffn["w_down"] = self._experts(f"{prefix}.experts.down", (h, F))
         else:
             ffn = {"w_gu": r(f"{prefix}.mlp.gu", (2 * c.dense_ffn, h)), "w_down": r(f"{prefix}.mlp.down", (h, c.dense_ffn))}
             if self.dcp_world > 1:                      # this rank's FFN columns (gate and up rows, down columns)
@@ -201,16 +210,16 @@ class MLAModel:
                 ffn["w_gu"] = torch.cat([ffn["w_gu"][lo:hi], ffn["w_gu"][D + lo:D + hi]]).contiguous()
                 ffn["w_down"] = ffn["w_down"][:, lo:hi].contiguous()
         w = MLALayerWeights(
-            n_in=ones(h), n_post=ones(h),
-            wq_a=r(f"{prefix}.wq_a", (c.q_lora, h)), q_norm=ones(c.q_lora),
+            n_in=nrm("n_in", h), n_post=nrm("n_post", h),
+            wq_a=r(f"{prefix}.wq_a", (c.q_lora, h)), q_norm=nrm("q_norm", c.q_lora),
             wq_b=r(f"{prefix}.wq_b", (c.num_heads * (c.qk_nope + c.qk_rope), c.q_lora)),
-            wkv_a=r(f"{prefix}.wkv_a", (c.kv_lora + c.qk_rope, h)), kv_norm=ones(c.kv_lora),
+            wkv_a=r(f"{prefix}.wkv_a", (c.kv_lora + c.qk_rope, h)), kv_norm=nrm("kv_norm", c.kv_lora),
             w_uk=wkv_b[:, :c.qk_nope, :].contiguous(),
             w_uv=wkv_b[:, c.qk_nope:, :].transpose(1, 2).contiguous(),
             wo=r(f"{prefix}.wo", (h, c.num_heads * c.v_head)),
             wi_q=r(f"{prefix}.wi_q", (c.index_heads * c.index_dim, c.q_lora)),
-            wi_k=r(f"{prefix}.wi_k", (c.index_dim, h)), wi_kn=ones(c.index_dim),
-            wi_kb=torch.zeros(c.index_dim, dtype=torch.bfloat16, device=self.device),
+            wi_k=r(f"{prefix}.wi_k", (c.index_dim, h)), wi_kn=nrm("wi_kn", c.index_dim),
+            wi_kb=nrm("wi_kb", c.index_dim, 0.0),
             wi_w=r(f"{prefix}.wi_w", (c.index_heads, h)), ffn=ffn)
         del wkv_b
         if self.dcp_world > 1:                          # this rank's head group feeds a row-parallel W_UV / W_o
@@ -231,6 +240,13 @@ class MLAModel:
                         ffn[k] = None
         return w
 
+    def _experts(self, name: str, shape) -> torch.Tensor:
+        """This rank's routed experts [e_lo, e_hi) of a stacked expert weight (each expert fetched by its own name)."""
+        if self.e_hi <= self.e_lo:
+            return torch.empty(0, *shape, dtype=torch.bfloat16, device=self.device)
+        return torch.stack([self.src.tensor(f"{name}.{e}", shape, self.cfg.init_std)
+                            for e in range(self.e_lo, self.e_hi)])
+
     def _build_ffn(self, prefix: str, i: int, ffn: dict):
         """Grouped block-scaled FFN of layer i: MoE (this rank's routed experts + the shared one) or the dense FFN as
         one expert holding every token.  Experts are generated and packed one at a time unless masters are kept."""
@@ -249,8 +265,8 @@ class MLAModel:
                                       fmt=c.expert_dtype)
 
         def gen(e):
-            gu = _rand(f"{prefix}.experts.gu.{e}", (2 * F, c.hidden), c.init_std, self.device, self.seed)
-            d = _rand(f"{prefix}.experts.down.{e}", (c.hidden, F), c.init_std, self.device, self.seed)
+            gu = self.src.tensor(f"{prefix}.experts.gu.{e}", (2 * F, c.hidden), c.init_std)
+            d = self.src.tensor(f"{prefix}.experts.down.{e}", (c.hidden, F), c.init_std)
             return gu[:F], gu[F:], d
         return BlockScaledExperts.build(self.e_lo, self.e_hi, F, c.hidden, gen, shared=sh, fmt=c.expert_dtype,
                                         device=self.device)
@@ -288,10 +304,10 @@ class MLAModel:
         i = c.num_layers
         # the draft layer is built exactly like a target layer with index num_layers (MoE, since i >= first_dense)
         self.layers.append(self._make_layer(f"mtp.{i}", i))
-        self.eh_proj = _rand("mtp.eh_proj", (h, 2 * h), c.init_std, self.device, self.seed)
+        self.eh_proj = self.src.tensor("mtp.eh_proj", (h, 2 * h), c.init_std)
         self.eh = L.Linear(self.eh_proj, self._lin_kind()) if self._kernels() else None
-        ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=self.device)  # noqa: E731
-        self.enorm, self.hnorm, self.draft_norm = ones(h), ones(h), ones(h)
+        self.enorm, self.hnorm = self.src.norm("mtp.enorm", h, 1.0), self.src.norm("mtp.hnorm", h, 1.0)
+        self.draft_norm = self.src.norm("mtp.norm", h, 1.0)
         self.draft = True
 
     def moe_layers(self) -> list:
