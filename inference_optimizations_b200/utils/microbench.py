@@ -4,6 +4,7 @@ profiles/.  Usage:
     python -m inference_optimizations_b200.utils.microbench gqa_decode --b 8 --ctx 8192 --d 512 --fmt nvfp4
     python -m inference_optimizations_b200.utils.microbench mla_decode --b 64 --heads 128 --ctx 131072 --fmt nvfp4
     python -m inference_optimizations_b200.utils.microbench moe_gemm --b 64 --topk 8 --experts 32 --total-experts 256
+    python -m inference_optimizations_b200.utils.microbench hotops --only rmsnorm_fp8,router,kv_write --tokens 64,8192
 
 `--launches N` runs exactly N launches and no timing loop (the form used under ncu: `-s N-1 -c 1`).
 Each timed case prints one JSON line with microseconds, bytes moved and GB/s against the measured HBM peak.
@@ -241,6 +242,51 @@ def indexer_case(b: int, ctx: int, topk: int, heads: int = 64, launches: int = 0
     nbytes = b * ctx * 132
     return {"kernel": "indexer_logits+topk", "tokens": b, "ctx": ctx, "topk": topk, "heads": heads,
             "us": round(us, 2), "bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1),
+            "frac_hbm": round(nbytes / us / 1e3 / PEAKS["hbm_gbs"], 3), "l2": "flushed before each launch"}
+
+
+def hotops_case(op: str, t: int, hidden: int = 7168, experts: int = 256, launches: int = 0) -> dict:
+    """The small per-layer kernels of the DSA-MoE step at `t` tokens:
+    `rmsnorm_fp8`  residual add + RMSNorm + E4M3 / UE8M0-per-128 quantization of [t, hidden] (K12/K34 form);
+    `router`       sigmoid + bias, group-limited top-8 over fp32 [t, experts] logits, renormalised (K39);
+    `kv_write`     NVFP4 352-byte latent rows (512 E2M1 + E4M3 per 16, E4M3 rope) written to t random pool slots (K25).
+    Bytes are the op's algorithmic reads + writes; L2 flushed before each launch."""
+    from ..ops import basic as B
+    from ..ops import kvcache as K
+    from ..ops import moe as MOE
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(3)
+    if op == "rmsnorm_fp8":
+        x = torch.randn(t, hidden, device=dev, generator=g).to(torch.bfloat16)
+        res = torch.randn(t, hidden, device=dev, generator=g).to(torch.bfloat16)
+        w = torch.rand(hidden, device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty_like(x)
+        q8 = torch.empty(t, hidden, dtype=torch.uint8, device=dev)
+        qs = torch.empty(t, hidden // 128, dtype=torch.int32, device=dev)
+        fn = lambda: B.rmsnorm(x, w, 1e-6, residual=res, out=out, fp8=(q8, qs))  # noqa: E731
+        nbytes = t * hidden * (2 + 2 + 2 + 2 + 1) + t * hidden // 128 * 4
+    elif op == "router":
+        logits = torch.randn(t, experts, device=dev, generator=g)
+        bias = 0.01 * torch.randn(experts, device=dev, generator=g)
+        fn = lambda: MOE.route(logits, bias, 8, 8, 4, 2.5, "sigmoid")  # noqa: E731
+        nbytes = t * experts * 4 + t * 8 * 8
+    elif op == "kv_write":
+        rows = max(1 << 20, 4 * t)
+        pool = torch.zeros(rows, 352, dtype=torch.uint8, device=dev)
+        nope = torch.randn(t, 512, device=dev, generator=g).to(torch.bfloat16)
+        rope = torch.randn(t, 64, device=dev, generator=g).to(torch.bfloat16)
+        slot = torch.randperm(rows, device=dev)[:t].int()
+        fn = lambda: K.mla_write(nope, rope, slot, pool)  # noqa: E731
+        nbytes = t * (576 * 2 + 352 + 4)
+    else:
+        raise SystemExit(f"hotops: unknown op {op}")
+    if launches:
+        for _ in range(launches):
+            fn()
+        torch.cuda.synchronize()
+        return {}
+    us = _time_flushed(fn, iters=20)
+    return {"kernel": op, "tokens": t, "us": round(us, 2), "bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1),
             "frac_hbm": round(nbytes / us / 1e3 / PEAKS["hbm_gbs"], 3), "l2": "flushed before each launch"}
 
 
@@ -730,12 +776,14 @@ def kv4mla_compare_case(tokens: list, topk: int = 2048, rows: int = 600000, head
     return out_rows
 
 
-def dsa_profile_case(layers: int, sessions: int, ctx: int, steps: int, prefill: int, top: int = 40) -> dict:
+def dsa_profile_case(layers: int, sessions: int, ctx: int, steps: int, prefill: int, top: int = 40,
+                     trace_out: str = "") -> dict:
     """Per-kernel device time of the DSA-MoE serving step (the bench's engine: DP attention + EP over the launched
     ranks, CUDA-graph decode), from the CUDA activity records of the torch profiler (kernel durations as CUPTI reports
     them; the shares, not the absolutes, are the point: the bench's own CUDA-event timing is the throughput figure).
     Sessions hold `ctx` positions of random well-formed KV written by the pool writers (no prefill compute before the
-    decode steps); with `prefill` > 0 one more request of that many tokens per rank is prefilled and profiled too."""
+    decode steps); with `prefill` > 0 one more request of that many tokens per rank is prefilled and profiled too.
+    `trace_out`: also write rank 0's decode-step activity as a Chrome trace (kernel order, starts and gaps)."""
     import torch.distributed as dist
     from torch.profiler import ProfilerActivity, profile
     from ..config import EngineConfig, model_config
@@ -775,6 +823,8 @@ def dsa_profile_case(layers: int, sessions: int, ctx: int, steps: int, prefill: 
             eng.step()
         torch.cuda.synchronize()
     res["decode_step"] = table(prof, steps)
+    if trace_out and rank == 0:
+        prof.export_chrome_trace(trace_out)
     if prefill:
         g = torch.Generator().manual_seed(7 + rank)
         eng.add_request(torch.randint(1, cfg.vocab, (prefill,), generator=g).tolist(), SamplingParams(max_new_tokens=4))
@@ -818,6 +868,7 @@ def main() -> None:
     p.add_argument("--only", default="", help="proj_gemms: comma-separated op names")
     p.add_argument("--nt", default="", help="proj_gemms: token tiles to sweep (comma-separated)")
     p.add_argument("--ks", default="", help="proj_gemms: K splits to sweep (comma-separated)")
+    p.add_argument("--trace-out", default="", help="dsa_profile: Chrome trace of the decode steps (rank 0)")
     a = p.parse_args()
     if a.kernel == "gqa_decode":
         r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches, a.splits, a.trace)
@@ -825,6 +876,13 @@ def main() -> None:
         r = gqa_extend_case(a.chunk, a.ctx, a.hk, a.hq, a.d, a.fmt, a.window, a.launches)
     elif a.kernel == "indexer":
         r = indexer_case(a.b, a.ctx, a.topk, launches=a.launches)
+    elif a.kernel == "hotops":
+        r = {}
+        for op in a.only.split(",") if a.only else ("rmsnorm_fp8", "router", "kv_write"):
+            for t in [int(v) for v in a.tokens.split(",")]:
+                row = hotops_case(op, t, launches=a.launches)
+                if row:
+                    print(json.dumps(row), flush=True)
     elif a.kernel == "moe_tactics":
         r = moe_tactics_case(a.experts, a.total_experts, a.topk, a.hidden, a.ffn, a.wfmt)
     elif a.kernel == "dense_linear":
@@ -879,7 +937,7 @@ def main() -> None:
         if world > 1:
             torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
             dist.init_process_group("nccl", device_id=torch.device("cuda", torch.cuda.current_device()))
-        r = dsa_profile_case(a.layers, a.sessions, a.ctx, a.steps, a.prefill)
+        r = dsa_profile_case(a.layers, a.sessions, a.ctx, a.steps, a.prefill, trace_out=a.trace_out)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
