@@ -180,6 +180,9 @@ def run_dsa(args, info, dev, layers: int, steps: int, warm: int) -> dict:
     if eng.runner.model.ep:
         for ex in eng.runner.model.ep.values():
             status |= int(ex.status.item()) if hasattr(ex, "status") else 0
+    for d in (eng.runner.kv.idx_ws, eng.runner.kv.mla_ws):      # indexer / sparse-MLA bounded waits, range checks
+        for ws in d.values():
+            status |= int(ws.status.item())
     status = int(D.max_over_ranks(float(status)))
     table1 = eng.runner.kv.table.bytes_synced if hasattr(eng.runner.kv.table, "bytes_synced") else 0
     h2d = 5 * 4 * bucket + (table1 - table0) // max(1, steps)

@@ -373,16 +373,18 @@ void ar_norm2(const at::Tensor& peers, int64_t flag_offset, int64_t rows_cap, in
 }
 
 void moe_route(const at::Tensor& logits, const at::Tensor& bias, at::Tensor ids, at::Tensor wts, int64_t n_group,
-               int64_t topk_group, double scale) {
+               int64_t topk_group, double scale, int64_t ksplit) {
   req(logits, at::kFloat, "logits");
   req(bias, at::kFloat, "bias");
   req(ids, at::kInt, "ids");
   req(wts, at::kFloat, "wts");
-  TORCH_CHECK(logits.dim() == 2 && logits.is_contiguous() && bias.numel() == logits.size(1), "logits [T, E]");
+  // logits [T, E], or the router GEMM's split-K partials [ksplit * T, E] (split-major)
+  TORCH_CHECK(ksplit >= 1 && logits.dim() == 2 && logits.is_contiguous() && bias.numel() == logits.size(1) &&
+              logits.size(0) == ksplit * ids.size(0), "logits [ksplit * T, E]");
   const at::cuda::CUDAGuard g(logits.device());
   CHECK_CUDA_OK(iob::moe_route(logits.data_ptr<float>(), bias.data_ptr<float>(), ids.data_ptr<int>(),
-                               wts.data_ptr<float>(), logits.size(0), logits.size(1), ids.size(1), n_group, topk_group,
-                               scale, stream()));
+                               wts.data_ptr<float>(), ids.size(0), logits.size(1), ids.size(1), n_group, topk_group,
+                               scale, stream(), ksplit));
 }
 
 void moe_gemm(const at::Tensor& wpack, const at::Tensor& x, const at::Tensor& x_scale, const at::Tensor& off,

@@ -176,8 +176,10 @@ struct ArNormArgs {
 cudaError_t ar_norm2(const ArNormArgs& a, cudaStream_t s);
 
 // ---- MoE router (moe.cu): sigmoid, bias-corrected group-limited top-k, renormalised * scale.
+// ksplit > 1: `logits` holds ksplit fp32 partials [ksplit][T][E] of the router GEMM, summed here in split order
+// (register form only: E and the group size multiples of 32).
 cudaError_t moe_route(const float* logits, const float* bias, int* ids, float* wts, int T, int E, int K, int G,
-                      int KG, float scale, cudaStream_t s);
+                      int KG, float scale, cudaStream_t s, int ksplit = 1);
 
 // ---- primitive check (umma_test.cu): C[M, N] fp32 = A[M, K] * B[N, K]^T, bf16 inputs, one CTA per 128 rows.
 // ---- grouped block-scaled expert GEMM + routing prep (moe_gemm.cu)

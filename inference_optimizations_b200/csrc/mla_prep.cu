@@ -39,6 +39,8 @@ __device__ __forceinline__ void rope4(float (&v)[4], int lane, const float* cs) 
   }
 }
 
+constexpr int kQaMax = 16;          // q_lora <= 16 x 128 (DeepSeek-V3 1536, GLM-5 2048)
+
 __global__ void __launch_bounds__(256) mla_prep_kv_kernel(const MlaPrepArgs a) {
   const int t = blockIdx.x;
   const int warp = warp_id(), lane = lane_id();
@@ -50,32 +52,48 @@ __global__ void __launch_bounds__(256) mla_prep_kv_kernel(const MlaPrepArgs a) {
   __shared__ float red[4];
   if (warp < 4) {
     // ---------------------------------------------------------------- q_a RMSNorm (128 threads)
+    // Thread tid holds element tid of every 128-wide block (kQaMax blocks at most), loaded up front: one round of
+    // independent loads instead of a dependent load per block, and one barrier for every block's FP8 amax.
     const int tid = threadIdx.x;
-    float ss = 0.f;
-    for (int c = tid; c < a.q_lora; c += 128) {
-      const float v = bfv(y, c);
-      ss += v * v;
+    float v[kQaMax], wv[kQaMax];
+    const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(a.q_norm);
+#pragma unroll
+    for (int j = 0; j < kQaMax; ++j) {
+      const int c = tid + 128 * j;
+      v[j] = c < a.q_lora ? bfv(y, c) : 0.f;
+      wv[j] = c < a.q_lora ? bfv(w, c) : 0.f;
     }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kQaMax; ++j) ss += v[j] * v[j];
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
     asm volatile("bar.sync 1, 128;");
     const float inv = rsqrtf((red[0] + red[1] + red[2] + red[3]) / a.q_lora + a.eps);
-    const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(a.q_norm);
     __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.qa_out) + static_cast<size_t>(t) * a.q_lora;
-    // thread tid holds element tid of every 128-wide block: the block amax for the FP8 output is a 4-warp max
-    __shared__ float bmax[4];
-    for (int c = tid; c < a.q_lora; c += 128) {
-      const __nv_bfloat16 v = __float2bfloat16(bfv(y, c) * inv * bfv(w, c));
-      o[c] = v;
-      if (a.qa_q) {
-        const float f = __bfloat162float(v);
-        const float m = warp_max(fabsf(f));
-        asm volatile("bar.sync 1, 128;");                 // the previous block's maxima are consumed
-        if (lane == 0) bmax[warp] = m;
-        asm volatile("bar.sync 1, 128;");
-        const uint32_t eb = ue8m0_for(fmaxf(fmaxf(bmax[0], bmax[1]), fmaxf(bmax[2], bmax[3])));
-        a.qa_q[static_cast<size_t>(t) * a.q_lora + c] = float_to_e4m3(f * __uint_as_float((254u - eb) << 23));
-        if (tid == 0) a.qa_s[static_cast<size_t>(t) * (a.q_lora / 128) + c / 128] = eb * 0x01010101u;
+    __shared__ float bmax[4][kQaMax];
+#pragma unroll
+    for (int j = 0; j < kQaMax; ++j) {
+      const int c = tid + 128 * j;
+      const __nv_bfloat16 b = __float2bfloat16(v[j] * inv * wv[j]);
+      if (c < a.q_lora) o[c] = b;
+      v[j] = __bfloat162float(b);
+    }
+    if (a.qa_q) {
+#pragma unroll
+      for (int j = 0; j < kQaMax; ++j) {
+        const float m = warp_max(fabsf(v[j]));
+        if (lane == 0) bmax[warp][j] = m;
+      }
+      asm volatile("bar.sync 1, 128;");
+#pragma unroll
+      for (int j = 0; j < kQaMax; ++j) {
+        const int c = tid + 128 * j;
+        if (c < a.q_lora) {
+          const uint32_t eb = ue8m0_for(fmaxf(fmaxf(bmax[0][j], bmax[1][j]), fmaxf(bmax[2][j], bmax[3][j])));
+          a.qa_q[static_cast<size_t>(t) * a.q_lora + c] = float_to_e4m3(v[j] * __uint_as_float((254u - eb) << 23));
+          if (tid == 0) a.qa_s[static_cast<size_t>(t) * (a.q_lora / 128) + j] = eb * 0x01010101u;
+        }
       }
     }
   } else if (warp == 4) {
@@ -213,7 +231,7 @@ __global__ void __launch_bounds__(256) mla_prep_q_kernel(const MlaPrepArgs a) {
 
 cudaError_t mla_prep_kv(const MlaPrepArgs& a, cudaStream_t s) {
   if (a.T == 0) return cudaSuccess;
-  if (a.q_lora <= 0 || a.Hi <= 0 || (a.latent_fmt != kKvNvfp4 && a.latent_fmt != kKvFp8) || !a.ya || !a.rope ||
+  if (a.q_lora <= 0 || a.q_lora > 128 * kQaMax || a.Hi <= 0 || (a.latent_fmt != kKvNvfp4 && a.latent_fmt != kKvFp8) || !a.ya || !a.rope ||
       !a.pos || !a.slot || !a.qa_out || !a.latent_pool || !a.index_pool || !a.iw_out ||
       (a.qa_q && (!a.qa_s || a.q_lora % 128)))
     return cudaErrorInvalidValue;

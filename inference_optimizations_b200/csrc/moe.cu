@@ -1,6 +1,12 @@
 // MoE router: sigmoid scores, bias-corrected group-limited top-k, renormalised weights (ops/moe.py route_ref is the
 // oracle; semantics of the DeepSeek `noaux_tc` router).  One warp per token; the E <= 256 biased scores are staged
 // in shared memory, groups and experts are picked by repeated warp arg-max (ties: lower index).
+//
+// Register form (E a multiple of 32, groups of a multiple of 32 experts: DeepSeek-V3 256 / 8, GLM-5 160 / 1): lane l
+// holds experts l + 32 j in registers, so a group is a set of whole registers; group scores come from one top-2
+// butterfly per group, the K picks from register arg-max + one warp arg-max each -- no shared-memory passes.  It
+// also reads the router GEMM's split-K fp32 partials directly (summed in split order, as the reduction kernel
+// would), so the reduction launch disappears.  Same picks and weights as the shared-memory form, bit for bit.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -83,14 +89,125 @@ __global__ void __launch_bounds__(32 * kRouteWarps) moe_route_kernel(const float
   }
 }
 
+// (b1, b2) = the two largest of a warp's (b1, b2) pairs (duplicates counted), on every lane.
+__device__ __forceinline__ void warp_top2(float& b1, float& b2) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float o1 = __shfl_xor_sync(0xffffffffu, b1, o), o2 = __shfl_xor_sync(0xffffffffu, b2, o);
+    const float hi = fmaxf(b1, o1), lo = fmaxf(fminf(b1, o1), fmaxf(b2, o2));
+    b1 = hi;
+    b2 = lo;
+  }
+}
+
+template <int NJ>
+__global__ void __launch_bounds__(32 * kRouteWarps) moe_route_reg_kernel(const float* __restrict__ part, int ksplit,
+                                                                         const float* __restrict__ bias, int* ids,
+                                                                         float* wts, int T, int K, int G, int KG,
+                                                                         float scale) {
+  constexpr int E = 32 * NJ;
+  const int lane = lane_id();
+  const int t = blockIdx.x * kRouteWarps + warp_id();
+  if (t >= T) return;
+  float acc[NJ], p[NJ], v[NJ];
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) acc[j] = 0.f;
+  for (int k = 0; k < ksplit; ++k) {
+    const float* lg = part + (static_cast<size_t>(k) * T + t) * E;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) acc[j] += lg[lane + 32 * j];
+  }
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    p[j] = 1.f / (1.f + __expf(-acc[j]));
+    v[j] = p[j] + bias[lane + 32 * j];
+  }
+  if (G > 1) {
+    const int jpg = NJ / G;                  // registers per group
+    float gscore[NJ];
+#pragma unroll
+    for (int g = 0; g < NJ; ++g) {
+      gscore[g] = -INFINITY;
+      if (g < G) {
+        float b1 = -INFINITY, b2 = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          if (j / jpg == g) {
+            const float x = v[j];
+            if (x > b1) { b2 = b1; b1 = x; } else if (x > b2) { b2 = x; }
+          }
+        }
+        warp_top2(b1, b2);
+        gscore[g] = b1 + b2;
+      }
+    }
+    unsigned keep = 0;
+    for (int r = 0; r < KG; ++r) {
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int g = 0; g < NJ; ++g)
+        if (g < G && !((keep >> g) & 1u) && (gscore[g] > best || (gscore[g] == best && g < bi))) {
+          best = gscore[g];
+          bi = g;
+        }
+      if (bi < G) keep |= 1u << bi;
+    }
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+      if (!((keep >> (j / jpg)) & 1u)) v[j] = -INFINITY;
+  }
+  float sum = 0.f;
+  int myid = -1;
+  float myw = 0.f;
+  for (int r = 0; r < K; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int e = lane + 32 * j;
+      if (v[j] > bv || (v[j] == bv && e < bi)) { bv = v[j]; bi = e; }
+    }
+    warp_argmax(bv, bi);
+    if (bi >= E) bi = 0;
+    float pw = 0.f;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
+      if (j == bi / 32) {
+        pw = p[j];
+        if (lane == (bi & 31)) v[j] = -INFINITY;     // taken
+      }
+    pw = __shfl_sync(0xffffffffu, pw, bi & 31);
+    sum += pw;
+    if (lane == r) { myid = bi; myw = pw; }
+  }
+  if (lane < K) {
+    ids[static_cast<size_t>(t) * K + lane] = myid;
+    wts[static_cast<size_t>(t) * K + lane] = myw / fmaxf(sum, 1e-20f) * scale;
+  }
+}
+
 }  // namespace
 
 cudaError_t moe_route(const float* logits, const float* bias, int* ids, float* wts, int T, int E, int K, int G,
-                      int KG, float scale, cudaStream_t s) {
+                      int KG, float scale, cudaStream_t s, int ksplit) {
   if (T == 0) return cudaSuccess;
-  if (E > 256 || K > 32 || K > E || G < 1 || G > 32 || E % G || KG < 1 || KG > G) return cudaErrorInvalidValue;
-  moe_route_kernel<<<(T + kRouteWarps - 1) / kRouteWarps, 32 * kRouteWarps, 0, s>>>(logits, bias, ids, wts, T, E, K, G,
-                                                                                     KG, scale);
+  if (E > 256 || K > 32 || K > E || G < 1 || G > 32 || E % G || KG < 1 || KG > G || ksplit < 1)
+    return cudaErrorInvalidValue;
+  const int grid = (T + kRouteWarps - 1) / kRouteWarps;
+  if (E % 32 == 0 && (E / G) % 32 == 0) {
+    switch (E / 32) {
+#define IOB_ROUTE(nj)                                                                                             \
+  case nj:                                                                                                        \
+    moe_route_reg_kernel<nj><<<grid, 32 * kRouteWarps, 0, s>>>(logits, ksplit, bias, ids, wts, T, K, G, KG, scale); \
+    return cudaGetLastError();
+      IOB_ROUTE(1) IOB_ROUTE(2) IOB_ROUTE(3) IOB_ROUTE(4) IOB_ROUTE(5) IOB_ROUTE(6) IOB_ROUTE(7) IOB_ROUTE(8)
+#undef IOB_ROUTE
+      default: break;
+    }
+  }
+  if (ksplit != 1) return cudaErrorInvalidValue;     // the shared-memory form reads summed logits
+  moe_route_kernel<<<grid, 32 * kRouteWarps, 0, s>>>(logits, bias, ids, wts, T, E, K, G, KG, scale);
   return cudaGetLastError();
 }
 

@@ -755,11 +755,14 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* rows, int T, int topk, i
 // Quantize one row of H values given by val(c) (already rounded to bf16): fmt 0 = E4M3 + one UE8M0 scale per 128
 // (stored as four identical bytes, the layout the block-scaled GEMM reads), fmt 1 = NVFP4 (E2M1 pairs + one E4M3 scale
 // per 16).  Called by every thread of the block.
+// part / parts: this CTA's share of the row's column groups (a row spread over several CTAs when there are few rows).
 template <class Val>
-__device__ __forceinline__ void quant_row(Val val, int row, int H, int fmt, uint8_t* q, uint32_t* sc) {
+__device__ __forceinline__ void quant_row(Val val, int row, int H, int fmt, uint8_t* q, uint32_t* sc, int part = 0,
+                                          int parts = 1) {
   if (fmt == 0) {
     // one warp per 128-column group: 4 values per lane
-    for (int g = warp_id(); g < H / 128; g += blockDim.x / 32) {
+    const int nw = blockDim.x / 32;
+    for (int g = part * nw + warp_id(); g < H / 128; g += parts * nw) {
       float v[4];
       float m = 0.f;
 #pragma unroll
@@ -779,7 +782,7 @@ __device__ __forceinline__ void quant_row(Val val, int row, int H, int fmt, uint
   } else {
     // one thread per 16-column block
     uint8_t* sb_row = reinterpret_cast<uint8_t*>(sc) + static_cast<size_t>(row) * (H / 16);
-    for (int b = threadIdx.x; b < H / 16; b += blockDim.x) {
+    for (int b = part * blockDim.x + threadIdx.x; b < H / 16; b += parts * blockDim.x) {
       float v[16];
       float m = 0.f;
 #pragma unroll
@@ -828,7 +831,7 @@ __global__ void rmsnorm_quant_kernel(const __nv_bfloat16* x, const __nv_bfloat16
     float f = __bfloat162float(xr[c]);
     if (w) f = __bfloat162float(__float2bfloat16(f * inv * (__bfloat162float(w[c]) + plus_one)));
     return f;
-  }, row, H, fmt, q, sc);
+  }, row, H, fmt, q, sc, blockIdx.y, gridDim.y);
 }
 
 // act(gate) * up -> quantized, one pass over gate_up [T, 2F] (gate = first F columns): the GEMM1 -> GEMM2 glue of a
@@ -948,8 +951,16 @@ cudaError_t rmsnorm_quant(const void* x, const void* w, float eps, float plus_on
                           uint32_t* sc, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   if ((fmt == 0 && H % 128) || (fmt == 1 && H % 64) || fmt < 0 || fmt > 1) return cudaErrorInvalidValue;
-  rmsnorm_quant_kernel<<<T, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
-                                         static_cast<const __nv_bfloat16*>(w), eps, plus_one, H, fmt, q, sc);
+  // without a norm (no row-wide sum) a row may spread over several CTAs: with few rows each warp then quantizes one
+  // or two column groups instead of walking the row (a chain of dependent loads per warp at decode sizes)
+  int parts = 1;
+  if (!w) {
+    const int per_cta = fmt == 0 ? 8 * 128 : 256 * 16;   // columns one pass of a 256-thread CTA covers
+    parts = max(1, min((H + per_cta - 1) / per_cta, (2 * 148 + T - 1) / T));
+  }
+  rmsnorm_quant_kernel<<<dim3(T, parts), 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                      static_cast<const __nv_bfloat16*>(w), eps, plus_one, H, fmt,
+                                                      q, sc);
   return cudaGetLastError();
 }
 

@@ -118,6 +118,33 @@ class MLAKVCache:
         self.mla_ws: dict = {}
         self.idx_ws: dict = {}
 
+    def workspaces(self, t: int, max_ctx: int, heads: int, topk: int):
+        """(indexer workspace, sparse-MLA workspace) of a step with t tokens and context bound max_ctx, shared by
+        every layer of the step (layers run one after another).  Made on first use outside stream capture, so a
+        captured decode graph reuses the ones its eager warm-up made (no per-layer allocation or status clear in
+        the graph); their status words accumulate over layers and steps (`check`).  None inside a capture that
+        found none, and for prefill-sized steps (> 256 tokens: the ops allocate per call, so chunks of varying length
+        hold no memory between steps)."""
+        if self.device.type != "cuda" or t > 256:
+            return None, None
+        ik, mk = (t, max_ctx), (t, topk)
+        if ik not in self.idx_ws or mk not in self.mla_ws:
+            if torch.cuda.is_current_stream_capturing():
+                return self.idx_ws.get(ik), self.mla_ws.get(mk)
+            if ik not in self.idx_ws:
+                self.idx_ws[ik] = I.IndexerWorkspace.allocate(t, max_ctx, self.device)
+            if mk not in self.mla_ws:
+                self.mla_ws[mk] = M.MlaWorkspace.allocate(t, heads, M.mla_split_policy(t, topk)[0], self.device)
+        return self.idx_ws[ik], self.mla_ws[mk]
+
+    def check(self) -> None:
+        """Raise if a bounded wait or range check of the indexer / sparse-MLA kernels recorded a non-zero status."""
+        for name, d in (("indexer", self.idx_ws), ("sparse-MLA decode", self.mla_ws)):
+            for key, ws in d.items():
+                v = int(ws.status.item())
+                if v:
+                    raise RuntimeError(f"{name} workspace {key}: status {v}")
+
     def bytes_per_token(self) -> int:
         return self.cfg.num_layers * (M.ROW_BYTES[self.fmt] + F.INDEX_ROW_BYTES)
 
@@ -421,12 +448,22 @@ class MLAModel:
             return k["gate"](x, out_f32=True)
         return Fn.linear(x.float(), self.layers[i].ffn["gate"].float())
 
+    def _route(self, i: int, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Router of MoE layer i -> (expert ids, weights).  On the kernels the router GEMM's split-K partials go
+        straight to the router kernel, which sums them (one launch fewer than GEMM + reduction + router)."""
+        c, f, k = self.cfg, self.layers[i].ffn, self.layers[i].k
+        if (k is not None and "gate" in k and x.is_cuda and k["gate"].Np == k["gate"].N
+                and MOE.route_fuses_splitk(c.num_experts, c.n_group, c.router)):
+            part, ks = k["gate"].partials(x)
+            return MOE.route(part, f["e_bias"], c.topk, c.n_group, c.topk_group, c.routed_scale, c.router, ksplit=ks)
+        logits = self._router_logits(i, x)
+        return MOE.route(logits, f["e_bias"], c.topk, c.n_group, c.topk_group, c.routed_scale, c.router)
+
     def _ffn(self, i: int, x: torch.Tensor, xq8: Optional[tuple] = None) -> torch.Tensor:
         """xq8: x block-quantized by the norm that produced it (FP8 FFN weights), or None."""
         c, f = self.cfg, self.layers[i].ffn
         if self.ep is not None and c.is_moe(i):
-            logits = self._router_logits(i, x)
-            ids, w = MOE.route(logits, f["e_bias"], c.topk, c.n_group, c.topk_group, c.routed_scale, c.router)
+            ids, w = self._route(i, x)
             t, per = x.shape[0], self.ep_T_max
             outs = []
             for p in range(self.ep_pieces):      # every rank runs the same number of exchanges (agreed per step)
@@ -440,8 +477,7 @@ class MLAModel:
             if not c.is_moe(i):
                 ids = torch.zeros(t, 1, dtype=torch.int32, device=x.device)
                 return ex.forward(x, ids, torch.ones(t, 1, device=x.device), xq8=xq8)
-            logits = self._router_logits(i, x)
-            ids, w = MOE.route(logits, f["e_bias"], c.topk, c.n_group, c.topk_group, c.routed_scale, c.router)
+            ids, w = self._route(i, x)
             return ex.forward(x, ids, w, xq8=xq8)
         if not c.is_moe(i):
             return MOE.swiglu(x, f["w_gu"], f["w_down"])
@@ -532,8 +568,7 @@ class MLAModel:
                 ids = torch.zeros(t, 1, dtype=torch.int32, device=x.device)
                 return self._block_scaled(i).forward(x, ids, torch.ones(t, 1, device=x.device))
             return MOE.swiglu(x, f["w_gu"], f["w_down"])
-        logits = self._router_logits(i, x)
-        ids, w = MOE.route(logits, f["e_bias"], c.topk, c.n_group, c.topk_group, c.routed_scale, c.router)
+        ids, w = self._route(i, x)
         local = (ids >= self.e_lo) & (ids < self.e_hi)
         w = torch.where(local, w, torch.zeros_like(w))
         if self._quantized_ffn(i):
@@ -602,7 +637,7 @@ class MLAModel:
         w_eff = torch.empty(t, c.index_heads, dtype=torch.float32, device=dev)
         ext().mla_prep_q(yb, cs, st.pos, qf, q8, w_eff, iw, c.num_heads, c.qk_nope, c.index_heads)
         sel = I.indexer_select(q8, w_eff, kv.index[i], kv.table.dev, st.limit, c.index_topk, st.max_ctx,
-                               req_idx=st.req_idx, ws=kv.idx_ws.get((t, st.max_ctx)))
+                               req_idx=st.req_idx, ws=kv.workspaces(t, st.max_ctx, c.num_heads, c.index_topk)[0])
         return qf, sel
 
     def _query_torch(self, i: int, x: torch.Tensor, st: MLAStep, kv: MLAKVCache,
@@ -629,7 +664,7 @@ class MLAModel:
         iw = iw_.float() * (c.index_heads ** -0.5 * c.index_dim ** -0.5)
         q8, w_eff = I.indexer_q_quant(iq, iw)
         sel = I.indexer_select(q8, w_eff, kv.index[i], kv.table.dev, st.limit, c.index_topk, st.max_ctx,
-                               req_idx=st.req_idx, ws=kv.idx_ws.get((t, st.max_ctx)))
+                               req_idx=st.req_idx, ws=kv.workspaces(t, st.max_ctx, c.num_heads, c.index_topk)[0])
         return torch.cat([q_lat, q_pe], dim=-1).contiguous(), sel
 
     def layer_forward(self, i: int, h: torch.Tensor, x: torch.Tensor, st: MLAStep, kv: MLAKVCache,
@@ -641,7 +676,8 @@ class MLAModel:
         t, eps = x.shape[0], c.rms_eps
         qf, sel = (self._query_fused if self._fused_glue(w) else self._query_torch)(i, x, st, kv)
         # absorbed sparse attention over the latent pool
-        o_lat = M.mla_decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt, ws=kv.mla_ws.get((t, c.index_topk)))
+        o_lat = M.mla_decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt,
+                             ws=kv.workspaces(t, st.max_ctx, c.num_heads, c.index_topk)[1])
         # h += attn; x2 = norm_post(h), also block-quantized when the FFN's expert GEMMs take FP8 input
         o = self._o_proj(w, o_lat, t)
         xq8 = None

@@ -135,6 +135,28 @@ class DenseLinear:
         _splitk_gemm(self, xb, xb, out, t, self.K // 64, 2, pk)
         return out
 
+    def partials(self, x: torch.Tensor) -> tuple[torch.Tensor, int]:
+        """fp32 x W^T left as its split-K partials: ([ks * t, N] split-major, ks), for a consumer that sums the
+        splits itself in split order (the router kernel); ks = 1 is the plain fp32 product.  No reduction launch."""
+        t = x.shape[0]
+        kc = self.K // 64
+        nt = FORCE["nt"] or MG.pick_nt(t)
+        n_tiles = self.N // (TILE * self.g)
+        ks = FORCE["ks"] or split_k(n_tiles, t, nt, kc, self.num_ctas, g=self.g)
+        if ks == 1 or t == 0:
+            return self(x, out_f32=True), 1
+        key = (t, ks)
+        if key not in self._parts:
+            self._parts[key] = (torch.empty(ks * t, self.N, dtype=torch.float32, device=x.device),
+                                torch.zeros(n_tiles * -(-t // nt), dtype=torch.int32, device=x.device))
+        part = self._parts[key][0]
+        off, pairs, static = self._index(t, x.device)
+        xb = x.contiguous().view(torch.uint8)
+        MG.gemm(self.wpack, xb, xb, off, pairs, part, self.status, n_tiles=n_tiles, kc=kc, g=self.g, nt=nt,
+                mode=MODE_F32_SPLIT, src_div=1, num_ctas=self.num_ctas, kind=2, ksplit=ks, split_rows=t,
+                static_index=static)
+        return part, ks
+
 
 class Fp8Linear:
     """y = x W^T with W stored FP8 E4M3 + one UE8M0 scale per 128 x 128 block and x quantized per 1 x 128 on the fly
@@ -290,6 +312,11 @@ class Linear:
         else:
             y = self.lin(x)
         return y[:, :self.N] if self.Np != self.N else y
+
+    def partials(self, x: torch.Tensor) -> tuple[torch.Tensor, int]:
+        """bf16 GEMM, fp32 split-K partials ([ks * t, N], ks) of x W^T, unpadded widths only (`DenseLinear.partials`)."""
+        assert self.kind == "bf16" and self.Np == self.N, "partials: bf16 GEMM of an unpadded width"
+        return self.lin.partials(x)
 
     def split(self, y: torch.Tensor) -> list:
         out, c = [], 0

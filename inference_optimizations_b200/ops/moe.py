@@ -16,16 +16,25 @@ from .._ext import ext
 
 
 def route(logits: torch.Tensor, e_bias: torch.Tensor, topk: int, n_group: int, topk_group: int,
-          routed_scale: float, kind: str = "sigmoid") -> tuple[torch.Tensor, torch.Tensor]:
-    """logits fp32 [T, E] -> (expert ids int32 [T, topk], weights fp32 [T, topk]).  Ties: lower expert id."""
+          routed_scale: float, kind: str = "sigmoid", ksplit: int = 1) -> tuple[torch.Tensor, torch.Tensor]:
+    """logits fp32 [T, E] -> (expert ids int32 [T, topk], weights fp32 [T, topk]).  Ties: lower expert id.
+    ksplit > 1 (CUDA, E and E / n_group multiples of 32): `logits` is the router GEMM's split-K partials
+    [ksplit * T, E], summed by the router kernel in split order."""
     if logits.is_cuda and kind == "sigmoid":
-        t, e = logits.shape
+        t = logits.shape[0] // ksplit
         ids = torch.empty(t, topk, dtype=torch.int32, device=logits.device)
         w = torch.empty(t, topk, dtype=torch.float32, device=logits.device)
         ext().moe_route(logits.float().contiguous(), e_bias.float().contiguous(), ids, w, n_group, topk_group,
-                        routed_scale)
+                        routed_scale, ksplit)
         return ids, w
+    if ksplit > 1:
+        logits = logits.view(ksplit, -1, logits.shape[1]).sum(0)
     return route_ref(logits, e_bias, topk, n_group, topk_group, routed_scale, kind)
+
+
+def route_fuses_splitk(num_experts: int, n_group: int, kind: str = "sigmoid") -> bool:
+    """The router kernel sums split-K partials itself for this geometry (its register form)."""
+    return kind == "sigmoid" and num_experts % 32 == 0 and num_experts <= 256 and (num_experts // n_group) % 32 == 0
 
 
 def _topk_stable(x: torch.Tensor, k: int) -> torch.Tensor:

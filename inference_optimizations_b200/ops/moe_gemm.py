@@ -285,6 +285,7 @@ class BlockScaledExperts:
         self.num_ctas = num_ctas or (torch.cuda.get_device_properties(dev).multi_processor_count
                                      if dev.type == "cuda" else 1)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._parts: dict = {}
 
     @classmethod
     def build(cls, e_lo: int, e_hi: int, F: int, H: int, gen, shared: tuple | None = None, fmt: str = "fp8",
@@ -330,6 +331,7 @@ class BlockScaledExperts:
             del g, u, d
         self.num_ctas = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 1
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._parts: dict = {}
         return self
 
     @classmethod
@@ -358,6 +360,7 @@ class BlockScaledExperts:
         self.q = None
         self.num_ctas = torch.cuda.get_device_properties(device).multi_processor_count
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self._parts = {}
         return self
 
     def dequant(self):
@@ -404,14 +407,39 @@ class BlockScaledExperts:
             hs = torch.empty(P + extra, self.F // 64, dtype=torch.int32, device=dev)
         gemm(self.w1, xq, xs, off, pairs, h, self.status, n_tiles=self.F // TILE, kc=kc1, g=2, nt=nt, mode=1,
              src_div=k, src_limit=P, out_scale=hs, num_ctas=self.num_ctas, kind=self.kind, expert_mul=self.mul1)
+        n2 = self.H // (TILE * self.g2)
+        ks = self._dense_split(n2, kc2, nt) if (self.E == 1 and not self.has_shared and k == 1 and t <= 64) else 1
+        if ks > 1:
+            # a dense FFN at decode sizes: its down projection has only H / 256 output tiles, so K is split and the
+            # fp32 partials are summed in split order by one reduction kernel straight into the output (one pair
+            # per token, weight 1: no combine).  The split depends on the weight shape only, so every batch of up to
+            # 64 tokens rounds the same way (data-parallel ranks agree with one GPU).
+            key = (P, ks)
+            if key not in self._parts:
+                self._parts[key] = torch.empty(ks * P, self.H, dtype=torch.float32, device=dev)
+            part = self._parts[key]
+            gemm(self.w2, h, hs, off, pairs, part, self.status, n_tiles=n2, kc=kc2, g=self.g2, nt=nt, mode=3,
+                 src_div=1, num_ctas=self.num_ctas, kind=self.kind, expert_mul=self.mul2, ksplit=ks, split_rows=P,
+                 static_index=True)
+            y = torch.empty(t, self.H, dtype=torch.bfloat16, device=dev)
+            ext().splitk_reduce(part, ks, y, None, 0, 0, 0)
+            return y
         # expert rows stay unweighted in bf16; the combine applies the routing weights in fp32 -- the same rounding
-        # points as the expert-parallel exchange (parallel/ep.py), so EP at any width reproduces this path bit for bit
+        # points as the expert-parallel exchange (parallel/ep.py), so EP at any width reproduces this path bit for bit.
+        # The work list (off / pairs) was complete before the gate/up GEMM passed its dependency wait, so this launch
+        # may build it and stream weights while that GEMM finishes.
         rows = torch.empty(P + extra, self.H, dtype=torch.bfloat16, device=dev)
-        gemm(self.w2, h, hs, off, pairs, rows, self.status, n_tiles=self.H // (TILE * self.g2), kc=kc2, g=self.g2,
-             nt=nt, mode=0, src_div=1, num_ctas=self.num_ctas, kind=self.kind, expert_mul=self.mul2)
+        gemm(self.w2, h, hs, off, pairs, rows, self.status, n_tiles=n2, kc=kc2, g=self.g2,
+             nt=nt, mode=0, src_div=1, num_ctas=self.num_ctas, kind=self.kind, expert_mul=self.mul2,
+             static_index=True)
         y = torch.empty(t, self.H, dtype=torch.bfloat16, device=dev)
         ext().moe_combine(rows, t, k, P if self.has_shared else -1, w.float().contiguous(), y)
         return y
+
+    def _dense_split(self, n_tiles: int, kc: int, nt: int) -> int:
+        """K splits of a dense FFN's down projection at decode sizes (the linear layers' split rule at one token)."""
+        from .linear import split_k
+        return split_k(n_tiles, 1, nt, kc, self.num_ctas, g=self.g2)
 
     def forward_ref(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """fp32 oracle of the same arithmetic: quantized activations, quantized SwiGLU output, bf16 rows, fp32

@@ -147,11 +147,13 @@ class EPMoE:
                 n_tiles=self.F // 128, kc=self.H // vals, g=2, nt=self.nt, mode=1, src_div=k,
                 src_limit=P, src_shared_base=self.rank * self.T_max, out_scale=self.hs, num_ctas=ex.num_ctas,
                 kind=self.kind, expert_mul=ex.mul1)
+        # off / pairs were complete before the gate/up GEMM passed its dependency wait: this launch may build its work
+        # list and stream weights while that GEMM finishes
         MG.gemm(ex.w2, self.h, self.hs, self.off, self.pairs, self.comb, self.status,
                 n_tiles=self.H // (128 * ex.g2), kc=self.F // vals, g=ex.g2, nt=self.nt, mode=0, src_div=1,
                 num_ctas=ex.num_ctas, kind=self.kind, expert_mul=ex.mul2, out_peers=self.peers,
                 out_offset=L.off_comb, out_div=self.T_max * k, out_rank=self.rank,
-                out_shared_base=self.T_max * k, pairs_total=P)
+                out_shared_base=self.T_max * k, pairs_total=P, static_index=True)
         self.barrier()
         y = torch.empty(T, self.H, dtype=torch.bfloat16, device=x.device)
         ext().moe_combine(self.comb, T, k, self.T_max * k if ex.has_shared else -1, w.float().contiguous(), y)

@@ -104,3 +104,22 @@ def test_mla_mtp_speculation_gpu(cuda):
         eng = Engine(ecfg, cfg, max_seq=256)
         outs.append(eng.generate(prompts, SamplingParams(max_new_tokens=8)))
     assert outs[0] == outs[1], outs
+
+
+@pytest.mark.parametrize("e,k,g,kg,ks", [(256, 8, 8, 4, 3), (160, 8, 1, 1, 2), (256, 8, 8, 4, 1)])
+def test_router_sums_split_k_partials(cuda, e, k, g, kg, ks):
+    """The router kernel fed the router GEMM's split-K partials (summed in split order inside) picks the same
+    experts with the same weights as the kernel fed the summed logits, and agrees with the oracle."""
+    torch.manual_seed(e + ks)
+    T = 21
+    part = torch.randn(ks * T, e) * 1.5
+    bias = torch.randn(e) * 0.1
+    summed = part[:T].clone()
+    for j in range(1, ks):
+        summed += part[j * T:(j + 1) * T]
+    ids, w = MOE.route(part.to(cuda), bias.to(cuda), k, g, kg, 2.5, ksplit=ks)
+    ids1, w1 = MOE.route(summed.to(cuda), bias.to(cuda), k, g, kg, 2.5)
+    assert torch.equal(ids, ids1) and torch.equal(w, w1)
+    rid, rw = MOE.route_ref(summed, bias, k, g, kg, 2.5)
+    assert torch.equal(ids.cpu().sort(-1).values, rid.sort(-1).values)
+    assert torch.allclose(w.cpu().sort(-1).values, rw.sort(-1).values, rtol=1e-4, atol=1e-5)

@@ -293,3 +293,41 @@ def test_dense_linear_split_k(cuda, t, n, k):
     ref = x.float() @ w.float().T
     err = (y.float() - ref).abs() / (ref.abs() + 1e-2 * ref.abs().max())
     assert err.max().item() < 1e-2, err.max().item()
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_rmsnorm_quant_wide_rows_spread_over_ctas(cuda, fmt):
+    """Few wide rows without a norm spread each row over several CTAs (the decode-size quantization of the o_proj
+    input): the same bytes as the row-per-CTA oracle."""
+    from inference_optimizations_b200._ext import ext
+    torch.manual_seed(5)
+    T, H = 3, 16384
+    x = (torch.randn(T, H) * torch.exp2(torch.randint(-5, 6, (T, H // 128)).float().repeat_interleave(128, 1)))
+    x = x.to(torch.bfloat16)
+    q = torch.empty(T, H if fmt == 0 else H // 2, dtype=torch.uint8, device=cuda)
+    sc = torch.empty(T, H // 128 if fmt == 0 else H // 64, dtype=torch.int32, device=cuda)
+    ext().rmsnorm_quant(x.to(cuda), None, 0.0, 0.0, q, sc, fmt)
+    rq, rs = MG.quant_rows(x.float()) if fmt == 0 else MG.quant_nvfp4_rows(x.float())
+    assert torch.equal(q.cpu(), rq) and torch.equal(sc.cpu(), rs)
+
+
+def test_dense_ffn_split_down_projection(cuda):
+    """A dense FFN (one expert holding every token) at decode sizes splits its down projection over K; the result
+    matches the fp32 oracle, and a token's output does not depend on the batch it runs in (up to 64 tokens)."""
+    torch.manual_seed(12)
+    F, H = 4096, 1024
+    wg = torch.randn(1, F, H, device=cuda) * 0.03
+    wu = torch.randn(1, F, H, device=cuda) * 0.03
+    wd = torch.randn(1, H, F, device=cuda) * 0.03
+    ex = MG.Fp8Experts(wg, wu, wd)
+    assert ex._dense_split(H // (128 * ex.g2), F // 128, 16) > 1
+    x = torch.randn(9, H, device=cuda).to(torch.bfloat16)
+    one = lambda n: (torch.zeros(n, 1, dtype=torch.int32, device=cuda), torch.ones(n, 1, device=cuda))  # noqa: E731
+    y = ex.forward(x, *one(9))
+    torch.cuda.synchronize()
+    assert ex.status.item() == 0
+    ref = ex.forward_ref(x, *one(9))
+    cos = Fn.cosine_similarity(y.float().flatten(), ref.float().flatten(), dim=0).item()
+    assert cos > 0.999, cos
+    y3 = ex.forward(x[:3].contiguous(), *one(3))
+    assert torch.equal(y3, y[:3])
