@@ -18,8 +18,9 @@ and device->host result read, timed on the device around the whole loop (max ove
 (tens of GB) are far larger than the 126 MB L2, so no flush is needed between steps.
 
 Depth: `--layers` (default 13 = the 3 dense layers + 10 MoE layers, the deepest stack whose 256 experts per layer fit
-one GPU) is the same at every N so the 1/2/4/8 curve measures one model; `--full-depth` additionally runs the full
-61-layer model (it needs the expert memory of 8 GPUs) and reports it as the `full_depth` field.
+one GPU) is the same at every N so the 1/2/4/8 curve measures one model; at 8 GPUs (or with `--full-depth`) the full
+61-layer model (it needs the expert memory of 8 GPUs) runs too and is reported as the `full_depth` field, with its
+`vs_baseline` against the published 8 x B200 figure.
 """
 from __future__ import annotations
 
@@ -44,7 +45,9 @@ def parse():
     p.add_argument("--ctx", type=int, default=None, help="prompt tokens (dsa_moe 8192, gemma31b 32768)")
     p.add_argument("--max-new", type=int, default=None, help="output tokens (dsa_moe 1024, gemma31b 512)")
     p.add_argument("--layers", type=int, default=13, help="dsa_moe: depth of the scaling-curve model")
-    p.add_argument("--full-depth", action="store_true", help="dsa_moe: also run the full-depth model")
+    p.add_argument("--full-depth", dest="full_depth", action="store_true", default=None,
+                   help="dsa_moe: also run the full 61-layer model (default: on at 8 GPUs, the published config)")
+    p.add_argument("--no-full-depth", dest="full_depth", action="store_false")
     p.add_argument("--kv", default="nvfp4", choices=["nvfp4", "fp8", "bf16"])
     p.add_argument("--spec", type=int, default=1,
                    help="gemma31b: 1 = speculative decoding, the config's 1-layer draft proposing 3 tokens; 0 = plain")
@@ -99,6 +102,32 @@ def _sum_ranks(x: int, dev) -> int:
     t = torch.tensor([x], dtype=torch.int64, device=dev)
     dist.all_reduce(t)
     return int(t.item())
+
+
+def _tokens_check(eng, dev) -> dict:
+    """Correctness of the multi-GPU step on the driver's path: the next decode step of every session computed three
+    ways from the same state -- the captured graph (the timed path), eager with the peer-memory expert exchange, eager
+    with the NCCL baseline exchange -- must give the same greedy tokens on every rank.  Re-running a step rewrites
+    the same KV rows, so the check leaves the sessions as they were (nothing is committed to the scheduler)."""
+    runner, model = eng.runner, eng.runner.model
+    reqs = list(eng.sched.running)
+    graphs = runner.ecfg.cuda_graphs
+    out_graph = runner.decode(reqs)
+    runner.ecfg.cuda_graphs = False
+    try:
+        out_eager = runner.decode(reqs)
+        for ex in model.ep.values():
+            ex.use_nccl = True
+        out_nccl = runner.decode(reqs)
+    finally:
+        for ex in model.ep.values():
+            ex.use_nccl = False
+        runner.ecfg.cuda_graphs = graphs
+    same = int(out_graph == out_eager == out_nccl)
+    from inference_optimizations_b200.parallel import dist as D
+    return {"tokens_match": bool(D.max_over_ranks(float(1 - same)) == 0.0), "sessions_checked": len(reqs),
+            "compared": "greedy tokens of one decode step: CUDA graph (timed path) vs eager peer-memory EP vs eager "
+                        "NCCL EP (all-gather + all-to-all), every rank"}
 
 
 def run_dsa(args, info, dev, layers: int, steps: int, warm: int) -> dict:
@@ -184,6 +213,7 @@ def run_dsa(args, info, dev, layers: int, steps: int, warm: int) -> dict:
         for ws in d.values():
             status |= int(ws.status.item())
     status = int(D.max_over_ranks(float(status)))
+    check = _tokens_check(eng, dev) if n > 1 else None
     table1 = eng.runner.kv.table.bytes_synced if hasattr(eng.runner.kv.table, "bytes_synced") else 0
     h2d = 5 * 4 * bucket + (table1 - table0) // max(1, steps)
     mem_gb = D.max_over_ranks(torch.cuda.max_memory_allocated(dev) / 1e9)
@@ -203,7 +233,7 @@ def run_dsa(args, info, dev, layers: int, steps: int, warm: int) -> dict:
                     "note": "every session's prompt prefilled through Engine.step() (chunks of one prompt per step "
                             "per rank, sessions queued at t = 0), device time max over ranks; TTFT = host time from "
                             "the start of the phase to the step that returned the session's first token"},
-        "status": status, "max_mem_gb": round(mem_gb, 1), "build_s": round(build_s, 1),
+        "status": status, "check": check, "max_mem_gb": round(mem_gb, 1), "build_s": round(build_s, 1),
         "clocks": ck, "rejected": rejected(ck),
     }
     eng.runner.graphs.clear()
@@ -224,13 +254,15 @@ def bench_dsa(args) -> int:
     n = info.world
     r = run_dsa(args, info, dev, args.layers, steps, warm)
     full = None
+    if args.full_depth is None:          # the published figures are for the 61-layer model on 8 GPUs
+        args.full_depth = n == 8 and args.layers < 61
     if args.full_depth:
         torch.cuda.empty_cache()
         f = run_dsa(args, info, dev, 61, steps, warm)
         full = {"layers": 61, "value": round(f["value"], 2), "ms_per_step": round(f["ms_per_step"], 4),
                 "e2e_value": round(f["e2e_value"], 2), "per_user_tok_s": round(f["value"] / args.sessions, 3),
                 "vs_baseline": round(f["value"] / BASELINE_TOK_S, 3), "prefill": f["prefill"],
-                "status": f["status"], "max_mem_gb": f["max_mem_gb"],
+                "status": f["status"], "correctness": f["check"], "max_mem_gb": f["max_mem_gb"],
                 "clocks": {k: f["clocks"].get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons")}}
     res = {
         "metric": (f"output tok/s: DSA-MoE decode of {args.sessions} sessions after their {args.ctx}-token prompts "
@@ -265,6 +297,7 @@ def bench_dsa(args) -> int:
                 "ms_per_step": round(r["e2e_ms_per_step"], 4)},
         "gpu_launches": r["launches"],
         "status": r["status"],
+        "correctness": r["check"],
         "max_mem_gb": r["max_mem_gb"],
         "vs_baseline_note": ("BASELINE.md row 4 (1,813-1,996 steady tok/s at 64 sessions on 8 x B200) is a 61-layer "
                              "number; see full_depth.vs_baseline (--full-depth)"),

@@ -204,6 +204,13 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int& 
   return res;
 }
 
+// Keys a thread holds in registers in the register form (score rows up to kRegKeys x kKThreads = 16384 positions).
+constexpr int kRegKeys = 16;
+
+// REG: the row's order keys are loaded once into registers (each thread a contiguous range of up to kRegKeys
+// positions, 16-byte loads) and every radix pass and the compaction run from them -- one round of global loads
+// instead of five passes over the row.  Otherwise every pass re-reads the scores (rows longer than 16384).
+template <bool REG>
 __global__ void __launch_bounds__(kKThreads) indexer_topk_kernel(const IndexerArgs a) {
   __shared__ int hist[4096];
   __shared__ int warp_sums[33];
@@ -223,6 +230,25 @@ __global__ void __launch_bounds__(kKThreads) indexer_topk_kernel(const IndexerAr
     for (int i = threadIdx.x; i < K; i += kKThreads) emit(i, i < L ? i : -1);
     return;
   }
+  // this thread's contiguous range [i0, i1) (position order is thread order: the compaction emits in it)
+  const int chunk = REG ? (((L + kKThreads - 1) / kKThreads + 3) & ~3) : (L + kKThreads - 1) / kKThreads;
+  const int i0 = threadIdx.x * chunk, i1 = min(L, i0 + chunk);
+  uint32_t keys[REG ? kRegKeys : 1];
+  if constexpr (REG) {
+#pragma unroll
+    for (int j = 0; j < kRegKeys; j += 4) {
+      if (i0 + j + 3 < i1) {
+        const float4 v = *reinterpret_cast<const float4*>(sc + i0 + j);
+        keys[j] = order_key(v.x);
+        keys[j + 1] = order_key(v.y);
+        keys[j + 2] = order_key(v.z);
+        keys[j + 3] = order_key(v.w);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) keys[j + q] = i0 + j + q < i1 ? order_key(sc[i0 + j + q]) : 0u;
+      }
+    }
+  }
   // ---- radix select of the K-th largest order key: 12 + 12 + 8 bits
   uint32_t prefix = 0, mask = 0;
   int remaining = K;
@@ -233,9 +259,15 @@ __global__ void __launch_bounds__(kKThreads) indexer_topk_kernel(const IndexerAr
     const int sh = shifts[pass], nb = 1 << widths[pass];
     for (int b = threadIdx.x; b < 4096; b += kKThreads) hist[b] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < L; i += kKThreads) {
-      const uint32_t u = order_key(sc[i]);
-      if ((u & mask) == prefix) atomicAdd(&hist[(u >> sh) & (nb - 1)], 1);
+    if constexpr (REG) {
+#pragma unroll
+      for (int j = 0; j < kRegKeys; ++j)
+        if (i0 + j < i1 && (keys[j] & mask) == prefix) atomicAdd(&hist[(keys[j] >> sh) & (nb - 1)], 1);
+    } else {
+      for (int i = threadIdx.x; i < L; i += kKThreads) {
+        const uint32_t u = order_key(sc[i]);
+        if ((u & mask) == prefix) atomicAdd(&hist[(u >> sh) & (nb - 1)], 1);
+      }
     }
     __syncthreads();
     // suffix sums from the top bin: each thread owns 4 consecutive bins (nb / 1024 <= 4)
@@ -261,22 +293,35 @@ __global__ void __launch_bounds__(kKThreads) indexer_topk_kernel(const IndexerAr
     __syncthreads();
   }
   // ---- compaction in position order: keys above the threshold, then the first `remaining` equal ones
-  const int chunk = (L + kKThreads - 1) / kKThreads;
-  const int i0 = threadIdx.x * chunk, i1 = min(L, i0 + chunk);
   int gt = 0, eq = 0;
-  for (int i = i0; i < i1; ++i) {
-    const uint32_t u = order_key(sc[i]);
-    gt += u > prefix;
-    eq += u == prefix;
+  if constexpr (REG) {
+#pragma unroll
+    for (int j = 0; j < kRegKeys; ++j)
+      if (i0 + j < i1) {
+        gt += keys[j] > prefix;
+        eq += keys[j] == prefix;
+      }
+  } else {
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t u = order_key(sc[i]);
+      gt += u > prefix;
+      eq += u == prefix;
+    }
   }
   int tot;
   const int eq_before = block_exclusive_scan(eq, warp_sums, tot);
   const int take_eq = max(0, min(eq, remaining - eq_before));
   const int off = block_exclusive_scan(gt + take_eq, warp_sums, tot);
   int w = off, eq_seen = 0;
-  for (int i = i0; i < i1; ++i) {
-    const uint32_t u = order_key(sc[i]);
-    if (u > prefix || (u == prefix && eq_seen++ < take_eq)) emit(w++, i);
+  if constexpr (REG) {
+#pragma unroll
+    for (int j = 0; j < kRegKeys; ++j)
+      if (i0 + j < i1 && (keys[j] > prefix || (keys[j] == prefix && eq_seen++ < take_eq))) emit(w++, i0 + j);
+  } else {
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t u = order_key(sc[i]);
+      if (u > prefix || (u == prefix && eq_seen++ < take_eq)) emit(w++, i);
+    }
   }
 }
 
@@ -295,7 +340,10 @@ cudaError_t indexer_logits(const IndexerArgs& a, cudaStream_t s) {
 cudaError_t indexer_topk(const IndexerArgs& a, cudaStream_t s) {
   if (a.T == 0) return cudaSuccess;
   if (a.topk < 1) return cudaErrorInvalidValue;
-  indexer_topk_kernel<<<a.T, kKThreads, 0, s>>>(a);
+  if (a.score_stride <= kRegKeys * kKThreads)
+    indexer_topk_kernel<true><<<a.T, kKThreads, 0, s>>>(a);
+  else
+    indexer_topk_kernel<false><<<a.T, kKThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -112,7 +112,23 @@ __global__ void __launch_bounds__(32 * kRouteWarps) moe_route_reg_kernel(const f
   float acc[NJ], p[NJ], v[NJ];
 #pragma unroll
   for (int j = 0; j < NJ; ++j) acc[j] = 0.f;
-  for (int k = 0; k < ksplit; ++k) {
+  // partials of kB splits are loaded before any is added (independent loads in flight), then summed in split order
+  constexpr int kB = NJ <= 4 ? 8 : 4;
+  int k = 0;
+  for (; k + kB <= ksplit; k += kB) {
+    float r[kB][NJ];
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+      const float* lg = part + (static_cast<size_t>(k + u) * T + t) * E;
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) r[u][j] = lg[lane + 32 * j];
+    }
+#pragma unroll
+    for (int u = 0; u < kB; ++u)
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) acc[j] += r[u][j];
+  }
+  for (; k < ksplit; ++k) {
     const float* lg = part + (static_cast<size_t>(k) * T + t) * E;
 #pragma unroll
     for (int j = 0; j < NJ; ++j) acc[j] += lg[lane + 32 * j];

@@ -74,6 +74,7 @@ class EPComm:
         self.buf = symm.empty(L.nbytes, dtype=torch.uint8, device=device)
         self.buf.zero_()
         grp = group if group is not None else dist.group.WORLD
+        self.group = grp
         self.handle = symm.rendezvous(self.buf, grp)
         self.peers = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64, device=device)
         rows = world * T_max
@@ -117,8 +118,9 @@ class EPMoE:
                           experts.w1.device, group)
         assert (comm.T_max, comm.topk, comm.world, comm.E_loc) == (T_max, topk, world, self.E_loc)
         self.comm = comm
+        self.use_nccl = False             # True: `forward` runs the NCCL baseline exchange (`forward_nccl`)
         for name in ("layout", "buf", "handle", "peers", "recv_x", "recv_s", "recv_ids", "comb", "epoch", "status",
-                     "xq", "xs", "off", "pairs", "h", "hs", "nt"):
+                     "xq", "xs", "off", "pairs", "h", "hs", "nt", "group"):
             setattr(self, name, getattr(comm, name))
 
     def barrier(self) -> None:
@@ -127,6 +129,8 @@ class EPMoE:
     def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, xq8: tuple | None = None) -> torch.Tensor:
         """x bf16 [T, H] normalized, ids int32 [T, topk] global expert ids, w fp32 [T, topk] -> bf16 [T, H].
         xq8: (E4M3 [T, H], scales [T, H / 128]) when the norm that produced x already quantized it (FP8 experts)."""
+        if self.use_nccl:
+            return self.forward_nccl(x, ids, w, xq8)
         L, ex = self.layout, self.ex
         T, k = ids.shape
         if T > self.T_max:
@@ -157,6 +161,58 @@ class EPMoE:
         self.barrier()
         y = torch.empty(T, self.H, dtype=torch.bfloat16, device=x.device)
         ext().moe_combine(self.comb, T, k, self.T_max * k if ex.has_shared else -1, w.float().contiguous(), y)
+        return y
+
+    def forward_nccl(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor,
+                     xq8: tuple | None = None) -> torch.Tensor:
+        """The same exchange over NCCL collectives instead of peer memory -- the baseline of the fused path and its
+        correctness reference: quantized rows, scales and ids all-gathered (padded to T_max), the same grouped GEMMs
+        on local buffers, every rank's expert rows returned to their token's rank by one all-to-all, each row taken
+        from its expert's owner, the same slot-order combine.  Every value is computed by the same kernels at the
+        same rounding points, so the output equals `forward`'s bit for bit."""
+        L, ex, grp = self.layout, self.ex, self.group
+        T, k = ids.shape
+        if T > self.T_max:
+            raise ValueError(f"{T} tokens > T_max {self.T_max}")
+        dev, Tm, W = x.device, self.T_max, self.world
+        xq = torch.zeros(Tm, L.row_bytes, dtype=torch.uint8, device=dev)
+        xs = torch.zeros(Tm, L.scale_words, dtype=torch.int32, device=dev)
+        if T:
+            if xq8 is not None and self.kind == 0:
+                xq[:T], xs[:T] = xq8
+            else:
+                ext().rmsnorm_quant(x.contiguous(), None, 0.0, 0.0, xq[:T], xs[:T], self.kind)
+        idp = torch.full((Tm, k), -1, dtype=torch.int32, device=dev)
+        idp[:T] = ids
+        rx = torch.empty(W * Tm, L.row_bytes, dtype=torch.uint8, device=dev)
+        rs = torch.empty(W * Tm, L.scale_words, dtype=torch.int32, device=dev)
+        ri = torch.empty(W * Tm * k, dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(rx, xq, group=grp)
+        dist.all_gather_into_tensor(rs, xs, group=grp)
+        dist.all_gather_into_tensor(ri, idp.view(-1), group=grp)
+        extra = T if ex.has_shared else 0
+        ext().moe_align(ri, self.rank * self.E_loc, self.E_loc, extra, self.off, self.pairs)
+        P = L.pairs_total
+        vals = 128 if self.kind == 0 else 256
+        MG.gemm(ex.w1, rx, rs, self.off, self.pairs, self.h, self.status,
+                n_tiles=self.F // 128, kc=self.H // vals, g=2, nt=self.nt, mode=1, src_div=k,
+                src_limit=P, src_shared_base=self.rank * Tm, out_scale=self.hs, num_ctas=ex.num_ctas,
+                kind=self.kind, expert_mul=ex.mul1)
+        rows = torch.empty(P + Tm, self.H, dtype=torch.bfloat16, device=dev)   # row = pair id; shared: P + t
+        MG.gemm(ex.w2, self.h, self.hs, self.off, self.pairs, rows, self.status,
+                n_tiles=self.H // (128 * ex.g2), kc=self.F // vals, g=ex.g2, nt=self.nt, mode=0, src_div=1,
+                num_ctas=ex.num_ctas, kind=self.kind, expert_mul=ex.mul2)
+        back = torch.empty(P, self.H, dtype=torch.bfloat16, device=dev)        # block q: my pairs as rank q saw them
+        dist.all_to_all_single(back, rows[:P], group=grp)
+        comb = torch.zeros(L.comb_rows, self.H, dtype=torch.bfloat16, device=dev)
+        if T:
+            slot = torch.arange(T * k, device=dev)
+            owner = (ids.reshape(-1).long() // self.E_loc).clamp(0, W - 1)
+            comb[:T * k] = back[owner * (Tm * k) + slot]
+            if ex.has_shared:
+                comb[Tm * k:Tm * k + T] = rows[P:P + T]
+        y = torch.empty(T, self.H, dtype=torch.bfloat16, device=dev)
+        ext().moe_combine(comb, T, k, Tm * k if ex.has_shared else -1, w.float().contiguous(), y)
         return y
 
     def check(self) -> None:

@@ -1,6 +1,6 @@
 """Expert-parallel MoE over peer memory (parallel/ep.py) on 2 GPUs: each rank's output equals the single-GPU
 grouped-expert path on the same tokens with all experts local, for FP8 and NVFP4 weights, with an idle rank, and
-across repeated layers (buffer reuse).  Runs as two child processes (needs >= 2 GPUs)."""
+across repeated layers (buffer reuse); the NCCL baseline exchange (`forward_nccl`) gives the same output bit for bit.  Runs as two child processes (needs >= 2 GPUs)."""
 import os
 import subprocess
 import sys
@@ -42,6 +42,11 @@ WORKER = textwrap.dedent("""
         y = ep.forward(x, ids, w)
         torch.cuda.synchronize()
         ep.check()
+        yn = ep.forward_nccl(x, ids, w)          # NCCL baseline exchange: the same values bit for bit
+        torch.cuda.synchronize()
+        if not torch.equal(y, yn):
+            print(f"rank {rank} layer {layer}: NCCL path differs", flush=True)
+            worst = -1.0
         if T:
             ref = full.forward(x, ids, w)
             cos = Fn.cosine_similarity(y.float().flatten(), ref.float().flatten(), dim=0).item()

@@ -306,3 +306,29 @@ def test_gqa_extend(cuda, fmt, d, window):
         dec = A.gqa_decode(q[s0:s0 + m].contiguous(), pool, pt, kvl, 1, hk, fmt, sm, window, *scale, req_idx=rix)
         torch.cuda.synchronize()
         assert (dec.float() - out[s0:s0 + m].float()).abs().max().item() < tol
+
+
+@pytest.mark.parametrize("width", [9216, 20480])
+def test_indexer_topk_ties_both_forms(cuda, width):
+    """Top-k selection alone over score rows with many exact ties (the register form for rows up to 16384
+    positions, the re-reading form beyond): the same positions, in position order, as the oracle."""
+    from inference_optimizations_b200._ext import ext
+    from inference_optimizations_b200.ops import indexer as I
+    torch.manual_seed(2)
+    lens = [width, width - 37, 3000, 2048, 1]
+    t, topk = len(lens), 2048
+    per = -(-width // 64)
+    pt = torch.randperm(t * per + 1)[: t * per].view(t, per).int()
+    scores = (torch.randn(t, width) * 4).round() / 4                  # few distinct values: ties at the threshold
+    limit = torch.tensor(lens, dtype=torch.int32)
+    slots = torch.empty(t, topk, dtype=torch.int32, device=cuda)
+    pos = torch.empty(t, topk, dtype=torch.int32, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    q8 = torch.zeros(t, 64, 128, dtype=torch.uint8, device=cuda)
+    w = torch.zeros(t, 64, device=cuda)
+    pool = torch.zeros(1, K.INDEX_PAGE_BYTES, dtype=torch.uint8, device=cuda)
+    sc = scores.to(cuda)
+    ext().indexer(q8, w, pool, pt.to(cuda), None, limit.to(cuda), sc, slots, pos, status, 1, width // 128, 0, 1)
+    torch.cuda.synchronize()
+    rs, rp = I.topk_ref(scores, limit, topk, pt)
+    assert torch.equal(pos.cpu(), rp) and torch.equal(slots.cpu(), rs)
