@@ -100,39 +100,31 @@ __device__ __forceinline__ void warp_top2(float& b1, float& b2) {
   }
 }
 
+// One CTA (8 warps) per token: the warps stage the token's ksplit x E partials in shared memory with coalesced
+// loads (one round of independent loads however many splits), then warp 0 sums them in split order and routes.
+constexpr int kRegThreads = 256;
+
 template <int NJ>
-__global__ void __launch_bounds__(32 * kRouteWarps) moe_route_reg_kernel(const float* __restrict__ part, int ksplit,
-                                                                         const float* __restrict__ bias, int* ids,
-                                                                         float* wts, int T, int K, int G, int KG,
-                                                                         float scale) {
+__global__ void __launch_bounds__(kRegThreads) moe_route_reg_kernel(const float* __restrict__ part, int ksplit,
+                                                                    const float* __restrict__ bias, int* ids,
+                                                                    float* wts, int T, int K, int G, int KG,
+                                                                    float scale) {
   constexpr int E = 32 * NJ;
+  extern __shared__ float stage[];                          // [ksplit][E]
+  const int t = blockIdx.x;
+  for (int i = threadIdx.x; i < ksplit * E; i += kRegThreads) {
+    const int k = i / E, e = i - k * E;
+    stage[i] = part[(static_cast<size_t>(k) * T + t) * E + e];
+  }
+  __syncthreads();
+  if (warp_id() != 0) return;
   const int lane = lane_id();
-  const int t = blockIdx.x * kRouteWarps + warp_id();
-  if (t >= T) return;
   float acc[NJ], p[NJ], v[NJ];
 #pragma unroll
   for (int j = 0; j < NJ; ++j) acc[j] = 0.f;
-  // partials of kB splits are loaded before any is added (independent loads in flight), then summed in split order
-  constexpr int kB = NJ <= 4 ? 8 : 4;
-  int k = 0;
-  for (; k + kB <= ksplit; k += kB) {
-    float r[kB][NJ];
+  for (int k = 0; k < ksplit; ++k)
 #pragma unroll
-    for (int u = 0; u < kB; ++u) {
-      const float* lg = part + (static_cast<size_t>(k + u) * T + t) * E;
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) r[u][j] = lg[lane + 32 * j];
-    }
-#pragma unroll
-    for (int u = 0; u < kB; ++u)
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) acc[j] += r[u][j];
-  }
-  for (; k < ksplit; ++k) {
-    const float* lg = part + (static_cast<size_t>(k) * T + t) * E;
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) acc[j] += lg[lane + 32 * j];
-  }
+    for (int j = 0; j < NJ; ++j) acc[j] += stage[k * E + lane + 32 * j];
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
     p[j] = 1.f / (1.f + __expf(-acc[j]));
@@ -211,11 +203,16 @@ cudaError_t moe_route(const float* logits, const float* bias, int* ids, float* w
   if (E > 256 || K > 32 || K > E || G < 1 || G > 32 || E % G || KG < 1 || KG > G || ksplit < 1)
     return cudaErrorInvalidValue;
   const int grid = (T + kRouteWarps - 1) / kRouteWarps;
-  if (E % 32 == 0 && (E / G) % 32 == 0) {
+  const int stage_bytes = ksplit * E * static_cast<int>(sizeof(float));
+  if (E % 32 == 0 && (E / G) % 32 == 0 && stage_bytes <= 200 * 1024) {
     switch (E / 32) {
-#define IOB_ROUTE(nj)                                                                                             \
-  case nj:                                                                                                        \
-    moe_route_reg_kernel<nj><<<grid, 32 * kRouteWarps, 0, s>>>(logits, ksplit, bias, ids, wts, T, K, G, KG, scale); \
+#define IOB_ROUTE(nj)                                                                                              \
+  case nj:                                                                                                         \
+    if (stage_bytes > 48 * 1024)                                                                                   \
+      IOB_CUDA_CHECK(cudaFuncSetAttribute(moe_route_reg_kernel<nj>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
+                                          stage_bytes));                                                           \
+    moe_route_reg_kernel<nj><<<T, kRegThreads, stage_bytes, s>>>(logits, ksplit, bias, ids, wts, T, K, G, KG,      \
+                                                                 scale);                                           \
     return cudaGetLastError();
       IOB_ROUTE(1) IOB_ROUTE(2) IOB_ROUTE(3) IOB_ROUTE(4) IOB_ROUTE(5) IOB_ROUTE(6) IOB_ROUTE(7) IOB_ROUTE(8)
 #undef IOB_ROUTE
