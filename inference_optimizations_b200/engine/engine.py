@@ -28,7 +28,8 @@ class StepStats:
 class Engine:
     def __init__(self, ecfg: EngineConfig, model_cfg=None, max_seq: int = 4096, tp_rank: int = 0, tp: int = 1,
                  all_reduce=None, argmax_merge=None, global_pages: Optional[int] = None, ep_rank: int = 0,
-                 ep_group=None, dcp_rank: int = 0, dcp_group=None):
+                 ep_group=None, dcp_rank: int = 0, dcp_group=None, kv_storage=None):
+        """kv_storage (MLA family): places the KV pools (`MLAKVCache(storage=)`; prefill / decode disaggregation)."""
         self.ecfg = ecfg
         self.cfg = model_cfg if model_cfg is not None else model_config(ecfg.model)
         self.device = torch.device(ecfg.device)
@@ -38,7 +39,7 @@ class Engine:
         else:
             from .mla_runner import MLARunner
             self.runner = MLARunner(self.cfg, ecfg, self.device, max_seq, tp_rank, tp, ep_rank, ep_group, dcp_rank,
-                                    dcp_group)
+                                    dcp_group, kv_storage=kv_storage)
         self.sched = Scheduler(ecfg.max_running, ecfg.chunked_prefill, ecfg.decode_burst,
                                can_admit=self.runner.can_admit, on_admit=getattr(self.runner, "on_admit", None))
         self.stats: list[StepStats] = []

@@ -39,7 +39,7 @@ def pool_pages(ecfg: EngineConfig, need: int, page_bytes: int, device) -> int:
 
 class MLARunner:
     def __init__(self, cfg: MLAMoEConfig, ecfg: EngineConfig, device, max_seq: int, tp_rank: int = 0, tp: int = 1,
-                 ep_rank: int = 0, ep_group=None, dcp_rank: int = 0, dcp_group=None):
+                 ep_rank: int = 0, ep_group=None, dcp_rank: int = 0, dcp_group=None, kv_storage=None):
         """ecfg.ep > 1: data-parallel attention + expert-parallel MoE.  Every rank runs its own requests (its own
         scheduler, pools and replicated attention weights); every MoE layer is an exchange over `ep_group` with
         `ecfg.ep` ranks, so all ranks step in lockstep: before each forward the ranks agree on the largest token
@@ -78,7 +78,8 @@ class MLARunner:
         pages = pool_pages(ecfg, self.max_running * per_req + 2,
                            (cfg.num_layers + int(self.spec)) * 64 * (M_ROW_BYTES[fmt] + INDEX_ROW_BYTES), self.device)
         self.kv = MLAKVCache(cfg, self.device, fmt, self.max_running + 1, per_req, pages,
-                             extra_layers=1 if self.spec else 0, latent_div=self.dcp_world)
+                             extra_layers=1 if self.spec else 0, latent_div=self.dcp_world, storage=kv_storage)
+        pages = self.kv.pages
         self.pool_tokens = 64 * (pages - 2)           # KV positions the pool holds (the boot-time capacity)
         self.dummy_row = self.max_running
         self.pages: dict[int, RequestPages] = {}

@@ -102,16 +102,24 @@ class MLAStep:
 
 class MLAKVCache:
     def __init__(self, cfg: MLAMoEConfig, device, fmt: int, rows: int, max_pages: int, pages: int,
-                 extra_layers: int = 0, latent_div: int = 1):
+                 extra_layers: int = 0, latent_div: int = 1, storage=None):
         """latent_div S > 1 (decode context parallelism): this rank's latent pools hold the rows it owns, 1 / S of
-        the page space (pool row v at local row v // S); the index pools stay whole (every rank scores every row)."""
+        the page space (pool row v at local row v // S); the index pools stay whole (every rank scores every row).
+        storage(layers, pages, row_bytes) -> (pages, latent pools [pages * 64, row_bytes], index pools [pages,
+        8448]): pools placed by the caller (prefill / decode disaggregation maps them from symmetric memory); it may
+        lower the page count (both sides of a pair agree on one)."""
         self.cfg, self.device, self.fmt = cfg, torch.device(device), fmt
         rb = M.ROW_BYTES[fmt]
         n = cfg.num_layers + extra_layers           # extra: the MTP draft layer's pools (same page ids)
-        lat_rows = -(-pages * 64 // latent_div)
-        self.latent = [torch.zeros(lat_rows, rb, dtype=torch.uint8, device=self.device) for _ in range(n)]
-        self.index = [torch.zeros(pages, K.INDEX_PAGE_BYTES, dtype=torch.uint8, device=self.device)
-                      for _ in range(n)]
+        if storage is not None:
+            assert latent_div == 1, "placed pools hold whole pages"
+            pages, self.latent, self.index = storage(n, pages, rb)
+        else:
+            lat_rows = -(-pages * 64 // latent_div)
+            self.latent = [torch.zeros(lat_rows, rb, dtype=torch.uint8, device=self.device) for _ in range(n)]
+            self.index = [torch.zeros(pages, K.INDEX_PAGE_BYTES, dtype=torch.uint8, device=self.device)
+                          for _ in range(n)]
+        self.pages = pages
         from ..kv.allocator import PageAllocator, PageTable
         self.alloc = PageAllocator(pages)
         self.table = PageTable(rows, max_pages, self.device)

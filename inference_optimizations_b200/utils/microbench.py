@@ -362,7 +362,8 @@ def ep_moe_case(tokens: int, total_experts: int, topk: int, hidden: int, ffn: in
     """Expert-parallel MoE layer (parallel/ep.py) under torchrun: each rank routes `tokens` tokens top-k over
     `total_experts`, owns total_experts / world of them (+ a shared expert); one forward = quantize, dispatch,
     barrier, align, two grouped GEMMs (peer-store epilogue), barrier, combine.  Device time per layer, max over
-    ranks (CUDA events around `iters` forwards, synchronized and barriered on both sides)."""
+    ranks (CUDA events around `iters` forwards, synchronized and barriered on both sides); the same for the NCCL
+    baseline exchange (`EPMoE.forward_nccl`: all-gather + the same GEMMs + all-to-all) on the same inputs."""
     import torch.distributed as dist
     from ..ops import moe_gemm as MG
     from ..parallel.ep import EPMoE
@@ -389,6 +390,21 @@ def ep_moe_case(tokens: int, total_experts: int, topk: int, hidden: int, ffn: in
     ep.check()
     us = torch.tensor([e0.elapsed_time(e1) / iters * 1e3], device=dev)
     dist.all_reduce(us, op=dist.ReduceOp.MAX)
+    # the NCCL baseline exchange (all-gather + all-to-all) around the same GEMMs, same inputs
+    ep.use_nccl = True
+    for _ in range(3):
+        ep.forward(x, ids, w)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0.record()
+    for _ in range(iters):
+        ep.forward(x, ids, w)
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ep.use_nccl = False
+    us_nccl = torch.tensor([e0.elapsed_time(e1) / iters * 1e3], device=dev)
+    dist.all_reduce(us_nccl, op=dist.ReduceOp.MAX)
     # roofline: touched local experts' weights once (HBM) vs rows crossing NVLink
     all_ids = [torch.empty_like(ids) for _ in range(world)]
     dist.all_gather(all_ids, ids)
@@ -406,6 +422,7 @@ def ep_moe_case(tokens: int, total_experts: int, topk: int, hidden: int, ffn: in
            "experts_total": total_experts, "hidden": hidden, "ffn": ffn, "us_max_over_ranks": round(float(us), 1),
            "touched_local_experts": touched, "roofline_us": round(floor, 1),
            "frac_of_roofline": round(floor / float(us), 3),
+           "nccl_baseline_us": round(float(us_nccl), 1), "speedup_vs_nccl": round(float(us_nccl) / float(us), 2),
            "roofline_basis": "max(touched weights / measured HBM, remote rows / 770 GB/s)"}
     del ep
     return res if rank == 0 else {}

@@ -1,6 +1,8 @@
 """Prefill -> decode page transfer over peer memory (parallel/pd.py) on 2 GPUs: pages of every layer land at the
 planned decode pages bit for bit, the decode side's device wait releases on the published sequence number, and a
-sequence number nobody publishes ends the wait with a status instead of a hang.  Two child processes."""
+sequence number nobody publishes ends the wait with a status instead of a hang.  The disaggregated serving pair
+(engine/pd_serve.py: prefill engine on GPU 0, decode engine on GPU 1) generates what one engine generates.  Two child
+processes per test."""
 import os
 import subprocess
 import sys
@@ -52,15 +54,61 @@ WORKER = textwrap.dedent("""
 
 
 def test_pd_page_transfer_two_gpus(cuda, tmp_path):
+    _run_pair(tmp_path, WORKER, "29591")
+
+
+SERVE_WORKER = textwrap.dedent("""
+    import os, sys, torch, torch.distributed as dist
+    from inference_optimizations_b200.config import EngineConfig, model_config
+    from inference_optimizations_b200.engine.engine import Engine
+    from inference_optimizations_b200.engine.pd_serve import PDPair, DECODE
+    from inference_optimizations_b200.engine.scheduler import SamplingParams
+    rank = int(os.environ["RANK"])
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", device_id=dev)
+    cpu = dist.new_group(backend="gloo")
+    cfg = model_config("tiny_mla", expert_ffn=256, dense_ffn=512, weight_dtype="fp8", expert_dtype="fp8")
+    prompts = [[(17 * i + 5 * j) % 500 + 1 for j in range(40 + 37 * i)] for i in range(5)]
+    params = SamplingParams(max_new_tokens=7)
+    ok = True
+    for running in (1, 4):
+        ecfg = EngineConfig(model="tiny_mla", device=str(dev), kv_dtype="nvfp4", max_running=running,
+                            chunked_prefill=96, graph_batch_sizes="1,2,4", prefix_cache=False,
+                            max_total_tokens=4096)
+        pair = PDPair(ecfg, cfg, max_seq=512, cpu_group=cpu)
+        outs = pair.serve(prompts if rank == DECODE else None, params)
+        if rank == DECODE:
+            ref = Engine(ecfg, cfg, max_seq=512).generate(prompts, params)     # one engine on the decode GPU
+            agree = sum(a == b for o, r in zip(outs, ref) for a, b in zip(o, r)) / sum(len(r) for r in ref)
+            first = all(o[0] == r[0] for o, r in zip(outs, ref))
+            print(f"max_running {running}: transfers via pair, agreement {agree:.3f} first {first}", flush=True)
+            # one request at a time: every step has the same shapes as the single engine's -> identical tokens;
+            # concurrent: the first tokens (prefill) are identical, decode batches may group differently
+            ok &= first and (outs == ref if running == 1 else agree >= 0.9)
+        else:
+            ok &= pair.transfers == len(prompts)
+        del pair
+        dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if ok else 1)
+""")
+
+
+def test_pd_disaggregated_serving_two_gpus(cuda, tmp_path):
+    _run_pair(tmp_path, SERVE_WORKER, "29592")
+
+
+def _run_pair(tmp_path, worker: str, port: str):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     script = tmp_path / "pd_worker.py"
-    script.write_text(WORKER)
+    script.write_text(worker)
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     procs = []
     for r in range(2):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
-                   MASTER_PORT="29591", NCCL_NVLS_ENABLE="0",
+                   MASTER_PORT=port, NCCL_NVLS_ENABLE="0",
                    PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
         procs.append(subprocess.Popen([sys.executable, str(script)], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
