@@ -258,7 +258,12 @@ def bench_dsa(args) -> int:
         args.full_depth = n == 8 and args.layers < 61
     if args.full_depth:
         torch.cuda.empty_cache()
-        f = run_dsa(args, info, dev, 61, steps, warm)
+        try:
+            f = run_dsa(args, info, dev, 61, steps, warm)
+        except (RuntimeError, torch.OutOfMemoryError) as e:     # the scaling-curve line is still printed
+            f = None
+            full = {"layers": 61, "error": f"{type(e).__name__}: {str(e)[:300]}"}
+    if args.full_depth and f is not None:
         full = {"layers": 61, "value": round(f["value"], 2), "ms_per_step": round(f["ms_per_step"], 4),
                 "e2e_value": round(f["e2e_value"], 2), "per_user_tok_s": round(f["value"] / args.sessions, 3),
                 "vs_baseline": round(f["value"] / BASELINE_TOK_S, 3), "prefill": f["prefill"],

@@ -202,6 +202,8 @@ class EngineConfig:
     tp_push: bool = True                 # TP: row-parallel GEMMs push their tiles to every rank (fused GEMM ->
                                          # all-reduce); False = GEMM, then a pull-form reduce over NVLink
     tp_nvls: bool = False                # TP: switch-side reduction (NVLS multimem) after the GEMM instead of push
+    tp_qar: bool = False                 # TP: FP8-quantized two-shot all-reduce over peer memory (half the wire
+                                         # bytes, lossy; for byte-bound links) instead of the fused bf16 forms
     # diagnostics
     trace: str = ""                      # directory for the per-rank scheduler trace (JSONL); empty = off
     bounds_check: bool = False           # host-polled index checks before kernels (the IMA locator)

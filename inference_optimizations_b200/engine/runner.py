@@ -101,7 +101,16 @@ class GQARunner:
                               weights=shard_gqa(ck, cfg, tp_rank, tp, device, draft=True) if ck else None) \
             if self.spec else None
         self.tp_comm = None
-        if tp > 1 and ecfg.fused_comm and self.device.type == "cuda":
+        self.qar = None
+        if tp > 1 and ecfg.tp_qar and self.device.type == "cuda":
+            # FP8 two-shot all-reduce (csrc/qar.cu) as the model's all-reduce; the norms run as their own kernels
+            from ..parallel.qar import QuantAllReduce
+            rows = max(ecfg.chunked_prefill, 4 * max(ecfg.graph_sizes() + [ecfg.max_running]))
+            self.qar = QuantAllReduce(tp_rank, tp, rows, cfg.hidden, self.device)
+            for m in (self.model, self.draft):
+                if m is not None:
+                    m.all_reduce = self.qar
+        elif tp > 1 and ecfg.fused_comm and self.device.type == "cuda":
             from ..parallel.symm import TPComm
             rows = max(ecfg.chunked_prefill, 4 * max(ecfg.graph_sizes() + [ecfg.max_running]))
             push = (ecfg.tp_push and not ecfg.tp_nvls and self.model.can_push()
