@@ -88,7 +88,8 @@ MODEL_WORKER = textwrap.dedent("""
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
     dev = torch.device("cuda", rank)
-    over = dict(expert_ffn=256, dense_ffn=512, weight_dtype="fp8", expert_dtype="fp8", hidden=512, q_lora=256,
+    wdt = os.environ["DCP_WDT"]
+    over = dict(expert_ffn=256, dense_ffn=512, weight_dtype=wdt, expert_dtype=wdt, hidden=512, q_lora=256,
                 qk_nope=128, v_head=128, index_heads=8, num_heads=8)
     cfg = model_config("tiny_mla", **over)
     prompt = [(13 * j + 7) % 500 + 1 for j in range(150)]
@@ -120,9 +121,13 @@ MODEL_WORKER = textwrap.dedent("""
     same = torch.equal(both[0], both[1])
     print(f"rank {rank} cos median {cos.median().item():.5f} min {cos.min().item():.5f} same {same} {outs}",
           flush=True)
-    # FP8 activations and split partial sums round differently from the one-GPU model (a random-init router can flip
-    # a near-tie expert on a rare token): the same bounds as the model's GPU-vs-oracle test
-    ok = cos.median().item() > 0.99 and cos.min().item() > 0.9 and same
+    # The context-parallel model sums bf16 partials (row-parallel W_UV / W_o, split FFN) where the one-GPU model
+    # accumulates once, and each rank's sparse attention rounds P to E4M3 against its own running max.  With bf16
+    # weights these differences stay at bf16 level (tight bound).  With FP8 weights every activation is re-quantized
+    # to E4M3 (3 mantissa bits) at each projection, so a one-ulp bf16 difference upstream can move a value across an
+    # E4M3 rounding boundary and the random-init stack amplifies it: a looser bound there.
+    med, lo = (0.995, 0.95) if wdt == "bf16" else (0.97, 0.85)
+    ok = cos.median().item() > med and cos.min().item() > lo and same
     dist.barrier()
     del eng
     dist.destroy_process_group()
@@ -130,7 +135,8 @@ MODEL_WORKER = textwrap.dedent("""
 """)
 
 
-def test_dcp_model_two_gpus(cuda, tmp_path):
+@pytest.mark.parametrize("wdt", ["bf16", "fp8"])
+def test_dcp_model_two_gpus(cuda, tmp_path, wdt):
     """The MLA model with decode context parallelism on 2 GPUs (owned latent rows, peer-memory merge, fused
     all-reduce + norm of the row-parallel products) tracks the whole model on one GPU; both ranks agree exactly."""
     if torch.cuda.device_count() < 2:
@@ -141,7 +147,7 @@ def test_dcp_model_two_gpus(cuda, tmp_path):
     procs = []
     for r in range(2):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
-                   MASTER_PORT="29583", NCCL_NVLS_ENABLE="0",
+                   MASTER_PORT="29583" if wdt == "bf16" else "29584", NCCL_NVLS_ENABLE="0", DCP_WDT=wdt,
                    PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
         procs.append(subprocess.Popen([sys.executable, str(script)], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
