@@ -182,6 +182,10 @@ class EngineConfig:
     decode_burst: int = 1                # --num-continuous-decode-steps semantics (`scheduler/decode-burst/decode_burst.py`)
     burst_queue_cap: int = 2
     max_delay_passes: int = 8
+    dp_pace_steps: int = 0               # DP: passes a lone continuing chunked prefill may be parked so idle decoders
+                                         # run (`dp_policy.pace_decide`); 0 = off
+    dp_skew_floor: int = 0               # DP: cap a rank's prefill chunk at max(floor, other ranks' extends) while
+                                         # the others mostly decode (`dp_policy.skew_chunk_cap`); 0 = off
     # speculative decoding
     spec: bool = False
     draft_tokens: int = 3

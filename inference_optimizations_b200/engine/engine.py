@@ -68,14 +68,15 @@ class Engine:
     def add_request(self, prompt: list, params: Optional[SamplingParams] = None) -> Request:
         return self.sched.new_request(prompt, params or SamplingParams())
 
-    def step(self, hold: Optional[bool] = None, chunk_cap: int = 0) -> dict:
-        """One engine iteration.  Returns rid -> tokens produced this step.  hold / chunk_cap: the data-parallel
-        ranks' joint decode-burst decision and prefill budget for this pass (`generate_dp`); default: local rules."""
+    def step(self, hold: Optional[bool] = None, chunk_cap: int = 0, park: bool = False) -> dict:
+        """One engine iteration.  Returns rid -> tokens produced this step.  hold / chunk_cap / park: the
+        data-parallel ranks' joint decode-burst decision, prefill budget and pacing decision for this pass
+        (`generate_dp`); default: local rules."""
         if self.pdmux is not None:
             return self._pdmux_step()
         t0 = time.perf_counter()
         rec = self.trace.begin() if self.trace else None
-        batch = self.sched.schedule(hold, chunk_cap)
+        batch = self.sched.schedule(hold, chunk_cap, park)
         if batch is None:
             if getattr(self.runner, "ep_world", 1) > 1:
                 self.runner.idle_step()          # data-parallel attention: join the busy ranks' MoE exchanges
@@ -162,7 +163,7 @@ class Engine:
         (the same assignment on every rank) and the return value is {global index: output} for this rank's share."""
         import torch.distributed as dist
         from .burst import RankFacts, dp_hold
-        from .dp_policy import DPBalancer, prefill_budget
+        from .dp_policy import DPBalancer, pace_decide, prefill_budget, skew_chunk_cap
         if self.pdmux is not None and self.pdmux.group is None:
             raise ValueError("generate_dp with pdmux needs the lanes' CPU group (PdmuxEngine(group=...)): the lanes "
                              "of data-parallel ranks advance in lockstep through it")
@@ -174,7 +175,7 @@ class Engine:
         else:
             reqs = {i: self.add_request(p, params) for i, p in enumerate(prompts)}
         dev = self.device if dist.get_backend(group) == "nccl" else torch.device("cpu")
-        delayed = 0
+        delayed = pace_streak = 0
         self.dp_log: list = []
         while True:
             f = self.sched.facts()
@@ -188,8 +189,22 @@ class Engine:
                            self.ecfg.burst_queue_cap, self.ecfg.max_delay_passes)
             cap = prefill_budget([r[6] for r in rows], self.ecfg.chunked_prefill, min_tokens=min(
                 2048, self.ecfg.chunked_prefill), page=self.ecfg.page_size)
-            self.dp_log.append((hold, cap))
-            self.step(hold=hold, chunk_cap=cap)
+            park = False
+            if self.ecfg.dp_pace_steps > 0:
+                # pacing: park lone continuing chunked prefills for a bounded number of passes while other ranks
+                # only decode (every rank takes the same decision from the same rows)
+                action, pace_streak = pace_decide([r[0] > 0 for r in rows], [r[4] > 0 for r in rows],
+                                                  [r[1] for r in rows], [r[0] for r in rows], pace_streak,
+                                                  steps=self.ecfg.dp_pace_steps)
+                park = action == "park"
+            if self.ecfg.dp_skew_floor > 0:
+                # skew: a rank extending while the others extend less takes at most max(floor, their largest)
+                ext = [min(r[6], self.ecfg.chunked_prefill) if (r[4] or (r[0] and not hold)) else 0 for r in rows]
+                sk = skew_chunk_cap(ext[rank], ext[:rank] + ext[rank + 1:], floor=self.ecfg.dp_skew_floor,
+                                    page=self.ecfg.page_size)
+                cap = min(c for c in (cap, sk) if c > 0) if (cap or sk) else 0
+            self.dp_log.append((hold, cap, park))
+            self.step(hold=hold, chunk_cap=cap, park=park)
             delayed = delayed + 1 if hold else 0
         if route:
             return {i: r.output for i, r in reqs.items()}

@@ -105,7 +105,9 @@ class GQARunner:
         if tp > 1 and ecfg.tp_qar and self.device.type == "cuda":
             # FP8 two-shot all-reduce (csrc/qar.cu) as the model's all-reduce; the norms run as their own kernels
             from ..parallel.qar import QuantAllReduce
-            rows = max(ecfg.chunked_prefill, 4 * max(ecfg.graph_sizes() + [ecfg.max_running]))
+            # a packed prefill batch pads every segment to a multiple of its query group (<= 16 tokens)
+            rows = max(ecfg.chunked_prefill, 4 * max(ecfg.graph_sizes() + [ecfg.max_running])) + \
+                16 * (ecfg.max_running + 1)
             self.qar = QuantAllReduce(tp_rank, tp, rows, cfg.hidden, self.device)
             for m in (self.model, self.draft):
                 if m is not None:

@@ -102,10 +102,16 @@ class Scheduler:
             self.on_admit(r)
         return r
 
-    def schedule(self, hold: Optional[bool] = None, chunk_cap: int = 0) -> Optional[Batch]:
+    def schedule(self, hold: Optional[bool] = None, chunk_cap: int = 0, park: bool = False) -> Optional[Batch]:
         """hold: the decode-burst decision taken elsewhere (data-parallel ranks decide together, `burst.dp_hold`);
-        None = this scheduler's own rule.  chunk_cap: prefill tokens this pass may take (0 = the chunk size)."""
-        # an unfinished chunked prefill always continues; otherwise admission follows the decode-burst rule
+        None = this scheduler's own rule.  chunk_cap: prefill tokens this pass may take (0 = the chunk size).
+        park: the data-parallel pacing decision to park a continuing chunked prefill for this pass (the running
+        requests decode instead; `dp_policy.pace_decide`, bounded by its step count)."""
+        if park and self.prefilling is not None and self.running:
+            self.streak = next_streak(self.burst, self.streak, False)
+            self.last_was_extend = False
+            return Batch("decode", [Segment(r, r.kv_len, [r.pending], True) for r in self.running])
+        # an unfinished chunked prefill otherwise always continues; admission follows the decode-burst rule
         if self.prefilling is None:
             if hold is None:
                 hold = hold_prefill(self.burst, self.streak, self.last_was_extend, bool(self.running))

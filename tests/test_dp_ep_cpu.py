@@ -106,4 +106,46 @@ def test_dp_policies_in_the_serving_loop():
     assert set(got[0][0]).isdisjoint(got[1][0]) and got[0][0] and got[1][0]
     assert all(served[i] == ref[i] for i in served), (served, ref)
     assert got[0][1] == got[1][1]                     # identical joint decisions on both ranks
-    assert any(h for h, _ in got[0][1])               # decode bursts held prefill on some passes
+    assert any(h for h, *_ in got[0][1])              # decode bursts held prefill on some passes
+
+
+PACE_SPLIT = {0: [[(3 * j + 1) % 500 + 1 for j in range(20)], [(7 * j + 2) % 500 + 1 for j in range(200)]],
+              1: [[(5 * j + 3) % 500 + 1 for j in range(20)], [(11 * j + 4) % 500 + 1 for j in range(30)]]}
+
+
+def _pace_worker(rank: int, port: int, q):
+    """generate_dp with pacing (park a lone continuing chunked prefill for up to 2 passes while the other rank only
+    decodes) and the skew chunk cap on."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2")
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    try:
+        ecfg = EngineConfig(model="tiny_mla", device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=32,
+                            cuda_graphs=False, ep=2, prefix_cache=False, dp_pace_steps=2, dp_skew_floor=64)
+        eng = Engine(ecfg, model_config("tiny_mla"), max_seq=256, ep_rank=rank, ep_group=dist.group.WORLD)
+        outs = eng.generate_dp(PACE_SPLIT[rank], SamplingParams(max_new_tokens=6))
+        q.put((rank, outs, eng.dp_log))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dp_pacing_and_skew_cap_in_the_serving_loop():
+    """Pacing parks rank 0's long chunked prefill on some passes (its running request decodes instead) and the
+    outputs still equal the single-process engine's: the policies move work between passes, never change it."""
+    prompts = PACE_SPLIT[0] + PACE_SPLIT[1]
+    ref = _engine(1, 0).generate(prompts, SamplingParams(max_new_tokens=6))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_pace_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        rank, outs, log = q.get(timeout=600)
+        got[rank] = (outs, log)
+    for p in procs:
+        p.join(timeout=120)
+    assert got[0][0] == ref[:2] and got[1][0] == ref[2:], (got, ref)
+    assert [p for *_, p in got[0][1]] == [p for *_, p in got[1][1]]    # one pacing decision per pass, all ranks
+    parks = sum(p for *_, p in got[0][1])
+    assert 1 <= parks, got[0][1]

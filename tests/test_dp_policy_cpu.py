@@ -79,3 +79,21 @@ def test_router_piggyback_round_trip():
     s2, i2, w2 = MOE.piggyback_unpack(packed, 56, 9, 8)
     assert torch.equal(s2, sc) and torch.equal(i2, ids) and torch.equal(w2, w)
     assert torch.all(packed[:, 56 + 8] == -1)
+
+
+def test_scheduler_park_defers_a_continuing_prefill():
+    """park=True (the pacing decision): a request part-way through its chunked prefill waits one pass while the
+    running requests decode; the next pass resumes the prefill where it stopped."""
+    from inference_optimizations_b200.engine.scheduler import SamplingParams, Scheduler
+    s = Scheduler(max_running=4, chunked_prefill=16)
+    a = s.new_request(list(range(1, 9)), SamplingParams(max_new_tokens=4))
+    b = s.new_request(list(range(1, 41)), SamplingParams(max_new_tokens=4))
+    first = s.schedule()
+    assert first.kind == "prefill" and [len(x.tokens) for x in first.segments] == [8, 8]
+    s.commit_prefill(first, {a.rid: 7})
+    assert s.prefilling is b and b.prefilled == 8
+    parked = s.schedule(park=True)
+    assert parked.kind == "decode" and [x.req for x in parked.segments] == [a] and b.prefilled == 8
+    s.commit_decode({a.rid: [9]})
+    resumed = s.schedule()
+    assert resumed.kind == "prefill" and resumed.segments[0].req is b and resumed.segments[0].start == 8
