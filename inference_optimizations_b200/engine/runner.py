@@ -311,7 +311,17 @@ class GQARunner:
 
     def split_layers(self, sp: dict, count: int) -> bool:
         """Enqueue layers [index, index + count) of the split on the current stream; after the last layer also the
-        logits / argmax of the rows that want a token.  Returns True when the split's device work is all enqueued."""
+        logits / argmax of the rows that want a token.  Returns True when the split's device work is all enqueued.
+        Its launches use the lane's own split-K scratch (`moe_gemm.LANE`): decode may run concurrently on another
+        stream with a batch of the same size."""
+        from ..ops import moe_gemm as MG
+        MG.LANE[0] = 1
+        try:
+            return self._split_layers(sp, count)
+        finally:
+            MG.LANE[0] = 0
+
+    def _split_layers(self, sp: dict, count: int) -> bool:
         n_layers = len(self.model.layers)
         lo = sp["index"]
         hi = min(lo + max(1, count), n_layers)

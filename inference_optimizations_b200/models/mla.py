@@ -135,7 +135,8 @@ class MLAKVCache:
         hold no memory between steps)."""
         if self.device.type != "cuda" or t > 256:
             return None, None
-        ik, mk = (t, max_ctx), (t, topk)
+        from ..ops.moe_gemm import LANE
+        ik, mk = (t, max_ctx, LANE[0]), (t, topk, LANE[0])
         if ik not in self.idx_ws or mk not in self.mla_ws:
             if torch.cuda.is_current_stream_capturing():
                 return self.idx_ws.get(ik), self.mla_ws.get(mk)
@@ -178,7 +179,9 @@ class MLAModel:
         if c.num_experts % max(ep_world, dcp_world) or c.num_heads % dcp_world or c.dense_ffn % (128 * dcp_world):
             raise ValueError("experts / heads / dense FFN columns must divide evenly over the ranks")
         self.ep_rank, self.ep_world = ep_rank, ep_world
-        self.dcp_rank, self.dcp_world = dcp_rank, dcp_world
+        # a rank index only means something with context parallelism on (with dcp_world 1 every rank holds the
+        # whole model: shared expert, all heads, all FFN columns)
+        self.dcp_rank, self.dcp_world = (dcp_rank if dcp_world > 1 else 0), dcp_world
         self.dcp = None                                  # attach_dcp(): merge + reduce communicators
         self.dcp_push = None                             # push-form reduce for the row-parallel W_o (CUDA)
         pr, pw = (dcp_rank, dcp_world) if dcp_world > 1 else (ep_rank, ep_world)

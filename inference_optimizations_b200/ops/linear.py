@@ -66,7 +66,7 @@ def _splitk_gemm(lin, x, xs, out, t: int, kc: int, kind: int, push=None) -> None
                 mode=MODE_F32_SPLIT if f32 else 0, src_div=1, num_ctas=lin.num_ctas, kind=kind,
                 split_rows=t if f32 else 0, static_index=static, **pk)
         return
-    key = (t, ks)
+    key = (t, ks, MG.LANE[0])
     if key not in lin._parts:
         # fp32 partials and the per-tile counters of the folded reduction (zero between launches: the split that
         # completes a tile re-arms its counter)
@@ -145,7 +145,7 @@ class DenseLinear:
         ks = FORCE["ks"] or split_k(n_tiles, t, nt, kc, self.num_ctas, g=self.g)
         if ks == 1 or t == 0:
             return self(x, out_f32=True), 1
-        key = (t, ks)
+        key = (t, ks, MG.LANE[0])
         if key not in self._parts:
             self._parts[key] = (torch.empty(ks * t, self.N, dtype=torch.float32, device=x.device),
                                 torch.zeros(n_tiles * -(-t // nt), dtype=torch.int32, device=x.device))

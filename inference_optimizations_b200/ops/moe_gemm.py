@@ -194,6 +194,10 @@ def gemm(wpack, x, x_scale, off, pairs, out, status, *, n_tiles: int, kc: int, g
 
 TRACE: list = [None]
 PDL: list = [True]
+# Which set of cached scratch buffers (split-K partials, per-step workspaces) the launches use: 0 by default, 1 while
+# the split-prefill lane enqueues its layers (`engine/pdmux.py`) -- that lane runs concurrently with decode on another
+# stream, so the two must never share a scratch buffer of the same shape.
+LANE: list = [0]
 
 
 def static_index_tensors(make) -> tuple:
@@ -414,7 +418,7 @@ class BlockScaledExperts:
             # fp32 partials are summed in split order by one reduction kernel straight into the output (one pair
             # per token, weight 1: no combine).  The split depends on the weight shape only, so every batch of up to
             # 64 tokens rounds the same way (data-parallel ranks agree with one GPU).
-            key = (P, ks)
+            key = (P, ks, LANE[0])
             if key not in self._parts:
                 self._parts[key] = torch.empty(ks * P, self.H, dtype=torch.float32, device=dev)
             part = self._parts[key]

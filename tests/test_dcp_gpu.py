@@ -122,13 +122,9 @@ MODEL_WORKER = textwrap.dedent("""
     print(f"rank {rank} cos median {cos.median().item():.5f} min {cos.min().item():.5f} same {same} {outs}",
           flush=True)
     # The context-parallel model sums bf16 partials (row-parallel W_UV / W_o, split FFN) where the one-GPU model
-    # accumulates once, and each rank's sparse attention rounds P to E4M3 against its own running max.  With bf16
-    # weights these differences stay at bf16 level (tight bound).  With FP8 weights every activation is re-quantized
-    # to E4M3 (3 mantissa bits) at each projection, so a one-ulp bf16 difference upstream can move a value across an
-    # E4M3 rounding boundary and the random-init stack amplifies it: a looser bound there.
-    # (measured: bf16 median 0.9995, min 0.943 -- the minimum is a token whose near-tie random-init expert choice
-    # flipped between the two rounding orders; FP8 median ~0.98)
-    med, lo = (0.995, 0.9) if wdt == "bf16" else (0.97, 0.85)
+    # accumulates once, and each rank's sparse attention rounds P to E4M3 against its own running max; a random-init
+    # router can flip a near-tie expert on a rare token (measured with bf16 weights: median 0.9995, minimum 0.943).
+    med, lo = 0.99, 0.9
     ok = cos.median().item() > med and cos.min().item() > lo and same
     dist.barrier()
     del eng

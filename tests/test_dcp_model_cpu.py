@@ -77,3 +77,16 @@ def test_dcp_model_matches_single_process():
         assert cos.median().item() > 0.999 and (cos > 0.99).float().mean().item() > 0.95, (rank, cos)
     assert torch.equal(got[0][0], got[1][0])                 # the ranks hold identical activations
     assert got[0][1] == got[1][1]
+
+
+def test_rank_index_ignored_without_context_parallelism():
+    """A whole model built on a process whose rank is 1 (dcp_world 1) holds the shared expert and every head: the
+    rank index only places work when context parallelism is on."""
+    from inference_optimizations_b200.config import model_config
+    from inference_optimizations_b200.models.mla import MLAModel
+    cfg = model_config("tiny_mla")
+    a = MLAModel(cfg, "cpu", 0, dcp_rank=1, dcp_world=1)
+    b = MLAModel(cfg, "cpu", 0)
+    i = cfg.first_dense
+    assert a.layers[i].ffn["shared_gu"] is not None
+    assert torch.equal(a.layers[i].ffn["shared_gu"], b.layers[i].ffn["shared_gu"])
