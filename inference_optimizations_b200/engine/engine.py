@@ -49,9 +49,9 @@ class Engine:
         if getattr(ecfg, "pdmux", False):
             # the lanes split a GQA prefill by layer ranges on one rank; refuse the combinations that would only fail
             # at the first prefill (inside split_begin), e.g. in the middle of an HTTP serving loop
-            bad = [why for cond, why in ((not isinstance(self.runner, GQARunner), "a non-GQA model family"),
-                                         (bool(ecfg.spec), "speculative decoding"), (tp > 1, "tp > 1"),
-                                         (max(1, ecfg.ep) > 1, "expert parallelism"))
+            bad = [why for cond, why in ((bool(ecfg.spec), "speculative decoding"), (tp > 1, "tp > 1"),
+                                         (max(1, ecfg.ep) > 1, "expert parallelism"),
+                                         (max(1, ecfg.dcp) > 1, "context parallelism"))
                    if cond]
             if bad:
                 raise ValueError("EngineConfig(pdmux=True) does not support " + ", ".join(bad))

@@ -218,6 +218,56 @@ class MLARunner:
                 k += 1
         return res
 
+    # ------------------------------------------------------------------------------------------ split prefill
+    # The prefill lane of the SM-partitioned lanes (`engine/pdmux.py`): a prefill batch runs by layer ranges on its
+    # own stream while decode graphs replay on the decode lane.  Its launches use the lane's own scratch buffers
+    # (`moe_gemm.LANE`), so a chunk the size of a decode batch never shares one with it.
+    def split_begin(self, batch: Batch) -> dict:
+        if self.spec or self.ep_world > 1 or self.dcp_world > 1:
+            raise NotImplementedError("split prefill lanes: speculation, expert / context parallelism not supported")
+        for s in batch.segments:
+            if s.req.rid not in self.pages:
+                self.attach(s.req)
+        st, rows = self._step(batch.segments)
+        return {"batch": batch, "st": st, "rows": rows, "x": None, "h": None, "x8": None, "index": 0}
+
+    def split_layers(self, sp: dict, count: int) -> bool:
+        """Enqueue target layers [index, index + count) of the split on the current stream; after the last layer also
+        the LM head and argmax of the rows that want a token (copied to pinned host memory without a wait).  Returns
+        True when the split's device work is all enqueued."""
+        from ..ops import moe_gemm as MG
+        MG.LANE[0] = 1
+        try:
+            n = self.model.n_target
+            lo = sp["index"]
+            hi = min(lo + max(1, count), n)
+            sp["x"], sp["h"], sp["x8"] = self.model.forward_layers(sp["st"], self.kv, lo, hi, sp["x"], sp["h"],
+                                                                   sp["x8"])
+            sp["index"] = hi
+            if hi < n:
+                return False
+            if sp["rows"]:
+                rows = torch.tensor(sp["rows"], dtype=torch.long)
+                rows = rows.pin_memory().to(self.device, non_blocking=True) if self.device.type == "cuda" else rows
+                ids = B.argmax(self.model.logits(sp["x"][rows]))
+                host = torch.empty(ids.shape, dtype=ids.dtype, pin_memory=self.device.type == "cuda")
+                host.copy_(ids, non_blocking=True)
+                sp["out_host"] = host
+            sp["x"] = sp["h"] = sp["x8"] = None
+            return True
+        finally:
+            MG.LANE[0] = 0
+
+    def split_finish(self, sp: dict) -> dict:
+        """Host side of a finished split, after its stream's work completed: rid -> first generated token."""
+        res, k = {}, 0
+        out = sp.get("out_host")
+        for s in sp["batch"].segments:
+            if s.logits:
+                res[s.req.rid] = int(out[k])
+                k += 1
+        return res
+
     # ------------------------------------------------------------------------------------------ MTP speculation
     # Depth-1 multi-token prediction (the DeepSeek-V3 MTP draft; the reference's MLA draft models,
     # `speculative/k3-mla-draft`, and frozen-KV MTP no-sync hooks): the draft layer keeps its own KV for every
@@ -396,6 +446,10 @@ class MLARunner:
             return self.model.logits(self.model.forward(st, self.kv)).float().cpu()
         finally:
             self.detach(r)
+
+    def has_graph(self, n: int) -> bool:
+        """The decode graph of n's batch bucket is captured."""
+        return self._bucket(n) in self.graphs
 
     def warm_graphs(self, n: int) -> None:
         """Capture the decode graph of the bucket holding n requests (before any timed step).  Under expert

@@ -125,7 +125,8 @@ class _StreamCtx:
 
 
 class PdmuxEngine:
-    """Drives an `Engine` (GQA family, tp = 1, no speculation) with the prefill and decode lanes.
+    """Drives an `Engine` (GQA or MLA family, tp = 1, no speculation, expert or context parallelism) with the
+    prefill and decode lanes.
 
     group: optional CPU (gloo) process group of the data-parallel ranks; every rank then calls `step()` in lockstep
     (`generate` loops until no rank has work)."""
@@ -139,7 +140,8 @@ class PdmuxEngine:
         self.thresholds = tuple(thresholds)
         self.group = group
         self.lanes = Lanes(engine.device, n_groups, divisions)
-        self.num_layers = len(engine.runner.model.layers)
+        model = engine.runner.model
+        self.num_layers = getattr(model, "n_target", len(model.layers))
         self.split: Optional[dict] = None
         self.pending: Optional[dict] = None   # a split whose device work is all enqueued, not yet committed
         self._p_event = None
@@ -205,8 +207,7 @@ class PdmuxEngine:
         out: dict = {}
         if dbatch is not None:
             reqs = [s.req for s in dbatch.segments]
-            if run.device.type == "cuda" and run.ecfg.cuda_graphs and \
-                    ("decode", run._bucket(len(reqs))) not in run.graphs:
+            if run.device.type == "cuda" and run.ecfg.cuda_graphs and not run.has_graph(len(reqs)):
                 run.warm_graphs(len(reqs))
             with _StreamCtx(ds):
                 out = run.decode(reqs)

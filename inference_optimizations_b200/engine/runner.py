@@ -485,6 +485,10 @@ class GQARunner:
         self.graphs[key] = fn
         return fn
 
+    def has_graph(self, n: int) -> bool:
+        """The decode graph of n's batch bucket is captured."""
+        return ("decode", self._bucket(n)) in self.graphs
+
     def warm_graphs(self, n: int) -> None:
         """Capture the decode (and speculative) graphs of n's batch bucket on padding-only inputs (no KV writes, the
         dummy request row), so that capture never lands inside a timed or policy-priced step."""

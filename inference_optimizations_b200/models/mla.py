@@ -721,6 +721,24 @@ class MLAModel:
         """-> final-normed hidden [T, H]."""
         return self.forward_hidden(st, kv)[0]
 
+    def forward_layers(self, st: MLAStep, kv: MLAKVCache, lo: int, hi: int, x: Optional[torch.Tensor],
+                       h: Optional[torch.Tensor], x8=None) -> tuple:
+        """Target layers [lo, hi) of a forward split by layer ranges (the split prefill of the SM-partitioned lanes).
+        x: the normed input of layer lo (None at lo = 0: embedding and first norm here); h: the residual stream.
+        x8: the block-quantized copy of x the previous range's last norm wrote for layer lo's FP8 projection.
+        -> (x, h, x8) after layer hi - 1 (x is the final-normed hidden after the last layer)."""
+        n = self.n_target
+        if lo == 0:
+            h = B.embed(st.ids, self.embed)
+            x = self._norm_out(h, self.layers[0].n_in, None, 0)
+        else:
+            self._x8 = x8
+        for i in range(lo, hi):
+            nxt = self.layers[i + 1].n_in if i + 1 < n else self.final_norm
+            x = self.layer_forward(i, h, x, st, kv, nxt)
+        x8, self._x8 = self._x8, None
+        return x, h, x8
+
     def forward_hidden(self, st: MLAStep, kv: MLAKVCache) -> tuple[torch.Tensor, torch.Tensor]:
         """-> (final-normed hidden [T, H], residual stream after the last target layer [T, H])."""
         h = B.embed(st.ids, self.embed)

@@ -106,3 +106,23 @@ def test_engine_config_flag():
     eng = Engine(ecfg, max_seq=256)
     assert eng.generate(PROMPTS, params) == ref
     assert eng.pdmux.log and not eng.has_work()
+
+
+def test_pdmux_mla_family_matches_plain_engine():
+    """The MLA family through the lanes: prefill split by layer ranges beside decode steps gives the plain engine's
+    tokens, the split's last range ends with the LM head, pages are released."""
+    from inference_optimizations_b200.config import model_config
+
+    def mla_engine():
+        ecfg = EngineConfig(model="tiny_mla", device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=40,
+                            cuda_graphs=False, prefix_cache=False)
+        return Engine(ecfg, model_config("tiny_mla"), max_seq=256)
+    params = SamplingParams(max_new_tokens=6)
+    ref = mla_engine().generate(PROMPTS, params)
+    pm = PdmuxEngine(mla_engine(), token_budget=40)          # 40-token chunks -> one layer per iteration
+    outs = pm.generate(PROMPTS, params)
+    assert outs == ref
+    both = [e for e in pm.log if e[1] is not None and e[2] > 0]
+    assert both
+    assert any(e[1][1] - e[1][0] == 1 for e in pm.log if e[1] is not None)
+    assert pm.engine.runner.kv.alloc.used == 0

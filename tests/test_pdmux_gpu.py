@@ -66,3 +66,20 @@ def test_pdmux_five_groups():
     used = {g for g, s, n in pm.log if s is not None and n > 0}
     assert used == {3}
     assert pm.lanes.sms[3][1] > pm.lanes.sms[3][0]
+
+
+def test_pdmux_mla_family_matches_plain_engine():
+    """The DSA-MoE family (FP8 block-scaled projections and experts, NVFP4 latent KV) through the lanes: prefill split
+    by layer ranges on the prefill partition beside CUDA-graph decode on the decode partition gives the plain
+    engine's tokens; the split's launches use their own scratch buffers (a chunk of a decode batch's size included)."""
+    from inference_optimizations_b200.config import model_config
+    cfg = model_config("tiny_mla", expert_ffn=256, dense_ffn=512, weight_dtype="fp8", expert_dtype="fp8")
+    params = SamplingParams(max_new_tokens=8, ignore_eos=True)
+    ecfg = EngineConfig(model="tiny_mla", device="cuda:0", kv_dtype="nvfp4", max_running=4, chunked_prefill=64,
+                        graph_batch_sizes="1,2,4", prefix_cache=False)
+    ref = Engine(ecfg, cfg, max_seq=1024).generate(PROMPTS, params)
+    pm = PdmuxEngine(Engine(ecfg, cfg, max_seq=1024), token_budget=64)     # one layer per iteration of a chunk
+    outs = pm.generate(PROMPTS, params)
+    assert outs == ref
+    assert any(g == 1 and s is not None and n > 0 for g, s, n in pm.log)
+    assert pm.engine.runner.kv.alloc.used == 0
