@@ -260,18 +260,10 @@ __global__ void __launch_bounds__(kKThreads) indexer_topk_kernel(const IndexerAr
     for (int b = threadIdx.x; b < 4096; b += kKThreads) hist[b] = 0;
     __syncthreads();
     if constexpr (REG) {
-      // warp-aggregated counts: scores crowd into few top-12-bit bins (one exponent range), so lanes hitting the
-      // same bin add once through their lowest lane instead of serialising on one shared-memory address
+      // (warp-aggregated counts through __match_any_sync measured slower here: 12.6 -> 19.4 us per call at 8 tokens)
 #pragma unroll
-      for (int j = 0; j < kRegKeys; ++j) {
-        const bool in = i0 + j < i1 && (keys[j] & mask) == prefix;
-        const unsigned act = __ballot_sync(0xffffffffu, in);
-        if (in) {
-          const int bin = (keys[j] >> sh) & (nb - 1);
-          const unsigned same = __match_any_sync(act, bin);
-          if ((threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&hist[bin], __popc(same));
-        }
-      }
+      for (int j = 0; j < kRegKeys; ++j)
+        if (i0 + j < i1 && (keys[j] & mask) == prefix) atomicAdd(&hist[(keys[j] >> sh) & (nb - 1)], 1);
     } else {
       for (int i = threadIdx.x; i < L; i += kKThreads) {
         const uint32_t u = order_key(sc[i]);
