@@ -174,6 +174,10 @@ class EngineConfig:
     # KV pool
     page_size: int = 64
     kv_dtype: str = "nvfp4"              # "nvfp4" | "fp8" | "bf16" (GQA pools); MLA: "nvfp4" (352 B) | "fp8" (576 B)
+                                         # | "kvmix" (FP8 and NVFP4 rows in one page space, per-request placement)
+    kvmix_threshold: int = 262144        # kvmix: requests whose length reaches this live in NVFP4 (promoted when
+                                         # they grow past it), shorter ones in FP8
+    kvmix_fp8_share: float = 0.5         # kvmix: share of the pool's latent bytes given to FP8 pages
     max_running: int = 64
     max_total_tokens: int = 0            # KV pool cap in tokens; 0 = the requests' need, bounded by free memory
     mem_fraction: float = 0.90           # share of the device memory free at boot (less a reserve) the pool may take

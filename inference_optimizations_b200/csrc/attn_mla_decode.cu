@@ -208,6 +208,7 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
   const int ntiles = min(ntiles_all, tile0 + a.tiles_per_split) - tile0;
   const int warp = warp_id(), lane = lane_id();
   const int* idx_row = a.idx + static_cast<size_t>(t) * a.idx_stride;
+  if (a.tok_sel && a.tok_sel[t] != a.sel) return;        // this token's rows live in the other pool's launch
 
   if (ntiles <= 0) {  // empty split: an empty partial
     if (a.num_splits > 1 && half == 0 && threadIdx.x < a.H)
@@ -416,8 +417,10 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
     auto row_id = [&](int j) -> int {
       const int p = (tile0 + j) * kMTile + trow;
       if (!MLA_IN_RANGE(p >= 0, 4)) return -1;
-      const int id = (j < ntiles && p < a.topk) ? idx_row[p] : -1;
-      if (id >= a.pool_rows) {           // a row outside the pool: treated as masked, reported once
+      const int id0 = (j < ntiles && p < a.topk) ? idx_row[p] : -1;
+      if (id0 < 0) return -1;
+      const int id = id0 - a.row_lo;
+      if (id < 0 || id >= a.pool_rows) {  // a row outside the pool: treated as masked, reported once
         record_status(a.status, kBadIndex);
         return -1;
       }
@@ -577,8 +580,8 @@ __global__ void __launch_bounds__(kMThreads, 1) mla_decode_kernel(const MlaDecod
       // ------------------------------------------------------------ warm L2 with the split's rows, in order
       const int p0 = tile0 * kMTile, p1 = min(a.topk, (tile0 + ntiles) * kMTile);
       for (int p = p0 + lane; p < p1 && !*abort; p += 32) {
-        const int id = idx_row[p];
-        if (id >= 0 && id < a.pool_rows) prefetch_l2(a.pool + static_cast<size_t>(id) * RB, RB);
+        const int id = idx_row[p] - a.row_lo;
+        if (idx_row[p] >= 0 && id >= 0 && id < a.pool_rows) prefetch_l2(a.pool + static_cast<size_t>(id) * RB, RB);
       }
     }
   }
@@ -636,6 +639,7 @@ __global__ void __launch_bounds__(128) mla_q_quant_kernel(const __nv_bfloat16* _
 __global__ void __launch_bounds__(128) mla_combine_kernel(const MlaDecodeArgs a) {
   griddep_launch();
   const int row = blockIdx.x;  // t * H + h
+  if (a.tok_sel && a.tok_sel[row / a.H] != a.sel) return;
   const size_t plane = static_cast<size_t>(a.T) * a.H;
   float m = -INFINITY;
   for (int s = 0; s < a.num_splits; ++s) m = fmaxf(m, a.lse_part[s * plane + row]);

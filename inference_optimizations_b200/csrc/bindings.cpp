@@ -239,7 +239,8 @@ void gqa_decode(const at::Tensor& q, const at::Tensor& pool, const at::Tensor& p
 void mla_decode(c10::optional<at::Tensor> q, at::Tensor q8, at::Tensor q_scale, const at::Tensor& pool,
                 const at::Tensor& idx, at::Tensor out, c10::optional<at::Tensor> lse, at::Tensor o_part,
                 at::Tensor lse_part, at::Tensor status, int64_t fmt, int64_t tiles_per_split, int64_t num_splits,
-                double sm_scale, c10::optional<at::Tensor> trace) {
+                double sm_scale, c10::optional<at::Tensor> trace, c10::optional<at::Tensor> tok_sel, int64_t sel,
+                int64_t row_lo) {
   req(q8, at::kByte, "q8");
   req(q_scale, at::kFloat, "q_scale");
   req(pool, at::kByte, "pool");
@@ -284,6 +285,13 @@ void mla_decode(c10::optional<at::Tensor> q, at::Tensor q8, at::Tensor q_scale, 
   a.idx_stride = idx.stride(0);
   a.fmt = fmt;
   a.pool_rows = static_cast<int>(std::min<int64_t>(pool.size(0), INT32_MAX));
+  if (tok_sel.has_value()) {
+    req(*tok_sel, at::kInt, "tok_sel");
+    TORCH_CHECK(tok_sel->numel() >= T && row_lo >= 0, "tok_sel [T], row_lo >= 0");
+    a.tok_sel = tok_sel->data_ptr<int>();
+    a.sel = static_cast<int>(sel);
+    a.row_lo = static_cast<int>(row_lo);
+  }
   a.tiles_per_split = tiles_per_split;
   a.num_splits = num_splits;
   a.sm_scale = sm_scale;
@@ -816,7 +824,8 @@ void mla_prep_kv(const at::Tensor& ya, const at::Tensor& q_norm, const at::Tenso
                  const at::Tensor& ik_b, const at::Tensor& rope, const at::Tensor& pos, const at::Tensor& slot,
                  at::Tensor qa_out, at::Tensor latent_pool, at::Tensor index_pool, at::Tensor iw_out, double iw_scale,
                  int64_t q_lora, int64_t Hi, double eps, const c10::optional<at::Tensor>& lat_slot,
-                 const c10::optional<at::Tensor>& qa_q, const c10::optional<at::Tensor>& qa_s) {
+                 const c10::optional<at::Tensor>& qa_q, const c10::optional<at::Tensor>& qa_s,
+                 const c10::optional<at::Tensor>& latent_pool2, int64_t split_slot) {
   req(ya, at::kBFloat16, "ya");
   req(rope, at::kFloat, "rope");
   req(pos, at::kInt, "pos");
@@ -861,6 +870,15 @@ void mla_prep_kv(const at::Tensor& ya, const at::Tensor& q_norm, const at::Tenso
   a.qa_out = qa_out.data_ptr();
   a.latent_pool = latent_pool.data_ptr<uint8_t>();
   a.latent_fmt = latent_pool.size(1) == 352 ? iob::kKvNvfp4 : iob::kKvFp8;
+  if (latent_pool2.has_value()) {
+    req(*latent_pool2, at::kByte, "latent_pool2");
+    TORCH_CHECK(latent_pool2->dim() == 2 && (latent_pool2->size(1) == 352 || latent_pool2->size(1) == 576) &&
+                    latent_pool2->is_contiguous() && split_slot >= 0,
+                "latent_pool2 [slots, 352 | 576]");
+    a.latent_pool2 = latent_pool2->data_ptr<uint8_t>();
+    a.latent_fmt2 = latent_pool2->size(1) == 352 ? iob::kKvNvfp4 : iob::kKvFp8;
+    a.split_slot = static_cast<int>(split_slot);
+  }
   a.index_pool = index_pool.data_ptr<uint8_t>();
   a.iw_out = iw_out.data_ptr<float>();
   a.iw_scale = static_cast<float>(iw_scale);

@@ -126,6 +126,11 @@ struct MlaDecodeArgs {
   int T, H, topk, idx_stride, fmt;
   int pool_rows;           // rows in the pool: an index outside [0, pool_rows) is treated as masked (status kBadIndex)
   int tiles_per_split, num_splits;  // 128-row tiles of the top-k list per split
+  // Mixed-format pools (one launch per pool format over one page-id space): index i of a token addresses pool row
+  // i - row_lo; tokens with tok_sel[t] != sel are skipped by this launch (their rows live in the other pool and
+  // another launch writes their output).  tok_sel null: every token, row_lo 0.
+  const int* tok_sel;
+  int sel, row_lo;
   float sm_scale;
   long long* trace;        // optional [40 events x 64 tiles] clock64 timeline of CTA (0, 0, 0), else null
 };
@@ -264,6 +269,8 @@ struct MlaPrepArgs {
   uint32_t* qa_s;             // FP8 block-scaled input of the next projection; null = not written)
   uint8_t* latent_pool;       // [slots, 352] NVFP4 or [slots, 576] E4M3
   int latent_fmt;
+  uint8_t* latent_pool2;      // optional second pool (mixed-format page space): latent slots >= split_slot are row
+  int latent_fmt2, split_slot;  // slot - split_slot of this pool, in its format; null = one pool
   uint8_t* index_pool;        // [pages, 64 * 132]
   float* iw_out;              // fp32 [T, Hi]: w_i * iw_scale
   float iw_scale;

@@ -114,9 +114,14 @@ __global__ void __launch_bounds__(256) mla_prep_kv_kernel(const MlaPrepArgs a) {
     const float x1 = bfv(kv, 512 + lane), x2 = bfv(kv, 512 + 32 + lane);
     const float c = cs[lane], s = cs[32 + lane];
     const float r1 = rbf(x1 * c - x2 * s), r2 = rbf(x2 * c + x1 * s);
+    // mixed-format page space: slots from split_slot on live in the second pool, in its format
+    const bool second = a.latent_pool2 != nullptr && lat_slot >= a.split_slot;
+    const int fmt = second ? a.latent_fmt2 : a.latent_fmt;
+    uint8_t* const pool = second ? a.latent_pool2 : a.latent_pool;
+    const int lrow = second ? lat_slot - a.split_slot : lat_slot;
     if (lat_slot >= 0) {
-      if (a.latent_fmt == kKvNvfp4) {
-        uint8_t* row = a.latent_pool + static_cast<size_t>(lat_slot) * 352;
+      if (fmt == kKvNvfp4) {
+        uint8_t* row = pool + static_cast<size_t>(lrow) * 352;
         float amax = 0.f;
 #pragma unroll
         for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
@@ -132,7 +137,7 @@ __global__ void __launch_bounds__(256) mla_prep_kv_kernel(const MlaPrepArgs a) {
         row[288 + lane] = float_to_e4m3(r1);
         row[288 + 32 + lane] = float_to_e4m3(r2);
       } else {
-        uint8_t* row = a.latent_pool + static_cast<size_t>(lat_slot) * 576;
+        uint8_t* row = pool + static_cast<size_t>(lrow) * 576;
         uint32_t wq[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -231,6 +236,8 @@ __global__ void __launch_bounds__(256) mla_prep_q_kernel(const MlaPrepArgs a) {
 
 cudaError_t mla_prep_kv(const MlaPrepArgs& a, cudaStream_t s) {
   if (a.T == 0) return cudaSuccess;
+  if (a.latent_pool2 && ((a.latent_fmt2 != kKvNvfp4 && a.latent_fmt2 != kKvFp8) || a.split_slot < 0))
+    return cudaErrorInvalidValue;
   if (a.q_lora <= 0 || a.q_lora > 128 * kQaMax || a.Hi <= 0 || (a.latent_fmt != kKvNvfp4 && a.latent_fmt != kKvFp8) || !a.ya || !a.rope ||
       !a.pos || !a.slot || !a.qa_out || !a.latent_pool || !a.index_pool || !a.iw_out ||
       (a.qa_q && (!a.qa_s || a.q_lora % 128)))

@@ -16,6 +16,8 @@ from ..config import EngineConfig, MLAMoEConfig
 from ..kv.allocator import RequestPages
 from ..models.mla import MLAKVCache, MLAModel, MLAStep
 from ..ops import basic as B
+from ..ops import formats as M_FMT
+from ..ops import kvcache as K_OPS
 from ..ops.kvcache import FMT_FP8, FMT_NVFP4
 from .scheduler import Batch, Request, SamplingParams, Segment
 from ..ops.formats import INDEX_ROW_BYTES
@@ -72,13 +74,29 @@ class MLARunner:
             # tokens per exchange: a decode step of every running request (with its draft), or a prefill piece
             self.ep_T_max = max(2 * ecfg.max_running, min(ecfg.chunked_prefill, 1024))
             self.model.attach_ep(ep_group, self.ep_T_max)
+        self.mixed = ecfg.kv_dtype == "kvmix"
+        if self.mixed and (self.dcp_world > 1 or ecfg.prefix_cache or kv_storage is not None):
+            raise NotImplementedError("kvmix pools run without context parallelism, the prefix cache or placed pools")
         fmt = FMT_NVFP4 if ecfg.kv_dtype == "nvfp4" else FMT_FP8
         self.max_running = ecfg.max_running
         per_req = (max_seq + 64 + 63) // 64 + 1
+        n_layers = cfg.num_layers + int(self.spec)
         pages = pool_pages(ecfg, self.max_running * per_req + 2,
-                           (cfg.num_layers + int(self.spec)) * 64 * (M_ROW_BYTES[fmt] + INDEX_ROW_BYTES), self.device)
+                           n_layers * 64 * (M_ROW_BYTES[fmt] + INDEX_ROW_BYTES), self.device)
+        mix = None
+        if self.mixed:
+            # the byte budget of `pages` FP8 pages, split between FP8 and NVFP4 pages by kvmix_fp8_share
+            b8 = n_layers * 64 * (M_ROW_BYTES[FMT_FP8] + INDEX_ROW_BYTES)
+            b4 = n_layers * 64 * (M_ROW_BYTES[FMT_NVFP4] + INDEX_ROW_BYTES)
+            budget = pages * b8
+            p8 = max(2, int(budget * ecfg.kvmix_fp8_share) // b8)
+            p4 = max(1, int(budget * (1 - ecfg.kvmix_fp8_share)) // b4)
+            mix, pages = (p8, p4, ecfg.kvmix_threshold), p8 + p4
         self.kv = MLAKVCache(cfg, self.device, fmt, self.max_running + 1, per_req, pages,
-                             extra_layers=1 if self.spec else 0, latent_div=self.dcp_world, storage=kv_storage)
+                             extra_layers=1 if self.spec else 0, latent_div=self.dcp_world, storage=kv_storage,
+                             mix=mix)
+        self.placement: dict = {}                     # kvmix: rid -> pool chosen at admission ("fp8" | "nvfp4")
+        self.promotions = 0
         pages = self.kv.pages
         self.pool_tokens = 64 * (pages - 2)           # KV positions the pool holds (the boot-time capacity)
         self.dummy_row = self.max_running
@@ -94,6 +112,8 @@ class MLARunner:
     # ------------------------------------------------------------------------------------------ memory
     def can_admit(self, r: Request) -> bool:
         need = (r.prompt_len + r.params.max_new_tokens + 64) // 64 + 1
+        if self.mixed:
+            return self._place(r, need)
         reserved = sum(max(0, rp.high_pages - len(rp.pages)) for rp in self.pages.values())
         short = need + reserved - self.kv.alloc.free
         if short > 0 and self.prefix_cache is not None:
@@ -101,7 +121,31 @@ class MLARunner:
             short = need + reserved - self.kv.alloc.free
         return short <= 0
 
+    def _place(self, r: Request, need: int) -> bool:
+        """kvmix admission: the request's pool -- NVFP4 when its length reaches the threshold, else FP8 -- or the
+        other pool when the preferred one cannot hold its whole budget (cross-pool fallback); every page of the
+        request then comes from that pool."""
+        space = self.kv.alloc
+        first = space.mix.preferred(r.prompt_len + r.params.max_new_tokens)
+        for fmt in (first, "nvfp4" if first == "fp8" else "fp8"):
+            reserved = sum(max(0, rp.high_pages - len(rp.pages)) for rp in self.pages.values()
+                           if getattr(rp, "fmt", None) == fmt)
+            if space.free_in(fmt) - reserved >= need:
+                if fmt != first:
+                    space.mix.fallbacks += 1
+                self.placement[r.rid] = fmt
+                return True
+        return False
+
     def attach(self, r: Request) -> None:
+        if self.mixed:
+            fmt = self.placement.get(r.rid) or self.kv.alloc.mix.preferred(r.prompt_len + r.params.max_new_tokens)
+            rp = RequestPages(self.kv.alloc.view(fmt), self.kv.table, r.slot)
+            rp.fmt = fmt
+            rp.high_pages = (r.prompt_len + r.params.max_new_tokens + 64) // 64 + 1
+            rp.cached = []
+            self.pages[r.rid] = rp
+            return
         rp = RequestPages(self.kv.alloc, self.kv.table, r.slot)
         rp.high_pages = (r.prompt_len + r.params.max_new_tokens + 64) // 64 + 1
         rp.cached = []
@@ -124,6 +168,7 @@ class MLARunner:
 
     def detach(self, r: Request) -> None:
         rp = self.pages.pop(r.rid, None)
+        self.placement.pop(r.rid, None)
         if rp is None:
             return
         if self.prefix_cache is None:
@@ -162,10 +207,14 @@ class MLARunner:
 
     # ------------------------------------------------------------------------------------------ steps
     def _step(self, segs: list, agreed: bool = False) -> tuple[MLAStep, list]:
-        ids, pos, slot, limit, rix, logit_rows = [], [], [], [], [], []
+        ids, pos, slot, limit, rix, logit_rows, psel = [], [], [], [], [], [], []
+        if self.mixed:
+            self._promote([s.req for s in segs], {s.req.rid: s.start + len(s.tokens) for s in segs})
         for s in segs:
             rp = self.pages[s.req.rid]
             rp.ensure(s.start + len(s.tokens))
+            if self.mixed:
+                psel += [int(rp.fmt == "nvfp4")] * len(s.tokens)
             for j, tok in enumerate(s.tokens):
                 p = s.start + j
                 ids.append(int(tok))
@@ -181,10 +230,50 @@ class MLARunner:
             check_mla_step(ids, pos, slot, limit, rix, self.kv, self.max_running + 1, self.cfg.vocab)
         dev = self.device
         mk = lambda v: torch.tensor(v, dtype=torch.int32).to(dev, non_blocking=True)  # noqa: E731
-        st = MLAStep(mk(ids), mk(pos), mk(slot), mk(limit), mk(rix), self.max_seq + 1)
+        st = MLAStep(mk(ids), mk(pos), mk(slot), mk(limit), mk(rix), self.max_seq + 1,
+                     pool_sel=mk(psel) if self.mixed else None)
         if not agreed:
             self._agree(len(ids))
         return st, logit_rows
+
+    def _promote(self, reqs: list, new_len: dict) -> None:
+        """kvmix promotion: a request in the FP8 pool whose length reaches the threshold moves to NVFP4 -- fresh
+        NVFP4 pages for all its pages, every layer's latent rows re-quantized FP8 -> NVFP4 through the pool writer, its
+        index-key pages copied, the page table re-pointed, the FP8 pages freed (stream-ordered before the step that
+        reads them).  Without NVFP4 room for the request's whole budget it stays in FP8."""
+        space = self.kv.alloc
+        thr = space.mix.threshold
+        for r in reqs:
+            rp = self.pages[r.rid]
+            if rp.fmt != "fp8" or new_len[r.rid] < thr or not rp.pages:
+                continue
+            reserved = sum(max(0, q.high_pages - len(q.pages)) for q in self.pages.values()
+                           if getattr(q, "fmt", None) == "nvfp4")
+            if space.free_in("nvfp4") - reserved < rp.high_pages:
+                continue
+            lps = sorted(rp.pages)
+            old = [rp.pages[lp] for lp in lps]
+            new = space.mix.alloc(len(lps), "nvfp4", fallback=False)
+            n_tok = rp.length
+            dev = self.device
+            src = torch.tensor(old, dtype=torch.long, device=dev)
+            dst = torch.tensor(new, dtype=torch.long, device=dev)
+            rows = (src[:, None] * 64 + torch.arange(64, device=dev)).reshape(-1)
+            drow = ((dst - space.mix.P8)[:, None] * 64 + torch.arange(64, device=dev)).reshape(-1)
+            keep = torch.arange(rows.numel(), device=dev) < n_tok        # positions written so far
+            for i in range(len(self.kv.latent)):
+                lat = M_FMT.mla_fp8_row_dequantize(self.kv.latent[i][rows[keep]])
+                K_OPS.mla_write(lat[:, :512].contiguous(), lat[:, 512:].contiguous(), drow[keep].int(),
+                                self.kv.latent4[i])
+                self.kv.index[i][dst] = self.kv.index[i][src]
+            for lp, pg in zip(lps, new):
+                rp.pages[lp] = pg
+                self.kv.table.set(r.slot, lp, pg)
+            space.release(old)
+            rp.alloc = space.view("nvfp4")
+            rp.fmt = "nvfp4"
+            self.placement[r.rid] = "nvfp4"
+            self.promotions += 1
 
     def _run(self, segs: list, agreed: bool = False) -> list:
         st, rows = self._step(segs, agreed)
@@ -277,7 +366,7 @@ class MLARunner:
     # draft is its prediction at P + 1 when the draft was accepted, else at P.  Greedy verification: the emitted
     # tokens are exactly plain greedy decoding's.
     def _mtp_step(self, st: MLAStep, ids: torch.Tensor) -> MLAStep:
-        return MLAStep(ids, st.pos, st.slot, st.limit, st.req_idx, st.max_ctx)
+        return MLAStep(ids, st.pos, st.slot, st.limit, st.req_idx, st.max_ctx, pool_sel=st.pool_sel)
 
     def _prefill_spec(self, segs: list) -> dict:
         st, rows = self._step(segs)
@@ -385,12 +474,13 @@ class MLARunner:
         if bucket in self.graphs:
             return self.graphs[bucket]
         dev = self.device
-        host = torch.zeros(5, bucket, dtype=torch.int32).pin_memory()
+        host = torch.zeros(6 if self.mixed else 5, bucket, dtype=torch.int32).pin_memory()
         host[2].fill_(-1)
         host[3].fill_(1)
         host[4].fill_(self.dummy_row)
         step = host.to(dev)
-        st = MLAStep(step[0], step[1], step[2], step[3], step[4], self.max_seq + 1)
+        st = MLAStep(step[0], step[1], step[2], step[3], step[4], self.max_seq + 1,
+                     pool_sel=step[5] if self.mixed else None)
         out = torch.zeros(bucket, dtype=torch.int32, device=dev)
         self.model.ep_pieces = 1                # a decode step is one exchange per MoE layer on every rank
         side = torch.cuda.Stream(dev)
@@ -411,13 +501,18 @@ class MLARunner:
         g, step, out, host = self._graph(bucket)
         n = len(reqs)
         rows = []
+        if self.mixed:
+            self._promote(reqs, {r.rid: r.kv_len + 1 for r in reqs})
         for r in reqs:
             rp = self.pages[r.rid]
             p = r.kv_len
             rp.ensure(p + 1)
-            rows.append((int(r.pending), p, rp.slot_of(p), p + 1, r.slot))
+            row = (int(r.pending), p, rp.slot_of(p), p + 1, r.slot)
+            rows.append(row + (int(rp.fmt == "nvfp4"),) if self.mixed else row)
         # one host tensor for the step's inputs (per-element writes into the pinned buffer cost ~1 us each)
         host[:, :n].copy_(torch.tensor(rows, dtype=torch.int32).t())
+        if self.mixed:
+            host[5, n:] = 0
         host[0, n:] = 0
         host[1, n:] = 0
         host[2, n:] = -1

@@ -101,7 +101,12 @@ def synth_mla_sessions(engine, n: int, ctx: int, max_new: int, seed: int = 0, ch
             m = s.numel()
             lat = torch.randn(m, cfg.kv_lora, generator=gd, device=dev).to(torch.bfloat16)
             rope = torch.randn(m, cfg.qk_rope, generator=gd, device=dev).to(torch.bfloat16)
-            K.mla_write(lat, rope, s, runner.kv.latent[layer])
+            if getattr(runner.kv, "mixed", False):           # kvmix: slots past the split are NVFP4 rows
+                sp = runner.kv.split_slot
+                K.mla_write(lat, rope, torch.where(s < sp, s, torch.full_like(s, -1)), runner.kv.latent[layer])
+                K.mla_write(lat, rope, torch.where(s >= sp, s - sp, torch.full_like(s, -1)), runner.kv.latent4[layer])
+            else:
+                K.mla_write(lat, rope, s, runner.kv.latent[layer])
             ik = torch.randn(m, cfg.index_dim, generator=gd, device=dev).to(torch.bfloat16)
             K.index_key_write(ik, s, runner.kv.index[layer])
     return reqs

@@ -140,3 +140,51 @@ def capacity_gain(pages_fp8_equivalent_bytes: int, frac_fp4: float) -> float:
     b8, b4 = F.MLA_FP8_ROW_BYTES, F.MLA_ROW_BYTES
     per_tok = (1 - frac_fp4) * b8 + frac_fp4 * b4
     return (pages_fp8_equivalent_bytes / per_tok) / (pages_fp8_equivalent_bytes / b8)
+
+
+class KVMixPageSpace:
+    """The kvmix id space as the page allocator the MLA runner and its requests use (`free`, `used`, `alloc`,
+    `release`, `num_pages`), with one pool per request: `view(fmt)` is an allocator drawing only from that pool, so a
+    request's pages never straddle the formats (its tokens are served by one sparse-attention launch).  Page 0 is
+    reserved like the plain allocator's dummy page (padding rows of a step read it)."""
+
+    def __init__(self, pages_fp8: int, pages_fp4: int, threshold: int = DEFAULT_THRESHOLD):
+        self.mix = KVMixAllocator(pages_fp8, pages_fp4, threshold)
+        self.mix.free8.remove(0)
+        self.num_pages = pages_fp8 + pages_fp4
+        self.reserved = 1
+
+    @property
+    def free(self) -> int:
+        return len(self.mix.free8) + len(self.mix.free4)
+
+    @property
+    def used(self) -> int:
+        return self.num_pages - self.reserved - self.free
+
+    def free_in(self, fmt: str) -> int:
+        return len(self.mix.free8 if fmt == "fp8" else self.mix.free4)
+
+    def alloc(self, n: int) -> list:
+        return self.mix.alloc(n, "fp8")
+
+    def release(self, pages) -> None:
+        self.mix.release(pages)
+
+    def view(self, fmt: str) -> "_PoolView":
+        return _PoolView(self, fmt)
+
+
+class _PoolView:
+    def __init__(self, space: KVMixPageSpace, fmt: str):
+        self.space, self.fmt = space, fmt
+
+    @property
+    def free(self) -> int:
+        return self.space.free_in(self.fmt)
+
+    def alloc(self, n: int) -> list:
+        return self.space.mix.alloc(n, self.fmt, fallback=False)
+
+    def release(self, pages) -> None:
+        self.space.release(pages)

@@ -98,20 +98,39 @@ class MLAStep:
     limit: torch.Tensor         # int32 [T] visible positions (the token's own included)
     req_idx: torch.Tensor       # int32 [T] page-table row
     max_ctx: int                # bound on limit (fixed per CUDA graph)
+    pool_sel: Optional[torch.Tensor] = None   # int32 [T] kvmix pool of the token's request (0 FP8, 1 NVFP4)
 
 
 class MLAKVCache:
     def __init__(self, cfg: MLAMoEConfig, device, fmt: int, rows: int, max_pages: int, pages: int,
-                 extra_layers: int = 0, latent_div: int = 1, storage=None):
+                 extra_layers: int = 0, latent_div: int = 1, storage=None, mix: Optional[tuple] = None):
         """latent_div S > 1 (decode context parallelism): this rank's latent pools hold the rows it owns, 1 / S of
         the page space (pool row v at local row v // S); the index pools stay whole (every rank scores every row).
         storage(layers, pages, row_bytes) -> (pages, latent pools [pages * 64, row_bytes], index pools [pages,
         8448]): pools placed by the caller (prefill / decode disaggregation maps them from symmetric memory); it may
-        lower the page count (both sides of a pair agree on one)."""
+        lower the page count (both sides of a pair agree on one).
+        mix = (pages_fp8, pages_fp4, threshold): a kvmix page space (`kv/kvmix.py`): latent rows of pages [0, P8) in
+        FP8 pools (576 B), of pages [P8, P8 + P4) in NVFP4 pools (352 B, `latent4`), index pools over every page;
+        `alloc` hands each request pages of one pool."""
         self.cfg, self.device, self.fmt = cfg, torch.device(device), fmt
-        rb = M.ROW_BYTES[fmt]
         n = cfg.num_layers + extra_layers           # extra: the MTP draft layer's pools (same page ids)
-        if storage is not None:
+        self.mixed = mix is not None
+        self.latent4 = None
+        if self.mixed:
+            assert storage is None and latent_div == 1, "kvmix pools are local and whole"
+            p8, p4, thr = mix
+            pages = p8 + p4
+            self.fmt = fmt = M.FMT_FP8
+            self.latent4 = [torch.zeros(p4 * 64, M.ROW_BYTES[M.FMT_NVFP4], dtype=torch.uint8, device=self.device)
+                            for _ in range(n)]
+            self.split_slot = p8 * 64
+            pages_fp8 = p8
+        rb = M.ROW_BYTES[fmt]
+        if self.mixed:
+            self.latent = [torch.zeros(pages_fp8 * 64, rb, dtype=torch.uint8, device=self.device) for _ in range(n)]
+            self.index = [torch.zeros(pages, K.INDEX_PAGE_BYTES, dtype=torch.uint8, device=self.device)
+                          for _ in range(n)]
+        elif storage is not None:
             assert latent_div == 1, "placed pools hold whole pages"
             pages, self.latent, self.index = storage(n, pages, rb)
         else:
@@ -121,7 +140,11 @@ class MLAKVCache:
                           for _ in range(n)]
         self.pages = pages
         from ..kv.allocator import PageAllocator, PageTable
-        self.alloc = PageAllocator(pages)
+        if self.mixed:
+            from ..kv.kvmix import KVMixPageSpace
+            self.alloc = KVMixPageSpace(mix[0], mix[1], mix[2])
+        else:
+            self.alloc = PageAllocator(pages)
         self.table = PageTable(rows, max_pages, self.device)
         self.mla_ws: dict = {}
         self.idx_ws: dict = {}
@@ -640,7 +663,8 @@ class MLAModel:
         qa_s = torch.empty(t, c.q_lora // 128, dtype=torch.int32, device=dev) if fp8_b else None
         ext().mla_prep_kv(ya, w.q_norm, w.kv_norm, w.wi_kn, w.wi_kb, cs, st.pos, st.slot, qa, kv.latent[i],
                           kv.index[i], iw, c.index_heads ** -0.5 * c.index_dim ** -0.5, c.q_lora, c.index_heads, eps,
-                          lat_slot, qa_q, qa_s)
+                          lat_slot, qa_q, qa_s, kv.latent4[i] if kv.mixed else None,
+                          kv.split_slot if kv.mixed else 0)
         yb = w.k["b"].lin.forward_quantized(qa_q, qa_s) if fp8_b else w.k["b"].lin(qa)
         qf = torch.empty(t, c.num_heads, 576, dtype=torch.bfloat16, device=dev)
         w.k["uk"](yb, t, row_stride=w.k["b_stride"], out=qf.view(t * c.num_heads, 576)[:, :512])
@@ -665,7 +689,14 @@ class MLAModel:
         q_pe = self._rope(q_pe, st.pos, cs)
         lat = B.rmsnorm(kva[:, :c.kv_lora].contiguous(), w.kv_norm, eps)
         k_pe = self._rope(kva[:, None, c.kv_lora:], st.pos, cs)[:, 0]
-        K.mla_write(lat, k_pe.contiguous(), st.slot if lat_slot is None else lat_slot, kv.latent[i])
+        slot = st.slot if lat_slot is None else lat_slot
+        if kv.mixed:                                # kvmix: slots past the split live in the NVFP4 pool
+            lo = torch.where(slot < kv.split_slot, slot, torch.full_like(slot, -1))
+            hi = torch.where(slot >= kv.split_slot, slot - kv.split_slot, torch.full_like(slot, -1))
+            K.mla_write(lat, k_pe.contiguous(), lo, kv.latent[i])
+            K.mla_write(lat, k_pe.contiguous(), hi, kv.latent4[i])
+        else:
+            K.mla_write(lat, k_pe.contiguous(), slot, kv.latent[i])
         # DSA indexer
         iq = torch.cat([self._rope(iq[..., :c.qk_rope], st.pos, cs), iq[..., c.qk_rope:]], dim=-1)
         ik = Fn.layer_norm(ik_.float(), (c.index_dim,), w.wi_kn.float(), w.wi_kb.float(), eps)
@@ -687,8 +718,13 @@ class MLAModel:
         t, eps = x.shape[0], c.rms_eps
         qf, sel = (self._query_fused if self._fused_glue(w) else self._query_torch)(i, x, st, kv)
         # absorbed sparse attention over the latent pool
-        o_lat = M.mla_decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt,
-                             ws=kv.workspaces(t, st.max_ctx, c.num_heads, c.index_topk)[1])
+        if kv.mixed:                                # one launch per pool format over the kvmix id space
+            o_lat = M.mla_decode_mixed(qf, [kv.latent[i], kv.latent4[i]], [M.FMT_FP8, M.FMT_NVFP4],
+                                       [0, kv.split_slot], sel, st.pool_sel, self.sm_scale,
+                                       ws=kv.workspaces(t, st.max_ctx, c.num_heads, c.index_topk)[1])
+        else:
+            o_lat = M.mla_decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt,
+                                 ws=kv.workspaces(t, st.max_ctx, c.num_heads, c.index_topk)[1])
         # h += attn; x2 = norm_post(h), also block-quantized when the FFN's expert GEMMs take FP8 input
         o = self._o_proj(w, o_lat, t)
         xq8 = None

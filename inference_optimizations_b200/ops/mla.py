@@ -91,8 +91,38 @@ def mla_decode(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_scale:
         ws = MlaWorkspace.allocate(t, h, ns, device=q.device)
     assert ws.fits(t, h, ns), "workspace too small"
     ext().mla_decode(q.contiguous(), ws.q8[:t], ws.q_scale[:t], pool, idx, out, lse, ws.o_part, ws.lse_part, ws.status,
-                     fmt, tps, ns, sm_scale, trace)
+                     fmt, tps, ns, sm_scale, trace, None, 0, 0)
     return (out, lse) if return_lse else out
+
+
+def mla_decode_mixed(q: torch.Tensor, pools: list, fmts: list, row_los: list, idx: torch.Tensor,
+                     tok_pool: torch.Tensor, sm_scale: float, ws: Optional[MlaWorkspace] = None,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Sparse MLA decode over a mixed-format page space (kvmix): pool k holds the rows [row_los[k], row_los[k] +
+    rows_k) of one id space in format fmts[k]; every token's rows live in the pool tok_pool[t] names.  One launch per
+    pool, each over all tokens, skipping those of the other pool (so a CUDA graph holds a fixed launch list whatever
+    the requests' placement); the query is quantized once, by the first launch.  -> out bf16 [T, H, 512]."""
+    t, h, _ = q.shape
+    if out is None:
+        out = torch.empty(t, h, F.MLA_NOPE, dtype=torch.bfloat16, device=q.device)
+    if not q.is_cuda:
+        sel = tok_pool.cpu()
+        for k, (pool, fmt, lo) in enumerate(zip(pools, fmts, row_los)):
+            rows = (sel == k).nonzero().flatten()
+            if rows.numel():
+                ik = idx[rows]
+                ik = torch.where(ik >= 0, ik - lo, ik)
+                o, _ = mla_decode_ref(q[rows], pool, ik, sm_scale, fmt)
+                out[rows] = o.to(out.dtype)
+        return out
+    ns, tps = mla_split_policy(t, idx.shape[1])
+    if ws is None:
+        ws = MlaWorkspace.allocate(t, h, ns, device=q.device)
+    assert ws.fits(t, h, ns), "workspace too small"
+    for k, (pool, fmt, lo) in enumerate(zip(pools, fmts, row_los)):
+        ext().mla_decode(q.contiguous() if k == 0 else None, ws.q8[:t], ws.q_scale[:t], pool, idx, out, None,
+                         ws.o_part, ws.lse_part, ws.status, fmt, tps, ns, sm_scale, None, tok_pool, k, lo)
+    return out
 
 
 def dense_indices(page_table: torch.Tensor, kv_len: torch.Tensor, max_ctx: int, page: int = 64) -> torch.Tensor:
