@@ -262,7 +262,8 @@ class MLARunner:
             drow = ((dst - space.mix.P8)[:, None] * 64 + torch.arange(64, device=dev)).reshape(-1)
             keep = torch.arange(rows.numel(), device=dev) < n_tok        # positions written so far
             for i in range(len(self.kv.latent)):
-                lat = M_FMT.mla_fp8_row_dequantize(self.kv.latent[i][rows[keep]])
+                # E4M3 values are exact in bf16, the writer kernel's input type
+                lat = M_FMT.mla_fp8_row_dequantize(self.kv.latent[i][rows[keep]]).to(torch.bfloat16)
                 K_OPS.mla_write(lat[:, :512].contiguous(), lat[:, 512:].contiguous(), drow[keep].int(),
                                 self.kv.latent4[i])
                 self.kv.index[i][dst] = self.kv.index[i][src]

@@ -546,6 +546,13 @@ class GQARunner:
         self.spec_out_host = torch.zeros(self.max_running, 7, dtype=torch.int32, pin_memory=pin)
         self.dec_resid = torch.zeros(max(self.ecfg.graph_sizes() + [self.max_running]), h, dtype=torch.bfloat16,
                                      device=self.device)
+        # scripted drafts (benchmarks with a controlled acceptance rate): per request row, 3 tokens and a mask; a
+        # masked-in draft token replaces the draft head's proposal just before verification
+        nb = max(self.ecfg.graph_sizes() + [self.max_running])
+        self.script_tok = torch.zeros(nb, 3, dtype=torch.int32, device=self.device)
+        self.script_mask = torch.zeros(nb, 3, dtype=torch.bool, device=self.device)
+        self.script_host = torch.zeros(nb, 4, dtype=torch.int32, pin_memory=pin)
+        self.draft_script = None          # callable(request, L) -> [(token, use)] x 3, or None (the draft head alone)
 
     def _draft_prefill(self, batch: Batch, p: Packed, resid: torch.Tensor, st: StepTensors) -> None:
         """Fill the draft layer's KV over each prefill segment: draft input at position q is (token q, target hidden
@@ -576,6 +583,7 @@ class GQARunner:
         h = self.cfg.hidden
         rows = torch.arange(bucket, device=self.device) * 4
         d_tok = torch.zeros(3, bucket, dtype=torch.int32, device=self.device)
+        scripted = self.draft_script is not None            # fixed when the graph is captured
         t_tok = torch.zeros(bucket * 4, dtype=torch.int32, device=self.device)
 
         def body():
@@ -591,6 +599,8 @@ class GQARunner:
                 stk.ids.copy_(d_tok[k - 1])
                 x, g = self._draft_forward(stk, g)
                 self._greedy(x, d_tok[k])
+            if scripted:                                         # controlled acceptance (benchmarks)
+                d_tok.copy_(torch.where(self.script_mask[:bucket].t(), self.script_tok[:bucket].t(), d_tok))
             # 4. verify [x_L, d1, d2, d3]
             ids4 = st_ver.ids.view(bucket, 4)
             ids4[:, 1:].copy_(d_tok.t())
@@ -628,6 +638,17 @@ class GQARunner:
         self.kv.sync_tables()
         for st in (self.st_ext, self.st_d2, self.st_d3, self.st_ver):
             st.upload()
+        if self.draft_script is not None:
+            rows = [[0, 0, 0, 0] for _ in range(bucket)]
+            for i, r in enumerate(reqs):
+                for k, (tok, use) in enumerate(self.draft_script(r, r.kv_len)):
+                    rows[i][k] = int(tok)
+                    rows[i][3] |= int(bool(use)) << k
+            hs = self.script_host[:bucket]
+            hs.copy_(torch.tensor(rows, dtype=torch.int32))
+            dev_rows = hs.to(self.device, non_blocking=True)
+            self.script_tok[:bucket].copy_(dev_rows[:, :3])
+            self.script_mask[:bucket].copy_((dev_rows[:, 3:4] >> torch.arange(3, device=self.device)) & 1 == 1)
         self._timed(self._spec_fn(bucket))
         n = len(reqs)
         self.spec_out_host[:n].copy_(self.spec_out[:n], non_blocking=True)

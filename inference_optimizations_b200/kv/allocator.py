@@ -48,6 +48,11 @@ class PageAllocator:
             if p >= self.reserved:
                 self._free.append(p)
 
+    def reset(self) -> None:
+        """Every page free again, in the initial order (only with no request holding pages): a re-registered set of
+        requests then gets the same physical pages as the first time."""
+        self._free = list(range(self.num_pages - 1, self.reserved - 1, -1))
+
 
 class PageTable:
     """Device page table with a pinned host mirror."""

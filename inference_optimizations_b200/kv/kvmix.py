@@ -129,7 +129,7 @@ def _copy_promote(pools: KVMixPools, src_pages: list, dst_pages: list, n_tokens:
         if n <= 0:
             break
         s0 = pools.alloc.local(src) * PAGE
-        lat = F.mla_fp8_row_dequantize(pools.fp8[s0:s0 + n])
+        lat = F.mla_fp8_row_dequantize(pools.fp8[s0:s0 + n]).to(torch.bfloat16)   # E4M3 values are exact in bf16
         d0 = pools.alloc.local(dst) * PAGE
         slot = torch.arange(d0, d0 + n, dtype=torch.int32, device=lat.device)
         K.mla_write(lat[:, :F.MLA_NOPE].contiguous(), lat[:, F.MLA_NOPE:].contiguous(), slot, pools.fp4)

@@ -109,3 +109,27 @@ def test_step_trace_records(tmp_path):
     assert len(recs) == len(eng.stats)
     assert {r["kind"] for r in recs} >= {"prefill", "decode"}
     assert all("schedule" in r["phases"] for r in recs) and recs[0]["step"] == 0
+
+
+def test_scripted_drafts_control_acceptance():
+    """Scripted drafts (the benchmark's controlled acceptance): when the script proposes the plain engine's own
+    greedy continuation, every speculative step accepts all 3 drafts and the output is the plain output; when it
+    proposes wrong tokens, none is accepted and the output is still the plain output."""
+    torch.manual_seed(6)
+    prompts = [torch.randint(1, 500, (n,)).tolist() for n in (40, 25)]
+    params = SamplingParams(max_new_tokens=13)
+    base = _engine().generate(prompts, params)
+    for truth in (True, False):
+        eng = _engine(spec=True, draft_tokens=3, spec_policy="always")
+        reqs = [eng.add_request(p, params) for p in prompts]
+        cont = {r.rid: list(p) + list(b) for r, p, b in zip(reqs, prompts, base)}
+
+        def script(r, L, cont=cont, truth=truth):
+            toks = [cont[r.rid][L + 1 + k] if L + 1 + k < len(cont[r.rid]) else 1 for k in range(3)]
+            return [(t if truth else t % 499 + 1, True) for t in toks]
+        eng.runner.draft_script = script
+        while eng.has_work():
+            eng.step()
+        assert [r.output for r in reqs] == base
+        acc = sum(r.accepted for r in reqs) / max(1, sum(r.spec_steps for r in reqs))
+        assert (acc > 2.0) if truth else (acc == 0.0), acc
