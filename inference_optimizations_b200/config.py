@@ -109,9 +109,19 @@ class MLAMoEConfig:
     init_std: float = 0.02
     draft_layers: int = 1
     draft_tokens: int = 1
+    # hybrid linear attention (Kimi-Linear class): with kda_every = n > 0, layer i is a Kimi-delta-attention layer
+    # unless (i + 1) % n == 0 (an MLA layer); KDA heads of 128 key / 128 value dims, a short causal conv of kda_conv
+    # taps, low-rank (kda_rank) forget / output gates
+    kda_every: int = 0
+    kda_heads: int = 0
+    kda_conv: int = 4
+    kda_rank: int = 128
 
     def is_moe(self, layer: int) -> bool:
         return layer >= self.first_dense
+
+    def is_kda(self, layer: int) -> bool:
+        return self.kda_every > 0 and layer < self.num_layers and (layer + 1) % self.kda_every != 0
 
     def num_params(self) -> int:
         h = self.hidden
@@ -139,10 +149,20 @@ PRESETS: dict[str, Any] = {
                                  qk_rope=64, v_head=256, index_heads=32, num_experts=160, topk=8, expert_ffn=2048,
                                  dense_ffn=12288, n_group=1, topk_group=1, routed_scale=2.5,
                                  weight_dtype="fp8", expert_dtype="nvfp4", vocab=154880),
+    # hybrid KDA + MLA + MoE (Kimi-Linear class): three KDA layers per MLA layer
+    "kimi_linear": lambda: MLAMoEConfig(name="kimi_linear", num_layers=27, hidden=2304, num_heads=32, q_lora=1536,
+                                        qk_nope=128, qk_rope=64, v_head=128, index_heads=32, num_experts=256, topk=8,
+                                        expert_ffn=1024, first_dense=1, dense_ffn=9216, n_group=1, topk_group=1,
+                                        vocab=163840, kda_every=4, kda_heads=32, kda_rank=128),
     # small shapes for tests (same code paths, tiny dims)
     "tiny_gqa": lambda: GQAConfig(name="tiny_gqa", num_layers=6, hidden=256, num_q_heads=4, num_kv_heads=2,
                                   num_kv_heads_global=2, head_dim=128, head_dim_global=256, global_every=3,
                                   sliding_window=48, ffn=512, vocab=512),
+    "tiny_kda": lambda: MLAMoEConfig(name="tiny_kda", num_layers=3, hidden=256, num_heads=4, q_lora=128, kv_lora=512,
+                                     qk_nope=32, qk_rope=64, v_head=32, index_heads=4, index_dim=128, index_topk=64,
+                                     first_dense=1, dense_ffn=512, num_experts=8, topk=2, num_shared=1,
+                                     expert_ffn=128, n_group=2, topk_group=1, vocab=512, weight_dtype="bf16",
+                                     expert_dtype="bf16", kda_every=3, kda_heads=2, kda_rank=32),
     "tiny_mla": lambda: MLAMoEConfig(name="tiny_mla", num_layers=3, hidden=256, num_heads=4, q_lora=128, kv_lora=512,
                                      qk_nope=32, qk_rope=64, v_head=32, index_heads=4, index_dim=128, index_topk=64,
                                      first_dense=1, dense_ffn=512, num_experts=8, topk=2, num_shared=1,

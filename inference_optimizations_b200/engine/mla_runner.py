@@ -105,7 +105,10 @@ class MLARunner:
         self.graph_launches: dict = {}
         self.event_log = None
         self.prefix_cache = None
-        if ecfg.prefix_cache:
+        if cfg.kda_every and self.spec:
+            raise NotImplementedError("hybrid KDA models run without the MTP draft")
+        # hybrid models: a cached prefix's pages hold no KDA recurrent state, so prefixes are not reused
+        if ecfg.prefix_cache and not cfg.kda_every:
             from ..kv.radix import RadixCache
             self.prefix_cache = RadixCache(self.kv.alloc)
 
@@ -138,6 +141,8 @@ class MLARunner:
         return False
 
     def attach(self, r: Request) -> None:
+        if self.kv.kda:
+            self.kv.reset_state(r.slot)         # a new request starts from zero recurrent state
         if self.mixed:
             fmt = self.placement.get(r.rid) or self.kv.alloc.mix.preferred(r.prompt_len + r.params.max_new_tokens)
             rp = RequestPages(self.kv.alloc.view(fmt), self.kv.table, r.slot)
@@ -207,7 +212,7 @@ class MLARunner:
 
     # ------------------------------------------------------------------------------------------ steps
     def _step(self, segs: list, agreed: bool = False) -> tuple[MLAStep, list]:
-        ids, pos, slot, limit, rix, logit_rows, psel = [], [], [], [], [], [], []
+        ids, pos, slot, limit, rix, logit_rows, psel, kseg = [], [], [], [], [], [], [], []
         if self.mixed:
             self._promote([s.req for s in segs], {s.req.rid: s.start + len(s.tokens) for s in segs})
         for s in segs:
@@ -215,6 +220,7 @@ class MLARunner:
             rp.ensure(s.start + len(s.tokens))
             if self.mixed:
                 psel += [int(rp.fmt == "nvfp4")] * len(s.tokens)
+            kseg.append((len(ids), len(s.tokens), s.req.slot))
             for j, tok in enumerate(s.tokens):
                 p = s.start + j
                 ids.append(int(tok))
@@ -231,7 +237,7 @@ class MLARunner:
         dev = self.device
         mk = lambda v: torch.tensor(v, dtype=torch.int32).to(dev, non_blocking=True)  # noqa: E731
         st = MLAStep(mk(ids), mk(pos), mk(slot), mk(limit), mk(rix), self.max_seq + 1,
-                     pool_sel=mk(psel) if self.mixed else None)
+                     pool_sel=mk(psel) if self.mixed else None, segs=kseg if self.cfg.kda_every else None)
         if not agreed:
             self._agree(len(ids))
         return st, logit_rows

@@ -87,6 +87,7 @@ class MLALayerWeights:
     wi_w: torch.Tensor          # [Hi, H]
     ffn: dict
     k: Optional[dict] = None    # GEMM kernels of the projections (GPU); None: torch reference path
+    kda: Optional[dict] = None  # a Kimi-delta-attention layer's weights (hybrid models); the MLA fields are then None
 
 
 @dataclass
@@ -99,6 +100,8 @@ class MLAStep:
     req_idx: torch.Tensor       # int32 [T] page-table row
     max_ctx: int                # bound on limit (fixed per CUDA graph)
     pool_sel: Optional[torch.Tensor] = None   # int32 [T] kvmix pool of the token's request (0 FP8, 1 NVFP4)
+    segs: Optional[list] = None               # host (first row, tokens, request row) per segment (hybrid KDA
+                                              # prefill); None: every token its own request (decode)
 
 
 class MLAKVCache:
@@ -139,6 +142,20 @@ class MLAKVCache:
             self.index = [torch.zeros(pages, K.INDEX_PAGE_BYTES, dtype=torch.uint8, device=self.device)
                           for _ in range(n)]
         self.pages = pages
+        # hybrid models: per request row, the recurrent state of every Kimi-delta-attention layer (conv taps, fp32
+        # delta-rule state); those layers' latent / index pools are never read (one page each)
+        self.kda: dict = {}
+        if cfg.kda_every:
+            H, D, W = cfg.kda_heads, 128, cfg.kda_conv
+            for i in range(cfg.num_layers):
+                if not cfg.is_kda(i):
+                    continue
+                z = lambda *shape: torch.zeros(*shape, dtype=torch.float32, device=self.device)  # noqa: E731
+                self.kda[i] = {"csq": z(rows, H * D, W - 1), "csk": z(rows, H * D, W - 1),
+                               "csv": z(rows, H * D, W - 1), "S": z(rows, H, D, D)}
+                if not self.mixed and storage is None:
+                    self.latent[i] = torch.zeros(64, rb, dtype=torch.uint8, device=self.device)
+                    self.index[i] = torch.zeros(1, K.INDEX_PAGE_BYTES, dtype=torch.uint8, device=self.device)
         from ..kv.allocator import PageAllocator, PageTable
         if self.mixed:
             from ..kv.kvmix import KVMixPageSpace
@@ -148,6 +165,12 @@ class MLAKVCache:
         self.table = PageTable(rows, max_pages, self.device)
         self.mla_ws: dict = {}
         self.idx_ws: dict = {}
+
+    def reset_state(self, row: int) -> None:
+        """Zero the recurrent KDA states of request row `row` (a new request taking the row)."""
+        for st in self.kda.values():
+            for v in st.values():
+                v[row].zero_()
 
     def workspaces(self, t: int, max_ctx: int, heads: int, topk: int):
         """(indexer workspace, sparse-MLA workspace) of a step with t tokens and context bound max_ctx, shared by
@@ -243,12 +266,38 @@ class MLAModel:
         weight format applies to experts only)."""
         return self.cuda and self.cfg.weight_dtype in ("fp8", "bf16")
 
+    def _make_kda(self, prefix: str) -> dict:
+        """A Kimi-delta-attention layer (hybrid models): fused q | k | v projection, output projection, the small
+        projections (beta, low-rank forget gate, low-rank output gate; fused into one GEMM + one batched GEMM,
+        `ops/kda.py KDASmallProjections`), causal conv taps, decay bias / log-rate, output norm."""
+        from ..ops import kda as KDA
+        c, h = self.cfg, self.cfg.hidden
+        H, D, W, R = c.kda_heads, 128, c.kda_conv, c.kda_rank
+        r = lambda name, shape, s=c.init_std: self.src.tensor(f"{prefix}.{name}", shape, s)  # noqa: E731
+        f32 = lambda name, shape, s: r(name, shape, s).float()  # noqa: E731
+        kd = {"w_qkv": r("kda.qkv", (3 * H * D, h)), "wo": r("kda.o", (h, H * D)),
+              "small": KDA.KDASmallProjections(r("kda.b", (H, h)), r("kda.f_a", (R, h)), r("kda.f_b", (H * D, R)),
+                                               r("kda.g_a", (R, h)), r("kda.g_b", (H * D, R))),
+              "cwq": f32("kda.conv_q", (H * D, W), 0.5), "cwk": f32("kda.conv_k", (H * D, W), 0.5),
+              "cwv": f32("kda.conv_v", (H * D, W), 0.5), "dt_bias": f32("kda.dt_bias", (H * D,), 0.1),
+              "A_log": f32("kda.a_log", (H,), 0.5), "norm_w": self.src.norm(f"{prefix}.kda.norm", D, 1.0,
+                                                                             torch.float32)}
+        kd["small"].fuse()
+        if self._kernels():
+            kd["qkv"] = L.Linear(kd["w_qkv"], "bf16")
+            kd["o"] = L.Linear(kd["wo"], "bf16")
+            if not self.keep_master:
+                kd["w_qkv"] = kd["wo"] = None
+        return kd
+
     def _make_layer(self, prefix: str, i: int) -> "MLALayerWeights":
         """Layer i's weights (named `prefix`.*; the MTP draft layer uses prefix "mtp.<i>"), with the GEMM kernels
         built and, unless keep_master, the bf16 masters dropped."""
         c, h = self.cfg, self.cfg.hidden
         r = lambda name, shape, s=c.init_std: self.src.tensor(name, shape, s)  # noqa: E731
         nrm = lambda name, n, fill=1.0: self.src.norm(f"{prefix}.{name}", n, fill)  # noqa: E731
+        if c.is_kda(i):
+            return self._make_kda_layer(prefix, i, r, nrm)
         wkv_b = r(f"{prefix}.wkv_b", (c.num_heads * (c.qk_nope + c.v_head), c.kv_lora)).view(
             c.num_heads, c.qk_nope + c.v_head, c.kv_lora)
         moe = c.is_moe(i)
@@ -300,6 +349,72 @@ class MLAModel:
                     for k in ("w_gu", "w_down", "shared_gu", "shared_down"):
                         ffn[k] = None
         return w
+
+    def _make_kda_layer(self, prefix: str, i: int, r, nrm) -> "MLALayerWeights":
+        c, h = self.cfg, self.cfg.hidden
+        if self.dcp_world > 1:
+            raise NotImplementedError("hybrid KDA layers run without context parallelism")
+        moe = c.is_moe(i)
+        F = c.expert_ffn
+        if moe:
+            ffn = {"gate": r(f"{prefix}.gate", (c.num_experts, h)),
+                   "e_bias": self.src.norm(f"{prefix}.e_bias", c.num_experts, 0.0, torch.float32),
+                   "w_gu": None, "w_down": None,
+                   "shared_gu": r(f"{prefix}.shared.gu", (2 * F * c.num_shared, h)) if c.num_shared else None,
+                   "shared_down": r(f"{prefix}.shared.down", (h, F * c.num_shared)) if c.num_shared else None}
+            if self.keep_master or not self._quantized_ffn(i):
+                ffn["w_gu"] = self._experts(f"{prefix}.experts.gu", (2 * F, h))
+                ffn["w_down"] = self._experts(f"{prefix}.experts.down", (h, F))
+        else:
+            ffn = {"w_gu": r(f"{prefix}.mlp.gu", (2 * c.dense_ffn, h)), "w_down": r(f"{prefix}.mlp.down", (h, c.dense_ffn))}
+        none = {k: None for k in ("wq_a", "q_norm", "wq_b", "wkv_a", "kv_norm", "w_uk", "w_uv", "wo", "wi_q", "wi_k",
+                                  "wi_kn", "wi_kb", "wi_w")}
+        w = MLALayerWeights(n_in=nrm("n_in", h), n_post=nrm("n_post", h), ffn=ffn, kda=self._make_kda(prefix),
+                            **none)
+        idx = len(self.layers)
+        if self._quantized_ffn(i) and self.cuda:
+            self._bs[idx] = self._build_ffn(prefix, i, ffn)
+            if not self.keep_master:
+                for k in ("w_gu", "w_down", "shared_gu", "shared_down"):
+                    ffn[k] = None
+        if self._kernels() and moe and ffn.get("gate") is not None:
+            w.k = {"gate": L.Linear(ffn["gate"], "bf16")}
+        return w
+
+    def _kda_attention(self, i: int, x: torch.Tensor, st: "MLAStep", kv: "MLAKVCache") -> torch.Tensor:
+        """Kimi delta attention of layer i -> its output projection [T, hidden].  Recurrent states live per request
+        row (`kv.kda[i]`): a step of single tokens (decode; CUDA graphs) gathers its rows' states, runs the fused
+        decode kernel and scatters them back; a prefill step runs each segment's chunked prefill on that request's
+        state in place (the state carries across chunks)."""
+        from ..ops import kda as KDA
+        c, kd = self.cfg, self.layers[i].kda
+        t = x.shape[0]
+        H, D = c.kda_heads, 128
+        qkv = kd["qkv"](x) if "qkv" in kd else Fn.linear(x, kd["w_qkv"])
+        q, k, v = qkv[:, :H * D], qkv[:, H * D:2 * H * D], qkv[:, 2 * H * D:]
+        b, f, g2 = kd["small"].forward(x)
+        beta = torch.sigmoid(b.float())
+        S = kv.kda[i]
+        args = (kd["dt_bias"], kd["A_log"])
+        if st.segs is None or all(n == 1 for _r0, n, _slot in st.segs):
+            rix = st.req_idx.long()
+            cq, ck, cv, sv = (S[name].index_select(0, rix) for name in ("csq", "csk", "csv", "S"))
+            o = KDA.kda_decode(q.reshape(t, H, D), k.reshape(t, H, D), v.reshape(t, H, D), f.reshape(t, H, D),
+                               *args, beta, g2.reshape(t, H, D), kd["norm_w"], kd["cwq"], kd["cwk"], kd["cwv"],
+                               cq, ck, cv, sv)
+            for name, val in (("csq", cq), ("csk", ck), ("csv", cv), ("S", sv)):
+                S[name].index_copy_(0, rix, val)
+        else:
+            o = torch.empty(t, H, D, dtype=torch.bfloat16, device=x.device)
+            for r0, n, slot in st.segs:
+                sl = slice(r0, r0 + n)
+                rows = slice(slot, slot + 1)
+                o[sl] = KDA.kda_prefill(q[sl].reshape(1, n, H, D), k[sl].reshape(1, n, H, D),
+                                        v[sl].reshape(1, n, H, D), f[sl].reshape(1, n, H, D), *args, beta[sl][None],
+                                        g2[sl].reshape(1, n, H, D), kd["norm_w"], kd["cwq"], kd["cwk"], kd["cwv"],
+                                        S["csq"][rows], S["csk"][rows], S["csv"][rows], S["S"][rows])[0]
+        o = o.reshape(t, H * D)
+        return kd["o"](o) if "o" in kd else Fn.linear(o, kd["wo"])
 
     def _experts(self, name: str, shape) -> torch.Tensor:
         """This rank's routed experts [e_lo, e_hi) of a stacked expert weight (each expert fetched by its own name)."""
@@ -716,6 +831,8 @@ class MLAModel:
             return self._layer_forward_dcp(i, h, x, st, kv, next_norm)
         c, w = self.cfg, self.layers[i]
         t, eps = x.shape[0], c.rms_eps
+        if w.kda is not None:                          # hybrid model: a Kimi-delta-attention layer
+            return self._post_attention(i, self._kda_attention(i, x, st, kv), h, next_norm)
         qf, sel = (self._query_fused if self._fused_glue(w) else self._query_torch)(i, x, st, kv)
         # absorbed sparse attention over the latent pool
         if kv.mixed:                                # one launch per pool format over the kvmix id space
@@ -725,8 +842,13 @@ class MLAModel:
         else:
             o_lat = M.mla_decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt,
                                  ws=kv.workspaces(t, st.max_ctx, c.num_heads, c.index_topk)[1])
-        # h += attn; x2 = norm_post(h), also block-quantized when the FFN's expert GEMMs take FP8 input
-        o = self._o_proj(w, o_lat, t)
+        return self._post_attention(i, self._o_proj(w, o_lat, t), h, next_norm)
+
+    def _post_attention(self, i: int, o: torch.Tensor, h: torch.Tensor, next_norm: torch.Tensor) -> torch.Tensor:
+        """h += attention output; x2 = norm_post(h), also block-quantized when the FFN's expert GEMMs take FP8 input;
+        h += FFN(x2); -> the next norm of h."""
+        c, w = self.cfg, self.layers[i]
+        t, eps = o.shape[0], c.rms_eps
         xq8 = None
         fp8_ffn = (self._quantized_ffn(i) and c.hidden % 128 == 0 and
                    (c.expert_dtype if c.is_moe(i) else c.weight_dtype) == "fp8")
