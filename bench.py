@@ -51,10 +51,6 @@ def parse():
     p.add_argument("--kv", default="nvfp4", choices=["nvfp4", "fp8", "bf16"])
     p.add_argument("--spec", type=int, default=1,
                    help="gemma31b: 1 = speculative decoding, the config's 1-layer draft proposing 3 tokens; 0 = plain")
-    p.add_argument("--spec-accept", type=float, default=None,
-                   help="gemma31b: controlled acceptance -- each draft token is the target's own greedy continuation "
-                        "(recorded by a plain-decode pass over identical sessions) with this probability, so draft + "
-                        "split-K verify run in every timed step at a known acceptance; the draft head still runs")
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--tp-form", default="push", choices=["push", "pull", "nvls"],
                    help="gemma31b, tp > 1: fused GEMM -> all-reduce form (push: GEMM epilogue stores to every rank; "
@@ -321,50 +317,6 @@ def bench_dsa(args) -> int:
     if n > 1:
         D.shutdown()
     return 0
-def _script_drafts(eng, args, max_new: int, spec_steps: int) -> dict:
-    """Controlled acceptance for the speculative step: a plain-decode pass over the synthetic sessions records the
-    target's greedy continuation; the sessions are then registered again identically (same prompts, same pages, same
-    random KV) and each speculative step's draft token k is the recorded token with probability `spec_accept` (else a
-    wrong one), substituted for the draft head's proposal just before verification.  Acceptance differs from the
-    probability only where the 4-position verify and single-token decode round a near-tie differently."""
-    import random
-    from inference_optimizations_b200.engine.synthetic import synth_decode_sessions
-    run, sched = eng.runner, eng.sched
-    n_rec = 4 * spec_steps + 8
-    reqs = synth_decode_sessions(eng, args.sessions, args.ctx, max_new, seed=1)
-    start = {i: r.kv_len for i, r in enumerate(reqs)}
-    for _ in range(n_rec):                                     # plain greedy continuation of every session
-        out = run.decode(list(sched.running))
-        sched.commit_decode(out)
-    cont = {i: list(r.output) for i, r in enumerate(reqs)}     # cont[i][j]: token at position start + j
-    for r in reqs:                                             # back to the registration state
-        sched.running.remove(r)
-        run.detach(r)
-        sched.free_slots.append(r.slot)
-    for a in run.kv.alloc.values():
-        a.reset()
-    reqs = synth_decode_sessions(eng, args.sessions, args.ctx, max_new, seed=1)
-    index = {r.rid: i for i, r in enumerate(reqs)}
-    rng = random.Random(1234)
-    vocab = eng.cfg.vocab
-    stats = {"proposed": 0, "true": 0}
-
-    def script(r, L):
-        i = index[r.rid]
-        j = L - start[i]
-        toks = []
-        for k in range(3):
-            tok = cont[i][j + 1 + k] if j + 1 + k < len(cont[i]) else 1
-            ok = rng.random() < args.spec_accept
-            toks.append((tok if ok else (tok % (vocab - 1)) + 1, True))
-            stats["proposed"] += 1
-            stats["true"] += int(ok)
-        return toks
-    run.draft_script = script
-    eng.spec_policy.mode = "always"
-    return stats
-
-
 def bench_gemma(args) -> int:
     """Gemma-class dense GQA model, tensor parallel over the N GPUs, decode throughput over 32
     sessions whose 32k-token prompts are in the paged pool."""
@@ -393,18 +345,14 @@ def bench_gemma(args) -> int:
     eng = Engine(ecfg, cfg, max_seq=max_seq, tp_rank=rank, tp=tp,
                  all_reduce=D.nccl_all_reduce if tp > 1 else None,
                  argmax_merge=D.argmax_merge if tp > 1 else None)
-    scripted = None
-    if ecfg.spec and args.spec_accept is not None:
-        scripted = _script_drafts(eng, args, max_new, steps + warm)
-    else:
-        synth_decode_sessions(eng, args.sessions, args.ctx, max_new, seed=1)
+    synth_decode_sessions(eng, args.sessions, args.ctx, max_new, seed=1)
     eng.runner.warm_graphs(args.sessions)
     torch.cuda.synchronize()
     for _ in range(warm):
         eng.step()
     # the adaptive speculation policy probes, prices and decides before the timed steps (all ranks alike)
     extra = 0
-    while ecfg.spec and scripted is None and eng.spec_policy.decided is None and extra < 64:
+    while ecfg.spec and eng.spec_policy.decided is None and extra < 64:
         eng.step()
         extra += 1
     bucket = eng.runner._bucket(args.sessions)
@@ -497,13 +445,6 @@ def bench_gemma(args) -> int:
         res["config"]["spec_policy"] = {
             "mode": ecfg.spec_policy, "timed_steps": {k: kinds.count(k) for k in set(kinds)},
             "probe": {k: (round(v, 5) if isinstance(v, float) else v) for k, v in hist.items()}}
-        if scripted is not None:
-            res["config"]["spec_controlled_acceptance"] = {
-                "target_probability": args.spec_accept,
-                "draft_tokens_true_fraction": round(scripted["true"] / max(1, scripted["proposed"]), 4),
-                "note": ("draft tokens replaced, with the given probability, by the target's own greedy continuation "
-                         "recorded over identical sessions; the draft head and the split-K verify run in every timed "
-                         "step; the policy forced to speculate")}
         res["config"]["spec_note"] = ("random-init draft head: acceptance is whatever the untrained draft achieves "
                                       "against the random-init target; the adaptive policy (speculate only while "
                                       "n * E[tokens] / t(step) beats plain decode) priced both modes before the "
