@@ -391,8 +391,8 @@ class MLAModel:
         t = x.shape[0]
         H, D = c.kda_heads, 128
         qkv = kd["qkv"](x) if "qkv" in kd else Fn.linear(x, kd["w_qkv"])
-        q, k, v = qkv[:, :H * D], qkv[:, H * D:2 * H * D], qkv[:, 2 * H * D:]
-        b, f, g2 = kd["small"].forward(x)
+        q, k, v = (qkv[:, j * H * D:(j + 1) * H * D].contiguous() for j in range(3))
+        b, f, g2 = (u.contiguous() for u in kd["small"].forward(x))
         beta = torch.sigmoid(b.float())
         S = kv.kda[i]
         args = (kd["dt_bias"], kd["A_log"])
@@ -549,8 +549,10 @@ class MLAModel:
         for mine, theirs in zip(self.layers, other.layers):
             for f in vars(theirs):
                 v = getattr(theirs, f)
-                if f == "k":
+                if f == "k" or v is None:
                     continue
+                if f == "kda":
+                    raise NotImplementedError("copy_from: hybrid KDA layers")
                 if isinstance(v, dict):
                     setattr(mine, f, {k: (t.to(dev) if t is not None else None) for k, t in v.items()})
                 else:
