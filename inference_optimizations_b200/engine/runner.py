@@ -85,6 +85,8 @@ class GQARunner:
     def __init__(self, cfg: GQAConfig, ecfg: EngineConfig, device, max_seq: int, tp_rank: int = 0, tp: int = 1,
                  all_reduce: Optional[Callable] = None, argmax_merge: Optional[Callable] = None,
                  global_pages: Optional[int] = None):
+        if ecfg.kv_dtype == "kvmix":
+            raise ValueError("kv_dtype 'kvmix' (FP8 + NVFP4 latent rows in one page space) is an MLA-family pool")
         self.cfg, self.ecfg, self.device = cfg, ecfg, torch.device(device)
         self.tp, self.tp_rank = tp, tp_rank
         self.max_seq = max_seq
