@@ -130,6 +130,25 @@ def _tokens_check(eng, dev) -> dict:
                         "NCCL EP (all-gather + all-to-all), every rank"}
 
 
+def _pool_capacity(eng, cfg, dev) -> dict:
+    """KV-pool capacity at boot on this GPU, this model: the memory free after the weights (plus what the running
+    pool itself took) sized into pages the way the engine sizes a memory-bound pool (`mla_runner.pool_pages`:
+    mem_fraction of the free memory less a reserve), for the NVFP4 352-byte and the FP8 576-byte latent rows (+ the
+    132-byte index key each); the bench's own pool holds just what its sessions need."""
+    import torch
+    from inference_optimizations_b200.ops.formats import INDEX_ROW_BYTES
+    from inference_optimizations_b200.ops.mla import ROW_BYTES, FMT_FP8, FMT_NVFP4
+    kv = eng.runner.kv
+    own = sum(t.numel() for t in kv.latent + kv.index + (kv.latent4 or []))
+    free, _ = torch.cuda.mem_get_info(dev)
+    avail = max(0, free + own - (8 << 30)) * eng.ecfg.mem_fraction
+    tok = {name: int(avail // (cfg.num_layers * (ROW_BYTES[f] + INDEX_ROW_BYTES)))
+           for name, f in (("nvfp4", FMT_NVFP4), ("fp8", FMT_FP8))}
+    return {"tokens_nvfp4": tok["nvfp4"], "tokens_fp8": tok["fp8"],
+            "ratio_nvfp4_vs_fp8": round(tok["nvfp4"] / max(1, tok["fp8"]), 3),
+            "note": "latent + index-key bytes of every layer per token, in the memory free at boot after the weights"}
+
+
 def run_dsa(args, info, dev, layers: int, steps: int, warm: int) -> dict:
     """One DSA-MoE serving run (prefill every prompt, then timed decode steps); the measurements as a dict."""
     import torch
@@ -154,6 +173,7 @@ def run_dsa(args, info, dev, layers: int, steps: int, warm: int) -> dict:
                  ep_group=dist.group.WORLD if n > 1 else None)
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t_build
+    pool = _pool_capacity(eng, cfg, dev)
     g = torch.Generator().manual_seed(1000 + rank)
     reqs = [eng.add_request(torch.randint(1, cfg.vocab, (args.ctx,), generator=g).tolist(),
                             SamplingParams(max_new_tokens=args.max_new)) for _ in range(per)]
@@ -234,6 +254,7 @@ def run_dsa(args, info, dev, layers: int, steps: int, warm: int) -> dict:
                             "per rank, sessions queued at t = 0), device time max over ranks; TTFT = host time from "
                             "the start of the phase to the step that returned the session's first token"},
         "status": status, "check": check, "max_mem_gb": round(mem_gb, 1), "build_s": round(build_s, 1),
+        "kv_pool": pool,
         "clocks": ck, "rejected": rejected(ck),
     }
     eng.runner.graphs.clear()
@@ -267,7 +288,8 @@ def bench_dsa(args) -> int:
         full = {"layers": 61, "value": round(f["value"], 2), "ms_per_step": round(f["ms_per_step"], 4),
                 "e2e_value": round(f["e2e_value"], 2), "per_user_tok_s": round(f["value"] / args.sessions, 3),
                 "vs_baseline": round(f["value"] / BASELINE_TOK_S, 3), "prefill": f["prefill"],
-                "status": f["status"], "correctness": f["check"], "max_mem_gb": f["max_mem_gb"],
+                "status": f["status"], "correctness": f["check"], "kv_pool_capacity_at_boot": f["kv_pool"],
+                "max_mem_gb": f["max_mem_gb"],
                 "clocks": {k: f["clocks"].get(k) for k in ("sm_mhz", "sm_max_mhz", "reasons")}}
     res = {
         "metric": (f"output tok/s: DSA-MoE decode of {args.sessions} sessions after their {args.ctx}-token prompts "
@@ -303,6 +325,7 @@ def bench_dsa(args) -> int:
         "gpu_launches": r["launches"],
         "status": r["status"],
         "correctness": r["check"],
+        "kv_pool_capacity_at_boot": r["kv_pool"],
         "max_mem_gb": r["max_mem_gb"],
         "vs_baseline_note": ("BASELINE.md row 4 (1,813-1,996 steady tok/s at 64 sessions on 8 x B200) is a 61-layer "
                              "number; see full_depth.vs_baseline (--full-depth)"),
