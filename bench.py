@@ -30,7 +30,8 @@ import os
 import sys
 import time
 
-# DeepSeek V4 Pro final composed recipe, 64 sessions on 8 x B200: 1,813 - 1,996 steady tok/s
+# The reference's published final composed DeepSeek V4 Pro recipe, 64 sessions on 8 x B200: 1,813 - 1,996 steady tok/s
+# (`evidence/gate/deepseek-v4-pro_standard_B200:8_final_pro_full_20261002-191557.json` in the reference)
 BASELINE_TOK_S = 1996.0
 
 
@@ -263,7 +264,7 @@ def run_dsa(args, info, dev, layers: int, steps: int, warm: int) -> dict:
 
 
 def bench_dsa(args) -> int:
-    """DSA + MoE (DeepSeek-V3.2 geometry, FP8 128x128 weights), DP attention + EP over N GPUs."""
+    """The flagship serving config: DSA + MoE (DeepSeek-V3.2 geometry, FP8 128x128 weights), DP attention + EP over N GPUs."""
     import torch
     from inference_optimizations_b200.parallel import dist as D
 
@@ -327,7 +328,7 @@ def bench_dsa(args) -> int:
         "correctness": r["check"],
         "kv_pool_capacity_at_boot": r["kv_pool"],
         "max_mem_gb": r["max_mem_gb"],
-        "vs_baseline_note": ("BASELINE.md row 4 (1,813-1,996 steady tok/s at 64 sessions on 8 x B200) is a 61-layer "
+        "vs_baseline_note": ("the published reference figure (1,813-1,996 steady tok/s at 64 sessions on 8 x B200) is a 61-layer "
                              "number; see full_depth.vs_baseline (--full-depth)"),
         "impl": "ours",
     }
@@ -341,7 +342,7 @@ def bench_dsa(args) -> int:
         D.shutdown()
     return 0
 def bench_gemma(args) -> int:
-    """Gemma-class dense GQA model, tensor parallel over the N GPUs, decode throughput over 32
+    """The Gemma-class serving config: dense GQA model, tensor parallel over the N GPUs, decode throughput over 32
     sessions whose 32k-token prompts are in the paged pool."""
     import torch
     from inference_optimizations_b200.config import EngineConfig, model_config

@@ -140,11 +140,11 @@ class MLAMoEConfig:
 
 
 PRESETS: dict[str, Any] = {
-    # dense GQA hd512 model (Gemma class, 31B)
+    # dense GQA hd512 model (Gemma class, 31B): the tensor-parallel serving benchmark model
     "gemma31b": lambda: GQAConfig(),
-    # DSA+MoE model (DeepSeek-V3-class) with FP8 128x128 block-scaled weights
+    # DSA+MoE model (DeepSeek-V3-class) with FP8 128x128 block-scaled weights: the flagship serving benchmark model
     "dsa_moe": lambda: MLAMoEConfig(),
-    # long-context MLA-DSA MoE (GLM-5 class) with NVFP4 experts
+    # long-context MLA-DSA MoE (GLM-5 class) with NVFP4 experts (context-parallel decode)
     "glm5": lambda: MLAMoEConfig(name="glm5", num_layers=78, hidden=6144, num_heads=64, q_lora=2048, qk_nope=192,
                                  qk_rope=64, v_head=256, index_heads=32, num_experts=160, topk=8, expert_ffn=2048,
                                  dense_ffn=12288, n_group=1, topk_group=1, routed_scale=2.5,

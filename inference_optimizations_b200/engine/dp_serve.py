@@ -1,4 +1,4 @@
-"""Data-parallel attention + expert-parallel MoE serving benchmark for the MLA + DSA + MoE family (BASELINE config 3
+"""Data-parallel attention + expert-parallel MoE serving benchmark for the MLA + DSA + MoE family (the flagship serving config
 shape: DeepSeek-V3.2 geometry, FP8 block-scaled experts, EP over every GPU of the node).  One process per GPU:
 
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 --master-port P \\

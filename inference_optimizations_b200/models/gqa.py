@@ -1,4 +1,4 @@
-"""Dense GQA decoder with interleaved sliding-window / global layers (Gemma class), tensor parallel.
+"""Dense GQA decoder with interleaved sliding-window / global layers (Gemma class, 31B), tensor parallel.
 
 Per layer (Gemma-3 block): x = norm_in(h); qkv = x W_qkv; q, k = qk-norm + RoPE; k, v -> paged pool (fused kernel);
 a = attention(q, pool); o = a W_o (TP all-reduce); h += norm_post_attn(o); x = norm_pre_ffn(h);

@@ -1,4 +1,4 @@
-"""MLA + DSA + MoE decoder (DeepSeek-V3.2 / GLM-5 class; BASELINE configs 3 and 5), single GPU.
+"""MLA + DSA + MoE decoder (DeepSeek-V3.2 / GLM-5 class), single GPU.
 
 Per layer (pre-norm):
   x = norm_in(h)

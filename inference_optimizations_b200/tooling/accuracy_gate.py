@@ -16,7 +16,7 @@ Both engines hold the same random-init weights (same seed), so the comparison is
 format).  Exact-match items come from a JSONL file of token ids (`{"prompt_ids": [...], "answer_ids": [...]}` per
 line, e.g. a tokenized GSM8K test split; nothing is fetched from the network) or, without one, from a pinned oracle:
 the greedy continuation of the same model with bf16 KV, so "correct" means "the answer full precision gives".  The
-BASELINE target is KL <= 0.03 vs bf16 KV.
+The target for a 4-bit KV pool is KL <= 0.03 against bf16 KV.
 """
 from __future__ import annotations
 

@@ -1,5 +1,5 @@
-"""Kernel microbenchmarks (CUDA-event timed, warm, inputs larger than L2 unless stated) for the ncu summaries in
-profiles/.  Usage:
+"""Kernel microbenchmarks (CUDA-event timed, warm, inputs larger than L2 unless stated), the small cases the ncu
+captures run.  Usage:
 
     python -m inference_optimizations_b200.utils.microbench gqa_decode --b 8 --ctx 8192 --d 512 --fmt nvfp4
     python -m inference_optimizations_b200.utils.microbench mla_decode --b 64 --heads 128 --ctx 131072 --fmt nvfp4
@@ -171,7 +171,7 @@ def mla_pool_random(rows: int, fmt: int, dev, distinct: int = 1 << 16, seed: int
 
 
 def mla_decode_case(b: int, heads: int, ctx: int, topk: int, fmt_name: str, n_q: int = 1, launches: int = 0) -> dict:
-    """BASELINE config 2 shape: b sequences x n_q query tokens, `heads` heads x 576, `ctx` cached tokens each in a
+    """The sparse-MLA decode microbenchmark shape: b sequences x n_q query tokens, `heads` heads x 576, `ctx` cached tokens each in a
     page-64 pool, top-`topk` positions per token from a random-normal indexer score, mapped through a random page
     table to pool rows."""
     from ..ops import kvcache as K

@@ -1,4 +1,4 @@
-"""Sparse MLA (DSA) decode on CPU: the fp32 oracle and BASELINE config 1 (NVFP4 KV quantize + dequant-gather +
+"""Sparse MLA (DSA) decode on CPU: the fp32 oracle and the CPU plumbing config (NVFP4 KV quantize + dequant-gather +
 sparse MLA decode against unquantized attention), plus the split planner."""
 import math
 
