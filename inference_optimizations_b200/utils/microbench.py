@@ -170,7 +170,8 @@ def mla_pool_random(rows: int, fmt: int, dev, distinct: int = 1 << 16, seed: int
     return base.repeat(reps, 1)[:rows].contiguous()
 
 
-def mla_decode_case(b: int, heads: int, ctx: int, topk: int, fmt_name: str, n_q: int = 1, launches: int = 0) -> dict:
+def mla_decode_case(b: int, heads: int, ctx: int, topk: int, fmt_name: str, n_q: int = 1, launches: int = 0,
+                    splits_override: str = "") -> dict:
     """The sparse-MLA decode microbenchmark shape: b sequences x n_q query tokens, `heads` heads x 576, `ctx` cached tokens each in a
     page-64 pool, top-`topk` positions per token from a random-normal indexer score, mapped through a random page
     table to pool rows."""
@@ -191,6 +192,8 @@ def mla_decode_case(b: int, heads: int, ctx: int, topk: int, fmt_name: str, n_q:
     del scores
     q = torch.randn(t, heads, 576, device=dev, generator=gen).to(torch.bfloat16)
     splits = M.mla_split_policy(t, topk)
+    if splits_override:                       # "num_splits,tiles_per_split"
+        splits = tuple(int(v) for v in splits_override.split(","))
     ws = M.MlaWorkspace.allocate(t, heads, splits[0], device=dev)
     out = torch.empty(t, heads, 512, dtype=torch.bfloat16, device=dev)
     sm = M.mla_sm_scale()
@@ -867,7 +870,8 @@ def main() -> None:
     p.add_argument("--fmt", default="nvfp4")
     p.add_argument("--nq", type=int, default=1)
     p.add_argument("--chunk", type=int, default=2048)
-    p.add_argument("--splits", default="", help="gqa_decode: force (num_splits,tiles_per_split)")
+    p.add_argument("--splits", default="", help="gqa_decode: force (num_splits,tiles_per_split); mla_decode: "
+                                                "';'-separated list of such pairs to sweep")
     p.add_argument("--window", type=int, default=0)
     p.add_argument("--topk", type=int, default=2048)
     p.add_argument("--launches", type=int, default=0)
@@ -959,7 +963,11 @@ def main() -> None:
             dist.barrier()
             dist.destroy_process_group()
     elif a.kernel == "mla_decode":
-        r = mla_decode_case(a.b, a.heads, a.ctx, a.topk, a.fmt, a.nq, a.launches)
+        for sp in (a.splits.split(";") if a.splits else [""]):
+            row = mla_decode_case(a.b, a.heads, a.ctx, a.topk, a.fmt, a.nq, a.launches, sp)
+            if row:
+                print(json.dumps(row), flush=True)
+        r = {}
     else:
         raise SystemExit(f"unknown kernel {a.kernel}")
     if r:
