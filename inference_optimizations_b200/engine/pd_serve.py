@@ -48,6 +48,9 @@ class PDPair:
         if ecfg.spec or max(1, ecfg.ep) > 1 or max(1, ecfg.dcp) > 1 or ecfg.prefix_cache:
             raise ValueError("prefill / decode pairs run without speculation, expert / context parallelism and the "
                              "prefix cache")
+        if getattr(cfg, "kda_every", 0) or ecfg.kv_dtype == "kvmix":
+            raise ValueError("prefill / decode pairs move paged KV only: hybrid KDA models (recurrent states) and "
+                             "kvmix pools are not transferred")
         dev = torch.device(ecfg.device)
         self.pools = {}
         # without GPUs (gloo ranks) the pages travel inside the host messages instead of over peer memory: the same
