@@ -7,12 +7,12 @@ same order (the HTTP front end broadcasts them, `server/http.py`), so the per-st
 from __future__ import annotations
 
 import time
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import Optional
 
 import torch
 
-from ..config import EngineConfig, GQAConfig, MLAMoEConfig, model_config
+from ..config import EngineConfig, GQAConfig, model_config
 from .runner import GQARunner
 from .scheduler import Request, SamplingParams, Scheduler
 from .spec_policy import SpecPolicy

@@ -13,14 +13,13 @@ position.
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 from typing import Callable, Optional
 
 import torch
 
 from ..config import EngineConfig, GQAConfig
-from ..kv.allocator import DUMMY_PAGE, OutOfPages, RequestPages
+from ..kv.allocator import RequestPages
 from ..models.gqa import GQAKVCache, GQAModel, StepTensors
 from ..ops import attention as A
 from ..ops import basic as B
