@@ -1,7 +1,8 @@
 """Per-step rooflines at served shapes: for every op the floor max(HBM bytes / bandwidth, FLOPs / tensor peak), and
 the NVLink floor of the collectives, per GPU (the reference's `tooling/rooflines/*_roofline.py` method,
 `pro_roofline.py:1-35`, `glm_roofline.py:1-60`).  Peaks come from MEASURED_PEAKS.json (copy bandwidth, cuBLAS bf16)
-when present, else the nominal B200 figures; NVLink uses the measured 770 GB/s per direction per GPU.
+when present, else an earlier measurement on this kind of B200 (6.65 TB/s, 1.59 PFLOP/s); NVLink uses the measured 770
+GB/s per direction per GPU.
 
     python -m inference_optimizations_b200.tooling.rooflines --model gemma31b --batch 32 --ctx 32768 --tp 1
     python -m inference_optimizations_b200.tooling.rooflines --model dsa_moe --batch 64 --ctx 8192 --ep 8
@@ -15,12 +16,14 @@ from dataclasses import dataclass
 
 from ..config import GQAConfig, MLAMoEConfig, model_config
 
-NOMINAL = {"hbm_gbs": 7700.0, "bf16_tflops": 2250.0, "nvlink_gbs": 770.0}
+# without MEASURED_PEAKS.json: an earlier copy-bandwidth / cuBLAS measurement on this kind of B200 (not the nominal
+# 7.7 TB/s / 2.25 PFLOP/s, which no kernel reaches)
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "nvlink_gbs": 770.0}
 KV_BYTES = {"bf16": 2.0, "fp8": 1.0, "nvfp4": 0.5 + 1.0 / 16}      # per element incl. block scales
 
 
 def peaks() -> dict:
-    p = dict(NOMINAL)
+    p = dict(FALLBACK)
     path = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
     if os.path.exists(path):
         with open(path) as f:
@@ -28,7 +31,7 @@ def peaks() -> dict:
         p.update({k: float(d[k]) for k in ("hbm_gbs", "bf16_tflops") if k in d})
         p["source"] = "measured"
     else:
-        p["source"] = "nominal"
+        p["source"] = "fallback"
     return p
 
 
@@ -79,16 +82,19 @@ def mla_decode_ops(cfg: MLAMoEConfig, batch: int, ctx: int, kv: str, ep: int) ->
         ops.append(Op(f"L{i}.sparse_mla", batch * topk * row,
                       2 * batch * cfg.num_heads * topk * (cfg.kv_lora + cfg.qk_rope + cfg.kv_lora), fp8=True))
         if cfg.is_moe(i):
-            # experts touched per GPU per step: all local experts once tokens spread over them
+            # experts touched per GPU per step under uniform routing: of E experts, batch * ep * topk pairs leave
+            # E (1 - (1 - 1/E)^pairs) distinct ones touched, 1 / ep of them local
             local = cfg.num_experts // ep
             tokens = batch * ep * cfg.topk / ep          # token-expert pairs landing on this GPU
-            ew = min(local, max(1.0, tokens)) * 3 * h * cfg.expert_ffn
+            touched = local * (1.0 - (1.0 - 1.0 / cfg.num_experts) ** (batch * ep * cfg.topk))
+            ew = max(1.0, touched) * 3 * h * cfg.expert_ffn
             sh = cfg.num_shared * 3 * h * cfg.expert_ffn
             ops.append(Op(f"L{i}.experts", ew + sh, 2 * (tokens + batch * cfg.num_shared) * 3 * h * cfg.expert_ffn,
                           nvlink_bytes=2 * batch * cfg.topk * h * (ep - 1) / ep if ep > 1 else 0.0, fp8=True))
         else:
             ops.append(Op(f"L{i}.mlp", 3 * h * cfg.dense_ffn, 2 * batch * 3 * h * cfg.dense_ffn, fp8=True))
-    ops.append(Op("lm_head", cfg.vocab * h * 2, 2 * batch * cfg.vocab * h))
+    fp8 = cfg.weight_dtype == "fp8"
+    ops.append(Op("lm_head", cfg.vocab * h * (1 if fp8 else 2), 2 * batch * cfg.vocab * h, fp8=fp8))
     return ops
 
 
@@ -112,8 +118,9 @@ def main(argv=None) -> None:
     ap.add_argument("--kv", default="nvfp4")
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--ep", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=0, help="truncate the model to this many layers (0: all)")
     a = ap.parse_args(argv)
-    cfg = model_config(a.model)
+    cfg = model_config(a.model, **({"num_layers": a.layers} if a.layers else {}))
     ops = gqa_decode_ops(cfg, a.batch, a.ctx, a.kv, a.tp) if isinstance(cfg, GQAConfig) else \
         mla_decode_ops(cfg, a.batch, a.ctx, a.kv, a.ep)
     print(json.dumps({"model": a.model, "batch": a.batch, "ctx": a.ctx, "kv": a.kv, "tp": a.tp, "ep": a.ep,
