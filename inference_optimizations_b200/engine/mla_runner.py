@@ -75,8 +75,8 @@ class MLARunner:
             self.ep_T_max = max(2 * ecfg.max_running, min(ecfg.chunked_prefill, 1024))
             self.model.attach_ep(ep_group, self.ep_T_max)
         self.mixed = ecfg.kv_dtype == "kvmix"
-        if self.mixed and (self.dcp_world > 1 or ecfg.prefix_cache or kv_storage is not None):
-            raise NotImplementedError("kvmix pools run without context parallelism, the prefix cache or placed pools")
+        if self.mixed and (self.dcp_world > 1 or kv_storage is not None):
+            raise NotImplementedError("kvmix pools run without context parallelism or placed pools")
         fmt = FMT_NVFP4 if ecfg.kv_dtype == "nvfp4" else FMT_FP8
         self.max_running = ecfg.max_running
         per_req = (max_seq + 64 + 63) // 64 + 1
@@ -107,8 +107,9 @@ class MLARunner:
         self.prefix_cache = None
         if cfg.kda_every and self.spec:
             raise NotImplementedError("hybrid KDA models run without the MTP draft")
-        # hybrid models: a cached prefix's pages hold no KDA recurrent state, so prefixes are not reused
-        if ecfg.prefix_cache and not cfg.kda_every:
+        # prefixes are not reused by hybrid models (a cached prefix's pages hold no KDA recurrent state) nor in kvmix
+        # pools (a promotion would move pages other requests share)
+        if ecfg.prefix_cache and not cfg.kda_every and not self.mixed:
             from ..kv.radix import RadixCache
             self.prefix_cache = RadixCache(self.kv.alloc)
 
