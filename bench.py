@@ -131,31 +131,13 @@ def _tokens_check(eng, dev) -> dict:
                         "NCCL EP (all-gather + all-to-all), every rank"}
 
 
-def _pool_capacity(eng, cfg, dev) -> dict:
-    """KV-pool capacity at boot on this GPU, this model: the memory free after the weights (plus what the running
-    pool itself took) sized into pages the way the engine sizes a memory-bound pool (`mla_runner.pool_pages`:
-    mem_fraction of the free memory less a reserve), for the NVFP4 352-byte and the FP8 576-byte latent rows (+ the
-    132-byte index key each); the bench's own pool holds just what its sessions need."""
-    import torch
-    from inference_optimizations_b200.ops.formats import INDEX_ROW_BYTES
-    from inference_optimizations_b200.ops.mla import ROW_BYTES, FMT_FP8, FMT_NVFP4
-    kv = eng.runner.kv
-    own = sum(t.numel() for t in kv.latent + kv.index + (kv.latent4 or []))
-    free, _ = torch.cuda.mem_get_info(dev)
-    avail = max(0, free + own - (8 << 30)) * eng.ecfg.mem_fraction
-    tok = {name: int(avail // (cfg.num_layers * (ROW_BYTES[f] + INDEX_ROW_BYTES)))
-           for name, f in (("nvfp4", FMT_NVFP4), ("fp8", FMT_FP8))}
-    return {"tokens_nvfp4": tok["nvfp4"], "tokens_fp8": tok["fp8"],
-            "ratio_nvfp4_vs_fp8": round(tok["nvfp4"] / max(1, tok["fp8"]), 3),
-            "note": "latent + index-key bytes of every layer per token, in the memory free at boot after the weights"}
-
-
 def run_dsa(args, info, dev, layers: int, steps: int, warm: int) -> dict:
     """One DSA-MoE serving run (prefill every prompt, then timed decode steps); the measurements as a dict."""
     import torch
     import torch.distributed as dist
     from inference_optimizations_b200.config import EngineConfig, model_config
     from inference_optimizations_b200.engine.engine import Engine
+    from inference_optimizations_b200.engine.mla_runner import pool_capacity
     from inference_optimizations_b200.engine.scheduler import SamplingParams
     from inference_optimizations_b200.parallel import dist as D
     from inference_optimizations_b200.utils.clocks import ClockSampler, rejected
@@ -174,7 +156,7 @@ def run_dsa(args, info, dev, layers: int, steps: int, warm: int) -> dict:
                  ep_group=dist.group.WORLD if n > 1 else None)
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t_build
-    pool = _pool_capacity(eng, cfg, dev)
+    pool = pool_capacity(eng.runner)
     g = torch.Generator().manual_seed(1000 + rank)
     reqs = [eng.add_request(torch.randint(1, cfg.vocab, (args.ctx,), generator=g).tolist(),
                             SamplingParams(max_new_tokens=args.max_new)) for _ in range(per)]

@@ -39,6 +39,25 @@ def pool_pages(ecfg: EngineConfig, need: int, page_bytes: int, device) -> int:
     return need
 
 
+def pool_capacity(runner) -> dict:
+    """KV-pool capacity at boot on this device for this runner's model: the memory free after the weights (plus what
+    the runner's own pools took) sized the way `pool_pages` sizes a memory-bound pool (`mem_fraction` of it, less the
+    8 GB activation reserve), in tokens for the NVFP4 352-byte and the FP8 576-byte latent rows (+ the 132-byte index
+    key each, every layer)."""
+    from ..ops.formats import INDEX_ROW_BYTES
+    from ..ops.mla import FMT_FP8, FMT_NVFP4, ROW_BYTES
+    kv = runner.kv
+    own = sum(t.numel() for t in kv.latent + kv.index + (getattr(kv, "latent4", None) or []))
+    free, _ = torch.cuda.mem_get_info(runner.device)
+    avail = max(0, free + own - (8 << 30)) * runner.ecfg.mem_fraction
+    layers = runner.cfg.num_layers
+    tok = {name: int(avail // (layers * (ROW_BYTES[f] + INDEX_ROW_BYTES)))
+           for name, f in (("nvfp4", FMT_NVFP4), ("fp8", FMT_FP8))}
+    return {"tokens_nvfp4": tok["nvfp4"], "tokens_fp8": tok["fp8"],
+            "ratio_nvfp4_vs_fp8": round(tok["nvfp4"] / max(1, tok["fp8"]), 3),
+            "note": "latent + index-key bytes of every layer per token, in the memory free at boot after the weights"}
+
+
 class MLARunner:
     def __init__(self, cfg: MLAMoEConfig, ecfg: EngineConfig, device, max_seq: int, tp_rank: int = 0, tp: int = 1,
                  ep_rank: int = 0, ep_group=None, dcp_rank: int = 0, dcp_group=None, kv_storage=None):

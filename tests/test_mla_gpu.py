@@ -53,6 +53,44 @@ def test_mla_model_gpu_vs_cpu_oracles(cuda, kv):
     assert all(len(o) == 6 for o in out)
 
 
+@pytest.mark.parametrize("dn,dv,hi,efmt", [(128, 128, 64, "fp8"), (192, 256, 32, "nvfp4")])
+def test_fused_glue_head_geometries_vs_cpu_oracle(cuda, dn, dv, hi, efmt):
+    """The fused attention glue (`mla_prep_kv` / `mla_prep_q`, the FP8 a / b / o projections, the head-batched W_UK
+    and W_UV products, the indexer) at the DeepSeek-V3.2 head geometry (q_nope 128, v 128, 64 indexer heads) and the
+    GLM-5 one (q_nope 192, v 256, 32 indexer heads, NVFP4 experts): prefill logits stay close to the fp32-oracle
+    forward of the same weights on the CPU, and decode steps run end to end."""
+    from inference_optimizations_b200.engine.scheduler import Request, Segment
+    over = dict(hidden=256, num_heads=8, q_lora=256, qk_nope=dn, v_head=dv, index_heads=hi, weight_dtype="fp8",
+                expert_dtype=efmt, expert_ffn=256, dense_ffn=512)
+    cfg = model_config("tiny_mla", **over)
+    engines = []
+    for dev in (str(cuda), "cpu"):
+        ecfg = EngineConfig(model="tiny_mla", device=dev, kv_dtype="nvfp4", max_running=4, chunked_prefill=128,
+                            cuda_graphs=False, prefix_cache=False)
+        engines.append(Engine(ecfg, cfg, max_seq=256))
+    gpu, cpu = engines
+    mg = gpu.runner.model
+    assert all(mg._fused_glue(mg.layers[i]) for i in range(cfg.num_layers))
+    cpu.runner.model.copy_from(mg)
+    torch.manual_seed(5)
+    prompt = torch.randint(0, cfg.vocab, (90,)).tolist()
+    logits = []
+    for eng in (gpu, cpu):
+        r = Request(rid=0, prompt=prompt, params=SamplingParams(max_new_tokens=1))
+        r.slot = 0
+        eng.runner.attach(r)
+        st, _ = eng.runner._step([Segment(r, 0, prompt, True)])
+        x = eng.runner.model.forward(st, eng.runner.kv)
+        logits.append(eng.runner.model.logits(x).float().cpu())
+        eng.runner.detach(r)
+    cos = torch.nn.functional.cosine_similarity(logits[0], logits[1], dim=-1)
+    assert cos.mean().item() > 0.98 and cos.min().item() > 0.9, (cos.mean().item(), cos.min().item())
+    out = gpu.generate([prompt[:70], prompt[:9]], SamplingParams(max_new_tokens=5))
+    assert all(len(o) == 5 for o in out)
+    for d in (gpu.runner.kv.idx_ws, gpu.runner.kv.mla_ws):
+        assert all(int(ws.status.item()) == 0 for ws in d.values())
+
+
 @pytest.mark.parametrize("fmt", ["fp8", "nvfp4"])
 def test_block_scaled_experts_in_model(cuda, fmt):
     """The MLA model with FP8 / NVFP4 block-scaled experts (grouped tcgen05 GEMMs) tracks its bf16 twin."""
