@@ -326,6 +326,129 @@ __global__ void __launch_bounds__(kKThreads) indexer_topk_kernel(const IndexerAr
   }
 }
 
+// Cluster form for long rows (16,384 < positions <= kClMax x kClKeys x kKThreads = 262,144): the row is split into
+// CL contiguous spans, one per CTA of a thread-block cluster, each span's order keys held in registers (up to
+// kClKeys per thread).  Each radix pass builds one histogram per CTA; every CTA then sums the CL histograms of its
+// bins over distributed shared memory and takes the same threshold decision, so the select costs one round of
+// global loads spread over CL SMs instead of one SM re-reading the row five times.  The compaction keeps position
+// order across the cluster: a CTA's outputs start after the keys above the threshold, and the equal keys taken, of
+// the spans before it.  All waits are the cluster's hardware barriers, which every CTA of the cluster reaches (the
+// branch on the row length is the same for the whole cluster).
+constexpr int kClKeys = 32;
+constexpr int kClMax = 8;
+
+__global__ void __launch_bounds__(kKThreads, 1) indexer_topk_cluster_kernel(const IndexerArgs a) {
+  __shared__ int hist[4096];
+  __shared__ int warp_sums[33];
+  __shared__ int sel_bin, sel_above;
+  __shared__ int sums[4096];                 // the cluster-wide counts of the bins this CTA's threads own
+  __shared__ int counts[2];                  // this span's keys above the threshold / equal to it
+  const int t = blockIdx.y;
+  const int cr = static_cast<int>(cluster_ctarank()), cn = static_cast<int>(cluster_nctarank());
+  const int L = min(a.limit[t], a.score_stride);
+  const int K = a.topk;
+  const float* sc = a.scores + static_cast<size_t>(t) * a.score_stride;
+  const int* pt = a.page_table + static_cast<size_t>(a.req_idx ? a.req_idx[t] : t) * a.pt_stride;
+  int* out = a.out_slots + static_cast<size_t>(t) * K;
+  int* out_pos = a.out_pos ? a.out_pos + static_cast<size_t>(t) * K : nullptr;
+  auto emit = [&](int i, int p) {
+    out[i] = p >= 0 ? pt[p >> 6] * 64 + (p & 63) : -1;
+    if (out_pos) out_pos[i] = p;
+  };
+  if (L <= K) {
+    if (cr == 0)
+      for (int i = threadIdx.x; i < K; i += kKThreads) emit(i, i < L ? i : -1);
+    return;
+  }
+  // this CTA's span [c0, c1) and this thread's n positions from i0 in it (multiples of 4: 16-byte loads)
+  const int span = ((L + cn - 1) / cn + 3) & ~3;               // <= kClKeys x kKThreads (host-side bound)
+  const int c0 = min(L, cr * span), c1 = min(L, c0 + span);
+  const int chunk = ((span + kKThreads - 1) / kKThreads + 3) & ~3;
+  const int i0 = c0 + threadIdx.x * chunk, n = max(0, min(c1, i0 + chunk) - i0);
+  uint32_t keys[kClKeys];
+#pragma unroll
+  for (int j = 0; j < kClKeys; j += 4) {
+    if (j + 3 < n) {
+      const float4 v = *reinterpret_cast<const float4*>(sc + i0 + j);
+      keys[j] = order_key(v.x);
+      keys[j + 1] = order_key(v.y);
+      keys[j + 2] = order_key(v.z);
+      keys[j + 3] = order_key(v.w);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) keys[j + q] = j + q < n ? order_key(sc[i0 + j + q]) : 0u;
+    }
+  }
+  const uint32_t hist_addr = smem_u32(hist);
+  uint32_t prefix = 0, mask = 0;
+  int remaining = K;
+  const int shifts[3] = {20, 8, 0};
+  const int widths[3] = {12, 12, 8};
+#pragma unroll 1
+  for (int pass = 0; pass < 3; ++pass) {
+    const int sh = shifts[pass], nb = 1 << widths[pass];
+    for (int b = threadIdx.x; b < 4096; b += kKThreads) hist[b] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kClKeys; ++j)
+      if (j < n && (keys[j] & mask) == prefix) atomicAdd(&hist[(keys[j] >> sh) & (nb - 1)], 1);
+    cluster_sync_all();                      // every span's histogram complete and visible to the cluster
+    // this thread's `per` bins (thread 0 the highest), summed over the cluster's histograms in CTA order
+    const int per = nb / kKThreads > 0 ? nb / kKThreads : 1;
+    const int b0 = nb - (threadIdx.x + 1) * per;
+    int mine = 0;
+    if (b0 >= 0)
+      for (int k = 0; k < per; ++k) {
+        int c = 0;
+        for (int r = 0; r < cn; ++r) c += static_cast<int>(ld_cluster_u32(mapa_shared(hist_addr + 4u * (b0 + k), r)));
+        sums[b0 + k] = c;
+        mine += c;
+      }
+    int total;
+    const int above = block_exclusive_scan(mine, warp_sums, total);
+    if (b0 >= 0 && above < remaining && above + mine >= remaining) {
+      int acc = above;
+      for (int k = per - 1; k >= 0; --k) {
+        const int c = sums[b0 + k];
+        if (acc + c >= remaining) { sel_bin = b0 + k; sel_above = acc; break; }
+        acc += c;
+      }
+    }
+    __syncthreads();
+    remaining -= sel_above;
+    prefix |= static_cast<uint32_t>(sel_bin) << sh;
+    mask |= static_cast<uint32_t>(nb - 1) << sh;
+    cluster_sync_all();                      // no CTA clears its histogram while another still reads it
+  }
+  // ---- compaction in position order across the cluster
+  int gt = 0, eq = 0;
+#pragma unroll
+  for (int j = 0; j < kClKeys; ++j)
+    if (j < n) {
+      gt += keys[j] > prefix;
+      eq += keys[j] == prefix;
+    }
+  int gt_span, eq_span;
+  const int eq_before = block_exclusive_scan(eq, warp_sums, eq_span);
+  block_exclusive_scan(gt, warp_sums, gt_span);
+  if (threadIdx.x == 0) { counts[0] = gt_span; counts[1] = eq_span; }
+  cluster_sync_all();
+  int gt_prev = 0, eq_prev = 0;               // the spans before this one
+  const uint32_t counts_addr = smem_u32(counts);
+  for (int r = 0; r < cr; ++r) {
+    gt_prev += static_cast<int>(ld_cluster_u32(mapa_shared(counts_addr, r)));
+    eq_prev += static_cast<int>(ld_cluster_u32(mapa_shared(counts_addr + 4u, r)));
+  }
+  cluster_sync_all();                        // last remote read: a CTA may exit after this barrier
+  const int take_eq = max(0, min(eq, remaining - eq_prev - eq_before));
+  int tot;
+  const int off = gt_prev + min(eq_prev, remaining) + block_exclusive_scan(gt + take_eq, warp_sums, tot);
+  int w = off, eq_seen = 0;
+#pragma unroll
+  for (int j = 0; j < kClKeys; ++j)
+    if (j < n && (keys[j] > prefix || (keys[j] == prefix && eq_seen++ < take_eq))) emit(w++, i0 + j);
+}
+
 }  // namespace
 
 cudaError_t indexer_logits(const IndexerArgs& a, cudaStream_t s) {
@@ -341,10 +464,27 @@ cudaError_t indexer_logits(const IndexerArgs& a, cudaStream_t s) {
 cudaError_t indexer_topk(const IndexerArgs& a, cudaStream_t s) {
   if (a.T == 0) return cudaSuccess;
   if (a.topk < 1) return cudaErrorInvalidValue;
-  if (a.score_stride <= kRegKeys * kKThreads)
+  constexpr int kClSpan = kClKeys * kKThreads;
+  if (a.score_stride <= kRegKeys * kKThreads) {
     indexer_topk_kernel<true><<<a.T, kKThreads, 0, s>>>(a);
-  else
+  } else if (a.score_stride <= kClMax * kClSpan && a.T <= 65535) {
+    const unsigned cl = static_cast<unsigned>((a.score_stride + kClSpan - 1) / kClSpan);   // 1 .. 8 CTAs per row
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cl, a.T);
+    cfg.blockDim = dim3(kKThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, indexer_topk_cluster_kernel, a);
+  } else {
     indexer_topk_kernel<false><<<a.T, kKThreads, 0, s>>>(a);
+  }
   return cudaGetLastError();
 }
 

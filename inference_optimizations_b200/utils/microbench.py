@@ -245,7 +245,8 @@ def indexer_case(b: int, ctx: int, topk: int, heads: int = 64, launches: int = 0
     nbytes = b * ctx * 132
     return {"kernel": "indexer_logits+topk", "tokens": b, "ctx": ctx, "topk": topk, "heads": heads,
             "us": round(us, 2), "bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1),
-            "frac_hbm": round(nbytes / us / 1e3 / PEAKS["hbm_gbs"], 3), "l2": "flushed before each launch"}
+            "frac_hbm": round(nbytes / us / 1e3 / PEAKS["hbm_gbs"], 3), "l2": "flushed before each launch",
+            "kernels_us": _kernel_times(fn)}
 
 
 def hotops_case(op: str, t: int, hidden: int = 7168, experts: int = 256, launches: int = 0) -> dict:
@@ -797,13 +798,14 @@ def kv4mla_compare_case(tokens: list, topk: int = 2048, rows: int = 600000, head
 
 
 def dsa_profile_case(layers: int, sessions: int, ctx: int, steps: int, prefill: int, top: int = 40,
-                     trace_out: str = "") -> dict:
+                     trace_out: str = "", model: str = "dsa_moe") -> dict:
     """Per-kernel device time of the DSA-MoE serving step (the bench's engine: DP attention + EP over the launched
     ranks, CUDA-graph decode), from the CUDA activity records of the torch profiler (kernel durations as CUPTI reports
     them; the shares, not the absolutes, are the point: the bench's own CUDA-event timing is the throughput figure).
     Sessions hold `ctx` positions of random well-formed KV written by the pool writers (no prefill compute before the
     decode steps); with `prefill` > 0 one more request of that many tokens per rank is prefilled and profiled too.
-    `trace_out`: also write rank 0's decode-step activity as a Chrome trace (kernel order, starts and gaps)."""
+    `trace_out`: also write rank 0's decode-step activity as a Chrome trace (kernel order, starts and gaps).
+    `model`: the MLA + DSA + MoE preset (`dsa_moe`, or `glm5` for the long-context geometry)."""
     import torch.distributed as dist
     from torch.profiler import ProfilerActivity, profile
     from ..config import EngineConfig, model_config
@@ -814,8 +816,8 @@ def dsa_profile_case(layers: int, sessions: int, ctx: int, steps: int, prefill: 
     rank = dist.get_rank() if dist.is_initialized() else 0
     dev = torch.device("cuda", torch.cuda.current_device())
     per = sessions // world
-    cfg = model_config("dsa_moe", num_layers=layers)
-    ecfg = EngineConfig(model="dsa_moe", device=str(dev), kv_dtype="nvfp4", max_running=per + 1,
+    cfg = model_config(model, num_layers=layers)
+    ecfg = EngineConfig(model=model, device=str(dev), kv_dtype="nvfp4", max_running=per + 1,
                         chunked_prefill=max(prefill, 64), graph_batch_sizes=str(per), ep=world, prefix_cache=False)
     eng = Engine(ecfg, cfg, max_seq=ctx + max(prefill, 0) + 256, ep_rank=rank,
                  ep_group=dist.group.WORLD if world > 1 else None)
@@ -890,6 +892,7 @@ def main() -> None:
     p.add_argument("--nt", default="", help="proj_gemms: token tiles to sweep (comma-separated)")
     p.add_argument("--ks", default="", help="proj_gemms: K splits to sweep (comma-separated)")
     p.add_argument("--trace-out", default="", help="dsa_profile: Chrome trace of the decode steps (rank 0)")
+    p.add_argument("--model", default="dsa_moe", help="dsa_profile: MLA + DSA + MoE preset")
     a = p.parse_args()
     if a.kernel == "gqa_decode":
         r = gqa_decode_case(a.b, a.hk, a.hq, a.d, a.ctx, a.fmt, a.nq, a.window, a.launches, a.splits, a.trace)
@@ -958,7 +961,7 @@ def main() -> None:
         if world > 1:
             torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
             dist.init_process_group("nccl", device_id=torch.device("cuda", torch.cuda.current_device()))
-        r = dsa_profile_case(a.layers, a.sessions, a.ctx, a.steps, a.prefill, trace_out=a.trace_out)
+        r = dsa_profile_case(a.layers, a.sessions, a.ctx, a.steps, a.prefill, trace_out=a.trace_out, model=a.model)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()

@@ -308,10 +308,11 @@ def test_gqa_extend(cuda, fmt, d, window):
         assert (dec.float() - out[s0:s0 + m].float()).abs().max().item() < tol
 
 
-@pytest.mark.parametrize("width", [9216, 20480])
-def test_indexer_topk_ties_both_forms(cuda, width):
-    """Top-k selection alone over score rows with many exact ties (the register form for rows up to 16384
-    positions, the re-reading form beyond): the same positions, in position order, as the oracle."""
+@pytest.mark.parametrize("width", [9216, 20480, 70016, 204800, 262144, 300032])
+def test_indexer_topk_ties_every_form(cuda, width):
+    """Top-k selection alone over score rows with many exact ties (the one-CTA register form for rows up to 16384
+    positions, the cluster form of 1 to 8 CTAs up to 262,144, the re-reading form beyond): the same positions, in
+    position order, as the oracle."""
     from inference_optimizations_b200._ext import ext
     from inference_optimizations_b200.ops import indexer as I
     torch.manual_seed(2)
