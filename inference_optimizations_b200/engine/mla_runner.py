@@ -18,7 +18,7 @@ from ..models.mla import MLAKVCache, MLAModel, MLAStep
 from ..ops import basic as B
 from ..ops import formats as M_FMT
 from ..ops import kvcache as K_OPS
-from ..ops.kvcache import FMT_FP8, FMT_NVFP4
+from ..ops.kvcache import FMT_BF16, FMT_FP8, FMT_NVFP4
 from .scheduler import Batch, Request, SamplingParams, Segment
 from ..ops.formats import INDEX_ROW_BYTES
 from ..ops.mla import ROW_BYTES as M_ROW_BYTES
@@ -96,7 +96,17 @@ class MLARunner:
         self.mixed = ecfg.kv_dtype == "kvmix"
         if self.mixed and (self.dcp_world > 1 or kv_storage is not None):
             raise NotImplementedError("kvmix pools run without context parallelism or placed pools")
-        fmt = FMT_NVFP4 if ecfg.kv_dtype == "nvfp4" else FMT_FP8
+        fmts = {"nvfp4": FMT_NVFP4, "fp8": FMT_FP8, "kvmix": FMT_FP8, "bf16": FMT_BF16}
+        if ecfg.kv_dtype not in fmts:
+            raise ValueError(f"MLA latent pools hold nvfp4, fp8, kvmix or bf16 rows, not {ecfg.kv_dtype!r}")
+        fmt = fmts[ecfg.kv_dtype]
+        # bf16: unquantized 1152-byte rows, the accuracy reference of the quantized pools; no kernel reads them, so the
+        # attention block runs its torch form (separate writers, fp32 attention) and decode steps are not graphed
+        self.ref_pool = fmt == FMT_BF16
+        if self.ref_pool:
+            if self.dcp_world > 1 or kv_storage is not None:
+                raise NotImplementedError("the bf16 reference pool runs without context parallelism or placed pools")
+            self.model.fuse_glue = False
         self.max_running = ecfg.max_running
         per_req = (max_seq + 64 + 63) // 64 + 1
         n_layers = cfg.num_layers + int(self.spec)
@@ -490,7 +500,7 @@ class MLARunner:
         the host)."""
         # context parallelism: the merge and reduce kernels pick their buffer half on the host, per call
         return (self.ecfg.cuda_graphs and self.device.type == "cuda" and not self.spec and self.dcp_world == 1
-                and all(self.model._quantized_ffn(i) for i in range(self.cfg.num_layers)))
+                and not self.ref_pool and all(self.model._quantized_ffn(i) for i in range(self.cfg.num_layers)))
 
     def _decode_body(self, st: MLAStep, out: torch.Tensor) -> None:
         x = self.model.forward(st, self.kv)

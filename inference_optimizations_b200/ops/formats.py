@@ -37,6 +37,7 @@ MLA_SCALE_OFF = MLA_NOPE // 2         # 256
 MLA_ROPE_OFF = MLA_SCALE_OFF + MLA_NOPE // FP4_BLOCK   # 288
 MLA_ROW_BYTES = MLA_ROPE_OFF + MLA_ROPE                # 352
 MLA_FP8_ROW_BYTES = MLA_QK                             # 576
+MLA_BF16_ROW_BYTES = 2 * MLA_QK                        # 1152: unquantized bf16 row (the accuracy reference pool)
 INDEX_DIM = 128
 INDEX_ROW_BYTES = INDEX_DIM + 4                        # 132
 

@@ -140,7 +140,13 @@ def gqa_prep(qkv: torch.Tensor, q_norm: Optional[torch.Tensor], k_norm: Optional
 
 
 def mla_write(nope: torch.Tensor, rope: torch.Tensor, slot: torch.Tensor, pool: torch.Tensor) -> None:
-    """Latent rows into an MLA pool ([slots, 352] NVFP4 or [slots, 576] FP8); slot -1 skipped."""
+    """Latent rows into an MLA pool ([slots, 352] NVFP4, [slots, 576] FP8 or [slots, 1152] unquantized bf16, the
+    accuracy reference); slot -1 skipped."""
+    if pool.shape[-1] == F.MLA_BF16_ROW_BYTES:
+        rows = torch.cat([nope, rope], -1).to(torch.bfloat16).contiguous().view(torch.uint8)
+        keep = slot >= 0
+        pool[slot[keep].long()] = rows[keep]
+        return
     fmt = FMT_NVFP4 if pool.shape[-1] == F.MLA_ROW_BYTES else FMT_FP8
     if nope.is_cuda:
         ext().mla_quant_write(nope, rope, slot.int(), pool, fmt)

@@ -5,7 +5,8 @@ Semantics of the reference's sparse FP4 decode (`kv-cache-4bit/glm-kv4/glm_kv4.p
 the pool rows idx[t, :] (-1 = masked); K = the full row, V = its 512 latent values; returns out [T, H, 512] and the
 natural-log LSE [T, H].  Rows are NVFP4 352-B rows (FMT_NVFP4), E4M3 576-B rows (FMT_FP8) or rope-free NVFP4
 288-B rows (FMT_NVFP4_NOROPE, the GLM-Flash latent) or 320-B / 384-B DeepSeek V4 Pro cells (FMT_V4PRO, E4M3 rope;
-FMT_V4PRO_BF16, bf16 rope)."""
+FMT_V4PRO_BF16, bf16 rope); unquantized 1152-B bf16 rows (FMT_BF16) are the accuracy reference pool, attended by
+the fp32 torch path on any device (no kernel reads them)."""
 from __future__ import annotations
 
 import math
@@ -16,7 +17,7 @@ import torch
 
 from .._ext import ext
 from . import formats as F
-from .kvcache import FMT_FP8, FMT_NVFP4
+from .kvcache import FMT_BF16, FMT_FP8, FMT_NVFP4
 
 FMT_NVFP4_NOROPE = 3      # the rope-free 288-byte NVFP4 row (GLM-Flash latent): attention over the 512 latent dims
 FMT_V4PRO = 4             # the 320-byte DeepSeek V4 Pro cell: 448 NVFP4 latent dims (dims 448..511 read as zero) + 64 E4M3
@@ -25,7 +26,8 @@ FMT_V4PRO_BF16 = 5        # the 384-byte V4 Pro cell: as FMT_V4PRO with 64 bf16 
 NUM_SMS = 148
 TILE = 128                # rows per kernel tile (split granularity and lazy-rescale step)
 ROW_BYTES = {FMT_NVFP4: F.MLA_ROW_BYTES, FMT_FP8: F.MLA_FP8_ROW_BYTES, FMT_NVFP4_NOROPE: F.GLMFLASH_ROW_BYTES,
-             FMT_V4PRO: F.v4pro_cell_bytes("fp8"), FMT_V4PRO_BF16: F.v4pro_cell_bytes("bf16")}
+             FMT_V4PRO: F.v4pro_cell_bytes("fp8"), FMT_V4PRO_BF16: F.v4pro_cell_bytes("bf16"),
+             FMT_BF16: F.MLA_BF16_ROW_BYTES}
 
 
 def mla_split_policy(tokens: int, topk: int, overhead_tiles: float = 2.0) -> tuple[int, int]:
@@ -78,8 +80,9 @@ def mla_decode(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_scale:
         out = torch.empty(t, h, F.MLA_NOPE, dtype=torch.bfloat16, device=q.device)
     if return_lse and lse is None:
         lse = torch.empty(t, h, dtype=torch.float32, device=q.device)
-    if not q.is_cuda:
-        o, l = mla_decode_ref(q, pool, idx, sm_scale, fmt)
+    if not q.is_cuda or fmt == FMT_BF16:
+        o, l = (mla_decode_bf16_pool(q, pool, idx, sm_scale) if fmt == FMT_BF16 else
+                mla_decode_ref(q, pool, idx, sm_scale, fmt))
         out.copy_(o.to(out.dtype))
         if lse is not None:
             lse.copy_(l)
@@ -147,6 +150,8 @@ def mla_dense_decode(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tens
 
 def dequant_rows(pool: torch.Tensor, fmt: int) -> torch.Tensor:
     """Rows -> fp32 [rows, 576] (latent, rope); the rope-free row's rope part is zero."""
+    if fmt == FMT_BF16:
+        return pool.contiguous().view(torch.bfloat16).view(pool.shape[0], F.MLA_QK).float()
     if fmt == FMT_NVFP4:
         return F.mla_row_dequantize(pool)
     if fmt == FMT_FP8:
@@ -159,6 +164,30 @@ def dequant_rows(pool: torch.Tensor, fmt: int) -> torch.Tensor:
         z = torch.zeros(c.shape[0], F.MLA_NOPE - F.V4P_NOPE, dtype=c.dtype, device=c.device)
         return torch.cat([c[:, :F.V4P_NOPE], z, c[:, F.V4P_NOPE:]], -1)
     raise ValueError(fmt)
+
+
+def mla_decode_bf16_pool(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_scale: float,
+                         chunk: int = 32) -> tuple[torch.Tensor, torch.Tensor]:
+    """Sparse MLA attention over unquantized bf16 rows ([rows, 1152] bytes = 576 bf16 values), in fp32 on q's
+    device, `chunk` tokens at a time (the rows they select gathered once per chunk).  The accuracy reference of the
+    quantized pools.  -> (out fp32 [T, H, 512], lse fp32 [T, H]; a token with no valid row gives 0 and -inf)."""
+    t, h, _ = q.shape
+    rows = pool.view(torch.bfloat16).view(pool.shape[0], F.MLA_QK)
+    out = torch.zeros(t, h, F.MLA_NOPE, dtype=torch.float32, device=q.device)
+    lse = torch.full((t, h), float("-inf"), dtype=torch.float32, device=q.device)
+    for a in range(0, t, chunk):
+        ic = idx[a:a + chunk].long()
+        k = rows[ic.clamp(min=0)].float()                                   # [c, topk, 576]
+        s = torch.einsum("chd,ckd->chk", q[a:a + chunk].float(), k) * sm_scale
+        s = s.masked_fill((ic < 0)[:, None, :], float("-inf"))
+        m = s.amax(-1, keepdim=True)
+        ok = torch.isfinite(m)
+        p = torch.where(ok, torch.exp(s - torch.where(ok, m, torch.zeros_like(m))), torch.zeros_like(s))
+        den = p.sum(-1, keepdim=True)
+        out[a:a + chunk] = torch.einsum("chk,ckd->chd", p / den.clamp(min=1e-30), k[..., :F.MLA_NOPE])
+        lse[a:a + chunk] = torch.where(ok[..., 0], (m + torch.log(den.clamp(min=1e-30)))[..., 0],
+                                       torch.full_like(m[..., 0], float("-inf")))
+    return out, lse
 
 
 def mla_decode_ref(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_scale: float, fmt: int = FMT_NVFP4):

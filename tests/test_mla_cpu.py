@@ -101,3 +101,65 @@ def test_mla_latent_and_expanded_layouts_agree():
     assert a.shape == (t, h, dv) and (a - b).abs().max().item() < 1e-9
     k, v = M.mla_expand_kv(c_kv, k_pe, w_uk, w_uv)
     assert k.shape == (s, h, 256) and torch.all(k[..., dn + dr:] == 0) and torch.all(v[..., dv:] == 0)
+
+
+def test_bf16_reference_pool_attention_matches_oracle():
+    """Unquantized bf16 latent rows (the accuracy reference pool): the chunked fp32 attention equals the per-token
+    oracle over the same rows, masked slots and a token with no valid row included, on any device."""
+    from inference_optimizations_b200.ops import formats as F
+    from inference_optimizations_b200.ops import kvcache as K
+    from inference_optimizations_b200.ops import mla as M
+    torch.manual_seed(7)
+    rows, t, h, topk = 300, 5, 4, 40
+    pool = torch.zeros(rows, F.MLA_BF16_ROW_BYTES, dtype=torch.uint8)
+    nope, rope = torch.randn(rows, 512), torch.randn(rows, 64)
+    K.mla_write(nope, rope, torch.arange(rows), pool)
+    back = M.dequant_rows(pool, M.FMT_BF16)
+    assert torch.equal(back, torch.cat([nope, rope], -1).to(torch.bfloat16).float())
+    q = torch.randn(t, h, 576).to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(rows)[:topk] for _ in range(t)]).int()
+    idx[torch.rand(t, topk) < 0.2] = -1
+    idx[3] = -1
+    sm = M.mla_sm_scale()
+    o, lse = M.mla_decode_bf16_pool(q, pool, idx, sm, chunk=2)
+    ro, rl = F.sparse_mla_reference(q.float(), back, idx, sm)
+    assert torch.allclose(o, ro, atol=1e-5, rtol=1e-5) and torch.equal(o[3], torch.zeros_like(o[3]))
+    assert torch.allclose(lse, rl, atol=1e-5) and torch.isinf(lse[3]).all()
+    out = M.mla_decode(q, pool, idx, sm, M.FMT_BF16)
+    assert torch.allclose(out.float(), ro.to(torch.bfloat16).float(), atol=2e-2)
+
+
+def test_mla_engine_latent_pool_formats():
+    """kv_dtype picks the latent row: nvfp4 352 B, fp8 576 B, bf16 1152 B (unquantized, the reference: torch
+    attention path, no graphs); the three engines share weights and agree closely on prefill logits; an unknown
+    kv_dtype is refused."""
+    import pytest
+    from inference_optimizations_b200.config import EngineConfig, model_config
+    from inference_optimizations_b200.engine.engine import Engine
+    from inference_optimizations_b200.engine.scheduler import Request, SamplingParams, Segment
+    cfg = model_config("tiny_mla")
+    engines = {}
+    for kv in ("bf16", "fp8", "nvfp4"):
+        ecfg = EngineConfig(model="tiny_mla", device="cpu", kv_dtype=kv, max_running=2, chunked_prefill=64)
+        engines[kv] = Engine(ecfg, cfg, max_seq=128)
+    assert [engines[k].runner.kv.latent[0].shape[1] for k in ("bf16", "fp8", "nvfp4")] == [1152, 576, 352]
+    assert engines["bf16"].runner.ref_pool and not engines["bf16"].runner._graphable()
+    torch.manual_seed(1)
+    prompt = torch.randint(1, cfg.vocab, (60,)).tolist()
+    logits = {}
+    for kv, eng in engines.items():
+        if kv != "bf16":
+            eng.runner.model.copy_from(engines["bf16"].runner.model)
+        r = Request(rid=0, prompt=prompt, params=SamplingParams(max_new_tokens=1))
+        r.slot = 0
+        eng.runner.attach(r)
+        st, _ = eng.runner._step([Segment(r, 0, prompt, True)])
+        logits[kv] = eng.runner.model.logits(eng.runner.model.forward(st, eng.runner.kv)).float()
+        eng.runner.detach(r)
+    for kv in ("fp8", "nvfp4"):
+        cos = torch.nn.functional.cosine_similarity(logits[kv], logits["bf16"], dim=-1)
+        assert cos.min().item() > 0.9, (kv, cos.min().item())
+    out = engines["bf16"].generate([prompt[:30]], SamplingParams(max_new_tokens=4))
+    assert len(out[0]) == 4
+    with pytest.raises(ValueError):
+        Engine(EngineConfig(model="tiny_mla", device="cpu", kv_dtype="int4", max_running=2), cfg, max_seq=128)

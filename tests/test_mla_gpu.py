@@ -161,3 +161,37 @@ def test_router_sums_split_k_partials(cuda, e, k, g, kg, ks):
     rid, rw = MOE.route_ref(summed, bias, k, g, kg, 2.5)
     assert torch.equal(ids.cpu().sort(-1).values, rid.sort(-1).values)
     assert torch.allclose(w.cpu().sort(-1).values, rw.sort(-1).values, rtol=1e-4, atol=1e-5)
+
+
+def test_bf16_reference_pool_on_gpu(cuda):
+    """The unquantized bf16 latent pool (the accuracy reference) on the GPU: the engine writes 1152-byte rows and
+    attends in fp32 through torch; its prefill logits match the same engine on the CPU, and the FP8-weight model's
+    NVFP4-pool engine stays close to it."""
+    from inference_optimizations_b200.engine.scheduler import Request, Segment
+    over = dict(hidden=256, num_heads=8, q_lora=256, qk_nope=128, v_head=128, index_heads=64, weight_dtype="fp8",
+                expert_dtype="fp8", expert_ffn=256, dense_ffn=512)
+    cfg = model_config("tiny_mla", **over)
+    engs = {}
+    for name, dev, kv in (("gpu_bf16", str(cuda), "bf16"), ("cpu_bf16", "cpu", "bf16"), ("gpu_nvfp4", str(cuda), "nvfp4")):
+        ecfg = EngineConfig(model="tiny_mla", device=dev, kv_dtype=kv, max_running=2, chunked_prefill=128,
+                            prefix_cache=False)
+        engs[name] = Engine(ecfg, cfg, max_seq=256)
+    src = engs["gpu_bf16"].runner.model
+    assert engs["gpu_bf16"].runner.kv.latent[0].shape[1] == 1152 and not src.fuse_glue
+    engs["cpu_bf16"].runner.model.copy_from(src)
+    engs["gpu_nvfp4"].runner.model.copy_from(src)
+    torch.manual_seed(8)
+    prompt = torch.randint(0, cfg.vocab, (80,)).tolist()
+    logits = {}
+    for name, eng in engs.items():
+        r = Request(rid=0, prompt=prompt, params=SamplingParams(max_new_tokens=1))
+        r.slot = 0
+        eng.runner.attach(r)
+        st, _ = eng.runner._step([Segment(r, 0, prompt, True)])
+        logits[name] = eng.runner.model.logits(eng.runner.model.forward(st, eng.runner.kv)).float().cpu()
+        eng.runner.detach(r)
+    cos = lambda a, b: torch.nn.functional.cosine_similarity(logits[a], logits[b], dim=-1)  # noqa: E731
+    assert cos("gpu_bf16", "cpu_bf16").min().item() > 0.98
+    assert cos("gpu_nvfp4", "gpu_bf16").mean().item() > 0.95
+    out = engs["gpu_bf16"].generate([prompt[:50]], SamplingParams(max_new_tokens=4))
+    assert len(out[0]) == 4
