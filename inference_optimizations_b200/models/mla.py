@@ -237,6 +237,7 @@ class MLAModel:
         self.keep_master = keep_master if keep_master is not None else c.num_params() < 2e9
         self.cuda = self.device.type == "cuda"
         self.fuse_glue = True                            # the fused attention-block glue kernels where they apply
+        self.exact_attention = False                     # fp32 attention over exactly decoded rows (accuracy arm)
         self._x8 = None                                  # (data_ptr of x, E4M3 x, scales) written by the last norm
         self._bs: dict = {}
         self.src = source if source is not None else RandomSource(seed, self.device)
@@ -843,7 +844,8 @@ class MLAModel:
                                        ws=kv.workspaces(t, st.max_ctx, c.num_heads, c.index_topk)[1])
         else:
             o_lat = M.mla_decode(qf, kv.latent[i], sel, self.sm_scale, kv.fmt,
-                                 ws=kv.workspaces(t, st.max_ctx, c.num_heads, c.index_topk)[1])
+                                 ws=kv.workspaces(t, st.max_ctx, c.num_heads, c.index_topk)[1],
+                                 exact=self.exact_attention)
         return self._post_attention(i, self._o_proj(w, o_lat, t), h, next_norm)
 
     def _post_attention(self, i: int, o: torch.Tensor, h: torch.Tensor, next_norm: torch.Tensor) -> torch.Tensor:

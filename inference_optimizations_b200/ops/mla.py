@@ -72,16 +72,17 @@ class MlaWorkspace:
 def mla_decode(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_scale: float, fmt: int = FMT_NVFP4,
                splits: Optional[tuple[int, int]] = None, ws: Optional[MlaWorkspace] = None,
                out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
-               return_lse: bool = False, trace: Optional[torch.Tensor] = None):
-    """q bf16 [T, H, 576], pool uint8 [rows, 352 | 576], idx int32 [T, topk] -> out bf16 [T, H, 512]
-    (and lse fp32 [T, H], natural log, with return_lse)."""
+               return_lse: bool = False, trace: Optional[torch.Tensor] = None, exact: bool = False):
+    """q bf16 [T, H, 576], pool uint8 [rows, 352 | 576 | 1152], idx int32 [T, topk] -> out bf16 [T, H, 512]
+    (and lse fp32 [T, H], natural log, with return_lse).  exact: fp32 attention over the exactly decoded rows
+    (`mla_decode_exact`) instead of the kernel; bf16 rows always take it."""
     t, h, _ = q.shape
     if out is None:
         out = torch.empty(t, h, F.MLA_NOPE, dtype=torch.bfloat16, device=q.device)
     if return_lse and lse is None:
         lse = torch.empty(t, h, dtype=torch.float32, device=q.device)
-    if not q.is_cuda or fmt == FMT_BF16:
-        o, l = (mla_decode_bf16_pool(q, pool, idx, sm_scale) if fmt == FMT_BF16 else
+    if not q.is_cuda or fmt == FMT_BF16 or exact:
+        o, l = (mla_decode_exact(q, pool, idx, sm_scale, fmt) if fmt == FMT_BF16 or exact else
                 mla_decode_ref(q, pool, idx, sm_scale, fmt))
         out.copy_(o.to(out.dtype))
         if lse is not None:
@@ -166,18 +167,20 @@ def dequant_rows(pool: torch.Tensor, fmt: int) -> torch.Tensor:
     raise ValueError(fmt)
 
 
-def mla_decode_bf16_pool(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_scale: float,
-                         chunk: int = 32) -> tuple[torch.Tensor, torch.Tensor]:
-    """Sparse MLA attention over unquantized bf16 rows ([rows, 1152] bytes = 576 bf16 values), in fp32 on q's
-    device, `chunk` tokens at a time (the rows they select gathered once per chunk).  The accuracy reference of the
-    quantized pools.  -> (out fp32 [T, H, 512], lse fp32 [T, H]; a token with no valid row gives 0 and -inf)."""
+def mla_decode_exact(q: torch.Tensor, pool: torch.Tensor, idx: torch.Tensor, sm_scale: float,
+                     fmt: int = FMT_BF16, chunk: int = 32) -> tuple[torch.Tensor, torch.Tensor]:
+    """Sparse MLA attention in fp32 on q's device over the rows `idx` selects, each decoded exactly from its pool
+    format (unquantized bf16 rows, [rows, 1152] bytes, as they are), `chunk` tokens at a time (their rows gathered
+    and decoded once per chunk).  The attention of the bf16 reference pool, and the exact-arithmetic arm of the
+    accuracy gate for the quantized pools (the kernel also rounds the query to E4M3).  -> (out fp32 [T, H, 512],
+    lse fp32 [T, H]; a token with no valid row gives 0 and -inf)."""
     t, h, _ = q.shape
-    rows = pool.view(torch.bfloat16).view(pool.shape[0], F.MLA_QK)
     out = torch.zeros(t, h, F.MLA_NOPE, dtype=torch.float32, device=q.device)
     lse = torch.full((t, h), float("-inf"), dtype=torch.float32, device=q.device)
     for a in range(0, t, chunk):
         ic = idx[a:a + chunk].long()
-        k = rows[ic.clamp(min=0)].float()                                   # [c, topk, 576]
+        c, kk = ic.shape
+        k = dequant_rows(pool[ic.clamp(min=0).flatten()], fmt).view(c, kk, F.MLA_QK)   # [c, topk, 576] fp32
         s = torch.einsum("chd,ckd->chk", q[a:a + chunk].float(), k) * sm_scale
         s = s.masked_fill((ic < 0)[:, None, :], float("-inf"))
         m = s.amax(-1, keepdim=True)

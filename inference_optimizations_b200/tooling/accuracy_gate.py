@@ -184,6 +184,9 @@ def main(argv=None) -> None:
     ap.add_argument("--em-file", default="", help="JSONL items of token ids (default: a bf16-KV oracle)")
     ap.add_argument("--em-answer", type=int, default=8, help="oracle answer length in tokens")
     ap.add_argument("--calibrate", action="store_true", help="measure control-vs-control noise first")
+    ap.add_argument("--attn", default="kernel", choices=["kernel", "exact"],
+                    help="MLA family: exact = both arms run the unfused attention glue and fp32 attention over the "
+                         "exactly decoded rows, so the arms differ by the latent row format alone")
     ap.add_argument("--out", default="")
     a = ap.parse_args(argv)
     cfg = model_config(a.model)
@@ -195,8 +198,12 @@ def main(argv=None) -> None:
     max_seq = a.len + max(64, a.em_answer + 64)
 
     def mk(kv, chunk=None):
-        return Engine(EngineConfig(model=a.model, device=a.device, kv_dtype=kv, max_running=4,
-                                   chunked_prefill=chunk or a.len, cuda_graphs=False), cfg, max_seq=max_seq)
+        eng = Engine(EngineConfig(model=a.model, device=a.device, kv_dtype=kv, max_running=4,
+                                  chunked_prefill=chunk or a.len, cuda_graphs=False), cfg, max_seq=max_seq)
+        if a.attn == "exact" and hasattr(eng.runner.model, "exact_attention"):
+            eng.runner.model.fuse_glue = False
+            eng.runner.model.exact_attention = True
+        return eng
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, cfg.vocab, (a.len,), generator=g).tolist() for _ in range(a.prompts)]
     ctl, arm = mk(a.ref_kv), mk(a.test_kv)
@@ -216,6 +223,7 @@ def main(argv=None) -> None:
                                                                                  a.em_answer), [x for _, x in items])
     v = verdict(res, em, noise)
     rec = {"model": a.model, "layers": cfg.num_layers, "prompt_len": a.len, "ref_kv": a.ref_kv, "test_kv": a.test_kv,
+           "attention": a.attn,
            **vars(res), "exact_match": (asdict(em) | {"drop_pts": em.drop_pts}) if em else None, "noise": noise,
            "verdict": v, "pass": v["pass"], "kl_target_pass": res.passed(a.kl_max)}
     if a.out:

@@ -121,7 +121,7 @@ def test_bf16_reference_pool_attention_matches_oracle():
     idx[torch.rand(t, topk) < 0.2] = -1
     idx[3] = -1
     sm = M.mla_sm_scale()
-    o, lse = M.mla_decode_bf16_pool(q, pool, idx, sm, chunk=2)
+    o, lse = M.mla_decode_exact(q, pool, idx, sm, chunk=2)
     ro, rl = F.sparse_mla_reference(q.float(), back, idx, sm)
     assert torch.allclose(o, ro, atol=1e-5, rtol=1e-5) and torch.equal(o[3], torch.zeros_like(o[3]))
     assert torch.allclose(lse, rl, atol=1e-5) and torch.isinf(lse[3]).all()
@@ -163,3 +163,24 @@ def test_mla_engine_latent_pool_formats():
     assert len(out[0]) == 4
     with pytest.raises(ValueError):
         Engine(EngineConfig(model="tiny_mla", device="cpu", kv_dtype="int4", max_running=2), cfg, max_seq=128)
+
+
+def test_exact_attention_over_quantized_rows_matches_oracle():
+    """The exact-arithmetic arm: fp32 attention over NVFP4 / FP8 rows decoded exactly equals the per-token oracle
+    over the same dequantized rows."""
+    from inference_optimizations_b200.ops import formats as F
+    from inference_optimizations_b200.ops import kvcache as K
+    from inference_optimizations_b200.ops import mla as M
+    torch.manual_seed(9)
+    rows, t, h, topk = 200, 4, 4, 32
+    nope, rope = torch.randn(rows, 512), torch.randn(rows, 64)
+    q = torch.randn(t, h, 576).to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(rows)[:topk] for _ in range(t)]).int()
+    idx[torch.rand(t, topk) < 0.25] = -1
+    sm = M.mla_sm_scale()
+    for fmt, width in ((M.FMT_NVFP4, F.MLA_ROW_BYTES), (M.FMT_FP8, F.MLA_FP8_ROW_BYTES)):
+        pool = torch.zeros(rows, width, dtype=torch.uint8)
+        K.mla_write(nope, rope, torch.arange(rows), pool)
+        o, lse = M.mla_decode_exact(q, pool, idx, sm, fmt, chunk=3)
+        ro, rl = M.mla_decode_ref(q, pool, idx, sm, fmt)
+        assert torch.allclose(o, ro, atol=1e-5, rtol=1e-5) and torch.allclose(lse, rl, atol=1e-5)
