@@ -481,10 +481,14 @@ cudaError_t indexer_topk(const IndexerArgs& a, cudaStream_t s) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, indexer_topk_cluster_kernel, a);
-  } else {
-    indexer_topk_kernel<false><<<a.T, kKThreads, 0, s>>>(a);
+    // a cluster of full-SM CTAs needs cl SMs of one GPC free to it (an SM partition of the device may hold fewer):
+    // the re-reading form serves the row when no such cluster fits
+    int fits = 0;
+    if (cudaOccupancyMaxActiveClusters(&fits, indexer_topk_cluster_kernel, &cfg) == cudaSuccess && fits > 0)
+      return cudaLaunchKernelEx(&cfg, indexer_topk_cluster_kernel, a);
+    (void)cudaGetLastError();
   }
+  if (a.score_stride > kRegKeys * kKThreads) indexer_topk_kernel<false><<<a.T, kKThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 
