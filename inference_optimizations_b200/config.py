@@ -195,6 +195,7 @@ class EngineConfig:
     page_size: int = 64
     kv_dtype: str = "nvfp4"              # "nvfp4" | "fp8" | "bf16" (GQA pools); MLA: "nvfp4" (352 B) | "fp8" (576 B)
                                          # | "kvmix" (FP8 and NVFP4 rows in one page space, per-request placement)
+                                         # | "bf16" (unquantized 1152-B rows: the accuracy reference)
     kvmix_threshold: int = 262144        # kvmix: requests whose length reaches this live in NVFP4 (promoted when
                                          # they grow past it), shorter ones in FP8
     kvmix_fp8_share: float = 0.5         # kvmix: share of the pool's latent bytes given to FP8 pages
@@ -215,6 +216,10 @@ class EngineConfig:
     draft_tokens: int = 3
     spec_policy: str = "adaptive"        # "adaptive": speculate only while it beats plain decode; "always"
     prefix_cache: bool = True            # radix prefix reuse (MLA family; sliding-window GQA models do not reuse)
+    kda_state_cache: str = ""            # hybrid KDA models: "" = no prefix reuse; "fp32" | "bf16" | "fp8" = the
+                                         # prefix cache also keeps each request's recurrent state at page
+                                         # boundaries, stored in that row format, and restores it on a match
+    kda_state_cache_max: int = 64        # recurrent-state snapshots the prefix cache keeps (least recent dropped)
     # runtime
     cuda_graphs: bool = True
     extend_kernel: bool = True           # GQA prefill over NVFP4 / FP8 pools through the 128-row extend kernel

@@ -136,9 +136,17 @@ class MLARunner:
         self.prefix_cache = None
         if cfg.kda_every and self.spec:
             raise NotImplementedError("hybrid KDA models run without the MTP draft")
-        # prefixes are not reused by hybrid models (a cached prefix's pages hold no KDA recurrent state) nor in kvmix
-        # pools (a promotion would move pages other requests share)
-        if ecfg.prefix_cache and not cfg.kda_every and not self.mixed:
+        # hybrid models: a cached prefix's pages hold no KDA recurrent state, so their prefixes are reused only with
+        # the state cache on (`kda_state_cache`: each request's state is snapshotted whenever its processed length
+        # reaches a page boundary, the latest snapshot goes to the prefix's radix node when the request leaves, and
+        # a match is cut back to the deepest node holding a state, which is restored into the new request's row).
+        # kvmix pools do not reuse prefixes (a promotion would move pages other requests share).
+        self.state_fmt = ecfg.kda_state_cache if cfg.kda_every else ""
+        if self.state_fmt not in ("", "fp32", "bf16", "fp8"):
+            raise ValueError(f"kda_state_cache keeps fp32, bf16 or fp8 state rows, not {self.state_fmt!r}")
+        self.snaps: dict = {}                         # rid -> (tokens covered, state snapshot) at a page boundary
+        self.state_hits = 0
+        if ecfg.prefix_cache and not self.mixed and (not cfg.kda_every or self.state_fmt):
             from ..kv.radix import RadixCache
             self.prefix_cache = RadixCache(self.kv.alloc)
 
@@ -193,6 +201,13 @@ class MLARunner:
         if self.prefix_cache is None:
             return
         path = self.prefix_cache.match(r.prompt[: ((r.prompt_len - 1) // 64) * 64])
+        if self.state_fmt:                      # hybrid model: reuse only up to the deepest stored recurrent state
+            j = max((k for k, n in enumerate(path) if n.state is not None), default=-1)
+            self.prefix_cache.release(path[j + 1:])
+            path = path[:j + 1]
+            if path:
+                self.kv.restore_state(r.slot, path[-1].state, self.state_fmt)
+                self.state_hits += 1
         rp = self.pages[r.rid]
         for lp, node in enumerate(path):
             rp.pages[lp] = node.page
@@ -204,6 +219,7 @@ class MLARunner:
     def detach(self, r: Request) -> None:
         rp = self.pages.pop(r.rid, None)
         self.placement.pop(r.rid, None)
+        snap = self.snaps.pop(r.rid, None)
         if rp is None:
             return
         if self.prefix_cache is None:
@@ -214,11 +230,32 @@ class MLARunner:
         cached = {n.page for n in rp.cached}
         donate = [rp.pages[lp] for lp in range(full)]
         rejected = set(self.prefix_cache.insert(hist[: 64 * full], donate))
+        if snap is not None and 0 < snap[0] <= 64 * full:
+            nodes = self.prefix_cache.path(hist[: snap[0]])
+            if len(nodes) == snap[0] // 64 and nodes[-1].state is None:
+                nodes[-1].state = snap[1]
+                self._trim_states()
         self.prefix_cache.release(rp.cached)
         keep = set(donate) - rejected
         self.kv.alloc.release([pg for pg in rp.pages.values() if pg not in keep and pg not in cached])
         rp.pages.clear()
         self.kv.table.clear(r.slot)
+
+    def _trim_states(self) -> None:
+        """Keep at most `kda_state_cache_max` recurrent-state snapshots in the prefix cache, least recent dropped."""
+        nodes = self.prefix_cache.states()
+        extra = len(nodes) - max(1, self.ecfg.kda_state_cache_max)
+        for n in sorted(nodes, key=lambda n: n.last)[:max(0, extra)]:
+            n.state = None
+
+    def _snapshot(self, pairs) -> None:
+        """Hybrid models with the state cache: (request, tokens its state now covers) after a forward; a request
+        whose processed length sits on a page boundary keeps a snapshot of its recurrent state there."""
+        if not self.state_fmt:
+            return
+        for r, n in pairs:
+            if n > 0 and n % 64 == 0:
+                self.snaps[r.rid] = (n, self.kv.snapshot_state(r.slot, self.state_fmt))
 
     # ------------------------------------------------------------------------------------------ lockstep (EP)
     def _agree(self, tokens: int) -> int:
@@ -337,6 +374,7 @@ class MLARunner:
         if self.spec:
             return self._prefill_spec(batch.segments)
         out = self._run(batch.segments)
+        self._snapshot((s.req, s.start + len(s.tokens)) for s in batch.segments)
         res, k = {}, 0
         for s in batch.segments:
             if s.logits:
@@ -388,6 +426,7 @@ class MLARunner:
         """Host side of a finished split, after its stream's work completed: rid -> first generated token."""
         res, k = {}, 0
         out = sp.get("out_host")
+        self._snapshot((s.req, s.start + len(s.tokens)) for s in sp["batch"].segments)
         for s in sp["batch"].segments:
             if s.logits:
                 res[s.req.rid] = int(out[k])
@@ -486,6 +525,7 @@ class MLARunner:
         else:
             segs = [Segment(r, r.kv_len, [r.pending], True) for r in reqs]
             out = self._run(segs, agreed)
+        self._snapshot((r, r.kv_len + 1) for r in reqs)
         return {r.rid: [int(out[i])] for i, r in enumerate(reqs)}
 
     # ------------------------------------------------------------------------------------------ CUDA graphs

@@ -11,12 +11,13 @@ from typing import Optional
 
 
 class _Node:
-    __slots__ = ("children", "page", "ref", "last", "parent", "key")
+    __slots__ = ("children", "page", "ref", "last", "parent", "key", "state")
 
     def __init__(self, parent: Optional["_Node"], key: Optional[tuple], page: int):
         self.children: dict = {}
         self.page, self.ref, self.parent, self.key = page, 0, parent, key
         self.last = 0
+        self.state = None                   # hybrid models: recurrent state after this node's last token
 
 
 class RadixCache:
@@ -68,6 +69,26 @@ class RadixCache:
             nxt.last = t
             node = nxt
         return rejected
+
+    def path(self, tokens: list) -> list:
+        """The cached nodes of the page-aligned prefix of `tokens`, in order, without referencing them."""
+        node, out = self.root, []
+        for key in self._chunks(tokens):
+            node = node.children.get(key)
+            if node is None:
+                break
+            out.append(node)
+        return out
+
+    def states(self) -> list:
+        """Every node holding a recurrent state."""
+        out, stack = [], [self.root]
+        while stack:
+            n = stack.pop()
+            if n.state is not None:
+                out.append(n)
+            stack.extend(n.children.values())
+        return out
 
     def _leaves(self):
         stack = [self.root]

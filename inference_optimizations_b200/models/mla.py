@@ -172,6 +172,27 @@ class MLAKVCache:
             for v in st.values():
                 v[row].zero_()
 
+    def snapshot_state(self, row: int, fmt: str) -> dict:
+        """Copy of request row `row`'s recurrent states (every KDA layer): the delta-rule state as rows of 128 in
+        `fmt` ("fp32" kept as is, "bf16" / "fp8" through `ops/kda.py quant_state_rows`), the short conv taps fp32."""
+        from ..ops import kda as KDA
+        snap = {}
+        for i, st in self.kda.items():
+            S = st["S"][row]
+            rows = S.reshape(-1, 128).clone() if fmt == "fp32" else KDA.quant_state_rows(S.reshape(-1, 128), fmt)
+            snap[i] = {"S": rows, **{k: st[k][row].clone() for k in ("csq", "csk", "csv")}}
+        return snap
+
+    def restore_state(self, row: int, snap: dict, fmt: str) -> None:
+        """Load a `snapshot_state` copy into request row `row`."""
+        from ..ops import kda as KDA
+        for i, st in self.kda.items():
+            rows = snap[i]["S"]
+            S = rows if fmt == "fp32" else KDA.dequant_state_rows(rows, fmt)
+            st["S"][row].copy_(S.view_as(st["S"][row]))
+            for k in ("csq", "csk", "csv"):
+                st[k][row].copy_(snap[i][k])
+
     def workspaces(self, t: int, max_ctx: int, heads: int, topk: int):
         """(indexer workspace, sparse-MLA workspace) of a step with t tokens and context bound max_ctx, shared by
         every layer of the step (layers run one after another).  Made on first use outside stream capture, so a

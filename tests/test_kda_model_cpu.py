@@ -36,3 +36,57 @@ def test_kda_hybrid_generation_matches_full_recompute():
                 assert tok == int(logits.argmax()), (len(seq), tok, int(logits.argmax()))
             seq.append(tok)
     assert eng.runner.kv.alloc.used == 0
+
+
+def _cached_engine(fmt: str, keep: int = 64) -> Engine:
+    ecfg = EngineConfig(model="tiny_kda", device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=64,
+                        cuda_graphs=False, prefix_cache=bool(fmt), kda_state_cache=fmt, kda_state_cache_max=keep)
+    return Engine(ecfg, model_config("tiny_kda"), max_seq=512)
+
+
+def _two_turns(eng: Engine) -> tuple:
+    """A 150-token first turn (prefill snapshots at 64 and 128), then a second turn whose prompt extends the first
+    turn's prompt and output."""
+    torch.manual_seed(11)
+    p1 = torch.randint(1, 500, (150,)).tolist()
+    o1 = eng.generate([p1], SamplingParams(max_new_tokens=6))[0]
+    p2 = p1 + o1 + torch.randint(1, 500, (40,)).tolist()
+    r2 = eng.add_request(p2, SamplingParams(max_new_tokens=6))
+    while eng.has_work():
+        eng.step()
+    return o1, r2
+
+
+def test_kda_state_cache_prefix_reuse_is_exact_in_fp32():
+    """Hybrid-model prefix reuse: the second turn reuses the first turn's pages up to the deepest page boundary with
+    a stored recurrent state (128 tokens here) and, with fp32 state rows, generates exactly what a cold engine does."""
+    warm, cold = _cached_engine("fp32"), _cached_engine("")
+    o1w, r2w = _two_turns(warm)
+    o1c, r2c = _two_turns(cold)
+    assert cold.runner.prefix_cache is None and r2c.cached_tokens == 0
+    assert warm.runner.state_hits == 1 and r2w.cached_tokens == 128
+    assert o1w == o1c and r2w.output == r2c.output
+
+
+def test_kda_state_cache_quantized_rows_and_trim():
+    """bf16 / fp8 state rows restore close to the fp32 state; the cache keeps at most kda_state_cache_max
+    snapshots; an unknown state format is refused."""
+    import pytest
+    from inference_optimizations_b200.ops import kda as KD
+    for fmt in ("bf16", "fp8"):
+        eng = _cached_engine(fmt, keep=1)
+        _, r2 = _two_turns(eng)
+        assert eng.runner.state_hits == 1 and r2.cached_tokens == 128 and len(r2.output) == 6
+        assert len(eng.runner.prefix_cache.states()) <= 1
+        kv = eng.runner.kv
+        row = 0
+        kv.kda[0]["S"][row].normal_()
+        ref = kv.kda[0]["S"][row].clone()
+        snap = kv.snapshot_state(row, fmt)
+        kv.reset_state(row)
+        kv.restore_state(row, snap, fmt)
+        err = ((kv.kda[0]["S"][row] - ref).norm() / ref.norm()).item()
+        assert err < (0.01 if fmt == "bf16" else 0.05), (fmt, err)
+        assert snap[0]["S"].shape[1] == KD.ROW_BYTES[fmt]
+    with pytest.raises(ValueError):
+        _cached_engine("nvfp4")
