@@ -134,8 +134,6 @@ class MLARunner:
         self.graph_launches: dict = {}
         self.event_log = None
         self.prefix_cache = None
-        if cfg.kda_every and self.spec:
-            raise NotImplementedError("hybrid KDA models run without the MTP draft")
         # hybrid models: a cached prefix's pages hold no KDA recurrent state, so their prefixes are reused only with
         # the state cache on (`kda_state_cache`: each request's state is snapshotted whenever its processed length
         # reaches a page boundary, the latest snapshot goes to the prefix's radix node when the request leaves, and
@@ -487,7 +485,12 @@ class MLARunner:
     def spec_decode(self, reqs: list) -> dict:
         segs = [Segment(r, r.kv_len, [r.pending, r.draft_state.get("d", 0)], False) for r in reqs]
         st, _ = self._step(segs)
-        x, h = self.model.forward_hidden(st, self.kv)
+        # hybrid models: the verify keeps each row's KDA state after its first token (`MLAModel.kda_mid`)
+        self.model.kda_mid = {} if self.kv.kda else None
+        try:
+            x, h = self.model.forward_hidden(st, self.kv)
+        finally:
+            mid, self.model.kda_mid = self.model.kda_mid, None
         o = B.argmax(self.model.logits(x))                               # [2n]: (o0, o1) per request
         m = B.argmax(self.model.logits(self.model.draft_forward(self._mtp_step(st, o), self.kv, h)))
         both = torch.stack([o, m]).cpu()
@@ -499,6 +502,12 @@ class MLARunner:
             r.draft_state["d"] = int(both[1, 2 * i + 1] if acc else both[1, 2 * i])
             r.accepted += int(acc)
             r.spec_steps += 1
+            if mid and not acc:                  # rejected draft: the recurrent states advance by the first token only
+                for (layer, row), state in mid.items():
+                    if row == r.slot:
+                        for name, val in state.items():
+                            self.kv.kda[layer][name][row].copy_(val)
+        self._snapshot((r, r.kv_len + len(res[r.rid])) for r in reqs)
         return res
 
     def draft_row(self, r: Request) -> int:

@@ -259,6 +259,8 @@ class MLAModel:
         self.cuda = self.device.type == "cuda"
         self.fuse_glue = True                            # the fused attention-block glue kernels where they apply
         self.exact_attention = False                     # fp32 attention over exactly decoded rows (accuracy arm)
+        self.kda_mid = None                              # speculative verify of a hybrid model: (layer, row) ->
+                                                         # recurrent state after the segment's first token
         self._x8 = None                                  # (data_ptr of x, E4M3 x, scales) written by the last norm
         self._bs: dict = {}
         self.src = source if source is not None else RandomSource(seed, self.device)
@@ -429,12 +431,19 @@ class MLAModel:
         else:
             o = torch.empty(t, H, D, dtype=torch.bfloat16, device=x.device)
             for r0, n, slot in st.segs:
-                sl = slice(r0, r0 + n)
                 rows = slice(slot, slot + 1)
-                o[sl] = KDA.kda_prefill(q[sl].reshape(1, n, H, D), k[sl].reshape(1, n, H, D),
-                                        v[sl].reshape(1, n, H, D), f[sl].reshape(1, n, H, D), *args, beta[sl][None],
-                                        g2[sl].reshape(1, n, H, D), kd["norm_w"], kd["cwq"], kd["cwk"], kd["cwv"],
-                                        S["csq"][rows], S["csk"][rows], S["csv"][rows], S["S"][rows])[0]
+                # speculative verify (`kda_mid` set): the segment's first token runs alone and the state after it is
+                # kept, so a rejected draft's row can be set back to it (the commit fold)
+                parts = [(r0, 1), (r0 + 1, n - 1)] if self.kda_mid is not None and n > 1 else [(r0, n)]
+                for a, m in parts:
+                    sl = slice(a, a + m)
+                    o[sl] = KDA.kda_prefill(q[sl].reshape(1, m, H, D), k[sl].reshape(1, m, H, D),
+                                            v[sl].reshape(1, m, H, D), f[sl].reshape(1, m, H, D), *args,
+                                            beta[sl][None], g2[sl].reshape(1, m, H, D), kd["norm_w"], kd["cwq"],
+                                            kd["cwk"], kd["cwv"], S["csq"][rows], S["csk"][rows], S["csv"][rows],
+                                            S["S"][rows])[0]
+                    if self.kda_mid is not None and a == r0 and len(parts) > 1:
+                        self.kda_mid[(i, slot)] = {name: S[name][slot].clone() for name in ("csq", "csk", "csv", "S")}
         o = o.reshape(t, H * D)
         return kd["o"](o) if "o" in kd else Fn.linear(o, kd["wo"])
 

@@ -90,3 +90,35 @@ def test_kda_state_cache_quantized_rows_and_trim():
         assert snap[0]["S"].shape[1] == KD.ROW_BYTES[fmt]
     with pytest.raises(ValueError):
         _cached_engine("nvfp4")
+
+
+def test_kda_mtp_speculation_commit_fold_keeps_greedy_output():
+    """MTP speculation on the hybrid model: a verify step runs each request's [pending, draft] through the KDA layers
+    as two single-token updates and keeps the state after the first; a rejected draft sets the row back to it (the
+    commit fold), so the emitted tokens are plain greedy decoding's.  Half of the drafts are scripted to the true
+    next token so both the accepted and the rolled-back paths run."""
+    torch.manual_seed(3)
+    prompts = [torch.randint(1, 500, (n,)).tolist() for n in (50, 13, 77)]
+
+    def eng_(spec):
+        ecfg = EngineConfig(model="tiny_kda", device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=64,
+                            cuda_graphs=False, prefix_cache=False, spec=spec, spec_policy="always")
+        return Engine(ecfg, model_config("tiny_kda"), max_seq=256)
+    plain = eng_(False).generate(prompts, SamplingParams(max_new_tokens=10))
+    eng = eng_(True)
+    run = eng.runner
+    inner = run.spec_decode
+
+    def scripted(reqs):
+        for r in reqs:
+            k = len(r.output)
+            ref = plain[[p for p in prompts].index(r.prompt)]
+            if k < len(ref) and k % 2 == 0:
+                r.draft_state["d"] = ref[k]
+        return inner(reqs)
+    run.spec_decode = scripted
+    outs = eng.generate(prompts, SamplingParams(max_new_tokens=10))
+    assert outs == plain
+    acc = sum(r.accepted for r in eng.finished)
+    steps = sum(r.spec_steps for r in eng.finished)
+    assert 0 < acc < steps, (acc, steps)
