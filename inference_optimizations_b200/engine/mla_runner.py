@@ -231,7 +231,7 @@ class MLARunner:
         if snap is not None and 0 < snap[0] <= 64 * full:
             nodes = self.prefix_cache.path(hist[: snap[0]])
             if len(nodes) == snap[0] // 64 and nodes[-1].state is None:
-                nodes[-1].state = snap[1]
+                self.prefix_cache.set_state(nodes[-1], snap[1])
                 self._trim_states()
         self.prefix_cache.release(rp.cached)
         keep = set(donate) - rejected
@@ -241,10 +241,12 @@ class MLARunner:
 
     def _trim_states(self) -> None:
         """Keep at most `kda_state_cache_max` recurrent-state snapshots in the prefix cache, least recent dropped."""
+        extra = len(self.prefix_cache.stateful) - max(1, self.ecfg.kda_state_cache_max)
+        if extra <= 0:
+            return
         nodes = self.prefix_cache.states()
-        extra = len(nodes) - max(1, self.ecfg.kda_state_cache_max)
         for n in sorted(nodes, key=lambda n: n.last)[:max(0, extra)]:
-            n.state = None
+            self.prefix_cache.set_state(n, None)
 
     def _snapshot(self, pairs) -> None:
         """Hybrid models with the state cache: (request, tokens its state now covers) after a forward; a request

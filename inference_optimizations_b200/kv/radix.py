@@ -27,6 +27,7 @@ class RadixCache:
         self.clock = itertools.count(1)
         self.held = 0                       # pages owned by the tree
         self.hits = self.lookups = 0
+        self.stateful: set = set()          # nodes holding a recurrent state (hybrid models)
 
     def _chunks(self, tokens: list):
         n = len(tokens) // self.page
@@ -80,15 +81,17 @@ class RadixCache:
             out.append(node)
         return out
 
+    def set_state(self, node: _Node, state) -> None:
+        """Attach (or, with None, drop) the recurrent state after `node`'s last token."""
+        node.state = state
+        if state is None:
+            self.stateful.discard(node)
+        else:
+            self.stateful.add(node)
+
     def states(self) -> list:
         """Every node holding a recurrent state."""
-        out, stack = [], [self.root]
-        while stack:
-            n = stack.pop()
-            if n.state is not None:
-                out.append(n)
-            stack.extend(n.children.values())
-        return out
+        return list(self.stateful)
 
     def _leaves(self):
         stack = [self.root]
@@ -109,6 +112,7 @@ class RadixCache:
                 if freed >= n_pages:
                     break
                 del lf.parent.children[lf.key]
+                self.stateful.discard(lf)
                 self.alloc.release([lf.page])
                 self.held -= 1
                 freed += 1
