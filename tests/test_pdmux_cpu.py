@@ -3,6 +3,7 @@ plain engine's tokens, and the data-parallel lockstep (gloo ranks agree on every
 import os
 import socket
 
+import pytest
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
@@ -108,15 +109,17 @@ def test_engine_config_flag():
     assert eng.pdmux.log and not eng.has_work()
 
 
-def test_pdmux_mla_family_matches_plain_engine():
-    """The MLA family through the lanes: prefill split by layer ranges beside decode steps gives the plain engine's
-    tokens, the split's last range ends with the LM head, pages are released."""
+@pytest.mark.parametrize("model", ["tiny_mla", "tiny_kda"])
+def test_pdmux_mla_family_matches_plain_engine(model):
+    """The MLA family (and the hybrid KDA + MLA model, whose recurrent states the split prefill carries) through the
+    lanes: prefill split by layer ranges beside decode steps gives the plain engine's tokens, the split's last range
+    ends with the LM head, pages are released."""
     from inference_optimizations_b200.config import model_config
 
     def mla_engine():
-        ecfg = EngineConfig(model="tiny_mla", device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=40,
+        ecfg = EngineConfig(model=model, device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=40,
                             cuda_graphs=False, prefix_cache=False)
-        return Engine(ecfg, model_config("tiny_mla"), max_seq=256)
+        return Engine(ecfg, model_config(model), max_seq=256)
     params = SamplingParams(max_new_tokens=6)
     ref = mla_engine().generate(PROMPTS, params)
     pm = PdmuxEngine(mla_engine(), token_budget=40)          # 40-token chunks -> one layer per iteration
