@@ -20,19 +20,22 @@ PROMPTS = [[(17 * i + 5 * j) % 500 + 1 for j in range(20 + 45 * i)] for i in ran
 SPLIT = {0: [0, 2, 3], 1: [1]}
 
 
-def _engine(ep: int, rank: int, spec: bool = False) -> Engine:
-    ecfg = EngineConfig(model="tiny_mla", device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=32,
+def _engine(ep: int, rank: int, spec: bool = False, model: str = "tiny_mla") -> Engine:
+    # the hybrid model's recurrent prefill rounds differently for other chunk boundaries (and co-batched prompts
+    # share a step's chunk budget), so it prefills every prompt in one chunk on both sides of the comparison
+    chunk = 512 if model == "tiny_kda" else 32
+    ecfg = EngineConfig(model=model, device="cpu", kv_dtype="nvfp4", max_running=4, chunked_prefill=chunk,
                         cuda_graphs=False, ep=ep, prefix_cache=False, spec=spec, spec_policy="always")
-    return Engine(ecfg, model_config("tiny_mla"), max_seq=256, ep_rank=rank,
+    return Engine(ecfg, model_config(model), max_seq=256, ep_rank=rank,
                   ep_group=dist.group.WORLD if ep > 1 else None)
 
 
-def _worker(rank: int, port: int, spec: bool, q):
+def _worker(rank: int, port: int, spec: bool, q, model: str = "tiny_mla"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2")
     dist.init_process_group("gloo", rank=rank, world_size=2)
     try:
-        eng = _engine(2, rank, spec)
-        assert eng.runner.model.layers[-1].ffn["w_gu"].shape[0] == model_config("tiny_mla").num_experts // 2
+        eng = _engine(2, rank, spec, model)
+        assert eng.runner.model.layers[-1].ffn["w_gu"].shape[0] == model_config(model).num_experts // 2
         outs = eng.generate_dp([PROMPTS[i] for i in SPLIT[rank]], SamplingParams(max_new_tokens=6))
         q.put((rank, outs))
     finally:
@@ -45,12 +48,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _run(spec: bool) -> None:
-    ref = _engine(1, 0, spec).generate(PROMPTS, SamplingParams(max_new_tokens=6))
+def _run(spec: bool, model: str = "tiny_mla") -> None:
+    ref = _engine(1, 0, spec, model).generate(PROMPTS, SamplingParams(max_new_tokens=6))
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, spec, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, port, spec, q, model)) for r in range(2)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=600) for _ in range(2))
@@ -62,6 +65,12 @@ def _run(spec: bool) -> None:
 
 def test_dp_attention_ep_moe_matches_single_process():
     _run(spec=False)
+
+
+def test_dp_ep_hybrid_kda_model_matches_single_process():
+    """The hybrid KDA + MLA + MoE model under DP attention + EP: each rank's recurrent states stay with its own
+    requests while the MoE layers exchange tokens; outputs equal the single-process engine."""
+    _run(spec=False, model="tiny_kda")
 
 
 def test_dp_ep_with_mtp_speculation():
