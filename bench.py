@@ -45,7 +45,8 @@ def parse():
     p.add_argument("--sessions", type=int, default=None, help="sessions over all ranks (dsa_moe 64, gemma31b 32)")
     p.add_argument("--ctx", type=int, default=None, help="prompt tokens (dsa_moe 8192, gemma31b 32768)")
     p.add_argument("--max-new", type=int, default=None, help="output tokens (dsa_moe 1024, gemma31b 512)")
-    p.add_argument("--layers", type=int, default=13, help="dsa_moe: depth of the scaling-curve model")
+    p.add_argument("--layers", type=int, default=None,
+                   help="dsa_moe: depth of the scaling-curve model (13); glm5: depth run on every rank (8)")
     p.add_argument("--full-depth", dest="full_depth", action="store_true", default=None,
                    help="dsa_moe: also run the full 61-layer model (default: on at 8 GPUs, the published config)")
     p.add_argument("--no-full-depth", dest="full_depth", action="store_false")
@@ -59,10 +60,17 @@ def parse():
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                    help="gemma31b tensor-parallel all-reduce: own peer-memory kernel fused with the norms or NCCL")
     a = p.parse_args()
+    if a.model == "glm5":              # long-context config: 8 sessions of 204,800 cached tokens per rank
+        a.sessions = a.sessions or 8 * int(os.environ.get("WORLD_SIZE", "1"))
+        a.ctx = a.ctx or 204800
+        a.max_new = a.max_new or 256
+        a.layers = a.layers or 8
+        return a
     gemma = a.model != "dsa_moe"
     a.sessions = a.sessions or (32 if gemma else 64)
     a.ctx = a.ctx or (32768 if gemma else 8192)
     a.max_new = a.max_new or (512 if gemma else 1024)
+    a.layers = a.layers or 13
     return a
 
 
@@ -468,6 +476,25 @@ def bench_gemma(args) -> int:
 
 
 
+def bench_long(args) -> int:
+    """The long-context config (GLM-5-class: sessions holding `ctx` cached tokens, data-parallel attention + EP over
+    the launched ranks): per-user decode rate, and the KV-pool capacity at boot for NVFP4 vs FP8 rows, from the DP
+    serving benchmark (`engine/dp_serve.py`; the sessions' prompts sit in the pool as rows written by the pool
+    writers, the prefill is not run).  One JSON line from rank 0."""
+    from inference_optimizations_b200.engine import dp_serve
+    for k, v in (("RANK", "0"), ("LOCAL_RANK", "0"), ("WORLD_SIZE", "1"), ("MASTER_ADDR", "127.0.0.1")):
+        os.environ.setdefault(k, v)
+    if "MASTER_PORT" not in os.environ:
+        import socket
+        with socket.socket() as sk:
+            sk.bind(("127.0.0.1", 0))
+            os.environ["MASTER_PORT"] = str(sk.getsockname()[1])
+    dp_serve.main(["--model", "glm5", "--layers", str(args.layers), "--sessions", str(args.sessions),
+                   "--ctx", str(args.ctx), "--steps", str(args.steps), "--warmup", str(max(3, args.warmup)),
+                   "--kv", args.kv] + (["--no-graphs"] if args.no_graphs else []))
+    return 0
+
+
 def main() -> int:
     args = parse()
     if args.impl == "reference":
@@ -476,6 +503,8 @@ def main() -> int:
         return 0
     if args.model == "dsa_moe":
         return bench_dsa(args)
+    if args.model == "glm5":
+        return bench_long(args)
     return bench_gemma(args)
 
 
