@@ -83,14 +83,31 @@ class IndexerWorkspace:
                                 torch.zeros(1, dtype=torch.int32, device=device))
 
 
+# fp32 score rows one selection call may hold (tokens x context x 4 B): a long prefill chunk over a long context
+# (8192 tokens x 204,800 positions = 6.7 GB) selects in row blocks under this instead
+SCORE_BYTES_MAX = 1 << 30
+
+
 def indexer_select(q8: torch.Tensor, w: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor,
                    limit: torch.Tensor, topk: int, max_ctx: int, req_idx: Optional[torch.Tensor] = None,
                    ws: Optional[IndexerWorkspace] = None, tiles_per_cta: int = 0,
                    with_pos: bool = False):
     """-> slots int32 [T, topk] (and positions with `with_pos`).  `max_ctx` bounds limit (fixed per CUDA graph).
     tiles_per_cta 0: as many 128-position tiles per CTA as fill every SM about once (at most 32), so a decode step
-    of a few tokens still spreads its score pass over the GPU; depends only on (T, max_ctx), so graphs stay valid."""
+    of a few tokens still spreads its score pass over the GPU; depends only on (T, max_ctx), so graphs stay valid.
+    Without a workspace, a step whose score rows exceed SCORE_BYTES_MAX runs in blocks of rows (exact: a token's
+    selection reads only its own row)."""
     t = q8.shape[0]
+    width = max(TILE, -(-max_ctx // TILE) * TILE)
+    block = max(1, SCORE_BYTES_MAX // (4 * width))
+    if ws is None and t > block:
+        rix = req_idx if req_idx is not None else torch.arange(t, dtype=torch.int32, device=q8.device)
+        parts = [indexer_select(q8[a:a + block], w[a:a + block], pool, page_table, limit[a:a + block], topk,
+                                max_ctx, rix[a:a + block], None, tiles_per_cta, with_pos)
+                 for a in range(0, t, block)]
+        if with_pos:
+            return torch.cat([p[0] for p in parts]), torch.cat([p[1] for p in parts])
+        return torch.cat(parts)
     slots = torch.empty(t, topk, dtype=torch.int32, device=q8.device)
     pos = torch.empty(t, topk, dtype=torch.int32, device=q8.device) if with_pos else None
     if not q8.is_cuda:

@@ -80,3 +80,32 @@ def test_expert_quantization_one_expert_at_a_time():
     q1, e1 = MG._quant_blocks_per_expert(w)
     q2, e2 = MG.quant_blocks(w)
     assert torch.equal(q1, q2) and torch.equal(e1, e2)
+
+
+def test_indexer_selection_in_row_blocks_is_exact(monkeypatch):
+    """Indexer logits chunked by rows (the reference's logits-OOM fix): a step whose fp32 score rows exceed the
+    budget selects in blocks of token rows, with the same slots and positions as one pass (page-table rows by
+    request index or, without one, by token)."""
+    from inference_optimizations_b200.ops import indexer as I
+    from inference_optimizations_b200.ops import kvcache as K
+    torch.manual_seed(13)
+    lens = [300, 700, 64, 500, 1, 0, 450]
+    t = len(lens)
+    per = max(-(-n // 64) for n in lens)
+    pages = t * per + 2
+    pt = torch.randperm(pages)[: t * per].view(t, per).int()
+    pool = torch.zeros(pages, K.INDEX_PAGE_BYTES, dtype=torch.uint8)
+    for i, n in enumerate(lens):
+        if n:
+            pos = torch.arange(n)
+            K.index_key_write(torch.randn(n, 128).to(torch.bfloat16), (pt[i][pos // 64] * 64 + pos % 64).int(), pool)
+    q8, w = I.indexer_q_quant(torch.randn(t, 8, 128), torch.rand(t, 8))
+    limit = torch.tensor(lens, dtype=torch.int32)
+    rix = torch.tensor([6, 5, 4, 3, 2, 1, 0], dtype=torch.int32)
+    whole = [I.indexer_select(q8, w, pool, pt, limit if r is None else limit[r.long()], 128, 768, req_idx=r,
+                              with_pos=True) for r in (None, rix)]
+    monkeypatch.setattr(I, "SCORE_BYTES_MAX", 3 * 4 * 768)        # blocks of 3 rows
+    blocks = [I.indexer_select(q8, w, pool, pt, limit if r is None else limit[r.long()], 128, 768, req_idx=r,
+                               with_pos=True) for r in (None, rix)]
+    for (s0, p0), (s1, p1) in zip(whole, blocks):
+        assert torch.equal(s0, s1) and torch.equal(p0, p1)
